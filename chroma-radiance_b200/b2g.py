@@ -1,0 +1,234 @@
+"""Python host side of the B200 GEMM engine, over its C ABI (include/b2g.h).
+
+The functions mirror the reference's GEMM interface in cublas_ops.cuh — same names,
+argument meaning and dtype rules — on torch CUDA tensors (torch is only the device-memory
+and stream plumbing here; every byte of math runs in libb2g.so's kernels):
+
+    linear(x, W, bias, out)                          cublas_ops.cuh:359-500
+    linear_lt(M, K, N, x, x_type, w, w_type, bias, out)   cublas_ops.cuh:214-288
+    linear_gated_residual(x, W, bias, residual, gate, M, N_out)   cublas_ops.cuh:684-723
+    batched_matmul_Bt(A, B, C)                       cublas_ops.cuh:558-585
+
+plus the engine's own fused entry point `gemm(...)` (bias / GELU / gated residual fused
+into the tensor-core epilogue, bf16/fp16/F32 output).  Where the reference prints and
+calls exit(1) on an error, these raise B2GError with the engine's message.  There is no
+CPU fallback: without the library or a B200 every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libb2g.so"
+
+# b2g_dtype
+F32, F16, BF16, E4M3 = 0, 1, 2, 3
+# cudaDataType_t values used by linear_lt's signature
+CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF = 0, 2, 14
+# b2g_epilogue
+EPI_NONE, EPI_GELU, EPI_GATED_RESIDUAL = 0, 1, 2
+
+_TORCH_TO_B2G = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+_TORCH_TO_CUDA = {torch.float32: CUDA_R_32F, torch.float16: CUDA_R_16F, torch.bfloat16: CUDA_R_16BF}
+_EPILOGUES = {"none": EPI_NONE, "gelu": EPI_GELU, "gated_residual": EPI_GATED_RESIDUAL}
+
+
+class B2GError(RuntimeError):
+    """A non-OK b2g_status, with the library's message."""
+
+
+class GemmDesc(ctypes.Structure):
+    """Mirror of b2g_gemm_desc."""
+
+    _fields_ = [
+        ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+        ("a", ctypes.c_void_p), ("a_dtype", ctypes.c_int), ("lda", ctypes.c_int64),
+        ("b", ctypes.c_void_p), ("b_dtype", ctypes.c_int), ("ldb", ctypes.c_int64),
+        ("bias", ctypes.c_void_p), ("bias_dtype", ctypes.c_int),
+        ("d", ctypes.c_void_p), ("d_dtype", ctypes.c_int), ("ldd", ctypes.c_int64),
+        ("epilogue", ctypes.c_int),
+        ("gate", ctypes.c_void_p),
+    ]
+
+
+_lib = None
+
+# Exported symbols of libb2g.so with their ctypes signatures (status-returning unless noted).
+_SIGNATURES = {
+    "b2g_init": ([], ctypes.c_int),
+    "b2g_shutdown": ([], ctypes.c_int),
+    "b2g_last_error": ([], ctypes.c_char_p),
+    "b2g_version": ([], ctypes.c_char_p),
+    "b2g_gemm": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p], ctypes.c_int),
+    "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                               ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "b2g_linear_lt_stream": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p],
+                             ctypes.c_int),
+    "b2g_linear_gated_residual": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                   ctypes.c_int64], ctypes.c_int),
+    "b2g_batched_matmul_Bt": ([ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4, ctypes.c_int),
+    "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
+    "b2g_launch_count": ([], ctypes.c_uint64),
+}
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Loads libb2g.so (once) and declares its signatures.  Raises B2GError if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise B2GError(f"{p} is missing: build it with `python chroma-radiance_b200/build.py`")
+    lib = ctypes.CDLL(str(p))
+    for name, (args, res) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def _check(status: int) -> None:
+    if status != 0:
+        msg = _lib.b2g_last_error().decode(errors="replace")
+        raise B2GError(f"b2g status {status}: {msg}")
+
+
+def init() -> None:
+    """Replaces init_cublas() (cublas_ops.cuh:152): validates the device (sm_100)."""
+    _check(load().b2g_init())
+
+
+def launch_count() -> int:
+    """How many of the engine's kernels have been launched in this process."""
+    return int(load().b2g_launch_count())
+
+
+def check_device_error() -> None:
+    """Synchronises and raises if a kernel gave up on a pipeline wait (then clears it)."""
+    code = ctypes.c_int(0)
+    _check(load().b2g_check_device_error(ctypes.byref(code)))
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise B2GError("all tensors must be CUDA tensors")
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, epilogue: str = "none", gate: torch.Tensor | None = None,
+         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out[M, N] = epilogue(x[M, K] . w[N, K]^T + bias) on the tensor-core path.
+
+    x, w: 2-D, unit stride along K (row strides may exceed K).  epilogue: "none", "gelu"
+    (tanh GELU) or "gated_residual" (out is an F32 residual updated in place:
+    out += gate * (x.w^T + bias)).  Runs on `stream` (default: torch's current stream).
+    """
+    lib = load()
+    _require_cuda(x, w, bias, out, gate)
+    if x.dim() != 2 or w.dim() != 2 or x.stride(1) != 1 or w.stride(1) != 1:
+        raise B2GError("gemm: x and w must be 2-D with unit stride along K")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise B2GError(f"gemm: K mismatch {tuple(x.shape)} vs {tuple(w.shape)}")
+    epi = _EPILOGUES[epilogue]
+    if out is None:
+        if epi == EPI_GATED_RESIDUAL:
+            raise B2GError("gemm: gated_residual needs `out` (the residual)")
+        out = torch.empty((M, N), device=x.device, dtype=out_dtype or torch.float32)
+    if out.dim() != 2 or out.shape != (M, N) or out.stride(1) != 1:
+        raise B2GError("gemm: out must be [M, N] with unit column stride")
+    d = GemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.a, d.a_dtype, d.lda = x.data_ptr(), _TORCH_TO_B2G[x.dtype], x.stride(0) if M > 1 else K
+    d.b, d.b_dtype, d.ldb = w.data_ptr(), _TORCH_TO_B2G[w.dtype], w.stride(0) if N > 1 else K
+    d.bias = _ptr(bias)
+    d.bias_dtype = _TORCH_TO_B2G[bias.dtype] if bias is not None else F32
+    d.d, d.d_dtype, d.ldd = out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0) if M > 1 else N
+    d.epilogue = epi
+    d.gate = _ptr(gate)
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
+    return out
+
+
+def linear_lt(M: int, K: int, N: int, x: torch.Tensor, x_type: int, w: torch.Tensor, w_type: int,
+              bias: torch.Tensor | None, out: torch.Tensor) -> None:
+    """linear_lt (cublas_ops.cuh:214): out[M,N] F32 = x[M,K] . w[N,K]^T + bias (F32 or None).
+
+    x_type/w_type are cudaDataType_t codes (CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF); runs on the
+    legacy default stream like the reference.
+    """
+    lib = load()
+    _require_cuda(x, w, bias, out)
+    _check(lib.b2g_linear_lt(M, K, N, x.data_ptr(), x_type, w.data_ptr(), w_type, _ptr(bias), out.data_ptr()))
+
+
+def linear(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None, output: torch.Tensor) -> None:
+    """linear (cublas_ops.cuh:359): output (F32, numel M*N) = x . W^T + bias.
+
+    M = x.numel() / x.shape[-1].  Like the reference, the bias is used only when it is an F32
+    tensor, and F32 activations with BF16/FP16 weights are rounded to the weight dtype first.
+    """
+    lib = load()
+    _require_cuda(x, W, bias, output)
+    if W.dim() != 2 or x.shape[-1] != W.shape[1]:
+        raise B2GError("linear: W must be [N, K] with K = x.shape[-1]")
+    K = x.shape[-1]
+    M = x.numel() // K if K else 0
+    N = W.shape[0]
+    if output.numel() != M * N or output.dtype != torch.float32:
+        raise B2GError("linear: output must be F32 with M*N elements")
+    if not (x.is_contiguous() and W.is_contiguous() and output.is_contiguous()):
+        raise B2GError("linear: tensors must be contiguous")
+    b = bias if (bias is not None and bias.dtype == torch.float32) else None
+    xt, wt = x.dtype, W.dtype
+    if not (xt == wt or (xt == torch.float32 and wt in (torch.bfloat16, torch.float16))):
+        raise B2GError(f"Unsupported dtype combo in linear: x={xt} W={wt}")
+    d = GemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.a, d.a_dtype, d.lda = x.data_ptr(), _TORCH_TO_B2G[xt], K
+    d.b, d.b_dtype, d.ldb = W.data_ptr(), _TORCH_TO_B2G[wt], K
+    d.bias, d.bias_dtype = _ptr(b), F32
+    d.d, d.d_dtype, d.ldd = output.data_ptr(), F32, N
+    d.epilogue = EPI_NONE
+    _check(lib.b2g_gemm(ctypes.byref(d), ctypes.c_void_p(0)))
+
+
+def linear_gated_residual(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None,
+                          residual_inout: torch.Tensor, gate: torch.Tensor, M: int, N_out: int) -> None:
+    """linear_gated_residual (cublas_ops.cuh:684): residual += gate * (x . W^T + bias), one kernel."""
+    lib = load()
+    _require_cuda(x, W, bias, residual_inout, gate)
+    K = x.shape[-1]
+    b = bias if (bias is not None and bias.dtype == torch.float32) else None
+    _check(lib.b2g_linear_gated_residual(x.data_ptr(), _TORCH_TO_CUDA[x.dtype], W.data_ptr(),
+                                         _TORCH_TO_CUDA[W.dtype], _ptr(b), residual_inout.data_ptr(),
+                                         gate.data_ptr(), M, K, N_out))
+
+
+def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None:
+    """batched_matmul_Bt (cublas_ops.cuh:558): C[b] = A[b] . B[b]^T, F32, operands rounded to bf16."""
+    lib = load()
+    _require_cuda(A, B, C)
+    if A.dim() != 3 or B.dim() != 3 or C.dim() != 3:
+        raise B2GError("batched_matmul_Bt: 3-D tensors expected")
+    batch, M, K = A.shape
+    N = B.shape[1]
+    if B.shape != (batch, N, K) or C.shape != (batch, M, N):
+        raise B2GError("batched_matmul_Bt: shape mismatch")
+    if not all(t.dtype == torch.float32 and t.is_contiguous() for t in (A, B, C)):
+        raise B2GError("batched_matmul_Bt: contiguous F32 tensors expected")
+    _check(lib.b2g_batched_matmul_Bt(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, K, N))

@@ -1,0 +1,277 @@
+// capi.cu — the extern "C" entry points of libb2g.so (declared in include/b2g.h), plus the
+// library state they share: last-error message, per-device info, the device error word
+// and the cast workspace.
+#include <cuda_runtime.h>
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include "engine.cuh"
+
+namespace b2g {
+
+namespace {
+
+// Kernels OR a role code in here when a pipeline wait exceeds its limit (ptx_sm100.cuh).
+__device__ int g_device_error_word = 0;
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_devices[kMaxDevices];
+
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int device = -1;
+};
+Workspace g_ws[kMaxDevices];
+
+b2g_dtype from_cuda_type(cudaDataType_t t, bool* ok) {
+  *ok = true;
+  switch (t) {
+    case CUDA_R_32F: return B2G_F32;
+    case CUDA_R_16F: return B2G_F16;
+    case CUDA_R_16BF: return B2G_BF16;
+    default: *ok = false; return B2G_F32;
+  }
+}
+
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+}  // namespace
+
+b2g_status set_error(b2g_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+b2g_status check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return B2G_OK;
+  return set_error(B2G_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+b2g_status device_info(DeviceInfo** out) {
+  int dev = -1;
+  b2g_status s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (s != B2G_OK) return s;
+  if (dev < 0 || dev >= kMaxDevices) return set_error(B2G_ERR_NO_DEVICE, "device ordinal out of range");
+  DeviceInfo& d = g_devices[dev];
+  if (d.device != dev) {
+    cudaDeviceProp prop;
+    if ((s = check_cuda(cudaGetDeviceProperties(&prop, dev), "cudaGetDeviceProperties")) != B2G_OK) return s;
+    if (prop.major != 10 || prop.minor != 0)
+      return set_error(B2G_ERR_NO_DEVICE, "device " + std::to_string(dev) + " is sm_" + std::to_string(prop.major) +
+                                              std::to_string(prop.minor) + "; this library is built for sm_100a only");
+    void* ew = nullptr;
+    if ((s = check_cuda(cudaGetSymbolAddress(&ew, g_device_error_word), "cudaGetSymbolAddress(error word)")) != B2G_OK)
+      return s;
+    d.num_sms = prop.multiProcessorCount;
+    d.cc_major = prop.major;
+    d.cc_minor = prop.minor;
+    d.err_word = static_cast<int*>(ew);
+    d.device = dev;
+  }
+  *out = &d;
+  return B2G_OK;
+}
+
+b2g_status workspace_get(size_t bytes, void** ptr) {
+  int dev = -1;
+  b2g_status s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  if (s != B2G_OK) return s;
+  Workspace& w = g_ws[dev];
+  if (w.bytes < bytes) {
+    if (w.ptr) {
+      // The old buffer may still be read by queued kernels.
+      if ((s = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize (workspace grow)")) != B2G_OK) return s;
+      cudaFree(w.ptr);
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    const size_t want = static_cast<size_t>(round_up(static_cast<int64_t>(bytes), 1 << 20));
+    if ((s = check_cuda(cudaMalloc(&w.ptr, want), "cudaMalloc (workspace)")) != B2G_OK) return s;
+    w.bytes = want;
+    w.device = dev;
+  }
+  *ptr = w.ptr;
+  return B2G_OK;
+}
+
+void workspace_release() {
+  for (auto& w : g_ws) {
+    if (w.ptr) {
+      int cur = -1;
+      cudaGetDevice(&cur);
+      cudaSetDevice(w.device);
+      cudaDeviceSynchronize();
+      cudaFree(w.ptr);
+      cudaSetDevice(cur);
+    }
+    w = Workspace{};
+  }
+}
+
+// Runs one (possibly batched) GEMM, converting F32 activations to the weight dtype first
+// when the weights are 16-bit, exactly as linear() does before calling cuBLASLt.
+b2g_status run_gemm(GemmProblem p, cudaStream_t st) {
+  if (p.M == 0 || p.N == 0 || p.batch == 0) return B2G_OK;
+  if (p.a_dtype == B2G_F32 && (p.b_dtype == B2G_BF16 || p.b_dtype == B2G_F16) && p.K > 0) {
+    const int64_t kp = round_up(p.K, 8);  // TMA row stride must be a multiple of 16 bytes
+    void* ws = nullptr;
+    b2g_status s = workspace_get(static_cast<size_t>(p.batch * p.M * kp) * 2, &ws);
+    if (s != B2G_OK) return s;
+    s = cast_f32_to_16(static_cast<const float*>(p.a), ws, p.b_dtype, p.batch, p.M, p.K, p.lda,
+                       p.batch > 1 ? p.a_bstride : 0, kp, p.M * kp, st);
+    if (s != B2G_OK) return s;
+    p.a = ws;
+    p.a_dtype = p.b_dtype;
+    p.lda = kp;
+    p.a_bstride = p.M * kp;
+  }
+  if (p.K > 0 && tc_gemm_supported(p, nullptr)) return tc_gemm_launch(p, st);
+  return simt_gemm_launch(p, st);
+}
+
+}  // namespace b2g
+
+using namespace b2g;
+
+extern "C" {
+
+b2g_status b2g_init(void) {
+  DeviceInfo* d = nullptr;
+  return device_info(&d);
+}
+
+b2g_status b2g_shutdown(void) {
+  workspace_release();
+  return B2G_OK;
+}
+
+const char* b2g_last_error(void) { return g_last_error.c_str(); }
+
+const char* b2g_version(void) { return "b2g 0.1 (sm_100a tcgen05)"; }
+
+uint64_t b2g_launch_count(void) { return g_launches.load(); }
+
+b2g_status b2g_gemm(const b2g_gemm_desc* d, void* stream) {
+  if (!d) return set_error(B2G_ERR_INVALID, "b2g_gemm: null descriptor");
+  if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, "b2g_gemm: negative size");
+  if (d->M == 0 || d->N == 0) return B2G_OK;
+  if (!d->d || (d->K > 0 && (!d->a || !d->b))) return set_error(B2G_ERR_INVALID, "b2g_gemm: null operand");
+  if (d->K > 0 && (d->lda < d->K || d->ldb < d->K)) return set_error(B2G_ERR_INVALID, "b2g_gemm: lda/ldb < K");
+  if (d->ldd < d->N) return set_error(B2G_ERR_INVALID, "b2g_gemm: ldd < N");
+  if (d->epilogue == B2G_EPI_GATED_RESIDUAL && (!d->gate || d->d_dtype != B2G_F32))
+    return set_error(B2G_ERR_INVALID, "b2g_gemm: gated residual needs a gate and an F32 output");
+  if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_GATED_RESIDUAL)
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: unknown epilogue");
+  if (d->a_dtype == B2G_E4M3 || d->b_dtype == B2G_E4M3 || d->d_dtype == B2G_E4M3)
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: E4M3 operands are not implemented");
+  const bool ab16 = d->b_dtype == B2G_BF16 || d->b_dtype == B2G_F16;
+  if (!(d->a_dtype == d->b_dtype || (d->a_dtype == B2G_F32 && ab16)))
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: unsupported operand dtype combination");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  GemmProblem p;
+  p.M = d->M; p.N = d->N; p.K = d->K;
+  p.a = d->a; p.a_dtype = d->a_dtype; p.lda = d->lda;
+  p.b = d->b; p.b_dtype = d->b_dtype; p.ldb = d->ldb;
+  p.bias = d->bias; p.bias_dtype = d->bias_dtype;
+  p.d = d->d; p.d_dtype = d->d_dtype; p.ldd = d->ldd;
+  p.epilogue = d->epilogue;
+  p.gate = d->gate;
+  return run_gemm(p, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_linear_lt_stream(int64_t M, int64_t K, int64_t N, const void* x_data, cudaDataType_t x_type,
+                                const void* w_data, cudaDataType_t w_type, const void* bias_data, void* out_data,
+                                void* stream) {
+  bool okx = false, okw = false;
+  const b2g_dtype xt = from_cuda_type(x_type, &okx), wt = from_cuda_type(w_type, &okw);
+  if (!okx || !okw || xt != wt) return set_error(B2G_ERR_UNSUPPORTED, "b2g_linear_lt: x_type and w_type must be equal "
+                                                                     "and one of CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF");
+  b2g_gemm_desc d{};
+  d.M = M; d.N = N; d.K = K;
+  d.a = x_data; d.a_dtype = xt; d.lda = K;
+  d.b = w_data; d.b_dtype = wt; d.ldb = K;
+  d.bias = bias_data; d.bias_dtype = B2G_F32;
+  d.d = out_data; d.d_dtype = B2G_F32; d.ldd = N;
+  d.epilogue = B2G_EPI_NONE;
+  return b2g_gemm(&d, stream);
+}
+
+b2g_status b2g_linear_lt(int64_t M, int64_t K, int64_t N, const void* x_data, cudaDataType_t x_type,
+                         const void* w_data, cudaDataType_t w_type, const void* bias_data, void* out_data) {
+  return b2g_linear_lt_stream(M, K, N, x_data, x_type, w_data, w_type, bias_data, out_data, nullptr);
+}
+
+b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type, const void* w, cudaDataType_t w_type,
+                                     const float* bias, float* residual_inout, const float* gate, int64_t M, int64_t K,
+                                     int64_t N_out) {
+  bool okx = false, okw = false;
+  const b2g_dtype xt = from_cuda_type(x_type, &okx), wt = from_cuda_type(w_type, &okw);
+  if (!okx || !okw || (wt != B2G_BF16 && wt != B2G_F16) || !(xt == wt || xt == B2G_F32))
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_linear_gated_residual: w must be BF16/F16 and x F32 or w's dtype");
+  b2g_gemm_desc d{};
+  d.M = M; d.N = N_out; d.K = K;
+  d.a = x; d.a_dtype = xt; d.lda = K;
+  d.b = w; d.b_dtype = wt; d.ldb = K;
+  d.bias = bias; d.bias_dtype = B2G_F32;
+  d.d = residual_inout; d.d_dtype = B2G_F32; d.ldd = N_out;
+  d.epilogue = B2G_EPI_GATED_RESIDUAL;
+  d.gate = gate;
+  return b2g_gemm(&d, nullptr);
+}
+
+b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
+                                 int64_t N) {
+  if (batch < 0 || M < 0 || K < 0 || N < 0) return set_error(B2G_ERR_INVALID, "b2g_batched_matmul_Bt: negative size");
+  if (batch == 0 || M == 0 || N == 0) return B2G_OK;
+  if (!A || !B || !C) return set_error(B2G_ERR_INVALID, "b2g_batched_matmul_Bt: null operand");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  // CUBLAS_COMPUTE_32F_FAST_16BF semantics: both operands rounded to bf16, fp32 accumulate.
+  const int64_t kp = round_up(K > 0 ? K : 1, 8);
+  const size_t a_bytes = static_cast<size_t>(round_up(batch * M * kp * 2, 256));
+  const size_t b_bytes = static_cast<size_t>(batch * N * kp * 2);
+  void* ws = nullptr;
+  if ((s = workspace_get(a_bytes + b_bytes, &ws)) != B2G_OK) return s;
+  void* wa = ws;
+  void* wb = static_cast<char*>(ws) + a_bytes;
+  cudaStream_t st = nullptr;
+  if ((s = cast_f32_to_16(A, wa, B2G_BF16, batch, M, K, K, M * K, kp, M * kp, st)) != B2G_OK) return s;
+  if ((s = cast_f32_to_16(B, wb, B2G_BF16, batch, N, K, K, N * K, kp, N * kp, st)) != B2G_OK) return s;
+  GemmProblem p;
+  p.M = M; p.N = N; p.K = K; p.batch = batch;
+  p.a = wa; p.a_dtype = B2G_BF16; p.lda = kp; p.a_bstride = M * kp;
+  p.b = wb; p.b_dtype = B2G_BF16; p.ldb = kp; p.b_bstride = N * kp;
+  p.d = C; p.d_dtype = B2G_F32; p.ldd = N; p.d_bstride = M * N;
+  return run_gemm(p, st);
+}
+
+b2g_status b2g_check_device_error(int* code) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  if ((s = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) != B2G_OK) return s;
+  int v = 0;
+  if ((s = check_cuda(cudaMemcpy(&v, dev->err_word, sizeof(int), cudaMemcpyDeviceToHost), "read error word")) != B2G_OK)
+    return s;
+  if (code) *code = v;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpy(dev->err_word, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    return set_error(B2G_ERR_DEVICE_TIMEOUT, "a tensor-core kernel gave up waiting on its pipeline (code " +
+                                                 std::to_string(v) + ")");
+  }
+  return B2G_OK;
+}
+
+}  // extern "C"

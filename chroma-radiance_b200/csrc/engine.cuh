@@ -1,0 +1,54 @@
+// engine.cuh — internal declarations shared by the engine's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <string>
+#include "../../include/b2g.h"
+
+namespace b2g {
+
+// Normalised problem handed from the C ABI to a kernel launcher.  All pointers are device
+// pointers; strides are in elements.  A GEMM with batch > 1 uses the *_bstride fields.
+struct GemmProblem {
+  int64_t M = 0, N = 0, K = 0, batch = 1;
+  const void* a = nullptr; b2g_dtype a_dtype = B2G_BF16; int64_t lda = 0, a_bstride = 0;
+  const void* b = nullptr; b2g_dtype b_dtype = B2G_BF16; int64_t ldb = 0, b_bstride = 0;
+  const void* bias = nullptr; b2g_dtype bias_dtype = B2G_F32;
+  void* d = nullptr; b2g_dtype d_dtype = B2G_F32; int64_t ldd = 0, d_bstride = 0;
+  b2g_epilogue epilogue = B2G_EPI_NONE;
+  const float* gate = nullptr;
+};
+
+// Records a message for b2g_last_error() and returns `st`.
+b2g_status set_error(b2g_status st, const std::string& msg);
+b2g_status check_cuda(cudaError_t e, const char* what);
+
+// Per-device state resolved on first use of a device.
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int cc_major = 0, cc_minor = 0;
+  int* err_word = nullptr;  // device address of the kernels' error word
+};
+b2g_status device_info(DeviceInfo** out);
+
+// Counts launches of this library's kernels (reported by b2g_launch_count).
+void note_launch(uint64_t n = 1);
+
+// Workspace (device memory owned by the library, grown on demand, never shrunk).
+b2g_status workspace_get(size_t bytes, void** ptr);
+void workspace_release();
+
+// True if the tensor-core path can run this problem (dtypes, strides, alignment).
+bool tc_gemm_supported(const GemmProblem& p, std::string* why);
+b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
+
+// Exact-fp32 CUDA-core path for everything the tensor-core path does not take.
+b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st);
+
+// Elementwise F32 -> bf16/fp16 conversion of `batch` row blocks (strides in elements).
+b2g_status cast_f32_to_16(const float* src, void* dst, b2g_dtype dst_dtype, int64_t batch, int64_t rows,
+                          int64_t cols, int64_t src_ld, int64_t src_bs, int64_t dst_ld, int64_t dst_bs,
+                          cudaStream_t st);
+
+}  // namespace b2g

@@ -1,0 +1,131 @@
+/*
+ * b2g.h — C ABI of the B200 GEMM engine for Chroma Radiance and its T5-XXL encoder.
+ *
+ * Every entry point takes plain device pointers, sizes and an optional CUDA stream
+ * (passed as `void*`, NULL = legacy default stream 0, which is what every call in the
+ * reference uses).  Nothing here allocates per call: a workspace for F32->bf16
+ * activation casts is created on first need and reused (it only grows).
+ *
+ * Layout convention (row-major, the reference's convention):
+ *     X  [M, K]  activations, row stride lda (elements)
+ *     W  [N, K]  weights,     row stride ldb (elements)   -> D = X . W^T
+ *     D  [M, N]  output,      row stride ldd (elements)
+ *
+ * Errors: every call returns a b2g_status; b2g_last_error() gives the message.  The
+ * reference instead prints and calls exit(1) (cublas_ops.cuh:73-79, :496-499); the C++
+ * drop-in header (chroma-radiance_b200/dropin/cublas_ops.cuh) maps a non-OK status back
+ * to that behaviour.
+ *
+ * Thread safety: none, like the reference (single host thread, global state).
+ */
+#ifndef B2G_H
+#define B2G_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <library_types.h> /* cudaDataType_t: plain C enum from the CUDA toolkit */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  B2G_OK = 0,
+  B2G_ERR_INVALID = 1,       /* bad argument (null pointer, negative size, shape mismatch) */
+  B2G_ERR_UNSUPPORTED = 2,   /* dtype combination or epilogue the engine does not implement */
+  B2G_ERR_CUDA = 3,          /* a CUDA runtime/driver call failed */
+  B2G_ERR_NO_DEVICE = 4,     /* no sm_100 device, or the library was built without it */
+  B2G_ERR_DEVICE_TIMEOUT = 5 /* a kernel gave up waiting on a pipeline barrier (see below) */
+} b2g_status;
+
+typedef enum {
+  B2G_F32 = 0,
+  B2G_F16 = 1,
+  B2G_BF16 = 2,
+  B2G_E4M3 = 3
+} b2g_dtype;
+
+typedef enum {
+  B2G_EPI_NONE = 0,           /* D = acc (+ bias)                                   */
+  B2G_EPI_GELU = 1,           /* D = gelu_tanh(acc (+ bias))                        */
+  B2G_EPI_GATED_RESIDUAL = 2  /* D[m,n] (F32, read-modify-write) += gate[n] * (acc (+ bias)) */
+} b2g_epilogue;
+
+/* One GEMM with a fused epilogue.  a/b dtypes: (BF16,BF16), (F16,F16) run on the
+ * tcgen05 tensor-core path; (F32,BF16) and (F32,F16) cast X first (as the reference's
+ * linear() does, cublas_ops.cuh:484-495); (F32,F32) runs an exact-fp32 path.  */
+typedef struct {
+  int64_t M, N, K;
+  const void* a; b2g_dtype a_dtype; int64_t lda;   /* X [M,K] */
+  const void* b; b2g_dtype b_dtype; int64_t ldb;   /* W [N,K] */
+  const void* bias; b2g_dtype bias_dtype;          /* [N] (F32 or BF16) or NULL */
+  void* d; b2g_dtype d_dtype; int64_t ldd;         /* D [M,N]: F32, BF16 or F16 */
+  b2g_epilogue epilogue;
+  const float* gate;                               /* [N], B2G_EPI_GATED_RESIDUAL only */
+} b2g_gemm_desc;
+
+/* Library setup.  Replaces init_cublas() (cublas_ops.cuh:152-159): selects nothing,
+ * queries the current device, checks it is sm_100, sets kernel attributes. Idempotent. */
+b2g_status b2g_init(void);
+/* Frees the cast workspace.  The reference never frees its handles; this is extra. */
+b2g_status b2g_shutdown(void);
+/* Message for the last non-OK status returned on this host thread's library state. */
+const char* b2g_last_error(void);
+/* Engine version string. */
+const char* b2g_version(void);
+
+/* General fused GEMM.  New entry point (no reference counterpart beyond linear_lt). */
+b2g_status b2g_gemm(const b2g_gemm_desc* desc, void* stream);
+
+/* out[M,N] (F32) = x[M,K] . w[N,K]^T + bias[N] (F32, may be NULL).
+ * Same arguments, meaning and dtype rules as the reference's
+ *   static void linear_lt(int64_t M, int64_t K, int64_t N, const void* x_data,
+ *       cudaDataType_t x_type, const void* w_data, cudaDataType_t w_type,
+ *       const void* bias_data, void* out_data)          cublas_ops.cuh:214-288
+ * x_type == w_type in {CUDA_R_16BF, CUDA_R_16F, CUDA_R_32F}; runs on stream 0. */
+b2g_status b2g_linear_lt(int64_t M, int64_t K, int64_t N,
+                         const void* x_data, cudaDataType_t x_type,
+                         const void* w_data, cudaDataType_t w_type,
+                         const void* bias_data, void* out_data);
+
+/* Same as b2g_linear_lt on an explicit stream. */
+b2g_status b2g_linear_lt_stream(int64_t M, int64_t K, int64_t N,
+                                const void* x_data, cudaDataType_t x_type,
+                                const void* w_data, cudaDataType_t w_type,
+                                const void* bias_data, void* out_data, void* stream);
+
+/* residual[M,N_out] (F32, in place) += gate[N_out] * (x[M,K] . w[N_out,K]^T + bias).
+ * Replaces the BF16 branch of
+ *   static void linear_gated_residual(const Tensor& x, const Tensor& W, const Tensor* bias,
+ *       float* residual_inout, const float* gate, int64_t M, int64_t N_out)
+ *                                                        cublas_ops.cuh:684-723
+ * which runs linear() into a temporary and then gated_residual_cuda (kernels.cu:942-968);
+ * here it is one kernel.  x dtype: F32 (cast to w's dtype first, as linear() does), BF16
+ * or F16; w: BF16 or F16; bias: F32 or NULL.  Stream 0. */
+b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type,
+                                     const void* w, cudaDataType_t w_type,
+                                     const float* bias, float* residual_inout,
+                                     const float* gate, int64_t M, int64_t K, int64_t N_out);
+
+/* C[b] = A[b] . B[b]^T for b in [0,batch); A [batch,M,K], B [batch,N,K], C [batch,M,N],
+ * all F32, densely packed.  Replaces
+ *   static void batched_matmul_Bt(const Tensor& A, const Tensor& B, Tensor& C)
+ *                                                        cublas_ops.cuh:558-585
+ * (cuBLAS CUBLAS_COMPUTE_32F_FAST_16BF: operands rounded to bf16, fp32 accumulate;
+ * this engine does the same rounding).  Stream 0. */
+b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
+                                 int64_t batch, int64_t M, int64_t K, int64_t N);
+
+/* Reads and clears the device-side error word that the tensor-core kernels set when a
+ * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
+ * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the
+ * raw word (which role gave up), may be NULL. */
+b2g_status b2g_check_device_error(int* code);
+
+/* Number of this library's kernels launched since load (host-side counter). */
+uint64_t b2g_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2G_H */

@@ -1,0 +1,194 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes access to the two checkers built by oracle/Makefile.
+
+  Oracle (liboracle.so)   fp32 C restatement of the reference's GEMM path, numpy in/out.
+  Ref    (_ref/libref_cublaslt.so)  the reference's own cublas_ops.cuh / kernels.cu compiled
+                           from its sources; device pointers in, runs on the GPU.
+
+Only tests/, __graft_entry__.smoke() and bench.py (its CPU-baseline leg and its
+--impl reference arm) use this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_PATH = HERE / "liboracle.so"
+REF_PATH = HERE / "_ref" / "libref_cublaslt.so"
+
+F32, F16, BF16 = 0, 1, 2          # reference DType codes (tensor.cuh:116)
+CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF = 0, 2, 14
+
+_c_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+
+def _np_ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+class Oracle:
+    """fp32 CPU oracle (oracle.c)."""
+
+    def __init__(self, path: str | os.PathLike = ORACLE_PATH):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle`")
+        lib = ctypes.CDLL(str(path))
+        lib.oracle_linear.argtypes = [_i64, _i64, _i64, _c_p, ctypes.c_int, _i64, _c_p, ctypes.c_int, _i64, _c_p,
+                                      _c_p, _i64, ctypes.c_int]
+        lib.oracle_linear.restype = ctypes.c_int
+        lib.oracle_batched_matmul_bt.argtypes = [_c_p, _c_p, _c_p, _i64, _i64, _i64, _i64, ctypes.c_int,
+                                                 ctypes.c_int]
+        lib.oracle_batched_matmul_bt.restype = ctypes.c_int
+        for name in ("oracle_gelu",):
+            getattr(lib, name).argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_gelu_to_bf16.argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_gated_residual.argtypes = [_c_p, _c_p, _c_p, _c_p, _i64, _i64]
+        lib.oracle_modulate.argtypes = [_c_p, _c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
+        lib.oracle_rms_norm.argtypes = [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
+        lib.oracle_round.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
+        lib.oracle_f32_to_bf16_array.argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_f32_to_f16_array.argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_to_f32.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
+        lib.oracle_num_threads.restype = ctypes.c_int
+        self.lib = lib
+
+    def num_threads(self) -> int:
+        return int(self.lib.oracle_num_threads())
+
+    # --- formats -----------------------------------------------------------------
+    def to_bf16_bits(self, a: np.ndarray) -> np.ndarray:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        out = np.empty(a.shape, dtype=np.uint16)
+        self.lib.oracle_f32_to_bf16_array(_np_ptr(a), _np_ptr(out), a.size)
+        return out
+
+    def to_f16_bits(self, a: np.ndarray) -> np.ndarray:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        out = np.empty(a.shape, dtype=np.uint16)
+        self.lib.oracle_f32_to_f16_array(_np_ptr(a), _np_ptr(out), a.size)
+        return out
+
+    def to_f32(self, bits: np.ndarray, dtype: int) -> np.ndarray:
+        bits = np.ascontiguousarray(bits)
+        out = np.empty(bits.shape, dtype=np.float32)
+        self.lib.oracle_to_f32(_np_ptr(bits), dtype, _np_ptr(out), bits.size)
+        return out
+
+    def round(self, a: np.ndarray, dtype: int) -> np.ndarray:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        out = np.empty_like(a)
+        self.lib.oracle_round(_np_ptr(a), dtype, _np_ptr(out), a.size)
+        return out
+
+    # --- GEMM --------------------------------------------------------------------
+    def linear(self, x: np.ndarray, xdt: int, w: np.ndarray, wdt: int, bias: np.ndarray | None = None,
+               nthreads: int = 0) -> np.ndarray:
+        """linear_lt semantics: x [M,K], w [N,K] given as F32 arrays or uint16 bit arrays of
+        dtype xdt/wdt; returns F32 [M,N] = x.w^T + bias."""
+        x = np.ascontiguousarray(x)
+        w = np.ascontiguousarray(w)
+        M, K = x.shape
+        N = w.shape[0]
+        out = np.empty((M, N), dtype=np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        rc = self.lib.oracle_linear(M, K, N, _np_ptr(x), xdt, K, _np_ptr(w), wdt, K, _np_ptr(b), _np_ptr(out), N,
+                                    nthreads)
+        if rc != 0:
+            raise MemoryError("oracle_linear")
+        return out
+
+    def batched_matmul_bt(self, A: np.ndarray, B: np.ndarray, round_bf16: bool = True,
+                          nthreads: int = 0) -> np.ndarray:
+        A = np.ascontiguousarray(A, dtype=np.float32)
+        B = np.ascontiguousarray(B, dtype=np.float32)
+        batch, M, K = A.shape
+        N = B.shape[1]
+        C = np.empty((batch, M, N), dtype=np.float32)
+        self.lib.oracle_batched_matmul_bt(_np_ptr(A), _np_ptr(B), _np_ptr(C), batch, M, K, N, int(round_bf16),
+                                          nthreads)
+        return C
+
+    # --- elementwise ---------------------------------------------------------------
+    def gelu(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        self.lib.oracle_gelu(_np_ptr(x), _np_ptr(out), x.size)
+        return out
+
+    def gelu_to_bf16(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(x.shape, dtype=np.uint16)
+        self.lib.oracle_gelu_to_bf16(_np_ptr(x), _np_ptr(out), x.size)
+        return out
+
+    def gated_residual(self, x: np.ndarray, y: np.ndarray, gate: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        gate = np.ascontiguousarray(gate, dtype=np.float32)
+        M, C = x.shape
+        out = np.empty_like(x)
+        self.lib.oracle_gated_residual(_np_ptr(x), _np_ptr(y), _np_ptr(gate), _np_ptr(out), M, C)
+        return out
+
+    def modulate(self, x, shift, scale, eps=1e-6):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        M, C = x.shape
+        self.lib.oracle_modulate(_np_ptr(x), _np_ptr(np.ascontiguousarray(shift, np.float32)),
+                                 _np_ptr(np.ascontiguousarray(scale, np.float32)), _np_ptr(out), M, C, eps)
+        return out
+
+    def rms_norm(self, x, scale, eps=1e-6):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty_like(x)
+        rows, C = x.shape
+        self.lib.oracle_rms_norm(_np_ptr(x), _np_ptr(np.ascontiguousarray(scale, np.float32)), _np_ptr(out), rows,
+                                 C, eps)
+        return out
+
+
+class Ref:
+    """The reference's own GEMM path (cuBLASLt), built from its sources; device pointers."""
+
+    def __init__(self, path: str | os.PathLike = REF_PATH):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} missing: it is built by `make -C oracle` where the reference "
+                                    "sources are present")
+        lib = ctypes.CDLL(str(path))
+        sig = {
+            "ref_init": [],
+            "ref_sync": [],
+            "ref_cublaslt_version": [],
+            "ref_linear_lt": [_i64, _i64, _i64, _c_p, ctypes.c_int, _c_p, ctypes.c_int, _c_p, _c_p],
+            "ref_linear": [_c_p, ctypes.c_int, _c_p, ctypes.c_int, _c_p, _c_p, _i64, _i64, _i64],
+            "ref_linear_gated_residual": [_c_p, ctypes.c_int, _c_p, ctypes.c_int, _c_p, _c_p, _c_p, _i64, _i64,
+                                          _i64],
+            "ref_batched_matmul_Bt": [_c_p, _c_p, _c_p, _i64, _i64, _i64, _i64],
+            "ref_gelu": [_c_p, _c_p, _i64],
+            "ref_gelu_to_bf16": [_c_p, _c_p, _i64],
+            "ref_gated_residual": [_c_p, _c_p, _c_p, _c_p, _i64, _i64],
+            "ref_f32_to_bf16": [_c_p, _c_p, _i64],
+            "ref_f32_to_fp16": [_c_p, _c_p, _i64],
+            "ref_modulate_to_bf16": [_c_p, _c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float],
+            "ref_rms_norm": [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float],
+            "ref_concat_last_dim_to_bf16": [_c_p, _c_p, _c_p, _i64, _i64, _i64],
+            "ref_bench_linear_lt": [_i64, _i64, _i64, ctypes.c_int, _c_p, _c_p, _c_p, ctypes.c_int, ctypes.c_int,
+                                    _i64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)],
+        }
+        for name, args in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        self.lib = lib
+        self.lib.ref_init()
+
+    def __getattr__(self, name):
+        return getattr(self.lib, "ref_" + name)
+
+
+def available() -> dict:
+    return {"oracle": ORACLE_PATH.exists(), "ref": REF_PATH.exists()}
