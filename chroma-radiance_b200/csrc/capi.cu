@@ -159,6 +159,12 @@ const char* b2g_version(void) { return "b2g 0.1 (sm_100a tcgen05)"; }
 
 uint64_t b2g_launch_count(void) { return g_launches.load(); }
 
+b2g_status b2g_set_gemm_variant(int variant) {
+  if (variant < -1 || variant > 2) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: variant in [-1, 2]");
+  tc_gemm_set_variant(variant, 1);
+  return B2G_OK;
+}
+
 b2g_status b2g_gemm(const b2g_gemm_desc* d, void* stream) {
   if (!d) return set_error(B2G_ERR_INVALID, "b2g_gemm: null descriptor");
   if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, "b2g_gemm: negative size");

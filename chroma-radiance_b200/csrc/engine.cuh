@@ -42,6 +42,9 @@ void workspace_release();
 // True if the tensor-core path can run this problem (dtypes, strides, alignment).
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
+// Kernel variant override for tests/tuning: -1 automatic, 0 = 1-CTA 128x128 tiles,
+// 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
+void tc_gemm_set_variant(int force_variant, int allow_pair);
 
 // Exact-fp32 CUDA-core path for everything the tensor-core path does not take.
 b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st);

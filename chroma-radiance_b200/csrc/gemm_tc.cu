@@ -321,7 +321,195 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------- 2-CTA variant
+//
+// A cluster of two CTAs (on two SMs) computes one 256x256 output tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  CTA r of the pair loads rows
+// [m0 + 128r, +128) of A and rows [n0 + 128r, +128) of B into its own shared memory; the
+// MMA, issued by CTA 0, reads both halves and leaves rows [m0 + 128r, +128) x 256 columns
+// of the accumulator in CTA r's TMEM.  Per SM this moves 32 KB of operands per 64-wide
+// k-block instead of 48 KB for a 1-CTA 128x256 tile with the same MMA time, and the
+// smaller stage allows a 6-deep ring.
+//   full[s]   (CTA 0 only)  both CTAs' TMA bytes for stage s; CTA 0 arms it for 64 KB.
+//   empty[s]  (each CTA)    the pair's MMAs reading stage s have retired (broadcast commit).
+//   tfull[a]  (each CTA)    accumulator a is complete (broadcast commit).
+//   tempty[a] (CTA 0 only)  all 8 epilogue warps of the pair have read accumulator a.
+template <int STAGES, int EPI, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const TcParams p) {
+  constexpr int BN = 256;                          // pair tile is 256 x 256
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;      // this CTA's 128 rows of A
+  constexpr uint32_t B_BYTES = 128 * kBK * 2;      // this CTA's 128 rows of B
+  constexpr uint32_t TMEM_COLS = 2 * BN;           // two 128-lane x 256-column accumulators
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* drain_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = static_cast<int>(cluster_id_x());
+  const int nclusters = static_cast<int>(num_clusters_x());
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barrier inits and the TMEM allocation are visible pair-wide
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last();
+      const uint64_t stream = policy_evict_first();
+      const uint64_t pa = p.a_keep ? keep : stream;
+      const uint64_t pb = p.a_keep ? stream : keep;
+      int stage = 0;
+      uint32_t phase = 0, issued = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += nclusters) {
+        int bz, mb, nb;
+        tile_coords(tile, p, bz, mb, nb);
+        const int arow = mb * 256 + static_cast<int>(rank) * 128;
+        const int brow = nb * 256 + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrWaitProducer)) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (A_BYTES + B_BYTES));
+          const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
+          tma_load_3d_pair(sA + stage * A_BYTES, &tmA, leader_full, kb * kBK, arow, bz, pa);
+          tma_load_3d_pair(sB + stage * B_BYTES, &tmB, leader_full, kb * kBK, brow, bz, pb);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        const uint32_t n = issued < static_cast<uint32_t>(STAGES) ? issued : static_cast<uint32_t>(STAGES);
+        for (uint32_t k = issued - n; k < issued; ++k) mbar_wait_drain(&full_bar[k % STAGES], (k / STAGES) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (CTA 0 only)
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = p.idesc;  // M=256, N=256
+      int stage = 0;
+      uint32_t phase = 0, local = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += nclusters, ++local) {
+        const uint32_t acc = local & 1u;
+        const uint32_t acc_phase = (local >> 1) & 1u;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kErrWaitMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_f16_pair(d_tmem, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
+                          (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_bcast(&empty_bar[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair_bcast(&tfull_bar[acc], 0x3);
+      }
+      if (!ok) {
+        umma_commit_pair(drain_bar);
+        mbar_wait_drain(drain_bar, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    uint32_t local = 0;
+    const uint32_t leader_tempty0 = map_to_cta(smem_u32(&tempty_bar[0]), 0);
+    const uint32_t leader_tempty1 = map_to_cta(smem_u32(&tempty_bar[1]), 0);
+    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
+      int bz, mb, nb;
+      tile_coords(tile, p, bz, mb, nb);
+      const uint32_t acc = local & 1u;
+      const uint32_t acc_phase = (local >> 1) & 1u;
+      const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int m = mb * 256 + static_cast<int>(rank) * 128 + row;
+      const uint32_t t0 = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t0 + c * 32, r);
+        tmem_wait_ld();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+        }
+        const int n0 = nb * BN + c * 32;
+        if (m < p.M && n0 < p.N) store_chunk<EPI, OUT>(p, bz, m, n0, r);
+      }
+    }
+  }
+
+  // Neither CTA may leave (or free TMEM) while its peer can still touch its shared memory
+  // or barriers: every role has finished, then both CTAs release the pair's TMEM.
+  tc_fence_before();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------- host side
+
+// Relative per-tile time of the 2-CTA kernel vs the 1-CTA 128x256 kernel (tuned on B200).
+constexpr double kPairSpeed = 0.85;
+int g_force_variant = -1;  // -1 auto, 0 = 1-CTA 128, 1 = 1-CTA 256, 2 = 2-CTA pair
+bool g_allow_pair = true;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -355,11 +543,9 @@ b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, in
   return B2G_OK;
 }
 
-template <int BN, int STAGES, int EPI, int OUT>
-b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid, cudaStream_t st) {
-  auto kern = tc_gemm_kernel<BN, STAGES, EPI, OUT>;
-  constexpr size_t smem = smem_bytes(BN, STAGES);
-  static_assert(smem <= 227 * 1024, "shared memory budget");
+template <typename Kern>
+b2g_status launch_kernel(Kern kern, size_t smem, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm,
+                         int grid, cudaStream_t st) {
   b2g_status s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "cudaFuncSetAttribute(tc_gemm)");
   if (s != B2G_OK) return s;
@@ -368,18 +554,33 @@ b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcPara
   return check_cuda(cudaGetLastError(), "tc_gemm launch");
 }
 
-template <int BN, int STAGES>
+// Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.
+template <bool PAIR, int BN, int STAGES, int EPI, int OUT>
+b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid, cudaStream_t st) {
+  if constexpr (PAIR) {
+    constexpr size_t smem = 1024 + static_cast<size_t>(STAGES) * (kBM * kBK * 2 + 128 * kBK * 2) + 256;
+    static_assert(smem <= 227 * 1024, "shared memory budget");
+    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT>, smem, ta, tb, prm, grid, st);
+  } else {
+    constexpr size_t smem = smem_bytes(BN, STAGES);
+    static_assert(smem <= 227 * 1024, "shared memory budget");
+    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT>, smem, ta, tb, prm, grid, st);
+  }
+}
+
+template <bool PAIR, int BN, int STAGES>
 b2g_status dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid,
                         b2g_epilogue epi, b2g_dtype out, cudaStream_t st) {
-  if (epi == B2G_EPI_GATED_RESIDUAL) return launch_one<BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32>(ta, tb, prm, grid, st);
+  if (epi == B2G_EPI_GATED_RESIDUAL)
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32>(ta, tb, prm, grid, st);
   if (epi == B2G_EPI_GELU) {
-    if (out == B2G_F32) return launch_one<BN, STAGES, B2G_EPI_GELU, OUT_F32>(ta, tb, prm, grid, st);
-    if (out == B2G_BF16) return launch_one<BN, STAGES, B2G_EPI_GELU, OUT_BF16>(ta, tb, prm, grid, st);
-    return launch_one<BN, STAGES, B2G_EPI_GELU, OUT_F16>(ta, tb, prm, grid, st);
+    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32>(ta, tb, prm, grid, st);
+    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16>(ta, tb, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16>(ta, tb, prm, grid, st);
   }
-  if (out == B2G_F32) return launch_one<BN, STAGES, B2G_EPI_NONE, OUT_F32>(ta, tb, prm, grid, st);
-  if (out == B2G_BF16) return launch_one<BN, STAGES, B2G_EPI_NONE, OUT_BF16>(ta, tb, prm, grid, st);
-  return launch_one<BN, STAGES, B2G_EPI_NONE, OUT_F16>(ta, tb, prm, grid, st);
+  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32>(ta, tb, prm, grid, st);
+  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16>(ta, tb, prm, grid, st);
+  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16>(ta, tb, prm, grid, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -411,25 +612,37 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   if ((s = get_encode()) != B2G_OK) return s;
 
   const int sms = dev->num_sms;
-  const long long mblocks = (p.M + kBM - 1) / kBM;
-  const long long t256 = p.batch * mblocks * ((p.N + 255) / 256);
-  const long long t128 = p.batch * mblocks * ((p.N + 127) / 128);
-  // Estimated time in units of one 128x256 tile: whole waves over the SMs.  A 128-wide
-  // tile does half the work of a 256-wide one but re-reads A, hence the 10% penalty.
+  const long long m128 = (p.M + 127) / 128, m256 = (p.M + 255) / 256;
+  const long long t128 = p.batch * m128 * ((p.N + 127) / 128);
+  const long long t256 = p.batch * m128 * ((p.N + 255) / 256);
+  const long long tpair = p.batch * m256 * ((p.N + 255) / 256);
+  const int pairs = sms / 2;
+  // Estimated time in units of one 128x256 tile on one SM at the 1-CTA kernel's rate:
+  // whole waves over the SMs.  A 128-wide tile does half the work of a 256-wide one but
+  // re-reads A (10% penalty); a 2-CTA pair tile is one such unit on two SMs and runs at a
+  // higher tensor-pipe utilisation (operand bandwidth per SM is a third lower).
   const double cost256 = static_cast<double>((t256 + sms - 1) / sms);
   const double cost128 = static_cast<double>((t128 + sms - 1) / sms) * 0.55;
-  const int bn = (p.N <= 128 || cost128 < cost256) ? 128 : 256;
+  const double costpair = static_cast<double>((tpair + pairs - 1) / pairs) * kPairSpeed;
+  enum { V128, V256, VPAIR } v;
+  if (p.N <= 128) v = V128;
+  else if (costpair <= cost256 && costpair <= cost128 && g_allow_pair) v = VPAIR;
+  else v = cost128 < cost256 ? V128 : V256;
+  if (g_force_variant >= 0) v = static_cast<decltype(v)>(g_force_variant);
+  const int bn = v == V128 ? 128 : 256;
+  const int tile_m = v == VPAIR ? 256 : kBM;
 
   TcParams prm{};
   prm.M = static_cast<int>(p.M);
   prm.N = static_cast<int>(p.N);
   prm.K = static_cast<int>(p.K);
   prm.batch = static_cast<int>(p.batch);
-  prm.num_m_blocks = static_cast<int>(mblocks);
+  prm.num_m_blocks = static_cast<int>((p.M + tile_m - 1) / tile_m);
   prm.num_n_blocks = static_cast<int>((p.N + bn - 1) / bn);
   prm.num_k_blocks = static_cast<int>((p.K + kBK - 1) / kBK);
   prm.num_tiles = prm.batch * prm.num_m_blocks * prm.num_n_blocks;
-  prm.group_m = prm.num_m_blocks <= 16 ? prm.num_m_blocks : 16;
+  const int group = v == VPAIR ? 8 : 16;
+  prm.group_m = prm.num_m_blocks <= group ? prm.num_m_blocks : group;
   prm.d = p.d;
   prm.ldd = p.ldd;
   prm.d_bstride = p.batch > 1 ? p.d_bstride : 0;
@@ -437,7 +650,7 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.gate = p.gate;
   prm.err = dev->err_word;
-  prm.idesc = idesc_f16(p.a_dtype == B2G_BF16, kBM, bn);
+  prm.idesc = idesc_f16(p.a_dtype == B2G_BF16, tile_m, bn);
   const int out_bytes = p.d_dtype == B2G_F32 ? 4 : 2;
   prm.vec_ok = aligned16(p.d) && ((p.ldd * out_bytes) % 16 == 0) &&
                (p.batch <= 1 || (p.d_bstride * out_bytes) % 16 == 0);
@@ -448,12 +661,22 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   CUtensorMap ta, tb;
   const int64_t a_bs = p.batch > 1 ? p.a_bstride : p.lda * p.M;
   const int64_t b_bs = p.batch > 1 ? p.b_bstride : p.ldb * p.N;
+  const uint32_t b_box = v == V128 ? 128u : (v == V256 ? 256u : 128u);
   if ((s = make_operand_map(&ta, p.a, p.a_dtype, p.K, p.M, p.lda, p.batch, a_bs, kBM)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tb, p.b, p.b_dtype, p.K, p.N, p.ldb, p.batch, b_bs, bn)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tb, p.b, p.b_dtype, p.K, p.N, p.ldb, p.batch, b_bs, b_box)) != B2G_OK) return s;
 
+  if (v == VPAIR) {
+    const int grid = 2 * static_cast<int>(prm.num_tiles < pairs ? prm.num_tiles : pairs);
+    return dispatch_epi<true, 256, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+  }
   const int grid = static_cast<int>(prm.num_tiles < sms ? prm.num_tiles : sms);
-  if (bn == 256) return dispatch_epi<256, 4>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
-  return dispatch_epi<128, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+  if (v == V256) return dispatch_epi<false, 256, 4>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+  return dispatch_epi<false, 128, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+}
+
+void tc_gemm_set_variant(int force_variant, int allow_pair) {
+  g_force_variant = force_variant;
+  g_allow_pair = allow_pair != 0;
 }
 
 }  // namespace b2g

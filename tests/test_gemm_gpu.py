@@ -1,0 +1,313 @@
+"""GPU parity of the engine's GEMM path against the C oracle, the reference's own cuBLASLt
+build, and a plain fp32 product, through the C ABI.
+
+Tolerance (north star): per GEMM, max|got - ref| / max|ref| <= 2e-3 for bf16 operands.  F32
+outputs are held to 1e-4 (fp32 accumulation order only).  A bf16 or fp16 *output* adds one
+rounding whose size no GEMM can avoid: half an ulp of the value, up to 2^-8 of max|ref| for
+bf16 when the largest value sits just above a power of two.  Those outputs are therefore
+checked element by element for correct rounding: |got - ref| <= ulp(ref)/2 + 1e-5 max|ref|
+(the second term is fp32 accumulation-order noise).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TOL_F32_OUT = 1e-4
+
+
+def seeded(shape, seed, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype).to(DEV)
+
+
+def fp32_ref(x, w, bias=None):
+    y = x.double() @ w.double().t()
+    if bias is not None:
+        y = y + bias.double()
+    return y
+
+
+def assert_rounded(got16: torch.Tensor, ref: torch.Tensor):
+    """got16 (bf16/fp16) is ref correctly rounded, up to fp32 accumulation noise."""
+    mant = 7 if got16.dtype == torch.bfloat16 else 10
+    g = got16.double().cpu()
+    r = ref.double().cpu()
+    mag = r.abs().clamp_min(torch.finfo(torch.float32).tiny)
+    ulp = torch.exp2(torch.floor(torch.log2(mag)) - mant)
+    bound = 0.5 * ulp + 1e-5 * r.abs().max()
+    excess = ((g - r).abs() - bound).max().item()
+    assert excess <= 0, f"rounding error exceeds half an ulp by {excess:.3e}"
+
+
+def check(out, ref):
+    if out.dtype == torch.float32:
+        assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) <= TOL_F32_OUT
+    else:
+        assert_rounded(out, ref)
+
+
+def gelu_t(y):
+    return 0.5 * y * (1 + torch.tanh(0.7978845608 * (y + 0.044715 * y ** 3)))
+
+
+SHAPES = [
+    # M, N, K
+    (128, 256, 64),        # one tile, one k-block
+    (256, 512, 1024),
+    (100, 200, 72),        # ragged M, N and K
+    (1, 8, 8),             # smallest
+    (7, 1000, 136),
+    (300, 130, 3000),      # K tail, N < 256 tile
+    (1536, 3072, 3072),    # single-block Q/K/V at 512^2
+    (512, 9216, 3072),     # double-block txt qkv
+    (1024, 3072, 12288),   # double-block img mlp2
+    (1536, 3072, 15360),   # single-block linear2
+    (344, 5120, 5120),     # approximator (skinny M)
+]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_gemm_bias_vs_fp64(engine, M, N, K, out_dtype):
+    x = seeded((M, K), M + N + K)
+    w = seeded((N, K), M * N + 1, 0.02)
+    bias = seeded((N,), 7, 0.02, torch.float32)
+    out = engine.gemm(x, w, bias, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    check(out, fp32_ref(x, w, bias))
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 700, 520), (1536, 3072, 3072), (100, 200, 72),
+                                   (513, 300, 3000)])
+def test_every_kernel_variant(engine, variant, M, N, K):
+    """Each tensor-core kernel (1-CTA 128/256-wide, 2-CTA pair) forced on ragged shapes."""
+    x = seeded((M, K), 3 * M + K)
+    w = seeded((N, K), 5 * N + K, 0.02)
+    bias = seeded((N,), 9, 0.02, torch.float32)
+    try:
+        engine.set_gemm_variant(variant)
+        out = engine.gemm(x, w, bias, out_dtype=torch.float32)
+        out16 = engine.gemm(x, w, bias, out_dtype=torch.bfloat16, epilogue="gelu")
+        torch.cuda.synchronize()
+    finally:
+        engine.set_gemm_variant(-1)
+    ref = fp32_ref(x, w, bias)
+    check(out, ref)
+    check(out16, gelu_t(ref))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(512, 4096, 4096), (512, 10240, 4096), (512, 4096, 10240), (19, 40, 136)])
+def test_gemm_t5_shapes_fp16_and_bf16(engine, dt, M, N, K):
+    x = seeded((M, K), 11, 1.0, dt)
+    w = seeded((N, K), 12, 0.02, dt)
+    out = engine.gemm(x, w, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), fp32_ref(x, w).cpu().numpy()) <= TOL_F32_OUT
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 12288, 3072), (100, 300, 64), (1536, 12288, 3072)])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_gelu_epilogue(engine, M, N, K, out_dtype):
+    x = seeded((M, K), 21)
+    w = seeded((N, K), 22, 0.02)
+    bias = seeded((N,), 23, 0.02, torch.float32)
+    out = engine.gemm(x, w, bias, out_dtype=out_dtype, epilogue="gelu")
+    torch.cuda.synchronize()
+    check(out, gelu_t(fp32_ref(x, w, bias)))
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 3072, 12288), (1536, 3072, 15360), (33, 70, 96)])
+def test_gemm_gated_residual_epilogue(engine, M, N, K):
+    x = seeded((M, K), 31)
+    w = seeded((N, K), 32, 0.02)
+    bias = seeded((N,), 33, 0.02, torch.float32)
+    resid = seeded((M, N), 34, 1.0, torch.float32)
+    gate = seeded((N,), 35, 1.0, torch.float32)
+    want = resid.double() + gate.double() * fp32_ref(x, w, bias)
+    engine.gemm(x, w, bias, out=resid, epilogue="gated_residual", gate=gate)
+    torch.cuda.synchronize()
+    assert rel_err(resid.cpu().numpy(), want.cpu().numpy()) <= TOL_F32_OUT
+
+
+def test_gemm_vs_c_oracle(engine, oracle):
+    """Same seeded bf16 inputs through the engine and the fp32 C oracle."""
+    M, N, K = 200, 384, 520
+    x = seeded((M, K), 41)
+    w = seeded((N, K), 42, 0.02)
+    bias = seeded((N,), 43, 0.02, torch.float32)
+    out = engine.gemm(x, w, bias, out_dtype=torch.float32)
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    wb = w.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = oracle.linear(xb, 2, wb, 2, bias.cpu().numpy())
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), want) <= TOL_F32_OUT
+
+
+@pytest.mark.parametrize("M,K,N", [(1536, 3072, 21504), (512, 3072, 9216), (37, 200, 72)])
+def test_linear_lt_vs_reference_cublaslt(engine, ref, M, K, N):
+    """b2g_linear_lt and the reference's linear_lt (cuBLASLt) on identical device buffers."""
+    x = seeded((M, K), 51)
+    w = seeded((N, K), 52, 0.02)
+    bias = seeded((N,), 53, 0.02, torch.float32)
+    mine = torch.empty((M, N), device=DEV)
+    theirs = torch.empty((M, N), device=DEV)
+    engine.linear_lt(M, K, N, x, engine.CUDA_R_16BF, w, engine.CUDA_R_16BF, bias, mine)
+    ref.linear_lt(M, K, N, x.data_ptr(), 14, w.data_ptr(), 14, bias.data_ptr(), theirs.data_ptr())
+    torch.cuda.synchronize()
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= 2e-3
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= TOL_F32_OUT
+
+
+def test_config1_bf16_out_vs_reference(engine, ref):
+    """BASELINE config 1 (linear1 GEMM+bias, seed 0): the engine's F32 output within the
+    north-star 2e-3 of the reference's, and its bf16 output the reference's correctly rounded."""
+    M, K, N = 1536, 3072, 21504
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn((M, K), generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn((N,), generator=g) * 0.02).to(torch.bfloat16).float().to(DEV)
+    mine = engine.gemm(x, w, bias, out_dtype=torch.bfloat16)
+    theirs = torch.empty((M, N), device=DEV)
+    ref.linear_lt(M, K, N, x.data_ptr(), 14, w.data_ptr(), 14, bias.data_ptr(), theirs.data_ptr())
+    mine32 = engine.gemm(x, w, bias, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert rel_err(mine32.cpu().numpy(), theirs.cpu().numpy()) <= 2e-3
+    assert_rounded(mine, theirs)
+
+
+@pytest.mark.parametrize("wdt", [torch.bfloat16, torch.float16])
+def test_linear_f32_activation_cast_matches_reference(engine, ref, wdt):
+    """linear() with F32 x and 16-bit W casts x first, in both implementations."""
+    M, K, N = 512, 4096, 1024
+    x = seeded((M, K), 61, 1.0, torch.float32)
+    w = seeded((N, K), 62, 0.02, wdt)
+    bias = seeded((N,), 63, 0.02, torch.float32)
+    mine = torch.empty((M, N), device=DEV)
+    theirs = torch.empty((M, N), device=DEV)
+    engine.linear(x, w, bias, mine)
+    wcode = 2 if wdt == torch.bfloat16 else 1
+    ref.linear(x.data_ptr(), 0, w.data_ptr(), wcode, bias.data_ptr(), theirs.data_ptr(), M, K, N)
+    torch.cuda.synchronize()
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= TOL_F32_OUT
+
+
+def test_linear_f32_f32_exact_path(engine, ref):
+    M, K, N = 64, 67, 96  # K=67 like the NeRF embedder: no TMA, exact fp32 CUDA-core path
+    x = seeded((M, K), 71, 1.0, torch.float32)
+    w = seeded((N, K), 72, 0.1, torch.float32)
+    bias = seeded((N,), 73, 0.02, torch.float32)
+    mine = torch.empty((M, N), device=DEV)
+    theirs = torch.empty((M, N), device=DEV)
+    engine.linear(x, w, bias, mine)
+    ref.linear(x.data_ptr(), 0, w.data_ptr(), 0, bias.data_ptr(), theirs.data_ptr(), M, K, N)
+    torch.cuda.synchronize()
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= 1e-5
+
+
+def test_linear_gated_residual_vs_reference(engine, ref):
+    M, K, N = 1024, 3072, 3072
+    x = seeded((M, K), 81, 1.0, torch.float32)   # attention output is F32 in the reference
+    w = seeded((N, K), 82, 0.02)
+    bias = seeded((N,), 83, 0.02, torch.float32)
+    gate = seeded((N,), 84, 1.0, torch.float32)
+    r0 = seeded((M, N), 85, 1.0, torch.float32)
+    mine, theirs = r0.clone(), r0.clone()
+    engine.linear_gated_residual(x, w, bias, mine, gate, M, N)
+    ref.linear_gated_residual(x.data_ptr(), 0, w.data_ptr(), 2, bias.data_ptr(), theirs.data_ptr(),
+                              gate.data_ptr(), M, K, N)
+    torch.cuda.synchronize()
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= TOL_F32_OUT
+
+
+BATCHED = [(64, 256, 64, 256), (5, 256, 256, 64), (3, 16, 64, 24), (2, 50, 70, 30)]
+
+
+@pytest.mark.parametrize("batch,M,K,N", BATCHED)
+def test_batched_matmul_bt_vs_oracle(engine, oracle, batch, M, K, N):
+    A = seeded((batch, M, K), 91, 1.0, torch.float32)
+    B = seeded((batch, N, K), 92, 1.0, torch.float32)
+    mine = torch.empty((batch, M, N), device=DEV)
+    engine.batched_matmul_Bt(A, B, mine)
+    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy(), round_bf16=True)
+    torch.cuda.synchronize()
+    got = mine.cpu().numpy()
+    for b in range(batch):
+        assert rel_err(got[b], want[b]) <= TOL_F32_OUT, f"batch {b}"
+
+
+@pytest.mark.parametrize("batch,M,K,N", BATCHED)
+def test_batched_matmul_bt_vs_reference(engine, ref, oracle, batch, M, K, N):
+    A = seeded((batch, M, K), 91, 1.0, torch.float32)
+    B = seeded((batch, N, K), 92, 1.0, torch.float32)
+    mine = torch.empty((batch, M, N), device=DEV)
+    theirs = torch.zeros((batch, M, N), device=DEV)
+    engine.batched_matmul_Bt(A, B, mine)
+    ref.batched_matmul_Bt(A.data_ptr(), B.data_ptr(), theirs.data_ptr(), batch, M, K, N)
+    torch.cuda.synchronize()
+    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy(), round_bf16=True)
+    t = theirs.cpu().numpy()
+    per_batch_ref = [rel_err(t[b], want[b]) for b in range(batch)]
+    assert rel_err(mine.cpu().numpy(), t) <= TOL_F32_OUT, f"reference vs oracle per batch: {per_batch_ref}"
+
+
+def test_strided_views_like_txt_img_rows(engine):
+    """Operands and outputs that are row-offset views of larger buffers (the reference's
+    txt/img views) with row strides larger than K / N."""
+    big_x = seeded((1536, 3200), 101)
+    x = big_x[512:, 64:64 + 3072]            # row stride 3200, base offset 128 B
+    w = seeded((3072, 3072), 102, 0.02)
+    big_out = torch.zeros((1536, 3328), device=DEV)
+    out = big_out[512:, 128:128 + 3072]
+    engine.gemm(x, w, None, out=out)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), fp32_ref(x, w).cpu().numpy()) <= TOL_F32_OUT
+    assert float(big_out[:512].abs().max()) == 0.0          # nothing written outside the view
+    assert float(big_out[512:, :128].abs().max()) == 0.0
+    assert float(big_out[512:, 128 + 3072:].abs().max()) == 0.0
+
+
+def test_unaligned_stride_uses_exact_fallback(engine):
+    x = seeded((50, 67), 111)            # K=67: row stride not a multiple of 8 elements
+    w = seeded((40, 67), 112, 0.1)
+    out = engine.gemm(x, w, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), fp32_ref(x, w).cpu().numpy()) <= 1e-5
+
+
+def test_empty_and_degenerate_sizes(engine):
+    w = seeded((16, 64), 121)
+    x0 = torch.empty((0, 64), dtype=torch.bfloat16, device=DEV)
+    assert engine.gemm(x0, w).shape == (0, 16)
+    # K = 0: the product is empty, the output is the bias
+    xk = torch.empty((4, 0), dtype=torch.bfloat16, device=DEV)
+    wk = torch.empty((8, 0), dtype=torch.bfloat16, device=DEV)
+    bias = torch.arange(8, dtype=torch.float32, device=DEV)
+    out = engine.gemm(xk, wk, bias)
+    torch.cuda.synchronize()
+    assert torch.equal(out, bias.expand(4, 8))
+
+
+def test_errors_are_raised_not_silenced(engine):
+    x = seeded((8, 64), 131)
+    w = seeded((8, 32), 132)
+    with pytest.raises(engine.B2GError):
+        engine.gemm(x, w)                              # K mismatch
+    with pytest.raises(engine.B2GError):
+        engine.gemm(x, seeded((8, 64), 1, 1.0, torch.float16))   # mixed 16-bit operand types
+
+
+def test_native_kernels_ran_and_no_device_timeouts(engine):
+    n0 = engine.launch_count()
+    x = seeded((256, 256), 141)
+    engine.gemm(x, x)
+    assert engine.launch_count() > n0
+    engine.check_device_error()

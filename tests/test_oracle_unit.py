@@ -1,0 +1,69 @@
+"""CPU self-checks of the oracle's number formats and GEMM against numpy/torch (no GPU)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+
+def test_bf16_rounding_matches_torch(oracle):
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100000).astype(np.float32) * 10,
+                        np.array([0.0, -0.0, 1e-40, -1e-40, 3.4e38, -3.4e38, np.inf, -np.inf], np.float32)])
+    got = oracle.to_bf16_bits(x)
+    want = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, want)
+
+
+def test_f16_rounding_matches_torch(oracle):
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.standard_normal(100000).astype(np.float32) * 100,
+                        rng.standard_normal(20000).astype(np.float32) * 1e-5,   # subnormal halves
+                        np.array([0.0, -0.0, 65504.0, 65520.0, 70000.0, -1e9, 2.0 ** -25, 2.0 ** -24,
+                                  1.5 * 2.0 ** -24, np.inf], np.float32)])
+    got = oracle.to_f16_bits(x)
+    want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got, want)
+    back = oracle.to_f32(got, 1)
+    assert np.array_equal(back, want.view(np.float16).astype(np.float32))
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (5, 17, 3), (64, 256, 96), (33, 3000, 7)])
+def test_linear_matches_float64(oracle, M, K, N):
+    rng = np.random.default_rng(M * 1000 + K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = rng.standard_normal((N, K)).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    got = oracle.linear(x, 0, w, 0, b)
+    want = x.astype(np.float64) @ w.astype(np.float64).T + b
+    assert rel_err(got, want) < 1e-5
+
+
+def test_linear_bf16_inputs_are_exact(oracle):
+    rng = np.random.default_rng(3)
+    x = oracle.to_bf16_bits(rng.standard_normal((20, 100)).astype(np.float32))
+    w = oracle.to_bf16_bits(rng.standard_normal((30, 100)).astype(np.float32))
+    got = oracle.linear(x, 2, w, 2)
+    want = oracle.to_f32(x, 2).astype(np.float64) @ oracle.to_f32(w, 2).astype(np.float64).T
+    assert rel_err(got, want) < 1e-5
+
+
+def test_gelu_formula(oracle):
+    x = np.linspace(-10, 10, 2001, dtype=np.float32)
+    xd = x.astype(np.float64)
+    want = 0.5 * xd * (1 + np.tanh(0.7978845608 * (xd + 0.044715 * xd ** 3)))
+    assert np.abs(oracle.gelu(x) - want).max() < 1e-5
+
+
+def test_modulate_and_rms_norm(oracle):
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((3, 64)).astype(np.float32)
+    sh = rng.standard_normal(64).astype(np.float32)
+    sc = rng.standard_normal(64).astype(np.float32)
+    xd = x.astype(np.float64)
+    ln = (xd - xd.mean(1, keepdims=True)) / np.sqrt(xd.var(1, keepdims=True) + 1e-6)
+    assert rel_err(oracle.modulate(x, sh, sc), ln * (1 + sc) + sh) < 1e-5
+    rms = xd / np.sqrt((xd ** 2).mean(1, keepdims=True) + 1e-6) * sc
+    assert rel_err(oracle.rms_norm(x, sc), rms) < 1e-5
