@@ -17,6 +17,7 @@ struct GemmProblem {
   void* d = nullptr; b2g_dtype d_dtype = B2G_F32; int64_t ldd = 0, d_bstride = 0;
   b2g_epilogue epilogue = B2G_EPI_NONE;
   const float* gate = nullptr;
+  bool allow_tf32 = false;  // F32 x F32 may run as TF32 products (batched_matmul_Bt only)
 };
 
 // Records a message for b2g_last_error() and returns `st`.
@@ -50,6 +51,8 @@ void tc_gemm_set_variant(int force_variant, int allow_pair);
 b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st);
 
 // Elementwise F32 -> bf16/fp16 conversion of `batch` row blocks (strides in elements).
+// dst_dtype B2G_F32 rounds to TF32 precision (round to nearest even, 10 mantissa bits)
+// and keeps fp32 storage.
 b2g_status cast_f32_to_16(const float* src, void* dst, b2g_dtype dst_dtype, int64_t batch, int64_t rows,
                           int64_t cols, int64_t src_ld, int64_t src_bs, int64_t dst_ld, int64_t dst_bs,
                           cudaStream_t st);

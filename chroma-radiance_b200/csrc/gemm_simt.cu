@@ -96,6 +96,19 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
   }
 }
 
+// fp32 -> fp32 rounded to TF32 precision (10 explicit mantissa bits), round to nearest even;
+// Inf/NaN pass through.  This is the operand rounding cuBLAS applies in the reference's
+// batched_matmul_Bt (CUBLAS_COMPUTE_32F_FAST_16BF runs as TF32 on B200; verified against the
+// reference's own outputs to 2e-7).
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u & 0x7F800000u) != 0x7F800000u) {
+    u += 0xFFFu + ((u >> 13) & 1u);
+    u &= 0xFFFFE000u;
+  }
+  return __uint_as_float(u);
+}
+
 // F32 -> bf16/fp16 copy with round-to-nearest-even, as f32_to_bf16_kernel /
 // f32_to_fp16_kernel do (kernels.cu:40-60); here batched and strided on both sides.
 template <typename T>
@@ -109,6 +122,7 @@ __global__ void cast_rows_kernel(const float* __restrict__ src, T* __restrict__ 
     const long long r = rc / cols, c = rc - r * cols;
     const float v = src[b * src_bs + r * src_ld + c];
     if constexpr (std::is_same<T, __nv_bfloat16>::value) dst[b * dst_bs + r * dst_ld + c] = __float2bfloat16(v);
+    else if constexpr (std::is_same<T, float>::value) dst[b * dst_bs + r * dst_ld + c] = round_tf32(v);
     else dst[b * dst_bs + r * dst_ld + c] = __float2half(v);
   }
 }
@@ -123,6 +137,8 @@ __global__ void cast_dense4_kernel(const float4* __restrict__ src, T* __restrict
       __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
       reinterpret_cast<__nv_bfloat162*>(dst)[2 * i] = lo;
       reinterpret_cast<__nv_bfloat162*>(dst)[2 * i + 1] = hi;
+    } else if constexpr (std::is_same<T, float>::value) {
+      reinterpret_cast<float4*>(dst)[i] = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
     } else {
       __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
       reinterpret_cast<__half2*>(dst)[2 * i] = lo;
@@ -163,7 +179,7 @@ b2g_status cast_f32_to_16(const float* src, void* dst, b2g_dtype dst_dtype, int6
   const int threads = 256;
   const long long cap = 148LL * 16;
   const bool dense = (src_ld == cols) && (dst_ld == cols) && (batch == 1 || (src_bs == rows * cols && dst_bs == rows * cols)) &&
-                     ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 7u) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) && ((reinterpret_cast<uintptr_t>(dst) & 15u) == 0) &&
                      (total % 4 == 0);
   if (dense) {
     const long long n4 = total / 4;
@@ -171,6 +187,9 @@ b2g_status cast_f32_to_16(const float* src, void* dst, b2g_dtype dst_dtype, int6
     if (dst_dtype == B2G_BF16)
       cast_dense4_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(reinterpret_cast<const float4*>(src),
                                                                     static_cast<__nv_bfloat16*>(dst), n4);
+    else if (dst_dtype == B2G_F32)
+      cast_dense4_kernel<float><<<blocks, threads, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                            static_cast<float*>(dst), n4);
     else
       cast_dense4_kernel<__half><<<blocks, threads, 0, st>>>(reinterpret_cast<const float4*>(src),
                                                              static_cast<__half*>(dst), n4);
@@ -179,6 +198,9 @@ b2g_status cast_f32_to_16(const float* src, void* dst, b2g_dtype dst_dtype, int6
     if (dst_dtype == B2G_BF16)
       cast_rows_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(src, static_cast<__nv_bfloat16*>(dst), batch, rows,
                                                                   cols, src_ld, src_bs, dst_ld, dst_bs);
+    else if (dst_dtype == B2G_F32)
+      cast_rows_kernel<float><<<blocks, threads, 0, st>>>(src, static_cast<float*>(dst), batch, rows, cols, src_ld,
+                                                          src_bs, dst_ld, dst_bs);
     else
       cast_rows_kernel<__half><<<blocks, threads, 0, st>>>(src, static_cast<__half*>(dst), batch, rows, cols, src_ld,
                                                            src_bs, dst_ld, dst_bs);

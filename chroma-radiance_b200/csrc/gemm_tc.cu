@@ -34,7 +34,10 @@ namespace b2g {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 64;          // 64 x 2 B = one 128-byte swizzle row
+constexpr int kBK = 64;          // 64 x 2 B = one 128-byte swizzle row (16-bit operands)
+// K elements per 128-byte stage row: 64 for bf16/fp16 (KIND 0), 32 for tf32 (KIND 1).
+template <int KIND>
+constexpr int kKElems = KIND == 1 ? 32 : 64;
 constexpr int kThreads = 192;
 enum { OUT_F32 = 0, OUT_BF16 = 1, OUT_F16 = 2 };
 
@@ -158,7 +161,7 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
   }
 }
 
-template <int BN, int STAGES, int EPI, int OUT>
+template <int BN, int STAGES, int EPI, int OUT, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const TcParams p) {
@@ -223,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
-          tma_load_3d(sA + stage * A_BYTES, &tmA, &full_bar[stage], kb * kBK, mb * kBM, bz, pa);
-          tma_load_3d(sB + stage * B_BYTES, &tmB, &full_bar[stage], kb * kBK, nb * BN, bz, pb);
+          tma_load_3d(sA + stage * A_BYTES, &tmA, &full_bar[stage], kb * kKElems<KIND>, mb * kBM, bz, pa);
+          tma_load_3d(sB + stage * B_BYTES, &tmB, &full_bar[stage], kb * kKElems<KIND>, nb * BN, bz, pb);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -262,10 +265,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // Advancing K by 16 elements = 32 bytes inside the 128-byte swizzle row.
-            umma_f16(d_tmem, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), p.idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {
+            // One MMA consumes 32 bytes of K (16 bf16/fp16 or 8 tf32 elements) inside the
+            // 128-byte swizzle row: advance the descriptors by 32 bytes.
+            const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
+            if constexpr (KIND == 1) umma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+            else umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -334,7 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   empty[s]  (each CTA)    the pair's MMAs reading stage s have retired (broadcast commit).
 //   tfull[a]  (each CTA)    accumulator a is complete (broadcast commit).
 //   tempty[a] (CTA 0 only)  all 8 epilogue warps of the pair have read accumulator a.
-template <int STAGES, int EPI, int OUT>
+template <int STAGES, int EPI, int OUT, int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const TcParams p) {
@@ -405,8 +410,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (A_BYTES + B_BYTES));
           const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
-          tma_load_3d_pair(sA + stage * A_BYTES, &tmA, leader_full, kb * kBK, arow, bz, pa);
-          tma_load_3d_pair(sB + stage * B_BYTES, &tmB, leader_full, kb * kBK, brow, bz, pb);
+          tma_load_3d_pair(sA + stage * A_BYTES, &tmA, leader_full, kb * kKElems<KIND>, arow, bz, pa);
+          tma_load_3d_pair(sB + stage * B_BYTES, &tmB, leader_full, kb * kKElems<KIND>, brow, bz, pb);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -444,9 +449,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
           const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_f16_pair(d_tmem, smem_desc_k_sw128(a0 + k * 32), smem_desc_k_sw128(b0 + k * 32), idesc,
-                          (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
+            if constexpr (KIND == 1) umma_tf32_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            else umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit_pair_bcast(&empty_bar[stage], 0x3);
           if (++stage == STAGES) {
@@ -526,16 +532,19 @@ b2g_status get_encode() {
   return B2G_OK;
 }
 
-// 3-D K-major operand map: dims {K, rows, batch}, box {64, box_rows, 1}, 128-byte swizzle,
+// 3-D K-major operand map: dims {K, rows, batch}, box {128 bytes of K, box_rows, 1}, 128-byte swizzle,
 // out-of-bounds elements read as zero (so ragged M, N and K tiles need no special case).
 b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, int64_t K, int64_t rows,
                             int64_t ld, int64_t batch, int64_t bstride, uint32_t box_rows) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows),
                               static_cast<cuuint64_t>(batch)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2u, static_cast<cuuint64_t>(bstride) * 2u};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), box_rows, 1u};
+  const cuuint64_t esz = dt == B2G_F32 ? 4u : 2u;
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * esz, static_cast<cuuint64_t>(bstride) * esz};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / esz), box_rows, 1u};  // 128-byte rows
   const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUtensorMapDataType t = dt == B2G_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType t = dt == B2G_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : dt == B2G_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUresult r = g_encode(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -555,32 +564,37 @@ b2g_status launch_kernel(Kern kern, size_t smem, const CUtensorMap& ta, const CU
 }
 
 // Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.
-template <bool PAIR, int BN, int STAGES, int EPI, int OUT>
+template <bool PAIR, int BN, int STAGES, int EPI, int OUT, int KIND>
 b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid, cudaStream_t st) {
   if constexpr (PAIR) {
     constexpr size_t smem = 1024 + static_cast<size_t>(STAGES) * (kBM * kBK * 2 + 128 * kBK * 2) + 256;
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT>, smem, ta, tb, prm, grid, st);
+    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, ta, tb, prm, grid, st);
   } else {
     constexpr size_t smem = smem_bytes(BN, STAGES);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT>, smem, ta, tb, prm, grid, st);
+    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, ta, tb, prm, grid, st);
   }
 }
 
 template <bool PAIR, int BN, int STAGES>
 b2g_status dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid,
-                        b2g_epilogue epi, b2g_dtype out, cudaStream_t st) {
-  if (epi == B2G_EPI_GATED_RESIDUAL)
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32>(ta, tb, prm, grid, st);
-  if (epi == B2G_EPI_GELU) {
-    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32>(ta, tb, prm, grid, st);
-    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16>(ta, tb, prm, grid, st);
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16>(ta, tb, prm, grid, st);
+                        b2g_epilogue epi, b2g_dtype out, bool tf32, cudaStream_t st) {
+  if (tf32) {
+    // fp32 operands (batched_matmul_Bt): plain F32 output only.
+    if (epi != B2G_EPI_NONE || out != B2G_F32) return set_error(B2G_ERR_UNSUPPORTED, "tf32 path: F32 output only");
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(ta, tb, prm, grid, st);
   }
-  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32>(ta, tb, prm, grid, st);
-  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16>(ta, tb, prm, grid, st);
-  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16>(ta, tb, prm, grid, st);
+  if (epi == B2G_EPI_GATED_RESIDUAL)
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(ta, tb, prm, grid, st);
+  if (epi == B2G_EPI_GELU) {
+    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(ta, tb, prm, grid, st);
+    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(ta, tb, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(ta, tb, prm, grid, st);
+  }
+  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(ta, tb, prm, grid, st);
+  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(ta, tb, prm, grid, st);
+  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(ta, tb, prm, grid, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -592,14 +606,17 @@ bool tc_gemm_supported(const GemmProblem& p, std::string* why) {
     if (why) *why = m;
     return false;
   };
-  if (!((p.a_dtype == B2G_BF16 && p.b_dtype == B2G_BF16) || (p.a_dtype == B2G_F16 && p.b_dtype == B2G_F16)))
+  const bool tf32 = p.a_dtype == B2G_F32 && p.b_dtype == B2G_F32 && p.allow_tf32;
+  if (!((p.a_dtype == B2G_BF16 && p.b_dtype == B2G_BF16) || (p.a_dtype == B2G_F16 && p.b_dtype == B2G_F16) || tf32))
     return no("operand dtypes");
+  if (tf32 && (p.epilogue != B2G_EPI_NONE || p.d_dtype != B2G_F32)) return no("tf32: F32 output, no epilogue");
   if (p.d_dtype != B2G_F32 && p.d_dtype != B2G_BF16 && p.d_dtype != B2G_F16) return no("output dtype");
   if (p.epilogue == B2G_EPI_GATED_RESIDUAL && p.d_dtype != B2G_F32) return no("gated residual needs F32 output");
   if (p.bias && p.bias_dtype != B2G_F32 && p.bias_dtype != B2G_BF16) return no("bias dtype");
   if (!aligned16(p.a) || !aligned16(p.b)) return no("operand base not 16-byte aligned");
-  if ((p.lda & 7) || (p.ldb & 7)) return no("operand row stride not a multiple of 8 elements");
-  if (p.batch > 1 && ((p.a_bstride & 7) || (p.b_bstride & 7))) return no("batch stride not a multiple of 8");
+  const int64_t align = tf32 ? 3 : 7;  // 16-byte row and batch strides
+  if ((p.lda & align) || (p.ldb & align)) return no("operand row stride not a multiple of 16 bytes");
+  if (p.batch > 1 && ((p.a_bstride & align) || (p.b_bstride & align))) return no("batch stride not 16-byte aligned");
   if (p.M > (1ll << 31) - kBM || p.N > (1ll << 31) - 256 || p.K > (1ll << 31)) return no("size");
   if (p.batch > 65535) return no("batch");
   return true;
@@ -639,7 +656,9 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.batch = static_cast<int>(p.batch);
   prm.num_m_blocks = static_cast<int>((p.M + tile_m - 1) / tile_m);
   prm.num_n_blocks = static_cast<int>((p.N + bn - 1) / bn);
-  prm.num_k_blocks = static_cast<int>((p.K + kBK - 1) / kBK);
+  const bool tf32 = p.a_dtype == B2G_F32;
+  const int kelems = tf32 ? 32 : 64;
+  prm.num_k_blocks = static_cast<int>((p.K + kelems - 1) / kelems);
   prm.num_tiles = prm.batch * prm.num_m_blocks * prm.num_n_blocks;
   const int group = v == VPAIR ? 8 : 16;
   prm.group_m = prm.num_m_blocks <= group ? prm.num_m_blocks : group;
@@ -650,7 +669,7 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.gate = p.gate;
   prm.err = dev->err_word;
-  prm.idesc = idesc_f16(p.a_dtype == B2G_BF16, tile_m, bn);
+  prm.idesc = idesc_make(tf32 ? kFmtTF32 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16), tile_m, bn);
   const int out_bytes = p.d_dtype == B2G_F32 ? 4 : 2;
   prm.vec_ok = aligned16(p.d) && ((p.ldd * out_bytes) % 16 == 0) &&
                (p.batch <= 1 || (p.d_bstride * out_bytes) % 16 == 0);
@@ -667,11 +686,11 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
 
   if (v == VPAIR) {
     const int grid = 2 * static_cast<int>(prm.num_tiles < pairs ? prm.num_tiles : pairs);
-    return dispatch_epi<true, 256, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+    return dispatch_epi<true, 256, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
   }
   const int grid = static_cast<int>(prm.num_tiles < sms ? prm.num_tiles : sms);
-  if (v == V256) return dispatch_epi<false, 256, 4>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
-  return dispatch_epi<false, 128, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, st);
+  if (v == V256) return dispatch_epi<false, 256, 4>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  return dispatch_epi<false, 128, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
 }
 
 void tc_gemm_set_variant(int force_variant, int allow_pair) {

@@ -111,8 +111,9 @@ b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type,
  * all F32, densely packed.  Replaces
  *   static void batched_matmul_Bt(const Tensor& A, const Tensor& B, Tensor& C)
  *                                                        cublas_ops.cuh:558-585
- * (cuBLAS CUBLAS_COMPUTE_32F_FAST_16BF: operands rounded to bf16, fp32 accumulate;
- * this engine does the same rounding).  Stream 0. */
+ * The reference asks cuBLAS for CUBLAS_COMPUTE_32F_FAST_16BF, which on B200 runs as TF32
+ * products of round-to-nearest TF32 operands with fp32 accumulation (checked against the
+ * reference's own outputs); this engine does the same on kind::tf32 tensor cores.  Stream 0. */
 b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
                                  int64_t batch, int64_t M, int64_t K, int64_t N);
 

@@ -97,11 +97,22 @@ void oracle_to_f32(const void* src, int dt, float* dst, int64_t n) {
   for (int64_t i = 0; i < n; ++i) dst[i] = load_as_f32(src, dt, i);
 }
 
-/* Round fp32 values to bf16 (dt=2) or fp16 (dt=1) precision, keeping them as fp32. */
+/* fp32 rounded to TF32 precision (10 explicit mantissa bits), round to nearest even. */
+float oracle_round_tf32(float f) {
+  uint32_t u = f32_to_bits(f);
+  if ((u & 0x7F800000u) == 0x7F800000u) return f;
+  u += 0xFFFu + ((u >> 13) & 1u);
+  return bits_to_f32(u & 0xFFFFE000u);
+}
+
+enum { O_TF32 = 3 }; /* rounding target only (storage stays fp32) */
+
+/* Round fp32 values to bf16 (dt=2), fp16 (dt=1) or tf32 (dt=3) precision, kept as fp32. */
 void oracle_round(const float* src, int dt, float* dst, int64_t n) {
   for (int64_t i = 0; i < n; ++i) {
     if (dt == O_BF16) dst[i] = oracle_bf16_to_f32(oracle_f32_to_bf16(src[i]));
     else if (dt == O_F16) dst[i] = oracle_f16_to_f32(oracle_f32_to_f16(src[i]));
+    else if (dt == O_TF32) dst[i] = oracle_round_tf32(src[i]);
     else dst[i] = src[i];
   }
 }
@@ -223,11 +234,12 @@ int oracle_linear(int64_t M, int64_t K, int64_t N, const void* x, int xdt, int64
 /*
  * C[b] = A[b] . B[b]^T, all fp32 [batch, M, K] x [batch, N, K] -> [batch, M, N].
  * The reference's batched_matmul_Bt (cublas_ops.cuh:558-585) runs cuBLAS with
- * CUBLAS_COMPUTE_32F_FAST_16BF: operands are rounded to bf16, products summed in fp32.
- * round_bf16 = 1 restates that; 0 computes exact fp32 products.
+ * CUBLAS_COMPUTE_32F_FAST_16BF.  On B200 that executes as TF32: operands rounded to nearest
+ * TF32, products summed in fp32 (tests/golden/batched_matmul_Bt.npz matches that to 2e-7).
+ * rounding: 0 exact fp32 operands, 2 (O_BF16) bf16 operands, 3 (O_TF32) tf32 operands.
  */
 int oracle_batched_matmul_bt(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
-                             int64_t N, int round_bf16, int nthreads) {
+                             int64_t N, int rounding, int nthreads) {
   float* ar = (float*)malloc(sizeof(float) * (size_t)(M * K > 0 ? M * K : 1));
   float* br = (float*)malloc(sizeof(float) * (size_t)(N * K > 0 ? N * K : 1));
   if (!ar || !br) {
@@ -238,9 +250,9 @@ int oracle_batched_matmul_bt(const float* A, const float* B, float* C, int64_t b
   for (int64_t b = 0; b < batch; ++b) {
     const float* a = A + b * M * K;
     const float* bb = B + b * N * K;
-    if (round_bf16) {
-      oracle_round(a, O_BF16, ar, M * K);
-      oracle_round(bb, O_BF16, br, N * K);
+    if (rounding) {
+      oracle_round(a, rounding, ar, M * K);
+      oracle_round(bb, rounding, br, N * K);
     } else {
       memcpy(ar, a, sizeof(float) * (size_t)(M * K));
       memcpy(br, bb, sizeof(float) * (size_t)(N * K));

@@ -20,6 +20,7 @@ ORACLE_PATH = HERE / "liboracle.so"
 REF_PATH = HERE / "_ref" / "libref_cublaslt.so"
 
 F32, F16, BF16 = 0, 1, 2          # reference DType codes (tensor.cuh:116)
+TF32 = 3                          # oracle rounding target only
 CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF = 0, 2, 14
 
 _c_p = ctypes.c_void_p
@@ -101,14 +102,15 @@ class Oracle:
             raise MemoryError("oracle_linear")
         return out
 
-    def batched_matmul_bt(self, A: np.ndarray, B: np.ndarray, round_bf16: bool = True,
+    def batched_matmul_bt(self, A: np.ndarray, B: np.ndarray, rounding: int = TF32,
                           nthreads: int = 0) -> np.ndarray:
+        """rounding: TF32 (the reference's behaviour on B200), BF16, or 0 for exact fp32."""
         A = np.ascontiguousarray(A, dtype=np.float32)
         B = np.ascontiguousarray(B, dtype=np.float32)
         batch, M, K = A.shape
         N = B.shape[1]
         C = np.empty((batch, M, N), dtype=np.float32)
-        self.lib.oracle_batched_matmul_bt(_np_ptr(A), _np_ptr(B), _np_ptr(C), batch, M, K, N, int(round_bf16),
+        self.lib.oracle_batched_matmul_bt(_np_ptr(A), _np_ptr(B), _np_ptr(C), batch, M, K, N, int(rounding),
                                           nthreads)
         return C
 

@@ -237,7 +237,7 @@ def test_batched_matmul_bt_vs_oracle(engine, oracle, batch, M, K, N):
     B = seeded((batch, N, K), 92, 1.0, torch.float32)
     mine = torch.empty((batch, M, N), device=DEV)
     engine.batched_matmul_Bt(A, B, mine)
-    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy(), round_bf16=True)
+    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy())  # TF32 operand rounding
     torch.cuda.synchronize()
     got = mine.cpu().numpy()
     for b in range(batch):
@@ -253,7 +253,7 @@ def test_batched_matmul_bt_vs_reference(engine, ref, oracle, batch, M, K, N):
     engine.batched_matmul_Bt(A, B, mine)
     ref.batched_matmul_Bt(A.data_ptr(), B.data_ptr(), theirs.data_ptr(), batch, M, K, N)
     torch.cuda.synchronize()
-    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy(), round_bf16=True)
+    want = oracle.batched_matmul_bt(A.cpu().numpy(), B.cpu().numpy())
     t = theirs.cpu().numpy()
     per_batch_ref = [rel_err(t[b], want[b]) for b in range(batch)]
     assert rel_err(mine.cpu().numpy(), t) <= TOL_F32_OUT, f"reference vs oracle per batch: {per_batch_ref}"

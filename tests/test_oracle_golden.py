@@ -77,12 +77,15 @@ def test_gated_residual(oracle):
 
 
 def test_batched_matmul_bt(oracle):
+    """CUBLAS_COMPUTE_32F_FAST_16BF on B200 is TF32 with round-to-nearest operands."""
+    from oracle import BF16, TF32
+
     g = load("batched_matmul_Bt")
-    got = oracle.batched_matmul_bt(g["A"], g["B"], round_bf16=True)
+    got = oracle.batched_matmul_bt(g["A"], g["B"], rounding=TF32)
     assert rel_err(got, g["out"]) < 1e-5
-    exact = oracle.batched_matmul_bt(g["A"], g["B"], round_bf16=False)
-    # FAST_16BF rounding is visible at this size: the bf16-rounded restatement is closer.
-    assert rel_err(got, g["out"]) < rel_err(exact, g["out"])
+    # Neither exact fp32 nor bf16 operands reproduce it: the fixture pins the rounding.
+    assert rel_err(oracle.batched_matmul_bt(g["A"], g["B"], rounding=0), g["out"]) > 1e-4
+    assert rel_err(oracle.batched_matmul_bt(g["A"], g["B"], rounding=BF16), g["out"]) > 1e-3
 
 
 def test_modulate_to_bf16(oracle):
