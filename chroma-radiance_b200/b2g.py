@@ -74,7 +74,7 @@ _SIGNATURES = {
     "b2g_batched_matmul_Bt": ([ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4, ctypes.c_int),
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
-    "b2g_set_gemm_variant": ([ctypes.c_int], ctypes.c_int),
+    "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
 }
 
 
@@ -111,9 +111,10 @@ def launch_count() -> int:
     return int(load().b2g_launch_count())
 
 
-def set_gemm_variant(variant: int) -> None:
-    """-1 automatic, 0 = 1-CTA 128x128, 1 = 1-CTA 128x256, 2 = 2-CTA 256x256 tiles."""
-    _check(load().b2g_set_gemm_variant(variant))
+def set_gemm_variant(variant: int, splits: int = 0) -> None:
+    """variant -1 automatic, 0 = 1-CTA 128x128, 1 = 1-CTA 128x256, 2 = 2-CTA 256x256 tiles;
+    splits 0 automatic, else the split-K factor."""
+    _check(load().b2g_set_gemm_variant(variant, splits))
 
 
 def check_device_error() -> None:

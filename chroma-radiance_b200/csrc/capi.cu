@@ -26,7 +26,7 @@ struct Workspace {
   size_t bytes = 0;
   int device = -1;
 };
-Workspace g_ws[kMaxDevices];
+Workspace g_ws[kMaxDevices][kWsSlots];
 
 b2g_dtype from_cuda_type(cudaDataType_t t, bool* ok) {
   *ok = true;
@@ -80,11 +80,11 @@ b2g_status device_info(DeviceInfo** out) {
   return B2G_OK;
 }
 
-b2g_status workspace_get(size_t bytes, void** ptr) {
+b2g_status workspace_get(size_t bytes, void** ptr, int slot) {
   int dev = -1;
   b2g_status s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (s != B2G_OK) return s;
-  Workspace& w = g_ws[dev];
+  Workspace& w = g_ws[dev][slot];
   if (w.bytes < bytes) {
     if (w.ptr) {
       // The old buffer may still be read by queued kernels.
@@ -95,6 +95,8 @@ b2g_status workspace_get(size_t bytes, void** ptr) {
     }
     const size_t want = static_cast<size_t>(round_up(static_cast<int64_t>(bytes), 1 << 20));
     if ((s = check_cuda(cudaMalloc(&w.ptr, want), "cudaMalloc (workspace)")) != B2G_OK) return s;
+    if (slot == kWsCounters && (s = check_cuda(cudaMemset(w.ptr, 0, want), "cudaMemset (counters)")) != B2G_OK)
+      return s;
     w.bytes = want;
     w.device = dev;
   }
@@ -103,16 +105,18 @@ b2g_status workspace_get(size_t bytes, void** ptr) {
 }
 
 void workspace_release() {
-  for (auto& w : g_ws) {
-    if (w.ptr) {
-      int cur = -1;
-      cudaGetDevice(&cur);
-      cudaSetDevice(w.device);
-      cudaDeviceSynchronize();
-      cudaFree(w.ptr);
-      cudaSetDevice(cur);
+  for (auto& per_dev : g_ws) {
+    for (auto& w : per_dev) {
+      if (w.ptr) {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        cudaSetDevice(w.device);
+        cudaDeviceSynchronize();
+        cudaFree(w.ptr);
+        cudaSetDevice(cur);
+      }
+      w = Workspace{};
     }
-    w = Workspace{};
   }
 }
 
@@ -159,9 +163,10 @@ const char* b2g_version(void) { return "b2g 0.1 (sm_100a tcgen05)"; }
 
 uint64_t b2g_launch_count(void) { return g_launches.load(); }
 
-b2g_status b2g_set_gemm_variant(int variant) {
+b2g_status b2g_set_gemm_variant(int variant, int splits) {
   if (variant < -1 || variant > 2) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: variant in [-1, 2]");
-  tc_gemm_set_variant(variant, 1);
+  if (splits < 0 || splits > 16) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: splits in [0, 16]");
+  tc_gemm_set_variant(variant, 1, splits);
   return B2G_OK;
 }
 

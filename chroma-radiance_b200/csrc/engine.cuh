@@ -36,8 +36,11 @@ b2g_status device_info(DeviceInfo** out);
 // Counts launches of this library's kernels (reported by b2g_launch_count).
 void note_launch(uint64_t n = 1);
 
-// Workspace (device memory owned by the library, grown on demand, never shrunk).
-b2g_status workspace_get(size_t bytes, void** ptr);
+// Workspaces (device memory owned by the library, grown on demand, never shrunk), one per
+// purpose so that one call can use several.  kWsCounters is zero-filled when (re)allocated
+// and kernels leave it zero.
+enum WorkspaceSlot { kWsOperands = 0, kWsSplitK = 1, kWsCounters = 2, kWsSlots = 3 };
+b2g_status workspace_get(size_t bytes, void** ptr, int slot = kWsOperands);
 void workspace_release();
 
 // True if the tensor-core path can run this problem (dtypes, strides, alignment).
@@ -45,7 +48,7 @@ bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // Kernel variant override for tests/tuning: -1 automatic, 0 = 1-CTA 128x128 tiles,
 // 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
-void tc_gemm_set_variant(int force_variant, int allow_pair);
+void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits);
 
 // Exact-fp32 CUDA-core path for everything the tensor-core path does not take.
 b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st);

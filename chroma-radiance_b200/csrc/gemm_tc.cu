@@ -2,29 +2,37 @@
 //
 //   D[b, m, n] = epilogue( sum_k A[b, m, k] * B[b, n, k] + bias[n] )
 //
-// A (activations) and B (weights) are K-major bf16 or fp16 in global memory.  This is the
-// computation of the reference's cuBLASLt call in linear_lt (cublas_ops.cuh:214-288:
-// TRANSA=T on W, TRANSB=N on x, fp32 compute, bias epilogue), with the elementwise work
-// that the reference runs as separate kernels after it (gelu_to_bf16 kernels.cu:297-310,
-// gated_residual kernels.cu:942-968) fused into the store.
+// A (activations) and B (weights) are K-major bf16 / fp16 (kind::f16) or TF32-rounded fp32
+// (kind::tf32) in global memory.  This is the computation of the reference's cuBLASLt call
+// in linear_lt (cublas_ops.cuh:214-288: TRANSA=T on W, TRANSB=N on x, fp32 compute, bias
+// epilogue), with the elementwise work that the reference runs as separate kernels after
+// it (gelu_to_bf16 kernels.cu:297-310, gated_residual kernels.cu:942-968) fused into the
+// store.
 //
-// Design (one persistent CTA per SM, 192 threads, warp-specialised):
-//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte swizzle,
-//               STAGES-deep ring of shared-memory stages guarded by full/empty mbarriers.
-//   warp 1      allocates TMEM (2 accumulators of 128 lanes x BN fp32 columns) and issues
-//               tcgen05.mma (M=128, N=BN, K=16) from one thread; tcgen05.commit frees a
-//               smem stage when the MMAs reading it retire, and signals a finished
-//               accumulator to the epilogue.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w owns TMEM lanes
-//               32*(w%4)..+31 = tile rows), add bias, apply GELU or gate*y+residual,
-//               convert and store with 16-byte vector stores.  The accumulator is handed
-//               back as soon as it is read, so tile i's epilogue overlaps tile i+1's MMAs.
+// Two persistent, warp-specialised kernels (320 threads, one CTA per SM):
+//   warp 0      TMA producer: STAGES-deep ring of (A tile, B tile) shared-memory stages,
+//               128-byte swizzle, guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM and issues tcgen05.mma from one thread; tcgen05.commit
+//               frees a stage when the MMAs reading it retire and signals a finished
+//               accumulator.  Two accumulators, so tile i's epilogue overlaps tile i+1.
+//   warps 2-9   epilogue: two warps per TMEM lane quarter (warp w owns lanes 32*(w%4)..,
+//               i.e. 32 tile rows), each taking half of the columns; tcgen05.ld 32 columns
+//               at a time with the next chunk's load in flight, bias from shared memory,
+//               GELU, then a swizzled shared-memory chunk written by one TMA store (or
+//               direct stores for the gated residual, which reads D).
+//   tc_gemm_kernel       1 CTA  per 128 x BN tile   (BN = 128 or 256), tcgen05 cta_group::1
+//   tc_gemm_pair_kernel  2 CTAs per 256 x 256 tile, tcgen05 cta_group::2 (CTA r loads its
+//                        own halves of A and B: no multicast anywhere)
+// Split-K: a work item is (split, tile); each split stores its fp32 partial in a workspace
+// and the split that arrives last on the tile's counter sums them in split order.
 // Every wait is bounded (ptx_sm100.cuh): on timeout the kernel records an error word,
-// waits for its own TMA copies / MMAs in flight, frees TMEM and returns.
+// drains its own TMA copies / MMAs, frees TMEM and returns.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include "engine.cuh"
 #include "ptx_sm100.cuh"
@@ -35,11 +43,19 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;          // 64 x 2 B = one 128-byte swizzle row (16-bit operands)
+constexpr int kThreads = 320;    // producer, MMA, 8 epilogue warps
+constexpr int kEpiThreads = 256;
+constexpr int kEpiWarps = 8;
 // K elements per 128-byte stage row: 64 for bf16/fp16 (KIND 0), 32 for tf32 (KIND 1).
 template <int KIND>
 constexpr int kKElems = KIND == 1 ? 32 : 64;
-constexpr int kThreads = 192;
 enum { OUT_F32 = 0, OUT_BF16 = 1, OUT_F16 = 2 };
+
+// Output staging: one 4 KB buffer per epilogue warp (32 rows x 32 fp32 or 16-bit columns),
+// swizzled like the D tensor map so neither the st.shared nor the TMA store conflicts.
+constexpr int kOutBufBytes = 4096;
+constexpr int kOutStageBytes = kEpiWarps * kOutBufBytes;  // 32 KB
+constexpr int kBiasBytes = 256 * 4;                       // bias of one tile (<= 256 columns)
 
 struct TcParams {
   int M, N, K, batch;
@@ -54,11 +70,16 @@ struct TcParams {
   uint32_t idesc;
   int vec_ok;              // D base/ldd allow 16-byte vector stores
   int a_keep;              // 1: keep A in L2 (evict_last), stream B (evict_first); 0: reverse
+  int splits;              // split-K factor S (1 = none); work item = (split, tile)
+  int num_items;           // num_tiles * splits
+  float* ws;               // split-K partials [slot][split][128][BN] fp32
+  int* counters;           // split-K arrival counter per slot (zero between launches)
+  int tma_store;           // 1: outputs leave through smem staging + TMA bulk tensor stores
 };
 
-__host__ __device__ constexpr size_t smem_bytes(int bn, int stages) {
-  return 1024 /* alignment slack */ + static_cast<size_t>(stages) * (kBM * kBK * 2 + bn * kBK * 2) +
-         256 /* barriers + TMEM slot */;
+__host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int stages) {
+  return 1024 /* alignment slack */ + static_cast<size_t>(stages) * (a_bytes + b_bytes) + kOutStageBytes + kBiasBytes +
+         256 /* barriers, TMEM slot, broadcast word */;
 }
 
 __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& bz, int& mb, int& nb) {
@@ -76,34 +97,64 @@ __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& bz
   nb = r / gm;
 }
 
+// Work item -> (tile, split, k-block range).  Items are split-major so the CTAs running at
+// the same time share K ranges (and therefore A/B panels in L2).
+__device__ __forceinline__ void item_coords(int item, const TcParams& p, int& tile, int& split, int& kb0, int& kb1) {
+  split = item / p.num_tiles;
+  tile = item - split * p.num_tiles;
+  kb0 = static_cast<int>(static_cast<long long>(split) * p.num_k_blocks / p.splits);
+  kb1 = static_cast<int>(static_cast<long long>(split + 1) * p.num_k_blocks / p.splits);
+}
+
 // tanh-form GELU, the formula of the reference's gelu_val (kernels.cu:266-269).
 __device__ __forceinline__ float gelu_tanh(float v) {
   const float inner = 0.7978845608f * (v + 0.044715f * v * v * v);
   return 0.5f * v * (1.0f + tanhf(inner));
 }
 
-template <int EPI, int OUT>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, int n0, const uint32_t (&r)[32]) {
-  float v[32];
+// acc + bias (bias staged in shared memory, zero past N), then GELU if asked.
+template <int EPI>
+__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], const float* sb, float (&v)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-  const bool full = (n0 + 32 <= p.N);
-  const int nvalid = full ? 32 : (p.N - n0);
-  if (p.bias_kind == 1) {
-    const float* bp = static_cast<const float*>(p.bias) + n0;
+  if (sb) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || j < nvalid) v[j] += __ldg(bp + j);
-  } else if (p.bias_kind == 2) {
-    const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(p.bias) + n0;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || j < nvalid) v[j] += __bfloat162float(bp[j]);
+    for (int j = 0; j < 32; j += 4) {
+      const float4 b = *reinterpret_cast<const float4*>(sb + j);
+      v[j] += b.x;
+      v[j + 1] += b.y;
+      v[j + 2] += b.z;
+      v[j + 3] += b.w;
+    }
   }
   if constexpr (EPI == B2G_EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
   }
+}
+
+template <int OUT>
+__device__ __forceinline__ void pack16(const float (&v)[32], uint32_t (&packed)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if constexpr (OUT == OUT_BF16) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+      packed[j] = *reinterpret_cast<uint32_t*>(&h);
+    } else {
+      __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+      packed[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+}
+
+// Direct stores of one thread's 32 values of row m, columns [n0, n0+32).
+template <int EPI, int OUT>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, int n0, const uint32_t (&r)[32],
+                                            const float* sb) {
+  float v[32];
+  chunk_values<EPI>(r, sb, v);
+  const bool full = (n0 + 32 <= p.N);
+  const int nvalid = full ? 32 : (p.N - n0);
   const long long off = static_cast<long long>(bz) * p.d_bstride + static_cast<long long>(m) * p.ldd + n0;
   if constexpr (OUT == OUT_F32) {
     float* dp = static_cast<float*>(p.d) + off;
@@ -137,16 +188,7 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
     }
   } else {
     uint32_t packed[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      if constexpr (OUT == OUT_BF16) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-        packed[j] = *reinterpret_cast<uint32_t*>(&h);
-      } else {
-        __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-        packed[j] = *reinterpret_cast<uint32_t*>(&h);
-      }
-    }
+    pack16<OUT>(v, packed);
     uint16_t* dp = static_cast<uint16_t*>(p.d) + off;
     if (full && p.vec_ok) {
 #pragma unroll
@@ -161,10 +203,147 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
   }
 }
 
+// Stages one 32x32 chunk (this warp's 32 rows x columns [n0, n0+32)) in shared memory and
+// writes it with one TMA store; the tensor map clips rows >= M and columns >= N.
+template <int EPI, int OUT>
+__device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_t* buf, int bz, int m_warp0, int n0,
+                                                  const uint32_t (&r)[32], const float* sb, int lane) {
+  float v[32];
+  chunk_values<EPI>(r, sb, v);
+  if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
+  __syncwarp();
+  if constexpr (OUT == OUT_F32) {
+    // 128-byte rows, 128-byte swizzle: 16-byte chunk j of row `lane` goes to j ^ (lane % 8).
+    uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+    uint32_t packed[16];
+    pack16<OUT>(v, packed);
+    // 64-byte rows, 64-byte swizzle: 16-byte chunk j of row `lane` goes to j ^ ((lane / 2) % 4).
+    uint8_t* rowp = buf + lane * 64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(rowp + ((j ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tmD, buf, n0, m_warp0, bz);
+    bulk_commit_group();
+  }
+}
+
+// Writes one finished 32-column chunk: TMA-staged when enabled, else direct stores.
+template <int EPI, int OUT>
+__device__ __forceinline__ void emit_chunk(const TcParams& p, const CUtensorMap* tmD, uint8_t* buf, int bz, int m,
+                                           int m_warp0, int n0, const uint32_t (&r)[32], const float* sb, int lane) {
+  if (EPI != B2G_EPI_GATED_RESIDUAL && p.tma_store) {
+    if (m_warp0 < p.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, bz, m_warp0, n0, r, sb, lane);  // uniform
+  } else if (m < p.M && n0 < p.N) {
+    store_chunk<EPI, OUT>(p, bz, m, n0, r, sb);
+  }
+}
+
+// Per-CTA epilogue context (shared memory and the warp's place in the tile).
+struct EpiCtx {
+  uint8_t* buf;            // this warp's staging buffer
+  float* sbias;            // tile bias in shared memory (BN floats)
+  volatile int* bcast;     // split-K arrival broadcast word
+  int lane, row, q, half;  // row = TMEM lane = tile row; q = lane quarter; half = column half
+};
+
+// Loads this item's bias columns [n_base, n_base+BN) into shared memory (zero past N).
+template <int BN>
+__device__ __forceinline__ void stage_bias(const TcParams& p, float* sbias, int n_base) {
+  if (p.bias_kind == 0) return;
+  for (int i = static_cast<int>(threadIdx.x) - 64; i < BN; i += kEpiThreads) {
+    const int n = n_base + i;
+    float b = 0.f;
+    if (n < p.N)
+      b = p.bias_kind == 1 ? __ldg(static_cast<const float*>(p.bias) + n)
+                           : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
+    sbias[i] = b;
+  }
+}
+
+// Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
+// accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
+// after this warp's last chunk is read.  With split-K, each split stores its raw fp32
+// partial; the split arriving last on the slot's counter sums all partials in split order
+// (deterministic), runs the epilogue and re-arms the counter for the next launch.
+template <int BN, int EPI, int OUT, typename Release>
+__device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e, uint32_t tacc, Release release,
+                                              const CUtensorMap* tmD, int bz, int m, int n_base, int slot, int split) {
+  constexpr int NCH = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
+  const int c0 = e.half * NCH;
+  const int m_warp0 = m - e.lane;
+  const float* sb = p.bias_kind ? e.sbias : nullptr;
+  const bool splitk = p.splits > 1;
+  float* part = splitk ? p.ws + ((static_cast<size_t>(slot) * p.splits + split) * 128 + e.row) * BN : nullptr;
+  uint32_t r[2][32];
+  tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    tmem_wait_ld();
+    if (i + 1 < NCH) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);  // next chunk in flight
+    if (i == NCH - 1) release();
+    const int c = c0 + i;
+    if (!splitk) {
+      emit_chunk<EPI, OUT>(p, tmD, e.buf, bz, m, m_warp0, n_base + c * 32, r[i & 1], sb ? sb + c * 32 : nullptr,
+                           e.lane);
+    } else {
+      float4* dst = reinterpret_cast<float4*>(part + c * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        dst[j] = make_float4(__uint_as_float(r[i & 1][4 * j]), __uint_as_float(r[i & 1][4 * j + 1]),
+                             __uint_as_float(r[i & 1][4 * j + 2]), __uint_as_float(r[i & 1][4 * j + 3]));
+    }
+  }
+  if (splitk) {
+    __threadfence();
+    named_bar_sync(1, kEpiThreads);
+    if (threadIdx.x == 64) *e.bcast = atomicAdd(p.counters + slot, 1);
+    named_bar_sync(1, kEpiThreads);
+    if (*e.bcast == p.splits - 1) {
+      __threadfence();
+      const float* base = p.ws + (static_cast<size_t>(slot) * p.splits * 128 + e.row) * BN;
+#pragma unroll 1
+      for (int i = 0; i < NCH; ++i) {
+        const int c = c0 + i;
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+        for (int sp = 0; sp < p.splits; ++sp) {
+          const float4* src = reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * 128 * BN + c * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 v = __ldcg(src + j);
+            acc[4 * j] += v.x;
+            acc[4 * j + 1] += v.y;
+            acc[4 * j + 2] += v.z;
+            acc[4 * j + 3] += v.w;
+          }
+        }
+        uint32_t rr[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rr[j] = __float_as_uint(acc[j]);
+        emit_chunk<EPI, OUT>(p, tmD, e.buf, bz, m, m_warp0, n_base + c * 32, rr, sb ? sb + c * 32 : nullptr, e.lane);
+      }
+      if (threadIdx.x == 64) p.counters[slot] = 0;
+    }
+  }
+  named_bar_sync(1, kEpiThreads);  // shared bias and the broadcast word are reused next item
+}
+
+// ---------------------------------------------------------------------------- 1-CTA kernel
 template <int BN, int STAGES, int EPI, int OUT, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const TcParams p) {
+                   const __grid_constant__ CUtensorMap tmD, const TcParams p) {
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators; 256 or 512 (power of two)
@@ -174,12 +353,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sOut = sB + STAGES * B_BYTES;
+  float* sBias = reinterpret_cast<float*>(sOut + kOutStageBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -191,12 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty_bar[a], kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -217,10 +400,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        int bz, mb, nb;
+      for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+        int tile, split, kb0, kb1, bz, mb, nb;
+        item_coords(item, p, tile, split, kb0, kb1);
         tile_coords(tile, p, bz, mb, nb);
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrWaitProducer)) {
             ok = false;
             break;
@@ -247,7 +431,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+      for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x, ++local) {
+        int tile, split, kb0, kb1;
+        item_coords(item, p, tile, split, kb0, kb1);
         const uint32_t acc = local & 1u;
         const uint32_t acc_phase = (local >> 1) & 1u;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kErrWaitMma)) {
@@ -256,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma)) {
             ok = false;
             break;
@@ -269,8 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // One MMA consumes 32 bytes of K (16 bf16/fp16 or 8 tf32 elements) inside the
             // 128-byte swizzle row: advance the descriptors by 32 bytes.
             const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
-            if constexpr (KIND == 1) umma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
-            else umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+            const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
+            if constexpr (KIND == 1) umma_tf32(d_tmem, ad, bd, p.idesc, accum);
+            else umma_f16(d_tmem, ad, bd, p.idesc, accum);
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -287,35 +474,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
+    // ------------------------------------------------------------ epilogue (warps 2..9)
+    EpiCtx e;
+    e.lane = lane;
+    e.q = warp & 3;  // TMEM lane quarter this warp may access
+    e.half = (warp - 2) >> 2;
+    e.row = e.q * 32 + lane;
+    e.buf = sOut + (warp - 2) * kOutBufBytes;
+    e.sbias = sBias;
+    e.bcast = bcast;
     uint32_t local = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
-      int bz, mb, nb;
+    for (int item = blockIdx.x; item < p.num_items; item += gridDim.x, ++local) {
+      int tile, split, kb0, kb1, bz, mb, nb;
+      item_coords(item, p, tile, split, kb0, kb1);
       tile_coords(tile, p, bz, mb, nb);
+      stage_bias<BN>(p, sBias, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      if (!named_bar_all(1, kEpiThreads, ok)) break;  // also publishes the staged bias
       tc_fence_after();
-      const int m = mb * kBM + row;
-      const uint32_t t0 = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t0 + c * 32, r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          // Accumulator fully read: hand it back to the MMA warp before the last stores.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-        }
-        const int n0 = nb * BN + c * 32;
-        if (m < p.M && n0 < p.N) store_chunk<EPI, OUT>(p, bz, m, n0, r);
-      }
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(e.q * 32) << 16) + acc * BN;
+      auto release = [&] {
+        // This warp's part of the accumulator is read: hand it back to the MMA warp.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      };
+      epilogue_item<BN, EPI, OUT>(p, e, tacc, release, &tmD, bz, mb * kBM + e.row, nb * BN, tile, split);
     }
+    if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
 
   tc_fence_before();
@@ -326,38 +514,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------- 2-CTA variant
+// ---------------------------------------------------------------------------- 2-CTA kernel
 //
 // A cluster of two CTAs (on two SMs) computes one 256x256 output tile with
 // tcgen05.mma.cta_group::2 (M=256, N=256, K=16).  CTA r of the pair loads rows
 // [m0 + 128r, +128) of A and rows [n0 + 128r, +128) of B into its own shared memory; the
 // MMA, issued by CTA 0, reads both halves and leaves rows [m0 + 128r, +128) x 256 columns
 // of the accumulator in CTA r's TMEM.  Per SM this moves 32 KB of operands per 64-wide
-// k-block instead of 48 KB for a 1-CTA 128x256 tile with the same MMA time, and the
-// smaller stage allows a 6-deep ring.
+// k-block instead of 48 KB for a 1-CTA 128x256 tile with the same MMA time.
 //   full[s]   (CTA 0 only)  both CTAs' TMA bytes for stage s; CTA 0 arms it for 64 KB.
 //   empty[s]  (each CTA)    the pair's MMAs reading stage s have retired (broadcast commit).
 //   tfull[a]  (each CTA)    accumulator a is complete (broadcast commit).
-//   tempty[a] (CTA 0 only)  all 8 epilogue warps of the pair have read accumulator a.
+//   tempty[a] (CTA 0 only)  all 16 epilogue warps of the pair have read accumulator a.
 template <int STAGES, int EPI, int OUT, int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const TcParams p) {
-  constexpr int BN = 256;                          // pair tile is 256 x 256
-  constexpr uint32_t A_BYTES = kBM * kBK * 2;      // this CTA's 128 rows of A
-  constexpr uint32_t B_BYTES = 128 * kBK * 2;      // this CTA's 128 rows of B
-  constexpr uint32_t TMEM_COLS = 2 * BN;           // two 128-lane x 256-column accumulators
+                        const __grid_constant__ CUtensorMap tmD, const TcParams p) {
+  constexpr int BN = 256;
+  constexpr uint32_t A_BYTES = kBM * kBK * 2;  // this CTA's 128 rows of A
+  constexpr uint32_t B_BYTES = 128 * kBK * 2;  // this CTA's 128 rows of B
+  constexpr uint32_t TMEM_COLS = 512;          // two 128-lane x 256-column accumulators
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sOut = sB + STAGES * B_BYTES;
+  float* sBias = reinterpret_cast<float*>(sOut + kOutStageBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -372,12 +562,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 8);  // 4 epilogue warps x 2 CTAs
+      mbar_init(&tempty_bar[a], 2 * kEpiWarps);  // epilogue warps of both CTAs
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (p.tma_store) tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -398,12 +589,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, issued = 0;
       bool ok = true;
-      for (int tile = cluster; tile < p.num_tiles && ok; tile += nclusters) {
-        int bz, mb, nb;
+      for (int item = cluster; item < p.num_items && ok; item += nclusters) {
+        int tile, split, kb0, kb1, bz, mb, nb;
+        item_coords(item, p, tile, split, kb0, kb1);
         tile_coords(tile, p, bz, mb, nb);
         const int arow = mb * 256 + static_cast<int>(rank) * 128;
-        const int brow = nb * 256 + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        const int brow = nb * BN + static_cast<int>(rank) * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrWaitProducer)) {
             ok = false;
             break;
@@ -431,7 +623,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0, local = 0;
       bool ok = true;
-      for (int tile = cluster; tile < p.num_tiles && ok; tile += nclusters, ++local) {
+      for (int item = cluster; item < p.num_items && ok; item += nclusters, ++local) {
+        int tile, split, kb0, kb1;
+        item_coords(item, p, tile, split, kb0, kb1);
         const uint32_t acc = local & 1u;
         const uint32_t acc_phase = (local >> 1) & 1u;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kErrWaitMma)) {
@@ -440,7 +634,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma)) {
             ok = false;
             break;
@@ -451,8 +645,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
-            if constexpr (KIND == 1) umma_tf32_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
-            else umma_f16_pair(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
+            if constexpr (KIND == 1) umma_tf32_pair(d_tmem, ad, bd, idesc, accum);
+            else umma_f16_pair(d_tmem, ad, bd, idesc, accum);
           }
           umma_commit_pair_bcast(&empty_bar[stage], 0x3);
           if (++stage == STAGES) {
@@ -468,36 +663,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    uint32_t local = 0;
+    // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
+    EpiCtx e;
+    e.lane = lane;
+    e.q = warp & 3;
+    e.half = (warp - 2) >> 2;
+    e.row = e.q * 32 + lane;
+    e.buf = sOut + (warp - 2) * kOutBufBytes;
+    e.sbias = sBias;
+    e.bcast = bcast;
     const uint32_t leader_tempty0 = map_to_cta(smem_u32(&tempty_bar[0]), 0);
     const uint32_t leader_tempty1 = map_to_cta(smem_u32(&tempty_bar[1]), 0);
-    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
-      int bz, mb, nb;
+    uint32_t local = 0;
+    for (int item = cluster; item < p.num_items; item += nclusters, ++local) {
+      int tile, split, kb0, kb1, bz, mb, nb;
+      item_coords(item, p, tile, split, kb0, kb1);
       tile_coords(tile, p, bz, mb, nb);
+      stage_bias<BN>(p, sBias, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
-      if (!__all_sync(0xffffffffu, ok)) break;
+      if (!named_bar_all(1, kEpiThreads, ok)) break;
       tc_fence_after();
-      const int m = mb * 256 + static_cast<int>(rank) * 128 + row;
-      const uint32_t t0 = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t0 + c * 32, r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
-        }
-        const int n0 = nb * BN + c * 32;
-        if (m < p.M && n0 < p.N) store_chunk<EPI, OUT>(p, bz, m, n0, r);
-      }
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(e.q * 32) << 16) + acc * BN;
+      auto release = [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+      };
+      epilogue_item<BN, EPI, OUT>(p, e, tacc, release, &tmD, bz, mb * 256 + static_cast<int>(rank) * 128 + e.row,
+                                  nb * BN, tile * 2 + static_cast<int>(rank), split);
     }
+    if (lane == 0) bulk_wait_group_all();
   }
 
   // Neither CTA may leave (or free TMEM) while its peer can still touch its shared memory
@@ -512,10 +709,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------------------- host side
 
-// Relative per-tile time of the 2-CTA kernel vs the 1-CTA 128x256 kernel (tuned on B200).
-constexpr double kPairSpeed = 0.85;
+// Time per 64-wide k-block of one work item relative to a 2-CTA 256x256 pair tile, from the
+// sustained rates measured on B200 at the linear1 shape (pair 1469, 128x256 1247, 128x128
+// 913 TFLOP/s): a 128x128 tile on one SM takes 0.805 of a pair k-block, a 128x256 tile 1.178.
+constexpr double kCost128 = 0.805;
+constexpr double kCost256 = 1.178;
+constexpr double kCostPair = 1.0;
+// Fixed split-K overhead in pair-k-block units (partial store, arrival, last-split reduce).
+// Measured: the reduction is latency-bound and rarely pays, so automatic selection only
+// splits when it removes at least this much time.
+constexpr double kSplitOverhead = 24.0;
+// Shared-memory ring depth (6 x 32 KB measured slightly faster than 7 on B200).
+constexpr int kPairStages = 6;
+constexpr int kStages128 = 6;
+constexpr int kStages256 = 4;  // 4 x 48 KB
 int g_force_variant = -1;  // -1 auto, 0 = 1-CTA 128, 1 = 1-CTA 256, 2 = 2-CTA pair
+int g_force_splits = 0;    // 0 auto, else split-K factor
 bool g_allow_pair = true;
+int g_tma_store = -1;      // stage outputs through smem and TMA stores (B2G_TMA_STORE=0 disables)
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -532,8 +743,8 @@ b2g_status get_encode() {
   return B2G_OK;
 }
 
-// 3-D K-major operand map: dims {K, rows, batch}, box {128 bytes of K, box_rows, 1}, 128-byte swizzle,
-// out-of-bounds elements read as zero (so ragged M, N and K tiles need no special case).
+// 3-D K-major operand map: dims {K, rows, batch}, box {128 bytes of K, box_rows, 1}, 128-byte
+// swizzle, out-of-bounds elements read as zero (so ragged M, N and K tiles need no special case).
 b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, int64_t K, int64_t rows,
                             int64_t ld, int64_t batch, int64_t bstride, uint32_t box_rows) {
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows),
@@ -552,49 +763,70 @@ b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, in
   return B2G_OK;
 }
 
+// 3-D output map: dims {N, M, batch}, box {32, 32, 1} (one epilogue warp's chunk), swizzle
+// matching the staging layout (128 B for fp32 rows, 64 B for 16-bit rows).
+b2g_status make_output_map(CUtensorMap* map, void* base, b2g_dtype dt, int64_t N, int64_t M, int64_t ld,
+                           int64_t batch, int64_t bstride) {
+  const cuuint64_t esz = dt == B2G_F32 ? 4u : 2u;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(batch)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * esz, static_cast<cuuint64_t>(bstride) * esz};
+  const cuuint32_t box[3] = {32u, 32u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  const CUtensorMapDataType t = dt == B2G_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : dt == B2G_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapSwizzle sw = esz == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = g_encode(map, t, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(B2G_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed (" + std::to_string(r) + ")");
+  return B2G_OK;
+}
+
 template <typename Kern>
-b2g_status launch_kernel(Kern kern, size_t smem, const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm,
-                         int grid, cudaStream_t st) {
+b2g_status launch_kernel(Kern kern, size_t smem, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                         const TcParams& prm, int grid, cudaStream_t st) {
   b2g_status s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "cudaFuncSetAttribute(tc_gemm)");
   if (s != B2G_OK) return s;
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, prm);
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, td, prm);
   note_launch();
   return check_cuda(cudaGetLastError(), "tc_gemm launch");
 }
 
 // Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.
 template <bool PAIR, int BN, int STAGES, int EPI, int OUT, int KIND>
-b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid, cudaStream_t st) {
+b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const TcParams& prm,
+                      int grid, cudaStream_t st) {
   if constexpr (PAIR) {
-    constexpr size_t smem = 1024 + static_cast<size_t>(STAGES) * (kBM * kBK * 2 + 128 * kBK * 2) + 256;
+    constexpr size_t smem = smem_bytes(kBM * kBK * 2, 128 * kBK * 2, STAGES);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, ta, tb, prm, grid, st);
+    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, ta, tb, td, prm, grid, st);
   } else {
-    constexpr size_t smem = smem_bytes(BN, STAGES);
+    constexpr size_t smem = smem_bytes(kBM * kBK * 2, BN * kBK * 2, STAGES);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, ta, tb, prm, grid, st);
+    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, ta, tb, td, prm, grid, st);
   }
 }
 
 template <bool PAIR, int BN, int STAGES>
-b2g_status dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& prm, int grid,
-                        b2g_epilogue epi, b2g_dtype out, bool tf32, cudaStream_t st) {
+b2g_status dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const TcParams& prm,
+                        int grid, b2g_epilogue epi, b2g_dtype out, bool tf32, cudaStream_t st) {
   if (tf32) {
     // fp32 operands (batched_matmul_Bt): plain F32 output only.
     if (epi != B2G_EPI_NONE || out != B2G_F32) return set_error(B2G_ERR_UNSUPPORTED, "tf32 path: F32 output only");
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(ta, tb, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(ta, tb, td, prm, grid, st);
   }
   if (epi == B2G_EPI_GATED_RESIDUAL)
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(ta, tb, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(ta, tb, td, prm, grid, st);
   if (epi == B2G_EPI_GELU) {
-    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(ta, tb, prm, grid, st);
-    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(ta, tb, prm, grid, st);
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(ta, tb, prm, grid, st);
+    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(ta, tb, td, prm, grid, st);
+    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(ta, tb, td, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(ta, tb, td, prm, grid, st);
   }
-  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(ta, tb, prm, grid, st);
-  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(ta, tb, prm, grid, st);
-  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(ta, tb, prm, grid, st);
+  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(ta, tb, td, prm, grid, st);
+  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(ta, tb, td, prm, grid, st);
+  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(ta, tb, td, prm, grid, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -617,7 +849,7 @@ bool tc_gemm_supported(const GemmProblem& p, std::string* why) {
   const int64_t align = tf32 ? 3 : 7;  // 16-byte row and batch strides
   if ((p.lda & align) || (p.ldb & align)) return no("operand row stride not a multiple of 16 bytes");
   if (p.batch > 1 && ((p.a_bstride & align) || (p.b_bstride & align))) return no("batch stride not 16-byte aligned");
-  if (p.M > (1ll << 31) - kBM || p.N > (1ll << 31) - 256 || p.K > (1ll << 31)) return no("size");
+  if (p.M > (1ll << 31) - 256 || p.N > (1ll << 31) - 256 || p.K > (1ll << 31)) return no("size");
   if (p.batch > 65535) return no("batch");
   return true;
 }
@@ -627,27 +859,51 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
   if ((s = get_encode()) != B2G_OK) return s;
+  if (g_tma_store < 0) {
+    const char* t = getenv("B2G_TMA_STORE");
+    g_tma_store = (t && t[0] == '0') ? 0 : 1;
+  }
 
   const int sms = dev->num_sms;
-  const long long m128 = (p.M + 127) / 128, m256 = (p.M + 255) / 256;
-  const long long t128 = p.batch * m128 * ((p.N + 127) / 128);
-  const long long t256 = p.batch * m128 * ((p.N + 255) / 256);
-  const long long tpair = p.batch * m256 * ((p.N + 255) / 256);
   const int pairs = sms / 2;
-  // Estimated time in units of one 128x256 tile on one SM at the 1-CTA kernel's rate:
-  // whole waves over the SMs.  A 128-wide tile does half the work of a 256-wide one but
-  // re-reads A (10% penalty); a 2-CTA pair tile is one such unit on two SMs and runs at a
-  // higher tensor-pipe utilisation (operand bandwidth per SM is a third lower).
-  const double cost256 = static_cast<double>((t256 + sms - 1) / sms);
-  const double cost128 = static_cast<double>((t128 + sms - 1) / sms) * 0.55;
-  const double costpair = static_cast<double>((tpair + pairs - 1) / pairs) * kPairSpeed;
-  enum { V128, V256, VPAIR } v;
-  if (p.N <= 128) v = V128;
-  else if (costpair <= cost256 && costpair <= cost128 && g_allow_pair) v = VPAIR;
-  else v = cost128 < cost256 ? V128 : V256;
-  if (g_force_variant >= 0) v = static_cast<decltype(v)>(g_force_variant);
+  const bool tf32 = p.a_dtype == B2G_F32;
+  const int kelems = tf32 ? 32 : 64;
+  const long long nkb = (p.K + kelems - 1) / kelems;
+  // Kernel variant and split-K factor from a cost model in units of one 64-wide k-block of
+  // a pair tile: whole waves of work items over the SMs (or SM pairs), times the k-blocks
+  // per item, times the variant's measured relative cost per k-block, plus the split-K
+  // reduction overhead.
+  enum { V128 = 0, V256 = 1, VPAIR = 2 };
+  int v = VPAIR, splits = 1;
+  double best = 1e300;
+  for (int cand = 0; cand < 3; ++cand) {
+    if (cand == VPAIR && !g_allow_pair) continue;
+    if (cand != V128 && p.N <= 128) continue;
+    const long long tm = cand == VPAIR ? 256 : 128, tn = cand == V128 ? 128 : 256;
+    const long long tiles = p.batch * ((p.M + tm - 1) / tm) * ((p.N + tn - 1) / tn);
+    const long long slots = cand == VPAIR ? pairs : sms;
+    const double kb_cost = cand == V128 ? kCost128 : (cand == V256 ? kCost256 : kCostPair);
+    for (int sk = 1; sk <= 8 && sk <= nkb; ++sk) {
+      const long long items = tiles * sk;
+      const double waves = static_cast<double>((items + slots - 1) / slots);
+      const double per = static_cast<double>((nkb + sk - 1) / sk);
+      const double cost = kb_cost * (waves * per + (sk > 1 ? kSplitOverhead * sk : 0.0));
+      if (cost < best - 1e-9) {
+        best = cost;
+        v = cand;
+        splits = sk;
+      }
+    }
+  }
+  if (g_force_variant >= 0) {
+    v = g_force_variant;
+    if (g_force_splits <= 0) splits = 1;
+  }
+  if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
+  if (nkb == 0) splits = 1;
+  const bool pair = v == VPAIR;
   const int bn = v == V128 ? 128 : 256;
-  const int tile_m = v == VPAIR ? 256 : kBM;
+  const int tile_m = pair ? 256 : kBM;
 
   TcParams prm{};
   prm.M = static_cast<int>(p.M);
@@ -656,11 +912,11 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.batch = static_cast<int>(p.batch);
   prm.num_m_blocks = static_cast<int>((p.M + tile_m - 1) / tile_m);
   prm.num_n_blocks = static_cast<int>((p.N + bn - 1) / bn);
-  const bool tf32 = p.a_dtype == B2G_F32;
-  const int kelems = tf32 ? 32 : 64;
-  prm.num_k_blocks = static_cast<int>((p.K + kelems - 1) / kelems);
+  prm.num_k_blocks = static_cast<int>(nkb);
   prm.num_tiles = prm.batch * prm.num_m_blocks * prm.num_n_blocks;
-  const int group = v == VPAIR ? 8 : 16;
+  prm.splits = splits;
+  prm.num_items = prm.num_tiles * splits;
+  const int group = pair ? 8 : 16;
   prm.group_m = prm.num_m_blocks <= group ? prm.num_m_blocks : group;
   prm.d = p.d;
   prm.ldd = p.ldd;
@@ -677,25 +933,43 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.a_keep = a_bytes <= b_bytes ? 1 : 0;
   if (prm.num_tiles == 0) return B2G_OK;
 
-  CUtensorMap ta, tb;
+  if (splits > 1) {
+    const size_t slots = static_cast<size_t>(prm.num_tiles) * (pair ? 2 : 1);
+    void* ws = nullptr;
+    void* ctr = nullptr;
+    if ((s = workspace_get(slots * splits * 128 * bn * sizeof(float), &ws, kWsSplitK)) != B2G_OK) return s;
+    if ((s = workspace_get(slots * sizeof(int), &ctr, kWsCounters)) != B2G_OK) return s;
+    prm.ws = static_cast<float*>(ws);
+    prm.counters = static_cast<int*>(ctr);
+  }
+
+  CUtensorMap ta, tb, td;
   const int64_t a_bs = p.batch > 1 ? p.a_bstride : p.lda * p.M;
   const int64_t b_bs = p.batch > 1 ? p.b_bstride : p.ldb * p.N;
-  const uint32_t b_box = v == V128 ? 128u : (v == V256 ? 256u : 128u);
+  const uint32_t b_box = v == V256 ? 256u : 128u;
   if ((s = make_operand_map(&ta, p.a, p.a_dtype, p.K, p.M, p.lda, p.batch, a_bs, kBM)) != B2G_OK) return s;
   if ((s = make_operand_map(&tb, p.b, p.b_dtype, p.K, p.N, p.ldb, p.batch, b_bs, b_box)) != B2G_OK) return s;
-
-  if (v == VPAIR) {
-    const int grid = 2 * static_cast<int>(prm.num_tiles < pairs ? prm.num_tiles : pairs);
-    return dispatch_epi<true, 256, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  memset(&td, 0, sizeof(td));
+  prm.tma_store = 0;
+  if (p.epilogue != B2G_EPI_GATED_RESIDUAL && prm.vec_ok && g_tma_store) {
+    const int64_t d_bs = p.batch > 1 ? p.d_bstride : p.ldd * p.M;
+    if ((s = make_output_map(&td, p.d, p.d_dtype, p.N, p.M, p.ldd, p.batch, d_bs)) != B2G_OK) return s;
+    prm.tma_store = 1;
   }
-  const int grid = static_cast<int>(prm.num_tiles < sms ? prm.num_tiles : sms);
-  if (v == V256) return dispatch_epi<false, 256, 4>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
-  return dispatch_epi<false, 128, 6>(ta, tb, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+
+  if (pair) {
+    const int grid = 2 * static_cast<int>(prm.num_items < pairs ? prm.num_items : pairs);
+    return dispatch_epi<true, 256, kPairStages>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  }
+  const int grid = static_cast<int>(prm.num_items < sms ? prm.num_items : sms);
+  if (v == V256) return dispatch_epi<false, 256, kStages256>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  return dispatch_epi<false, 128, kStages128>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
 }
 
-void tc_gemm_set_variant(int force_variant, int allow_pair) {
+void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits) {
   g_force_variant = force_variant;
   g_allow_pair = allow_pair != 0;
+  g_force_splits = force_splits;
 }
 
 }  // namespace b2g

@@ -127,9 +127,10 @@ b2g_status b2g_check_device_error(int* code);
 uint64_t b2g_launch_count(void);
 
 /* Tensor-core kernel selection for tests and tuning (no reference counterpart):
- * -1 automatic (default), 0 = one CTA per 128x128 tile, 1 = one CTA per 128x256 tile,
- * 2 = a 2-CTA cluster per 256x256 tile.  Affects later calls in this process. */
-b2g_status b2g_set_gemm_variant(int variant);
+ * variant -1 automatic (default), 0 = one CTA per 128x128 tile, 1 = one CTA per 128x256
+ * tile, 2 = a 2-CTA cluster per 256x256 tile; splits 0 automatic, else the split-K factor
+ * (partials reduced in a fixed order by the last split).  Affects later calls. */
+b2g_status b2g_set_gemm_variant(int variant, int splits);
 
 #ifdef __cplusplus
 }

@@ -86,22 +86,64 @@ def test_gemm_bias_vs_fp64(engine, M, N, K, out_dtype):
 
 @pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (300, 700, 520), (1536, 3072, 3072), (100, 200, 72),
-                                   (513, 300, 3000)])
+                                   (513, 300, 3000), (777, 1300, 200)])
 def test_every_kernel_variant(engine, variant, M, N, K):
-    """Each tensor-core kernel (1-CTA 128/256-wide, 2-CTA pair) forced on ragged shapes."""
+    """Each tensor-core kernel (1-CTA 128/256-wide, 2-CTA 256x256 pair) forced on ragged
+    shapes, with bias and GELU epilogues and F32 / bf16 outputs."""
     x = seeded((M, K), 3 * M + K)
     w = seeded((N, K), 5 * N + K, 0.02)
     bias = seeded((N,), 9, 0.02, torch.float32)
     try:
-        engine.set_gemm_variant(variant)
+        engine.set_gemm_variant(variant, 1)
         out = engine.gemm(x, w, bias, out_dtype=torch.float32)
         out16 = engine.gemm(x, w, bias, out_dtype=torch.bfloat16, epilogue="gelu")
         torch.cuda.synchronize()
     finally:
-        engine.set_gemm_variant(-1)
+        engine.set_gemm_variant(-1, 0)
     ref = fp32_ref(x, w, bias)
     check(out, ref)
     check(out16, gelu_t(ref))
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("splits", [2, 3, 5])
+@pytest.mark.parametrize("M,N,K", [(512, 3072, 3072), (300, 700, 2000), (1024, 3072, 12288)])
+def test_split_k(engine, variant, splits, M, N, K):
+    """Split-K partial sums (workspace + last-arriver reduction) for every kernel variant and
+    epilogue kind, twice in a row (the arrival counters must re-arm themselves)."""
+    x = seeded((M, K), 7 * M + K)
+    w = seeded((N, K), 11 * N + K, 0.02)
+    bias = seeded((N,), 13, 0.02, torch.float32)
+    gate = seeded((N,), 14, 1.0, torch.float32)
+    r0 = seeded((M, N), 15, 1.0, torch.float32)
+    ref = fp32_ref(x, w, bias)
+    try:
+        engine.set_gemm_variant(variant, splits)
+        for _ in range(2):
+            out = engine.gemm(x, w, bias, out_dtype=torch.float32)
+            g16 = engine.gemm(x, w, bias, out_dtype=torch.bfloat16, epilogue="gelu")
+            res = r0.clone()
+            engine.gemm(x, w, bias, out=res, epilogue="gated_residual", gate=gate)
+            torch.cuda.synchronize()
+            check(out, ref)
+            check(g16, gelu_t(ref))
+            assert rel_err(res.cpu().numpy(), (r0.double() + gate.double() * ref).cpu().numpy()) <= TOL_F32_OUT
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    engine.check_device_error()
+
+
+def test_split_k_is_deterministic(engine):
+    x = seeded((512, 3072), 201)
+    w = seeded((3072, 3072), 202, 0.02)
+    try:
+        engine.set_gemm_variant(1, 4)
+        a = engine.gemm(x, w, out_dtype=torch.float32)
+        b = engine.gemm(x, w, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
