@@ -75,6 +75,8 @@ _SIGNATURES = {
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
     "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "b2g_attention_with_rope": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p,
+                                 ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
 
 
@@ -224,6 +226,24 @@ def linear_gated_residual(x: torch.Tensor, W: torch.Tensor, bias: torch.Tensor |
     _check(lib.b2g_linear_gated_residual(x.data_ptr(), _TORCH_TO_CUDA[x.dtype], W.data_ptr(),
                                          _TORCH_TO_CUDA[W.dtype], _ptr(b), residual_inout.data_ptr(),
                                          gate.data_ptr(), M, K, N_out))
+
+
+def attention_with_rope(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, pe: torch.Tensor, n_head: int,
+                        d_head: int, attn_mask: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """attention_with_rope (attention.cuh:23): F32 [L, n_head, d_head] Q/K/V -> F32 [L, n_head*d_head]."""
+    lib = load()
+    _require_cuda(Q, K, V, pe, attn_mask, out)
+    L = Q.shape[0]
+    for t in (Q, K, V, pe):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise B2GError("attention_with_rope: contiguous F32 tensors expected")
+    if out is None:
+        out = torch.empty((L, n_head * d_head), dtype=torch.float32, device=Q.device)
+    s = torch.cuda.current_stream(Q.device).cuda_stream
+    _check(lib.b2g_attention_with_rope(Q.data_ptr(), K.data_ptr(), V.data_ptr(), pe.data_ptr(), n_head, d_head, L,
+                                       _ptr(attn_mask), out.data_ptr(), ctypes.c_void_p(s)))
+    return out
 
 
 def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None:

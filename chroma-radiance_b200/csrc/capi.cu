@@ -269,6 +269,17 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64
   return run_gemm(p, st);
 }
 
+b2g_status b2g_attention_with_rope(const float* Q, const float* K, const float* V, const float* pe, int n_head,
+                                   int d_head, int64_t L, const float* attn_mask, float* out, void* stream) {
+  if (n_head < 0 || d_head < 0 || L < 0) return set_error(B2G_ERR_INVALID, "b2g_attention_with_rope: negative size");
+  if (L == 0 || n_head == 0) return B2G_OK;
+  if (!Q || !K || !V || !pe || !out) return set_error(B2G_ERR_INVALID, "b2g_attention_with_rope: null operand");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return attention_rope(Q, K, V, pe, attn_mask, out, L, n_head, d_head, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_check_device_error(int* code) {
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);

@@ -18,6 +18,7 @@ struct GemmProblem {
   b2g_epilogue epilogue = B2G_EPI_NONE;
   const float* gate = nullptr;
   bool allow_tf32 = false;  // F32 x F32 may run as TF32 products (batched_matmul_Bt only)
+  float alpha = 1.0f;       // D = epilogue(alpha * A.B^T + bias); internal (attention scores)
 };
 
 // Records a message for b2g_last_error() and returns `st`.
@@ -39,7 +40,7 @@ void note_launch(uint64_t n = 1);
 // Workspaces (device memory owned by the library, grown on demand, never shrunk), one per
 // purpose so that one call can use several.  kWsCounters is zero-filled when (re)allocated
 // and kernels leave it zero.
-enum WorkspaceSlot { kWsOperands = 0, kWsSplitK = 1, kWsCounters = 2, kWsSlots = 3 };
+enum WorkspaceSlot { kWsOperands = 0, kWsSplitK = 1, kWsCounters = 2, kWsAttention = 3, kWsSlots = 4 };
 b2g_status workspace_get(size_t bytes, void** ptr, int slot = kWsOperands);
 void workspace_release();
 
@@ -49,6 +50,11 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // Kernel variant override for tests/tuning: -1 automatic, 0 = 1-CTA 128x128 tiles,
 // 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits);
+
+// Attention with RoPE (attention.cu): q, k, v F32 [L, H*D], pe [L, D/2, 4], key_bias [L]
+// (0 / -inf) or null; out F32 [L, H*D].
+b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,
+                          float* out, int64_t L, int64_t H, int64_t D, cudaStream_t st);
 
 // Exact-fp32 CUDA-core path for everything the tensor-core path does not take.
 b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st);

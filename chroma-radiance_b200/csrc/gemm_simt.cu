@@ -25,6 +25,7 @@ struct SimtParams {
   void* d; int d_dtype; long long ldd, d_bstride;
   int epilogue;
   const float* gate;
+  float alpha;
 };
 
 __device__ __forceinline__ float load_elem(const void* base, int dt, long long idx) {
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
     for (int j = 0; j < 4; ++j) {
       const int n = n0 + tx * 4 + j;
       if (n >= p.N) continue;
-      float v = acc[i][j];
+      float v = p.alpha * acc[i][j];
       if (p.bias_kind == 1) v += static_cast<const float*>(p.bias)[n];
       else if (p.bias_kind == 2) v += __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
       const long long o = dbase + static_cast<long long>(m) * p.ldd + n;
@@ -162,6 +163,7 @@ b2g_status simt_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   s.d = p.d; s.d_dtype = p.d_dtype; s.ldd = p.ldd; s.d_bstride = p.d_bstride;
   s.epilogue = p.epilogue;
   s.gate = p.gate;
+  s.alpha = p.alpha;
   if (p.batch > 65535 || (p.M + kTile - 1) / kTile > 65535)
     return set_error(B2G_ERR_UNSUPPORTED, "SIMT GEMM: grid too large");
   dim3 grid(static_cast<unsigned>((p.N + kTile - 1) / kTile), static_cast<unsigned>((p.M + kTile - 1) / kTile),

@@ -75,6 +75,7 @@ struct TcParams {
   float* ws;               // split-K partials [slot][split][128][BN] fp32
   int* counters;           // split-K arrival counter per slot (zero between launches)
   int tma_store;           // 1: outputs leave through smem staging + TMA bulk tensor stores
+  float alpha;             // accumulator scale before the bias (1 for every linear layer)
 };
 
 __host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int stages) {
@@ -112,11 +113,15 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return 0.5f * v * (1.0f + tanhf(inner));
 }
 
-// acc + bias (bias staged in shared memory, zero past N), then GELU if asked.
+// alpha * acc + bias (bias staged in shared memory, zero past N), then GELU if asked.
 template <int EPI>
-__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], const float* sb, float (&v)[32]) {
+__device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], const float* sb, float alpha, float (&v)[32]) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+  if (alpha != 1.0f) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= alpha;
+  }
   if (sb) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
@@ -152,7 +157,7 @@ template <int EPI, int OUT>
 __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, int n0, const uint32_t (&r)[32],
                                             const float* sb) {
   float v[32];
-  chunk_values<EPI>(r, sb, v);
+  chunk_values<EPI>(r, sb, p.alpha, v);
   const bool full = (n0 + 32 <= p.N);
   const int nvalid = full ? 32 : (p.N - n0);
   const long long off = static_cast<long long>(bz) * p.d_bstride + static_cast<long long>(m) * p.ldd + n0;
@@ -204,13 +209,22 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
 }
 
 // Stages one 32x32 chunk (this warp's 32 rows x columns [n0, n0+32)) in shared memory and
-// writes it with one TMA store; the tensor map clips rows >= M and columns >= N.
+// writes it with one TMA store; the tensor map clips rows >= M and columns >= N.  The warp's
+// 4 KB staging area holds one fp32 chunk or two 16-bit chunks (double-buffered).
 template <int EPI, int OUT>
-__device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_t* buf, int bz, int m_warp0, int n0,
-                                                  const uint32_t (&r)[32], const float* sb, int lane) {
+__device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_t* stage, int& obuf, int bz,
+                                                  int m_warp0, int n0, const uint32_t (&r)[32], const float* sb,
+                                                  float alpha, int lane) {
   float v[32];
-  chunk_values<EPI>(r, sb, v);
-  if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
+  chunk_values<EPI>(r, sb, alpha, v);
+  uint8_t* buf = stage;
+  if constexpr (OUT == OUT_F32) {
+    if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
+  } else {
+    buf = stage + (obuf & 1) * 2048;
+    if (lane == 0) bulk_wait_group_read<1>();  // the store issued from this half two chunks ago
+  }
+  ++obuf;
   __syncwarp();
   if constexpr (OUT == OUT_F32) {
     // 128-byte rows, 128-byte swizzle: 16-byte chunk j of row `lane` goes to j ^ (lane % 8).
@@ -239,10 +253,11 @@ __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_
 
 // Writes one finished 32-column chunk: TMA-staged when enabled, else direct stores.
 template <int EPI, int OUT>
-__device__ __forceinline__ void emit_chunk(const TcParams& p, const CUtensorMap* tmD, uint8_t* buf, int bz, int m,
-                                           int m_warp0, int n0, const uint32_t (&r)[32], const float* sb, int lane) {
+__device__ __forceinline__ void emit_chunk(const TcParams& p, const CUtensorMap* tmD, uint8_t* buf, int& obuf, int bz,
+                                           int m, int m_warp0, int n0, const uint32_t (&r)[32], const float* sb,
+                                           int lane) {
   if (EPI != B2G_EPI_GATED_RESIDUAL && p.tma_store) {
-    if (m_warp0 < p.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, bz, m_warp0, n0, r, sb, lane);  // uniform
+    if (m_warp0 < p.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, obuf, bz, m_warp0, n0, r, sb, p.alpha, lane);
   } else if (m < p.M && n0 < p.N) {
     store_chunk<EPI, OUT>(p, bz, m, n0, r, sb);
   }
@@ -276,8 +291,9 @@ __device__ __forceinline__ void stage_bias(const TcParams& p, float* sbias, int 
 // partial; the split arriving last on the slot's counter sums all partials in split order
 // (deterministic), runs the epilogue and re-arms the counter for the next launch.
 template <int BN, int EPI, int OUT, typename Release>
-__device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e, uint32_t tacc, Release release,
-                                              const CUtensorMap* tmD, int bz, int m, int n_base, int slot, int split) {
+__device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e, int& obuf, uint32_t tacc,
+                                              Release release, const CUtensorMap* tmD, int bz, int m, int n_base,
+                                              int slot, int split) {
   constexpr int NCH = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
   const int c0 = e.half * NCH;
   const int m_warp0 = m - e.lane;
@@ -293,8 +309,8 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e
     if (i == NCH - 1) release();
     const int c = c0 + i;
     if (!splitk) {
-      emit_chunk<EPI, OUT>(p, tmD, e.buf, bz, m, m_warp0, n_base + c * 32, r[i & 1], sb ? sb + c * 32 : nullptr,
-                           e.lane);
+      emit_chunk<EPI, OUT>(p, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, r[i & 1],
+                           sb ? sb + c * 32 : nullptr, e.lane);
     } else {
       float4* dst = reinterpret_cast<float4*>(part + c * 32);
 #pragma unroll
@@ -331,7 +347,8 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e
         uint32_t rr[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) rr[j] = __float_as_uint(acc[j]);
-        emit_chunk<EPI, OUT>(p, tmD, e.buf, bz, m, m_warp0, n_base + c * 32, rr, sb ? sb + c * 32 : nullptr, e.lane);
+        emit_chunk<EPI, OUT>(p, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, rr, sb ? sb + c * 32 : nullptr,
+                             e.lane);
       }
       if (threadIdx.x == 64) p.counters[slot] = 0;
     }
@@ -483,6 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     e.buf = sOut + (warp - 2) * kOutBufBytes;
     e.sbias = sBias;
     e.bcast = bcast;
+    int obuf = 0;
     uint32_t local = 0;
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x, ++local) {
       int tile, split, kb0, kb1, bz, mb, nb;
@@ -501,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       };
-      epilogue_item<BN, EPI, OUT>(p, e, tacc, release, &tmD, bz, mb * kBM + e.row, nb * BN, tile, split);
+      epilogue_item<BN, EPI, OUT>(p, e, obuf, tacc, release, &tmD, bz, mb * kBM + e.row, nb * BN, tile, split);
     }
     if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
@@ -674,6 +692,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     e.bcast = bcast;
     const uint32_t leader_tempty0 = map_to_cta(smem_u32(&tempty_bar[0]), 0);
     const uint32_t leader_tempty1 = map_to_cta(smem_u32(&tempty_bar[1]), 0);
+    int obuf = 0;
     uint32_t local = 0;
     for (int item = cluster; item < p.num_items; item += nclusters, ++local) {
       int tile, split, kb0, kb1, bz, mb, nb;
@@ -691,8 +710,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
       };
-      epilogue_item<BN, EPI, OUT>(p, e, tacc, release, &tmD, bz, mb * 256 + static_cast<int>(rank) * 128 + e.row,
-                                  nb * BN, tile * 2 + static_cast<int>(rank), split);
+      epilogue_item<BN, EPI, OUT>(p, e, obuf, tacc, release, &tmD, bz,
+                                  mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN,
+                                  tile * 2 + static_cast<int>(rank), split);
     }
     if (lane == 0) bulk_wait_group_all();
   }
@@ -924,6 +944,7 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   prm.bias = p.bias;
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.gate = p.gate;
+  prm.alpha = p.alpha;
   prm.err = dev->err_word;
   prm.idesc = idesc_make(tf32 ? kFmtTF32 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16), tile_m, bn);
   const int out_bytes = p.d_dtype == B2G_F32 ? 4 : 2;

@@ -117,6 +117,18 @@ b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type,
 b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
                                  int64_t batch, int64_t M, int64_t K, int64_t N);
 
+/* out[L, n_head*d_head] (F32) = softmax(rope(Q) rope(K)^T / sqrt(d_head) + mask) V per head.
+ * Q, K, V: F32 [L, n_head, d_head] (Q and K already RMS-normed), pe: F32 [L, d_head/2, 4]
+ * (cos, -sin, sin, cos per rotation pair), attn_mask: F32 [L] key bias (0 or -inf) or NULL.
+ * Replaces
+ *   static Tensor attention_with_rope(const Tensor& Q, const Tensor& K, const Tensor& V,
+ *       const Tensor& pe, int n_head, int d_head, const float* attn_mask)  attention.cuh:23-28
+ * i.e. cudnn_attention_with_rope (cudnn_attention.cuh:449-476): RoPE + bf16 operands, fp32
+ * softmax, bf16 probabilities; here QK^T and PV are tcgen05 batched GEMMs.  Requires L and
+ * d_head to be multiples of 8.  Uses a library workspace of about n_head*L*L*6 bytes. */
+b2g_status b2g_attention_with_rope(const float* Q, const float* K, const float* V, const float* pe, int n_head,
+                                   int d_head, int64_t L, const float* attn_mask, float* out, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

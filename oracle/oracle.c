@@ -316,6 +316,69 @@ void oracle_rms_norm(const float* x, const float* scale, float* out, int64_t row
   }
 }
 
+/*
+ * Attention with RoPE, restating cudnn_attention_with_rope (cudnn_attention.cuh:449-476):
+ *   Qr, Kr = RoPE(Q), RoPE(K) rounded to bf16 (apply_rope_fused_bf16, rope.cuh:180-221:
+ *            out_even = x_e*cos + x_o*(-sin), out_odd = x_e*sin + x_o*cos from pe [L, D/2, 4]);
+ *   V rounded to bf16 (permute_and_convert_to_bf16, kernels.cu:3197);
+ *   S = Qr.Kr^T / sqrt(D) + mask[key]   (fp32; mask 0 or -inf);
+ *   P = softmax(S) rounded to bf16 (flash attention feeds bf16 probabilities to the PV
+ *   product); O = P.V in fp32, rounded to bf16 (SDPA writes bf16 O), returned as fp32
+ *   [L, H*D] (unpermute_bf16_to_f32, cudnn_attention.cuh:52-77).
+ * Q, K, V: [L, H, D] fp32.  Single-threaded over heads (small sizes only).
+ */
+int oracle_attention_rope(const float* Q, const float* K, const float* V, const float* pe, const float* mask,
+                          float* out, int64_t L, int64_t H, int64_t D) {
+  const int64_t HD = H * D, half = D / 2;
+  float* qr = (float*)malloc(sizeof(float) * (size_t)(L * D));
+  float* kr = (float*)malloc(sizeof(float) * (size_t)(L * D));
+  float* vr = (float*)malloc(sizeof(float) * (size_t)(L * D));
+  float* srow = (float*)malloc(sizeof(float) * (size_t)L);
+  if (!qr || !kr || !vr || !srow) {
+    free(qr); free(kr); free(vr); free(srow);
+    return -1;
+  }
+  const float scale = 1.0f / sqrtf((float)D);
+  for (int64_t h = 0; h < H; ++h) {
+    for (int64_t l = 0; l < L; ++l) {
+      for (int64_t j = 0; j < half; ++j) {
+        const float* p = pe + (l * half + j) * 4;
+        const int64_t i = l * HD + h * D + 2 * j;
+        const float qe = Q[i], qo = Q[i + 1], ke = K[i], ko = K[i + 1];
+        qr[l * D + 2 * j] = oracle_bf16_to_f32(oracle_f32_to_bf16(qe * p[0] + qo * p[1]));
+        qr[l * D + 2 * j + 1] = oracle_bf16_to_f32(oracle_f32_to_bf16(qe * p[2] + qo * p[3]));
+        kr[l * D + 2 * j] = oracle_bf16_to_f32(oracle_f32_to_bf16(ke * p[0] + ko * p[1]));
+        kr[l * D + 2 * j + 1] = oracle_bf16_to_f32(oracle_f32_to_bf16(ke * p[2] + ko * p[3]));
+      }
+      for (int64_t d = 0; d < D; ++d) vr[l * D + d] = oracle_bf16_to_f32(oracle_f32_to_bf16(V[l * HD + h * D + d]));
+    }
+    for (int64_t i = 0; i < L; ++i) {
+      float mx = -INFINITY;
+      for (int64_t j = 0; j < L; ++j) {
+        float acc = 0.f;
+        for (int64_t d = 0; d < D; ++d) acc += qr[i * D + d] * kr[j * D + d];
+        const float sv = acc * scale + (mask ? mask[j] : 0.f);
+        srow[j] = sv;
+        if (sv > mx) mx = sv;
+      }
+      double sum = 0.0;
+      for (int64_t j = 0; j < L; ++j) {
+        srow[j] = (mx == -INFINITY) ? 0.f : expf(srow[j] - mx);
+        sum += srow[j];
+      }
+      const float inv = sum > 0 ? (float)(1.0 / sum) : 0.f;
+      for (int64_t j = 0; j < L; ++j) srow[j] = oracle_bf16_to_f32(oracle_f32_to_bf16(srow[j] * inv));
+      for (int64_t d = 0; d < D; ++d) {
+        float acc = 0.f;
+        for (int64_t j = 0; j < L; ++j) acc += srow[j] * vr[j * D + d];
+        out[i * HD + h * D + d] = oracle_bf16_to_f32(oracle_f32_to_bf16(acc));
+      }
+    }
+  }
+  free(qr); free(kr); free(vr); free(srow);
+  return 0;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

@@ -55,6 +55,8 @@ class Oracle:
         lib.oracle_f32_to_f16_array.argtypes = [_c_p, _c_p, _i64]
         lib.oracle_to_f32.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
         lib.oracle_num_threads.restype = ctypes.c_int
+        lib.oracle_attention_rope.argtypes = [_c_p] * 6 + [_i64] * 3
+        lib.oracle_attention_rope.restype = ctypes.c_int
         self.lib = lib
 
     def num_threads(self) -> int:
@@ -144,6 +146,17 @@ class Oracle:
                                  _np_ptr(np.ascontiguousarray(scale, np.float32)), _np_ptr(out), M, C, eps)
         return out
 
+    def attention_rope(self, Q, K, V, pe, mask=None):
+        """Q, K, V F32 [L, H, D]; pe [L, D/2, 4]; mask [L] or None -> F32 [L, H*D]."""
+        Q, K, V, pe = (np.ascontiguousarray(a, np.float32) for a in (Q, K, V, pe))
+        L, H, D = Q.shape
+        out = np.empty((L, H * D), dtype=np.float32)
+        m = None if mask is None else np.ascontiguousarray(mask, np.float32)
+        if self.lib.oracle_attention_rope(_np_ptr(Q), _np_ptr(K), _np_ptr(V), _np_ptr(pe), _np_ptr(m), _np_ptr(out),
+                                          L, H, D) != 0:
+            raise MemoryError("oracle_attention_rope")
+        return out
+
     def rms_norm(self, x, scale, eps=1e-6):
         x = np.ascontiguousarray(x, dtype=np.float32)
         out = np.empty_like(x)
@@ -190,6 +203,29 @@ class Ref:
 
     def __getattr__(self, name):
         return getattr(self.lib, "ref_" + name)
+
+
+ATTN_REF_PATH = HERE / "_ref" / "libref_attention.so"
+
+
+class AttnRef:
+    """The reference's attention (cuDNN-frontend flash SDPA with RoPE), built from its sources."""
+
+    def __init__(self, path: str | os.PathLike = ATTN_REF_PATH):
+        if not Path(path).exists():
+            raise FileNotFoundError(f"{path} missing: built by `make -C oracle` where the reference sources are present")
+        lib = ctypes.CDLL(str(path))
+        lib.ref_attn_init.restype = ctypes.c_int
+        lib.ref_attention_with_rope.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, _c_p, _c_p]
+        lib.ref_attention_with_rope.restype = ctypes.c_int
+        lib.ref_bench_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, _c_p, ctypes.c_int,
+                                                         ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+        lib.ref_bench_attention.restype = ctypes.c_int
+        lib.ref_attn_init()
+        self.lib = lib
+
+    def attention_with_rope(self, Q, K, V, pe, n_head, d_head, L, mask, out):
+        return self.lib.ref_attention_with_rope(Q, K, V, pe, n_head, d_head, L, mask, out)
 
 
 def available() -> dict:

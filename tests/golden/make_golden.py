@@ -20,7 +20,7 @@ import torch
 
 REPO = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(REPO / "oracle"))
-from oracle import BF16, CUDA_R_16BF, CUDA_R_16F, CUDA_R_32F, F16, F32, Oracle, Ref  # noqa: E402
+from oracle import BF16, CUDA_R_16BF, CUDA_R_16F, CUDA_R_32F, F16, F32, AttnRef, Oracle, Ref  # noqa: E402
 
 DEV = torch.device("cuda:0")
 ORC = Oracle()  # only for float -> bf16/fp16 bit conversion of the seeded inputs
@@ -160,6 +160,22 @@ def main(out_dir: Path) -> None:
     ref.sync()
     save("modulate_to_bf16", x=mx, shift=sh, scale=sc, out_bf16=host(mo, np.uint16))
     save("rms_norm", x=rx, scale=rs, out=host(ro2, np.float32))
+
+    # attention_with_rope (attention.cuh:23 -> cuDNN SDPA), with a 0/-inf key mask
+    attn = AttnRef()
+    rng = np.random.default_rng(12)
+    L, H, D = 128, 2, 128
+    aq, ak, av = (rng.standard_normal((L, H, D), dtype=np.float32) for _ in range(3))
+    ang = rng.uniform(0, 2 * np.pi, (L, D // 2)).astype(np.float32)
+    pe = np.stack([np.cos(ang), -np.sin(ang), np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+    mask = np.zeros(L, np.float32)
+    mask[40:64] = -np.inf
+    dq, dk, dv, dpe, dm = dev(aq), dev(ak), dev(av), dev(pe), dev(mask)
+    ao = torch.zeros((L, H * D), dtype=torch.float32, device=DEV)
+    attn.attention_with_rope(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dpe.data_ptr(), H, D, L, dm.data_ptr(),
+                             ao.data_ptr())
+    torch.cuda.synchronize()
+    save("attention_rope", q=aq, k=ak, v=av, pe=pe, mask=mask, out=host(ao, np.float32))
 
     (out_dir / "MANIFEST.txt").write_text(
         "Golden vectors from the reference's own kernels (oracle/_ref/libref_cublaslt.so, cuBLASLt "

@@ -353,3 +353,56 @@ def test_native_kernels_ran_and_no_device_timeouts(engine):
     engine.gemm(x, x)
     assert engine.launch_count() > n0
     engine.check_device_error()
+
+
+def rope_table(L, D, seed):
+    g = np.random.default_rng(seed)
+    ang = g.uniform(0, 2 * np.pi, (L, D // 2))
+    return np.stack([np.cos(ang), -np.sin(ang), np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+
+
+@pytest.mark.parametrize("L,H,D,masked", [(64, 2, 64, 8), (200, 3, 128, 0), (136, 2, 128, 40)])
+def test_attention_vs_oracle(engine, oracle, L, H, D, masked):
+    g = torch.Generator().manual_seed(L + H)
+    Q, K, V = (torch.randn((L, H, D), generator=g) for _ in range(3))
+    pe = rope_table(L, D, L)
+    mask = np.zeros(L, np.float32)
+    if masked:
+        mask[L // 3:L // 3 + masked] = -np.inf
+    out = engine.attention_with_rope(Q.to(DEV), K.to(DEV), V.to(DEV), torch.from_numpy(pe).to(DEV), H, D,
+                                     torch.from_numpy(mask).to(DEV) if masked else None)
+    want = oracle.attention_rope(Q.numpy(), K.numpy(), V.numpy(), pe, mask if masked else None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) < 1e-2
+
+
+def attn_ref_or_skip():
+    from oracle import ATTN_REF_PATH, AttnRef
+
+    if not ATTN_REF_PATH.exists():
+        pytest.skip("reference attention library not built")
+    return AttnRef()
+
+
+@pytest.mark.parametrize("L,text_masked", [(1536, 400), (512, 0)])
+def test_attention_vs_reference_cudnn(engine, L, text_masked):
+    """Config 2: 24 heads x 128 at S=1536 with a 0/-inf key mask on 400 of the 512 text
+    tokens, against the reference's cuDNN SDPA path on identical buffers."""
+    ref = attn_ref_or_skip()
+    H, D = 24, 128
+    g = torch.Generator().manual_seed(7)
+    Q, K, V = (torch.randn((L, H, D), generator=g).to(DEV) for _ in range(3))
+    pe = torch.from_numpy(rope_table(L, D, 3)).to(DEV)
+    mask = torch.zeros(L, device=DEV)
+    if text_masked:
+        mask[512 - text_masked:512] = float("-inf")
+    mine = engine.attention_with_rope(Q, K, V, pe, H, D, mask)
+    theirs = torch.empty((L, H * D), device=DEV)
+    ref.attention_with_rope(Q.data_ptr(), K.data_ptr(), V.data_ptr(), pe.data_ptr(), H, D, L, mask.data_ptr(),
+                            theirs.data_ptr())
+    torch.cuda.synchronize()
+    a, b = mine.double().cpu().numpy().ravel(), theirs.double().cpu().numpy().ravel()
+    assert rel_err(a, b) < 1e-2
+    assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999

@@ -23,7 +23,7 @@ def load(name):
 def test_fixtures_present():
     expected = {"linear_lt_bf16_bias", "linear_lt_bf16_nobias", "linear_lt_fp16", "linear_lt_f32_k67",
                 "linear_f32x_bf16w", "linear_f32x_fp16w", "linear_gated_residual_bf16", "gelu",
-                "gated_residual", "batched_matmul_Bt", "modulate_to_bf16", "rms_norm"}
+                "gated_residual", "batched_matmul_Bt", "modulate_to_bf16", "rms_norm", "attention_rope"}
     missing = expected - set(FIXTURES)
     assert not missing, f"missing golden fixtures: {sorted(missing)}"
 
@@ -93,6 +93,17 @@ def test_modulate_to_bf16(oracle):
     got = oracle.to_bf16_bits(oracle.modulate(g["x"], g["shift"], g["scale"], 1e-6)).astype(np.int32)
     want = g["out_bf16"].astype(np.int32)
     assert np.abs(got - want).max() <= 1
+
+
+def test_attention_rope(oracle):
+    """The oracle's attention restatement against the reference's cuDNN SDPA path."""
+    g = load("attention_rope")
+    got = oracle.attention_rope(g["q"], g["k"], g["v"], g["pe"], g["mask"])
+    # bf16 operands and probabilities on both sides, different accumulation order and
+    # normalisation point: agreement to a few bf16 ulps of the largest output.
+    assert rel_err(got, g["out"]) < 1e-2
+    a, b = got.ravel().astype(np.float64), g["out"].ravel().astype(np.float64)
+    assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
 
 
 def test_rms_norm(oracle):

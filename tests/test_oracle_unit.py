@@ -67,3 +67,31 @@ def test_modulate_and_rms_norm(oracle):
     assert rel_err(oracle.modulate(x, sh, sc), ln * (1 + sc) + sh) < 1e-5
     rms = xd / np.sqrt((xd ** 2).mean(1, keepdims=True) + 1e-6) * sc
     assert rel_err(oracle.rms_norm(x, sc), rms) < 1e-5
+
+
+def test_attention_matches_float64_within_bf16(oracle):
+    rng = np.random.default_rng(5)
+    L, H, D = 24, 2, 16
+    Q, K, V = (rng.standard_normal((L, H, D)).astype(np.float32) for _ in range(3))
+    ang = rng.uniform(0, 2 * np.pi, (L, D // 2))
+    pe = np.stack([np.cos(ang), -np.sin(ang), np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+    mask = np.zeros(L, np.float32)
+    mask[5:9] = -np.inf
+    got = oracle.attention_rope(Q, K, V, pe, mask)
+
+    def rope(x):
+        e, o = x[..., 0::2].astype(np.float64), x[..., 1::2].astype(np.float64)
+        c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+        r = np.empty(x.shape)
+        r[..., 0::2], r[..., 1::2] = e * c - o * s, e * s + o * c
+        return r
+
+    q, k = rope(Q), rope(K)
+    want = np.empty((L, H * D))
+    for h in range(H):
+        s_ = q[:, h] @ k[:, h].T / np.sqrt(D) + mask[None, :]
+        p = np.exp(s_ - s_.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        want[:, h * D:(h + 1) * D] = p @ V[:, h].astype(np.float64)
+    assert rel_err(got, want) < 2e-2
+    assert np.all(got[:, :] == got[:, :])  # no NaN from the -inf keys
