@@ -1,27 +1,34 @@
-"""Benchmark of the B200 GEMM engine on BASELINE config 1, plus the reference's own arm.
+"""Benchmark of the B200 GEMM engine on BASELINE configs 2 and 1, plus the reference's own arm.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b2g|reference]
+                    [--workload config2|config1]
 
-Workload (the single-stream linear1 GEMM at 512^2): X bf16
-[1536, 3072] ~ N(0,1), W bf16 [21504, 3072] ~ N(0, 0.02), bias [21504] ~ N(0, 0.02) (bf16
-values), seed 0, fp32 accumulation.  The engine writes a bf16 output; the reference's
-linear_lt writes F32 (it has no bf16-output mode).  One "step" = one GEMM over that batch.
-Inputs come from numpy (PCG64, seed 0), identical for both arms.
+config2 (default; the configuration the metric is quoted on): one "step" = one Chroma
+double-stream block and one single-stream block at 512^2 (T=512 text + I=1024 image tokens,
+hidden 3072, 24 heads x 128, MLP 12288): every GEMM of both blocks (txt/img qkv, proj, MLP
+with GELU, linear1, linear2, with bias and gated residuals) and both attentions (qk-norm,
+RoPE, QK^T and PV over 24 heads, 0/-inf key mask on 400 of the 512 text tokens).  Weights
+~N(0,0.02) bf16, biases ~N(0,0.02), activations ~N(0,1), gates ~N(0,1), seeded.
+  value     TFLOP/s over all ranks: (linear + unmasked attention FLOPs = 753.77 GFLOP per
+            step) * steps * ranks / (max over ranks of the summed per-step CUDA-event time).
+            The engine replays the step as two CUDA graphs; weights (680 MB) are larger than
+            L2, and a 256 MB buffer is also written before every step, outside the events.
+  roofline  dominant kernel = the engine's tcgen05 GEMM (13 launches per step): GEMM FLOPs /
+            summed GEMM launch time, from events recorded between the launches inside the
+            graphs during the timed steps; peak = MEASURED_PEAKS.json bf16_tflops.
+  e2e       the same step through the public API with host buffers: the step's activations
+            (modulated bf16 inputs, F32 residual streams, gates) copied from pinned host
+            memory and the updated residual streams copied back, inside the event pair; the
+            copies run on side streams and overlap the other block's compute.
+config1: one GEMM, the single-stream linear1 at 512^2 (M=1536 K=3072 N=21504, bias, bf16 out),
+inputs from numpy PCG64 seed 0, identical for both arms.
+cpu_baseline  the fp32 C oracle (oracle/oracle.c, OpenMP, all host cores) on a bounded row
+            sample of the single-stream linear1 GEMM (rank 0, N=1 only).
 
-  value     TFLOP/s over all ranks: 2*M*N*K*steps*ranks / (max over ranks of the summed
-            per-step CUDA-event time); inputs resident in HBM; L2 flushed (256 MB write)
-            before every step, outside the event pair.
-  e2e       same metric through the public API with host buffers: per step, X copied from
-            pinned host memory, GEMM, output copied back, all inside the event pair.
-  roofline  tensor-bound: achieved = algorithmic FLOP per launch / mean launch time of the
-            GEMM kernel (events on its stream), peak = MEASURED_PEAKS.json bf16_tflops.
-  cpu_baseline  the fp32 C oracle (oracle/oracle.c, OpenMP, all host cores) on a bounded
-            sample of the same GEMM (rank 0, N=1 only).
-
---impl reference runs the reference's own linear_lt (cuBLASLt, compiled from its sources
-into oracle/_ref/) on the same inputs, timed the same way, and never imports the engine.
-Multi-GPU (torchrun): every rank runs its own replica (weak scaling, no collective on the
-data path); rank 0 prints the line.
+--impl reference runs the reference's own code (its cuBLASLt linear / linear_lt, rms_norm,
+cuDNN attention and elementwise kernels, compiled from its sources into oracle/_ref/) on the
+same workload, timed the same way, and never imports the engine.  Multi-GPU (torchrun): every
+rank runs its own replica (weak scaling, no collective on the data path); rank 0 prints.
 """
 from __future__ import annotations
 
@@ -139,7 +146,8 @@ def cpu_baseline(o, x, w, bias) -> dict:
     o.linear(x[:rows2], 2, w, 2, bias)
     dt = time.perf_counter() - t
     return {"value": 2.0 * rows2 * N * K / dt / 1e12, "unit": "TFLOP/s", "cores": o.num_threads(),
-            "kind": "port", "sample": f"{rows2} of {M} rows of X against all of W ({rows2 * 2 * N * K / 1e9:.1f} "
+            "kind": "port", "sample": f"single-stream linear1 GEMM (the config-1 shape, one of the block pair's "
+                                      f"GEMMs): {rows2} of {M} rows of X against all of W ({rows2 * 2 * N * K / 1e9:.1f} "
                                       f"GFLOP, {dt:.1f} s, bf16 inputs widened to fp32, fp32 accumulate)"}
 
 
@@ -150,7 +158,7 @@ def dist_setup():
     return world, rank, local
 
 
-def run_reference(args) -> None:
+def run_reference_config1(args) -> None:
     """The reference's linear_lt (cuBLASLt) from oracle/_ref, timed with CUDA events in C."""
     import ctypes
 
@@ -188,7 +196,7 @@ def run_reference(args) -> None:
     print(json.dumps(line))
 
 
-def run_engine(args) -> None:
+def run_engine_config1(args) -> None:
     import torch
 
     import b2g
@@ -290,20 +298,282 @@ def run_engine(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+T_TXT, I_IMG, MASKED = 512, 1024, 400
+WORKLOAD2 = ("config2: one double-stream + one single-stream Chroma block at 512^2 (T=512 txt + I=1024 img "
+             "tokens, hidden 3072, 24x128 heads, MLP 12288, key mask on 400 of 512 txt tokens)")
+
+
+def run_reference_config2(args) -> None:
+    """The reference's block code (oracle/_ref/libref_attention.so): its own linear(),
+    linear_gated_residual(), rms_norm, cuDNN attention and elementwise kernels in its own call
+    order, on inputs from its own Philox generator; timed with CUDA events in C."""
+    import ctypes
+
+    import oracle as oracle_mod
+
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    os.environ.setdefault("CUDA_VISIBLE_DEVICES", str(local))
+    if not oracle_mod.ATTN_REF_PATH.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_attention.so was not built "
+                          "(the reference sources were absent at build time)"}))
+        return
+    import blocks
+
+    ref = oracle_mod.AttnRef()
+    dp, sp = (ctypes.c_void_p * 32)(), (ctypes.c_void_p * 11)()
+    rc = ref.lib.ref_alloc_blocks(0, T_TXT, I_IMG, MASKED, dp, sp)
+    if rc != 0:
+        raise RuntimeError(f"ref_alloc_blocks failed: {rc}")
+    ms = ctypes.c_double(0)
+    with ClockSampler(local) as clk:
+        rc = ref.lib.ref_bench_blocks(dp, sp, T_TXT, I_IMG, args.steps, args.warmup, FLUSH_BYTES, ctypes.byref(ms))
+    if rc != 0:
+        raise RuntimeError(f"ref_bench_blocks failed: CUDA error {rc}")
+    lin, att = blocks.block_pair_flops(T_TXT, I_IMG)
+    per = ms.value / args.steps
+    value = (lin + att) / (per * 1e-3) / 1e12
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (reference Philox, seed 0)",
+        "config": {"workload": WORKLOAD2, "flop_per_step": lin + att,
+                   "l2": "weights 680 MB > L2; 256 MB buffer written before every step, outside the events"},
+        "cpu_baseline": {"kind": "reference", "cores": 0, "value": round(value, 2), "unit": "TFLOP/s",
+                         "sample": "the reference has no CPU path; this arm is its own block code (chroma.cuh "
+                                   "double/single block GEMM + attention calls, cublas_ops.cuh, cuDNN SDPA) "
+                                   "built from its sources and run on the B200"},
+        "e2e": {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "clocks": clk.summary(),
+    }))
+
+
+class _Marks:
+    """Timing events recorded between the launches of a captured block (external event nodes)."""
+
+    def __init__(self, torch, stream):
+        self.torch, self.stream = torch, stream
+        self.events, self.labels = [], []
+        self.start = torch.cuda.Event(enable_timing=True, external=True)
+
+    def begin(self):
+        self.start.record(self.stream)
+
+    def __call__(self, label):
+        ev = self.torch.cuda.Event(enable_timing=True, external=True)
+        ev.record(self.stream)
+        self.events.append(ev)
+        self.labels.append(label)
+
+    def durations(self):
+        out, prev = {}, self.start
+        for lab, ev in zip(self.labels, self.events):
+            out[lab] = prev.elapsed_time(ev)
+            prev = ev
+        return out
+
+
+def run_engine_config2(args) -> None:
+    import torch
+
+    import b2g
+    import blocks
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    b2g.init()
+    T, I = T_TXT, I_IMG
+    L = T + I
+    H = blocks.HIDDEN
+    gdev = torch.Generator(device=dev).manual_seed(0)
+    txt_w, img_w = blocks.random_stream(gdev, dev), blocks.random_stream(gdev, dev)
+    sw = blocks.random_single(gdev, dev)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=gdev, device=dev) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    mask = torch.zeros(L, device=dev)
+    mask[T - MASKED:T] = float("-inf")
+    # Step inputs: generated on the host (seeded) and kept pinned for the end-to-end leg.
+    gh = torch.Generator().manual_seed(1)
+    host = {}
+    for name, rows, dt in (("txt_mod1", T, torch.bfloat16), ("img_mod1", I, torch.bfloat16),
+                           ("txt_mod2", T, torch.bfloat16), ("img_mod2", I, torch.bfloat16),
+                           ("txt", T, torch.float32), ("img", I, torch.float32),
+                           ("x_mod", L, torch.bfloat16), ("x", L, torch.float32)):
+        host[name] = torch.randn((rows, H), generator=gh).to(dt).pin_memory()
+    host["gates"] = torch.randn((5, H), generator=gh).pin_memory()
+    d = {k: v.to(dev) for k, v in host.items()}
+    gt = d["gates"]
+    scratch = blocks.Scratch(T, I, dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def run_double(mark=None):
+        blocks.double_block(txt_w, img_w, d["txt_mod1"], d["img_mod1"], d["txt_mod2"], d["img_mod2"], d["txt"],
+                            d["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch, mark)
+
+    def run_single(mark=None):
+        blocks.single_block(sw, d["x_mod"], d["x"], gt[4], pe, mask, scratch, mark)
+
+    run_double()
+    run_single()  # sizes the engine's workspaces before capture
+    torch.cuda.synchronize(dev)
+    cap = torch.cuda.Stream(dev)
+    n0 = b2g.launch_count()
+    graphs, marks = [], []
+    for fn in (run_double, run_single):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            mk = _Marks(torch, cap)
+            with torch.cuda.graph(g, stream=cap):
+                mk.begin()
+                fn(mk)
+        graphs.append(g)
+        marks.append(mk)
+    launches_per_step = b2g.launch_count() - n0
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        for g in graphs:
+            g.replay()
+    barrier()
+    per_step, per_op = [], {}
+    with ClockSampler(local) as clk:
+        barrier()
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for g in graphs:
+                g.replay()
+            b.record(stream)
+            b.synchronize()
+            per_step.append(a.elapsed_time(b))
+            for mk in marks:
+                for lab, ms in mk.durations().items():
+                    per_op.setdefault(lab, []).append(ms)
+        barrier()
+    total_ms = sum(per_step)
+    b2g.check_device_error()
+
+    # End to end with host buffers: inputs in on one side stream, outputs back on another.
+    cin, cout = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    outs = {k: torch.empty_like(host[k]).pin_memory() for k in ("txt", "img", "x")}
+    dbl_in = ("txt_mod1", "img_mod1", "txt_mod2", "img_mod2", "txt", "img", "gates")
+    sgl_in = ("x_mod", "x")
+    h2d = sum(host[k].numel() * host[k].element_size() for k in dbl_in + sgl_in)
+    d2h = sum(v.numel() * v.element_size() for v in outs.values())
+
+    def e2e_step():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_din, e_sin, e_dd, e_dout = (torch.cuda.Event() for _ in range(4))
+        a.record(stream)
+        cin.wait_event(a)
+        with torch.cuda.stream(cin):
+            for k in dbl_in:
+                d[k].copy_(host[k], non_blocking=True)
+            e_din.record(cin)
+            for k in sgl_in:
+                d[k].copy_(host[k], non_blocking=True)
+            e_sin.record(cin)
+        stream.wait_event(e_din)
+        graphs[0].replay()
+        e_dd.record(stream)
+        cout.wait_event(e_dd)
+        with torch.cuda.stream(cout):
+            outs["txt"].copy_(d["txt"], non_blocking=True)
+            outs["img"].copy_(d["img"], non_blocking=True)
+            e_dout.record(cout)
+        stream.wait_event(e_sin)
+        graphs[1].replay()
+        outs["x"].copy_(d["x"], non_blocking=True)
+        stream.wait_event(e_dout)
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 50))
+    e2e_ms = 0.0
+    for i in range(e2e_steps):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize(dev)
+        e2e_ms += e2e_step()
+    e2e_per = e2e_ms / e2e_steps
+
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([total_ms, e2e_per], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_per = float(t[0]), float(t[1])
+    ops = blocks.block_pair_ops(T, I)
+    flop_step = sum(f for _, _, f in ops)
+    per = total_ms / args.steps
+    value = flop_step * args.steps * world / (total_ms * 1e-3) / 1e12
+    mean_op = {lab: statistics.mean(v) for lab, v in per_op.items()}
+    gemm_flop = sum(f for lab, kind, f in ops if kind == "gemm")
+    gemm_ms = sum(mean_op[lab] for lab, kind, _ in ops if kind == "gemm")
+    peaks = measured_peaks()
+    achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox/CPU generators, seeds 0/1)",
+        "config": {"workload": WORKLOAD2, "flop_per_step": flop_step, "parallelism": f"replicas x{world}",
+                   "l2": "weights 680 MB > L2; 256 MB buffer written before every step, outside the events",
+                   "execution": "two CUDA graphs (double block, single block) per step"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "traffic": profile_traffic(), "peak_source": peaks["source"] + " (burst bf16)",
+                     "kernel": "tc_gemm (13 launches per step; FLOP-weighted over the launches)",
+                     "gemm_ms_per_step": round(gemm_ms, 5)},
+        "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
+        "breakdown_tflops": {lab: round(f / (mean_op[lab] * 1e-3) / 1e12, 1) for lab, _, f in ops},
+        "e2e": {"value": round(flop_step * world / (e2e_per * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_per, 4)},
+        "clocks": clk.summary(),
+        "gpu_launches": int(launches_per_step * args.steps),
+        "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle as oracle_mod
+
+        o, x_h, w_h, bias_h = make_inputs(oracle_mod)
+        line["cpu_baseline"] = cpu_baseline(o, x_h, w_h, bias_h)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graphs
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100 for config2, 200 config1)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
+    ap.add_argument("--workload", choices=["config2", "config1"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_engine(args)
+    if args.steps is None:
+        args.steps = 100 if args.workload == "config2" else 200
+    fn = {("b2g", "config1"): run_engine_config1, ("reference", "config1"): run_reference_config1,
+          ("b2g", "config2"): run_engine_config2, ("reference", "config2"): run_reference_config2}
+    fn[(args.impl, args.workload)](args)
 
 
 if __name__ == "__main__":

@@ -75,6 +75,10 @@ _SIGNATURES = {
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
     "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "b2g_attention_qknorm_rope": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_void_p] * 4 +
+                                  [ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                   ctypes.c_void_p], ctypes.c_int),
     "b2g_attention_with_rope": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p,
                                  ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
@@ -243,6 +247,32 @@ def attention_with_rope(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, pe: t
     s = torch.cuda.current_stream(Q.device).cuda_stream
     _check(lib.b2g_attention_with_rope(Q.data_ptr(), K.data_ptr(), V.data_ptr(), pe.data_ptr(), n_head, d_head, L,
                                        _ptr(attn_mask), out.data_ptr(), ctypes.c_void_p(s)))
+    return out
+
+
+def attention_qknorm_rope(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pe: torch.Tensor, n_head: int,
+                          d_head: int, q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None,
+                          attn_mask: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                          out_dtype: torch.dtype = torch.float32, eps: float = 1e-6,
+                          q_norm2: torch.Tensor | None = None, k_norm2: torch.Tensor | None = None,
+                          norm_split: int = -1) -> torch.Tensor:
+    """Fused block-path attention: q/k/v are [L, n_head*d_head] F32 views (unit column
+    stride, any row stride); optional per-head RMSNorm scales (q_norm2/k_norm2 for rows
+    >= norm_split); output F32 or bf16 view."""
+    lib = load()
+    _require_cuda(q, k, v, pe, q_norm, k_norm, q_norm2, k_norm2, attn_mask, out)
+    L = q.shape[0]
+    for t in (q, k, v):
+        if t.dtype != torch.float32 or t.stride(1) != 1:
+            raise B2GError("attention_qknorm_rope: F32 views with unit column stride expected")
+    if out is None:
+        out = torch.empty((L, n_head * d_head), dtype=out_dtype, device=q.device)
+    s = torch.cuda.current_stream(q.device).cuda_stream
+    _check(lib.b2g_attention_qknorm_rope(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
+                                         v.stride(0), _ptr(q_norm), _ptr(k_norm), _ptr(q_norm2), _ptr(k_norm2),
+                                         norm_split, eps, pe.data_ptr(),
+                                         _ptr(attn_mask), out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0),
+                                         L, n_head, d_head, ctypes.c_void_p(s)))
     return out
 
 

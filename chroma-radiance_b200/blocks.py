@@ -1,0 +1,171 @@
+"""The GEMM + attention path of one Chroma double-stream and one single-stream block on the
+engine, with the fusions the engine offers.
+
+Mirrors the BF16 branch of the reference's block code, from the modulated bf16 inputs to the
+updated residual streams; LayerNorm/modulation and the modulation vector are inputs here:
+
+  double_block_forward (chroma.cuh:808-964), per stream s in {txt, img}:
+      qkv_s = x_mod1_s . Wqkv_s^T + b            reference: 3 linear() calls, F32 out
+      qk_norm + RoPE + attention over [txt; img]  reference: rms_norm x2, cuDNN SDPA, F32 out
+      x_s  += gate1_s * (attn_s . Wproj_s^T + b)  reference: linear_gated_residual
+      h_s   = gelu(x_mod2_s . Wmlp0_s^T + b)      reference: linear() F32 + gelu_to_bf16
+      x_s  += gate2_s * (h_s . Wmlp2_s^T + b)     reference: linear() F32 + gated_residual
+  single_block_forward (chroma.cuh:1101-1157):
+      qkv   = x_mod . W1[0:9216]^T + b            reference: 3 linear() calls, F32 out
+      mlp   = gelu(x_mod . W1[9216:]^T + b)       reference: linear() F32 + gelu_cuda
+      attn  = attention(qk_norm(qkv))             reference: rms_norm x2 + cuDNN SDPA
+      x    += gate * ([attn, mlp] . W2^T + b)     reference: concat_last_dim_to_bf16,
+                                                  linear() F32, gated_residual
+Engine fusions: the GELU and the gated residual are GEMM epilogues; qk_norm is fused into the
+attention's RoPE producer; the attention writes bf16 straight into the proj input / the
+concat buffer, and the MLP half of linear1 writes GELU'd bf16 into the other concat columns.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+import b2g
+
+HIDDEN, HEADS, DHEAD, MLP = 3072, 24, 128, 12288
+
+
+@dataclass
+class StreamWeights:
+    qkv_w: torch.Tensor   # bf16 [9216, 3072]
+    qkv_b: torch.Tensor   # f32 [9216]
+    q_norm: torch.Tensor  # f32 [128]
+    k_norm: torch.Tensor
+    proj_w: torch.Tensor  # bf16 [3072, 3072]
+    proj_b: torch.Tensor
+    mlp0_w: torch.Tensor  # bf16 [12288, 3072]
+    mlp0_b: torch.Tensor
+    mlp2_w: torch.Tensor  # bf16 [3072, 12288]
+    mlp2_b: torch.Tensor
+
+
+@dataclass
+class SingleWeights:
+    linear1_w: torch.Tensor  # bf16 [21504, 3072]
+    linear1_b: torch.Tensor  # f32 [21504]
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    linear2_w: torch.Tensor  # bf16 [3072, 15360]
+    linear2_b: torch.Tensor  # f32 [3072]
+
+
+def _randn(gen: torch.Generator, shape, scale=1.0, shift=0.0):
+    """N(shift, scale^2) drawn on the generator's own device."""
+    return torch.randn(shape, generator=gen, device=gen.device) * scale + shift
+
+
+def random_stream(gen: torch.Generator, dev) -> StreamWeights:
+    def w(n, k):
+        return _randn(gen, (n, k), 0.02).to(torch.bfloat16).to(dev)
+
+    def b(n):
+        return _randn(gen, n, 0.02).to(dev)
+
+    def nrm():
+        return _randn(gen, DHEAD, 0.1, 1.0).to(dev)
+
+    return StreamWeights(w(3 * HIDDEN, HIDDEN), b(3 * HIDDEN), nrm(), nrm(), w(HIDDEN, HIDDEN), b(HIDDEN),
+                         w(MLP, HIDDEN), b(MLP), w(HIDDEN, MLP), b(HIDDEN))
+
+
+def random_single(gen: torch.Generator, dev) -> SingleWeights:
+    return SingleWeights(_randn(gen, (3 * HIDDEN + MLP, HIDDEN), 0.02).to(torch.bfloat16).to(dev),
+                         _randn(gen, 3 * HIDDEN + MLP, 0.02).to(dev),
+                         _randn(gen, DHEAD, 0.1, 1.0).to(dev),
+                         _randn(gen, DHEAD, 0.1, 1.0).to(dev),
+                         _randn(gen, (HIDDEN, HIDDEN + MLP), 0.02).to(torch.bfloat16).to(dev),
+                         _randn(gen, HIDDEN, 0.02).to(dev))
+
+
+class Scratch:
+    """Activation buffers of one block pair, allocated once (no allocation inside a step)."""
+
+    def __init__(self, T: int, I: int, dev):
+        L = T + I
+        self.qkv = torch.empty((L, 3 * HIDDEN), dtype=torch.float32, device=dev)
+        self.attn = torch.empty((L, HIDDEN), dtype=torch.bfloat16, device=dev)
+        self.h_img = torch.empty((I, MLP), dtype=torch.bfloat16, device=dev)
+        self.h_txt = torch.empty((T, MLP), dtype=torch.bfloat16, device=dev)
+        self.cat = torch.empty((L, HIDDEN + MLP), dtype=torch.bfloat16, device=dev)
+
+
+def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1, txt_mod2, img_mod2, txt, img,
+                 txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask, s: Scratch, mark=None) -> None:
+    """Updates txt [T, 3072] and img [I, 3072] (F32 residual streams) in place.
+
+    `mark(label)`, when given, is called after each operation (labels and FLOPs in
+    block_pair_ops order) so a caller can record events between the launches."""
+    mark = mark or _no_mark
+    T = txt.shape[0]
+    b2g.gemm(txt_mod1, txt_w.qkv_w, txt_w.qkv_b, out=s.qkv[:T])
+    mark("double.txt_qkv")
+    b2g.gemm(img_mod1, img_w.qkv_w, img_w.qkv_b, out=s.qkv[T:])
+    mark("double.img_qkv")
+    q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
+    b2g.attention_qknorm_rope(q, k, v, pe, HEADS, DHEAD, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm,
+                              q_norm2=img_w.q_norm, k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    mark("double.attention")
+    b2g.gemm(s.attn[:T], txt_w.proj_w, txt_w.proj_b, out=txt, epilogue="gated_residual", gate=txt_gate1)
+    mark("double.txt_proj")
+    b2g.gemm(s.attn[T:], img_w.proj_w, img_w.proj_b, out=img, epilogue="gated_residual", gate=img_gate1)
+    mark("double.img_proj")
+    b2g.gemm(img_mod2, img_w.mlp0_w, img_w.mlp0_b, out=s.h_img, epilogue="gelu")
+    mark("double.img_mlp0")
+    b2g.gemm(s.h_img, img_w.mlp2_w, img_w.mlp2_b, out=img, epilogue="gated_residual", gate=img_gate2)
+    mark("double.img_mlp2")
+    b2g.gemm(txt_mod2, txt_w.mlp0_w, txt_w.mlp0_b, out=s.h_txt, epilogue="gelu")
+    mark("double.txt_mlp0")
+    b2g.gemm(s.h_txt, txt_w.mlp2_w, txt_w.mlp2_b, out=txt, epilogue="gated_residual", gate=txt_gate2)
+    mark("double.txt_mlp2")
+
+
+def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=None) -> None:
+    """Updates x [L, 3072] (F32 residual stream) in place.  `mark` as in double_block."""
+    mark = mark or _no_mark
+    n_qkv = 3 * HIDDEN
+    b2g.gemm(x_mod, w.linear1_w[:n_qkv], w.linear1_b[:n_qkv], out=s.qkv)
+    mark("single.linear1_qkv")
+    b2g.gemm(x_mod, w.linear1_w[n_qkv:], w.linear1_b[n_qkv:], out=s.cat[:, HIDDEN:], epilogue="gelu")
+    mark("single.linear1_mlp")
+    q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
+    b2g.attention_qknorm_rope(q, k, v, pe, HEADS, DHEAD, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask,
+                              out=s.cat[:, :HIDDEN])
+    mark("single.attention")
+    b2g.gemm(s.cat, w.linear2_w, w.linear2_b, out=x, epilogue="gated_residual", gate=gate)
+    mark("single.linear2")
+
+
+def _no_mark(label: str) -> None:
+    pass
+
+
+def block_pair_ops(T: int, I: int) -> list[tuple[str, str, float]]:
+    """(label, kind, FLOPs) of every operation of one double + one single block, in launch order.
+
+    kind "gemm" is one engine GEMM launch (2*M*N*K); kind "attention" is the whole attention
+    (QK^T + PV over 24 heads, 4*L*L*3072, counted unmasked)."""
+    L = T + I
+    H3, H = 3 * HIDDEN, HIDDEN
+    att = 4.0 * L * L * HIDDEN
+    return [("double.txt_qkv", "gemm", 2.0 * T * H3 * H), ("double.img_qkv", "gemm", 2.0 * I * H3 * H),
+            ("double.attention", "attention", att),
+            ("double.txt_proj", "gemm", 2.0 * T * H * H), ("double.img_proj", "gemm", 2.0 * I * H * H),
+            ("double.img_mlp0", "gemm", 2.0 * I * MLP * H), ("double.img_mlp2", "gemm", 2.0 * I * H * MLP),
+            ("double.txt_mlp0", "gemm", 2.0 * T * MLP * H), ("double.txt_mlp2", "gemm", 2.0 * T * H * MLP),
+            ("single.linear1_qkv", "gemm", 2.0 * L * H3 * H), ("single.linear1_mlp", "gemm", 2.0 * L * MLP * H),
+            ("single.attention", "attention", att), ("single.linear2", "gemm", 2.0 * L * H * (H + MLP))]
+
+
+def block_pair_flops(T: int, I: int) -> tuple[float, float]:
+    """(linear FLOPs, attention FLOPs counted unmasked) of one double + one single block."""
+    L = T + I
+    per_tok = HIDDEN * (3 * HIDDEN + HIDDEN + MLP + MLP)  # = 113,246,208 (both block types)
+    linears = 2.0 * L * per_tok * 2
+    attention = 2 * (4.0 * L * L * HIDDEN)
+    return linears, attention

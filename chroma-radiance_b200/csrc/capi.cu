@@ -280,6 +280,30 @@ b2g_status b2g_attention_with_rope(const float* Q, const float* K, const float* 
   return attention_rope(Q, K, V, pe, attn_mask, out, L, n_head, d_head, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                     int64_t ldv, const float* q_norm, const float* k_norm, const float* q_norm2,
+                                     const float* k_norm2, int64_t norm_split, float eps, const float* pe,
+                                     const float* attn_mask, void* out, b2g_dtype out_dtype, int64_t ldo, int64_t L,
+                                     int n_head, int d_head, void* stream) {
+  if (n_head < 0 || d_head < 0 || L < 0) return set_error(B2G_ERR_INVALID, "b2g_attention_qknorm_rope: negative size");
+  if (L == 0 || n_head == 0) return B2G_OK;
+  if (!q || !k || !v || !pe || !out) return set_error(B2G_ERR_INVALID, "b2g_attention_qknorm_rope: null operand");
+  const int64_t hd = static_cast<int64_t>(n_head) * d_head;
+  if (ldq < hd || ldk < hd || ldv < hd || ldo < hd)
+    return set_error(B2G_ERR_INVALID, "b2g_attention_qknorm_rope: row stride below n_head*d_head");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  AttnArgs a;
+  a.q = q; a.ldq = ldq; a.k = k; a.ldk = ldk; a.v = v; a.ldv = ldv;
+  a.q_norm = q_norm; a.k_norm = k_norm; a.eps = eps;
+  a.q_norm2 = q_norm2; a.k_norm2 = k_norm2; a.norm_split = norm_split;
+  a.pe = pe; a.key_bias = attn_mask;
+  a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
+  a.L = L; a.H = n_head; a.D = d_head;
+  return attention_rope_ex(a, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_check_device_error(int* code) {
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);

@@ -51,8 +51,25 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits);
 
-// Attention with RoPE (attention.cu): q, k, v F32 [L, H*D], pe [L, D/2, 4], key_bias [L]
-// (0 / -inf) or null; out F32 [L, H*D].
+// Attention with RoPE (attention.cu).  q, k, v F32 rows of H*D (row strides ldq/ldk/ldv);
+// q_norm/k_norm: optional per-head RMSNorm scales [D] (eps) fused into the Q/K producer;
+// pe [L, D/2, 4]; key_bias [L] (0 / -inf) or null; out [L, H*D] F32 or BF16 (row stride ldo).
+struct AttnArgs {
+  const float *q = nullptr, *k = nullptr, *v = nullptr;
+  int64_t ldq = 0, ldk = 0, ldv = 0;
+  const float *q_norm = nullptr, *k_norm = nullptr;    // rows [0, norm_split)
+  const float *q_norm2 = nullptr, *k_norm2 = nullptr;  // rows [norm_split, L) (null: same)
+  int64_t norm_split = -1;                             // -1: one set of scales for all rows
+  float eps = 1e-6f;
+  const float* pe = nullptr;
+  const float* key_bias = nullptr;
+  void* out = nullptr;
+  b2g_dtype out_dtype = B2G_F32;
+  int64_t ldo = 0;
+  int64_t L = 0, H = 0, D = 0;
+};
+b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st);
+// Contiguous F32 [L, H*D] form of the above (no norm), the reference's attention_with_rope.
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,
                           float* out, int64_t L, int64_t H, int64_t D, cudaStream_t st);
 

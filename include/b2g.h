@@ -129,6 +129,18 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
 b2g_status b2g_attention_with_rope(const float* Q, const float* K, const float* V, const float* pe, int n_head,
                                    int d_head, int64_t L, const float* attn_mask, float* out, void* stream);
 
+/* The fused form the engine's block path uses: Q, K, V are column ranges of one F32 qkv
+ * buffer (row strides ldq/ldk/ldv, e.g. 3*n_head*d_head); q_norm/k_norm (F32 [d_head], may be
+ * NULL) apply the per-head RMSNorm of qk_norm (chroma.cuh:513-515, rms_norm eps) inside the
+ * RoPE producer, with q_norm2/k_norm2 for rows >= norm_split (the double block's img rows;
+ * pass -1 for one set); the output is written as F32 or BF16 with row stride ldo, e.g.
+ * straight into the bf16 [L, 3072 + 12288] concat buffer that feeds linear2.  New entry point. */
+b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k, int64_t ldk, const float* v,
+                                     int64_t ldv, const float* q_norm, const float* k_norm, const float* q_norm2,
+                                     const float* k_norm2, int64_t norm_split, float eps, const float* pe,
+                                     const float* attn_mask, void* out, b2g_dtype out_dtype, int64_t ldo, int64_t L,
+                                     int n_head, int d_head, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

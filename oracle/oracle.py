@@ -221,8 +221,27 @@ class AttnRef:
         lib.ref_bench_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, _c_p, ctypes.c_int,
                                                          ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
         lib.ref_bench_attention.restype = ctypes.c_int
+        pp = ctypes.POINTER(ctypes.c_void_p)
+        lib.ref_double_block.argtypes = [pp, _i64, _i64]
+        lib.ref_single_block.argtypes = [pp, _i64]
+        lib.ref_alloc_blocks.argtypes = [ctypes.c_ulonglong, _i64, _i64, _i64, pp, pp]
+        lib.ref_bench_blocks.argtypes = [pp, pp, _i64, _i64, ctypes.c_int, ctypes.c_int, _i64,
+                                         ctypes.POINTER(ctypes.c_double)]
+        for f in ("ref_double_block", "ref_single_block", "ref_alloc_blocks", "ref_bench_blocks"):
+            getattr(lib, f).restype = ctypes.c_int
         lib.ref_attn_init()
         self.lib = lib
+
+    @staticmethod
+    def ptr_array(ptrs):
+        """ctypes void* array from device addresses (ints or None)."""
+        return (ctypes.c_void_p * len(ptrs))(*ptrs)
+
+    def double_block(self, ptrs, T, I):
+        return self.lib.ref_double_block(self.ptr_array(ptrs), T, I)
+
+    def single_block(self, ptrs, L):
+        return self.lib.ref_single_block(self.ptr_array(ptrs), L)
 
     def attention_with_rope(self, Q, K, V, pe, n_head, d_head, L, mask, out):
         return self.lib.ref_attention_with_rope(Q, K, V, pe, n_head, d_head, L, mask, out)

@@ -3,10 +3,27 @@
 // behind extern "C" functions: cuDNN-frontend flash SDPA with RoPE, exactly as the Chroma
 // blocks call it (chroma.cuh:721, 1092).
 #include <functional>
+#include <vector>
 #include "tensor.cuh"
 #include "cublas_ops.cuh"
 #include "kernels.cu"
 #include "attention.cuh"
+
+// kernels.cu host wrappers the block code uses (declared by the reference in chroma.cuh).
+void gelu_cuda(const float* x, float* out, int64_t n);
+void gelu_to_bf16_cuda(const float* x, __nv_bfloat16* out, int64_t n);
+void concat_last_dim_to_bf16_cuda(const float* a, const float* b, __nv_bfloat16* out, int64_t M, int64_t Da,
+                                  int64_t Db);
+void scale_cuda(float* x, float scale, int64_t n);
+void add_scalar_cuda(float* x, float val, int64_t n);
+
+// linear_forward (chroma.cuh:83-89): allocate the F32 output, then linear().
+static Tensor linear_forward(const Tensor& x, const Tensor& W, const Tensor* bias) {
+  int64_t M = x.numel() / x.shape[x.ndim - 1];
+  Tensor out = Tensor::alloc({M, W.shape[0]}, DType::F32, true);
+  linear(x, W, bias, out);
+  return out;
+}
 
 extern "C" {
 
@@ -57,6 +74,216 @@ int ref_bench_attention(const float* Q, const float* K, const float* V, const fl
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   return 0;
+}
+
+// ---------------------------------------------------------------------------------------
+// One double-stream and one single-stream block from the modulated bf16 inputs to the
+// updated residual streams, with exactly the reference's BF16-path calls
+// (double_block_forward chroma.cuh:808-964, single_block_forward :1101-1157, cfg_batch 1).
+//
+// Double-block pointers, in order:
+//   0 img_qkv_w 1 img_qkv_b 2 img_q_norm 3 img_k_norm 4 img_proj_w 5 img_proj_b 6 img_mlp0_w
+//   7 img_mlp0_b 8 img_mlp2_w 9 img_mlp2_b, 10-19 the same for txt, 20 img_mod1 21 txt_mod1
+//   22 img_mod2 23 txt_mod2 (bf16), 24 img 25 txt (F32 residual, updated), 26 img_gate1
+//   27 txt_gate1 28 img_gate2 29 txt_gate2, 30 pe, 31 mask (may be null)
+// Single-block pointers: 0 linear1_w 1 linear1_b 2 q_norm 3 k_norm 4 linear2_w 5 linear2_b
+//   6 x_mod (bf16) 7 x (F32, updated) 8 gate 9 pe 10 mask
+// ---------------------------------------------------------------------------------------
+static const int64_t kH = 3072, kHeads = 24, kD = 128, kMlp = 12288;
+
+static Tensor wview(void* base, int64_t row0, int64_t rows, int64_t cols) {
+  return Tensor::wrap_gpu(static_cast<__nv_bfloat16*>(base) + row0 * cols, {rows, cols}, DType::BF16);
+}
+static Tensor bview(void* base, int64_t off, int64_t n) {
+  return Tensor::wrap_gpu(static_cast<float*>(base) + off, {n}, DType::F32);
+}
+
+int ref_double_block(void** p, int64_t T, int64_t I) {
+  const int64_t L = T + I;
+  Tensor all_q = Tensor::alloc({L, kH}, DType::F32, true);
+  Tensor all_k = Tensor::alloc({L, kH}, DType::F32, true);
+  Tensor all_v = Tensor::alloc({L, kH}, DType::F32, true);
+  for (int s = 0; s < 2; ++s) {  // s = 0: img (rows T..L), s = 1: txt (rows 0..T)
+    void** w = p + 10 * s;
+    const int64_t M = s == 0 ? I : T, r0 = s == 0 ? T : 0;
+    Tensor xm = Tensor::wrap_gpu(p[20 + s], {M, kH}, DType::BF16);
+    Tensor qv = Tensor::wrap_gpu(all_q.f32() + r0 * kH, {M, kH}, DType::F32);
+    Tensor kv = Tensor::wrap_gpu(all_k.f32() + r0 * kH, {M, kH}, DType::F32);
+    Tensor vv = Tensor::wrap_gpu(all_v.f32() + r0 * kH, {M, kH}, DType::F32);
+    Tensor wq = wview(w[0], 0, kH, kH), wk = wview(w[0], kH, kH, kH), wv = wview(w[0], 2 * kH, kH, kH);
+    Tensor bq = bview(w[1], 0, kH), bk = bview(w[1], kH, kH), bv = bview(w[1], 2 * kH, kH);
+    linear(xm, wq, &bq, qv);
+    linear(xm, wk, &bk, kv);
+    linear(xm, wv, &bv, vv);
+    rms_norm_cuda(qv.f32(), static_cast<float*>(w[2]), qv.f32(), M * kHeads, kD, 1e-6f);
+    rms_norm_cuda(kv.f32(), static_cast<float*>(w[3]), kv.f32(), M * kHeads, kD, 1e-6f);
+  }
+  Tensor pe = Tensor::wrap_gpu(p[30], {L, kD / 2 * 4}, DType::F32);
+  Tensor q_r = all_q.reshape({L, kHeads, kD});
+  Tensor k_r = all_k.reshape({L, kHeads, kD});
+  Tensor v_r = all_v.reshape({L, kHeads, kD});
+  Tensor attn = attention_with_rope(q_r, k_r, v_r, pe, (int)kHeads, (int)kD, static_cast<const float*>(p[31]));
+  for (int s = 0; s < 2; ++s) {
+    void** w = p + 10 * s;
+    const int64_t M = s == 0 ? I : T, r0 = s == 0 ? T : 0;
+    float* x = static_cast<float*>(p[24 + s]);
+    Tensor a = Tensor::wrap_gpu(attn.f32() + r0 * kH, {M, kH}, DType::F32);
+    Tensor wp = wview(w[4], 0, kH, kH);
+    Tensor bp = bview(w[5], 0, kH);
+    linear_gated_residual(a, wp, &bp, x, static_cast<float*>(p[26 + s]), M, kH);
+  }
+  for (int s = 0; s < 2; ++s) {
+    void** w = p + 10 * s;
+    const int64_t M = s == 0 ? I : T;
+    float* x = static_cast<float*>(p[24 + s]);
+    Tensor xm2 = Tensor::wrap_gpu(p[22 + s], {M, kH}, DType::BF16);
+    Tensor w0 = wview(w[6], 0, kMlp, kH), w2 = wview(w[8], 0, kH, kMlp);
+    Tensor b0 = bview(w[7], 0, kMlp), b2 = bview(w[9], 0, kH);
+    Tensor h = linear_forward(xm2, w0, &b0);
+    Tensor hb = Tensor::alloc({M, kMlp}, DType::BF16, true);
+    gelu_to_bf16_cuda(h.f32(), hb.bf16(), M * kMlp);
+    Tensor o = linear_forward(hb, w2, &b2);
+    gated_residual_cuda(x, o.f32(), static_cast<float*>(p[28 + s]), x, M, kH);
+  }
+  return 0;
+}
+
+int ref_single_block(void** p, int64_t L) {
+  Tensor xm = Tensor::wrap_gpu(p[6], {L, kH}, DType::BF16);
+  Tensor q_t = Tensor::alloc({L, kH}, DType::F32, true);
+  Tensor k_t = Tensor::alloc({L, kH}, DType::F32, true);
+  Tensor v_t = Tensor::alloc({L, kH}, DType::F32, true);
+  Tensor mlp_t = Tensor::alloc({L, kMlp}, DType::F32, true);
+  Tensor sq = wview(p[0], 0, kH, kH), sk = wview(p[0], kH, kH, kH), sv = wview(p[0], 2 * kH, kH, kH);
+  Tensor sm = wview(p[0], 3 * kH, kMlp, kH);
+  Tensor bq = bview(p[1], 0, kH), bk = bview(p[1], kH, kH), bv = bview(p[1], 2 * kH, kH), bm = bview(p[1], 3 * kH, kMlp);
+  linear(xm, sq, &bq, q_t);
+  linear(xm, sk, &bk, k_t);
+  linear(xm, sv, &bv, v_t);
+  linear(xm, sm, &bm, mlp_t);
+  gelu_cuda(mlp_t.f32(), mlp_t.f32(), L * kMlp);
+  rms_norm_cuda(q_t.f32(), static_cast<float*>(p[2]), q_t.f32(), L * kHeads, kD, 1e-6f);
+  rms_norm_cuda(k_t.f32(), static_cast<float*>(p[3]), k_t.f32(), L * kHeads, kD, 1e-6f);
+  Tensor pe = Tensor::wrap_gpu(p[9], {L, kD / 2 * 4}, DType::F32);
+  Tensor q_r = q_t.reshape({L, kHeads, kD});
+  Tensor k_r = k_t.reshape({L, kHeads, kD});
+  Tensor v_r = v_t.reshape({L, kHeads, kD});
+  Tensor attn_out = attention_with_rope(q_r, k_r, v_r, pe, (int)kHeads, (int)kD, static_cast<const float*>(p[10]));
+  Tensor attn_mlp = Tensor::alloc({L, kH + kMlp}, DType::BF16, true);
+  concat_last_dim_to_bf16_cuda(attn_out.f32(), mlp_t.f32(), attn_mlp.bf16(), L, kH, kMlp);
+  Tensor w2 = wview(p[4], 0, kH, kH + kMlp);
+  Tensor b2 = bview(p[5], 0, kH);
+  Tensor out = linear_forward(attn_mlp, w2, &b2);
+  gated_residual_cuda(static_cast<float*>(p[7]), out.f32(), static_cast<float*>(p[8]), static_cast<float*>(p[7]), L,
+                      kH);
+  return 0;
+}
+
+// Allocates and fills the inputs of one block pair on the device with the reference's own
+// Philox generator (rand_normal_cuda, kernels.cu) so the reference arm of bench.py needs no
+// other library: weights ~ N(0, 0.02) bf16, biases ~ N(0, 0.02), norm scales ~ 1 + N(0, 0.1),
+// activations ~ N(0, 1), gates ~ N(0, 1), RoPE table of random rotations, key mask 0 / -inf
+// (the last `masked` text tokens).  dp: 32 pointers, sp: 11 pointers (orders above).
+static void* fill(int64_t n, DType dt, float scale, float shift, unsigned long long seed) {
+  float* f = nullptr;
+  CHECK_CUDA(cudaMalloc(&f, n * sizeof(float)));
+  rand_normal_cuda(f, n, seed);
+  scale_cuda(f, scale, n);
+  if (shift != 0.f) add_scalar_cuda(f, shift, n);
+  if (dt == DType::F32) return f;
+  void* b = nullptr;
+  CHECK_CUDA(cudaMalloc(&b, n * 2));
+  f32_to_bf16_cuda(f, static_cast<__nv_bfloat16*>(b), n);
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaFree(f);
+  return b;
+}
+
+int ref_alloc_blocks(unsigned long long seed, int64_t T, int64_t I, int64_t masked, void** dp, void** sp) {
+  const int64_t L = T + I;
+  unsigned long long s = seed;
+  for (int st = 0; st < 2; ++st) {
+    void** w = dp + 10 * st;
+    w[0] = fill(3 * kH * kH, DType::BF16, 0.02f, 0.f, ++s);
+    w[1] = fill(3 * kH, DType::F32, 0.02f, 0.f, ++s);
+    w[2] = fill(kD, DType::F32, 0.1f, 1.f, ++s);
+    w[3] = fill(kD, DType::F32, 0.1f, 1.f, ++s);
+    w[4] = fill(kH * kH, DType::BF16, 0.02f, 0.f, ++s);
+    w[5] = fill(kH, DType::F32, 0.02f, 0.f, ++s);
+    w[6] = fill(kMlp * kH, DType::BF16, 0.02f, 0.f, ++s);
+    w[7] = fill(kMlp, DType::F32, 0.02f, 0.f, ++s);
+    w[8] = fill(kH * kMlp, DType::BF16, 0.02f, 0.f, ++s);
+    w[9] = fill(kH, DType::F32, 0.02f, 0.f, ++s);
+  }
+  dp[20] = fill(I * kH, DType::BF16, 1.f, 0.f, ++s);
+  dp[21] = fill(T * kH, DType::BF16, 1.f, 0.f, ++s);
+  dp[22] = fill(I * kH, DType::BF16, 1.f, 0.f, ++s);
+  dp[23] = fill(T * kH, DType::BF16, 1.f, 0.f, ++s);
+  dp[24] = fill(I * kH, DType::F32, 1.f, 0.f, ++s);
+  dp[25] = fill(T * kH, DType::F32, 1.f, 0.f, ++s);
+  for (int g = 0; g < 4; ++g) dp[26 + g] = fill(kH, DType::F32, 1.f, 0.f, ++s);
+  // RoPE table: rotation angles a, rows (cos a, -sin a, sin a, cos a)
+  std::vector<float> pe(static_cast<size_t>(L) * kD / 2 * 4);
+  for (int64_t i = 0; i < L * kD / 2; ++i) {
+    const float a = 0.001f * static_cast<float>((i * 2654435761ull) % 6283);
+    pe[4 * i] = cosf(a);
+    pe[4 * i + 1] = -sinf(a);
+    pe[4 * i + 2] = sinf(a);
+    pe[4 * i + 3] = cosf(a);
+  }
+  CHECK_CUDA(cudaMalloc(&dp[30], pe.size() * 4));
+  CHECK_CUDA(cudaMemcpy(dp[30], pe.data(), pe.size() * 4, cudaMemcpyHostToDevice));
+  std::vector<float> mask(L, 0.f);
+  for (int64_t i = T - masked; i < T; ++i) mask[i] = -INFINITY;
+  CHECK_CUDA(cudaMalloc(&dp[31], L * 4));
+  CHECK_CUDA(cudaMemcpy(dp[31], mask.data(), L * 4, cudaMemcpyHostToDevice));
+  sp[0] = fill((3 * kH + kMlp) * kH, DType::BF16, 0.02f, 0.f, ++s);
+  sp[1] = fill(3 * kH + kMlp, DType::F32, 0.02f, 0.f, ++s);
+  sp[2] = fill(kD, DType::F32, 0.1f, 1.f, ++s);
+  sp[3] = fill(kD, DType::F32, 0.1f, 1.f, ++s);
+  sp[4] = fill(kH * (kH + kMlp), DType::BF16, 0.02f, 0.f, ++s);
+  sp[5] = fill(kH, DType::F32, 0.02f, 0.f, ++s);
+  sp[6] = fill(L * kH, DType::BF16, 1.f, 0.f, ++s);
+  sp[7] = fill(L * kH, DType::F32, 1.f, 0.f, ++s);
+  sp[8] = fill(kH, DType::F32, 1.f, 0.f, ++s);
+  sp[9] = dp[30];
+  sp[10] = dp[31];
+  CHECK_CUDA(cudaDeviceSynchronize());
+  return 0;
+}
+
+// Times `iters` block-pair steps (double then single) with CUDA events on stream 0, after
+// `warmup` untimed steps; *ms_total = summed per-step device time.  Before every timed step a
+// `flush_bytes` buffer is written (outside the event pair) so no step starts with a warm L2.
+int ref_bench_blocks(void** dp, void** sp, int64_t T, int64_t I, int iters, int warmup, int64_t flush_bytes,
+                     double* ms_total) {
+  for (int i = 0; i < warmup; ++i) {
+    ref_double_block(dp, T, I);
+    ref_single_block(sp, T + I);
+  }
+  void* flush = nullptr;
+  if (flush_bytes > 0) CHECK_CUDA(cudaMalloc(&flush, flush_bytes));
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  double total = 0;
+  for (int i = 0; i < iters; ++i) {
+    if (flush) cudaMemsetAsync(flush, i & 0xFF, flush_bytes, 0);
+    cudaEventRecord(e0, 0);
+    ref_double_block(dp, T, I);
+    ref_single_block(sp, T + I);
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    total += ms;
+  }
+  *ms_total = total;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (flush) cudaFree(flush);
+  return static_cast<int>(cudaGetLastError());
 }
 
 }  // extern "C"

@@ -378,6 +378,46 @@ def test_attention_vs_oracle(engine, oracle, L, H, D, masked):
     assert rel_err(got, want) < 1e-2
 
 
+@pytest.mark.parametrize("L,H,D,split,out_bf16", [(96, 2, 64, 40, False), (200, 3, 128, -1, True),
+                                                   (136, 2, 128, 64, True)])
+def test_attention_qknorm_rope_vs_oracle(engine, oracle, L, H, D, split, out_bf16):
+    """Fused qk RMSNorm (two scale sets split at row `split`, as the double block's txt/img
+    streams) + RoPE + attention, reading q/k/v as column views of one [L, 3*H*D] F32 buffer and
+    writing into a column view of a wider output, against oracle rms_norm + attention_rope."""
+    g = torch.Generator().manual_seed(L * 7 + H)
+    HD = H * D
+    qkv = torch.randn((L, 3 * HD), generator=g)
+    norms = [1.0 + 0.1 * torch.randn(D, generator=g) for _ in range(4)]
+    pe = rope_table(L, D, L + 1)
+    mask = np.zeros(L, np.float32)
+    mask[L // 4:L // 4 + 9] = -np.inf
+    dq = qkv.to(DEV)
+    out_w = torch.zeros((L, HD + 40), dtype=torch.bfloat16 if out_bf16 else torch.float32, device=DEV)
+    engine.attention_qknorm_rope(dq[:, :HD], dq[:, HD:2 * HD], dq[:, 2 * HD:], torch.from_numpy(pe).to(DEV), H, D,
+                                 q_norm=norms[0].to(DEV), k_norm=norms[1].to(DEV), q_norm2=norms[2].to(DEV),
+                                 k_norm2=norms[3].to(DEV), norm_split=split, attn_mask=torch.from_numpy(mask).to(DEV),
+                                 out=out_w[:, 8:8 + HD], out_dtype=out_w.dtype)
+    torch.cuda.synchronize()
+
+    def normed(x, s1, s2):
+        rows = x.reshape(L * H, D).numpy()
+        a = oracle.rms_norm(rows, s1.numpy()).reshape(L, H, D)
+        if split >= 0:
+            b = oracle.rms_norm(rows, s2.numpy()).reshape(L, H, D)
+            a[split:] = b[split:]
+        return a
+
+    q = normed(qkv[:, :HD], norms[0], norms[2])
+    k = normed(qkv[:, HD:2 * HD], norms[1], norms[3])
+    v = qkv[:, 2 * HD:].reshape(L, H, D).numpy()
+    want = oracle.attention_rope(q, k, v, pe, mask)
+    got_w = out_w.float().cpu().numpy()
+    assert np.all(got_w[:, :8] == 0) and np.all(got_w[:, 8 + HD:] == 0)   # nothing written outside the view
+    got = got_w[:, 8:8 + HD]
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) < 1e-2
+
+
 def attn_ref_or_skip():
     from oracle import ATTN_REF_PATH, AttnRef
 
