@@ -19,6 +19,7 @@ struct GemmProblem {
   const float* gate = nullptr;
   bool allow_tf32 = false;  // F32 x F32 may run as TF32 products (batched_matmul_Bt only)
   float alpha = 1.0f;       // D = epilogue(alpha * A.B^T + bias); internal (attention scores)
+  bool allow_split = true;  // false: never split K (split-K needs workspace; b2g_gemm_noalloc)
 };
 
 // Records a message for b2g_last_error() and returns `st`.

@@ -920,7 +920,7 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
     if (g_force_splits <= 0) splits = 1;
   }
   if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
-  if (nkb == 0) splits = 1;
+  if (nkb == 0 || !p.allow_split) splits = 1;
   const bool pair = v == VPAIR;
   const int bn = v == V128 ? 128 : 256;
   const int tile_m = pair ? 256 : kBM;

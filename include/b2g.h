@@ -141,6 +141,17 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
                                      const float* attn_mask, void* out, b2g_dtype out_dtype, int64_t ldo, int64_t L,
                                      int n_head, int d_head, void* stream);
 
+/* b2g_gemm that allocates nothing (no reference counterpart).  For callers that cannot let a
+ * library allocate device memory: engines that hand all of HBM to their own arena up front
+ * (the reference's tensor.cuh pool does), and loops that cannot take the device-wide sync that
+ * b2g_gemm's workspace growth (cudaMalloc, cudaFree) brings.  F32 activations with 16-bit
+ * weights are cast into an 8 MiB array compiled into the library, so M*round_up(K,8)*2 must be
+ * <= 8388608 bytes (else B2G_ERR_INVALID, nothing launched); K is never split.  Otherwise the
+ * same arguments, rules and results as b2g_gemm.  The array is shared per device: calls whose
+ * kernels can overlap race on it.  The first call on a device must come before any stream
+ * capture on it (it looks up the array's device address). */
+b2g_status b2g_gemm_noalloc(const b2g_gemm_desc* desc, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the
