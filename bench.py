@@ -13,7 +13,7 @@ RoPE, QK^T and PV over 24 heads, 0/-inf key mask on 400 of the 512 text tokens).
             step) * steps * ranks / (max over ranks of the summed per-step CUDA-event time).
             The engine replays the step as two CUDA graphs; weights (680 MB) are larger than
             L2, and a 256 MB buffer is also written before every step, outside the events.
-  roofline  dominant kernel = the engine's tcgen05 GEMM (13 launches per step): GEMM FLOPs /
+  roofline  dominant kernel = the engine's tcgen05 GEMM (the linear layers): GEMM FLOPs /
             summed GEMM launch time, from events recorded between the launches inside the
             graphs during the timed steps; peak = MEASURED_PEAKS.json bf16_tflops.
   e2e       the same step through the public API with host buffers: the step's activations
@@ -73,9 +73,9 @@ def measured_peaks() -> dict:
     return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
-def profile_traffic() -> float | None:
+def profile_traffic(name: str) -> float | None:
     """DRAM bytes per launch of the GEMM kernel from the committed ncu summary, if any."""
-    p = REPO / "profiles" / "tc_gemm_config1.md"
+    p = REPO / "profiles" / name
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -282,8 +282,9 @@ def run_engine_config1(args) -> None:
                    "l2": "flushed before every step (256 MB write, outside the event pair)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "traffic": profile_traffic(), "peak_source": peaks["source"] + " (burst bf16)",
-                     "kernel": "tc_gemm_kernel<256,4,none,bf16>"},
+                     "traffic": profile_traffic("tc_gemm_pair_config1.md"),
+                     "peak_source": peaks["source"] + " (burst bf16)",
+                     "kernel": "tc_gemm_pair_kernel<6,none,bf16> (2-CTA 256x256 tiles)"},
         "e2e": {"value": round(FLOP * world / (e2e_per * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
         "clocks": clk.summary(),
@@ -535,8 +536,9 @@ def run_engine_config2(args) -> None:
                    "execution": "two CUDA graphs (double block, single block) per step"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "traffic": profile_traffic(), "peak_source": peaks["source"] + " (burst bf16)",
-                     "kernel": "tc_gemm (13 launches per step; FLOP-weighted over the launches)",
+                     "traffic": profile_traffic("block_pair_config2_launches.md"),
+                     "peak_source": peaks["source"] + " (burst bf16)",
+                     "kernel": "tc_gemm: the block pair's linear-layer launches, FLOP-weighted",
                      "gemm_ms_per_step": round(gemm_ms, 5)},
         "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
         "breakdown_tflops": {lab: round(f / (mean_op[lab] * 1e-3) / 1e12, 1) for lab, _, f in ops},
