@@ -63,6 +63,7 @@ _SIGNATURES = {
     "b2g_last_error": ([], ctypes.c_char_p),
     "b2g_version": ([], ctypes.c_char_p),
     "b2g_gemm": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p], ctypes.c_int),
+    "b2g_gemm_group": ([ctypes.POINTER(GemmDesc), ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt_stream": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -139,16 +140,8 @@ def _require_cuda(*ts: torch.Tensor | None) -> None:
             raise B2GError("all tensors must be CUDA tensors")
 
 
-def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
-         out_dtype: torch.dtype | None = None, epilogue: str = "none", gate: torch.Tensor | None = None,
-         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
-    """out[M, N] = epilogue(x[M, K] . w[N, K]^T + bias) on the tensor-core path.
-
-    x, w: 2-D, unit stride along K (row strides may exceed K).  epilogue: "none", "gelu"
-    (tanh GELU) or "gated_residual" (out is an F32 residual updated in place:
-    out += gate * (x.w^T + bias)).  Runs on `stream` (default: torch's current stream).
-    """
-    lib = load()
+def _gemm_desc(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor | None,
+               out_dtype: torch.dtype | None, epilogue: str, gate: torch.Tensor | None) -> tuple[GemmDesc, torch.Tensor]:
     _require_cuda(x, w, bias, out, gate)
     if x.dim() != 2 or w.dim() != 2 or x.stride(1) != 1 or w.stride(1) != 1:
         raise B2GError("gemm: x and w must be 2-D with unit stride along K")
@@ -172,9 +165,40 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     d.d, d.d_dtype, d.ldd = out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0) if M > 1 else N
     d.epilogue = epi
     d.gate = _ptr(gate)
+    return d, out
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+         out_dtype: torch.dtype | None = None, epilogue: str = "none", gate: torch.Tensor | None = None,
+         stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out[M, N] = epilogue(x[M, K] . w[N, K]^T + bias) on the tensor-core path.
+
+    x, w: 2-D, unit stride along K (row strides may exceed K).  epilogue: "none", "gelu"
+    (tanh GELU) or "gated_residual" (out is an F32 residual updated in place:
+    out += gate * (x.w^T + bias)).  Runs on `stream` (default: torch's current stream).
+    """
+    lib = load()
+    d, out = _gemm_desc(x, w, bias, out, out_dtype, epilogue, gate)
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_gemm(ctypes.byref(d), ctypes.c_void_p(s)))
     return out
+
+
+def gemm_group(problems: list[dict], stream: torch.cuda.Stream | None = None) -> list[torch.Tensor]:
+    """Several gemm() problems (dicts of gemm's keyword arguments, x and w required) in one
+    call; two that share N, K, dtypes and epilogue run as one tensor-core launch."""
+    lib = load()
+    descs, outs = [], []
+    for pr in problems:
+        d, out = _gemm_desc(pr["x"], pr["w"], pr.get("bias"), pr.get("out"), pr.get("out_dtype"),
+                            pr.get("epilogue", "none"), pr.get("gate"))
+        descs.append(d)
+        outs.append(out)
+    arr = (GemmDesc * len(descs))(*descs)
+    dev = problems[0]["x"].device if problems else torch.device("cuda")
+    s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    _check(lib.b2g_gemm_group(arr, len(descs), ctypes.c_void_p(s)))
+    return outs
 
 
 def linear_lt(M: int, K: int, N: int, x: torch.Tensor, x_type: int, w: torch.Tensor, w_type: int,

@@ -16,7 +16,8 @@ updated residual streams; LayerNorm/modulation and the modulation vector are inp
       attn  = attention(qk_norm(qkv))             reference: rms_norm x2 + cuDNN SDPA
       x    += gate * ([attn, mlp] . W2^T + b)     reference: concat_last_dim_to_bf16,
                                                   linear() F32, gated_residual
-Engine fusions: the GELU and the gated residual are GEMM epilogues; qk_norm is fused into the
+Engine fusions: the txt and img GEMMs of each double-block layer share one launch; the GELU
+and the gated residual are GEMM epilogues; qk_norm is fused into the
 attention's RoPE producer; the attention writes bf16 straight into the proj input / the
 concat buffer, and the MLP half of linear1 writes GELU'd bf16 into the other concat columns.
 """
@@ -103,26 +104,28 @@ def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1,
     block_pair_ops order) so a caller can record events between the launches."""
     mark = mark or _no_mark
     T = txt.shape[0]
-    b2g.gemm(txt_mod1, txt_w.qkv_w, txt_w.qkv_b, out=s.qkv[:T])
-    mark("double.txt_qkv")
-    b2g.gemm(img_mod1, img_w.qkv_w, img_w.qkv_b, out=s.qkv[T:])
-    mark("double.img_qkv")
+    # Each layer's txt and img GEMMs share one launch (b2g_gemm_group): together their tiles
+    # fill the SMs where the txt GEMM alone (M=512) would leave most of them idle.
+    b2g.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
+                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
+    mark("double.qkv")
     q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
     b2g.attention_qknorm_rope(q, k, v, pe, HEADS, DHEAD, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm,
                               q_norm2=img_w.q_norm, k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
     mark("double.attention")
-    b2g.gemm(s.attn[:T], txt_w.proj_w, txt_w.proj_b, out=txt, epilogue="gated_residual", gate=txt_gate1)
-    mark("double.txt_proj")
-    b2g.gemm(s.attn[T:], img_w.proj_w, img_w.proj_b, out=img, epilogue="gated_residual", gate=img_gate1)
-    mark("double.img_proj")
-    b2g.gemm(img_mod2, img_w.mlp0_w, img_w.mlp0_b, out=s.h_img, epilogue="gelu")
-    mark("double.img_mlp0")
-    b2g.gemm(s.h_img, img_w.mlp2_w, img_w.mlp2_b, out=img, epilogue="gated_residual", gate=img_gate2)
-    mark("double.img_mlp2")
-    b2g.gemm(txt_mod2, txt_w.mlp0_w, txt_w.mlp0_b, out=s.h_txt, epilogue="gelu")
-    mark("double.txt_mlp0")
-    b2g.gemm(s.h_txt, txt_w.mlp2_w, txt_w.mlp2_b, out=txt, epilogue="gated_residual", gate=txt_gate2)
-    mark("double.txt_mlp2")
+    b2g.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, bias=txt_w.proj_b, out=txt, epilogue="gated_residual",
+                         gate=txt_gate1),
+                    dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, out=img, epilogue="gated_residual",
+                         gate=img_gate1)])
+    mark("double.proj")
+    b2g.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
+                    dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
+    mark("double.mlp0")
+    b2g.gemm_group([dict(x=s.h_txt, w=txt_w.mlp2_w, bias=txt_w.mlp2_b, out=txt, epilogue="gated_residual",
+                         gate=txt_gate2),
+                    dict(x=s.h_img, w=img_w.mlp2_w, bias=img_w.mlp2_b, out=img, epilogue="gated_residual",
+                         gate=img_gate2)])
+    mark("double.mlp2")
 
 
 def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=None) -> None:
@@ -148,24 +151,13 @@ def _no_mark(label: str) -> None:
 def block_pair_ops(T: int, I: int) -> list[tuple[str, str, float]]:
     """(label, kind, FLOPs) of every operation of one double + one single block, in launch order.
 
-    kind "gemm" is one engine GEMM launch (2*M*N*K); kind "attention" is the whole attention
-    (QK^T + PV over 24 heads, 4*L*L*3072, counted unmasked)."""
+    kind "gemm" is one engine GEMM launch (2*M*N*K summed over its problems); kind
+    "attention" is the whole attention (QK^T + PV over 24 heads, 4*L*L*3072, unmasked)."""
     L = T + I
     H3, H = 3 * HIDDEN, HIDDEN
     att = 4.0 * L * L * HIDDEN
-    return [("double.txt_qkv", "gemm", 2.0 * T * H3 * H), ("double.img_qkv", "gemm", 2.0 * I * H3 * H),
-            ("double.attention", "attention", att),
-            ("double.txt_proj", "gemm", 2.0 * T * H * H), ("double.img_proj", "gemm", 2.0 * I * H * H),
-            ("double.img_mlp0", "gemm", 2.0 * I * MLP * H), ("double.img_mlp2", "gemm", 2.0 * I * H * MLP),
-            ("double.txt_mlp0", "gemm", 2.0 * T * MLP * H), ("double.txt_mlp2", "gemm", 2.0 * T * H * MLP),
+    return [("double.qkv", "gemm", 2.0 * L * H3 * H), ("double.attention", "attention", att),
+            ("double.proj", "gemm", 2.0 * L * H * H), ("double.mlp0", "gemm", 2.0 * L * MLP * H),
+            ("double.mlp2", "gemm", 2.0 * L * H * MLP),
             ("single.linear1_qkv", "gemm", 2.0 * L * H3 * H), ("single.linear1_mlp", "gemm", 2.0 * L * MLP * H),
             ("single.attention", "attention", att), ("single.linear2", "gemm", 2.0 * L * H * (H + MLP))]
-
-
-def block_pair_flops(T: int, I: int) -> tuple[float, float]:
-    """(linear FLOPs, attention FLOPs counted unmasked) of one double + one single block."""
-    L = T + I
-    per_tok = HIDDEN * (3 * HIDDEN + HIDDEN + MLP + MLP)  # = 113,246,208 (both block types)
-    linears = 2.0 * L * per_tok * 2
-    attention = 2 * (4.0 * L * L * HIDDEN)
-    return linears, attention

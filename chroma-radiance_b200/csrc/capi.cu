@@ -170,34 +170,93 @@ b2g_status b2g_set_gemm_variant(int variant, int splits) {
   return B2G_OK;
 }
 
-b2g_status b2g_gemm(const b2g_gemm_desc* d, void* stream) {
-  if (!d) return set_error(B2G_ERR_INVALID, "b2g_gemm: null descriptor");
-  if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, "b2g_gemm: negative size");
-  if (d->M == 0 || d->N == 0) return B2G_OK;
-  if (!d->d || (d->K > 0 && (!d->a || !d->b))) return set_error(B2G_ERR_INVALID, "b2g_gemm: null operand");
-  if (d->K > 0 && (d->lda < d->K || d->ldb < d->K)) return set_error(B2G_ERR_INVALID, "b2g_gemm: lda/ldb < K");
-  if (d->ldd < d->N) return set_error(B2G_ERR_INVALID, "b2g_gemm: ldd < N");
+}  // extern "C"
+
+namespace b2g {
+namespace {
+
+// Checks one descriptor (the rules of b2g_gemm) and fills the internal problem.
+// *empty = true for an M == 0 or N == 0 problem (nothing to do).
+b2g_status desc_to_problem(const b2g_gemm_desc* d, const char* who, GemmProblem* p, bool* empty) {
+  const std::string w(who);
+  *empty = false;
+  if (!d) return set_error(B2G_ERR_INVALID, w + ": null descriptor");
+  if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, w + ": negative size");
+  if (d->M == 0 || d->N == 0) {
+    *empty = true;
+    return B2G_OK;
+  }
+  if (!d->d || (d->K > 0 && (!d->a || !d->b))) return set_error(B2G_ERR_INVALID, w + ": null operand");
+  if (d->K > 0 && (d->lda < d->K || d->ldb < d->K)) return set_error(B2G_ERR_INVALID, w + ": lda/ldb < K");
+  if (d->ldd < d->N) return set_error(B2G_ERR_INVALID, w + ": ldd < N");
   if (d->epilogue == B2G_EPI_GATED_RESIDUAL && (!d->gate || d->d_dtype != B2G_F32))
-    return set_error(B2G_ERR_INVALID, "b2g_gemm: gated residual needs a gate and an F32 output");
+    return set_error(B2G_ERR_INVALID, w + ": gated residual needs a gate and an F32 output");
   if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_GATED_RESIDUAL)
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: unknown epilogue");
+    return set_error(B2G_ERR_UNSUPPORTED, w + ": unknown epilogue");
   if (d->a_dtype == B2G_E4M3 || d->b_dtype == B2G_E4M3 || d->d_dtype == B2G_E4M3)
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: E4M3 operands are not implemented");
+    return set_error(B2G_ERR_UNSUPPORTED, w + ": E4M3 operands are not implemented");
   const bool ab16 = d->b_dtype == B2G_BF16 || d->b_dtype == B2G_F16;
   if (!(d->a_dtype == d->b_dtype || (d->a_dtype == B2G_F32 && ab16)))
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm: unsupported operand dtype combination");
+    return set_error(B2G_ERR_UNSUPPORTED, w + ": unsupported operand dtype combination");
+  p->M = d->M; p->N = d->N; p->K = d->K;
+  p->a = d->a; p->a_dtype = d->a_dtype; p->lda = d->lda;
+  p->b = d->b; p->b_dtype = d->b_dtype; p->ldb = d->ldb;
+  p->bias = d->bias; p->bias_dtype = d->bias_dtype;
+  p->d = d->d; p->d_dtype = d->d_dtype; p->ldd = d->ldd;
+  p->epilogue = d->epilogue;
+  p->gate = d->gate;
+  return B2G_OK;
+}
+
+}  // namespace
+}  // namespace b2g
+
+extern "C" {
+
+b2g_status b2g_gemm(const b2g_gemm_desc* d, void* stream) {
+  GemmProblem p;
+  bool empty = false;
+  b2g_status s = desc_to_problem(d, "b2g_gemm", &p, &empty);
+  if (s != B2G_OK || empty) return s;
+  DeviceInfo* dev = nullptr;
+  if ((s = device_info(&dev)) != B2G_OK) return s;
+  return run_gemm(p, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
+  if (count < 0 || (count > 0 && !descs)) return set_error(B2G_ERR_INVALID, "b2g_gemm_group: bad descriptor array");
+  GemmProblem ps[2];
+  int n = 0;
+  bool all_empty = true;
+  for (int i = 0; i < count; ++i) {
+    GemmProblem p;
+    bool empty = false;
+    b2g_status s = desc_to_problem(descs + i, "b2g_gemm_group", &p, &empty);
+    if (s != B2G_OK) return s;
+    if (!empty) {
+      all_empty = false;
+      if (n < 2) ps[n] = p;
+      ++n;
+    }
+  }
+  if (all_empty) return B2G_OK;
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
-  GemmProblem p;
-  p.M = d->M; p.N = d->N; p.K = d->K;
-  p.a = d->a; p.a_dtype = d->a_dtype; p.lda = d->lda;
-  p.b = d->b; p.b_dtype = d->b_dtype; p.ldb = d->ldb;
-  p.bias = d->bias; p.bias_dtype = d->bias_dtype;
-  p.d = d->d; p.d_dtype = d->d_dtype; p.ldd = d->ldd;
-  p.epilogue = d->epilogue;
-  p.gate = d->gate;
-  return run_gemm(p, static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // One launch when the (at most two) non-empty problems run on the tensor cores without an
+  // activation cast and agree on everything but M and their pointers; otherwise one GEMM
+  // after the other on the stream.
+  if (n == 2 && ps[0].K > 0 && tc_gemm_supported(ps[0], nullptr) && tc_gemm_supported(ps[1], nullptr) &&
+      tc_gemm_groupable(ps[0], ps[1]))
+    return tc_gemm_launch_group(ps, 2, st);
+  for (int i = 0; i < count; ++i) {
+    GemmProblem p;
+    bool empty = false;
+    if ((s = desc_to_problem(descs + i, "b2g_gemm_group", &p, &empty)) != B2G_OK) return s;
+    if (!empty && (s = run_gemm(p, st)) != B2G_OK) return s;
+  }
+  return B2G_OK;
 }
 
 b2g_status b2g_linear_lt_stream(int64_t M, int64_t K, int64_t N, const void* x_data, cudaDataType_t x_type,

@@ -48,6 +48,10 @@ void workspace_release();
 // True if the tensor-core path can run this problem (dtypes, strides, alignment).
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
+// One launch over `count` (<= 2) problems that tc_gemm_groupable() accepts pairwise; their
+// tiles share the persistent grid (fills the SMs where each problem alone would not).
+bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b);
+b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t st);
 // Kernel variant override for tests/tuning: -1 automatic, 0 = 1-CTA 128x128 tiles,
 // 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits);

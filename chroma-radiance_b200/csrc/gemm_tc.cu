@@ -57,18 +57,36 @@ constexpr int kOutBufBytes = 4096;
 constexpr int kOutStageBytes = kEpiWarps * kOutBufBytes;  // 32 KB
 constexpr int kBiasBytes = 256 * 4;                       // bias of one tile (<= 256 columns)
 
-struct TcParams {
-  int M, N, K, batch;
-  int num_m_blocks, num_n_blocks, num_k_blocks, num_tiles;
-  int group_m;             // rasterisation group (m-blocks that share B panels in flight)
+// A launch computes up to kMaxGroups independent problems that share N, K, dtypes and the
+// epilogue (the txt and img streams of a double block: same layer shapes, their own rows,
+// weights, biases and gates).  Their tiles are numbered one group after the other.
+constexpr int kMaxGroups = 2;
+
+struct TcGroup {
+  int M;                   // rows of A and D
+  int num_m_blocks;        // tile rows
+  int tile0;               // index of the group's first tile
+  int vec_ok;              // D base/ldd allow 16-byte vector stores
   void* d;
-  long long ldd, d_bstride;
+  long long ldd;
   const void* bias;
-  int bias_kind;           // 0 none, 1 f32, 2 bf16
   const float* gate;
+};
+
+// Tensor maps of every group (kernel parameter; indexed by group at run time).
+struct TcMaps {
+  CUtensorMap a[kMaxGroups], b[kMaxGroups], d[kMaxGroups];
+};
+
+struct TcParams {
+  int N, K, batch;
+  int num_n_blocks, num_k_blocks, num_tiles;  // num_tiles: all groups
+  int groups;
+  int raster_m;            // rasterisation group (m-blocks that share B panels in flight)
+  long long d_bstride;
+  int bias_kind;           // 0 none, 1 f32, 2 bf16
   int* err;
   uint32_t idesc;
-  int vec_ok;              // D base/ldd allow 16-byte vector stores
   int a_keep;              // 1: keep A in L2 (evict_last), stream B (evict_first); 0: reverse
   int splits;              // split-K factor S (1 = none); work item = (split, tile)
   int num_items;           // num_tiles * splits
@@ -76,6 +94,7 @@ struct TcParams {
   int* counters;           // split-K arrival counter per slot (zero between launches)
   int tma_store;           // 1: outputs leave through smem staging + TMA bulk tensor stores
   float alpha;             // accumulator scale before the bias (1 for every linear layer)
+  TcGroup g[kMaxGroups];
 };
 
 __host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int stages) {
@@ -83,16 +102,20 @@ __host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int st
          256 /* barriers, TMEM slot, broadcast word */;
 }
 
-__device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& bz, int& mb, int& nb) {
-  const int per_batch = p.num_m_blocks * p.num_n_blocks;
-  bz = tile / per_batch;
-  int r = tile - bz * per_batch;
-  // Groups of group_m m-blocks; inside a group m varies fastest, so the CTAs in flight
+__device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi, int& bz, int& mb, int& nb) {
+  gi = (p.groups > 1 && tile >= p.g[1].tile0) ? 1 : 0;
+  const int nmb = p.g[gi].num_m_blocks;
+  const int t = tile - p.g[gi].tile0;
+  const int per_batch = nmb * p.num_n_blocks;
+  bz = t / per_batch;
+  int r = t - bz * per_batch;
+  // Raster groups of raster_m m-blocks; inside one, m varies fastest, so the CTAs in flight
   // read the same few B panels and the same group of A rows (both stay in L2).
-  const int group_size = p.group_m * p.num_n_blocks;
+  const int rm = min(p.raster_m, nmb);
+  const int group_size = rm * p.num_n_blocks;
   const int g = r / group_size;
-  const int first_m = g * p.group_m;
-  const int gm = min(p.num_m_blocks - first_m, p.group_m);
+  const int first_m = g * rm;
+  const int gm = min(nmb - first_m, rm);
   r -= g * group_size;
   mb = first_m + r % gm;
   nb = r / gm;
@@ -154,18 +177,18 @@ __device__ __forceinline__ void pack16(const float (&v)[32], uint32_t (&packed)[
 
 // Direct stores of one thread's 32 values of row m, columns [n0, n0+32).
 template <int EPI, int OUT>
-__device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, int n0, const uint32_t (&r)[32],
-                                            const float* sb) {
+__device__ __forceinline__ void store_chunk(const TcParams& p, const TcGroup& G, int bz, int m, int n0,
+                                            const uint32_t (&r)[32], const float* sb) {
   float v[32];
   chunk_values<EPI>(r, sb, p.alpha, v);
   const bool full = (n0 + 32 <= p.N);
   const int nvalid = full ? 32 : (p.N - n0);
-  const long long off = static_cast<long long>(bz) * p.d_bstride + static_cast<long long>(m) * p.ldd + n0;
+  const long long off = static_cast<long long>(bz) * p.d_bstride + static_cast<long long>(m) * G.ldd + n0;
   if constexpr (OUT == OUT_F32) {
-    float* dp = static_cast<float*>(p.d) + off;
+    float* dp = static_cast<float*>(G.d) + off;
     if constexpr (EPI == B2G_EPI_GATED_RESIDUAL) {
-      const float* gp = p.gate + n0;
-      if (full && p.vec_ok) {
+      const float* gp = G.gate + n0;
+      if (full && G.vec_ok) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           float4 res = reinterpret_cast<const float4*>(dp)[j];
@@ -181,7 +204,7 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
           if (j < nvalid) dp[j] = dp[j] + __ldg(gp + j) * v[j];
       }
     } else {
-      if (full && p.vec_ok) {
+      if (full && G.vec_ok) {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           reinterpret_cast<float4*>(dp)[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
@@ -194,8 +217,8 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int bz, int m, in
   } else {
     uint32_t packed[16];
     pack16<OUT>(v, packed);
-    uint16_t* dp = static_cast<uint16_t*>(p.d) + off;
-    if (full && p.vec_ok) {
+    uint16_t* dp = static_cast<uint16_t*>(G.d) + off;
+    if (full && G.vec_ok) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         reinterpret_cast<uint4*>(dp)[j] =
@@ -253,13 +276,13 @@ __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_
 
 // Writes one finished 32-column chunk: TMA-staged when enabled, else direct stores.
 template <int EPI, int OUT>
-__device__ __forceinline__ void emit_chunk(const TcParams& p, const CUtensorMap* tmD, uint8_t* buf, int& obuf, int bz,
-                                           int m, int m_warp0, int n0, const uint32_t (&r)[32], const float* sb,
-                                           int lane) {
+__device__ __forceinline__ void emit_chunk(const TcParams& p, const TcGroup& G, const CUtensorMap* tmD, uint8_t* buf,
+                                           int& obuf, int bz, int m, int m_warp0, int n0, const uint32_t (&r)[32],
+                                           const float* sb, int lane) {
   if (EPI != B2G_EPI_GATED_RESIDUAL && p.tma_store) {
-    if (m_warp0 < p.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, obuf, bz, m_warp0, n0, r, sb, p.alpha, lane);
-  } else if (m < p.M && n0 < p.N) {
-    store_chunk<EPI, OUT>(p, bz, m, n0, r, sb);
+    if (m_warp0 < G.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, obuf, bz, m_warp0, n0, r, sb, p.alpha, lane);
+  } else if (m < G.M && n0 < p.N) {
+    store_chunk<EPI, OUT>(p, G, bz, m, n0, r, sb);
   }
 }
 
@@ -273,14 +296,14 @@ struct EpiCtx {
 
 // Loads this item's bias columns [n_base, n_base+BN) into shared memory (zero past N).
 template <int BN>
-__device__ __forceinline__ void stage_bias(const TcParams& p, float* sbias, int n_base) {
+__device__ __forceinline__ void stage_bias(const TcParams& p, const TcGroup& G, float* sbias, int n_base) {
   if (p.bias_kind == 0) return;
   for (int i = static_cast<int>(threadIdx.x) - 64; i < BN; i += kEpiThreads) {
     const int n = n_base + i;
     float b = 0.f;
     if (n < p.N)
-      b = p.bias_kind == 1 ? __ldg(static_cast<const float*>(p.bias) + n)
-                           : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
+      b = p.bias_kind == 1 ? __ldg(static_cast<const float*>(G.bias) + n)
+                           : __bfloat162float(static_cast<const __nv_bfloat16*>(G.bias)[n]);
     sbias[i] = b;
   }
 }
@@ -291,9 +314,9 @@ __device__ __forceinline__ void stage_bias(const TcParams& p, float* sbias, int 
 // partial; the split arriving last on the slot's counter sums all partials in split order
 // (deterministic), runs the epilogue and re-arms the counter for the next launch.
 template <int BN, int EPI, int OUT, typename Release>
-__device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e, int& obuf, uint32_t tacc,
-                                              Release release, const CUtensorMap* tmD, int bz, int m, int n_base,
-                                              int slot, int split) {
+__device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
+                                              uint32_t tacc, Release release, const CUtensorMap* tmD, int bz, int m,
+                                              int n_base, int slot, int split) {
   constexpr int NCH = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
   const int c0 = e.half * NCH;
   const int m_warp0 = m - e.lane;
@@ -309,7 +332,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e
     if (i == NCH - 1) release();
     const int c = c0 + i;
     if (!splitk) {
-      emit_chunk<EPI, OUT>(p, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, r[i & 1],
+      emit_chunk<EPI, OUT>(p, G, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, r[i & 1],
                            sb ? sb + c * 32 : nullptr, e.lane);
     } else {
       float4* dst = reinterpret_cast<float4*>(part + c * 32);
@@ -347,8 +370,8 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e
         uint32_t rr[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) rr[j] = __float_as_uint(acc[j]);
-        emit_chunk<EPI, OUT>(p, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, rr, sb ? sb + c * 32 : nullptr,
-                             e.lane);
+        emit_chunk<EPI, OUT>(p, G, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, rr,
+                             sb ? sb + c * 32 : nullptr, e.lane);
       }
       if (threadIdx.x == 64) p.counters[slot] = 0;
     }
@@ -359,8 +382,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const EpiCtx& e
 // ---------------------------------------------------------------------------- 1-CTA kernel
 template <int BN, int STAGES, int EPI, int OUT, int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmD, const TcParams p) {
+    tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcParams p) {
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
   constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators; 256 or 512 (power of two)
@@ -394,9 +416,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-    if (p.tma_store) tma_prefetch_desc(&tmD);
+    for (int gi = 0; gi < p.groups; ++gi) {
+      tma_prefetch_desc(&maps.a[gi]);
+      tma_prefetch_desc(&maps.b[gi]);
+      if (p.tma_store) tma_prefetch_desc(&maps.d[gi]);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -418,17 +442,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, issued = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
-        int tile, split, kb0, kb1, bz, mb, nb;
+        int tile, split, kb0, kb1, gi, bz, mb, nb;
         item_coords(item, p, tile, split, kb0, kb1);
-        tile_coords(tile, p, bz, mb, nb);
+        tile_coords(tile, p, gi, bz, mb, nb);
+        const CUtensorMap* tmA = &maps.a[gi];
+        const CUtensorMap* tmB = &maps.b[gi];
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrWaitProducer)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full_bar[stage], A_BYTES + B_BYTES);
-          tma_load_3d(sA + stage * A_BYTES, &tmA, &full_bar[stage], kb * kKElems<KIND>, mb * kBM, bz, pa);
-          tma_load_3d(sB + stage * B_BYTES, &tmB, &full_bar[stage], kb * kKElems<KIND>, nb * BN, bz, pb);
+          tma_load_3d(sA + stage * A_BYTES, tmA, &full_bar[stage], kb * kKElems<KIND>, mb * kBM, bz, pa);
+          tma_load_3d(sB + stage * B_BYTES, tmB, &full_bar[stage], kb * kKElems<KIND>, nb * BN, bz, pb);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -503,10 +529,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int obuf = 0;
     uint32_t local = 0;
     for (int item = blockIdx.x; item < p.num_items; item += gridDim.x, ++local) {
-      int tile, split, kb0, kb1, bz, mb, nb;
+      int tile, split, kb0, kb1, gi, bz, mb, nb;
       item_coords(item, p, tile, split, kb0, kb1);
-      tile_coords(tile, p, bz, mb, nb);
-      stage_bias<BN>(p, sBias, nb * BN);
+      tile_coords(tile, p, gi, bz, mb, nb);
+      const TcGroup& G = p.g[gi];
+      stage_bias<BN>(p, G, sBias, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
@@ -519,7 +546,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       };
-      epilogue_item<BN, EPI, OUT>(p, e, obuf, tacc, release, &tmD, bz, mb * kBM + e.row, nb * BN, tile, split);
+      epilogue_item<BN, EPI, OUT>(p, G, e, obuf, tacc, release, &maps.d[gi], bz, mb * kBM + e.row, nb * BN, tile,
+                                  split);
     }
     if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
@@ -546,8 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   tempty[a] (CTA 0 only)  all 16 epilogue warps of the pair have read accumulator a.
 template <int STAGES, int EPI, int OUT, int KIND>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                        const __grid_constant__ CUtensorMap tmD, const TcParams p) {
+    tc_gemm_pair_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcParams p) {
   constexpr int BN = 256;
   constexpr uint32_t A_BYTES = kBM * kBK * 2;  // this CTA's 128 rows of A
   constexpr uint32_t B_BYTES = 128 * kBK * 2;  // this CTA's 128 rows of B
@@ -584,9 +611,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-    if (p.tma_store) tma_prefetch_desc(&tmD);
+    for (int gi = 0; gi < p.groups; ++gi) {
+      tma_prefetch_desc(&maps.a[gi]);
+      tma_prefetch_desc(&maps.b[gi]);
+      if (p.tma_store) tma_prefetch_desc(&maps.d[gi]);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -608,9 +637,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, issued = 0;
       bool ok = true;
       for (int item = cluster; item < p.num_items && ok; item += nclusters) {
-        int tile, split, kb0, kb1, bz, mb, nb;
+        int tile, split, kb0, kb1, gi, bz, mb, nb;
         item_coords(item, p, tile, split, kb0, kb1);
-        tile_coords(tile, p, bz, mb, nb);
+        tile_coords(tile, p, gi, bz, mb, nb);
+        const CUtensorMap* tmA = &maps.a[gi];
+        const CUtensorMap* tmB = &maps.b[gi];
         const int arow = mb * 256 + static_cast<int>(rank) * 128;
         const int brow = nb * BN + static_cast<int>(rank) * 128;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -620,8 +651,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (A_BYTES + B_BYTES));
           const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
-          tma_load_3d_pair(sA + stage * A_BYTES, &tmA, leader_full, kb * kKElems<KIND>, arow, bz, pa);
-          tma_load_3d_pair(sB + stage * B_BYTES, &tmB, leader_full, kb * kKElems<KIND>, brow, bz, pb);
+          tma_load_3d_pair(sA + stage * A_BYTES, tmA, leader_full, kb * kKElems<KIND>, arow, bz, pa);
+          tma_load_3d_pair(sB + stage * B_BYTES, tmB, leader_full, kb * kKElems<KIND>, brow, bz, pb);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -695,10 +726,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     int obuf = 0;
     uint32_t local = 0;
     for (int item = cluster; item < p.num_items; item += nclusters, ++local) {
-      int tile, split, kb0, kb1, bz, mb, nb;
+      int tile, split, kb0, kb1, gi, bz, mb, nb;
       item_coords(item, p, tile, split, kb0, kb1);
-      tile_coords(tile, p, bz, mb, nb);
-      stage_bias<BN>(p, sBias, nb * BN);
+      tile_coords(tile, p, gi, bz, mb, nb);
+      const TcGroup& G = p.g[gi];
+      stage_bias<BN>(p, G, sBias, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
@@ -710,7 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
       };
-      epilogue_item<BN, EPI, OUT>(p, e, obuf, tacc, release, &tmD, bz,
+      epilogue_item<BN, EPI, OUT>(p, G, e, obuf, tacc, release, &maps.d[gi], bz,
                                   mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN,
                                   tile * 2 + static_cast<int>(rank), split);
     }
@@ -804,49 +836,47 @@ b2g_status make_output_map(CUtensorMap* map, void* base, b2g_dtype dt, int64_t N
 }
 
 template <typename Kern>
-b2g_status launch_kernel(Kern kern, size_t smem, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                         const TcParams& prm, int grid, cudaStream_t st) {
+b2g_status launch_kernel(Kern kern, size_t smem, const TcMaps& maps, const TcParams& prm, int grid, cudaStream_t st) {
   b2g_status s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "cudaFuncSetAttribute(tc_gemm)");
   if (s != B2G_OK) return s;
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, td, prm);
+  kern<<<grid, kThreads, smem, st>>>(maps, prm);
   note_launch();
   return check_cuda(cudaGetLastError(), "tc_gemm launch");
 }
 
 // Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.
 template <bool PAIR, int BN, int STAGES, int EPI, int OUT, int KIND>
-b2g_status launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const TcParams& prm,
-                      int grid, cudaStream_t st) {
+b2g_status launch_one(const TcMaps& maps, const TcParams& prm, int grid, cudaStream_t st) {
   if constexpr (PAIR) {
     constexpr size_t smem = smem_bytes(kBM * kBK * 2, 128 * kBK * 2, STAGES);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, ta, tb, td, prm, grid, st);
+    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
   } else {
     constexpr size_t smem = smem_bytes(kBM * kBK * 2, BN * kBK * 2, STAGES);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, ta, tb, td, prm, grid, st);
+    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
   }
 }
 
 template <bool PAIR, int BN, int STAGES>
-b2g_status dispatch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const TcParams& prm,
-                        int grid, b2g_epilogue epi, b2g_dtype out, bool tf32, cudaStream_t st) {
+b2g_status dispatch_epi(const TcMaps& maps, const TcParams& prm, int grid, b2g_epilogue epi, b2g_dtype out, bool tf32,
+                        cudaStream_t st) {
   if (tf32) {
     // fp32 operands (batched_matmul_Bt): plain F32 output only.
     if (epi != B2G_EPI_NONE || out != B2G_F32) return set_error(B2G_ERR_UNSUPPORTED, "tf32 path: F32 output only");
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(ta, tb, td, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(maps, prm, grid, st);
   }
   if (epi == B2G_EPI_GATED_RESIDUAL)
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(ta, tb, td, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(maps, prm, grid, st);
   if (epi == B2G_EPI_GELU) {
-    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(ta, tb, td, prm, grid, st);
-    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(ta, tb, td, prm, grid, st);
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(ta, tb, td, prm, grid, st);
+    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(maps, prm, grid, st);
+    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(maps, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(maps, prm, grid, st);
   }
-  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(ta, tb, td, prm, grid, st);
-  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(ta, tb, td, prm, grid, st);
-  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(ta, tb, td, prm, grid, st);
+  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(maps, prm, grid, st);
+  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(maps, prm, grid, st);
+  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(maps, prm, grid, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -874,7 +904,22 @@ bool tc_gemm_supported(const GemmProblem& p, std::string* why) {
   return true;
 }
 
-b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
+// Problems that can share one launch: same N, K, batch (1 when grouped), operand, bias and
+// output dtypes, epilogue and alpha.
+bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
+  return a.N == b.N && a.K == b.K && a.batch == 1 && b.batch == 1 && a.a_dtype == b.a_dtype &&
+         a.b_dtype == b.b_dtype && a.d_dtype == b.d_dtype && a.epilogue == b.epilogue && a.alpha == b.alpha &&
+         (a.bias == nullptr) == (b.bias == nullptr) && (!a.bias || a.bias_dtype == b.bias_dtype) &&
+         a.allow_split == b.allow_split;
+}
+
+b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) { return tc_gemm_launch_group(&p, 1, st); }
+
+b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t st) {
+  if (count < 1 || count > kMaxGroups) return set_error(B2G_ERR_INVALID, "tc_gemm: 1 or 2 problems per launch");
+  for (int i = 1; i < count; ++i)
+    if (!tc_gemm_groupable(ps[0], ps[i])) return set_error(B2G_ERR_INVALID, "tc_gemm: problems cannot share a launch");
+  const GemmProblem& p = ps[0];
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
@@ -892,7 +937,7 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   // Kernel variant and split-K factor from a cost model in units of one 64-wide k-block of
   // a pair tile: whole waves of work items over the SMs (or SM pairs), times the k-blocks
   // per item, times the variant's measured relative cost per k-block, plus the split-K
-  // reduction overhead.
+  // reduction overhead.  The tiles of all problems of the launch form one pool of work.
   enum { V128 = 0, V256 = 1, VPAIR = 2 };
   int v = VPAIR, splits = 1;
   double best = 1e300;
@@ -900,7 +945,8 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
     if (cand == VPAIR && !g_allow_pair) continue;
     if (cand != V128 && p.N <= 128) continue;
     const long long tm = cand == VPAIR ? 256 : 128, tn = cand == V128 ? 128 : 256;
-    const long long tiles = p.batch * ((p.M + tm - 1) / tm) * ((p.N + tn - 1) / tn);
+    long long tiles = 0;
+    for (int i = 0; i < count; ++i) tiles += ps[i].batch * ((ps[i].M + tm - 1) / tm) * ((p.N + tn - 1) / tn);
     const long long slots = cand == VPAIR ? pairs : sms;
     const double kb_cost = cand == V128 ? kCost128 : (cand == V256 ? kCost256 : kCostPair);
     for (int sk = 1; sk <= 8 && sk <= nkb; ++sk) {
@@ -926,31 +972,42 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
   const int tile_m = pair ? 256 : kBM;
 
   TcParams prm{};
-  prm.M = static_cast<int>(p.M);
   prm.N = static_cast<int>(p.N);
   prm.K = static_cast<int>(p.K);
   prm.batch = static_cast<int>(p.batch);
-  prm.num_m_blocks = static_cast<int>((p.M + tile_m - 1) / tile_m);
   prm.num_n_blocks = static_cast<int>((p.N + bn - 1) / bn);
   prm.num_k_blocks = static_cast<int>(nkb);
-  prm.num_tiles = prm.batch * prm.num_m_blocks * prm.num_n_blocks;
+  prm.groups = count;
+  prm.raster_m = pair ? 8 : 16;
+  const int out_bytes = p.d_dtype == B2G_F32 ? 4 : 2;
+  bool all_vec = true;
+  double a_bytes = 0, b_bytes = 0;
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const GemmProblem& q = ps[i];
+    TcGroup& G = prm.g[i];
+    G.M = static_cast<int>(q.M);
+    G.num_m_blocks = static_cast<int>((q.M + tile_m - 1) / tile_m);
+    G.tile0 = tiles;
+    tiles += prm.batch * G.num_m_blocks * prm.num_n_blocks;
+    G.d = q.d;
+    G.ldd = q.ldd;
+    G.bias = q.bias;
+    G.gate = q.gate;
+    G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
+               (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
+    all_vec = all_vec && G.vec_ok;
+    a_bytes += static_cast<double>(q.M) * q.K;
+    b_bytes += static_cast<double>(q.N) * q.K;
+  }
+  prm.num_tiles = tiles;
   prm.splits = splits;
   prm.num_items = prm.num_tiles * splits;
-  const int group = pair ? 8 : 16;
-  prm.group_m = prm.num_m_blocks <= group ? prm.num_m_blocks : group;
-  prm.d = p.d;
-  prm.ldd = p.ldd;
   prm.d_bstride = p.batch > 1 ? p.d_bstride : 0;
-  prm.bias = p.bias;
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
-  prm.gate = p.gate;
   prm.alpha = p.alpha;
   prm.err = dev->err_word;
   prm.idesc = idesc_make(tf32 ? kFmtTF32 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16), tile_m, bn);
-  const int out_bytes = p.d_dtype == B2G_F32 ? 4 : 2;
-  prm.vec_ok = aligned16(p.d) && ((p.ldd * out_bytes) % 16 == 0) &&
-               (p.batch <= 1 || (p.d_bstride * out_bytes) % 16 == 0);
-  const double a_bytes = static_cast<double>(p.M) * p.K, b_bytes = static_cast<double>(p.N) * p.K;
   prm.a_keep = a_bytes <= b_bytes ? 1 : 0;
   if (prm.num_tiles == 0) return B2G_OK;
 
@@ -964,27 +1021,29 @@ b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) {
     prm.counters = static_cast<int*>(ctr);
   }
 
-  CUtensorMap ta, tb, td;
-  const int64_t a_bs = p.batch > 1 ? p.a_bstride : p.lda * p.M;
-  const int64_t b_bs = p.batch > 1 ? p.b_bstride : p.ldb * p.N;
+  TcMaps maps;
+  memset(&maps, 0, sizeof(maps));
   const uint32_t b_box = v == V256 ? 256u : 128u;
-  if ((s = make_operand_map(&ta, p.a, p.a_dtype, p.K, p.M, p.lda, p.batch, a_bs, kBM)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tb, p.b, p.b_dtype, p.K, p.N, p.ldb, p.batch, b_bs, b_box)) != B2G_OK) return s;
-  memset(&td, 0, sizeof(td));
-  prm.tma_store = 0;
-  if (p.epilogue != B2G_EPI_GATED_RESIDUAL && prm.vec_ok && g_tma_store) {
-    const int64_t d_bs = p.batch > 1 ? p.d_bstride : p.ldd * p.M;
-    if ((s = make_output_map(&td, p.d, p.d_dtype, p.N, p.M, p.ldd, p.batch, d_bs)) != B2G_OK) return s;
-    prm.tma_store = 1;
+  prm.tma_store = p.epilogue != B2G_EPI_GATED_RESIDUAL && all_vec && g_tma_store ? 1 : 0;
+  for (int i = 0; i < count; ++i) {
+    const GemmProblem& q = ps[i];
+    const int64_t a_bs = q.batch > 1 ? q.a_bstride : q.lda * q.M;
+    const int64_t b_bs = q.batch > 1 ? q.b_bstride : q.ldb * q.N;
+    if ((s = make_operand_map(&maps.a[i], q.a, q.a_dtype, q.K, q.M, q.lda, q.batch, a_bs, kBM)) != B2G_OK) return s;
+    if ((s = make_operand_map(&maps.b[i], q.b, q.b_dtype, q.K, q.N, q.ldb, q.batch, b_bs, b_box)) != B2G_OK) return s;
+    if (prm.tma_store) {
+      const int64_t d_bs = q.batch > 1 ? q.d_bstride : q.ldd * q.M;
+      if ((s = make_output_map(&maps.d[i], q.d, q.d_dtype, q.N, q.M, q.ldd, q.batch, d_bs)) != B2G_OK) return s;
+    }
   }
 
   if (pair) {
     const int grid = 2 * static_cast<int>(prm.num_items < pairs ? prm.num_items : pairs);
-    return dispatch_epi<true, 256, kPairStages>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+    return dispatch_epi<true, 256, kPairStages>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
   }
   const int grid = static_cast<int>(prm.num_items < sms ? prm.num_items : sms);
-  if (v == V256) return dispatch_epi<false, 256, kStages256>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
-  return dispatch_epi<false, 128, kStages128>(ta, tb, td, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  if (v == V256) return dispatch_epi<false, 256, kStages256>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  return dispatch_epi<false, 128, kStages128>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
 }
 
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits) {

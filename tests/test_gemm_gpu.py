@@ -301,6 +301,73 @@ def test_batched_matmul_bt_vs_reference(engine, ref, oracle, batch, M, K, N):
     assert rel_err(mine.cpu().numpy(), t) <= TOL_F32_OUT, f"reference vs oracle per batch: {per_batch_ref}"
 
 
+GROUPS = [
+    # (M0, M1, N, K): the double block's txt/img layer pairs at 512^2, then ragged shapes
+    (512, 1024, 9216, 3072), (512, 1024, 3072, 3072), (512, 1024, 3072, 12288), (100, 300, 700, 136),
+    (1, 77, 64, 8),
+]
+
+
+@pytest.mark.parametrize("variant", [-1, 0, 1, 2])
+@pytest.mark.parametrize("M0,M1,N,K", GROUPS)
+@pytest.mark.parametrize("epilogue,out_dtype", [("none", torch.float32), ("gelu", torch.bfloat16),
+                                                ("gated_residual", torch.float32)])
+def test_gemm_group_one_launch(engine, variant, M0, M1, N, K, epilogue, out_dtype):
+    """Two problems with their own rows, weights, biases and gates in one launch."""
+    if variant in (1, 2) and N <= 128:
+        pytest.skip("256-wide tiles need N > 128")
+    engine.set_gemm_variant(variant, 0)
+    try:
+        probs, refs = [], []
+        for i, M in enumerate((M0, M1)):
+            x = seeded((M, K), 7 * M + i)
+            w = seeded((N, K), 11 * M + i, 0.02)
+            b = seeded((N,), 13 * M + i, 0.02, torch.float32)
+            gate = seeded((N,), 17 * M + i, 1.0, torch.float32) if epilogue == "gated_residual" else None
+            out = (seeded((M, N), 19 * M + i, 1.0, torch.float32) if gate is not None
+                   else torch.empty((M, N), dtype=out_dtype, device=DEV))
+            y = fp32_ref(x, w, b)
+            if epilogue == "gelu":
+                y = gelu_t(y)
+            elif gate is not None:
+                y = out.double() + gate.double() * y
+            refs.append(y)
+            probs.append(dict(x=x, w=w, bias=b, out=out, epilogue=epilogue, gate=gate))
+        n0 = engine.launch_count()
+        engine.gemm_group(probs)
+        torch.cuda.synchronize()
+        assert engine.launch_count() - n0 == 1
+        for pr, y in zip(probs, refs):
+            check(pr["out"], y)
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    engine.check_device_error()
+
+
+def test_gemm_group_split_k(engine):
+    engine.set_gemm_variant(2, 3)
+    try:
+        xs = [seeded((M, 3072), M) for M in (512, 1024)]
+        ws = [seeded((3072, 3072), M + 1, 0.02) for M in (512, 1024)]
+        outs = engine.gemm_group([dict(x=x, w=w) for x, w in zip(xs, ws)])
+        torch.cuda.synchronize()
+        for x, w, o in zip(xs, ws, outs):
+            check(o, fp32_ref(x, w))
+    finally:
+        engine.set_gemm_variant(-1, 0)
+
+
+def test_gemm_group_mismatched_problems_run_one_by_one(engine):
+    x0, w0 = seeded((64, 256), 1), seeded((128, 256), 2, 0.02)
+    x1, w1 = seeded((96, 256), 3), seeded((192, 256), 4, 0.02)      # different N: no shared launch
+    n0 = engine.launch_count()
+    o0, o1 = engine.gemm_group([dict(x=x0, w=w0), dict(x=x1, w=w1, out_dtype=torch.bfloat16)])
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 2
+    check(o0, fp32_ref(x0, w0))
+    check(o1, fp32_ref(x1, w1))
+
+
 def test_strided_views_like_txt_img_rows(engine):
     """Operands and outputs that are row-offset views of larger buffers (the reference's
     txt/img views) with row strides larger than K / N."""
