@@ -1,22 +1,22 @@
-// attention.cu — the Chroma transformer's attention as two tensor-core batched GEMMs.
+// attention.cu — the Chroma transformer's attention on the tensor cores.
 //
 // Replaces cudnn_attention_with_rope (cudnn_attention.cuh:449-476): RoPE + bf16 on Q and K
 // (apply_rope_fused_bf16, rope.cuh:180-221), V to bf16, softmax(Q K^T / sqrt(D) + key_bias) V
-// (cuDNN SDPA, cudnn_attention.cuh:408-443), output F32 [L, H*D].
+// (cuDNN SDPA, cudnn_attention.cuh:408-443), output F32 [L, H*D] (or bf16 for the block path).
 //
 //   1. qknorm_rope_bf16  Q, K F32 rows [L, H*D] -> optional per-head RMSNorm (qk_norm) ->
-//                        RoPE -> bf16 [L, H*D].  The layout is kept: the GEMMs below read
-//                        head h through TMA batch strides (row stride H*D, batch stride D),
-//                        so no permute pass.
-//   2. v_to_bf16_t       V F32 [L, H*D] -> bf16 [H, D, L] (the PV GEMM's K-major B operand).
-//   3. S = alpha Q K^T + key_bias     batched GEMM, batch = H, M = N = L, K = D, F32 out;
-//                        the key mask (0 / -inf) is the GEMM's per-column bias.
-//   4. softmax_rows      S -> P bf16 (rows normalised; masked keys get exactly 0).
-//   5. O = P V           batched GEMM, batch = H, M = L, N = D, K = L, written straight into
-//                        the F32 [L, H*D] output (row stride H*D, batch stride D).
+//                        RoPE -> bf16 [L, H*D].  The layout is kept: the attention kernel
+//                        reads head h through TMA (row stride H*D, head stride D).
+//   2. v_to_bf16_t       V F32 [L, H*D] -> bf16 [H, D, L] (K-major operand of P.V).
+//   3. key_bias_log2     key mask (0 / -inf) scaled by log2(e), -inf past L, padded to 128.
+//   4. flash_attn        one CTA per (128-query tile, head): S = Q K^T on the tensor cores
+//                        into TMEM, online softmax in registers, P (bf16) through shared
+//                        memory into O += P V, O / rowsum written to the output layout.
+//                        S never leaves the SM.
 #include <cuda_bf16.h>
 #include <cstdint>
 #include "engine.cuh"
+#include "ptx_sm100.cuh"
 
 namespace b2g {
 
@@ -74,73 +74,394 @@ __global__ void v_to_bf16_t_kernel(const float* __restrict__ v, long long ldv, _
   }
 }
 
-// One warp per row: max, sum of exp(s - max), then P = exp(s - max) / sum as bf16.
-// A row whose entries are all -inf gives zeros (cannot occur with image tokens present).
-__global__ void softmax_rows_bf16_kernel(const float* __restrict__ S, __nv_bfloat16* __restrict__ P, long long rows,
-                                         int cols) {
-  const long long row = blockIdx.x * static_cast<long long>(blockDim.y) + threadIdx.y;
-  if (row >= rows) return;
-  const float* s = S + row * cols;
-  const int lane = threadIdx.x;
-  float m = -INFINITY, l = 0.f;
-  for (int c = lane * 4; c < cols; c += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(s + c);
-    const float vm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-    const float nm = fmaxf(m, vm);
-    if (nm != -INFINITY) {
-      l = l * __expf(m - nm) + __expf(v.x - nm) + __expf(v.y - nm) + __expf(v.z - nm) + __expf(v.w - nm);
-      m = nm;
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// Key bias for the attention kernel in the exponent's base-2 units: out[k] = bias[k] * log2(e)
+// (bias may be NULL = 0) for k < L, -inf for L <= k < padded (keys past L are TMA zero fill).
+__global__ void key_bias_log2_kernel(const float* __restrict__ bias, float* __restrict__ out, int L, int padded) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= padded) return;
+  out[k] = k < L ? (bias ? bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------- fused attention
+//
+// CTA = (query tile of 128 rows, head h), 192 threads:
+//   warp 0      TMA producer: Q tile once; K tile j [128 keys x D] and Vt tile j [D x 128
+//               keys] into a 2-deep ring (128-byte swizzle, the layout the MMA reads).
+//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=128, K=D) into one of
+//               two TMEM S buffers, then O += P_j Vt_j^T (M=128, N=D, K=128) into TMEM O.
+//               S_{j+1} is issued before P_j is ready, so the tensor core computes the next
+//               scores while the softmax warps work on the current ones.
+//   warps 2-5   softmax, one thread per query row (warp w reads TMEM lanes 32*(w%4)..):
+//               t = S*log2(e)/sqrt(D) + key_bias_log2; running max m (raised only when a
+//               block's max exceeds it by more than 8, i.e. a factor 256, so O in TMEM is
+//               rescaled rarely); P = 2^(t - m) as bf16 into a swizzled shared-memory tile
+//               (double-buffered); l += sum P.  At the end O / l goes to the output.
+// Barriers: q_full; k_full[2], v_full[2] (TMA bytes); kv_empty[2] (MMA commit after P_j.Vt_j);
+// s_full[2] (MMA commit), s_empty[2] (4 softmax warps); p_full[2] (4 softmax warps),
+// p_empty[2] (MMA commit after P_j.Vt_j: P buffer free, and O holds blocks <= j).
+// Every wait is bounded; on timeout the kernel records the error word and winds down.
+constexpr int kFaThreads = 192;
+constexpr int kFaRows = 128;   // queries per CTA
+constexpr int kFaKeys = 128;   // keys per block
+constexpr uint32_t kFaBox = 128 * 128;  // bytes of one 128-row x 128-byte swizzled box
+constexpr float kFaRescaleLog2 = 8.0f;
+
+template <int D>
+struct FaLayout {
+  static constexpr uint32_t kQBytes = kFaRows * D * 2;   // D/64 boxes
+  static constexpr uint32_t kKBytes = kFaKeys * D * 2;   // D/64 boxes
+  static constexpr uint32_t kVBytes = D * kFaKeys * 2;   // 2 boxes of D rows x 64 keys
+  static constexpr uint32_t kVBox = D * 128;             // one D-row x 64-key box
+  static constexpr uint32_t kPBytes = kFaRows * kFaKeys * 2;  // 2 boxes
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK = kQ + kQBytes;
+  static constexpr uint32_t kV = kK + 2 * kKBytes;
+  static constexpr uint32_t kP = kV + 2 * kVBytes;
+  static constexpr uint32_t kBars = kP + 2 * kPBytes;
+  static constexpr uint32_t kSmem = 1024 + kBars + 256;
+  static constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+D)
+};
+
+struct FaParams {
+  int L;
+  int num_kb;             // key blocks of 128
+  float scale_log2;       // log2(e) / sqrt(D)
+  const float* bias_log2; // [num_kb * 128]
+  void* out;
+  long long ldo;
+  int out_bf16;
+  int* err;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  using Ly = FaLayout<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem + Ly::kQ;
+  uint8_t* sK = smem + Ly::kK;
+  uint8_t* sV = smem + Ly::kV;
+  uint8_t* sP = smem + Ly::kP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::kBars);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* v_full = bars + 3;
+  uint64_t* kv_empty = bars + 5;
+  uint64_t* s_full = bars + 7;
+  uint64_t* s_empty = bars + 9;
+  uint64_t* p_full = bars + 11;
+  uint64_t* p_empty = bars + 13;
+  uint64_t* drain_bar = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qtile = blockIdx.x;
+  const int head = blockIdx.y;
+  const int nkb = p.num_kb;
+
+  if (warp == 0 && lane == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_empty[i], 1);
     }
+    mbar_init(drain_bar, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
   }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Ly::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t once = policy_evict_first();
+      const uint64_t shared_kv = policy_evict_last();  // K/V tiles are read by every query tile
+      mbar_arrive_expect_tx(q_full, Ly::kQBytes);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, m, o);
-    const float ol = __shfl_xor_sync(0xffffffffu, l, o);
-    const float nm = fmaxf(m, om);
-    if (nm != -INFINITY) {
-      l = l * __expf(m - nm) + ol * __expf(om - nm);
-      m = nm;
+      for (int c = 0; c < D / 64; ++c) tma_load_3d(sQ + c * kFaBox, &tmQ, q_full, c * 64, qtile * kFaRows, head, once);
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < nkb && ok; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitProducer)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&k_full[st], Ly::kKBytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &k_full[st], c * 64, j * kFaKeys, head, shared_kv);
+        mbar_arrive_expect_tx(&v_full[st], Ly::kVBytes);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(sV + st * Ly::kVBytes + c * Ly::kVBox, &tmV, &v_full[st], j * kFaKeys + c * 64, 0, head,
+                      shared_kv);
+        ++issued;
+      }
+      // Let this thread's copies land before the CTA's shared memory goes away (they have,
+      // unless another role gave up early): Q and the last two stages.
+      mbar_wait_drain(q_full, 0);
+      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
+        mbar_wait_drain(&k_full[j & 1], (j >> 1) & 1);
+        mbar_wait_drain(&v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_make(kFmtBF16, kFaRows, kFaKeys);
+      constexpr uint32_t idesc_o = idesc_make(kFmtBF16, kFaRows, D);
+      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitMma);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1, sb = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1, p.err, kErrWaitMma)) return false;
+        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitMma)) return false;
+        tc_fence_after();
+        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * Ly::kKBytes);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + sb * kFaKeys, smem_desc_k_sw128(q0 + c * kFaBox + k * 32),
+                     smem_desc_k_sw128(k0 + c * kFaBox + k * 32), idesc_s, (c | k) != 0 ? 1u : 0u);
+        umma_commit(&s_full[sb]);
+        return true;
+      };
+      if (ok) {
+        tc_fence_after();
+        ok = issue_s(0);
+      }
+      for (int j = 0; j < nkb && ok; ++j) {
+        if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
+        const int pb = j & 1, st = j & 1;
+        if (!(ok = mbar_wait(&p_full[pb], (j >> 1) & 1, p.err, kErrWaitMma))) break;
+        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1, p.err, kErrWaitMma))) break;
+        tc_fence_after();
+        const uint32_t p0 = smem_u32(sP + pb * Ly::kPBytes), v0 = smem_u32(sV + st * Ly::kVBytes);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_f16(tmem + 2 * kFaKeys, smem_desc_k_sw128(p0 + c * kFaBox + k * 32),
+                     smem_desc_k_sw128(v0 + c * Ly::kVBox + k * 32), idesc_o, (j | c | k) != 0 ? 1u : 0u);
+        umma_commit(&kv_empty[st]);
+        umma_commit(&p_empty[pb]);
+      }
+      if (!ok) {
+        umma_commit(drain_bar);  // MMAs already issued retire before TMEM is released
+        mbar_wait_drain(drain_bar, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax (warps 2..5)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, kErrWaitEpilogue));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + c * 32, r[c]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[sb]);  // the MMA warp may overwrite this S buffer
+
+      const float* bias = p.bias_log2 + j * kFaKeys;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c * 32 + i));
+          const float t0 = fmaf(__uint_as_float(r[c][i]), p.scale_log2, b.x);
+          const float t1 = fmaf(__uint_as_float(r[c][i + 1]), p.scale_log2, b.y);
+          const float t2 = fmaf(__uint_as_float(r[c][i + 2]), p.scale_log2, b.z);
+          const float t3 = fmaf(__uint_as_float(r[c][i + 3]), p.scale_log2, b.w);
+          r[c][i] = __float_as_uint(t0);
+          r[c][i + 1] = __float_as_uint(t1);
+          r[c][i + 2] = __float_as_uint(t2);
+          r[c][i + 3] = __float_as_uint(t3);
+          mx = fmaxf(mx, fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)));
+        }
+      }
+      // Raise the running max only when this block exceeds it by more than a factor 2^8.
+      const bool raise = mx > m_used + kFaRescaleLog2;
+      const float alpha = raise ? fast_exp2(m_used - mx) : 1.f;  // 2^-inf = 0 on the first raise
+      if (raise) m_used = mx;
+      if (__any_sync(0xffffffffu, raise && j > 0)) {
+        // O holds blocks < j: wait for P_{j-1}.Vt_{j-1}, then scale this row of O by alpha.
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, kErrWaitEpilogue));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      l_sum *= alpha;
+      const float m_ref = m_used == -INFINITY ? 0.f : m_used;
+
+      // P_j into shared-memory buffer pb once P_{j-2}.Vt_{j-2} has read it.
+      const int pb = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitEpilogue));
+      if (!ok) break;
+      uint8_t* prow = sP + pb * Ly::kPBytes + row * 128;
+#pragma unroll
+      for (int g = 0; g < 16; ++g) {  // 16-byte groups of 8 keys; box g/8, swizzled chunk g%8
+        const int c = g >> 2, i0 = (g & 3) * 8;
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = fast_exp2(__uint_as_float(r[c][i0 + i]) - m_ref);
+          l_sum += e[i];
+        }
+        uint4 v;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(e[4], e[5]), h3 = __floats2bfloat162_rn(e[6], e[7]);
+        v.x = *reinterpret_cast<uint32_t*>(&h0);
+        v.y = *reinterpret_cast<uint32_t*>(&h1);
+        v.z = *reinterpret_cast<uint32_t*>(&h2);
+        v.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(prow + (g >> 3) * kFaBox + (((g & 7) ^ (row & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[pb]);
+    }
+    if (ok && nkb > 0) {
+      const int jl = nkb - 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jl & 1], (jl >> 1) & 1, p.err, kErrWaitEpilogue));
+      if (ok) {
+        tc_fence_after();
+        const int q = qtile * kFaRows + row;
+        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        const long long col0 = static_cast<long long>(head) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
+          tmem_wait_ld();
+          if (q < p.L) {
+            if (p.out_bf16) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + q * p.ldo + col0 + c * 32);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                __nv_bfloat162 a0 = __floats2bfloat162_rn(__uint_as_float(o[8 * i]) * inv,
+                                                          __uint_as_float(o[8 * i + 1]) * inv);
+                __nv_bfloat162 a1 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2]) * inv,
+                                                          __uint_as_float(o[8 * i + 3]) * inv);
+                __nv_bfloat162 a2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 4]) * inv,
+                                                          __uint_as_float(o[8 * i + 5]) * inv);
+                __nv_bfloat162 a3 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 6]) * inv,
+                                                          __uint_as_float(o[8 * i + 7]) * inv);
+                dst[i] = make_uint4(*reinterpret_cast<uint32_t*>(&a0), *reinterpret_cast<uint32_t*>(&a1),
+                                    *reinterpret_cast<uint32_t*>(&a2), *reinterpret_cast<uint32_t*>(&a3));
+              }
+            } else {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + q * p.ldo + col0 + c * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                     __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+            }
+          }
+        }
+      }
     }
   }
-  const float inv = (l > 0.f) ? 1.f / l : 0.f;
-  __nv_bfloat16* p = P + row * cols;
-  for (int c = lane * 4; c < cols; c += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(s + c);
-    const float a = m == -INFINITY ? 0.f : __expf(v.x - m) * inv;
-    const float b = m == -INFINITY ? 0.f : __expf(v.y - m) * inv;
-    const float cc = m == -INFINITY ? 0.f : __expf(v.z - m) * inv;
-    const float d = m == -INFINITY ? 0.f : __expf(v.w - m) * inv;
-    reinterpret_cast<__nv_bfloat162*>(p + c)[0] = __floats2bfloat162_rn(a, b);
-    reinterpret_cast<__nv_bfloat162*>(p + c)[1] = __floats2bfloat162_rn(cc, d);
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Ly::kTmemCols);
   }
 }
 
-int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+template <int D>
+b2g_status launch_flash(const __nv_bfloat16* qb, const __nv_bfloat16* kb, const __nv_bfloat16* vt, const FaParams& fp,
+                        int64_t L, int64_t H, cudaStream_t st) {
+  CUtensorMap tq, tk, tv;
+  b2g_status s;
+  const int64_t HD = H * D;
+  if ((s = make_operand_map(&tq, qb, B2G_BF16, D, L, HD, H, D, kFaRows)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tk, kb, B2G_BF16, D, L, HD, H, D, kFaKeys)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tv, vt, B2G_BF16, L, D, L, H, D * L, D)) != B2G_OK) return s;
+  constexpr uint32_t smem = FaLayout<D>::kSmem;
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  if ((s = check_cuda(cudaFuncSetAttribute(flash_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem)),
+                      "cudaFuncSetAttribute(flash_attn)")) != B2G_OK)
+    return s;
+  const dim3 grid(static_cast<unsigned>((L + kFaRows - 1) / kFaRows), static_cast<unsigned>(H));
+  flash_attn_kernel<D><<<grid, kFaThreads, smem, st>>>(tq, tk, tv, fp);
+  note_launch();
+  return check_cuda(cudaGetLastError(), "flash_attn launch");
+}
+
 
 }  // namespace
 
 b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   const int64_t L = a.L, H = a.H, D = a.D;
   if (L <= 0 || H <= 0) return B2G_OK;
-  // 16-byte TMA row strides for the bf16 operands (P and Vt rows are L long).
-  if (D % 8 != 0 || L % 8 != 0)
-    return set_error(B2G_ERR_UNSUPPORTED, "attention: head dim and sequence length must be multiples of 8");
+  if (D != 64 && D != 128) return set_error(B2G_ERR_UNSUPPORTED, "attention: head dim must be 64 or 128");
+  // 16-byte TMA row strides for Vt (rows are L long).
+  if (L % 8 != 0) return set_error(B2G_ERR_UNSUPPORTED, "attention: sequence length must be a multiple of 8");
+  if (L > (1ll << 30) || H > 65535) return set_error(B2G_ERR_UNSUPPORTED, "attention: size");
   if (a.out_dtype != B2G_F32 && a.out_dtype != B2G_BF16)
     return set_error(B2G_ERR_UNSUPPORTED, "attention: output must be F32 or BF16");
+  const size_t ob = a.out_dtype == B2G_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(a.out) & 15u) != 0 || (a.ldo * ob) % 16 != 0)
+    return set_error(B2G_ERR_UNSUPPORTED, "attention: output base and row stride must be 16-byte aligned");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
   const int64_t HD = H * D;
+  const int64_t nkb = (L + kFaKeys - 1) / kFaKeys;
   const size_t qk_bytes = static_cast<size_t>(round_up(L * HD * 2, 256));
   const size_t vt_bytes = static_cast<size_t>(round_up(HD * L * 2, 256));
-  const size_t s_bytes = static_cast<size_t>(round_up(H * L * L * 4, 256));
-  const size_t p_bytes = static_cast<size_t>(round_up(H * L * L * 2, 256));
+  const size_t bias_bytes = static_cast<size_t>(round_up(nkb * kFaKeys * 4, 256));
   void* ws = nullptr;
-  b2g_status s = workspace_get(2 * qk_bytes + vt_bytes + s_bytes + p_bytes, &ws, kWsAttention);
-  if (s != B2G_OK) return s;
+  if ((s = workspace_get(2 * qk_bytes + vt_bytes + bias_bytes, &ws, kWsAttention)) != B2G_OK) return s;
   char* base = static_cast<char*>(ws);
   __nv_bfloat16* qb = reinterpret_cast<__nv_bfloat16*>(base);
   __nv_bfloat16* kb = reinterpret_cast<__nv_bfloat16*>(base + qk_bytes);
   __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes);
-  float* S = reinterpret_cast<float*>(base + 2 * qk_bytes + vt_bytes);
-  __nv_bfloat16* P = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes + vt_bytes + s_bytes);
+  float* bias_log2 = reinterpret_cast<float*>(base + 2 * qk_bytes + vt_bytes);
 
   const dim3 nb(32, 8);
   const unsigned nrows = static_cast<unsigned>((L * H + 7) / 8);
@@ -153,31 +474,22 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
                                                 static_cast<int>(D));
   v_to_bf16_t_kernel<<<dim3(static_cast<unsigned>((L + 31) / 32), static_cast<unsigned>((HD + 31) / 32)), dim3(32, 8),
                        0, st>>>(a.v, a.ldv, vt, static_cast<int>(L), static_cast<int>(HD));
-  note_launch(3);
+  const int padded = static_cast<int>(nkb * kFaKeys);
+  key_bias_log2_kernel<<<(padded + 255) / 256, 256, 0, st>>>(a.key_bias, bias_log2, static_cast<int>(L), padded);
+  note_launch(4);
   if ((s = check_cuda(cudaGetLastError(), "attention prologue kernels")) != B2G_OK) return s;
 
-  // S[h] = (1/sqrt(D)) Q_h K_h^T + key_bias
-  GemmProblem g;
-  g.M = L; g.N = L; g.K = D; g.batch = H;
-  g.a = qb; g.a_dtype = B2G_BF16; g.lda = HD; g.a_bstride = D;
-  g.b = kb; g.b_dtype = B2G_BF16; g.ldb = HD; g.b_bstride = D;
-  g.bias = a.key_bias; g.bias_dtype = B2G_F32;
-  g.d = S; g.d_dtype = B2G_F32; g.ldd = L; g.d_bstride = L * L;
-  g.alpha = 1.0f / sqrtf(static_cast<float>(D));
-  if ((s = tc_gemm_launch(g, st)) != B2G_OK) return s;
-
-  const long long rows = H * L;
-  softmax_rows_bf16_kernel<<<static_cast<unsigned>((rows + 7) / 8), nb, 0, st>>>(S, P, rows, static_cast<int>(L));
-  note_launch();
-  if ((s = check_cuda(cudaGetLastError(), "softmax kernel")) != B2G_OK) return s;
-
-  // O[:, h*D:(h+1)*D] = P_h V_h, written in the caller's layout and dtype
-  GemmProblem o;
-  o.M = L; o.N = D; o.K = L; o.batch = H;
-  o.a = P; o.a_dtype = B2G_BF16; o.lda = L; o.a_bstride = L * L;
-  o.b = vt; o.b_dtype = B2G_BF16; o.ldb = L; o.b_bstride = D * L;
-  o.d = a.out; o.d_dtype = a.out_dtype; o.ldd = a.ldo; o.d_bstride = D;
-  return tc_gemm_launch(o, st);
+  FaParams fp{};
+  fp.L = static_cast<int>(L);
+  fp.num_kb = static_cast<int>(nkb);
+  fp.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  fp.bias_log2 = bias_log2;
+  fp.out = a.out;
+  fp.ldo = a.ldo;
+  fp.out_bf16 = a.out_dtype == B2G_BF16 ? 1 : 0;
+  fp.err = dev->err_word;
+  if (D == 128) return launch_flash<128>(qb, kb, vt, fp, L, H, st);
+  return launch_flash<64>(qb, kb, vt, fp, L, H, st);
 }
 
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,

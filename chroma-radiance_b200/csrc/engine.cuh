@@ -1,5 +1,6 @@
 // engine.cuh — internal declarations shared by the engine's translation units.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <string>
@@ -46,6 +47,12 @@ b2g_status workspace_get(size_t bytes, void** ptr, int slot = kWsOperands);
 void workspace_release();
 
 // True if the tensor-core path can run this problem (dtypes, strides, alignment).
+// 3-D TMA map over a K-major bf16/fp16/fp32 operand: dims {K, rows, batch}, row stride ld,
+// batch stride bstride (elements); box = 128 bytes of K x box_rows, 128-byte swizzle, zero
+// fill outside the tensor.  (CUtensorMap from <cuda.h>.)
+b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, int64_t K, int64_t rows, int64_t ld,
+                            int64_t batch, int64_t bstride, uint32_t box_rows);
+
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // One launch over `count` (<= 2) problems that tc_gemm_groupable() accepts pairwise; their

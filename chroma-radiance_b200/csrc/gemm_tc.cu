@@ -795,10 +795,14 @@ b2g_status get_encode() {
   return B2G_OK;
 }
 
+}  // namespace
+
 // 3-D K-major operand map: dims {K, rows, batch}, box {128 bytes of K, box_rows, 1}, 128-byte
 // swizzle, out-of-bounds elements read as zero (so ragged M, N and K tiles need no special case).
 b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, int64_t K, int64_t rows,
                             int64_t ld, int64_t batch, int64_t bstride, uint32_t box_rows) {
+  b2g_status s = get_encode();
+  if (s != B2G_OK) return s;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows),
                               static_cast<cuuint64_t>(batch)};
   const cuuint64_t esz = dt == B2G_F32 ? 4u : 2u;
@@ -814,6 +818,8 @@ b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, in
   if (r != CUDA_SUCCESS) return set_error(B2G_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return B2G_OK;
 }
+
+namespace {
 
 // 3-D output map: dims {N, M, batch}, box {32, 32, 1} (one epilogue warp's chunk), swizzle
 // matching the staging layout (128 B for fp32 rows, 64 B for 16-bit rows).
