@@ -4,12 +4,12 @@
 // (apply_rope_fused_bf16, rope.cuh:180-221), V to bf16, softmax(Q K^T / sqrt(D) + key_bias) V
 // (cuDNN SDPA, cudnn_attention.cuh:408-443), output F32 [L, H*D] (or bf16 for the block path).
 //
-//   1. qknorm_rope_bf16  Q, K F32 rows [L, H*D] -> optional per-head RMSNorm (qk_norm) ->
-//                        RoPE -> bf16 [L, H*D].  The layout is kept: the attention kernel
-//                        reads head h through TMA (row stride H*D, head stride D).
-//   2. v_to_bf16_t       V F32 [L, H*D] -> bf16 [H, D, L] (K-major operand of P.V).
-//   3. key_bias_log2     key mask (0 / -inf) scaled by log2(e), -inf past L, padded to 128.
-//   4. flash_attn        one CTA per (128-query tile, head): S = Q K^T on the tensor cores
+//   1. attn_prep         one launch: Q, K F32 rows [L, H*D] -> optional per-head RMSNorm
+//                        (qk_norm) -> RoPE -> bf16 [L, H*D] (the attention kernel reads head
+//                        h through TMA: row stride H*D, head stride D); V F32 -> bf16
+//                        [H, D, L] (K-major operand of P.V); key mask (0 / -inf) scaled by
+//                        log2(e), -inf past L, padded to a multiple of 128 keys.
+//   2. flash_attn        one CTA per (128-query tile, head): S = Q K^T on the tensor cores
 //                        into TMEM, online softmax in registers, P (bf16) through shared
 //                        memory into O += P V, O / rowsum written to the output layout.
 //                        S never leaves the SM.
@@ -22,67 +22,116 @@ namespace b2g {
 
 namespace {
 
-// Fused Q/K producer: per (token, head) row of D values, RMSNorm with a learned scale
-// (rms_norm, kernels.cu:174-207, as qk_norm applies it, chroma.cuh:513-515), then RoPE,
-// then bf16.  One warp per row; lane i handles rotation pairs i, i+32, ...
-// Rows l >= norm_split use norm2 (the double block's txt and img streams have their own
-// scales); pe row l holds D/2 groups of (cos, -sin, sin, cos), the table gen_pe builds
-// (rope.cuh:84) and apply_rope_fused_bf16 applies (rope.cuh:180-221).
-__global__ void qknorm_rope_bf16_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ norm1,
-                                        const float* __restrict__ norm2, int norm_split, float eps,
-                                        const float* __restrict__ pe, __nv_bfloat16* __restrict__ out, long long ldo,
-                                        int L, int H, int D) {
-  const long long row = blockIdx.x * static_cast<long long>(blockDim.y) + threadIdx.y;
-  if (row >= static_cast<long long>(L) * H) return;
-  const int l = static_cast<int>(row / H), h = static_cast<int>(row % H);
-  const float* norm = l < norm_split ? norm1 : norm2;
-  const float* xr = x + l * ldx + h * D;
-  const int half = D / 2;
-  float ss = 0.f;
-  for (int j = threadIdx.x; j < half; j += 32) {
-    const float2 v = *reinterpret_cast<const float2*>(xr + 2 * j);
-    ss += v.x * v.x + v.y * v.y;
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = norm ? rsqrtf(ss / static_cast<float>(D) + eps) : 1.f;
-  for (int j = threadIdx.x; j < half; j += 32) {
-    float2 v = *reinterpret_cast<const float2*>(xr + 2 * j);
-    if (norm) {
-      v.x = v.x * inv * norm[2 * j];
-      v.y = v.y * inv * norm[2 * j + 1];
-    }
-    const float4 p = *reinterpret_cast<const float4*>(pe + (static_cast<long long>(l) * half + j) * 4);
-    *reinterpret_cast<__nv_bfloat162*>(out + l * ldo + h * D + 2 * j) =
-        __floats2bfloat162_rn(v.x * p.x + v.y * p.y, v.x * p.z + v.y * p.w);
-  }
-}
+// Attention prologue, one launch, work items in three ranges of blocks (256 threads each):
+//   [0, n_rows)            Q then K rows: one warp per (token l, head h) row of D values:
+//                          RMSNorm with a learned scale (rms_norm, kernels.cu:174-207, as
+//                          qk_norm applies it, chroma.cuh:513-515; rows l >= norm_split use the
+//                          second scale set), RoPE with pe row l = D/2 groups of (cos, -sin,
+//                          sin, cos) (the table gen_pe builds, rope.cuh:84, applied as
+//                          apply_rope_fused_bf16 does, rope.cuh:180-221), bf16 out [L, H*D].
+//   [n_rows, +n_vtiles)    V [L, H*D] F32 -> Vt [H*D, L] bf16 through 64x64 smem tiles.
+//   last block             key bias in base-2 exponent units: bias[k]*log2(e) for k < L, -inf
+//                          up to the padded key count (keys past L are TMA zero fill).
+struct PrepArgs {
+  const float* x[2];        // Q, K
+  long long ldx[2];
+  const float* norm1[2];    // may be NULL (no qk_norm)
+  const float* norm2[2];
+  __nv_bfloat16* out[2];    // [L, H*D]
+  int norm_split;
+  float eps;
+  const float* pe;
+  const float* v;
+  long long ldv;
+  __nv_bfloat16* vt;        // [H*D, L]
+  const float* bias;        // may be NULL
+  float* bias_log2;         // [padded]
+  int L, H, padded;
+  int rows_blocks, vt_cols_tiles, vt_blocks;
+};
 
-// V [L, H*D] F32 -> Vt [H, D, L] bf16 through 32x32 shared-memory tiles.
-__global__ void v_to_bf16_t_kernel(const float* __restrict__ v, long long ldv, __nv_bfloat16* __restrict__ vt, int L,
-                                   int HD) {
-  __shared__ float tile[32][33];
-  const int l0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int l = l0 + r, c = c0 + threadIdx.x;
-    tile[r][threadIdx.x] = (l < L && c < HD) ? v[l * ldv + c] : 0.f;
+template <int D>
+__global__ void __launch_bounds__(256) attn_prep_kernel(const PrepArgs a) {
+  constexpr int kPerLane = D / 32;  // 4 (D=128) or 2 (D=64) consecutive values per lane
+  __shared__ float tile[64][65];
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (b < a.rows_blocks) {
+    const long long row = static_cast<long long>(b) * 8 + warp;
+    const long long per = static_cast<long long>(a.L) * a.H;
+    if (row >= 2 * per) return;
+    const int which = row >= per ? 1 : 0;
+    const long long r = row - which * per;
+    const int l = static_cast<int>(r / a.H), h = static_cast<int>(r % a.H);
+    const float* xr = a.x[which] + l * a.ldx[which] + h * D + lane * kPerLane;
+    float v[kPerLane];
+    if constexpr (kPerLane == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(xr);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(xr);
+      v[0] = t.x; v[1] = t.y;
+    }
+    const float* norm = l < a.norm_split ? a.norm1[which] : a.norm2[which];
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) ss += v[i] * v[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = rsqrtf(ss / static_cast<float>(D) + a.eps);
+#pragma unroll
+      for (int i = 0; i < kPerLane; ++i) v[i] = v[i] * inv * __ldg(norm + lane * kPerLane + i);
+    }
+    // pair p = lane*kPerLane/2 + i rotates (v[2i], v[2i+1]) by pe row l, group p.
+    const float4* pe = reinterpret_cast<const float4*>(a.pe) + static_cast<long long>(l) * (D / 2) + lane * kPerLane / 2;
+    uint32_t packed[kPerLane / 2];
+#pragma unroll
+    for (int i = 0; i < kPerLane / 2; ++i) {
+      const float4 c = __ldg(pe + i);
+      __nv_bfloat162 o = __floats2bfloat162_rn(v[2 * i] * c.x + v[2 * i + 1] * c.y, v[2 * i] * c.z + v[2 * i + 1] * c.w);
+      packed[i] = *reinterpret_cast<uint32_t*>(&o);
+    }
+    __nv_bfloat16* dst = a.out[which] + static_cast<long long>(l) * a.H * D + h * D + lane * kPerLane;
+    if constexpr (kPerLane == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+    else *reinterpret_cast<uint32_t*>(dst) = packed[0];
+    return;
   }
-  __syncthreads();
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int c = c0 + r, l = l0 + threadIdx.x;
-    if (c < HD && l < L) vt[static_cast<long long>(c) * L + l] = __float2bfloat16(tile[threadIdx.x][r]);
+  const int vb = b - a.rows_blocks;
+  if (vb < a.vt_blocks) {
+    const int HD = a.H * D;
+    const int l0 = (vb / a.vt_cols_tiles) * 64, c0 = (vb % a.vt_cols_tiles) * 64;
+    // read 64 rows (tokens) x 64 columns (features), float4 per thread, 4 passes of 16 rows
+    const int tc = (threadIdx.x & 15) * 4, tr = threadIdx.x >> 4;
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int rr = pass * 16 + tr, l = l0 + rr;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (l < a.L && c0 + tc < HD) t = *reinterpret_cast<const float4*>(a.v + l * a.ldv + c0 + tc);
+      tile[rr][tc] = t.x;
+      tile[rr][tc + 1] = t.y;
+      tile[rr][tc + 2] = t.z;
+      tile[rr][tc + 3] = t.w;
+    }
+    __syncthreads();
+    // write 64 feature rows x 64 tokens, 4 tokens (8 bytes) per thread, 4 passes of 16 rows
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int cc = pass * 16 + tr, c = c0 + cc, l = l0 + tc;
+      if (c < HD && l < a.L) {
+        __nv_bfloat162 p0 = __floats2bfloat162_rn(tile[tc][cc], tile[tc + 1][cc]);
+        __nv_bfloat162 p1 = __floats2bfloat162_rn(tile[tc + 2][cc], tile[tc + 3][cc]);
+        *reinterpret_cast<uint2*>(a.vt + static_cast<long long>(c) * a.L + l) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
+      }
+    }
+    return;
   }
+  for (int k = threadIdx.x; k < a.padded; k += blockDim.x)
+    a.bias_log2[k] = k < a.L ? (a.bias ? a.bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
-
-// Key bias for the attention kernel in the exponent's base-2 units: out[k] = bias[k] * log2(e)
-// (bias may be NULL = 0) for k < L, -inf for L <= k < padded (keys past L are TMA zero fill).
-__global__ void key_bias_log2_kernel(const float* __restrict__ bias, float* __restrict__ out, int L, int padded) {
-  const int k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= padded) return;
-  out[k] = k < L ? (bias ? bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
-}
 
 // ---------------------------------------------------------------------------- fused attention
 //
@@ -439,8 +488,12 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   const int64_t L = a.L, H = a.H, D = a.D;
   if (L <= 0 || H <= 0) return B2G_OK;
   if (D != 64 && D != 128) return set_error(B2G_ERR_UNSUPPORTED, "attention: head dim must be 64 or 128");
-  // 16-byte TMA row strides for Vt (rows are L long).
+  // 16-byte TMA row strides for Vt (rows are L long); 16-byte row loads of Q, K and V.
   if (L % 8 != 0) return set_error(B2G_ERR_UNSUPPORTED, "attention: sequence length must be a multiple of 8");
+  const uintptr_t qkv_bits = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                             reinterpret_cast<uintptr_t>(a.v);
+  if ((qkv_bits & 15u) != 0 || (a.ldq | a.ldk | a.ldv) % 4 != 0 || (a.pe && (reinterpret_cast<uintptr_t>(a.pe) & 15u)))
+    return set_error(B2G_ERR_UNSUPPORTED, "attention: q, k, v and pe must be 16-byte aligned with row strides % 4 == 0");
   if (L > (1ll << 30) || H > 65535) return set_error(B2G_ERR_UNSUPPORTED, "attention: size");
   if (a.out_dtype != B2G_F32 && a.out_dtype != B2G_BF16)
     return set_error(B2G_ERR_UNSUPPORTED, "attention: output must be F32 or BF16");
@@ -463,21 +516,29 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes);
   float* bias_log2 = reinterpret_cast<float*>(base + 2 * qk_bytes + vt_bytes);
 
-  const dim3 nb(32, 8);
-  const unsigned nrows = static_cast<unsigned>((L * H + 7) / 8);
-  const int split = a.norm_split >= 0 && a.norm_split < L ? static_cast<int>(a.norm_split) : static_cast<int>(L);
-  qknorm_rope_bf16_kernel<<<nrows, nb, 0, st>>>(a.q, a.ldq, a.q_norm, a.q_norm2 ? a.q_norm2 : a.q_norm, split, a.eps,
-                                                a.pe, qb, HD, static_cast<int>(L), static_cast<int>(H),
-                                                static_cast<int>(D));
-  qknorm_rope_bf16_kernel<<<nrows, nb, 0, st>>>(a.k, a.ldk, a.k_norm, a.k_norm2 ? a.k_norm2 : a.k_norm, split, a.eps,
-                                                a.pe, kb, HD, static_cast<int>(L), static_cast<int>(H),
-                                                static_cast<int>(D));
-  v_to_bf16_t_kernel<<<dim3(static_cast<unsigned>((L + 31) / 32), static_cast<unsigned>((HD + 31) / 32)), dim3(32, 8),
-                       0, st>>>(a.v, a.ldv, vt, static_cast<int>(L), static_cast<int>(HD));
-  const int padded = static_cast<int>(nkb * kFaKeys);
-  key_bias_log2_kernel<<<(padded + 255) / 256, 256, 0, st>>>(a.key_bias, bias_log2, static_cast<int>(L), padded);
-  note_launch(4);
-  if ((s = check_cuda(cudaGetLastError(), "attention prologue kernels")) != B2G_OK) return s;
+  // The V tiles write 4 tokens (8 bytes) per thread and read float4 rows.
+  PrepArgs pa{};
+  pa.x[0] = a.q; pa.x[1] = a.k;
+  pa.ldx[0] = a.ldq; pa.ldx[1] = a.ldk;
+  pa.norm1[0] = a.q_norm; pa.norm1[1] = a.k_norm;
+  pa.norm2[0] = a.q_norm2 ? a.q_norm2 : a.q_norm;
+  pa.norm2[1] = a.k_norm2 ? a.k_norm2 : a.k_norm;
+  pa.out[0] = qb; pa.out[1] = kb;
+  pa.norm_split = a.norm_split >= 0 && a.norm_split < L ? static_cast<int>(a.norm_split) : static_cast<int>(L);
+  pa.eps = a.eps;
+  pa.pe = a.pe;
+  pa.v = a.v; pa.ldv = a.ldv; pa.vt = vt;
+  pa.bias = a.key_bias; pa.bias_log2 = bias_log2;
+  pa.L = static_cast<int>(L); pa.H = static_cast<int>(H);
+  pa.padded = static_cast<int>(nkb * kFaKeys);
+  pa.rows_blocks = static_cast<int>((2 * L * H + 7) / 8);
+  pa.vt_cols_tiles = static_cast<int>((HD + 63) / 64);
+  pa.vt_blocks = static_cast<int>((L + 63) / 64) * pa.vt_cols_tiles;
+  const unsigned blocks = static_cast<unsigned>(pa.rows_blocks + pa.vt_blocks + 1);
+  if (D == 128) attn_prep_kernel<128><<<blocks, 256, 0, st>>>(pa);
+  else attn_prep_kernel<64><<<blocks, 256, 0, st>>>(pa);
+  note_launch();
+  if ((s = check_cuda(cudaGetLastError(), "attention prologue kernel")) != B2G_OK) return s;
 
   FaParams fp{};
   fp.L = static_cast<int>(L);
