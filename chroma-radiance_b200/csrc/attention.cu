@@ -23,7 +23,7 @@ namespace b2g {
 namespace {
 
 // Attention prologue, one launch, work items in three ranges of blocks (256 threads each):
-//   [0, n_rows)            Q then K rows: one warp per (token l, head h) row of D values:
+//   [0, n_rows)            Q then K rows: each warp 4 (token l, head h) rows of D values:
 //                          RMSNorm with a learned scale (rms_norm, kernels.cu:174-207, as
 //                          qk_norm applies it, chroma.cuh:513-515; rows l >= norm_split use the
 //                          second scale set), RoPE with pe row l = D/2 groups of (cos, -sin,
@@ -46,55 +46,80 @@ struct PrepArgs {
   __nv_bfloat16* vt;        // [H*D, L]
   const float* bias;        // may be NULL
   float* bias_log2;         // [padded]
+  int* bias_flags;          // [padded / 128]: 1 when any value of the 128-key block is nonzero
   int L, H, padded;
   int rows_blocks, vt_cols_tiles, vt_blocks;
 };
 
+constexpr int kRowsPerWarp = 4;
+
+// kRowsPerWarp Q or K rows (token l, head h) of D values starting at `row0`: RMSNorm, RoPE,
+// bf16 (see attn_prep_kernel).  All rows' loads are issued before any arithmetic.
 template <int D>
-__global__ void __launch_bounds__(256) attn_prep_kernel(const PrepArgs a) {
+__device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int lane) {
   constexpr int kPerLane = D / 32;  // 4 (D=128) or 2 (D=64) consecutive values per lane
-  __shared__ float tile[64][65];
-  const int b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (b < a.rows_blocks) {
-    const long long row = static_cast<long long>(b) * 8 + warp;
-    const long long per = static_cast<long long>(a.L) * a.H;
-    if (row >= 2 * per) return;
-    const int which = row >= per ? 1 : 0;
-    const long long r = row - which * per;
-    const int l = static_cast<int>(r / a.H), h = static_cast<int>(r % a.H);
-    const float* xr = a.x[which] + l * a.ldx[which] + h * D + lane * kPerLane;
-    float v[kPerLane];
+  const long long per = static_cast<long long>(a.L) * a.H;
+  float v[kRowsPerWarp][kPerLane];
+  float4 pe[kRowsPerWarp][kPerLane / 2];
+  int which[kRowsPerWarp], l[kRowsPerWarp], h[kRowsPerWarp];
+#pragma unroll
+  for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+    const long long row = row0 + rr;
+    const bool live = row < 2 * per;
+    which[rr] = row >= per ? 1 : 0;
+    const long long r = live ? row - which[rr] * per : 0;
+    l[rr] = static_cast<int>(r / a.H);
+    h[rr] = static_cast<int>(r % a.H);
+    const float* xr = a.x[which[rr] & 1] + l[rr] * a.ldx[which[rr] & 1] + h[rr] * D + lane * kPerLane;
     if constexpr (kPerLane == 4) {
-      const float4 t = *reinterpret_cast<const float4*>(xr);
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+      const float4 t = live ? *reinterpret_cast<const float4*>(xr) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[rr][0] = t.x; v[rr][1] = t.y; v[rr][2] = t.z; v[rr][3] = t.w;
     } else {
-      const float2 t = *reinterpret_cast<const float2*>(xr);
-      v[0] = t.x; v[1] = t.y;
+      const float2 t = live ? *reinterpret_cast<const float2*>(xr) : make_float2(0.f, 0.f);
+      v[rr][0] = t.x; v[rr][1] = t.y;
     }
-    const float* norm = l < a.norm_split ? a.norm1[which] : a.norm2[which];
+    const float4* pr = reinterpret_cast<const float4*>(a.pe) + static_cast<long long>(l[rr]) * (D / 2) +
+                       lane * kPerLane / 2;
+#pragma unroll
+    for (int i = 0; i < kPerLane / 2; ++i) pe[rr][i] = live ? __ldg(pr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int rr = 0; rr < kRowsPerWarp; ++rr) {
+    if (row0 + rr >= 2 * per) break;
+    const int w = which[rr];
+    const float* norm = l[rr] < a.norm_split ? a.norm1[w] : a.norm2[w];
     if (norm) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < kPerLane; ++i) ss += v[i] * v[i];
+      for (int i = 0; i < kPerLane; ++i) ss += v[rr][i] * v[rr][i];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float inv = rsqrtf(ss / static_cast<float>(D) + a.eps);
 #pragma unroll
-      for (int i = 0; i < kPerLane; ++i) v[i] = v[i] * inv * __ldg(norm + lane * kPerLane + i);
+      for (int i = 0; i < kPerLane; ++i) v[rr][i] = v[rr][i] * inv * __ldg(norm + lane * kPerLane + i);
     }
     // pair p = lane*kPerLane/2 + i rotates (v[2i], v[2i+1]) by pe row l, group p.
-    const float4* pe = reinterpret_cast<const float4*>(a.pe) + static_cast<long long>(l) * (D / 2) + lane * kPerLane / 2;
     uint32_t packed[kPerLane / 2];
 #pragma unroll
     for (int i = 0; i < kPerLane / 2; ++i) {
-      const float4 c = __ldg(pe + i);
-      __nv_bfloat162 o = __floats2bfloat162_rn(v[2 * i] * c.x + v[2 * i + 1] * c.y, v[2 * i] * c.z + v[2 * i + 1] * c.w);
+      const float4 c = pe[rr][i];
+      __nv_bfloat162 o = __floats2bfloat162_rn(v[rr][2 * i] * c.x + v[rr][2 * i + 1] * c.y,
+                                               v[rr][2 * i] * c.z + v[rr][2 * i + 1] * c.w);
       packed[i] = *reinterpret_cast<uint32_t*>(&o);
     }
-    __nv_bfloat16* dst = a.out[which] + static_cast<long long>(l) * a.H * D + h * D + lane * kPerLane;
+    __nv_bfloat16* dst = a.out[w] + static_cast<long long>(l[rr]) * a.H * D + h[rr] * D + lane * kPerLane;
     if constexpr (kPerLane == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
     else *reinterpret_cast<uint32_t*>(dst) = packed[0];
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256, 4) attn_prep_kernel(const PrepArgs a) {
+  __shared__ float tile[64][65];
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (b < a.rows_blocks) {
+    prep_rows<D>(a, (static_cast<long long>(b) * 8 + warp) * kRowsPerWarp, lane);
     return;
   }
   const int vb = b - a.rows_blocks;
@@ -127,33 +152,46 @@ __global__ void __launch_bounds__(256) attn_prep_kernel(const PrepArgs a) {
     }
     return;
   }
-  for (int k = threadIdx.x; k < a.padded; k += blockDim.x)
-    a.bias_log2[k] = k < a.L ? (a.bias ? a.bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
+  for (int k = threadIdx.x; k < a.padded / 128; k += blockDim.x) a.bias_flags[k] = 0;
+  __syncthreads();
+  for (int k = threadIdx.x; k < a.padded; k += blockDim.x) {
+    const float v = k < a.L ? (a.bias ? a.bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
+    a.bias_log2[k] = v;
+    if (v != 0.f) atomicOr(a.bias_flags + k / 128, 1);
+  }
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 // ---------------------------------------------------------------------------- fused attention
 //
-// CTA = (query tile of 128 rows, head h), 192 threads:
-//   warp 0      TMA producer: Q tile once; K tile j [128 keys x D] and Vt tile j [D x 128
-//               keys] into a 2-deep ring (128-byte swizzle, the layout the MMA reads).
-//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=128, K=D) into one of
-//               two TMEM S buffers, then O += P_j Vt_j^T (M=128, N=D, K=128) into TMEM O.
-//               S_{j+1} is issued before P_j is ready, so the tensor core computes the next
-//               scores while the softmax warps work on the current ones.
-//   warps 2-5   softmax, one thread per query row (warp w reads TMEM lanes 32*(w%4)..):
-//               t = S*log2(e)/sqrt(D) + key_bias_log2; running max m (raised only when a
+// CTA = (query tile of 128 rows, head h), 352 threads:
+//   warp 0      TMA: Q tile once, then K tile j [128 keys x D] into a 3-deep ring.
+//   warp 10     TMA: Vt tile j [D x 128 keys] into a 3-deep ring.
+//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=128, K=D; both from
+//               shared memory) into TMEM buffer j%3, then O += P_j Vt_j^T (M=128, N=D, K=128)
+//               with P_j read from TMEM (it overwrites the first 64 columns of S_j as bf16
+//               pairs) and Vt_j from shared memory.  S_{j+2} is issued before P_j is ready, so
+//               the tensor core computes scores ahead while the softmax warps work.
+//   warps 2-9   softmax, two warps per 32-row lane quarter (warp w reads TMEM lanes
+//               32*(w%4)..; warps 2-5 take keys 0-63 of each block, warps 6-9 keys 64-127):
+//               t = S*log2(e)/sqrt(D) + key_bias_log2; the two warps of a row combine their
+//               maxima through shared memory, each rounded to bf16 towards +inf so both get
+//               the same value, never below the true one; running max m (raised only when a
 //               block's max exceeds it by more than 8, i.e. a factor 256, so O in TMEM is
-//               rescaled rarely); P = 2^(t - m) as bf16 into a swizzled shared-memory tile
-//               (double-buffered); l += sum P.  At the end O / l goes to the output.
-// Barriers: q_full; k_full[2], v_full[2] (TMA bytes); kv_empty[2] (MMA commit after P_j.Vt_j);
-// s_full[2] (MMA commit), s_empty[2] (4 softmax warps); p_full[2] (4 softmax warps),
-// p_empty[2] (MMA commit after P_j.Vt_j: P buffer free, and O holds blocks <= j).
+//               rescaled rarely, each warp its half of O's columns); P = 2^(t - m) as bf16
+//               into TMEM with one tcgen05.st per warp; l += sum P.  At the end O / l.
+// Keeping P in TMEM and Q, K, Vt in 3-deep shared-memory rings keeps the shared-memory
+// traffic per block (MMA operand reads + TMA writes) within the SM's bandwidth.
+// Barriers: q_full; k_full[3], v_full[3] (TMA bytes); k_empty[3] (MMA commit after S_j),
+// v_empty[3] (MMA commit after P_j.Vt_j); s_full[3] (MMA commit after S_j); p_full[3]
+// (8 softmax warps: P_j stored); p_empty[3] (MMA commit after P_j.Vt_j: TMEM buffer j%3 free
+// for S_{j+3}, and O holds blocks <= j).
 // Every wait is bounded; on timeout the kernel records the error word and winds down.
-constexpr int kFaThreads = 192;
+constexpr int kFaThreads = 352;
 constexpr int kFaRows = 128;   // queries per CTA
 constexpr int kFaKeys = 128;   // keys per block
+constexpr int kFaStages = 3;   // K and Vt ring depth, and TMEM S/P buffers
 constexpr uint32_t kFaBox = 128 * 128;  // bytes of one 128-row x 128-byte swizzled box
 constexpr float kFaRescaleLog2 = 8.0f;
 
@@ -163,14 +201,14 @@ struct FaLayout {
   static constexpr uint32_t kKBytes = kFaKeys * D * 2;   // D/64 boxes
   static constexpr uint32_t kVBytes = D * kFaKeys * 2;   // 2 boxes of D rows x 64 keys
   static constexpr uint32_t kVBox = D * 128;             // one D-row x 64-key box
-  static constexpr uint32_t kPBytes = kFaRows * kFaKeys * 2;  // 2 boxes
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kK = kQ + kQBytes;
-  static constexpr uint32_t kV = kK + 2 * kKBytes;
-  static constexpr uint32_t kP = kV + 2 * kVBytes;
-  static constexpr uint32_t kBars = kP + 2 * kPBytes;
+  static constexpr uint32_t kV = kK + kFaStages * kKBytes;
+  static constexpr uint32_t kRed = kV + kFaStages * kVBytes;  // uint16 [2 parity][2 half][128 rows]
+  static constexpr uint32_t kBars = kRed + 2 * 2 * kFaRows * 2;
   static constexpr uint32_t kSmem = 1024 + kBars + 256;
-  static constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+D)
+  static constexpr uint32_t kO = kFaStages * kFaKeys;   // TMEM: S/P buffers [0, 384), O [384, 384+D)
+  static constexpr uint32_t kTmemCols = 512;
 };
 
 struct FaParams {
@@ -178,6 +216,7 @@ struct FaParams {
   int num_kb;             // key blocks of 128
   float scale_log2;       // log2(e) / sqrt(D)
   const float* bias_log2; // [num_kb * 128]
+  const int* bias_flags;  // [num_kb]: 0 when the block's 128 bias values are all zero
   void* out;
   long long ldo;
   int out_bf16;
@@ -189,23 +228,24 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const FaParams p) {
   using Ly = FaLayout<D>;
+  constexpr int S3 = kFaStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Ly::kQ;
   uint8_t* sK = smem + Ly::kK;
   uint8_t* sV = smem + Ly::kV;
-  uint8_t* sP = smem + Ly::kP;
+  uint16_t* red = reinterpret_cast<uint16_t*>(smem + Ly::kRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::kBars);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 3;
-  uint64_t* kv_empty = bars + 5;
-  uint64_t* s_full = bars + 7;
-  uint64_t* s_empty = bars + 9;
-  uint64_t* p_full = bars + 11;
-  uint64_t* p_empty = bars + 13;
-  uint64_t* drain_bar = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* v_full = k_full + S3;
+  uint64_t* k_empty = v_full + S3;
+  uint64_t* v_empty = k_empty + S3;
+  uint64_t* s_full = v_empty + S3;
+  uint64_t* p_full = s_full + S3;
+  uint64_t* p_empty = p_full + S3;
+  uint64_t* drain_bar = p_empty + S3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -215,13 +255,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < S3; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(drain_bar, 1);
@@ -239,40 +279,42 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 10) {
+    // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
-      const uint64_t once = policy_evict_first();
+      const bool is_k = warp == 0;
       const uint64_t shared_kv = policy_evict_last();  // K/V tiles are read by every query tile
-      mbar_arrive_expect_tx(q_full, Ly::kQBytes);
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_3d(sQ + c * kFaBox, &tmQ, q_full, c * 64, qtile * kFaRows, head, once);
-      int issued = 0;
-      bool ok = true;
-      for (int j = 0; j < nkb && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitProducer)) {
-          ok = false;
-          break;
-        }
-        mbar_arrive_expect_tx(&k_full[st], Ly::kKBytes);
+      uint64_t* full = is_k ? k_full : v_full;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      if (is_k) {
+        mbar_arrive_expect_tx(q_full, Ly::kQBytes);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &k_full[st], c * 64, j * kFaKeys, head, shared_kv);
-        mbar_arrive_expect_tx(&v_full[st], Ly::kVBytes);
+          tma_load_3d(sQ + c * kFaBox, &tmQ, q_full, c * 64, qtile * kFaRows, head, policy_evict_first());
+      }
+      int issued = 0;
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % S3;
+        if (!mbar_wait(&empty[st], ((j / S3) & 1) ^ 1u, p.err, kErrWaitProducer)) break;
+        if (is_k) {
+          mbar_arrive_expect_tx(&full[st], Ly::kKBytes);
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-          tma_load_3d(sV + st * Ly::kVBytes + c * Ly::kVBox, &tmV, &v_full[st], j * kFaKeys + c * 64, 0, head,
-                      shared_kv);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, j * kFaKeys, head, shared_kv);
+        } else {
+          mbar_arrive_expect_tx(&full[st], Ly::kVBytes);
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            tma_load_3d(sV + st * Ly::kVBytes + c * Ly::kVBox, &tmV, &full[st], j * kFaKeys + c * 64, 0, head,
+                        shared_kv);
+        }
         ++issued;
       }
       // Let this thread's copies land before the CTA's shared memory goes away (they have,
-      // unless another role gave up early): Q and the last two stages.
-      mbar_wait_drain(q_full, 0);
-      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
-        mbar_wait_drain(&k_full[j & 1], (j >> 1) & 1);
-        mbar_wait_drain(&v_full[j & 1], (j >> 1) & 1);
-      }
+      // unless another role gave up early).
+      if (is_k) mbar_wait_drain(q_full, 0);
+      for (int j = issued - S3 < 0 ? 0 : issued - S3; j < issued; ++j)
+        mbar_wait_drain(&full[j % S3], (j / S3) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -281,9 +323,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       constexpr uint32_t idesc_o = idesc_make(kFmtBF16, kFaRows, D);
       bool ok = mbar_wait(q_full, 0, p.err, kErrWaitMma);
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1, sb = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, p.err, kErrWaitMma)) return false;
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitMma)) return false;
+        const int st = j % S3, sb = j % S3;
+        if (!mbar_wait(&k_full[st], (j / S3) & 1, p.err, kErrWaitMma)) return false;
+        // TMEM buffer sb was last used by P_{j-3}.Vt_{j-3}
+        if (!mbar_wait(&p_empty[sb], ((j / S3) & 1) ^ 1u, p.err, kErrWaitMma)) return false;
         tc_fence_after();
         const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * Ly::kKBytes);
 #pragma unroll
@@ -293,26 +336,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             umma_f16(tmem + sb * kFaKeys, smem_desc_k_sw128(q0 + c * kFaBox + k * 32),
                      smem_desc_k_sw128(k0 + c * kFaBox + k * 32), idesc_s, (c | k) != 0 ? 1u : 0u);
         umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);  // K_j read: the producer may load K_{j+3}
         return true;
       };
       if (ok) {
         tc_fence_after();
         ok = issue_s(0);
+        if (ok && nkb > 1) ok = issue_s(1);
       }
       for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 1 < nkb && !(ok = issue_s(j + 1))) break;
-        const int pb = j & 1, st = j & 1;
-        if (!(ok = mbar_wait(&p_full[pb], (j >> 1) & 1, p.err, kErrWaitMma))) break;
-        if (!(ok = mbar_wait(&v_full[st], (j >> 1) & 1, p.err, kErrWaitMma))) break;
+        if (j + 2 < nkb && !(ok = issue_s(j + 2))) break;
+        const int pb = j % S3, st = j % S3;
+        if (!(ok = mbar_wait(&p_full[pb], (j / S3) & 1, p.err, kErrWaitMma))) break;
+        if (!(ok = mbar_wait(&v_full[st], (j / S3) & 1, p.err, kErrWaitMma))) break;
         tc_fence_after();
-        const uint32_t p0 = smem_u32(sP + pb * Ly::kPBytes), v0 = smem_u32(sV + st * Ly::kVBytes);
+        const uint32_t v0 = smem_u32(sV + st * Ly::kVBytes);
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_f16(tmem + 2 * kFaKeys, smem_desc_k_sw128(p0 + c * kFaBox + k * 32),
-                     smem_desc_k_sw128(v0 + c * Ly::kVBox + k * 32), idesc_o, (j | c | k) != 0 ? 1u : 0u);
-        umma_commit(&kv_empty[st]);
+        for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., Vt box k/4, 32-byte step k%4
+          umma_f16_ts(tmem + Ly::kO, tmem + pb * kFaKeys + 8 * k,
+                      smem_desc_k_sw128(v0 + (k >> 2) * Ly::kVBox + (k & 3) * 32), idesc_o,
+                      (j | k) != 0 ? 1u : 0u);
+        umma_commit(&v_empty[st]);
         umma_commit(&p_empty[pb]);
       }
       if (!ok) {
@@ -321,131 +365,162 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax (warps 2..5)
+    // ------------------------------------------------------------ softmax (warps 2..9)
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;         // which 64 keys of each block, which half of O
     const int row = quarter * 32 + lane;
+    const uint32_t bar_id = 1 + quarter;      // the two warps of this row group (64 threads)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    float m_used = -INFINITY, l_sum = 0.f;
-    bool ok = true;
+    constexpr int kOHalf = D / 2;             // O columns per warp
+    float m_used = -INFINITY, l_part = 0.f;
+    bool good = true;
     for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, kErrWaitEpilogue));
-      if (!ok) break;
+      const int sb = j % S3;
+      const bool biased = __ldg(p.bias_flags + j) != 0;  // issued before the wait hides its latency
+      good = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j / S3) & 1, p.err, kErrWaitEpilogue)) && good;
       tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + c * 32, r[c]);
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + half * 64, r[0]);
+      tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + half * 64 + 32, r[1]);
       tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sb]);  // the MMA warp may overwrite this S buffer
 
-      const float* bias = p.bias_log2 + j * kFaKeys;
-      float mx = -INFINITY;
+      // u = raw score (unmasked block: p = 2^(u*scale - m)) or scaled score + bias (p = 2^(u - m))
+      const float ua = biased ? 1.f : p.scale_log2;
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent max chains
+      if (biased) {
+        const float* bias = p.bias_log2 + j * kFaKeys + half * 64;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + c * 32 + i));
-          const float t0 = fmaf(__uint_as_float(r[c][i]), p.scale_log2, b.x);
-          const float t1 = fmaf(__uint_as_float(r[c][i + 1]), p.scale_log2, b.y);
-          const float t2 = fmaf(__uint_as_float(r[c][i + 2]), p.scale_log2, b.z);
-          const float t3 = fmaf(__uint_as_float(r[c][i + 3]), p.scale_log2, b.w);
-          r[c][i] = __float_as_uint(t0);
-          r[c][i + 1] = __float_as_uint(t1);
-          r[c][i + 2] = __float_as_uint(t2);
-          r[c][i + 3] = __float_as_uint(t3);
-          mx = fmaxf(mx, fmaxf(fmaxf(t0, t1), fmaxf(t2, t3)));
-        }
+          for (int i = 0; i < 32; i += 4) {
+            const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + c * 32 + i));
+            const float t0 = fmaf(__uint_as_float(r[c][i]), p.scale_log2, bb.x);
+            const float t1 = fmaf(__uint_as_float(r[c][i + 1]), p.scale_log2, bb.y);
+            const float t2 = fmaf(__uint_as_float(r[c][i + 2]), p.scale_log2, bb.z);
+            const float t3 = fmaf(__uint_as_float(r[c][i + 3]), p.scale_log2, bb.w);
+            r[c][i] = __float_as_uint(t0);
+            r[c][i + 1] = __float_as_uint(t1);
+            r[c][i + 2] = __float_as_uint(t2);
+            r[c][i + 3] = __float_as_uint(t3);
+            mx4[0] = fmaxf(mx4[0], t0);
+            mx4[1] = fmaxf(mx4[1], t1);
+            mx4[2] = fmaxf(mx4[2], t2);
+            mx4[3] = fmaxf(mx4[3], t3);
+          }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mx4[0] = fmaxf(mx4[0], __uint_as_float(r[c][i]));
+            mx4[1] = fmaxf(mx4[1], __uint_as_float(r[c][i + 1]));
+            mx4[2] = fmaxf(mx4[2], __uint_as_float(r[c][i + 2]));
+            mx4[3] = fmaxf(mx4[3], __uint_as_float(r[c][i + 3]));
+          }
       }
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      if (!biased) mx *= p.scale_log2;  // scale > 0: the max commutes with it
+      // Row max over both halves of the block, each half rounded to bf16 towards +inf (the
+      // same value in both warps, never below the true max).  The AND of `good` gives both
+      // warps of the row group one decision to stop (neither can then wait alone here).  The
+      // barrier also orders both warps' S loads before either overwrites columns with P.
+      uint32_t mb = __float_as_uint(mx);
+      if (!(mb & 0x80000000u)) mb += 0xFFFFu;
+      mb >>= 16;
+      red[(j & 1) * 256 + half * 128 + row] = static_cast<uint16_t>(mb);
+      tc_fence_before();
+      if (!named_bar_all(bar_id, 64, good)) break;
+      tc_fence_after();
+      const uint32_t ob = red[(j & 1) * 256 + (1 - half) * 128 + row];
+      mx = fmaxf(__uint_as_float(mb << 16), __uint_as_float(ob << 16));
+
       // Raise the running max only when this block exceeds it by more than a factor 2^8.
       const bool raise = mx > m_used + kFaRescaleLog2;
       const float alpha = raise ? fast_exp2(m_used - mx) : 1.f;  // 2^-inf = 0 on the first raise
       if (raise) m_used = mx;
       if (__any_sync(0xffffffffu, raise && j > 0)) {
-        // O holds blocks < j: wait for P_{j-1}.Vt_{j-1}, then scale this row of O by alpha.
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(&p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err, kErrWaitEpilogue));
-        if (!ok) break;
-        tc_fence_after();
+        // O holds blocks < j: wait for P_{j-1}.Vt_{j-1}, then scale this warp's half of the row.
+        const int jp = j - 1;
+        good = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp % S3], (jp / S3) & 1, p.err, kErrWaitEpilogue)) && good;
+        if (good) {
+          tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
-          tmem_wait_ld();
+          for (int c = 0; c < kOHalf / 32; ++c) {
+            uint32_t o[32];
+            const uint32_t oaddr = lane_base + Ly::kO + half * kOHalf + c * 32;
+            tmem_ld_32x32b_x32(oaddr, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(oaddr, o);
+          }
         }
-        tmem_wait_st();
       }
-      l_sum *= alpha;
-      const float m_ref = m_used == -INFINITY ? 0.f : m_used;
+      l_part *= alpha;
+      if (!good) continue;  // stop feeding the MMA warp; the next barrier ends the loop
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
 
-      // P_j into shared-memory buffer pb once P_{j-2}.Vt_{j-2} has read it.
-      const int pb = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1u, p.err, kErrWaitEpilogue));
-      if (!ok) break;
-      uint8_t* prow = sP + pb * Ly::kPBytes + row * 128;
+      // P_j: this warp's 64 keys as 32 columns of bf16 pairs over S_j's columns [half*32, +32).
+      uint32_t pk[32];
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent sum chains
 #pragma unroll
-      for (int g = 0; g < 16; ++g) {  // 16-byte groups of 8 keys; box g/8, swizzled chunk g%8
-        const int c = g >> 2, i0 = (g & 3) * 8;
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = fast_exp2(__uint_as_float(r[c][i0 + i]) - m_ref);
-          l_sum += e[i];
-        }
-        uint4 v;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(e[0], e[1]), h1 = __floats2bfloat162_rn(e[2], e[3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(e[4], e[5]), h3 = __floats2bfloat162_rn(e[6], e[7]);
-        v.x = *reinterpret_cast<uint32_t*>(&h0);
-        v.y = *reinterpret_cast<uint32_t*>(&h1);
-        v.z = *reinterpret_cast<uint32_t*>(&h2);
-        v.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(prow + (g >> 3) * kFaBox + (((g & 7) ^ (row & 7)) << 4)) = v;
+      for (int i = 0; i < 64; i += 2) {
+        const float e0 = fast_exp2(fmaf(__uint_as_float(r[i >> 5][i & 31]), ua, neg_m));
+        const float e1 = fast_exp2(fmaf(__uint_as_float(r[i >> 5][(i & 31) + 1]), ua, neg_m));
+        ls[(i >> 1) & 7] += e0 + e1;
+        __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
+        pk[i >> 1] = *reinterpret_cast<uint32_t*>(&h);
       }
-      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core's reads
+      tmem_st_32x32b_x32(lane_base + sb * kFaKeys + half * 32, pk);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[pb]);
+      if (lane == 0) mbar_arrive(&p_full[sb]);
+      l_part += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
     }
-    if (ok && nkb > 0) {
-      const int jl = nkb - 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[jl & 1], (jl >> 1) & 1, p.err, kErrWaitEpilogue));
-      if (ok) {
-        tc_fence_after();
-        const int q = qtile * kFaRows + row;
-        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-        const long long col0 = static_cast<long long>(head) * D;
+    // Final: wait for the last P.Vt, combine the two halves' row sums, write O / l.
+    const int jl = nkb - 1;
+    if (good)
+      good = __all_sync(0xffffffffu, mbar_wait(&p_empty[jl % S3], (jl / S3) & 1, p.err, kErrWaitEpilogue));
+    // Row sums meet in the Vt stages, dead once the last P.Vt has retired (when good).
+    float* lsum = reinterpret_cast<float*>(sV);
+    if (good) {
+      fence_proxy_async_smem();
+      lsum[half * 128 + row] = l_part;
+    }
+    if (named_bar_all(bar_id, 64, good)) {
+      tc_fence_after();
+      const float l_sum = l_part + lsum[(1 - half) * 128 + row];
+      const int q = qtile * kFaRows + row;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const long long col0 = static_cast<long long>(head) * D + half * kOHalf;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(lane_base + 2 * kFaKeys + c * 32, o);
-          tmem_wait_ld();
-          if (q < p.L) {
-            if (p.out_bf16) {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + q * p.ldo + col0 + c * 32);
+      for (int c = 0; c < kOHalf / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(lane_base + Ly::kO + half * kOHalf + c * 32, o);
+        tmem_wait_ld();
+        if (q < p.L) {
+          if (p.out_bf16) {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + q * p.ldo + col0 + c * 32);
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                __nv_bfloat162 a0 = __floats2bfloat162_rn(__uint_as_float(o[8 * i]) * inv,
-                                                          __uint_as_float(o[8 * i + 1]) * inv);
-                __nv_bfloat162 a1 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2]) * inv,
-                                                          __uint_as_float(o[8 * i + 3]) * inv);
-                __nv_bfloat162 a2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 4]) * inv,
-                                                          __uint_as_float(o[8 * i + 5]) * inv);
-                __nv_bfloat162 a3 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 6]) * inv,
-                                                          __uint_as_float(o[8 * i + 7]) * inv);
-                dst[i] = make_uint4(*reinterpret_cast<uint32_t*>(&a0), *reinterpret_cast<uint32_t*>(&a1),
-                                    *reinterpret_cast<uint32_t*>(&a2), *reinterpret_cast<uint32_t*>(&a3));
-              }
-            } else {
-              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + q * p.ldo + col0 + c * 32);
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
-                                     __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+            for (int i = 0; i < 4; ++i) {
+              __nv_bfloat162 a0 = __floats2bfloat162_rn(__uint_as_float(o[8 * i]) * inv,
+                                                        __uint_as_float(o[8 * i + 1]) * inv);
+              __nv_bfloat162 a1 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 2]) * inv,
+                                                        __uint_as_float(o[8 * i + 3]) * inv);
+              __nv_bfloat162 a2 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 4]) * inv,
+                                                        __uint_as_float(o[8 * i + 5]) * inv);
+              __nv_bfloat162 a3 = __floats2bfloat162_rn(__uint_as_float(o[8 * i + 6]) * inv,
+                                                        __uint_as_float(o[8 * i + 7]) * inv);
+              dst[i] = make_uint4(*reinterpret_cast<uint32_t*>(&a0), *reinterpret_cast<uint32_t*>(&a1),
+                                  *reinterpret_cast<uint32_t*>(&a2), *reinterpret_cast<uint32_t*>(&a3));
             }
+          } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + q * p.ldo + col0 + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                                   __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
           }
         }
       }
@@ -508,13 +583,15 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   const size_t qk_bytes = static_cast<size_t>(round_up(L * HD * 2, 256));
   const size_t vt_bytes = static_cast<size_t>(round_up(HD * L * 2, 256));
   const size_t bias_bytes = static_cast<size_t>(round_up(nkb * kFaKeys * 4, 256));
+  const size_t flag_bytes = static_cast<size_t>(round_up(nkb * 4, 256));
   void* ws = nullptr;
-  if ((s = workspace_get(2 * qk_bytes + vt_bytes + bias_bytes, &ws, kWsAttention)) != B2G_OK) return s;
+  if ((s = workspace_get(2 * qk_bytes + vt_bytes + bias_bytes + flag_bytes, &ws, kWsAttention)) != B2G_OK) return s;
   char* base = static_cast<char*>(ws);
   __nv_bfloat16* qb = reinterpret_cast<__nv_bfloat16*>(base);
   __nv_bfloat16* kb = reinterpret_cast<__nv_bfloat16*>(base + qk_bytes);
   __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes);
   float* bias_log2 = reinterpret_cast<float*>(base + 2 * qk_bytes + vt_bytes);
+  int* bias_flags = reinterpret_cast<int*>(base + 2 * qk_bytes + vt_bytes + bias_bytes);
 
   // The V tiles write 4 tokens (8 bytes) per thread and read float4 rows.
   PrepArgs pa{};
@@ -528,10 +605,10 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   pa.eps = a.eps;
   pa.pe = a.pe;
   pa.v = a.v; pa.ldv = a.ldv; pa.vt = vt;
-  pa.bias = a.key_bias; pa.bias_log2 = bias_log2;
+  pa.bias = a.key_bias; pa.bias_log2 = bias_log2; pa.bias_flags = bias_flags;
   pa.L = static_cast<int>(L); pa.H = static_cast<int>(H);
   pa.padded = static_cast<int>(nkb * kFaKeys);
-  pa.rows_blocks = static_cast<int>((2 * L * H + 7) / 8);
+  pa.rows_blocks = static_cast<int>((2 * L * H + 8 * kRowsPerWarp - 1) / (8 * kRowsPerWarp));
   pa.vt_cols_tiles = static_cast<int>((HD + 63) / 64);
   pa.vt_blocks = static_cast<int>((L + 63) / 64) * pa.vt_cols_tiles;
   const unsigned blocks = static_cast<unsigned>(pa.rows_blocks + pa.vt_blocks + 1);
@@ -545,6 +622,7 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   fp.num_kb = static_cast<int>(nkb);
   fp.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   fp.bias_log2 = bias_log2;
+  fp.bias_flags = bias_flags;
   fp.out = a.out;
   fp.ldo = a.ldo;
   fp.out_bf16 = a.out_dtype == B2G_BF16 ? 1 : 0;
