@@ -64,6 +64,10 @@ _SIGNATURES = {
     "b2g_version": ([], ctypes.c_char_p),
     "b2g_gemm": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p], ctypes.c_int),
     "b2g_gemm_group": ([ctypes.POINTER(GemmDesc), ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
+    "b2g_quantize_e4m3": ([ctypes.c_void_p, ctypes.c_int] + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int64,
+                                                                                   ctypes.c_void_p, ctypes.c_void_p],
+                          ctypes.c_int),
+    "b2g_gemm_fp8": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt_stream": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -199,6 +203,58 @@ def gemm_group(problems: list[dict], stream: torch.cuda.Stream | None = None) ->
     s = (stream or torch.cuda.current_stream(dev)).cuda_stream
     _check(lib.b2g_gemm_group(arr, len(descs), ctypes.c_void_p(s)))
     return outs
+
+
+def quantize_e4m3(x: torch.Tensor, stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row E4M3 quantisation of a 2-D F32/BF16/F16 CUDA tensor: (codes uint8 [rows, cols],
+    scales f32 [rows]) with scales = absmax/448 and codes = E4M3(x * 448/absmax)."""
+    lib = load()
+    _require_cuda(x)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise B2GError("quantize_e4m3: 2-D tensor with unit column stride expected")
+    rows, cols = x.shape
+    q = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
+    sc = torch.empty(rows, dtype=torch.float32, device=x.device)
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_quantize_e4m3(x.data_ptr(), _TORCH_TO_B2G[x.dtype], rows, cols, x.stride(0) if rows > 1 else cols,
+                                 q.data_ptr(), cols, sc.data_ptr(), ctypes.c_void_p(s)))
+    return q, sc
+
+
+def gemm_fp8(x: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor, bias: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, out_dtype: torch.dtype | None = None, epilogue: str = "none",
+             gate: torch.Tensor | None = None, x_scale: torch.Tensor | None = None,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """FP8 linear: out = epilogue((x . wq^T) * x_scale[m] * w_scale[n] + bias).
+
+    wq: uint8 E4M3 codes [N, K] from quantize_e4m3 (w_scale its scales).  x: uint8 E4M3 codes
+    with x_scale, or F32/BF16/F16 activations that the library quantises per token."""
+    lib = load()
+    _require_cuda(x, wq, w_scale, bias, out, gate, x_scale)
+    if x.dim() != 2 or wq.dim() != 2 or x.stride(1) != 1 or wq.stride(1) != 1 or wq.dtype != torch.uint8:
+        raise B2GError("gemm_fp8: 2-D x and uint8 wq with unit stride along K expected")
+    M, K = x.shape
+    N = wq.shape[0]
+    if wq.shape[1] != K:
+        raise B2GError("gemm_fp8: K mismatch")
+    epi = _EPILOGUES[epilogue]
+    if out is None:
+        if epi == EPI_GATED_RESIDUAL:
+            raise B2GError("gemm_fp8: gated_residual needs `out` (the residual)")
+        out = torch.empty((M, N), device=x.device, dtype=out_dtype or torch.float32)
+    d = GemmDesc()
+    d.M, d.N, d.K = M, N, K
+    d.a, d.lda = x.data_ptr(), x.stride(0) if M > 1 else K
+    d.a_dtype = E4M3 if x.dtype == torch.uint8 else _TORCH_TO_B2G[x.dtype]
+    d.b, d.b_dtype, d.ldb = wq.data_ptr(), E4M3, wq.stride(0) if N > 1 else K
+    d.bias = _ptr(bias)
+    d.bias_dtype = _TORCH_TO_B2G[bias.dtype] if bias is not None else F32
+    d.d, d.d_dtype, d.ldd = out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0) if M > 1 else N
+    d.epilogue = epi
+    d.gate = _ptr(gate)
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_gemm_fp8(ctypes.byref(d), _ptr(x_scale), w_scale.data_ptr(), ctypes.c_void_p(s)))
+    return out
 
 
 def linear_lt(M: int, K: int, N: int, x: torch.Tensor, x_type: int, w: torch.Tensor, w_type: int,

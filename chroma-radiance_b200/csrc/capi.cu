@@ -259,6 +259,65 @@ b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
   return B2G_OK;
 }
 
+b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
+                             uint8_t* dst, int64_t dst_ld, float* scales, void* stream) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return quantize_rows_e4m3(src, src_dtype, rows, cols, ld, dst, dst_ld, scales, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_gemm_fp8(const b2g_gemm_desc* d, const float* a_scale, const float* b_scale, void* stream) {
+  if (!d) return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: null descriptor");
+  if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: negative size");
+  if (d->M == 0 || d->N == 0) return B2G_OK;
+  if (d->K == 0) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_fp8: K must be positive");
+  if (!d->a || !d->b || !d->d) return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: null operand");
+  if (d->lda < d->K || d->ldb < d->K || d->ldd < d->N) return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: lda/ldb/ldd");
+  if (d->b_dtype != B2G_E4M3 || !b_scale)
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: weights must be E4M3 with per-row scales");
+  if (d->a_dtype == B2G_E4M3 && !a_scale)
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: E4M3 activations need per-row scales");
+  if (d->a_dtype != B2G_E4M3 && d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16 && d->a_dtype != B2G_F32)
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_fp8: activations must be E4M3, BF16, F16 or F32");
+  if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_GATED_RESIDUAL)
+    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_fp8: unknown epilogue");
+  if (d->epilogue == B2G_EPI_GATED_RESIDUAL && (!d->gate || d->d_dtype != B2G_F32))
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8: gated residual needs a gate and an F32 output");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GemmProblem p;
+  p.M = d->M; p.N = d->N; p.K = d->K;
+  p.a = d->a; p.a_dtype = d->a_dtype; p.lda = d->lda;
+  p.b = d->b; p.b_dtype = B2G_E4M3; p.ldb = d->ldb;
+  p.bias = d->bias; p.bias_dtype = d->bias_dtype;
+  p.d = d->d; p.d_dtype = d->d_dtype; p.ldd = d->ldd;
+  p.epilogue = d->epilogue;
+  p.gate = d->gate;
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  if (p.a_dtype != B2G_E4M3) {
+    // Per-token quantisation of the activations into the workspace: [M, round_up(K, 16)]
+    // E4M3 rows (16-byte TMA rows) followed by M fp32 scales.
+    const int64_t kp = round_up(p.K, 16);
+    const size_t q_bytes = static_cast<size_t>(round_up(p.M * kp, 256));
+    void* ws = nullptr;
+    if ((s = workspace_get(q_bytes + static_cast<size_t>(p.M) * 4, &ws)) != B2G_OK) return s;
+    uint8_t* q = static_cast<uint8_t*>(ws);
+    float* qs = reinterpret_cast<float*>(q + q_bytes);
+    if ((s = quantize_rows_e4m3(p.a, p.a_dtype, p.M, p.K, p.lda, q, kp, qs, st)) != B2G_OK) return s;
+    p.a = q;
+    p.a_dtype = B2G_E4M3;
+    p.lda = kp;
+    p.a_scale = qs;
+  }
+  std::string why;
+  if (!tc_gemm_supported(p, &why)) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_fp8: " + why);
+  return tc_gemm_launch(p, st);
+}
+
 b2g_status b2g_linear_lt_stream(int64_t M, int64_t K, int64_t N, const void* x_data, cudaDataType_t x_type,
                                 const void* w_data, cudaDataType_t w_type, const void* bias_data, void* out_data,
                                 void* stream) {

@@ -21,6 +21,9 @@ struct GemmProblem {
   bool allow_tf32 = false;  // F32 x F32 may run as TF32 products (batched_matmul_Bt only)
   float alpha = 1.0f;       // D = epilogue(alpha * A.B^T + bias); internal (attention scores)
   bool allow_split = true;  // false: never split K (split-K needs workspace; b2g_gemm_noalloc)
+  // E4M3 operands: D = (sum_k A.B) * a_scale[m] * b_scale[n] + bias, before the epilogue.
+  const float* a_scale = nullptr;
+  const float* b_scale = nullptr;
 };
 
 // Records a message for b2g_last_error() and returns `st`.
@@ -52,6 +55,11 @@ void workspace_release();
 // fill outside the tensor.  (CUtensorMap from <cuda.h>.)
 b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, int64_t K, int64_t rows, int64_t ld,
                             int64_t batch, int64_t bstride, uint32_t box_rows);
+
+// Per-row E4M3 quantisation (fp8.cu): scales[r] = absmax_r / 448 (1 for a zero row),
+// dst[r, c] = E4M3(src[r, c] * 448 / absmax_r), round to nearest even, saturating.
+b2g_status quantize_rows_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
+                              uint8_t* dst, int64_t dst_ld, float* scales, cudaStream_t st);
 
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);

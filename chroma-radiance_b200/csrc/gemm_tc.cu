@@ -46,9 +46,10 @@ constexpr int kBK = 64;          // 64 x 2 B = one 128-byte swizzle row (16-bit 
 constexpr int kThreads = 320;    // producer, MMA, 8 epilogue warps
 constexpr int kEpiThreads = 256;
 constexpr int kEpiWarps = 8;
-// K elements per 128-byte stage row: 64 for bf16/fp16 (KIND 0), 32 for tf32 (KIND 1).
+// K elements per 128-byte stage row: 64 for bf16/fp16 (KIND 0), 32 for tf32 (KIND 1), 128
+// for E4M3 (KIND 2, kind::f8f6f4).
 template <int KIND>
-constexpr int kKElems = KIND == 1 ? 32 : 64;
+constexpr int kKElems = KIND == 1 ? 32 : (KIND == 2 ? 128 : 64);
 enum { OUT_F32 = 0, OUT_BF16 = 1, OUT_F16 = 2 };
 
 // Output staging: one 4 KB buffer per epilogue warp (32 rows x 32 fp32 or 16-bit columns),
@@ -56,6 +57,9 @@ enum { OUT_F32 = 0, OUT_BF16 = 1, OUT_F16 = 2 };
 constexpr int kOutBufBytes = 4096;
 constexpr int kOutStageBytes = kEpiWarps * kOutBufBytes;  // 32 KB
 constexpr int kBiasBytes = 256 * 4;                       // bias of one tile (<= 256 columns)
+// E4M3 kernels also stage the tile's per-column weight scales (same size as the bias).
+template <int KIND>
+constexpr int kScaleBytes = KIND == 2 ? kBiasBytes : 0;
 
 // A launch computes up to kMaxGroups independent problems that share N, K, dtypes and the
 // epilogue (the txt and img streams of a double block: same layer shapes, their own rows,
@@ -71,6 +75,8 @@ struct TcGroup {
   long long ldd;
   const void* bias;
   const float* gate;
+  const float* a_scale;    // E4M3: per-row scale of A [M]
+  const float* b_scale;    // E4M3: per-column scale of B [N]
 };
 
 // Tensor maps of every group (kernel parameter; indexed by group at run time).
@@ -97,9 +103,9 @@ struct TcParams {
   TcGroup g[kMaxGroups];
 };
 
-__host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int stages) {
+__host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int stages, int scale_bytes) {
   return 1024 /* alignment slack */ + static_cast<size_t>(stages) * (a_bytes + b_bytes) + kOutStageBytes + kBiasBytes +
-         256 /* barriers, TMEM slot, broadcast word */;
+         scale_bytes + 256 /* barriers, TMEM slot, broadcast word */;
 }
 
 __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi, int& bz, int& mb, int& nb) {
@@ -290,6 +296,7 @@ __device__ __forceinline__ void emit_chunk(const TcParams& p, const TcGroup& G, 
 struct EpiCtx {
   uint8_t* buf;            // this warp's staging buffer
   float* sbias;            // tile bias in shared memory (BN floats)
+  float* sscale;           // E4M3: tile column scales in shared memory (BN floats)
   volatile int* bcast;     // split-K arrival broadcast word
   int lane, row, q, half;  // row = TMEM lane = tile row; q = lane quarter; half = column half
 };
@@ -308,15 +315,38 @@ __device__ __forceinline__ void stage_bias(const TcParams& p, const TcGroup& G, 
   }
 }
 
+// E4M3: loads this item's per-column weight scales into shared memory (zero past N).
+template <int BN>
+__device__ __forceinline__ void stage_scale(const TcParams& p, const TcGroup& G, float* sscale, int n_base) {
+  for (int i = static_cast<int>(threadIdx.x) - 64; i < BN; i += kEpiThreads) {
+    const int n = n_base + i;
+    sscale[i] = n < p.N ? __ldg(G.b_scale + n) : 0.f;
+  }
+}
+
+// acc * a_scale[row] * b_scale[column] for one 32-column chunk (E4M3 operands).
+__device__ __forceinline__ void scale_chunk(uint32_t (&r)[32], float rs, const float* cs) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 c = *reinterpret_cast<const float4*>(cs + j);
+    r[j] = __float_as_uint(__uint_as_float(r[j]) * rs * c.x);
+    r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) * rs * c.y);
+    r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) * rs * c.z);
+    r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) * rs * c.w);
+  }
+}
+
 // Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
 // accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
 // after this warp's last chunk is read.  With split-K, each split stores its raw fp32
 // partial; the split arriving last on the slot's counter sums all partials in split order
 // (deterministic), runs the epilogue and re-arms the counter for the next launch.
-template <int BN, int EPI, int OUT, typename Release>
+template <int BN, int EPI, int OUT, int KIND, typename Release>
 __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
                                               uint32_t tacc, Release release, const CUtensorMap* tmD, int bz, int m,
                                               int n_base, int slot, int split) {
+  float rs = 0.f;  // E4M3: this row's activation scale
+  if constexpr (KIND == 2) rs = m < G.M ? __ldg(G.a_scale + m) : 0.f;
   constexpr int NCH = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
   const int c0 = e.half * NCH;
   const int m_warp0 = m - e.lane;
@@ -332,6 +362,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
     if (i == NCH - 1) release();
     const int c = c0 + i;
     if (!splitk) {
+      if constexpr (KIND == 2) scale_chunk(r[i & 1], rs, e.sscale + c * 32);
       emit_chunk<EPI, OUT>(p, G, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, r[i & 1],
                            sb ? sb + c * 32 : nullptr, e.lane);
     } else {
@@ -370,6 +401,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
         uint32_t rr[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) rr[j] = __float_as_uint(acc[j]);
+        if constexpr (KIND == 2) scale_chunk(rr, rs, e.sscale + c * 32);
         emit_chunk<EPI, OUT>(p, G, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, rr,
                              sb ? sb + c * 32 : nullptr, e.lane);
       }
@@ -394,7 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sOut = sB + STAGES * B_BYTES;
   float* sBias = reinterpret_cast<float*>(sOut + kOutStageBytes);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes);
+  float* sScale = reinterpret_cast<float*>(sOut + kOutStageBytes + kBiasBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes + kScaleBytes<KIND>);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -495,11 +528,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            // One MMA consumes 32 bytes of K (16 bf16/fp16 or 8 tf32 elements) inside the
+            // One MMA consumes 32 bytes of K (16 bf16/fp16, 8 tf32 or 32 E4M3 elements) inside the
             // 128-byte swizzle row: advance the descriptors by 32 bytes.
             const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
             const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
             if constexpr (KIND == 1) umma_tf32(d_tmem, ad, bd, p.idesc, accum);
+            else if constexpr (KIND == 2) umma_f8(d_tmem, ad, bd, p.idesc, accum);
             else umma_f16(d_tmem, ad, bd, p.idesc, accum);
           }
           umma_commit(&empty_bar[stage]);
@@ -525,6 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     e.row = e.q * 32 + lane;
     e.buf = sOut + (warp - 2) * kOutBufBytes;
     e.sbias = sBias;
+    e.sscale = sScale;
     e.bcast = bcast;
     int obuf = 0;
     uint32_t local = 0;
@@ -534,6 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords(tile, p, gi, bz, mb, nb);
       const TcGroup& G = p.g[gi];
       stage_bias<BN>(p, G, sBias, nb * BN);
+      if constexpr (KIND == 2) stage_scale<BN>(p, G, sScale, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
@@ -546,8 +582,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       };
-      epilogue_item<BN, EPI, OUT>(p, G, e, obuf, tacc, release, &maps.d[gi], bz, mb * kBM + e.row, nb * BN, tile,
-                                  split);
+      epilogue_item<BN, EPI, OUT, KIND>(p, G, e, obuf, tacc, release, &maps.d[gi], bz, mb * kBM + e.row, nb * BN,
+                                        tile, split);
     }
     if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
@@ -586,7 +622,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sOut = sB + STAGES * B_BYTES;
   float* sBias = reinterpret_cast<float*>(sOut + kOutStageBytes);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes);
+  float* sScale = reinterpret_cast<float*>(sOut + kOutStageBytes + kBiasBytes);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + kOutStageBytes + kBiasBytes + kScaleBytes<KIND>);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -696,6 +733,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
             const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
             if constexpr (KIND == 1) umma_tf32_pair(d_tmem, ad, bd, idesc, accum);
+            else if constexpr (KIND == 2) umma_f8_pair(d_tmem, ad, bd, idesc, accum);
             else umma_f16_pair(d_tmem, ad, bd, idesc, accum);
           }
           umma_commit_pair_bcast(&empty_bar[stage], 0x3);
@@ -720,6 +758,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     e.row = e.q * 32 + lane;
     e.buf = sOut + (warp - 2) * kOutBufBytes;
     e.sbias = sBias;
+    e.sscale = sScale;
     e.bcast = bcast;
     const uint32_t leader_tempty0 = map_to_cta(smem_u32(&tempty_bar[0]), 0);
     const uint32_t leader_tempty1 = map_to_cta(smem_u32(&tempty_bar[1]), 0);
@@ -731,6 +770,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tile_coords(tile, p, gi, bz, mb, nb);
       const TcGroup& G = p.g[gi];
       stage_bias<BN>(p, G, sBias, nb * BN);
+      if constexpr (KIND == 2) stage_scale<BN>(p, G, sScale, nb * BN);
       const uint32_t acc = local & 1u;
       const uint32_t acc_phase = (local >> 1) & 1u;
       const bool ok = mbar_wait(&tfull_bar[acc], acc_phase, p.err, kErrWaitEpilogue);
@@ -742,7 +782,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
       };
-      epilogue_item<BN, EPI, OUT>(p, G, e, obuf, tacc, release, &maps.d[gi], bz,
+      epilogue_item<BN, EPI, OUT, KIND>(p, G, e, obuf, tacc, release, &maps.d[gi], bz,
                                   mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN,
                                   tile * 2 + static_cast<int>(rank), split);
     }
@@ -805,13 +845,14 @@ b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, in
   if (s != B2G_OK) return s;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows),
                               static_cast<cuuint64_t>(batch)};
-  const cuuint64_t esz = dt == B2G_F32 ? 4u : 2u;
+  const cuuint64_t esz = dt == B2G_F32 ? 4u : (dt == B2G_E4M3 ? 1u : 2u);
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * esz, static_cast<cuuint64_t>(bstride) * esz};
   const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / esz), box_rows, 1u};  // 128-byte rows
   const cuuint32_t estr[3] = {1u, 1u, 1u};
-  const CUtensorMapDataType t = dt == B2G_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                : dt == B2G_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUtensorMapDataType t = dt == B2G_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : dt == B2G_F16  ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                : dt == B2G_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUresult r = g_encode(map, t, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -855,34 +896,44 @@ b2g_status launch_kernel(Kern kern, size_t smem, const TcMaps& maps, const TcPar
 template <bool PAIR, int BN, int STAGES, int EPI, int OUT, int KIND>
 b2g_status launch_one(const TcMaps& maps, const TcParams& prm, int grid, cudaStream_t st) {
   if constexpr (PAIR) {
-    constexpr size_t smem = smem_bytes(kBM * kBK * 2, 128 * kBK * 2, STAGES);
+    constexpr size_t smem = smem_bytes(kBM * kBK * 2, 128 * kBK * 2, STAGES, kScaleBytes<KIND>);
     static_assert(smem <= 227 * 1024, "shared memory budget");
     return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
   } else {
-    constexpr size_t smem = smem_bytes(kBM * kBK * 2, BN * kBK * 2, STAGES);
+    constexpr size_t smem = smem_bytes(kBM * kBK * 2, BN * kBK * 2, STAGES, kScaleBytes<KIND>);
     static_assert(smem <= 227 * 1024, "shared memory budget");
     return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
   }
 }
 
-template <bool PAIR, int BN, int STAGES>
-b2g_status dispatch_epi(const TcMaps& maps, const TcParams& prm, int grid, b2g_epilogue epi, b2g_dtype out, bool tf32,
+// Epilogue and output-type dispatch for 16-bit (KIND 0) and E4M3 (KIND 2) operands.
+template <bool PAIR, int BN, int STAGES, int KIND>
+b2g_status dispatch_out(const TcMaps& maps, const TcParams& prm, int grid, b2g_epilogue epi, b2g_dtype out,
                         cudaStream_t st) {
-  if (tf32) {
+  if (epi == B2G_EPI_GATED_RESIDUAL)
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, KIND>(maps, prm, grid, st);
+  if (epi == B2G_EPI_GELU) {
+    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, KIND>(maps, prm, grid, st);
+    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, KIND>(maps, prm, grid, st);
+    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, KIND>(maps, prm, grid, st);
+  }
+  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, KIND>(maps, prm, grid, st);
+  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, KIND>(maps, prm, grid, st);
+  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, KIND>(maps, prm, grid, st);
+}
+
+// kind: 0 = bf16/fp16 (kind::f16), 1 = tf32, 2 = E4M3 (kind::f8f6f4, STAGES8 ring stages: the
+// column-scale staging area costs one stage's worth of shared memory in the larger variants).
+template <bool PAIR, int BN, int STAGES, int STAGES8>
+b2g_status dispatch_epi(const TcMaps& maps, const TcParams& prm, int grid, b2g_epilogue epi, b2g_dtype out, int kind,
+                        cudaStream_t st) {
+  if (kind == 1) {
     // fp32 operands (batched_matmul_Bt): plain F32 output only.
     if (epi != B2G_EPI_NONE || out != B2G_F32) return set_error(B2G_ERR_UNSUPPORTED, "tf32 path: F32 output only");
     return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 1>(maps, prm, grid, st);
   }
-  if (epi == B2G_EPI_GATED_RESIDUAL)
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, 0>(maps, prm, grid, st);
-  if (epi == B2G_EPI_GELU) {
-    if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, 0>(maps, prm, grid, st);
-    if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, 0>(maps, prm, grid, st);
-    return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, 0>(maps, prm, grid, st);
-  }
-  if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, 0>(maps, prm, grid, st);
-  if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, 0>(maps, prm, grid, st);
-  return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F16, 0>(maps, prm, grid, st);
+  if (kind == 2) return dispatch_out<PAIR, BN, STAGES8, 2>(maps, prm, grid, epi, out, st);
+  return dispatch_out<PAIR, BN, STAGES, 0>(maps, prm, grid, epi, out, st);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -895,14 +946,17 @@ bool tc_gemm_supported(const GemmProblem& p, std::string* why) {
     return false;
   };
   const bool tf32 = p.a_dtype == B2G_F32 && p.b_dtype == B2G_F32 && p.allow_tf32;
-  if (!((p.a_dtype == B2G_BF16 && p.b_dtype == B2G_BF16) || (p.a_dtype == B2G_F16 && p.b_dtype == B2G_F16) || tf32))
+  const bool fp8 = p.a_dtype == B2G_E4M3 && p.b_dtype == B2G_E4M3;
+  if (!((p.a_dtype == B2G_BF16 && p.b_dtype == B2G_BF16) || (p.a_dtype == B2G_F16 && p.b_dtype == B2G_F16) || tf32 ||
+        fp8))
     return no("operand dtypes");
+  if (fp8 && (!p.a_scale || !p.b_scale)) return no("E4M3 operands need row and column scales");
   if (tf32 && (p.epilogue != B2G_EPI_NONE || p.d_dtype != B2G_F32)) return no("tf32: F32 output, no epilogue");
   if (p.d_dtype != B2G_F32 && p.d_dtype != B2G_BF16 && p.d_dtype != B2G_F16) return no("output dtype");
   if (p.epilogue == B2G_EPI_GATED_RESIDUAL && p.d_dtype != B2G_F32) return no("gated residual needs F32 output");
   if (p.bias && p.bias_dtype != B2G_F32 && p.bias_dtype != B2G_BF16) return no("bias dtype");
   if (!aligned16(p.a) || !aligned16(p.b)) return no("operand base not 16-byte aligned");
-  const int64_t align = tf32 ? 3 : 7;  // 16-byte row and batch strides
+  const int64_t align = tf32 ? 3 : (fp8 ? 15 : 7);  // 16-byte row and batch strides
   if ((p.lda & align) || (p.ldb & align)) return no("operand row stride not a multiple of 16 bytes");
   if (p.batch > 1 && ((p.a_bstride & align) || (p.b_bstride & align))) return no("batch stride not 16-byte aligned");
   if (p.M > (1ll << 31) - 256 || p.N > (1ll << 31) - 256 || p.K > (1ll << 31)) return no("size");
@@ -916,7 +970,7 @@ bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
   return a.N == b.N && a.K == b.K && a.batch == 1 && b.batch == 1 && a.a_dtype == b.a_dtype &&
          a.b_dtype == b.b_dtype && a.d_dtype == b.d_dtype && a.epilogue == b.epilogue && a.alpha == b.alpha &&
          (a.bias == nullptr) == (b.bias == nullptr) && (!a.bias || a.bias_dtype == b.bias_dtype) &&
-         a.allow_split == b.allow_split;
+         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr);
 }
 
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) { return tc_gemm_launch_group(&p, 1, st); }
@@ -938,7 +992,8 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   const int sms = dev->num_sms;
   const int pairs = sms / 2;
   const bool tf32 = p.a_dtype == B2G_F32;
-  const int kelems = tf32 ? 32 : 64;
+  const int kind = tf32 ? 1 : (p.a_dtype == B2G_E4M3 ? 2 : 0);
+  const int kelems = kind == 1 ? 32 : (kind == 2 ? 128 : 64);
   const long long nkb = (p.K + kelems - 1) / kelems;
   // Kernel variant and split-K factor from a cost model in units of one 64-wide k-block of
   // a pair tile: whole waves of work items over the SMs (or SM pairs), times the k-blocks
@@ -1000,6 +1055,8 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     G.ldd = q.ldd;
     G.bias = q.bias;
     G.gate = q.gate;
+    G.a_scale = q.a_scale;
+    G.b_scale = q.b_scale;
     G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
                (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
     all_vec = all_vec && G.vec_ok;
@@ -1013,7 +1070,8 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.alpha = p.alpha;
   prm.err = dev->err_word;
-  prm.idesc = idesc_make(tf32 ? kFmtTF32 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16), tile_m, bn);
+  prm.idesc = idesc_make(kind == 1 ? kFmtTF32 : (kind == 2 ? kFmtE4M3 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16)),
+                         tile_m, bn);
   prm.a_keep = a_bytes <= b_bytes ? 1 : 0;
   if (prm.num_tiles == 0) return B2G_OK;
 
@@ -1045,11 +1103,12 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
 
   if (pair) {
     const int grid = 2 * static_cast<int>(prm.num_items < pairs ? prm.num_items : pairs);
-    return dispatch_epi<true, 256, kPairStages>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+    return dispatch_epi<true, 256, kPairStages, kPairStages - 1>(maps, prm, grid, p.epilogue, p.d_dtype, kind, st);
   }
   const int grid = static_cast<int>(prm.num_items < sms ? prm.num_items : sms);
-  if (v == V256) return dispatch_epi<false, 256, kStages256>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
-  return dispatch_epi<false, 128, kStages128>(maps, prm, grid, p.epilogue, p.d_dtype, tf32, st);
+  if (v == V256)
+    return dispatch_epi<false, 256, kStages256, kStages256 - 1>(maps, prm, grid, p.epilogue, p.d_dtype, kind, st);
+  return dispatch_epi<false, 128, kStages128, kStages128 - 1>(maps, prm, grid, p.epilogue, p.d_dtype, kind, st);
 }
 
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits) {

@@ -193,6 +193,27 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Same with kind::f8f6f4 (here E4M3 x E4M3 from shared memory, fp32 accumulation); one MMA
+// consumes 32 elements (32 bytes) of K.
+__device__ __forceinline__ void umma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Same with kind::tf32 (fp32 operands in shared memory, TF32 products, fp32 accumulation).
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
@@ -350,10 +371,11 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor for kind::f16 / kind::tf32 with fp32 accumulation, both operands
-// K-major.  bits 4-5 D format (1 = f32); 7-9 A format, 10-12 B format (0 = f16, 1 = bf16,
-// 2 = tf32); bits 15/16 A/B major (0 = K); bits 17-22 N >> 3; bits 24-28 M >> 4.
-enum : uint32_t { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2 };
+// Instruction descriptor for kind::f16 / kind::tf32 / kind::f8f6f4 with fp32 accumulation,
+// both operands K-major.  bits 4-5 D format (1 = f32); 7-9 A format, 10-12 B format
+// (kind::f16: 0 = f16, 1 = bf16; kind::tf32: 2; kind::f8f6f4: 0 = E4M3); bits 15/16 A/B
+// major (0 = K); bits 17-22 N >> 3; bits 24-28 M >> 4.
+enum : uint32_t { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2, kFmtE4M3 = 0 };
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t fmt, int m, int n) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);

@@ -159,6 +159,23 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
  * capture on it (it looks up the array's device address). */
 b2g_status b2g_gemm_noalloc(const b2g_gemm_desc* desc, void* stream);
 
+/* FP8 E4M3 quantisation of the rows of a matrix (no reference counterpart; the reference's
+ * quantised path is INT8, quantize_act / linear_prequant in cublas_ops.cuh:294-791).  For each
+ * row r of src [rows, cols] (F32, BF16 or F16, row stride ld): scales[r] = absmax_r / 448 (1
+ * for an all-zero row) and dst[r, c] = E4M3(src[r, c] * 448 / absmax_r), round to nearest
+ * even, saturating at +-448 (row stride dst_ld bytes).  Used once at load time on a weight
+ * [N, K] (one scale per output channel: the FP8 variant of load_weight, chroma.cuh:97-134)
+ * and per call on activations (one scale per token).  cols % 8 == 0, 16-byte source rows. */
+b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
+                             uint8_t* dst, int64_t dst_ld, float* scales, void* stream);
+
+/* FP8 linear (no reference counterpart): D = epilogue((A . W^T) * a_scale[m] * b_scale[n] +
+ * bias) with W = desc->b an E4M3 [N, K] weight from b2g_quantize_e4m3 and b_scale its scales.
+ * desc->a is either E4M3 with per-row scales a_scale, or BF16 / F16 / F32 activations, which
+ * are quantised per token first (a_scale ignored).  Products exact, fp32 accumulation; the
+ * same epilogues and output types as b2g_gemm.  K % 16 == 0 (16-byte rows). */
+b2g_status b2g_gemm_fp8(const b2g_gemm_desc* desc, const float* a_scale, const float* b_scale, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

@@ -124,6 +124,66 @@ void oracle_f32_to_f16_array(const float* src, uint16_t* dst, int64_t n) {
   for (int64_t i = 0; i < n; ++i) dst[i] = oracle_f32_to_f16(src[i]);
 }
 
+/* ------------------------------------------------------------------ FP8 E4M3
+ * E4M3 ("fn" variant): 1 sign, 4 exponent (bias 7), 3 mantissa bits; no infinities;
+ * S.1111.111 is NaN; largest finite 448 = 1.75 * 2^8; smallest normal 2^-6; subnormals
+ * m/8 * 2^-6.  This restates the format definition (the FP8 formats paper, Micikevicius et
+ * al. 2022) with round-to-nearest-even and saturation to +-448, the conversion
+ * cvt.rn.satfinite.e4m3x2.f32 performs.  The reference has no FP8 path: the format and the
+ * per-row absmax/448 scaling are the engine's FP8 variant as BASELINE's config 5 defines it. */
+uint8_t oracle_f32_to_e4m3(float x) {
+  const uint32_t u = f32_to_bits(x);
+  const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+  if (isnan(x)) return 0x7F;
+  float a = fabsf(x);
+  if (a >= 448.0f) return (uint8_t)(sign | 0x7E); /* saturate (also +-inf) */
+  if (a < ldexpf(1.0f, -6)) {
+    /* subnormal range: multiples of 2^-9 (q = 8 rounds up into the smallest normal) */
+    const float q = rintf(a * 512.0f); /* exact scaling by a power of two, then RNE */
+    return (uint8_t)(sign | (uint8_t)q);
+  }
+  int e;
+  frexpf(a, &e); /* a = f * 2^e, f in [0.5, 1): unbiased exponent of a is e - 1 */
+  const int ex = e - 1;
+  float q = rintf(ldexpf(a, 3 - ex)); /* mantissa with the implicit bit, in [8, 16] */
+  int ee = ex;
+  if (q >= 16.0f) {
+    q = 8.0f;
+    ee += 1;
+  }
+  if (ee > 8 || (ee == 8 && q > 14.0f)) return (uint8_t)(sign | 0x7E);
+  return (uint8_t)(sign | (uint8_t)(((ee + 7) << 3) | ((int)q - 8)));
+}
+
+float oracle_e4m3_to_f32(uint8_t b) {
+  const float sign = (b & 0x80) ? -1.0f : 1.0f;
+  const int ex = (b >> 3) & 0xF, m = b & 7;
+  if (ex == 0xF && m == 7) return NAN;
+  if (ex == 0) return sign * ldexpf((float)m, -9);
+  return sign * ldexpf((float)(8 + m), ex - 10);
+}
+
+void oracle_f32_to_e4m3_array(const float* src, uint8_t* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = oracle_f32_to_e4m3(src[i]);
+}
+void oracle_e4m3_to_f32_array(const uint8_t* src, float* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) dst[i] = oracle_e4m3_to_f32(src[i]);
+}
+
+/* Per-row quantisation as the engine defines it: scale_r = absmax_r / 448 (1 when the row is
+ * zero), q = E4M3(x * (448 / absmax_r)), all arithmetic in fp32. */
+void oracle_quantize_rows_e4m3(const float* src, int64_t rows, int64_t cols, uint8_t* dst, float* scales) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < rows; ++r) {
+    const float* x = src + r * cols;
+    float amax = 0.0f;
+    for (int64_t c = 0; c < cols; ++c) amax = fmaxf(amax, fabsf(x[c]));
+    const float inv = amax > 0.0f ? 448.0f / amax : 1.0f;
+    scales[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+    for (int64_t c = 0; c < cols; ++c) dst[r * cols + c] = oracle_f32_to_e4m3(x[c] * inv);
+  }
+}
+
 /* ------------------------------------------------------------------ GEMM */
 
 /* out[m, n] = sum_k X[m, k] * W[n, k] over fp32 operands, 16 interleaved fp32 partial sums

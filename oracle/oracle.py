@@ -51,6 +51,9 @@ class Oracle:
         lib.oracle_modulate.argtypes = [_c_p, _c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
         lib.oracle_rms_norm.argtypes = [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
         lib.oracle_round.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
+        lib.oracle_f32_to_e4m3_array.argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_e4m3_to_f32_array.argtypes = [_c_p, _c_p, _i64]
+        lib.oracle_quantize_rows_e4m3.argtypes = [_c_p, _i64, _i64, _c_p, _c_p]
         lib.oracle_f32_to_bf16_array.argtypes = [_c_p, _c_p, _i64]
         lib.oracle_f32_to_f16_array.argtypes = [_c_p, _c_p, _i64]
         lib.oracle_to_f32.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
@@ -155,6 +158,36 @@ class Oracle:
         if self.lib.oracle_attention_rope(_np_ptr(Q), _np_ptr(K), _np_ptr(V), _np_ptr(pe), _np_ptr(m), _np_ptr(out),
                                           L, H, D) != 0:
             raise MemoryError("oracle_attention_rope")
+        return out
+
+    # ---------------------------------------------------------------- FP8 E4M3
+    def to_e4m3_bits(self, a: np.ndarray) -> np.ndarray:
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        out = np.empty(a.shape, dtype=np.uint8)
+        self.lib.oracle_f32_to_e4m3_array(_np_ptr(a), _np_ptr(out), a.size)
+        return out
+
+    def e4m3_to_f32(self, bits: np.ndarray) -> np.ndarray:
+        bits = np.ascontiguousarray(bits, dtype=np.uint8)
+        out = np.empty(bits.shape, dtype=np.float32)
+        self.lib.oracle_e4m3_to_f32_array(_np_ptr(bits), _np_ptr(out), bits.size)
+        return out
+
+    def quantize_rows_e4m3(self, x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+        """Per-row E4M3 quantisation: (codes [rows, cols] uint8, scales [rows] f32)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = x.shape
+        q = np.empty((rows, cols), dtype=np.uint8)
+        s = np.empty(rows, dtype=np.float32)
+        self.lib.oracle_quantize_rows_e4m3(_np_ptr(x), rows, cols, _np_ptr(q), _np_ptr(s))
+        return q, s
+
+    def gemm_fp8(self, qa, sa, qb, sb, bias=None) -> np.ndarray:
+        """(sum_k a.b over the E4M3 values, exact products, float64 sums) * sa[m] * sb[n] + bias."""
+        acc = self.e4m3_to_f32(qa).astype(np.float64) @ self.e4m3_to_f32(qb).astype(np.float64).T
+        out = acc * sa.astype(np.float64)[:, None] * sb.astype(np.float64)[None, :]
+        if bias is not None:
+            out = out + bias.astype(np.float64)[None, :]
         return out
 
     def rms_norm(self, x, scale, eps=1e-6):
