@@ -560,21 +560,126 @@ def run_engine_config2(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+WORKLOAD4 = ("config4: one double-stream + one single-stream block at 1024^2 (T=512 txt + I=4096 img tokens), "
+             "tensor-parallel over all ranks (column-split qkv/linear1/mlp0, row-split proj/linear2/mlp2, "
+             "3 bf16 NCCL all-reduces of [4608, 3072] per step)")
+
+
+def run_engine_config4(args) -> None:
+    """Tensor-parallel block pair at 1024^2: every rank runs its shard; strong scaling."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import b2g
+    import blocks
+    import tp
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    b2g.init()
+    T, I = 512, 4096
+    L, H = T + I, blocks.HIDDEN
+    g = torch.Generator(device=dev).manual_seed(0)
+    txt_w, img_w = blocks.random_stream(g, dev), blocks.random_stream(g, dev)
+    sw = blocks.random_single(g, dev)
+    tw, iw, ts = tp.shard_stream(txt_w, rank, world), tp.shard_stream(img_w, rank, world), tp.shard_single(sw, rank,
+                                                                                                          world)
+    del txt_w, img_w, sw  # keep only this rank's shard resident
+    torch.cuda.empty_cache()
+    act = {k: torch.randn((n, H), generator=g, device=dev).to(torch.bfloat16) for k, n in
+           (("txt_mod1", T), ("img_mod1", I), ("txt_mod2", T), ("img_mod2", I), ("x_mod", L))}
+    res = {k: torch.randn((n, H), generator=g, device=dev) for k, n in (("txt", T), ("img", I), ("x", L))}
+    gt = [torch.randn(H, generator=g, device=dev) for _ in range(5)]
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=dev) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    mask = torch.zeros(L, device=dev)
+    mask[T - MASKED:T] = float("-inf")
+    scratch = tp.TPScratch(T, I, world, dev)
+    ops = tp.EngineOps()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                           res["txt"], res["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
+        tp.tp_single_block(ops, ts, act["x_mod"], res["x"], gt[4], pe, mask, scratch)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    n0 = b2g.launch_count()
+    per_step = []
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step()
+            b.record(stream)
+            b.synchronize()
+            per_step.append(a.elapsed_time(b))
+    launches = b2g.launch_count() - n0
+    b2g.check_device_error()
+    total_ms = sum(per_step)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t[0])
+    lin, att = blocks.block_pair_flops(T, I)
+    per = total_ms / args.steps
+    value = (lin + att) / (per * 1e-3) / 1e12
+    peaks = measured_peaks()
+    per_gpu = value / world
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox generator, seed 0)",
+        "config": {"workload": WORKLOAD4, "flop_per_step": lin + att, "parallelism": f"tp{world}",
+                   "allreduce_bytes_per_step": 3 * L * H * 2 if world > 1 else 0,
+                   "l2": "256 MB buffer written before every step, outside the events"},
+        "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(per_gpu / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_source": peaks["source"] + " (burst bf16)",
+                     "kernel": "whole step per GPU (GEMMs, attention, all-reduces)"},
+        "clocks": clk.summary(), "gpu_launches": int(launches),
+        "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100 for config2, 200 config1)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
-    ap.add_argument("--workload", choices=["config2", "config1"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config1", "config4"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = 100 if args.workload == "config2" else 200
+        args.steps = {"config2": 100, "config1": 200, "config4": 30}[args.workload]
     fn = {("b2g", "config1"): run_engine_config1, ("reference", "config1"): run_reference_config1,
-          ("b2g", "config2"): run_engine_config2, ("reference", "config2"): run_reference_config2}
+          ("b2g", "config2"): run_engine_config2, ("reference", "config2"): run_reference_config2,
+          ("b2g", "config4"): run_engine_config4,
+          ("reference", "config4"): lambda a: print(json.dumps({
+              "impl": "reference", "unavailable": "the reference has no tensor-parallel path; its single-GPU "
+                                                  "block code is the config2 reference arm"}))}
     fn[(args.impl, args.workload)](args)
 
 

@@ -68,6 +68,8 @@ _SIGNATURES = {
                                                                                    ctypes.c_void_p, ctypes.c_void_p],
                           ctypes.c_int),
     "b2g_gemm_fp8": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "b2g_bias_gated_residual": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                                ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt_stream": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -255,6 +257,20 @@ def gemm_fp8(x: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor, bias: tor
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_gemm_fp8(ctypes.byref(d), _ptr(x_scale), w_scale.data_ptr(), ctypes.c_void_p(s)))
     return out
+
+
+def bias_gated_residual(y: torch.Tensor, bias: torch.Tensor | None, gate: torch.Tensor, residual: torch.Tensor,
+                        stream: torch.cuda.Stream | None = None) -> None:
+    """residual[m, n] += gate[n] * (y[m, n] + bias[n]) (y BF16 or F32 [M, N], residual F32)."""
+    lib = load()
+    _require_cuda(y, bias, gate, residual)
+    M, N = residual.shape
+    if y.shape != (M, N) or y.stride(1) != 1 or residual.stride(1) != 1 or residual.dtype != torch.float32:
+        raise B2GError("bias_gated_residual: y [M, N] and F32 residual [M, N] with unit column stride expected")
+    s = (stream or torch.cuda.current_stream(y.device)).cuda_stream
+    _check(lib.b2g_bias_gated_residual(y.data_ptr(), _TORCH_TO_B2G[y.dtype], y.stride(0) if M > 1 else N, _ptr(bias),
+                                       gate.data_ptr(), residual.data_ptr(), residual.stride(0) if M > 1 else N, M, N,
+                                       ctypes.c_void_p(s)))
 
 
 def linear_lt(M: int, K: int, N: int, x: torch.Tensor, x_type: int, w: torch.Tensor, w_type: int,

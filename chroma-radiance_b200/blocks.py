@@ -161,3 +161,9 @@ def block_pair_ops(T: int, I: int) -> list[tuple[str, str, float]]:
             ("double.mlp2", "gemm", 2.0 * L * H * MLP),
             ("single.linear1_qkv", "gemm", 2.0 * L * H3 * H), ("single.linear1_mlp", "gemm", 2.0 * L * MLP * H),
             ("single.attention", "attention", att), ("single.linear2", "gemm", 2.0 * L * H * (H + MLP))]
+
+
+def block_pair_flops(T: int, I: int) -> tuple[float, float]:
+    """(linear FLOPs, attention FLOPs counted unmasked) of one double + one single block."""
+    ops = block_pair_ops(T, I)
+    return (sum(f for _, kind, f in ops if kind == "gemm"), sum(f for _, kind, f in ops if kind == "attention"))

@@ -318,6 +318,15 @@ b2g_status b2g_gemm_fp8(const b2g_gemm_desc* d, const float* a_scale, const floa
   return tc_gemm_launch(p, st);
 }
 
+b2g_status b2g_bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias,
+                                   const float* gate, float* residual, int64_t ldr, int64_t M, int64_t N,
+                                   void* stream) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return bias_gated_residual(y, y_dtype, ldy, bias, gate, residual, ldr, M, N, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_linear_lt_stream(int64_t M, int64_t K, int64_t N, const void* x_data, cudaDataType_t x_type,
                                 const void* w_data, cudaDataType_t w_type, const void* bias_data, void* out_data,
                                 void* stream) {

@@ -61,6 +61,11 @@ b2g_status make_operand_map(CUtensorMap* map, const void* base, b2g_dtype dt, in
 b2g_status quantize_rows_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
                               uint8_t* dst, int64_t dst_ld, float* scales, cudaStream_t st);
 
+// residual[m, n] += gate[n] * (y[m, n] + bias[n]) after a tensor-parallel all-reduce
+// (elementwise.cu); y BF16 or F32, bias may be NULL.
+b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias, const float* gate,
+                               float* residual, int64_t ldr, int64_t M, int64_t N, cudaStream_t st);
+
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // One launch over `count` (<= 2) problems that tc_gemm_groupable() accepts pairwise; their

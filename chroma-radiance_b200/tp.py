@@ -1,0 +1,182 @@
+"""Tensor-parallel Chroma block pair (large images across 2/4/8 GPUs).
+
+One process per GPU.  Each rank holds a slice of every block's weights, made once at load
+time (the TP-shard layout of the weight arena):
+  column-split (by heads / MLP columns, no communication):
+      qkv      rows [q_h0:q_h1, k_h0:k_h1, v_h0:v_h1] of qkv_w      (24/TP heads per rank)
+      mlp0     rows [m0:m1] of mlp0_w                                (12288/TP columns)
+      linear1  rows q, k, v of the rank's heads + MLP rows [m0:m1]
+  row-split (K-split) to match, producing a partial sum without bias:
+      proj     columns [h0*128:h1*128] of proj_w   (a view: the GEMM reads any row stride)
+      mlp2     columns [m0:m1] of mlp2_w           (a view)
+      linear2  columns of the rank's heads and MLP slice, packed once into [3072, HDl+MLPl]
+After each row-split layer one bf16 all-reduce (NCCL over NVLink) sums the partials of all
+ranks; bias and the gated residual are then applied once, in F32 (b2g_bias_gated_residual).
+Per block pair: 2 all-reduces in the double block (proj with txt and img rows together, then
+the MLP) and 1 in the single block, of [L, 3072] bf16 each.  Attention, qk-norm and RoPE are
+head-local.  Small images instead run one independent replica per GPU (bench.py config 2).
+
+The compute steps go through an `ops` object (EngineOps: libb2g kernels + torch.distributed);
+the CPU tests substitute an fp32 torch stand-in with gloo ranks to check the sharding logic.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from blocks import DHEAD, HEADS, HIDDEN, MLP, SingleWeights, StreamWeights
+
+
+@dataclass(frozen=True)
+class Dims:
+    """Block dimensions (Chroma: hidden 3072, 24 heads x 128, MLP 12288)."""
+
+    hidden: int = HIDDEN
+    heads: int = HEADS
+    dhead: int = DHEAD
+    mlp: int = MLP
+
+
+class EngineOps:
+    """The product path: libb2g's tensor-core GEMMs, fused attention and bias/gate kernel,
+    and an all-reduce over the default process group (NCCL on GPUs)."""
+
+    def __init__(self):
+        import b2g
+
+        self.b2g = b2g
+
+    def gemm_group(self, problems):
+        return self.b2g.gemm_group(problems)
+
+    def gemm(self, x, w, bias=None, out=None, epilogue="none", gate=None):
+        return self.b2g.gemm(x, w, bias, out=out, epilogue=epilogue, gate=gate)
+
+    def attention(self, q, k, v, pe, n_head, d_head, **kw):
+        return self.b2g.attention_qknorm_rope(q, k, v, pe, n_head, d_head, **kw)
+
+    def bias_gated_residual(self, y, bias, gate, residual):
+        self.b2g.bias_gated_residual(y, bias, gate, residual)
+
+    def all_reduce(self, t):
+        import torch.distributed as dist
+
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+            dist.all_reduce(t)
+
+
+@dataclass
+class TPStreamWeights:
+    qkv_w: torch.Tensor   # [3*HDl, 3072]   q, k, v rows of this rank's heads
+    qkv_b: torch.Tensor   # [3*HDl]
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    proj_w: torch.Tensor  # [3072, HDl] view (row stride 3072)
+    proj_b: torch.Tensor  # [3072] full: applied after the all-reduce
+    mlp0_w: torch.Tensor  # [MLPl, 3072]
+    mlp0_b: torch.Tensor  # [MLPl]
+    mlp2_w: torch.Tensor  # [3072, MLPl] view (row stride 12288)
+    mlp2_b: torch.Tensor  # [3072] full
+
+
+@dataclass
+class TPSingleWeights:
+    linear1_w: torch.Tensor  # [3*HDl + MLPl, 3072]
+    linear1_b: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    linear2_w: torch.Tensor  # [3072, HDl + MLPl] packed
+    linear2_b: torch.Tensor  # [3072] full
+
+
+def _split(world: int, d: Dims) -> tuple[int, int]:
+    if d.heads % world or d.mlp % world:
+        raise ValueError(f"tensor parallelism {world} must divide {d.heads} heads and {d.mlp} MLP columns")
+    return d.heads // world, d.mlp // world
+
+
+def head_range(rank: int, world: int, d: Dims = Dims()) -> tuple[int, int]:
+    hl, _ = _split(world, d)
+    return rank * hl * d.dhead, (rank + 1) * hl * d.dhead
+
+
+def mlp_range(rank: int, world: int, d: Dims = Dims()) -> tuple[int, int]:
+    _, ml = _split(world, d)
+    return rank * ml, (rank + 1) * ml
+
+
+def shard_stream(w: StreamWeights, rank: int, world: int, d: Dims = Dims()) -> TPStreamWeights:
+    c0, c1 = head_range(rank, world, d)
+    m0, m1 = mlp_range(rank, world, d)
+    qkv_rows = [slice(j * d.hidden + c0, j * d.hidden + c1) for j in range(3)]
+    return TPStreamWeights(
+        qkv_w=torch.cat([w.qkv_w[r] for r in qkv_rows]).contiguous(),
+        qkv_b=torch.cat([w.qkv_b[r] for r in qkv_rows]).contiguous(),
+        q_norm=w.q_norm, k_norm=w.k_norm,
+        proj_w=w.proj_w[:, c0:c1], proj_b=w.proj_b,
+        mlp0_w=w.mlp0_w[m0:m1], mlp0_b=w.mlp0_b[m0:m1],
+        mlp2_w=w.mlp2_w[:, m0:m1], mlp2_b=w.mlp2_b)
+
+
+def shard_single(w: SingleWeights, rank: int, world: int, d: Dims = Dims()) -> TPSingleWeights:
+    c0, c1 = head_range(rank, world, d)
+    m0, m1 = mlp_range(rank, world, d)
+    H = d.hidden
+    rows = [slice(j * H + c0, j * H + c1) for j in range(3)] + [slice(3 * H + m0, 3 * H + m1)]
+    return TPSingleWeights(
+        linear1_w=torch.cat([w.linear1_w[r] for r in rows]).contiguous(),
+        linear1_b=torch.cat([w.linear1_b[r] for r in rows]).contiguous(),
+        q_norm=w.q_norm, k_norm=w.k_norm,
+        linear2_w=torch.cat([w.linear2_w[:, c0:c1], w.linear2_w[:, H + m0:H + m1]], dim=1).contiguous(),
+        linear2_b=w.linear2_b)
+
+
+class TPScratch:
+    """Per-rank activation buffers of one block pair, allocated once."""
+
+    def __init__(self, T: int, I: int, world: int, dev, d: Dims = Dims()):
+        hl, ml = _split(world, d)
+        L, HDl = T + I, hl * d.dhead
+        self.d, self.hl, self.HDl, self.ml = d, hl, HDl, ml
+        self.qkv = torch.empty((L, 3 * HDl), dtype=torch.float32, device=dev)
+        self.attn = torch.empty((L, HDl), dtype=torch.bfloat16, device=dev)
+        self.part = torch.empty((L, d.hidden), dtype=torch.bfloat16, device=dev)
+        self.h_txt = torch.empty((T, ml), dtype=torch.bfloat16, device=dev)
+        self.h_img = torch.empty((I, ml), dtype=torch.bfloat16, device=dev)
+        self.cat = torch.empty((L, HDl + ml), dtype=torch.bfloat16, device=dev)
+
+
+def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, txt_mod2, img_mod2, txt,
+                    img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask, s: TPScratch) -> None:
+    """This rank's share of double_block (chroma.cuh:808-964); txt, img replicated F32 streams."""
+    T, HDl = txt.shape[0], s.HDl
+    ops.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
+                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
+    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
+    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm, q_norm2=img_w.q_norm,
+                  k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    ops.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, out=s.part[:T]),
+                    dict(x=s.attn[T:], w=img_w.proj_w, out=s.part[T:])])
+    ops.all_reduce(s.part)
+    ops.bias_gated_residual(s.part[:T], txt_w.proj_b, txt_gate1, txt)
+    ops.bias_gated_residual(s.part[T:], img_w.proj_b, img_gate1, img)
+    ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
+                    dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
+    ops.gemm_group([dict(x=s.h_txt, w=txt_w.mlp2_w, out=s.part[:T]),
+                    dict(x=s.h_img, w=img_w.mlp2_w, out=s.part[T:])])
+    ops.all_reduce(s.part)
+    ops.bias_gated_residual(s.part[:T], txt_w.mlp2_b, txt_gate2, txt)
+    ops.bias_gated_residual(s.part[T:], img_w.mlp2_b, img_gate2, img)
+
+
+def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch) -> None:
+    """This rank's share of single_block (chroma.cuh:1101-1157); x the replicated F32 stream."""
+    HDl = s.HDl
+    ops.gemm(x_mod, w.linear1_w[:3 * HDl], w.linear1_b[:3 * HDl], out=s.qkv)
+    ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
+    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
+    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask, out=s.cat[:, :HDl])
+    ops.gemm(s.cat, w.linear2_w, out=s.part)
+    ops.all_reduce(s.part)
+    ops.bias_gated_residual(s.part, w.linear2_b, gate, x)

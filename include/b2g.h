@@ -176,6 +176,14 @@ b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows,
  * same epilogues and output types as b2g_gemm.  K % 16 == 0 (16-byte rows). */
 b2g_status b2g_gemm_fp8(const b2g_gemm_desc* desc, const float* a_scale, const float* b_scale, void* stream);
 
+/* residual[m, n] (F32, row stride ldr) += gate[n] * (y[m, n] + bias[n]) for the tensor-parallel
+ * path: the reference's gated_residual (kernels.cu:942-968) with the linear's bias folded in,
+ * applied once after the all-reduce of the row-split layer's partial sums (which carry no
+ * bias).  y BF16 or F32 (row stride ldy); bias may be NULL.  N % 8 == 0, 16-byte rows. */
+b2g_status b2g_bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias,
+                                   const float* gate, float* residual, int64_t ldr, int64_t M, int64_t N,
+                                   void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

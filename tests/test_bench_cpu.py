@@ -1,0 +1,35 @@
+"""CPU checks of bench.py's bookkeeping: FLOP counts of the block pair (BASELINE: 347.89
+GFLOP of linears and 28.99 GFLOP of attention per block at 512^2) and that every workload and
+arm is wired to a function."""
+from __future__ import annotations
+
+import subprocess
+import sys
+from pathlib import Path
+
+import blocks
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def test_block_pair_flops_match_baseline():
+    lin, att = blocks.block_pair_flops(512, 1024)
+    assert abs(lin / 2 - 347.89e9) < 0.01e9
+    assert abs(att / 2 - 28.99e9) < 0.01e9
+    ops = blocks.block_pair_ops(512, 1024)
+    assert sum(f for _, _, f in ops) == lin + att
+
+
+def test_bench_help_lists_workloads():
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--help"], capture_output=True, text=True)
+    assert r.returncode == 0
+    for w in ("config1", "config2", "config4"):
+        assert w in r.stdout
+
+
+def test_reference_arm_without_gpu_reports_unavailable_or_runs():
+    """The config4 reference arm has no counterpart in the reference: one JSON line saying so."""
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--workload", "config4"],
+                       capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0
+    assert '"unavailable"' in r.stdout

@@ -1,0 +1,77 @@
+"""Worker for tests/test_tp_gpu.py, launched with torchrun (one process per GPU, NCCL).
+
+Every rank builds the same block-pair weights and inputs (seeded), shards them with tp.py,
+runs the tensor-parallel double + single block, and compares its replicated residual
+streams with the unsharded engine path (blocks.py) computed on its own GPU: update
+max|d|/max|ref| <= 1e-2 and cosine >= 0.9999.  Exit code 0 when every rank agrees."""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+REPO = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(REPO / "chroma-radiance_b200"))
+
+import b2g  # noqa: E402
+import blocks  # noqa: E402
+import tp  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    b2g.init()
+    T, I = 512, int(os.environ.get("TP_IMG_TOKENS", "1024"))
+    L = T + I
+    g = torch.Generator(device=dev).manual_seed(11)
+    txt_w, img_w = blocks.random_stream(g, dev), blocks.random_stream(g, dev)
+    sw = blocks.random_single(g, dev)
+    H = blocks.HIDDEN
+    act = {k: torch.randn((n, H), generator=g, device=dev).to(torch.bfloat16) for k, n in
+           (("txt_mod1", T), ("img_mod1", I), ("txt_mod2", T), ("img_mod2", I), ("x_mod", L))}
+    res = {k: torch.randn((n, H), generator=g, device=dev) for k, n in (("txt", T), ("img", I), ("x", L))}
+    gates = [torch.randn(H, generator=g, device=dev) for _ in range(5)]
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=dev) * 6.28
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    mask = torch.zeros(L, device=dev)
+    mask[T - 400:T] = float("-inf")
+
+    ref = {k: v.clone() for k, v in res.items()}
+    s1 = blocks.Scratch(T, I, dev)
+    blocks.double_block(txt_w, img_w, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"], ref["txt"],
+                        ref["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, s1)
+    blocks.single_block(sw, act["x_mod"], ref["x"], gates[4], pe, mask, s1)
+
+    ops = tp.EngineOps()
+    tw, iw, ts = tp.shard_stream(txt_w, rank, world), tp.shard_stream(img_w, rank, world), tp.shard_single(sw, rank,
+                                                                                                          world)
+    scratch = tp.TPScratch(T, I, world, dev)
+    got = {k: v.clone() for k, v in res.items()}
+    tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"], got["txt"],
+                       got["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
+    tp.tp_single_block(ops, ts, act["x_mod"], got["x"], gates[4], pe, mask, scratch)
+    torch.cuda.synchronize()
+    b2g.check_device_error()
+    ok = True
+    for k in got:
+        d1, d0 = (got[k] - res[k]).double().flatten(), (ref[k] - res[k]).double().flatten()
+        err = ((d1 - d0).abs().max() / d0.abs().max()).item()
+        cos = ((d1 @ d0) / (d1.norm() * d0.norm())).item()
+        print(f"rank {rank}/{world} {k}: err {err:.3e} cos {cos:.6f}", flush=True)
+        ok = ok and err <= 1e-2 and cos >= 0.9999
+    flag = torch.tensor([0 if ok else 1], device=dev)
+    dist.all_reduce(flag)
+    dist.destroy_process_group()
+    return int(flag.item() != 0)
+
+
+if __name__ == "__main__":
+    sys.exit(main())
