@@ -165,49 +165,57 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 // ---------------------------------------------------------------------------- fused attention
 //
-// CTA = (query tile of 128 rows, head h), 352 threads:
-//   warp 0      TMA: Q tile once, then K tile j [128 keys x D] into a 3-deep ring.
-//   warp 10     TMA: Vt tile j [D x 128 keys] into a 3-deep ring.
-//   warp 1      one thread issues tcgen05.mma: S_j = Q K_j^T (M=128, N=128, K=D; both from
-//               shared memory) into TMEM buffer j%3, then O += P_j Vt_j^T (M=128, N=D, K=128)
-//               with P_j read from TMEM (it overwrites the first 64 columns of S_j as bf16
-//               pairs) and Vt_j from shared memory.  S_{j+2} is issued before P_j is ready, so
-//               the tensor core computes scores ahead while the softmax warps work.
-//   warps 2-9   softmax, two warps per 32-row lane quarter (warp w reads TMEM lanes
-//               32*(w%4)..; warps 2-5 take keys 0-63 of each block, warps 6-9 keys 64-127):
-//               t = S*log2(e)/sqrt(D) + key_bias_log2; the two warps of a row combine their
-//               maxima through shared memory, each rounded to bf16 towards +inf so both get
-//               the same value, never below the true one; running max m (raised only when a
-//               block's max exceeds it by more than 8, i.e. a factor 256, so O in TMEM is
-//               rescaled rarely, each warp its half of O's columns); P = 2^(t - m) as bf16
-//               into TMEM with one tcgen05.st per warp; l += sum P.  At the end O / l.
-// Keeping P in TMEM and Q, K, Vt in 3-deep shared-memory rings keeps the shared-memory
-// traffic per block (MMA operand reads + TMA writes) within the SM's bandwidth.
-// Barriers: q_full; k_full[3], v_full[3] (TMA bytes); k_empty[3] (MMA commit after S_j),
-// v_empty[3] (MMA commit after P_j.Vt_j); s_full[3] (MMA commit after S_j); p_full[3]
-// (8 softmax warps: P_j stored); p_empty[3] (MMA commit after P_j.Vt_j: TMEM buffer j%3 free
-// for S_{j+3}, and O holds blocks <= j).
-// Every wait is bounded; on timeout the kernel records the error word and winds down.
-constexpr int kFaThreads = 352;
-constexpr int kFaRows = 128;   // queries per CTA
-constexpr int kFaKeys = 128;   // keys per block
-constexpr int kFaStages = 3;   // K and Vt ring depth, and TMEM S/P buffers
+// CTA = (two query tiles A and B of 128 rows = 256 queries, head h), 384 threads:
+//   warp 0      TMA: both Q tiles once, then K tile j [128 keys x D] into a 3-deep ring.
+//   warp 2      TMA: Vt tile j [D x 128 keys] into a 2-deep ring.
+//   warp 1      one thread issues tcgen05.mma for both tiles, alternating so the tensor core
+//               works for one tile while the other tile's softmax runs:
+//                 S_A(0), S_B(0), then per key block j:
+//                 O_A += P_A(j) Vt_j, S_A(j+1), O_B += P_B(j) Vt_j, S_B(j+1)
+//               S = Q K_j^T (M=128, N=128, K=D, both from shared memory) goes to the tile's
+//               TMEM S columns; P (bf16 pairs) overwrites the first 64 of them and is the A
+//               operand of P.Vt read straight from TMEM; O accumulates in TMEM.  S(j+1) is
+//               issued once P(j).Vt_j has retired (it overwrites P(j)).
+//   warp 3      idle (completes the first warpgroup, which runs on 64 registers per thread)
+//   warps 4-7   softmax of tile A, warps 8-11 of tile B (216 registers per thread); warp w
+//               reads TMEM lanes 32*(w%4)..,
+//               one thread per query row:
+//               the block's 128 scores in registers (one TMEM load round trip); row max of
+//               t = S*log2(e)/sqrt(D) + key_bias_log2; running max m raised only when the
+//               block exceeds it by more than 2^8 (then O is rescaled in TMEM: rare);
+//               P = 2^(t - m) (ex2.approx) written as bf16 pairs over the S columns; l += sum P.
+//               At the end O / l is written in the caller's layout.
+// TMEM: tile t at columns [256t, 256t+128) S/P and [256t+128, +D) O: 512 columns.
+// Barriers: q_full; k_full[3], k_empty[3] (commit after S_B(j)); v_full[2], v_empty[2]
+// (commit after P_B(j).Vt_j); per tile s_full (commit after S), p_full (4 softmax warps),
+// pv_done (commit after P.Vt).  Every wait is bounded; on timeout the kernel records the error
+// word and winds down.
+constexpr int kFaThreads = 384;  // 3 warpgroups
+// Registers: launched at 168 per thread (64,512 per CTA); the producer/MMA warpgroup gives
+// most of its share to the two softmax warpgroups, which hold a 128-key row in registers:
+// 4 x 32 x 64 + 8 x 32 x 216 = 63,488 <= 64,512.
+constexpr int kFaRegsIdle = 64;
+constexpr int kFaRegsSoftmax = 216;
+static_assert(4 * 32 * kFaRegsIdle + 8 * 32 * kFaRegsSoftmax <= kFaThreads * 168, "register split");
+constexpr int kFaRows = 128;    // queries per tile
+constexpr int kFaTiles = 2;     // query tiles per CTA
+constexpr int kFaKeys = 128;    // keys per block
+constexpr int kFaKStages = 3;
+constexpr int kFaVStages = 2;
 constexpr uint32_t kFaBox = 128 * 128;  // bytes of one 128-row x 128-byte swizzled box
 constexpr float kFaRescaleLog2 = 8.0f;
 
 template <int D>
 struct FaLayout {
-  static constexpr uint32_t kQBytes = kFaRows * D * 2;   // D/64 boxes
-  static constexpr uint32_t kKBytes = kFaKeys * D * 2;   // D/64 boxes
-  static constexpr uint32_t kVBytes = D * kFaKeys * 2;   // 2 boxes of D rows x 64 keys
-  static constexpr uint32_t kVBox = D * 128;             // one D-row x 64-key box
+  static constexpr uint32_t kQTileBytes = kFaRows * D * 2;  // D/64 boxes
+  static constexpr uint32_t kKBytes = kFaKeys * D * 2;      // D/64 boxes
+  static constexpr uint32_t kVBytes = D * kFaKeys * 2;      // 2 boxes of D rows x 64 keys
+  static constexpr uint32_t kVBox = D * 128;                // one D-row x 64-key box
   static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kK = kQ + kQBytes;
-  static constexpr uint32_t kV = kK + kFaStages * kKBytes;
-  static constexpr uint32_t kRed = kV + kFaStages * kVBytes;  // uint16 [2 parity][2 half][128 rows]
-  static constexpr uint32_t kBars = kRed + 2 * 2 * kFaRows * 2;
+  static constexpr uint32_t kK = kQ + kFaTiles * kQTileBytes;
+  static constexpr uint32_t kV = kK + kFaKStages * kKBytes;
+  static constexpr uint32_t kBars = kV + kFaVStages * kVBytes;
   static constexpr uint32_t kSmem = 1024 + kBars + 256;
-  static constexpr uint32_t kO = kFaStages * kFaKeys;   // TMEM: S/P buffers [0, 384), O [384, 384+D)
   static constexpr uint32_t kTmemCols = 512;
 };
 
@@ -228,41 +236,44 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const FaParams p) {
   using Ly = FaLayout<D>;
-  constexpr int S3 = kFaStages;
+  constexpr int KS = kFaKStages, VS = kFaVStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + Ly::kQ;
   uint8_t* sK = smem + Ly::kK;
   uint8_t* sV = smem + Ly::kV;
-  uint16_t* red = reinterpret_cast<uint16_t*>(smem + Ly::kRed);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Ly::kBars);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
-  uint64_t* v_full = k_full + S3;
-  uint64_t* k_empty = v_full + S3;
-  uint64_t* v_empty = k_empty + S3;
-  uint64_t* s_full = v_empty + S3;
-  uint64_t* p_full = s_full + S3;
-  uint64_t* p_empty = p_full + S3;
-  uint64_t* drain_bar = p_empty + S3;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;     // [tile]
+  uint64_t* p_full = s_full + kFaTiles;
+  uint64_t* pv_done = p_full + kFaTiles;
+  uint64_t* drain_bar = pv_done + kFaTiles;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qtile = blockIdx.x;
+  const int qpair = blockIdx.x;
   const int head = blockIdx.y;
   const int nkb = p.num_kb;
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < S3; ++i) {
+    for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&v_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
+      mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 8);
-      mbar_init(&p_empty[i], 1);
+    }
+    for (int t = 0; t < kFaTiles; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);
+      mbar_init(&pv_done[t], 1);
     }
     mbar_init(drain_bar, 1);
     fence_mbar_init();
@@ -279,23 +290,30 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 10) {
+  if (warp < 4) {
+   regs_dec<kFaRegsIdle>();
+   if (warp == 0 || warp == 2) {
     // ------------------------------------------------------------ TMA producers
     if (lane == 0) {
       const bool is_k = warp == 0;
-      const uint64_t shared_kv = policy_evict_last();  // K/V tiles are read by every query tile
+      const uint64_t shared_kv = policy_evict_last();  // K/V tiles are read by every query pair
+      const int stages = is_k ? KS : VS;
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       if (is_k) {
-        mbar_arrive_expect_tx(q_full, Ly::kQBytes);
+        mbar_arrive_expect_tx(q_full, kFaTiles * Ly::kQTileBytes);
+        const uint64_t once = policy_evict_first();
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c)
-          tma_load_3d(sQ + c * kFaBox, &tmQ, q_full, c * 64, qtile * kFaRows, head, policy_evict_first());
+        for (int t = 0; t < kFaTiles; ++t)
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sQ + t * Ly::kQTileBytes + c * kFaBox, &tmQ, q_full, c * 64,
+                        (qpair * kFaTiles + t) * kFaRows, head, once);
       }
       int issued = 0;
       for (int j = 0; j < nkb; ++j) {
-        const int st = j % S3;
-        if (!mbar_wait(&empty[st], ((j / S3) & 1) ^ 1u, p.err, kErrWaitProducer)) break;
+        const int st = j % stages;
+        if (!mbar_wait(&empty[st], ((j / stages) & 1) ^ 1u, p.err, kErrWaitProducer)) break;
         if (is_k) {
           mbar_arrive_expect_tx(&full[st], Ly::kKBytes);
 #pragma unroll
@@ -313,8 +331,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       // Let this thread's copies land before the CTA's shared memory goes away (they have,
       // unless another role gave up early).
       if (is_k) mbar_wait_drain(q_full, 0);
-      for (int j = issued - S3 < 0 ? 0 : issued - S3; j < issued; ++j)
-        mbar_wait_drain(&full[j % S3], (j / S3) & 1);
+      for (int j = issued - stages < 0 ? 0 : issued - stages; j < issued; ++j)
+        mbar_wait_drain(&full[j % stages], (j / stages) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -322,182 +340,157 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       constexpr uint32_t idesc_s = idesc_make(kFmtBF16, kFaRows, kFaKeys);
       constexpr uint32_t idesc_o = idesc_make(kFmtBF16, kFaRows, D);
       bool ok = mbar_wait(q_full, 0, p.err, kErrWaitMma);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % S3, sb = j % S3;
-        if (!mbar_wait(&k_full[st], (j / S3) & 1, p.err, kErrWaitMma)) return false;
-        // TMEM buffer sb was last used by P_{j-3}.Vt_{j-3}
-        if (!mbar_wait(&p_empty[sb], ((j / S3) & 1) ^ 1u, p.err, kErrWaitMma)) return false;
-        tc_fence_after();
-        const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK + st * Ly::kKBytes);
+      auto issue_s = [&](int t, int j) {  // K_j is loaded
+        const uint32_t q0 = smem_u32(sQ + t * Ly::kQTileBytes), k0 = smem_u32(sK + (j % KS) * Ly::kKBytes);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            umma_f16(tmem + sb * kFaKeys, smem_desc_k_sw128(q0 + c * kFaBox + k * 32),
+            umma_f16(tmem + t * 256, smem_desc_k_sw128(q0 + c * kFaBox + k * 32),
                      smem_desc_k_sw128(k0 + c * kFaBox + k * 32), idesc_s, (c | k) != 0 ? 1u : 0u);
-        umma_commit(&s_full[sb]);
-        umma_commit(&k_empty[st]);  // K_j read: the producer may load K_{j+3}
-        return true;
+        umma_commit(&s_full[t]);
+        if (t == kFaTiles - 1) umma_commit(&k_empty[j % KS]);  // both tiles have read K_j
       };
       if (ok) {
         tc_fence_after();
-        ok = issue_s(0);
-        if (ok && nkb > 1) ok = issue_s(1);
+        ok = mbar_wait(&k_full[0], 0, p.err, kErrWaitMma);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < kFaTiles; ++t) issue_s(t, 0);
+        }
       }
       for (int j = 0; j < nkb && ok; ++j) {
-        if (j + 2 < nkb && !(ok = issue_s(j + 2))) break;
-        const int pb = j % S3, st = j % S3;
-        if (!(ok = mbar_wait(&p_full[pb], (j / S3) & 1, p.err, kErrWaitMma))) break;
-        if (!(ok = mbar_wait(&v_full[st], (j / S3) & 1, p.err, kErrWaitMma))) break;
-        tc_fence_after();
-        const uint32_t v0 = smem_u32(sV + st * Ly::kVBytes);
+        const int vs = j % VS;
+        for (int t = 0; t < kFaTiles && ok; ++t) {
+          if (!(ok = mbar_wait(&p_full[t], j & 1, p.err, kErrWaitMma))) break;
+          if (t == 0 && !(ok = mbar_wait(&v_full[vs], (j / VS) & 1, p.err, kErrWaitMma))) break;
+          tc_fence_after();
+          const uint32_t v0 = smem_u32(sV + vs * Ly::kVBytes);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., Vt box k/4, 32-byte step k%4
-          umma_f16_ts(tmem + Ly::kO, tmem + pb * kFaKeys + 8 * k,
-                      smem_desc_k_sw128(v0 + (k >> 2) * Ly::kVBox + (k & 3) * 32), idesc_o,
-                      (j | k) != 0 ? 1u : 0u);
-        umma_commit(&v_empty[st]);
-        umma_commit(&p_empty[pb]);
+          for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., Vt box k/4, 32-byte step k%4
+            umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k,
+                        smem_desc_k_sw128(v0 + (k >> 2) * Ly::kVBox + (k & 3) * 32), idesc_o,
+                        (j | k) != 0 ? 1u : 0u);
+          umma_commit(&pv_done[t]);
+          if (t == kFaTiles - 1) umma_commit(&v_empty[vs]);  // both tiles have read Vt_j
+          if (j + 1 < nkb) {
+            if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, p.err, kErrWaitMma))) break;
+            // S(j+1) overwrites P(j): wait until P(j).Vt_j has retired.
+            if (!(ok = mbar_wait(&pv_done[t], j & 1, p.err, kErrWaitMma))) break;
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+        }
       }
       if (!ok) {
         umma_commit(drain_bar);  // MMAs already issued retire before TMEM is released
         mbar_wait_drain(drain_bar, 0);
       }
     }
+   }
   } else {
-    // ------------------------------------------------------------ softmax (warps 2..9)
+    regs_inc<kFaRegsSoftmax>();
+    // ------------------------------------------------------------ softmax (warps 4..11)
+    const int t = (warp - 4) >> 2;            // query tile
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;         // which 64 keys of each block, which half of O
     const int row = quarter * 32 + lane;
-    const uint32_t bar_id = 1 + quarter;      // the two warps of this row group (64 threads)
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    constexpr int kOHalf = D / 2;             // O columns per warp
-    float m_used = -INFINITY, l_part = 0.f;
+    const uint32_t sbase = tmem + t * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t obase = sbase + 128;
+    float m_used = -INFINITY, l_sum = 0.f;
     bool good = true;
-    for (int j = 0; j < nkb; ++j) {
-      const int sb = j % S3;
+    for (int j = 0; j < nkb && good; ++j) {
       const bool biased = __ldg(p.bias_flags + j) != 0;  // issued before the wait hides its latency
-      good = __all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j / S3) & 1, p.err, kErrWaitEpilogue)) && good;
+      const float* bias = p.bias_log2 + j * kFaKeys;
+      good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
+      if (!good) break;
       tc_fence_after();
-      uint32_t r[2][32];
-      tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + half * 64, r[0]);
-      tmem_ld_32x32b_x32(lane_base + sb * kFaKeys + half * 64 + 32, r[1]);
-      tmem_wait_ld();
-
-      // u = raw score (unmasked block: p = 2^(u*scale - m)) or scaled score + bias (p = 2^(u - m))
-      const float ua = biased ? 1.f : p.scale_log2;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // independent max chains
-      if (biased) {
-        const float* bias = p.bias_log2 + j * kFaKeys + half * 64;
+      // The whole 128-key row in registers: one TMEM round trip per block.  u = raw score
+      // (unmasked block: P = 2^(u*scale - m)) or, for blocks with masked keys, scaled score
+      // + bias folded in place (P = 2^(u - m)).
+      uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(sbase + c * 32, r[c]);
+      tmem_wait_ld();
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (biased) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + c * 32 + i));
-            const float t0 = fmaf(__uint_as_float(r[c][i]), p.scale_log2, bb.x);
-            const float t1 = fmaf(__uint_as_float(r[c][i + 1]), p.scale_log2, bb.y);
-            const float t2 = fmaf(__uint_as_float(r[c][i + 2]), p.scale_log2, bb.z);
-            const float t3 = fmaf(__uint_as_float(r[c][i + 3]), p.scale_log2, bb.w);
-            r[c][i] = __float_as_uint(t0);
-            r[c][i + 1] = __float_as_uint(t1);
-            r[c][i + 2] = __float_as_uint(t2);
-            r[c][i + 3] = __float_as_uint(t3);
-            mx4[0] = fmaxf(mx4[0], t0);
-            mx4[1] = fmaxf(mx4[1], t1);
-            mx4[2] = fmaxf(mx4[2], t2);
-            mx4[3] = fmaxf(mx4[3], t3);
+            const float b4[4] = {bb.x, bb.y, bb.z, bb.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float u = fmaf(__uint_as_float(r[c][i + q]), p.scale_log2, b4[q]);
+              r[c][i + q] = __float_as_uint(u);
+              mx4[q] = fmaxf(mx4[q], u);
+            }
           }
       } else {
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            mx4[0] = fmaxf(mx4[0], __uint_as_float(r[c][i]));
-            mx4[1] = fmaxf(mx4[1], __uint_as_float(r[c][i + 1]));
-            mx4[2] = fmaxf(mx4[2], __uint_as_float(r[c][i + 2]));
-            mx4[3] = fmaxf(mx4[3], __uint_as_float(r[c][i + 3]));
-          }
+          for (int i = 0; i < 32; i += 4)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) mx4[q] = fmaxf(mx4[q], __uint_as_float(r[c][i + q]));
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       if (!biased) mx *= p.scale_log2;  // scale > 0: the max commutes with it
-      // Row max over both halves of the block, each half rounded to bf16 towards +inf (the
-      // same value in both warps, never below the true max).  The AND of `good` gives both
-      // warps of the row group one decision to stop (neither can then wait alone here).  The
-      // barrier also orders both warps' S loads before either overwrites columns with P.
-      uint32_t mb = __float_as_uint(mx);
-      if (!(mb & 0x80000000u)) mb += 0xFFFFu;
-      mb >>= 16;
-      red[(j & 1) * 256 + half * 128 + row] = static_cast<uint16_t>(mb);
-      tc_fence_before();
-      if (!named_bar_all(bar_id, 64, good)) break;
-      tc_fence_after();
-      const uint32_t ob = red[(j & 1) * 256 + (1 - half) * 128 + row];
-      mx = fmaxf(__uint_as_float(mb << 16), __uint_as_float(ob << 16));
-
-      // Raise the running max only when this block exceeds it by more than a factor 2^8.
       const bool raise = mx > m_used + kFaRescaleLog2;
       const float alpha = raise ? fast_exp2(m_used - mx) : 1.f;  // 2^-inf = 0 on the first raise
       if (raise) m_used = mx;
       if (__any_sync(0xffffffffu, raise && j > 0)) {
-        // O holds blocks < j: wait for P_{j-1}.Vt_{j-1}, then scale this warp's half of the row.
-        const int jp = j - 1;
-        good = __all_sync(0xffffffffu, mbar_wait(&p_empty[jp % S3], (jp / S3) & 1, p.err, kErrWaitEpilogue)) && good;
-        if (good) {
-          tc_fence_after();
+        // O holds blocks < j: wait for P(j-1).Vt_{j-1}, then scale this row of O.
+        good = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (j - 1) & 1, p.err, kErrWaitEpilogue));
+        if (!good) break;
+        tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < kOHalf / 32; ++c) {
-            uint32_t o[32];
-            const uint32_t oaddr = lane_base + Ly::kO + half * kOHalf + c * 32;
-            tmem_ld_32x32b_x32(oaddr, o);
-            tmem_wait_ld();
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(obase + c * 32, o);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_32x32b_x32(oaddr, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(obase + c * 32, o);
         }
       }
-      l_part *= alpha;
-      if (!good) continue;  // stop feeding the MMA warp; the next barrier ends the loop
+      l_sum *= alpha;
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
-
-      // P_j: this warp's 64 keys as 32 columns of bf16 pairs over S_j's columns [half*32, +32).
-      uint32_t pk[32];
-      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent sum chains
+      // P chunk by chunk from the registers: keys 32c..32c+31 become bf16 pairs in columns
+      // 16c..16c+15 (S has been read in full above).
+      const float ua = biased ? 1.f : p.scale_log2;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        const float e0 = fast_exp2(fmaf(__uint_as_float(r[i >> 5][i & 31]), ua, neg_m));
-        const float e1 = fast_exp2(fmaf(__uint_as_float(r[i >> 5][(i & 31) + 1]), ua, neg_m));
-        ls[(i >> 1) & 7] += e0 + e1;
-        __nv_bfloat162 h = __floats2bfloat162_rn(e0, e1);
-        pk[i >> 1] = *reinterpret_cast<uint32_t*>(&h);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float e0 = fast_exp2(fmaf(__uint_as_float(r[c][i]), ua, neg_m));
+          const float e1 = fast_exp2(fmaf(__uint_as_float(r[c][i + 1]), ua, neg_m));
+          ls[(i >> 1) & 3] += e0 + e1;
+          __nv_bfloat162 hh = __floats2bfloat162_rn(e0, e1);
+          pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
+        }
+        tmem_st_32x32b_x16(sbase + c * 16, pk);
       }
-      tmem_st_32x32b_x32(lane_base + sb * kFaKeys + half * 32, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sb]);
-      l_part += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      if (lane == 0) mbar_arrive(&p_full[t]);
+      l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
     }
-    // Final: wait for the last P.Vt, combine the two halves' row sums, write O / l.
-    const int jl = nkb - 1;
+    // Final: wait for the last P.Vt of this tile, write O / l.
     if (good)
-      good = __all_sync(0xffffffffu, mbar_wait(&p_empty[jl % S3], (jl / S3) & 1, p.err, kErrWaitEpilogue));
-    // Row sums meet in the Vt stages, dead once the last P.Vt has retired (when good).
-    float* lsum = reinterpret_cast<float*>(sV);
+      good = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (nkb - 1) & 1, p.err, kErrWaitEpilogue));
     if (good) {
-      fence_proxy_async_smem();
-      lsum[half * 128 + row] = l_part;
-    }
-    if (named_bar_all(bar_id, 64, good)) {
       tc_fence_after();
-      const float l_sum = l_part + lsum[(1 - half) * 128 + row];
-      const int q = qtile * kFaRows + row;
+      const int q = (qpair * kFaTiles + t) * kFaRows + row;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const long long col0 = static_cast<long long>(head) * D + half * kOHalf;
+      const long long col0 = static_cast<long long>(head) * D;
 #pragma unroll
-      for (int c = 0; c < kOHalf / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
-        tmem_ld_32x32b_x32(lane_base + Ly::kO + half * kOHalf + c * 32, o);
+        tmem_ld_32x32b_x32(obase + c * 32, o);
         tmem_wait_ld();
         if (q < p.L) {
           if (p.out_bf16) {
@@ -550,7 +543,7 @@ b2g_status launch_flash(const __nv_bfloat16* qb, const __nv_bfloat16* kb, const 
                                            static_cast<int>(smem)),
                       "cudaFuncSetAttribute(flash_attn)")) != B2G_OK)
     return s;
-  const dim3 grid(static_cast<unsigned>((L + kFaRows - 1) / kFaRows), static_cast<unsigned>(H));
+  const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows)), static_cast<unsigned>(H));
   flash_attn_kernel<D><<<grid, kFaThreads, smem, st>>>(tq, tk, tv, fp);
   note_launch();
   return check_cuda(cudaGetLastError(), "flash_attn launch");
