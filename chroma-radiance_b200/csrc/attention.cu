@@ -23,7 +23,7 @@ namespace b2g {
 namespace {
 
 // Attention prologue, one launch, work items in three ranges of blocks (256 threads each):
-//   [0, n_rows)            Q then K rows: each warp 4 (token l, head h) rows of D values:
+//   [0, n_rows)            Q then K rows: each warp 2 (token l, head h) rows of D values:
 //                          RMSNorm with a learned scale (rms_norm, kernels.cu:174-207, as
 //                          qk_norm applies it, chroma.cuh:513-515; rows l >= norm_split use the
 //                          second scale set), RoPE with pe row l = D/2 groups of (cos, -sin,
@@ -46,12 +46,19 @@ struct PrepArgs {
   __nv_bfloat16* vt;        // [H*D, L]
   const float* bias;        // may be NULL
   float* bias_log2;         // [padded]
-  int* bias_flags;          // [padded / 128]: 1 when any value of the 128-key block is nonzero
+  int* bias_flags;          // [padded / 128][8]: kind, 3 unused, 4 mask words (see kBiasMask)
   int L, H, padded;
   int rows_blocks, vt_cols_tiles, vt_blocks;
 };
 
-constexpr int kRowsPerWarp = 4;
+constexpr int kRowsPerWarp = 2;
+
+// Per 128-key block the prologue records what its key bias holds: kind (bit 0: some keys are
+// -inf, i.e. masked; bit 1: some other nonzero value) and, for bit 0, a 128-bit mask of the
+// -inf keys (word c, bit i = key 32c+i).  Unmasked blocks skip the bias; blocks that are only
+// a 0/-inf mask (the key padding mask) apply it with one select per score.
+constexpr int kBiasMask = 1, kBiasGeneral = 2;
+constexpr int kBiasRec = 8;  // ints per block record
 
 // kRowsPerWarp Q or K rows (token l, head h) of D values starting at `row0`: RMSNorm, RoPE,
 // bf16 (see attn_prep_kernel).  All rows' loads are issued before any arithmetic.
@@ -89,6 +96,14 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
     const int w = which[rr];
     const float* norm = l[rr] < a.norm_split ? a.norm1[w] : a.norm2[w];
     if (norm) {
+      float nv[kPerLane];
+      if constexpr (kPerLane == 4) {
+        const float4 t4 = __ldg(reinterpret_cast<const float4*>(norm) + lane);
+        nv[0] = t4.x; nv[1] = t4.y; nv[2] = t4.z; nv[3] = t4.w;
+      } else {
+        const float2 t2 = __ldg(reinterpret_cast<const float2*>(norm) + lane);
+        nv[0] = t2.x; nv[1] = t2.y;
+      }
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < kPerLane; ++i) ss += v[rr][i] * v[rr][i];
@@ -96,7 +111,7 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float inv = rsqrtf(ss / static_cast<float>(D) + a.eps);
 #pragma unroll
-      for (int i = 0; i < kPerLane; ++i) v[rr][i] = v[rr][i] * inv * __ldg(norm + lane * kPerLane + i);
+      for (int i = 0; i < kPerLane; ++i) v[rr][i] = v[rr][i] * inv * nv[i];
     }
     // pair p = lane*kPerLane/2 + i rotates (v[2i], v[2i+1]) by pe row l, group p.
     uint32_t packed[kPerLane / 2];
@@ -152,12 +167,18 @@ __global__ void __launch_bounds__(256, 4) attn_prep_kernel(const PrepArgs a) {
     }
     return;
   }
-  for (int k = threadIdx.x; k < a.padded / 128; k += blockDim.x) a.bias_flags[k] = 0;
+  for (int k = threadIdx.x; k < a.padded / 128 * kBiasRec; k += blockDim.x) a.bias_flags[k] = 0;
   __syncthreads();
   for (int k = threadIdx.x; k < a.padded; k += blockDim.x) {
     const float v = k < a.L ? (a.bias ? a.bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
     a.bias_log2[k] = v;
-    if (v != 0.f) atomicOr(a.bias_flags + k / 128, 1);
+    int* rec = a.bias_flags + (k / 128) * kBiasRec;
+    if (v == -INFINITY) {
+      atomicOr(rec, kBiasMask);
+      atomicOr(rec + 4 + (k % 128) / 32, static_cast<int>(1u << (k % 32)));
+    } else if (v != 0.f) {
+      atomicOr(rec, kBiasGeneral);
+    }
   }
 }
 
@@ -224,7 +245,7 @@ struct FaParams {
   int num_kb;             // key blocks of 128
   float scale_log2;       // log2(e) / sqrt(D)
   const float* bias_log2; // [num_kb * 128]
-  const int* bias_flags;  // [num_kb]: 0 when the block's 128 bias values are all zero
+  const int* bias_flags;  // [num_kb][kBiasRec]: kind and -inf mask of each 128-key block
   void* out;
   long long ldo;
   int out_bf16;
@@ -399,14 +420,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     float m_used = -INFINITY, l_sum = 0.f;
     bool good = true;
     for (int j = 0; j < nkb && good; ++j) {
-      const bool biased = __ldg(p.bias_flags + j) != 0;  // issued before the wait hides its latency
+      // issued before the wait hides their latency
+      const int kind = __ldg(p.bias_flags + j * kBiasRec);
+      const uint4 mw = __ldg(reinterpret_cast<const uint4*>(p.bias_flags + j * kBiasRec + 4));
+      const bool biased = (kind & kBiasGeneral) != 0;
       const float* bias = p.bias_log2 + j * kFaKeys;
       good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
       if (!good) break;
       tc_fence_after();
       // The whole 128-key row in registers: one TMEM round trip per block.  u = raw score
-      // (unmasked block: P = 2^(u*scale - m)) or, for blocks with masked keys, scaled score
-      // + bias folded in place (P = 2^(u - m)).
+      // (P = 2^(u*scale - m); masked keys set to -inf, giving P = 0) or, for a block with a
+      // general bias, scaled score + bias folded in place (P = 2^(u - m)).
       uint32_t r[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(sbase + c * 32, r[c]);
@@ -427,6 +451,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             }
           }
       } else {
+        if (kind & kBiasMask) {
+          const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if ((words[c] >> i) & 1u) r[c][i] = 0xFF800000u;  // -inf
+        }
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -576,7 +608,7 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   const size_t qk_bytes = static_cast<size_t>(round_up(L * HD * 2, 256));
   const size_t vt_bytes = static_cast<size_t>(round_up(HD * L * 2, 256));
   const size_t bias_bytes = static_cast<size_t>(round_up(nkb * kFaKeys * 4, 256));
-  const size_t flag_bytes = static_cast<size_t>(round_up(nkb * 4, 256));
+  const size_t flag_bytes = static_cast<size_t>(round_up(nkb * kBiasRec * 4, 256));
   void* ws = nullptr;
   if ((s = workspace_get(2 * qk_bytes + vt_bytes + bias_bytes + flag_bytes, &ws, kWsAttention)) != B2G_OK) return s;
   char* base = static_cast<char*>(ws);

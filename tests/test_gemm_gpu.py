@@ -485,6 +485,24 @@ def test_attention_qknorm_rope_vs_oracle(engine, oracle, L, H, D, split, out_bf1
     assert rel_err(got, want) < 1e-2
 
 
+@pytest.mark.parametrize("L,H,D", [(136, 2, 128), (320, 3, 64)])
+def test_attention_general_key_bias(engine, oracle, L, H, D):
+    """A key bias with arbitrary finite values (not only the 0/-inf padding mask) and some
+    -inf keys: the kernel's general-bias path against the oracle's additive bias."""
+    g = torch.Generator().manual_seed(L + D)
+    Q, K, V = (torch.randn((L, H, D), generator=g) for _ in range(3))
+    pe = rope_table(L, D, 2 * L)
+    bias = (torch.randn(L, generator=g) * 2.0).numpy().astype(np.float32)
+    bias[7:19] = -np.inf
+    out = engine.attention_with_rope(Q.to(DEV), K.to(DEV), V.to(DEV), torch.from_numpy(pe).to(DEV), H, D,
+                                     torch.from_numpy(bias).to(DEV))
+    want = oracle.attention_rope(Q.numpy(), K.numpy(), V.numpy(), pe, bias)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) < 1e-2
+
+
 def attn_ref_or_skip():
     from oracle import ATTN_REF_PATH, AttnRef
 
