@@ -601,10 +601,21 @@ def run_engine_config4(args) -> None:
     mask[T - MASKED:T] = float("-inf")
     scratch = tp.TPScratch(T, I, world, dev)
     ops = tp.EngineOps()
+    fused = world > 1 and args.tp_comm == "fused"
+    if fused:
+        comm = tp.SymmetricComm(L, H, None, dev)
+        comm.res_double[:T].copy_(res["txt"])
+        comm.res_double[T:].copy_(res["img"])
+        comm.res_single.copy_(res["x"])
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step():
+        if fused:
+            tp.tp_double_block_fused(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"],
+                                     act["img_mod2"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
+            tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gt[4], pe, mask, scratch)
+            return
         tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
                            res["txt"], res["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
         tp.tp_single_block(ops, ts, act["x_mod"], res["x"], gt[4], pe, mask, scratch)
@@ -646,6 +657,8 @@ def run_engine_config4(args) -> None:
         "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox generator, seed 0)",
         "config": {"workload": WORKLOAD4, "flop_per_step": lin + att, "parallelism": f"tp{world}",
+                   "tp_comm": ("reduction fused into the row-split GEMMs over NVLink peer memory" if fused else
+                               "NCCL bf16 all-reduce" if world > 1 else "none"),
                    "allreduce_bytes_per_step": 3 * L * H * 2 if world > 1 else 0,
                    "l2": "256 MB buffer written before every step, outside the events"},
         "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peaks["bf16_tflops"],
@@ -669,6 +682,8 @@ def main():
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
     ap.add_argument("--workload", choices=["config2", "config1", "config4"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",
+                    help="config4: reduction of the row-split layers (fused into the GEMM, or NCCL)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

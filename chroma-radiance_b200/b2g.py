@@ -54,6 +54,17 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class TpReduceDesc(ctypes.Structure):
+    """Mirror of b2g_tp_reduce_desc."""
+
+    _fields_ = [
+        ("world", ctypes.c_int), ("rank", ctypes.c_int),
+        ("part_ptrs", ctypes.c_void_p), ("res_ptrs", ctypes.c_void_p),
+        ("ld_part", ctypes.c_int64), ("ld_res", ctypes.c_int64),
+        ("counters", ctypes.c_void_p), ("counter_slots", ctypes.c_int64),
+    ]
+
+
 _lib = None
 
 # Exported symbols of libb2g.so with their ctypes signatures (status-returning unless noted).
@@ -68,6 +79,10 @@ _SIGNATURES = {
                                                                                    ctypes.c_void_p, ctypes.c_void_p],
                           ctypes.c_int),
     "b2g_gemm_fp8": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "b2g_gemm_tp_reduce": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int64), ctypes.c_int,
+                            ctypes.POINTER(TpReduceDesc), ctypes.c_void_p], ctypes.c_int),
+    "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
+                       ctypes.c_int),
     "b2g_bias_gated_residual": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
                                  ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -257,6 +272,43 @@ def gemm_fp8(x: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor, bias: tor
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_gemm_fp8(ctypes.byref(d), _ptr(x_scale), w_scale.data_ptr(), ctypes.c_void_p(s)))
     return out
+
+
+def gemm_tp_reduce(problems: list[dict], row0: list[int], tp: TpReduceDesc,
+                   stream: torch.cuda.Stream | None = None) -> None:
+    """Row-split layer with the tensor-parallel reduction fused in (b2g_gemm_tp_reduce):
+    problems = [dict(x=, w=, bias=, gate=)] (this rank's K-slice), row0 = their first rows in
+    the peer-mapped partial / residual buffers described by `tp`."""
+    lib = load()
+    descs = []
+    for pr in problems:
+        x, w = pr["x"], pr["w"]
+        _require_cuda(x, w, pr.get("bias"), pr["gate"])
+        if x.dim() != 2 or w.dim() != 2 or x.stride(1) != 1 or w.stride(1) != 1 or w.shape[1] != x.shape[1]:
+            raise B2GError("gemm_tp_reduce: 2-D x [M, K] and w [N, K] with unit stride along K expected")
+        d = GemmDesc()
+        d.M, d.K, d.N = x.shape[0], x.shape[1], w.shape[0]
+        d.a, d.a_dtype, d.lda = x.data_ptr(), _TORCH_TO_B2G[x.dtype], x.stride(0) if x.shape[0] > 1 else x.shape[1]
+        d.b, d.b_dtype, d.ldb = w.data_ptr(), _TORCH_TO_B2G[w.dtype], w.stride(0)
+        d.bias = _ptr(pr.get("bias"))
+        d.bias_dtype = F32
+        d.d, d.d_dtype, d.ldd = None, F32, d.N
+        d.epilogue = EPI_GATED_RESIDUAL
+        d.gate = pr["gate"].data_ptr()
+        descs.append(d)
+    arr = (GemmDesc * len(descs))(*descs)
+    rows = (ctypes.c_int64 * len(row0))(*row0)
+    s = (stream or torch.cuda.current_stream(problems[0]["x"].device)).cuda_stream
+    _check(lib.b2g_gemm_tp_reduce(arr, rows, len(descs), ctypes.byref(tp), ctypes.c_void_p(s)))
+
+
+def tp_barrier(flag_ptrs: torch.Tensor, own_flags: torch.Tensor, world: int, rank: int, epoch: int,
+               stream: torch.cuda.Stream | None = None) -> None:
+    """Cross-rank barrier (b2g_tp_barrier): flag_ptrs an int64 CUDA tensor of every rank's flag
+    array address, own_flags this rank's int32 [world] array."""
+    lib = load()
+    s = (stream or torch.cuda.current_stream(own_flags.device)).cuda_stream
+    _check(lib.b2g_tp_barrier(flag_ptrs.data_ptr(), own_flags.data_ptr(), world, rank, epoch, ctypes.c_void_p(s)))
 
 
 def bias_gated_residual(y: torch.Tensor, bias: torch.Tensor | None, gate: torch.Tensor, residual: torch.Tensor,

@@ -259,6 +259,48 @@ b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
   return B2G_OK;
 }
 
+b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, int count,
+                              const b2g_tp_reduce_desc* tp, void* stream) {
+  if (!descs || !row0 || !tp || count < 1 || count > 2)
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_tp_reduce: 1 or 2 descriptors, row offsets and a tp descriptor");
+  GemmProblem ps[2];
+  TpReduce t;
+  t.world = tp->world; t.rank = tp->rank;
+  t.part_ptrs = tp->part_ptrs; t.res_ptrs = tp->res_ptrs;
+  t.ld_part = tp->ld_part; t.ld_res = tp->ld_res;
+  t.counters = tp->counters; t.counter_slots = tp->counter_slots;
+  for (int i = 0; i < count; ++i) {
+    const b2g_gemm_desc* d = descs + i;
+    if (d->M < 0 || d->N <= 0 || d->K <= 0) return set_error(B2G_ERR_INVALID, "b2g_gemm_tp_reduce: sizes");
+    if (!d->a || !d->b || !d->gate) return set_error(B2G_ERR_INVALID, "b2g_gemm_tp_reduce: null operand or gate");
+    if (d->lda < d->K || d->ldb < d->K) return set_error(B2G_ERR_INVALID, "b2g_gemm_tp_reduce: lda/ldb < K");
+    if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16))
+      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_tp_reduce: bf16 or fp16 operands of one type");
+    if (d->bias && d->bias_dtype != B2G_F32) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_tp_reduce: F32 bias");
+    GemmProblem& p = ps[i];
+    p.M = d->M; p.N = d->N; p.K = d->K;
+    p.a = d->a; p.a_dtype = d->a_dtype; p.lda = d->lda;
+    p.b = d->b; p.b_dtype = d->b_dtype; p.ldb = d->ldb;
+    p.bias = d->bias; p.bias_dtype = B2G_F32;
+    p.d = nullptr; p.d_dtype = B2G_F32; p.ldd = d->N;
+    p.epilogue = static_cast<b2g_epilogue>(kEpiTpReduce);
+    p.gate = d->gate;
+    p.tp = &t;
+    p.tp_row0 = row0[i];
+  }
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  for (int i = 0; i < count; ++i)
+    if (!tc_gemm_supported(ps[i], nullptr))
+      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_tp_reduce: operands not supported by the tensor-core path");
+  return tc_gemm_launch_group(ps, count, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream) {
+  return tp_barrier(flag_ptrs, own_flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
                              uint8_t* dst, int64_t dst_ld, float* scales, void* stream) {
   DeviceInfo* dev = nullptr;

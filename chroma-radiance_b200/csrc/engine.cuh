@@ -24,6 +24,22 @@ struct GemmProblem {
   // E4M3 operands: D = (sum_k A.B) * a_scale[m] * b_scale[n] + bias, before the epilogue.
   const float* a_scale = nullptr;
   const float* b_scale = nullptr;
+  // Tensor-parallel row-split layer (epilogue kEpiTpReduce): this rank's partial product is
+  // summed with the other ranks' over NVLink inside the GEMM, see TpReduce.
+  const struct TpReduce* tp = nullptr;
+  int64_t tp_row0 = 0;      // first row of this problem in the partial / residual buffers
+};
+
+// Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *
+// (sum + bias), the residual updated in every rank's copy.  All buffers are peer-mapped.
+constexpr int kEpiTpReduce = 3;
+struct TpReduce {
+  int world, rank;
+  void* const* part_ptrs;   // device array [world]: each rank's bf16 partial buffer [rows, ld_part]
+  float* const* res_ptrs;   // device array [world]: each rank's F32 residual copy [rows, ld_res]
+  int64_t ld_part, ld_res;
+  int* counters;            // rank 0's arrival counters (one per output tile slot), peer-mapped
+  int64_t counter_slots;    // capacity of `counters`
 };
 
 // Records a message for b2g_last_error() and returns `st`.
@@ -65,6 +81,9 @@ b2g_status quantize_rows_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows
 // (elementwise.cu); y BF16 or F32, bias may be NULL.
 b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias, const float* gate,
                                float* residual, int64_t ldr, int64_t M, int64_t N, cudaStream_t st);
+
+// Cross-rank barrier over peer-mapped flag arrays (tp_comm.cu), bounded wait.
+b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, cudaStream_t st);
 
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);

@@ -77,6 +77,7 @@ struct TcGroup {
   const float* gate;
   const float* a_scale;    // E4M3: per-row scale of A [M]
   const float* b_scale;    // E4M3: per-column scale of B [N]
+  long long tp_row0;       // tensor-parallel reduce: first row in the partial/residual buffers
 };
 
 // Tensor maps of every group (kernel parameter; indexed by group at run time).
@@ -100,6 +101,12 @@ struct TcParams {
   int* counters;           // split-K arrival counter per slot (zero between launches)
   int tma_store;           // 1: outputs leave through smem staging + TMA bulk tensor stores
   float alpha;             // accumulator scale before the bias (1 for every linear layer)
+  // tensor-parallel reduce epilogue (kEpiTpReduce)
+  int tp_world, tp_rank;
+  void* const* tp_part;    // [world] bf16 partial buffers
+  float* const* tp_res;    // [world] F32 residual copies
+  long long tp_ld_part, tp_ld_res;
+  int* tp_counters;        // rank 0's per-slot arrival counters (epoch counting, never reset)
   TcGroup g[kMaxGroups];
 };
 
@@ -336,6 +343,134 @@ __device__ __forceinline__ void scale_chunk(uint32_t (&r)[32], float rs, const f
   }
 }
 
+// Tensor-parallel row-split layer: this CTA's part of the tile leaves as a bf16 partial in this
+// rank's peer-mapped buffer; the CTA that completes the tile's count on rank 0 (the last of the
+// ranks to get there) sums all ranks' partials in rank order, adds the bias, and writes
+// residual + gate * sum into every rank's residual copy.  Stores are made visible system-wide
+// (__threadfence_system) before the arrival; peer data is read with .cv loads (not cached).
+template <int BN, typename Release>
+__device__ __forceinline__ void tp_epilogue_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, uint32_t tacc,
+                                                 Release release, int m, int n_base, int slot) {
+  constexpr int NCH = BN / 64;
+  const int c0 = e.half * NCH;
+  const bool row_ok = m < G.M;
+  const long long prow = G.tp_row0 + m;
+  uint16_t* part = static_cast<uint16_t*>(p.tp_part[p.tp_rank]);
+  uint32_t r[2][32];
+  tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    tmem_wait_ld();
+    if (i + 1 < NCH) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);
+    if (i == NCH - 1) release();
+    const int n0 = n_base + (c0 + i) * 32;
+    if (row_ok && n0 < p.N) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[i & 1][j]);
+      uint32_t packed[16];
+      pack16<OUT_BF16>(v, packed);
+      uint4* dst = reinterpret_cast<uint4*>(part + prow * p.tp_ld_part + n0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        dst[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+    }
+  }
+  __threadfence_system();
+  named_bar_sync(1, kEpiThreads);
+  if (threadIdx.x == 64) *e.bcast = atomicAdd_system(p.tp_counters + slot, 1);
+  named_bar_sync(1, kEpiThreads);
+  const int arrived = *e.bcast;
+  if (arrived % p.tp_world == p.tp_world - 1) {
+    // This CTA completes the tile: reduce its 128 rows x BN columns cooperatively.  Warp w of
+    // the 8 epilogue warps takes rows w, w+8, ..; lane l columns [8l, 8l+8) of the tile, so a
+    // warp reads 512 contiguous bytes of each rank's partial row and writes 1 KB of each
+    // rank's residual row; four rows' loads are in flight at once.
+    __threadfence_system();
+    const int et = static_cast<int>(threadIdx.x) - 64;
+    const int wq = et >> 5, ln = et & 31;
+    const int row_base = m - e.row;                       // first row of this CTA's tile part
+    const int ncol = min(BN, p.N - n_base);               // N % 32 == 0
+    const bool col_ok = ln * 8 < ncol;
+    const int n0 = n_base + ln * 8;
+    float bias8[8], gate8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bias8[j] = 0.f, gate8[j] = 0.f;
+    if (col_ok) {
+      if (p.bias_kind) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bias8[j] = e.sbias[ln * 8 + j];
+      }
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(G.gate + n0));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(G.gate + n0) + 1);
+      gate8[0] = g0.x; gate8[1] = g0.y; gate8[2] = g0.z; gate8[3] = g0.w;
+      gate8[4] = g1.x; gate8[5] = g1.y; gate8[6] = g1.z; gate8[7] = g1.w;
+    }
+    constexpr int kRowsInFlight = 4;
+#pragma unroll 1
+    for (int r0 = wq; r0 < 128; r0 += 8 * kRowsInFlight) {
+      float acc[kRowsInFlight][8];
+      float4 rv[kRowsInFlight][2];
+      bool ok[kRowsInFlight];
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        const int rr = r0 + u * 8;
+        ok[u] = col_ok && rr < 128 && row_base + rr < G.M;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[u][j] = 0.f;
+        rv[u][0] = rv[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        if (!ok[u]) continue;
+        const long long prow = G.tp_row0 + row_base + r0 + u * 8;
+        const float4* res = reinterpret_cast<const float4*>(p.tp_res[p.tp_rank] + prow * p.tp_ld_res + n0);
+        rv[u][0] = __ldcv(res);
+        rv[u][1] = __ldcv(res + 1);
+      }
+      for (int q = 0; q < p.tp_world; ++q) {  // fixed rank order: identical sums on every rank
+        uint4 pv[kRowsInFlight];
+#pragma unroll
+        for (int u = 0; u < kRowsInFlight; ++u) {
+          const long long prow = G.tp_row0 + row_base + r0 + u * 8;
+          if (ok[u])
+            pv[u] = __ldcv(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.tp_part[q]) +
+                                                          prow * p.tp_ld_part + n0));
+        }
+#pragma unroll
+        for (int u = 0; u < kRowsInFlight; ++u) {
+          if (!ok[u]) continue;
+          const uint32_t w[4] = {pv[u].x, pv[u].y, pv[u].z, pv[u].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            acc[u][2 * k] += __uint_as_float(w[k] << 16);
+            acc[u][2 * k + 1] += __uint_as_float(w[k] & 0xFFFF0000u);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kRowsInFlight; ++u) {
+        if (!ok[u]) continue;
+        const float4 o0 = make_float4(rv[u][0].x + gate8[0] * (acc[u][0] + bias8[0]),
+                                      rv[u][0].y + gate8[1] * (acc[u][1] + bias8[1]),
+                                      rv[u][0].z + gate8[2] * (acc[u][2] + bias8[2]),
+                                      rv[u][0].w + gate8[3] * (acc[u][3] + bias8[3]));
+        const float4 o1 = make_float4(rv[u][1].x + gate8[4] * (acc[u][4] + bias8[4]),
+                                      rv[u][1].y + gate8[5] * (acc[u][5] + bias8[5]),
+                                      rv[u][1].z + gate8[6] * (acc[u][6] + bias8[6]),
+                                      rv[u][1].w + gate8[7] * (acc[u][7] + bias8[7]));
+        const long long prow = G.tp_row0 + row_base + r0 + u * 8;
+        for (int q = 0; q < p.tp_world; ++q) {
+          float4* dst = reinterpret_cast<float4*>(p.tp_res[q] + prow * p.tp_ld_res + n0);
+          dst[0] = o0;
+          dst[1] = o1;
+        }
+      }
+    }
+  }
+  named_bar_sync(1, kEpiThreads);  // the broadcast word and staged bias are reused next item
+}
+
 // Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
 // accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
 // after this warp's last chunk is read.  With split-K, each split stores its raw fp32
@@ -345,6 +480,10 @@ template <int BN, int EPI, int OUT, int KIND, typename Release>
 __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
                                               uint32_t tacc, Release release, const CUtensorMap* tmD, int bz, int m,
                                               int n_base, int slot, int split) {
+  if constexpr (EPI == kEpiTpReduce) {
+    tp_epilogue_item<BN>(p, G, e, tacc, release, m, n_base, slot);
+    return;
+  }
   float rs = 0.f;  // E4M3: this row's activation scale
   if constexpr (KIND == 2) rs = m < G.M ? __ldg(G.a_scale + m) : 0.f;
   constexpr int NCH = BN / 64;  // 32-column chunks per warp (half of the tile's columns)
@@ -910,6 +1049,10 @@ b2g_status launch_one(const TcMaps& maps, const TcParams& prm, int grid, cudaStr
 template <bool PAIR, int BN, int STAGES, int KIND>
 b2g_status dispatch_out(const TcMaps& maps, const TcParams& prm, int grid, b2g_epilogue epi, b2g_dtype out,
                         cudaStream_t st) {
+  if constexpr (KIND == 0) {
+    if (static_cast<int>(epi) == kEpiTpReduce)
+      return launch_one<PAIR, BN, STAGES, kEpiTpReduce, OUT_F32, 0>(maps, prm, grid, st);
+  }
   if (epi == B2G_EPI_GATED_RESIDUAL)
     return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, KIND>(maps, prm, grid, st);
   if (epi == B2G_EPI_GELU) {
@@ -970,7 +1113,7 @@ bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
   return a.N == b.N && a.K == b.K && a.batch == 1 && b.batch == 1 && a.a_dtype == b.a_dtype &&
          a.b_dtype == b.b_dtype && a.d_dtype == b.d_dtype && a.epilogue == b.epilogue && a.alpha == b.alpha &&
          (a.bias == nullptr) == (b.bias == nullptr) && (!a.bias || a.bias_dtype == b.bias_dtype) &&
-         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr);
+         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr) && a.tp == b.tp;
 }
 
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) { return tc_gemm_launch_group(&p, 1, st); }
@@ -1027,7 +1170,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     if (g_force_splits <= 0) splits = 1;
   }
   if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
-  if (nkb == 0 || !p.allow_split) splits = 1;
+  if (nkb == 0 || !p.allow_split || p.tp) splits = 1;
   const bool pair = v == VPAIR;
   const int bn = v == V128 ? 128 : 256;
   const int tile_m = pair ? 256 : kBM;
@@ -1057,6 +1200,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     G.gate = q.gate;
     G.a_scale = q.a_scale;
     G.b_scale = q.b_scale;
+    G.tp_row0 = q.tp_row0;
     G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
                (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
     all_vec = all_vec && G.vec_ok;
@@ -1088,14 +1232,33 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   const uint32_t b_box = v == V256 ? 256u : 128u;
-  prm.tma_store = p.epilogue != B2G_EPI_GATED_RESIDUAL && all_vec && g_tma_store ? 1 : 0;
+  prm.tma_store = p.epilogue != B2G_EPI_GATED_RESIDUAL && all_vec && g_tma_store && !p.tp ? 1 : 0;
+  if (p.tp) {
+    const TpReduce& t = *p.tp;
+    if (kind != 0) return set_error(B2G_ERR_UNSUPPORTED, "tp reduce: bf16/fp16 operands only");
+    if (t.world < 1 || t.world > 8 || t.rank < 0 || t.rank >= t.world || !t.part_ptrs || !t.res_ptrs || !t.counters)
+      return set_error(B2G_ERR_INVALID, "tp reduce: world/rank/pointers");
+    if (p.N % 32 != 0 || t.ld_part % 8 != 0 || t.ld_res % 4 != 0 || t.ld_part < p.N || t.ld_res < p.N)
+      return set_error(B2G_ERR_UNSUPPORTED, "tp reduce: N % 32 and 16-byte partial / residual rows required");
+    if (static_cast<int64_t>(prm.num_tiles) * (pair ? 2 : 1) > t.counter_slots)
+      return set_error(B2G_ERR_INVALID, "tp reduce: not enough counter slots for this launch");
+    for (int i = 0; i < count; ++i)
+      if (!ps[i].gate) return set_error(B2G_ERR_INVALID, "tp reduce: a gate is required");
+    prm.tp_world = t.world;
+    prm.tp_rank = t.rank;
+    prm.tp_part = t.part_ptrs;
+    prm.tp_res = t.res_ptrs;
+    prm.tp_ld_part = t.ld_part;
+    prm.tp_ld_res = t.ld_res;
+    prm.tp_counters = t.counters;
+  }
   for (int i = 0; i < count; ++i) {
     const GemmProblem& q = ps[i];
     const int64_t a_bs = q.batch > 1 ? q.a_bstride : q.lda * q.M;
     const int64_t b_bs = q.batch > 1 ? q.b_bstride : q.ldb * q.N;
     if ((s = make_operand_map(&maps.a[i], q.a, q.a_dtype, q.K, q.M, q.lda, q.batch, a_bs, kBM)) != B2G_OK) return s;
     if ((s = make_operand_map(&maps.b[i], q.b, q.b_dtype, q.K, q.N, q.ldb, q.batch, b_bs, b_box)) != B2G_OK) return s;
-    if (prm.tma_store) {
+    if (prm.tma_store && q.d) {
       const int64_t d_bs = q.batch > 1 ? q.d_bstride : q.ldd * q.M;
       if ((s = make_output_map(&maps.d[i], q.d, q.d_dtype, q.N, q.M, q.ldd, q.batch, d_bs)) != B2G_OK) return s;
     }

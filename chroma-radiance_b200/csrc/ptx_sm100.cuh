@@ -12,6 +12,7 @@ enum : int {
   kErrWaitProducer = 1,   // TMA producer waited too long for a free smem stage
   kErrWaitMma = 2,        // MMA issuer waited too long for a filled stage / free accumulator
   kErrWaitEpilogue = 4,   // epilogue waited too long for a finished accumulator
+  kErrWaitTpBarrier = 8,  // a tensor-parallel barrier waited too long for another rank
 };
 
 // Upper bound on any single pipeline wait.  Legitimate waits are micro- to milliseconds.

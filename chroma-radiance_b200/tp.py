@@ -180,3 +180,98 @@ def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScra
     ops.gemm(s.cat, w.linear2_w, out=s.part)
     ops.all_reduce(s.part)
     ops.bias_gated_residual(s.part, w.linear2_b, gate, x)
+
+
+# ---------------------------------------------------------------------------- fused reduction
+class SymmetricComm:
+    """Peer-mapped (NVLink) buffers for the fused row-split layers (b2g_gemm_tp_reduce), made
+    with torch's symmetric memory: a bf16 partial buffer [rows, hidden], two replicated F32
+    residual copies (the double block's txt rows then img rows, and the single block's
+    stream), and the tile arrival counters (rank 0's copy is the one used).  `barrier()` is the
+    cross-rank barrier each fused layer needs before its outputs are read or its partial buffer
+    is reused (b2g_tp_barrier on a peer-mapped flag array)."""
+
+    COUNTER_SLOTS = 8192
+
+    def __init__(self, rows: int, hidden: int, group, dev):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        import b2g
+
+        self.b2g = b2g
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.part = symm.empty((rows, hidden), dtype=torch.bfloat16, device=dev)
+        self.res_double = symm.empty((rows, hidden), dtype=torch.float32, device=dev)
+        self.res_single = symm.empty((rows, hidden), dtype=torch.float32, device=dev)
+        self.counters = symm.empty(self.COUNTER_SLOTS, dtype=torch.int32, device=dev)
+        self.flags = symm.empty(self.world, dtype=torch.int32, device=dev)
+        self.counters.zero_()
+        self.flags.zero_()
+        name = group.group_name if group is not None else dist.group.WORLD.group_name
+        self._handles = [symm.rendezvous(t, name) for t in
+                         (self.part, self.res_double, self.res_single, self.counters, self.flags)]
+        torch.cuda.synchronize(dev)
+        dist.barrier(group)  # every rank's zeroed counters and flags are in place
+
+        def peers(t, h):  # every rank's address of this tensor, in this process
+            off = t.data_ptr() - h.buffer_ptrs[self.rank]
+            return [p + off for p in h.buffer_ptrs]
+
+        part = peers(self.part, self._handles[0])
+        self._part_ptrs = torch.tensor(part, dtype=torch.int64, device=dev)
+        self._res_ptrs = {name: torch.tensor(peers(t, h), dtype=torch.int64, device=dev) for name, t, h in
+                          (("double", self.res_double, self._handles[1]),
+                           ("single", self.res_single, self._handles[2]))}
+        counters0 = peers(self.counters, self._handles[3])[0]
+        self._flag_ptrs = torch.tensor(peers(self.flags, self._handles[4]), dtype=torch.int64, device=dev)
+        self.epoch = 0
+        self.desc = {}
+        for name, t in (("double", self.res_double), ("single", self.res_single)):
+            d = b2g.TpReduceDesc()
+            d.world, d.rank = self.world, self.rank
+            d.part_ptrs = self._part_ptrs.data_ptr()
+            d.res_ptrs = self._res_ptrs[name].data_ptr()
+            d.ld_part, d.ld_res = self.part.stride(0), t.stride(0)
+            d.counters = counters0
+            d.counter_slots = self.COUNTER_SLOTS
+            self.desc[name] = d
+
+    def reduce(self, which: str, problems: list[dict], row0: list[int]) -> None:
+        self.b2g.gemm_tp_reduce(problems, row0, self.desc[which])
+        self.barrier()
+
+    def barrier(self) -> None:
+        """All ranks' fused layers are done (bounded wait in libb2g's own barrier kernel)."""
+        self.epoch += 1
+        self.b2g.tp_barrier(self._flag_ptrs, self.flags, self.world, self.rank, self.epoch)
+
+
+def tp_double_block_fused(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1,
+                          img_mod1, txt_mod2, img_mod2, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask,
+                          s: TPScratch) -> None:
+    """tp_double_block with each row-split layer's all-reduce fused into its GEMM: the
+    replicated txt and img streams are comm.res_double[:T] and [T:]."""
+    T, HDl = txt_mod1.shape[0], s.HDl
+    ops.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
+                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
+    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
+    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm, q_norm2=img_w.q_norm,
+                  k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    comm.reduce("double", [dict(x=s.attn[:T], w=txt_w.proj_w, bias=txt_w.proj_b, gate=txt_gate1),
+                           dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, gate=img_gate1)], [0, T])
+    ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
+                    dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
+    comm.reduce("double", [dict(x=s.h_txt, w=txt_w.mlp2_w, bias=txt_w.mlp2_b, gate=txt_gate2),
+                           dict(x=s.h_img, w=img_w.mlp2_w, bias=img_w.mlp2_b, gate=img_gate2)], [0, T])
+
+
+def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, gate, pe, mask, s: TPScratch) -> None:
+    """tp_single_block with linear2's all-reduce fused into its GEMM: the replicated stream is
+    comm.res_single."""
+    HDl = s.HDl
+    ops.gemm(x_mod, w.linear1_w[:3 * HDl], w.linear1_b[:3 * HDl], out=s.qkv)
+    ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
+    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
+    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask, out=s.cat[:, :HDl])
+    comm.reduce("single", [dict(x=s.cat, w=w.linear2_w, bias=w.linear2_b, gate=gate)], [0])

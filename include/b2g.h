@@ -184,6 +184,35 @@ b2g_status b2g_bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy
                                    const float* gate, float* residual, int64_t ldr, int64_t M, int64_t N,
                                    void* stream);
 
+/* Tensor-parallel row-split layer with its all-reduce fused into the GEMM (no reference
+ * counterpart; replaces GEMM -> ncclAllReduce -> gated_residual, kernels.cu:942-968, on the
+ * path the north star adds to chroma.cuh for large images).  Every rank calls it with its
+ * K-slice: descs[i] = {M, N, K of the slice, a = this rank's activations, b = this rank's weight
+ * columns, bias = the full bias (F32, may be NULL), gate = the full gate}; d is ignored.  Each
+ * output tile's bf16 partial goes to this rank's part_ptrs[rank]; the last rank to finish a
+ * tile (arrival counted on rank 0's counters) sums all ranks' partials in rank order and
+ * writes residual + gate * (sum + bias) into every rank's res_ptrs[q] rows row0[i].. .
+ * part_ptrs / res_ptrs are device arrays of peer-mapped (NVLink) buffers; counters start at
+ * zero and are never reset (arrivals are counted modulo world).  The caller runs a cross-rank
+ * barrier after the call before anything reads a residual copy or reuses the partial buffer. */
+typedef struct {
+  int world, rank;
+  void* const* part_ptrs;    /* device array [world] of bf16 [rows, ld_part] buffers */
+  float* const* res_ptrs;    /* device array [world] of F32 [rows, ld_res] residual copies */
+  int64_t ld_part, ld_res;
+  int* counters;             /* rank 0's counter array (peer-mapped), counter_slots ints */
+  int64_t counter_slots;
+} b2g_tp_reduce_desc;
+b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, int count,
+                              const b2g_tp_reduce_desc* tp, void* stream);
+
+/* Cross-rank barrier for the fused tensor-parallel layers (no reference counterpart): rank
+ * `rank` stores `epoch` into slot `rank` of every rank's flag array (flag_ptrs: device array
+ * [world] of peer-mapped int[world] arrays, own_flags = this rank's) and waits until all slots
+ * of its own array reach `epoch`.  Call with the same increasing epoch on every rank.  The wait
+ * is bounded (2 s): on timeout the device error word gets bit 8 (b2g_check_device_error). */
+b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

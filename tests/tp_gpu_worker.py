@@ -1,4 +1,6 @@
 """Worker for tests/test_tp_gpu.py, launched with torchrun (one process per GPU, NCCL).
+Runs both the NCCL all-reduce path and the fused path (reduction inside the GEMM over
+peer-mapped memory).
 
 Every rank builds the same block-pair weights and inputs (seeded), shards them with tp.py,
 runs the tensor-parallel double + single block, and compares its replicated residual
@@ -58,6 +60,16 @@ def main() -> int:
     tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"], got["txt"],
                        got["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
     tp.tp_single_block(ops, ts, act["x_mod"], got["x"], gates[4], pe, mask, scratch)
+    # The same block pair with each row-split layer's reduction fused into its GEMM over
+    # peer-mapped memory (b2g_gemm_tp_reduce + b2g_tp_barrier).
+    comm = tp.SymmetricComm(L, H, None, dev)
+    comm.res_double[:T].copy_(res["txt"])
+    comm.res_double[T:].copy_(res["img"])
+    comm.res_single.copy_(res["x"])
+    tp.tp_double_block_fused(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                             gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
+    tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gates[4], pe, mask, scratch)
+    fused = {"txt": comm.res_double[:T], "img": comm.res_double[T:], "x": comm.res_single}
     torch.cuda.synchronize()
     b2g.check_device_error()
     ok = True
@@ -67,6 +79,12 @@ def main() -> int:
         cos = ((d1 @ d0) / (d1.norm() * d0.norm())).item()
         print(f"rank {rank}/{world} {k}: err {err:.3e} cos {cos:.6f}", flush=True)
         ok = ok and err <= 1e-2 and cos >= 0.9999
+        d2 = (fused[k] - res[k]).double().flatten()
+        err2 = ((d2 - d0).abs().max() / d0.abs().max()).item()
+        cos2 = ((d2 @ d0) / (d2.norm() * d0.norm())).item()
+        same = torch.equal(fused[k], got[k])
+        print(f"rank {rank}/{world} {k} fused: err {err2:.3e} cos {cos2:.6f} identical-to-nccl {same}", flush=True)
+        ok = ok and err2 <= 1e-2 and cos2 >= 0.9999
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
