@@ -83,6 +83,8 @@ _SIGNATURES = {
                             ctypes.POINTER(TpReduceDesc), ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
                        ctypes.c_int),
+    "b2g_t5_attention": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float,
+                                                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_bias_gated_residual": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
                                  ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p], ctypes.c_int),
     "b2g_linear_lt": ([ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
@@ -309,6 +311,25 @@ def tp_barrier(flag_ptrs: torch.Tensor, own_flags: torch.Tensor, world: int, ran
     lib = load()
     s = (stream or torch.cuda.current_stream(own_flags.device)).cuda_stream
     _check(lib.b2g_tp_barrier(flag_ptrs.data_ptr(), own_flags.data_ptr(), world, rank, epoch, ctypes.c_void_p(s)))
+
+
+def t5_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, rel_bias: torch.Tensor | None, n_head: int,
+                 d_head: int, scale: float = 1.0, attn_mask: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """t5_attention (attention.cuh:34-91): Q, K, V F32 [L, n_head, d_head] contiguous; rel_bias
+    [n_head, L, L] or None; attn_mask [L] or None -> F32 [L, n_head*d_head]."""
+    lib = load()
+    _require_cuda(Q, K, V, rel_bias, attn_mask, out)
+    L = Q.shape[0]
+    for t in (Q, K, V):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.numel() != L * n_head * d_head:
+            raise B2GError("t5_attention: contiguous F32 [L, n_head, d_head] tensors expected")
+    if out is None:
+        out = torch.empty((L, n_head * d_head), dtype=torch.float32, device=Q.device)
+    s = torch.cuda.current_stream(Q.device).cuda_stream
+    _check(lib.b2g_t5_attention(Q.data_ptr(), K.data_ptr(), V.data_ptr(), _ptr(rel_bias), n_head, d_head, L, scale,
+                                _ptr(attn_mask), out.data_ptr(), ctypes.c_void_p(s)))
+    return out
 
 
 def bias_gated_residual(y: torch.Tensor, bias: torch.Tensor | None, gate: torch.Tensor, residual: torch.Tensor,

@@ -301,6 +301,11 @@ b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int 
   return tp_barrier(flag_ptrs, own_flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head,
+                            int d_head, int64_t L, float scale, const float* attn_mask, float* out, void* stream) {
+  return t5_attention(Q, K, V, rel_bias, n_head, d_head, L, scale, attn_mask, out, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows, int64_t cols, int64_t ld,
                              uint8_t* dst, int64_t dst_ld, float* scales, void* stream) {
   DeviceInfo* dev = nullptr;

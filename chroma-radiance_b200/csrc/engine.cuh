@@ -85,6 +85,11 @@ b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, co
 // Cross-rank barrier over peer-mapped flag arrays (tp_comm.cu), bounded wait.
 b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, cudaStream_t st);
 
+// T5 attention (t5_attention.cu): Q, K, V [L, H, D] F32, rel_bias [H, L, L] or NULL, key mask
+// [L] or NULL, out [L, H*D] F32.
+b2g_status t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head,
+                        int d_head, int64_t L, float scale, const float* attn_mask, float* out, cudaStream_t st);
+
 bool tc_gemm_supported(const GemmProblem& p, std::string* why);
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st);
 // One launch over `count` (<= 2) problems that tc_gemm_groupable() accepts pairwise; their

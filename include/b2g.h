@@ -159,6 +159,17 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
  * capture on it (it looks up the array's device address). */
 b2g_status b2g_gemm_noalloc(const b2g_gemm_desc* desc, void* stream);
 
+/* T5 attention.  Same arguments and meaning as the reference's
+ *   static Tensor t5_attention(const Tensor& Q, const Tensor& K, const Tensor& V,
+ *       const float* rel_bias, int n_head, int d_head, float scale, const float* attn_mask)
+ *                                                             attention.cuh:34-91
+ * Q, K, V F32 [L, n_head, d_head]; rel_bias F32 [n_head, L, L] or NULL; attn_mask F32 [L]
+ * (0 / -inf on keys) or NULL; out F32 [L, n_head*d_head].  softmax(scale Q K^T + rel_bias +
+ * mask) V on the tensor cores: the scores with fp32-level accuracy from TF32 hi/lo operand
+ * splits (the reference runs exact fp32 SGEMMs), P.V in TF32.  L and d_head multiples of 4. */
+b2g_status b2g_t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head,
+                            int d_head, int64_t L, float scale, const float* attn_mask, float* out, void* stream);
+
 /* FP8 E4M3 quantisation of the rows of a matrix (no reference counterpart; the reference's
  * quantised path is INT8, quantize_act / linear_prequant in cublas_ops.cuh:294-791).  For each
  * row r of src [rows, cols] (F32, BF16 or F16, row stride ld): scales[r] = absmax_r / 448 (1

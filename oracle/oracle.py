@@ -262,6 +262,11 @@ class AttnRef:
                                          ctypes.POINTER(ctypes.c_double)]
         for f in ("ref_double_block", "ref_single_block", "ref_alloc_blocks", "ref_bench_blocks"):
             getattr(lib, f).restype = ctypes.c_int
+        lib.ref_t5_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, ctypes.c_float, _c_p, _c_p]
+        lib.ref_t5_attention.restype = ctypes.c_int
+        lib.ref_bench_t5_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, ctypes.c_float, _c_p,
+                                                            ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+        lib.ref_bench_t5_attention.restype = ctypes.c_int
         lib.ref_attn_init()
         self.lib = lib
 

@@ -35,6 +35,42 @@ int ref_attn_init(void) {
 
 // Q, K, V: F32 [L, n_head, d_head]; pe F32 [L, d_head/2*4]; mask F32 [L] or null;
 // out F32 [L, n_head*d_head].
+// The reference's T5 attention (attention.cuh:34-91): fp32 cuBLAS strided-batched GEMMs,
+// relative bias, masked softmax.
+int ref_t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head, int d_head,
+                     int64_t L, float scale, const float* mask, float* out) {
+  Tensor tq = Tensor::wrap_gpu(const_cast<float*>(Q), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  Tensor tk = Tensor::wrap_gpu(const_cast<float*>(K), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  Tensor tv = Tensor::wrap_gpu(const_cast<float*>(V), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  Tensor o = t5_attention(tq, tk, tv, rel_bias, n_head, d_head, scale, mask);
+  CHECK_CUDA(cudaMemcpy(out, o.data, o.nbytes(), cudaMemcpyDeviceToDevice));
+  return 0;
+}
+
+// Times `iters` calls of the reference's t5_attention with CUDA events (after `warmup`).
+int ref_bench_t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head,
+                           int d_head, int64_t L, float scale, const float* mask, int iters, int warmup,
+                           double* ms_total) {
+  Tensor tq = Tensor::wrap_gpu(const_cast<float*>(Q), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  Tensor tk = Tensor::wrap_gpu(const_cast<float*>(K), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  Tensor tv = Tensor::wrap_gpu(const_cast<float*>(V), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
+  for (int i = 0; i < warmup; ++i) Tensor o = t5_attention(tq, tk, tv, rel_bias, n_head, d_head, scale, mask);
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, 0);
+  for (int i = 0; i < iters; ++i) Tensor o = t5_attention(tq, tk, tv, rel_bias, n_head, d_head, scale, mask);
+  cudaEventRecord(e1, 0);
+  cudaEventSynchronize(e1);
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  *ms_total = ms;
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return static_cast<int>(cudaGetLastError());
+}
+
 int ref_attention_with_rope(const float* Q, const float* K, const float* V, const float* pe, int n_head, int d_head,
                             int64_t L, const float* mask, float* out) {
   Tensor tq = Tensor::wrap_gpu(const_cast<float*>(Q), {L, (int64_t)n_head, (int64_t)d_head}, DType::F32);
