@@ -144,9 +144,15 @@ __device__ __forceinline__ void item_coords(int item, const TcParams& p, int& ti
 }
 
 // tanh-form GELU, the formula of the reference's gelu_val (kernels.cu:266-269).
+// Evaluated through the identity 0.5 v (1 + tanh(u)) = v * sigmoid(2u) = v / (1 + e^(-2u)),
+// with e^(-2u) = 2^(-2u log2(e)) from the hardware base-2 exponential (ex2.approx, relative
+// error ~2^-22) and a fast division: a few instructions instead of an accurate tanhf, and
+// within a few fp32 ulps of the formula.  The exponent is capped at 2^126 (the quotient is
+// then -0 to fp32 precision, GELU's limit for large negative v).
 __device__ __forceinline__ float gelu_tanh(float v) {
-  const float inner = 0.7978845608f * (v + 0.044715f * v * v * v);
-  return 0.5f * v * (1.0f + tanhf(inner));
+  const float u = 0.7978845608f * (v + 0.044715f * v * v * v);
+  const float e = fast_exp2(fminf(-2.8853900817779268f * u, 126.0f));
+  return __fdividef(v, 1.0f + e);
 }
 
 // alpha * acc + bias (bias staged in shared memory, zero past N), then GELU if asked.
@@ -201,15 +207,18 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, const TcGroup& G,
     float* dp = static_cast<float*>(G.d) + off;
     if constexpr (EPI == B2G_EPI_GATED_RESIDUAL) {
       const float* gp = G.gate + n0;
-      if (full && G.vec_ok) {
+      if (full && G.vec_ok && (reinterpret_cast<uintptr_t>(gp) & 15u) == 0) {
+        float4 res[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) res[j] = reinterpret_cast<const float4*>(dp)[j];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float4 res = reinterpret_cast<const float4*>(dp)[j];
-          res.x += __ldg(gp + 4 * j + 0) * v[4 * j + 0];
-          res.y += __ldg(gp + 4 * j + 1) * v[4 * j + 1];
-          res.z += __ldg(gp + 4 * j + 2) * v[4 * j + 2];
-          res.w += __ldg(gp + 4 * j + 3) * v[4 * j + 3];
-          reinterpret_cast<float4*>(dp)[j] = res;
+          const float4 g = __ldg(reinterpret_cast<const float4*>(gp) + j);
+          res[j].x += g.x * v[4 * j + 0];
+          res[j].y += g.y * v[4 * j + 1];
+          res[j].z += g.z * v[4 * j + 2];
+          res[j].w += g.w * v[4 * j + 3];
+          reinterpret_cast<float4*>(dp)[j] = res[j];
         }
       } else {
 #pragma unroll
@@ -471,6 +480,23 @@ __device__ __forceinline__ void tp_epilogue_item(const TcParams& p, const TcGrou
   named_bar_sync(1, kEpiThreads);  // the broadcast word and staged bias are reused next item
 }
 
+// Gated residual: pulls this thread's row of the item's residual columns into L2 before the
+// accumulator is ready, so the epilogue's read-modify-write finds it there instead of waiting
+// on DRAM once per 32-column chunk.
+template <int BN>
+__device__ __forceinline__ void prefetch_residual(const TcParams& p, const TcGroup& G, const EpiCtx& e, int bz, int m,
+                                                  int n_base) {
+  if (m >= G.M) return;
+  const int c_begin = n_base + e.half * (BN / 2);
+  const float* row = static_cast<const float*>(G.d) + static_cast<long long>(bz) * p.d_bstride +
+                     static_cast<long long>(m) * G.ldd;
+#pragma unroll
+  for (int c = 0; c < BN / 2; c += 32) {  // one 128-byte line per 32 columns
+    if (c_begin + c < p.N)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(row + c_begin + c)) : "memory");
+  }
+}
+
 // Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
 // accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
 // after this warp's last chunk is read.  With split-K, each split stores its raw fp32
@@ -707,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       item_coords(item, p, tile, split, kb0, kb1);
       tile_coords(tile, p, gi, bz, mb, nb);
       const TcGroup& G = p.g[gi];
+      if constexpr (EPI == B2G_EPI_GATED_RESIDUAL) prefetch_residual<BN>(p, G, e, bz, mb * kBM + e.row, nb * BN);
       stage_bias<BN>(p, G, sBias, nb * BN);
       if constexpr (KIND == 2) stage_scale<BN>(p, G, sScale, nb * BN);
       const uint32_t acc = local & 1u;
@@ -908,6 +935,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       item_coords(item, p, tile, split, kb0, kb1);
       tile_coords(tile, p, gi, bz, mb, nb);
       const TcGroup& G = p.g[gi];
+      if constexpr (EPI == B2G_EPI_GATED_RESIDUAL)
+        prefetch_residual<BN>(p, G, e, bz, mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN);
       stage_bias<BN>(p, G, sBias, nb * BN);
       if constexpr (KIND == 2) stage_scale<BN>(p, G, sScale, nb * BN);
       const uint32_t acc = local & 1u;
