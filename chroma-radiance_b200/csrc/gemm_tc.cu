@@ -255,13 +255,31 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, const TcGroup& G,
 
 // Stages one 32x32 chunk (this warp's 32 rows x columns [n0, n0+32)) in shared memory and
 // writes it with one TMA store; the tensor map clips rows >= M and columns >= N.  The warp's
-// 4 KB staging area holds one fp32 chunk or two 16-bit chunks (double-buffered).
+// 4 KB staging area holds one fp32 chunk or two 16-bit chunks (double-buffered).  Gated
+// residual: the chunk holds gate * (acc + bias) and leaves as a TMA reduce-add into the fp32
+// residual, so residual + gate * y is formed in L2 (two roundings: the product, then the sum).
 template <int EPI, int OUT>
 __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_t* stage, int& obuf, int bz,
                                                   int m_warp0, int n0, const uint32_t (&r)[32], const float* sb,
-                                                  float alpha, int lane) {
+                                                  float alpha, int lane, const float* gate, int N) {
   float v[32];
   chunk_values<EPI>(r, sb, alpha, v);
+  if constexpr (EPI == B2G_EPI_GATED_RESIDUAL) {
+    const float* gp = gate + n0;
+    if (n0 + 32 <= N && (reinterpret_cast<uintptr_t>(gp) & 15u) == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 g = __ldg(reinterpret_cast<const float4*>(gp) + j);
+        v[4 * j] *= g.x;
+        v[4 * j + 1] *= g.y;
+        v[4 * j + 2] *= g.z;
+        v[4 * j + 3] *= g.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= (n0 + j < N) ? __ldg(gp + j) : 0.f;
+    }
+  }
   uint8_t* buf = stage;
   if constexpr (OUT == OUT_F32) {
     if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
@@ -291,7 +309,10 @@ __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_3d(tmD, buf, n0, m_warp0, bz);
+    if constexpr (EPI == B2G_EPI_GATED_RESIDUAL)
+      tma_reduce_add_3d(tmD, buf, n0, m_warp0, bz);
+    else
+      tma_store_3d(tmD, buf, n0, m_warp0, bz);
     bulk_commit_group();
   }
 }
@@ -301,8 +322,9 @@ template <int EPI, int OUT>
 __device__ __forceinline__ void emit_chunk(const TcParams& p, const TcGroup& G, const CUtensorMap* tmD, uint8_t* buf,
                                            int& obuf, int bz, int m, int m_warp0, int n0, const uint32_t (&r)[32],
                                            const float* sb, int lane) {
-  if (EPI != B2G_EPI_GATED_RESIDUAL && p.tma_store) {
-    if (m_warp0 < G.M && n0 < p.N) stage_store_chunk<EPI, OUT>(tmD, buf, obuf, bz, m_warp0, n0, r, sb, p.alpha, lane);
+  if (p.tma_store) {
+    if (m_warp0 < G.M && n0 < p.N)
+      stage_store_chunk<EPI, OUT>(tmD, buf, obuf, bz, m_warp0, n0, r, sb, p.alpha, lane, G.gate, p.N);
   } else if (m < G.M && n0 < p.N) {
     store_chunk<EPI, OUT>(p, G, bz, m, n0, r, sb);
   }
@@ -1261,7 +1283,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   const uint32_t b_box = v == V256 ? 256u : 128u;
-  prm.tma_store = p.epilogue != B2G_EPI_GATED_RESIDUAL && all_vec && g_tma_store && !p.tp ? 1 : 0;
+  prm.tma_store = all_vec && g_tma_store && !p.tp ? 1 : 0;
   if (p.tp) {
     const TpReduce& t = *p.tp;
     if (kind != 0) return set_error(B2G_ERR_UNSUPPORTED, "tp reduce: bf16/fp16 operands only");
