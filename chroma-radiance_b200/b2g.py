@@ -65,6 +65,11 @@ class TpReduceDesc(ctypes.Structure):
     ]
 
 
+class QkvRopeDesc(ctypes.Structure):
+    """b2g_qkv_rope_desc: RoPE rows and RMSNorm scales of one qkv projection problem."""
+    _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+
+
 _lib = None
 
 # Exported symbols of libb2g.so with their ctypes signatures (status-returning unless noted).
@@ -103,6 +108,11 @@ _SIGNATURES = {
                                   [ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                    ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                    ctypes.c_void_p], ctypes.c_int),
+    "b2g_gemm_qkv_rope": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(QkvRopeDesc), ctypes.c_int, ctypes.c_int,
+                           ctypes.c_float, ctypes.c_void_p], ctypes.c_int),
+    "b2g_attention_bf16": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                                                   ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_attention_with_rope": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p,
                                  ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
@@ -442,6 +452,63 @@ def attention_qknorm_rope(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, pe:
                                          norm_split, eps, pe.data_ptr(),
                                          _ptr(attn_mask), out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0),
                                          L, n_head, d_head, ctypes.c_void_p(s)))
+    return out
+
+
+def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
+                  stream: torch.cuda.Stream | None = None) -> list[torch.Tensor]:
+    """Attention input projections with qk_norm and RoPE in the GEMM epilogue.
+
+    Each problem: x [M, K] and w [3*n_head*128, K] (bf16/fp16), bias (F32), out (bf16 [M, N]
+    view with 16-byte aligned rows; allocated when absent), pe (F32 RoPE rows of the
+    problem's tokens, [M, 64, 4] or [M, 256]), q_norm / k_norm ([128] F32 or None).  Output
+    columns [q | k | v]: q and k heads normed and rotated, v the plain product (+ bias).
+    Two problems (txt and img streams) run as one launch.
+    """
+    lib = load()
+    descs, ropes, outs, keep = [], [], [], []
+    for pr in problems:
+        out = pr.get("out")
+        if out is None:
+            out = torch.empty((pr["x"].shape[0], pr["w"].shape[0]), device=pr["x"].device, dtype=torch.bfloat16)
+        d, out = _gemm_desc(pr["x"], pr["w"], pr.get("bias"), out, None, "none", None)
+        pe = pr["pe"]
+        qn, kn = pr.get("q_norm"), pr.get("k_norm")
+        _require_cuda(pe, qn, kn)
+        for t in (pe, qn, kn):
+            if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
+                raise B2GError("gemm_qkv_rope: pe and norm scales must be contiguous F32")
+        if pe.numel() < pr["x"].shape[0] * 256:
+            raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x")
+        descs.append(d)
+        ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn)))
+        outs.append(out)
+        keep.append(pe)
+    arr = (GemmDesc * len(descs))(*descs)
+    rarr = (QkvRopeDesc * len(ropes))(*ropes)
+    dev = problems[0]["x"].device
+    s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    _check(lib.b2g_gemm_qkv_rope(arr, rarr, len(descs), n_head, eps, ctypes.c_void_p(s)))
+    return outs
+
+
+def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_head: int, d_head: int,
+                   attn_mask: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                   out_dtype: torch.dtype = torch.float32, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """Fused attention on bf16 [L, n_head*d_head] views (unit column stride, row strides a
+    multiple of 8): softmax(q k^T / sqrt(d_head) + attn_mask[key]) v per head."""
+    lib = load()
+    _require_cuda(q, k, v, attn_mask, out)
+    L = q.shape[0]
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.stride(1) != 1 or t.shape[0] != L:
+            raise B2GError("attention_bf16: bf16 [L, H*D] views with unit column stride expected")
+    if out is None:
+        out = torch.empty((L, n_head * d_head), dtype=out_dtype, device=q.device)
+    s = (stream or torch.cuda.current_stream(q.device)).cuda_stream
+    _check(lib.b2g_attention_bf16(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+                                  L, n_head, d_head, _ptr(attn_mask), out.data_ptr(), _TORCH_TO_B2G[out.dtype],
+                                  out.stride(0), ctypes.c_void_p(s)))
     return out
 
 

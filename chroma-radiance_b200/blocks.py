@@ -89,7 +89,7 @@ class Scratch:
 
     def __init__(self, T: int, I: int, dev):
         L = T + I
-        self.qkv = torch.empty((L, 3 * HIDDEN), dtype=torch.float32, device=dev)
+        self.qkv = torch.empty((L, 3 * HIDDEN), dtype=torch.bfloat16, device=dev)  # normed, rotated
         self.attn = torch.empty((L, HIDDEN), dtype=torch.bfloat16, device=dev)
         self.h_img = torch.empty((I, MLP), dtype=torch.bfloat16, device=dev)
         self.h_txt = torch.empty((T, MLP), dtype=torch.bfloat16, device=dev)
@@ -105,13 +105,17 @@ def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1,
     mark = mark or _no_mark
     T = txt.shape[0]
     # Each layer's txt and img GEMMs share one launch (b2g_gemm_group): together their tiles
-    # fill the SMs where the txt GEMM alone (M=512) would leave most of them idle.
-    b2g.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
-                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
+    # fill the SMs where the txt GEMM alone (M=512) would leave most of them idle.  The qkv
+    # projection applies qk_norm and RoPE in its epilogue (txt rows take pe rows [0, T), img
+    # rows [T, L): the attention sequence is txt then img) and writes the attention's bf16
+    # operands.
+    b2g.gemm_qkv_rope([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T], pe=pe[:T],
+                            q_norm=txt_w.q_norm, k_norm=txt_w.k_norm),
+                       dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:], pe=pe[T:],
+                            q_norm=img_w.q_norm, k_norm=img_w.k_norm)], HEADS)
     mark("double.qkv")
     q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
-    b2g.attention_qknorm_rope(q, k, v, pe, HEADS, DHEAD, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm,
-                              q_norm2=img_w.q_norm, k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    b2g.attention_bf16(q, k, v, HEADS, DHEAD, attn_mask=mask, out=s.attn)
     mark("double.attention")
     b2g.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, bias=txt_w.proj_b, out=txt, epilogue="gated_residual",
                          gate=txt_gate1),
@@ -132,13 +136,13 @@ def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=No
     """Updates x [L, 3072] (F32 residual stream) in place.  `mark` as in double_block."""
     mark = mark or _no_mark
     n_qkv = 3 * HIDDEN
-    b2g.gemm(x_mod, w.linear1_w[:n_qkv], w.linear1_b[:n_qkv], out=s.qkv)
+    b2g.gemm_qkv_rope([dict(x=x_mod, w=w.linear1_w[:n_qkv], bias=w.linear1_b[:n_qkv], out=s.qkv, pe=pe,
+                            q_norm=w.q_norm, k_norm=w.k_norm)], HEADS)
     mark("single.linear1_qkv")
     b2g.gemm(x_mod, w.linear1_w[n_qkv:], w.linear1_b[n_qkv:], out=s.cat[:, HIDDEN:], epilogue="gelu")
     mark("single.linear1_mlp")
     q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
-    b2g.attention_qknorm_rope(q, k, v, pe, HEADS, DHEAD, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask,
-                              out=s.cat[:, :HIDDEN])
+    b2g.attention_bf16(q, k, v, HEADS, DHEAD, attn_mask=mask, out=s.cat[:, :HIDDEN])
     mark("single.attention")
     b2g.gemm(s.cat, w.linear2_w, w.linear2_b, out=x, epilogue="gated_residual", gate=gate)
     mark("single.linear2")

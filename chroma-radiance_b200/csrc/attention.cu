@@ -5,14 +5,15 @@
 // (cuDNN SDPA, cudnn_attention.cuh:408-443), output F32 [L, H*D] (or bf16 for the block path).
 //
 //   1. attn_prep         one launch: Q, K F32 rows [L, H*D] -> optional per-head RMSNorm
-//                        (qk_norm) -> RoPE -> bf16 [L, H*D] (the attention kernel reads head
-//                        h through TMA: row stride H*D, head stride D); V F32 -> bf16
-//                        [H, D, L] (K-major operand of P.V); key mask (0 / -inf) scaled by
-//                        log2(e), -inf past L, padded to a multiple of 128 keys.
-//   2. flash_attn        one CTA per (128-query tile, head): S = Q K^T on the tensor cores
-//                        into TMEM, online softmax in registers, P (bf16) through shared
-//                        memory into O += P V, O / rowsum written to the output layout.
-//                        S never leaves the SM.
+//                        (qk_norm) -> RoPE -> bf16 [L, H*D]; V F32 -> bf16 [L, H*D].  The
+//                        attention kernel reads head h of each through TMA (row stride H*D,
+//                        head stride D).  The block path skips this launch: its qkv GEMM
+//                        applies norm and RoPE in the epilogue and writes bf16 [L, 3*H*D]
+//                        (attention_bf16 below).
+//   2. flash_attn        two 128-query tiles of one head per CTA: S = Q K^T on the tensor
+//                        cores into TMEM, online softmax in registers, P (bf16) back into
+//                        TMEM as the A operand of O += P V (V read MN-major, as stored), O /
+//                        rowsum written to the output layout.  S never leaves the SM.
 #include <cuda_bf16.h>
 #include <cstdint>
 #include "engine.cuh"
@@ -22,46 +23,36 @@ namespace b2g {
 
 namespace {
 
-// Attention prologue, one launch, work items in three ranges of blocks (256 threads each):
-//   [0, n_rows)            Q then K rows: each warp 2 (token l, head h) rows of D values:
-//                          RMSNorm with a learned scale (rms_norm, kernels.cu:174-207, as
-//                          qk_norm applies it, chroma.cuh:513-515; rows l >= norm_split use the
-//                          second scale set), RoPE with pe row l = D/2 groups of (cos, -sin,
-//                          sin, cos) (the table gen_pe builds, rope.cuh:84, applied as
-//                          apply_rope_fused_bf16 does, rope.cuh:180-221), bf16 out [L, H*D].
-//   [n_rows, +n_vtiles)    V [L, H*D] F32 -> Vt [H*D, L] bf16 through 64x64 smem tiles.
-//   last block             key bias in base-2 exponent units: bias[k]*log2(e) for k < L, -inf
-//                          up to the padded key count (keys past L are TMA zero fill).
+// Attention prologue (256 threads per block): Q, K and V rows, each warp 2 (token l, head h)
+// rows of D values.  Q and K: RMSNorm with a learned scale (rms_norm, kernels.cu:174-207, as
+// qk_norm applies it, chroma.cuh:513-515; rows l >= norm_split use the second scale set), RoPE
+// with pe row l = D/2 groups of (cos, -sin, sin, cos) (the table gen_pe builds, rope.cuh:84,
+// applied as apply_rope_fused_bf16 does, rope.cuh:180-221), bf16 out [L, H*D].  V: bf16 out
+// [L, H*D] (cudnn_attention.cuh:459 converts V the same way).
 struct PrepArgs {
-  const float* x[2];        // Q, K
-  long long ldx[2];
+  const float* x[3];        // Q, K, V
+  long long ldx[3];
   const float* norm1[2];    // may be NULL (no qk_norm)
   const float* norm2[2];
-  __nv_bfloat16* out[2];    // [L, H*D]
+  __nv_bfloat16* out[3];    // [L, H*D] each
   int norm_split;
   float eps;
   const float* pe;
-  const float* v;
-  long long ldv;
-  __nv_bfloat16* vt;        // [H*D, L]
-  const float* bias;        // may be NULL
-  float* bias_log2;         // [padded]
-  int* bias_flags;          // [padded / 128][8]: kind, 3 unused, 4 mask words (see kBiasMask)
-  int L, H, padded;
-  int rows_blocks, vt_cols_tiles, vt_blocks;
+  int L, H;
 };
 
 constexpr int kRowsPerWarp = 2;
 
-// Per 128-key block the prologue records what its key bias holds: kind (bit 0: some keys are
-// -inf, i.e. masked; bit 1: some other nonzero value) and, for bit 0, a 128-bit mask of the
-// -inf keys (word c, bit i = key 32c+i).  Unmasked blocks skip the bias; blocks that are only
-// a 0/-inf mask (the key padding mask) apply it with one select per score.
+// Per 128-key block the softmax warps derive what the key bias holds: kind (bit 0: some keys
+// are -inf, i.e. masked, keys past L included; bit 1: some other nonzero value) and, for bit
+// 0, a 128-bit mask of the -inf keys (word c, bit i = key 32c+i).  Unmasked blocks skip the
+// bias; blocks that are only a 0/-inf mask (the key padding mask) apply it with one select
+// per score.
 constexpr int kBiasMask = 1, kBiasGeneral = 2;
-constexpr int kBiasRec = 8;  // ints per block record
 
-// kRowsPerWarp Q or K rows (token l, head h) of D values starting at `row0`: RMSNorm, RoPE,
-// bf16 (see attn_prep_kernel).  All rows' loads are issued before any arithmetic.
+// kRowsPerWarp Q, K or V rows (token l, head h) of D values starting at `row0`: RMSNorm, RoPE,
+// bf16 for Q and K, bf16 for V (see attn_prep_kernel).  All rows' loads are issued before any
+// arithmetic.
 template <int D>
 __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int lane) {
   constexpr int kPerLane = D / 32;  // 4 (D=128) or 2 (D=64) consecutive values per lane
@@ -72,12 +63,16 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
 #pragma unroll
   for (int rr = 0; rr < kRowsPerWarp; ++rr) {
     const long long row = row0 + rr;
-    const bool live = row < 2 * per;
-    which[rr] = row >= per ? 1 : 0;
+    const bool live = row < 3 * per;
+    which[rr] = live ? static_cast<int>(row / per) : 0;
     const long long r = live ? row - which[rr] * per : 0;
     l[rr] = static_cast<int>(r / a.H);
     h[rr] = static_cast<int>(r % a.H);
-    const float* xr = a.x[which[rr] & 1] + l[rr] * a.ldx[which[rr] & 1] + h[rr] * D + lane * kPerLane;
+    // (selects, not indexing: a dynamically indexed parameter array is copied to local memory)
+    const int w = which[rr];
+    const float* xb = w == 0 ? a.x[0] : (w == 1 ? a.x[1] : a.x[2]);
+    const long long ldx = w == 0 ? a.ldx[0] : (w == 1 ? a.ldx[1] : a.ldx[2]);
+    const float* xr = xb + l[rr] * ldx + h[rr] * D + lane * kPerLane;
     if constexpr (kPerLane == 4) {
       const float4 t = live ? *reinterpret_cast<const float4*>(xr) : make_float4(0.f, 0.f, 0.f, 0.f);
       v[rr][0] = t.x; v[rr][1] = t.y; v[rr][2] = t.z; v[rr][3] = t.w;
@@ -88,13 +83,27 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
     const float4* pr = reinterpret_cast<const float4*>(a.pe) + static_cast<long long>(l[rr]) * (D / 2) +
                        lane * kPerLane / 2;
 #pragma unroll
-    for (int i = 0; i < kPerLane / 2; ++i) pe[rr][i] = live ? __ldg(pr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < kPerLane / 2; ++i)
+      pe[rr][i] = live && which[rr] < 2 ? __ldg(pr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll
   for (int rr = 0; rr < kRowsPerWarp; ++rr) {
-    if (row0 + rr >= 2 * per) break;
+    if (row0 + rr >= 3 * per) break;
     const int w = which[rr];
-    const float* norm = l[rr] < a.norm_split ? a.norm1[w] : a.norm2[w];
+    __nv_bfloat16* ob = w == 0 ? a.out[0] : (w == 1 ? a.out[1] : a.out[2]);
+    __nv_bfloat16* dst = ob + static_cast<long long>(l[rr]) * a.H * D + h[rr] * D + lane * kPerLane;
+    if (w == 2) {  // V: bf16 only
+      uint32_t packed[kPerLane / 2];
+#pragma unroll
+      for (int i = 0; i < kPerLane / 2; ++i) {
+        __nv_bfloat162 o = __floats2bfloat162_rn(v[rr][2 * i], v[rr][2 * i + 1]);
+        packed[i] = *reinterpret_cast<uint32_t*>(&o);
+      }
+      if constexpr (kPerLane == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
+      else *reinterpret_cast<uint32_t*>(dst) = packed[0];
+      continue;
+    }
+    const float* norm = l[rr] < a.norm_split ? (w == 0 ? a.norm1[0] : a.norm1[1]) : (w == 0 ? a.norm2[0] : a.norm2[1]);
     if (norm) {
       float nv[kPerLane];
       if constexpr (kPerLane == 4) {
@@ -122,7 +131,6 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
                                                v[rr][2 * i] * c.z + v[rr][2 * i + 1] * c.w);
       packed[i] = *reinterpret_cast<uint32_t*>(&o);
     }
-    __nv_bfloat16* dst = a.out[w] + static_cast<long long>(l[rr]) * a.H * D + h[rr] * D + lane * kPerLane;
     if constexpr (kPerLane == 4) *reinterpret_cast<uint2*>(dst) = make_uint2(packed[0], packed[1]);
     else *reinterpret_cast<uint32_t*>(dst) = packed[0];
   }
@@ -130,56 +138,8 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
 
 template <int D>
 __global__ void __launch_bounds__(256, 4) attn_prep_kernel(const PrepArgs a) {
-  __shared__ float tile[64][65];
-  const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (b < a.rows_blocks) {
-    prep_rows<D>(a, (static_cast<long long>(b) * 8 + warp) * kRowsPerWarp, lane);
-    return;
-  }
-  const int vb = b - a.rows_blocks;
-  if (vb < a.vt_blocks) {
-    const int HD = a.H * D;
-    const int l0 = (vb / a.vt_cols_tiles) * 64, c0 = (vb % a.vt_cols_tiles) * 64;
-    // read 64 rows (tokens) x 64 columns (features), float4 per thread, 4 passes of 16 rows
-    const int tc = (threadIdx.x & 15) * 4, tr = threadIdx.x >> 4;
-#pragma unroll
-    for (int pass = 0; pass < 4; ++pass) {
-      const int rr = pass * 16 + tr, l = l0 + rr;
-      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (l < a.L && c0 + tc < HD) t = *reinterpret_cast<const float4*>(a.v + l * a.ldv + c0 + tc);
-      tile[rr][tc] = t.x;
-      tile[rr][tc + 1] = t.y;
-      tile[rr][tc + 2] = t.z;
-      tile[rr][tc + 3] = t.w;
-    }
-    __syncthreads();
-    // write 64 feature rows x 64 tokens, 4 tokens (8 bytes) per thread, 4 passes of 16 rows
-#pragma unroll
-    for (int pass = 0; pass < 4; ++pass) {
-      const int cc = pass * 16 + tr, c = c0 + cc, l = l0 + tc;
-      if (c < HD && l < a.L) {
-        __nv_bfloat162 p0 = __floats2bfloat162_rn(tile[tc][cc], tile[tc + 1][cc]);
-        __nv_bfloat162 p1 = __floats2bfloat162_rn(tile[tc + 2][cc], tile[tc + 3][cc]);
-        *reinterpret_cast<uint2*>(a.vt + static_cast<long long>(c) * a.L + l) =
-            make_uint2(*reinterpret_cast<uint32_t*>(&p0), *reinterpret_cast<uint32_t*>(&p1));
-      }
-    }
-    return;
-  }
-  for (int k = threadIdx.x; k < a.padded / 128 * kBiasRec; k += blockDim.x) a.bias_flags[k] = 0;
-  __syncthreads();
-  for (int k = threadIdx.x; k < a.padded; k += blockDim.x) {
-    const float v = k < a.L ? (a.bias ? a.bias[k] * 1.4426950408889634f : 0.f) : -INFINITY;
-    a.bias_log2[k] = v;
-    int* rec = a.bias_flags + (k / 128) * kBiasRec;
-    if (v == -INFINITY) {
-      atomicOr(rec, kBiasMask);
-      atomicOr(rec + 4 + (k % 128) / 32, static_cast<int>(1u << (k % 32)));
-    } else if (v != 0.f) {
-      atomicOr(rec, kBiasGeneral);
-    }
-  }
+  prep_rows<D>(a, (static_cast<long long>(blockIdx.x) * 8 + warp) * kRowsPerWarp, lane);
 }
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -188,15 +148,16 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 //
 // CTA = (two query tiles A and B of 128 rows = 256 queries, head h), 384 threads:
 //   warp 0      TMA: both Q tiles once, then K tile j [128 keys x D] into a 3-deep ring.
-//   warp 2      TMA: Vt tile j [D x 128 keys] into a 2-deep ring.
+//   warp 2      TMA: V tile j [128 keys x D] (as stored) into a 2-deep ring.
 //   warp 1      one thread issues tcgen05.mma for both tiles, alternating so the tensor core
 //               works for one tile while the other tile's softmax runs:
 //                 S_A(0), S_B(0), then per key block j:
-//                 O_A += P_A(j) Vt_j, S_A(j+1), O_B += P_B(j) Vt_j, S_B(j+1)
+//                 O_A += P_A(j) V_j, S_A(j+1), O_B += P_B(j) V_j, S_B(j+1)
 //               S = Q K_j^T (M=128, N=128, K=D, both from shared memory) goes to the tile's
 //               TMEM S columns; P (bf16 pairs) overwrites the first 64 of them and is the A
-//               operand of P.Vt read straight from TMEM; O accumulates in TMEM.  S(j+1) is
-//               issued once P(j).Vt_j has retired (it overwrites P(j)).
+//               operand of P.V read straight from TMEM, V_j the MN-major B operand; O
+//               accumulates in TMEM.  S(j+1) is issued once P(j).V_j has retired (it
+//               overwrites P(j)).
 //   warp 3      idle (completes the first warpgroup, which runs on 64 registers per thread)
 //   warps 4-7   softmax of tile A, warps 8-11 of tile B (216 registers per thread); warp w
 //               reads TMEM lanes 32*(w%4)..,
@@ -208,8 +169,8 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 //               At the end O / l is written in the caller's layout.
 // TMEM: tile t at columns [256t, 256t+128) S/P and [256t+128, +D) O: 512 columns.
 // Barriers: q_full; k_full[3], k_empty[3] (commit after S_B(j)); v_full[2], v_empty[2]
-// (commit after P_B(j).Vt_j); per tile s_full (commit after S), p_full (4 softmax warps),
-// pv_done (commit after P.Vt).  Every wait is bounded; on timeout the kernel records the error
+// (commit after P_B(j).V_j); per tile s_full (commit after S), p_full (4 softmax warps),
+// pv_done (commit after P.V).  Every wait is bounded; on timeout the kernel records the error
 // word and winds down.
 constexpr int kFaThreads = 384;  // 3 warpgroups
 // Registers: launched at 168 per thread (64,512 per CTA); the producer/MMA warpgroup gives
@@ -230,8 +191,7 @@ template <int D>
 struct FaLayout {
   static constexpr uint32_t kQTileBytes = kFaRows * D * 2;  // D/64 boxes
   static constexpr uint32_t kKBytes = kFaKeys * D * 2;      // D/64 boxes
-  static constexpr uint32_t kVBytes = D * kFaKeys * 2;      // 2 boxes of D rows x 64 keys
-  static constexpr uint32_t kVBox = D * 128;                // one D-row x 64-key box
+  static constexpr uint32_t kVBytes = kFaKeys * D * 2;      // D/64 boxes, like K
   static constexpr uint32_t kQ = 0;
   static constexpr uint32_t kK = kQ + kFaTiles * kQTileBytes;
   static constexpr uint32_t kV = kK + kFaKStages * kKBytes;
@@ -244,8 +204,7 @@ struct FaParams {
   int L;
   int num_kb;             // key blocks of 128
   float scale_log2;       // log2(e) / sqrt(D)
-  const float* bias_log2; // [num_kb * 128]
-  const int* bias_flags;  // [num_kb][kBiasRec]: kind and -inf mask of each 128-key block
+  const float* bias;      // [L] additive key bias (0 / -inf mask or general), NULL: none
   void* out;
   long long ldo;
   int out_bf16;
@@ -343,9 +302,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         } else {
           mbar_arrive_expect_tx(&full[st], Ly::kVBytes);
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            tma_load_3d(sV + st * Ly::kVBytes + c * Ly::kVBox, &tmV, &full[st], j * kFaKeys + c * 64, 0, head,
-                        shared_kv);
+          for (int c = 0; c < D / 64; ++c)
+            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, j * kFaKeys, head, shared_kv);
         }
         ++issued;
       }
@@ -359,7 +317,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = idesc_make(kFmtBF16, kFaRows, kFaKeys);
-      constexpr uint32_t idesc_o = idesc_make(kFmtBF16, kFaRows, D);
+      constexpr uint32_t idesc_o = idesc_make(kFmtBF16, kFaRows, D) | kIdescBMajorMN;
       bool ok = mbar_wait(q_full, 0, p.err, kErrWaitMma);
       auto issue_s = [&](int t, int j) {  // K_j is loaded
         const uint32_t q0 = smem_u32(sQ + t * Ly::kQTileBytes), k0 = smem_u32(sK + (j % KS) * Ly::kKBytes);
@@ -388,15 +346,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           tc_fence_after();
           const uint32_t v0 = smem_u32(sV + vs * Ly::kVBytes);
 #pragma unroll
-          for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., Vt box k/4, 32-byte step k%4
-            umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k,
-                        smem_desc_k_sw128(v0 + (k >> 2) * Ly::kVBox + (k & 3) * 32), idesc_o,
-                        (j | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., V rows 16k.. (2 KB step)
+            umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k, smem_desc_mn_sw128(v0 + k * 2048, kFaBox),
+                        idesc_o, (j | k) != 0 ? 1u : 0u);
           umma_commit(&pv_done[t]);
-          if (t == kFaTiles - 1) umma_commit(&v_empty[vs]);  // both tiles have read Vt_j
+          if (t == kFaTiles - 1) umma_commit(&v_empty[vs]);  // both tiles have read V_j
           if (j + 1 < nkb) {
             if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, p.err, kErrWaitMma))) break;
-            // S(j+1) overwrites P(j): wait until P(j).Vt_j has retired.
+            // S(j+1) overwrites P(j): wait until P(j).V_j has retired.
             if (!(ok = mbar_wait(&pv_done[t], j & 1, p.err, kErrWaitMma))) break;
             tc_fence_after();
             issue_s(t, j + 1);
@@ -420,13 +377,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     float m_used = -INFINITY, l_sum = 0.f;
     bool good = true;
     for (int j = 0; j < nkb && good; ++j) {
-      // issued before the wait hides their latency
-      const int kind = __ldg(p.bias_flags + j * kBiasRec);
-      const uint4 mw = __ldg(reinterpret_cast<const uint4*>(p.bias_flags + j * kBiasRec + 4));
-      const bool biased = (kind & kBiasGeneral) != 0;
-      const float* bias = p.bias_log2 + j * kFaKeys;
+      // The block's key bias, key 32c + lane in kb2[c], in base-2 exponent units (keys past L
+      // are -inf); loaded before the wait, which hides the latency.
+      float kb2[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int key = j * kFaKeys + c * 32 + lane;
+        kb2[c] = key < p.L ? (p.bias ? __ldg(p.bias + key) * 1.4426950408889634f : 0.f) : -INFINITY;
+      }
       good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
       if (!good) break;
+      // Warp votes: the -inf mask words and whether any other nonzero bias is present.
+      uint32_t words[4];
+      bool other = false;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        words[c] = __ballot_sync(0xffffffffu, kb2[c] == -INFINITY);
+        other |= kb2[c] != 0.f && kb2[c] != -INFINITY;
+      }
+      const bool biased = __any_sync(0xffffffffu, other);
+      const int kind = ((words[0] | words[1] | words[2] | words[3]) != 0u ? kBiasMask : 0) |
+                       (biased ? kBiasGeneral : 0);
       tc_fence_after();
       // The whole 128-key row in registers: one TMEM round trip per block.  u = raw score
       // (P = 2^(u*scale - m); masked keys set to -inf, giving P = 0) or, for a block with a
@@ -440,19 +411,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 bb = __ldg(reinterpret_cast<const float4*>(bias + c * 32 + i));
-            const float b4[4] = {bb.x, bb.y, bb.z, bb.w};
+          for (int i = 0; i < 32; i += 4)
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const float u = fmaf(__uint_as_float(r[c][i + q]), p.scale_log2, b4[q]);
+              const float u =
+                  fmaf(__uint_as_float(r[c][i + q]), p.scale_log2, __shfl_sync(0xffffffffu, kb2[c], i + q));
               r[c][i + q] = __float_as_uint(u);
               mx4[q] = fmaxf(mx4[q], u);
             }
-          }
       } else {
         if (kind & kBiasMask) {
-          const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -560,15 +528,17 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   }
 }
 
+// Q, K, V bf16 [L, ld] with head h at columns [h*D, (h+1)*D): one 3-D tensor map each
+// (D-wide rows, head stride D); rows past L are zero-filled by TMA.
 template <int D>
-b2g_status launch_flash(const __nv_bfloat16* qb, const __nv_bfloat16* kb, const __nv_bfloat16* vt, const FaParams& fp,
-                        int64_t L, int64_t H, cudaStream_t st) {
+b2g_status launch_flash(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, int64_t ldk,
+                        const __nv_bfloat16* v, int64_t ldv, const FaParams& fp, int64_t L, int64_t H,
+                        cudaStream_t st) {
   CUtensorMap tq, tk, tv;
   b2g_status s;
-  const int64_t HD = H * D;
-  if ((s = make_operand_map(&tq, qb, B2G_BF16, D, L, HD, H, D, kFaRows)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tk, kb, B2G_BF16, D, L, HD, H, D, kFaKeys)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tv, vt, B2G_BF16, L, D, L, H, D * L, D)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tq, q, B2G_BF16, D, L, ldq, H, D, kFaRows)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tk, k, B2G_BF16, D, L, ldk, H, D, kFaKeys)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tv, v, B2G_BF16, D, L, ldv, H, D, kFaKeys)) != B2G_OK) return s;
   constexpr uint32_t smem = FaLayout<D>::kSmem;
   static_assert(smem <= 227 * 1024, "shared memory budget");
   if ((s = check_cuda(cudaFuncSetAttribute(flash_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -581,79 +551,88 @@ b2g_status launch_flash(const __nv_bfloat16* qb, const __nv_bfloat16* kb, const 
   return check_cuda(cudaGetLastError(), "flash_attn launch");
 }
 
+// Shared checks and launch of the fused kernel on bf16 operands.
+b2g_status flash_checked(const AttnBf16Args& a, cudaStream_t st) {
+  const int64_t L = a.L, H = a.H, D = a.D;
+  if (a.out_dtype != B2G_F32 && a.out_dtype != B2G_BF16)
+    return set_error(B2G_ERR_UNSUPPORTED, "attention: output must be F32 or BF16");
+  const size_t ob = a.out_dtype == B2G_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(a.out) & 15u) != 0 || (a.ldo * ob) % 16 != 0 || a.ldo < H * D)
+    return set_error(B2G_ERR_UNSUPPORTED, "attention: output base and row stride must be 16-byte aligned");
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                         reinterpret_cast<uintptr_t>(a.v);
+  if ((bits & 15u) != 0 || (a.ldq | a.ldk | a.ldv) % 8 != 0 || a.ldq < H * D || a.ldk < H * D || a.ldv < H * D)
+    return set_error(B2G_ERR_UNSUPPORTED, "attention: bf16 q, k, v need 16-byte aligned bases and row strides");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  FaParams fp{};
+  fp.L = static_cast<int>(L);
+  fp.num_kb = static_cast<int>((L + kFaKeys - 1) / kFaKeys);
+  fp.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  fp.bias = a.key_bias;
+  fp.out = a.out;
+  fp.ldo = a.ldo;
+  fp.out_bf16 = a.out_dtype == B2G_BF16 ? 1 : 0;
+  fp.err = dev->err_word;
+  if (D == 128) return launch_flash<128>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, st);
+  return launch_flash<64>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, st);
+}
 
 }  // namespace
+
+b2g_status attention_bf16(const AttnBf16Args& a, cudaStream_t st) {
+  if (a.L <= 0 || a.H <= 0) return B2G_OK;
+  if (a.D != 64 && a.D != 128) return set_error(B2G_ERR_UNSUPPORTED, "attention: head dim must be 64 or 128");
+  if (a.L > (1ll << 30) || a.H > 65535) return set_error(B2G_ERR_UNSUPPORTED, "attention: size");
+  if (!a.q || !a.k || !a.v || !a.out) return set_error(B2G_ERR_INVALID, "attention: null operand");
+  return flash_checked(a, st);
+}
 
 b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   const int64_t L = a.L, H = a.H, D = a.D;
   if (L <= 0 || H <= 0) return B2G_OK;
   if (D != 64 && D != 128) return set_error(B2G_ERR_UNSUPPORTED, "attention: head dim must be 64 or 128");
-  // 16-byte TMA row strides for Vt (rows are L long); 16-byte row loads of Q, K and V.
-  if (L % 8 != 0) return set_error(B2G_ERR_UNSUPPORTED, "attention: sequence length must be a multiple of 8");
   const uintptr_t qkv_bits = reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
                              reinterpret_cast<uintptr_t>(a.v);
   if ((qkv_bits & 15u) != 0 || (a.ldq | a.ldk | a.ldv) % 4 != 0 || (a.pe && (reinterpret_cast<uintptr_t>(a.pe) & 15u)))
     return set_error(B2G_ERR_UNSUPPORTED, "attention: q, k, v and pe must be 16-byte aligned with row strides % 4 == 0");
+  if (!a.pe) return set_error(B2G_ERR_INVALID, "attention: pe is required");
   if (L > (1ll << 30) || H > 65535) return set_error(B2G_ERR_UNSUPPORTED, "attention: size");
-  if (a.out_dtype != B2G_F32 && a.out_dtype != B2G_BF16)
-    return set_error(B2G_ERR_UNSUPPORTED, "attention: output must be F32 or BF16");
-  const size_t ob = a.out_dtype == B2G_F32 ? 4 : 2;
-  if ((reinterpret_cast<uintptr_t>(a.out) & 15u) != 0 || (a.ldo * ob) % 16 != 0)
-    return set_error(B2G_ERR_UNSUPPORTED, "attention: output base and row stride must be 16-byte aligned");
-  DeviceInfo* dev = nullptr;
-  b2g_status s = device_info(&dev);
-  if (s != B2G_OK) return s;
   const int64_t HD = H * D;
-  const int64_t nkb = (L + kFaKeys - 1) / kFaKeys;
-  const size_t qk_bytes = static_cast<size_t>(round_up(L * HD * 2, 256));
-  const size_t vt_bytes = static_cast<size_t>(round_up(HD * L * 2, 256));
-  const size_t bias_bytes = static_cast<size_t>(round_up(nkb * kFaKeys * 4, 256));
-  const size_t flag_bytes = static_cast<size_t>(round_up(nkb * kBiasRec * 4, 256));
+  const size_t op_bytes = static_cast<size_t>(round_up(L * HD * 2, 256));
   void* ws = nullptr;
-  if ((s = workspace_get(2 * qk_bytes + vt_bytes + bias_bytes + flag_bytes, &ws, kWsAttention)) != B2G_OK) return s;
+  b2g_status s;
+  if ((s = workspace_get(3 * op_bytes, &ws, kWsAttention)) != B2G_OK) return s;
   char* base = static_cast<char*>(ws);
   __nv_bfloat16* qb = reinterpret_cast<__nv_bfloat16*>(base);
-  __nv_bfloat16* kb = reinterpret_cast<__nv_bfloat16*>(base + qk_bytes);
-  __nv_bfloat16* vt = reinterpret_cast<__nv_bfloat16*>(base + 2 * qk_bytes);
-  float* bias_log2 = reinterpret_cast<float*>(base + 2 * qk_bytes + vt_bytes);
-  int* bias_flags = reinterpret_cast<int*>(base + 2 * qk_bytes + vt_bytes + bias_bytes);
+  __nv_bfloat16* kb = reinterpret_cast<__nv_bfloat16*>(base + op_bytes);
+  __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(base + 2 * op_bytes);
 
-  // The V tiles write 4 tokens (8 bytes) per thread and read float4 rows.
   PrepArgs pa{};
-  pa.x[0] = a.q; pa.x[1] = a.k;
-  pa.ldx[0] = a.ldq; pa.ldx[1] = a.ldk;
+  pa.x[0] = a.q; pa.x[1] = a.k; pa.x[2] = a.v;
+  pa.ldx[0] = a.ldq; pa.ldx[1] = a.ldk; pa.ldx[2] = a.ldv;
   pa.norm1[0] = a.q_norm; pa.norm1[1] = a.k_norm;
   pa.norm2[0] = a.q_norm2 ? a.q_norm2 : a.q_norm;
   pa.norm2[1] = a.k_norm2 ? a.k_norm2 : a.k_norm;
-  pa.out[0] = qb; pa.out[1] = kb;
+  pa.out[0] = qb; pa.out[1] = kb; pa.out[2] = vb;
   pa.norm_split = a.norm_split >= 0 && a.norm_split < L ? static_cast<int>(a.norm_split) : static_cast<int>(L);
   pa.eps = a.eps;
   pa.pe = a.pe;
-  pa.v = a.v; pa.ldv = a.ldv; pa.vt = vt;
-  pa.bias = a.key_bias; pa.bias_log2 = bias_log2; pa.bias_flags = bias_flags;
   pa.L = static_cast<int>(L); pa.H = static_cast<int>(H);
-  pa.padded = static_cast<int>(nkb * kFaKeys);
-  pa.rows_blocks = static_cast<int>((2 * L * H + 8 * kRowsPerWarp - 1) / (8 * kRowsPerWarp));
-  pa.vt_cols_tiles = static_cast<int>((HD + 63) / 64);
-  pa.vt_blocks = static_cast<int>((L + 63) / 64) * pa.vt_cols_tiles;
-  const unsigned blocks = static_cast<unsigned>(pa.rows_blocks + pa.vt_blocks + 1);
+  const unsigned blocks = static_cast<unsigned>((3 * L * H + 8 * kRowsPerWarp - 1) / (8 * kRowsPerWarp));
   if (D == 128) attn_prep_kernel<128><<<blocks, 256, 0, st>>>(pa);
   else attn_prep_kernel<64><<<blocks, 256, 0, st>>>(pa);
   note_launch();
   if ((s = check_cuda(cudaGetLastError(), "attention prologue kernel")) != B2G_OK) return s;
 
-  FaParams fp{};
-  fp.L = static_cast<int>(L);
-  fp.num_kb = static_cast<int>(nkb);
-  fp.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  fp.bias_log2 = bias_log2;
-  fp.bias_flags = bias_flags;
-  fp.out = a.out;
-  fp.ldo = a.ldo;
-  fp.out_bf16 = a.out_dtype == B2G_BF16 ? 1 : 0;
-  fp.err = dev->err_word;
-  if (D == 128) return launch_flash<128>(qb, kb, vt, fp, L, H, st);
-  return launch_flash<64>(qb, kb, vt, fp, L, H, st);
+  AttnBf16Args f;
+  f.q = qb; f.k = kb; f.v = vb;
+  f.ldq = f.ldk = f.ldv = HD;
+  f.key_bias = a.key_bias;
+  f.out = a.out; f.out_dtype = a.out_dtype; f.ldo = a.ldo;
+  f.L = L; f.H = H; f.D = D;
+  return flash_checked(f, st);
 }
 
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,

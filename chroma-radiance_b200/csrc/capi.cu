@@ -478,6 +478,64 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
   return attention_rope_ex(a, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
+                             float eps, void* stream) {
+  if (!descs || !rope || count < 1 || count > 2 || n_head < 1)
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: 1 or 2 descriptors with rope descriptors, n_head >= 1");
+  GemmProblem ps[2];
+  QkvRope rs[2];
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    const b2g_gemm_desc* d = descs + i;
+    if (d->epilogue != B2G_EPI_NONE) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: epilogue must be NONE");
+    if (d->d_dtype != B2G_BF16) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 output");
+    if (d->N != 3ll * n_head * 128) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: N must be 3 * n_head * 128");
+    if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16))
+      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 or fp16 operands of one type");
+    if (!rope[i].pe) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe is required");
+    GemmProblem p;
+    bool empty = false;
+    b2g_status s = desc_to_problem(d, "b2g_gemm_qkv_rope", &p, &empty);
+    if (s != B2G_OK) return s;
+    if (empty) continue;
+    if (p.K == 0) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: K must be positive");
+    rs[n].heads = n_head;
+    rs[n].eps = eps;
+    rs[n].pe = rope[i].pe;
+    rs[n].q_norm = rope[i].q_norm;
+    rs[n].k_norm = rope[i].k_norm;
+    p.rope = &rs[n];
+    p.epilogue = static_cast<b2g_epilogue>(kEpiQkvRope);
+    std::string why;
+    if (!tc_gemm_supported(p, &why)) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: " + why);
+    ps[n++] = p;
+  }
+  if (n == 0) return B2G_OK;
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n == 2 && tc_gemm_groupable(ps[0], ps[1])) return tc_gemm_launch_group(ps, 2, st);
+  for (int i = 0; i < n; ++i)
+    if ((s = tc_gemm_launch_group(ps + i, 1, st)) != B2G_OK) return s;
+  return B2G_OK;
+}
+
+b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                              int64_t L, int n_head, int d_head, const float* key_bias, void* out,
+                              b2g_dtype out_dtype, int64_t ldo, void* stream) {
+  if (n_head < 0 || d_head < 0 || L < 0) return set_error(B2G_ERR_INVALID, "b2g_attention_bf16: negative size");
+  if (L == 0 || n_head == 0) return B2G_OK;
+  AttnBf16Args a;
+  a.q = static_cast<const __nv_bfloat16*>(q); a.ldq = ldq;
+  a.k = static_cast<const __nv_bfloat16*>(k); a.ldk = ldk;
+  a.v = static_cast<const __nv_bfloat16*>(v); a.ldv = ldv;
+  a.key_bias = key_bias;
+  a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
+  a.L = L; a.H = n_head; a.D = d_head;
+  return attention_bf16(a, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_check_device_error(int* code) {
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);

@@ -1,6 +1,7 @@
 // engine.cuh — internal declarations shared by the engine's translation units.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <string>
@@ -28,6 +29,19 @@ struct GemmProblem {
   // summed with the other ranks' over NVLink inside the GEMM, see TpReduce.
   const struct TpReduce* tp = nullptr;
   int64_t tp_row0 = 0;      // first row of this problem in the partial / residual buffers
+  // Attention input projection (epilogue kEpiQkvRope), see QkvRope.
+  const struct QkvRope* rope = nullptr;
+};
+
+// Internal epilogue: D = [q | k | v] (N = 3 * heads * 128, bf16 out) with per-head RMSNorm
+// (when scales are given) and RoPE applied to the q and k heads inside the GEMM.
+constexpr int kEpiQkvRope = 4;
+struct QkvRope {
+  int64_t heads = 0;                // H; head_dim is 128
+  float eps = 1e-6f;
+  const float* pe = nullptr;        // RoPE table rows of this problem's first token [M][64][4]
+  const float* q_norm = nullptr;    // RMSNorm scales [128] of the q heads (NULL: no norm)
+  const float* k_norm = nullptr;    // and of the k heads
 };
 
 // Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *
@@ -118,6 +132,19 @@ struct AttnArgs {
   int64_t L = 0, H = 0, D = 0;
 };
 b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st);
+// The fused attention kernel alone, on bf16 operands already normed and rotated: Q, K, V
+// [L, ld] with head h at columns [h*D, (h+1)*D) (e.g. the three sections of one [L, 3*H*D]
+// buffer written by the kEpiQkvRope GEMM epilogue).
+struct AttnBf16Args {
+  const __nv_bfloat16 *q = nullptr, *k = nullptr, *v = nullptr;
+  int64_t ldq = 0, ldk = 0, ldv = 0;
+  const float* key_bias = nullptr;  // [L] additive, NULL: none
+  void* out = nullptr;
+  b2g_dtype out_dtype = B2G_F32;
+  int64_t ldo = 0;
+  int64_t L = 0, H = 0, D = 0;
+};
+b2g_status attention_bf16(const AttnBf16Args& a, cudaStream_t st);
 // Contiguous F32 [L, H*D] form of the above (no norm), the reference's attention_with_rope.
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,
                           float* out, int64_t L, int64_t H, int64_t D, cudaStream_t st);

@@ -78,6 +78,9 @@ struct TcGroup {
   const float* a_scale;    // E4M3: per-row scale of A [M]
   const float* b_scale;    // E4M3: per-column scale of B [N]
   long long tp_row0;       // tensor-parallel reduce: first row in the partial/residual buffers
+  const float* pe;         // kEpiQkvRope: RoPE table rows of the group's first token [M][64][4]
+  const float* qn;         // kEpiQkvRope: RMSNorm scales of q and k heads [128] (NULL: none)
+  const float* kn;
 };
 
 // Tensor maps of every group (kernel parameter; indexed by group at run time).
@@ -107,6 +110,8 @@ struct TcParams {
   float* const* tp_res;    // [world] F32 residual copies
   long long tp_ld_part, tp_ld_res;
   int* tp_counters;        // rank 0's per-slot arrival counters (epoch counting, never reset)
+  int hd;                  // kEpiQkvRope: H * 128, the width of each of the q, k, v sections
+  float eps;               // kEpiQkvRope: RMSNorm epsilon
   TcGroup g[kMaxGroups];
 };
 
@@ -258,6 +263,10 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, const TcGroup& G,
 // 4 KB staging area holds one fp32 chunk or two 16-bit chunks (double-buffered).  Gated
 // residual: the chunk holds gate * (acc + bias) and leaves as a TMA reduce-add into the fp32
 // residual, so residual + gate * y is formed in L2 (two roundings: the product, then the sum).
+template <bool REDUCE, int OUT>
+__device__ __forceinline__ void stage_store_values(const CUtensorMap* tmD, uint8_t* stage, int& obuf, int bz,
+                                                   int m_warp0, int n0, const float (&v)[32], int lane);
+
 template <int EPI, int OUT>
 __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_t* stage, int& obuf, int bz,
                                                   int m_warp0, int n0, const uint32_t (&r)[32], const float* sb,
@@ -280,6 +289,14 @@ __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_
       for (int j = 0; j < 32; ++j) v[j] *= (n0 + j < N) ? __ldg(gp + j) : 0.f;
     }
   }
+  stage_store_values<EPI == B2G_EPI_GATED_RESIDUAL, OUT>(tmD, stage, obuf, bz, m_warp0, n0, v, lane);
+}
+
+// The 32x32 chunk of final values `v` (row `lane` of the warp's 32 rows) through the warp's
+// staging buffer into one TMA store (REDUCE: TMA reduce-add) at columns n0, rows m_warp0...
+template <bool REDUCE, int OUT>
+__device__ __forceinline__ void stage_store_values(const CUtensorMap* tmD, uint8_t* stage, int& obuf, int bz,
+                                                   int m_warp0, int n0, const float (&v)[32], int lane) {
   uint8_t* buf = stage;
   if constexpr (OUT == OUT_F32) {
     if (lane == 0) bulk_wait_group_read<0>();  // the previous store from this buffer has read it
@@ -309,7 +326,7 @@ __device__ __forceinline__ void stage_store_chunk(const CUtensorMap* tmD, uint8_
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    if constexpr (EPI == B2G_EPI_GATED_RESIDUAL)
+    if constexpr (REDUCE)
       tma_reduce_add_3d(tmD, buf, n0, m_warp0, bz);
     else
       tma_store_3d(tmD, buf, n0, m_warp0, bz);
@@ -519,6 +536,77 @@ __device__ __forceinline__ void prefetch_residual(const TcParams& p, const TcGro
   }
 }
 
+// Attention input projection (kEpiQkvRope, BN = 256): the tile's columns lie in one of the q,
+// k, v sections of [q | k | v] (each H heads of 128) and each thread owns one row of one
+// 128-column head.  q and k heads get RMSNorm with their learned scale (rms_norm,
+// kernels.cu:174-207, as qk_norm applies it, chroma.cuh:513-515: x * rsqrt(mean(x^2) + eps) *
+// w) and RoPE from the table row of the token (apply_rope_fused_bf16, rope.cuh:180-221: pair
+// (x0, x1) -> (x0 c0 + x1 c1, x0 c2 + x1 c3) with the row's (cos, -sin, sin, cos) group); v
+// passes through.  Everything leaves as bf16 through the TMA store path: the attention kernel
+// reads its operands from this buffer, so the fp32 projection never goes to memory.
+// Pass 1 reads the head's 128 accumulator columns from TMEM for the sum of squares, pass 2
+// reads them again and writes the result.
+template <int BN, typename Release>
+__device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
+                                              uint32_t tacc, Release release, const CUtensorMap* tmD, int m,
+                                              int n_base) {
+  static_assert(BN == 256, "one 128-column head per thread");
+  const int c0 = e.half * 4;           // this warp's first 32-column chunk in the tile
+  const int col = n_base + c0 * 32;    // first column of the head (uniform across the warp)
+  const int m_warp0 = m - e.lane;
+  const int sec = col / p.hd;          // 0 q, 1 k, 2 v
+  const float* norm = sec == 0 ? G.qn : (sec == 1 ? G.kn : nullptr);
+  const float* sb = p.bias_kind ? e.sbias + c0 * 32 : nullptr;
+  float inv = 1.f;
+  if (norm) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {
+      uint32_t r[32];
+      float v[32];
+      tmem_ld_32x32b_x32(tacc + (c0 + i) * 32, r);
+      tmem_wait_ld();
+      chunk_values<B2G_EPI_NONE>(r, sb ? sb + i * 32 : nullptr, p.alpha, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
+    }
+    inv = rsqrtf(ss / 128.0f + p.eps);
+  }
+  const float4* pe_row = reinterpret_cast<const float4*>(G.pe) + static_cast<long long>(m < G.M ? m : G.M - 1) * 64;
+  uint32_t r[2][32];
+  tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    tmem_wait_ld();
+    if (i + 1 < 4) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);
+    if (i == 3) release();
+    float v[32];
+    chunk_values<B2G_EPI_NONE>(r[i & 1], sb ? sb + i * 32 : nullptr, p.alpha, v);
+    if (sec < 2) {
+      if (norm) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(norm + i * 32 + j));
+          v[j] = v[j] * inv * w.x;
+          v[j + 1] = v[j + 1] * inv * w.y;
+          v[j + 2] = v[j + 2] * inv * w.z;
+          v[j + 3] = v[j + 3] * inv * w.w;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {  // pair i*16 + j of the head
+        const float4 c = __ldg(pe_row + i * 16 + j);
+        const float x0 = v[2 * j], x1 = v[2 * j + 1];
+        v[2 * j] = x0 * c.x + x1 * c.y;
+        v[2 * j + 1] = x0 * c.z + x1 * c.w;
+      }
+    }
+    if (m_warp0 < G.M && col < p.N) stage_store_values<false, OUT_BF16>(tmD, e.buf, obuf, 0, m_warp0, col + i * 32, v,
+                                                                       e.lane);
+  }
+  named_bar_sync(1, kEpiThreads);  // the staged bias is reused next item
+}
+
 // Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
 // accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
 // after this warp's last chunk is read.  With split-K, each split stores its raw fp32
@@ -530,6 +618,9 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
                                               int n_base, int slot, int split) {
   if constexpr (EPI == kEpiTpReduce) {
     tp_epilogue_item<BN>(p, G, e, tacc, release, m, n_base, slot);
+    return;
+  } else if constexpr (EPI == kEpiQkvRope) {
+    if constexpr (BN == 256) qkv_rope_item<BN>(p, G, e, obuf, tacc, release, tmD, m, n_base);
     return;
   }
   float rs = 0.f;  // E4M3: this row's activation scale
@@ -1103,6 +1194,10 @@ b2g_status dispatch_out(const TcMaps& maps, const TcParams& prm, int grid, b2g_e
   if constexpr (KIND == 0) {
     if (static_cast<int>(epi) == kEpiTpReduce)
       return launch_one<PAIR, BN, STAGES, kEpiTpReduce, OUT_F32, 0>(maps, prm, grid, st);
+    if (static_cast<int>(epi) == kEpiQkvRope) {
+      if constexpr (BN == 256) return launch_one<PAIR, BN, STAGES, kEpiQkvRope, OUT_BF16, 0>(maps, prm, grid, st);
+      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: 256-column tiles only");
+    }
   }
   if (epi == B2G_EPI_GATED_RESIDUAL)
     return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, KIND>(maps, prm, grid, st);
@@ -1164,7 +1259,9 @@ bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
   return a.N == b.N && a.K == b.K && a.batch == 1 && b.batch == 1 && a.a_dtype == b.a_dtype &&
          a.b_dtype == b.b_dtype && a.d_dtype == b.d_dtype && a.epilogue == b.epilogue && a.alpha == b.alpha &&
          (a.bias == nullptr) == (b.bias == nullptr) && (!a.bias || a.bias_dtype == b.bias_dtype) &&
-         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr) && a.tp == b.tp;
+         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr) && a.tp == b.tp &&
+         (a.rope == nullptr) == (b.rope == nullptr) &&
+         (!a.rope || (a.rope->heads == b.rope->heads && a.rope->eps == b.rope->eps));
 }
 
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) { return tc_gemm_launch_group(&p, 1, st); }
@@ -1199,6 +1296,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   for (int cand = 0; cand < 3; ++cand) {
     if (cand == VPAIR && !g_allow_pair) continue;
     if (cand != V128 && p.N <= 128) continue;
+    if (cand == V128 && p.rope) continue;  // the rope epilogue needs a whole head per thread
     const long long tm = cand == VPAIR ? 256 : 128, tn = cand == V128 ? 128 : 256;
     long long tiles = 0;
     for (int i = 0; i < count; ++i) tiles += ps[i].batch * ((ps[i].M + tm - 1) / tm) * ((p.N + tn - 1) / tn);
@@ -1221,7 +1319,8 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     if (g_force_splits <= 0) splits = 1;
   }
   if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
-  if (nkb == 0 || !p.allow_split || p.tp) splits = 1;
+  if (nkb == 0 || !p.allow_split || p.tp || p.rope) splits = 1;
+  if (p.rope && v == V128) v = g_allow_pair ? VPAIR : V256;
   const bool pair = v == VPAIR;
   const int bn = v == V128 ? 128 : 256;
   const int tile_m = pair ? 256 : kBM;
@@ -1252,6 +1351,9 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     G.a_scale = q.a_scale;
     G.b_scale = q.b_scale;
     G.tp_row0 = q.tp_row0;
+    G.pe = q.rope ? q.rope->pe : nullptr;
+    G.qn = q.rope ? q.rope->q_norm : nullptr;
+    G.kn = q.rope ? q.rope->k_norm : nullptr;
     G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
                (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
     all_vec = all_vec && G.vec_ok;
@@ -1284,6 +1386,21 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   memset(&maps, 0, sizeof(maps));
   const uint32_t b_box = v == V256 ? 256u : 128u;
   prm.tma_store = all_vec && g_tma_store && !p.tp ? 1 : 0;
+  if (p.rope) {
+    const QkvRope& r = *p.rope;
+    if (kind != 0 || p.d_dtype != B2G_BF16 || p.batch != 1)
+      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: bf16/fp16 operands, bf16 output, no batch");
+    if (r.heads < 1 || p.N != 3 * r.heads * 128)
+      return set_error(B2G_ERR_INVALID, "qkv rope epilogue: N must be 3 * heads * 128");
+    if (!prm.tma_store) return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: 16-byte aligned output rows required");
+    for (int i = 0; i < count; ++i) {
+      const QkvRope& ri = *ps[i].rope;
+      if (!ri.pe || !aligned16(ri.pe) || (ri.q_norm && !aligned16(ri.q_norm)) || (ri.k_norm && !aligned16(ri.k_norm)))
+        return set_error(B2G_ERR_INVALID, "qkv rope epilogue: pe and norm scales must be 16-byte aligned");
+    }
+    prm.hd = static_cast<int>(r.heads * 128);
+    prm.eps = r.eps;
+  }
   if (p.tp) {
     const TpReduce& t = *p.tp;
     if (kind != 0) return set_error(B2G_ERR_UNSUPPORTED, "tp reduce: bf16/fp16 operands only");

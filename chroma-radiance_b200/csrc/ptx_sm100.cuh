@@ -403,11 +403,26 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand with 128-byte swizzle (16-bit
+// types): each 128-byte row holds 64 consecutive M/N elements of one K index, as a TMA box of
+// 64 elements x rows writes it; 8-row groups (1024 bytes, the stride byte offset) step K by 8,
+// and the next 64 M/N elements start `atom_bytes` further on (the leading byte offset).
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(uint32_t saddr, uint32_t atom_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((atom_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(2u) << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 / kind::tf32 / kind::f8f6f4 with fp32 accumulation,
 // both operands K-major.  bits 4-5 D format (1 = f32); 7-9 A format, 10-12 B format
 // (kind::f16: 0 = f16, 1 = bf16; kind::tf32: 2; kind::f8f6f4: 0 = E4M3); bits 15/16 A/B
 // major (0 = K); bits 17-22 N >> 3; bits 24-28 M >> 4.
 enum : uint32_t { kFmtF16 = 0, kFmtBF16 = 1, kFmtTF32 = 2, kFmtE4M3 = 0 };
+constexpr uint32_t kIdescBMajorMN = 1u << 16;  // B operand MN-major (N contiguous in shared memory)
 __host__ __device__ constexpr uint32_t idesc_make(uint32_t fmt, int m, int n) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);

@@ -53,8 +53,11 @@ class EngineOps:
     def gemm(self, x, w, bias=None, out=None, epilogue="none", gate=None):
         return self.b2g.gemm(x, w, bias, out=out, epilogue=epilogue, gate=gate)
 
-    def attention(self, q, k, v, pe, n_head, d_head, **kw):
-        return self.b2g.attention_qknorm_rope(q, k, v, pe, n_head, d_head, **kw)
+    def qkv_rope(self, problems, n_head):
+        return self.b2g.gemm_qkv_rope(problems, n_head)
+
+    def attention_bf16(self, q, k, v, n_head, d_head, attn_mask=None, out=None):
+        return self.b2g.attention_bf16(q, k, v, n_head, d_head, attn_mask=attn_mask, out=out)
 
     def bias_gated_residual(self, y, bias, gate, residual):
         self.b2g.bias_gated_residual(y, bias, gate, residual)
@@ -139,7 +142,7 @@ class TPScratch:
         hl, ml = _split(world, d)
         L, HDl = T + I, hl * d.dhead
         self.d, self.hl, self.HDl, self.ml = d, hl, HDl, ml
-        self.qkv = torch.empty((L, 3 * HDl), dtype=torch.float32, device=dev)
+        self.qkv = torch.empty((L, 3 * HDl), dtype=torch.bfloat16, device=dev)  # normed, rotated
         self.attn = torch.empty((L, HDl), dtype=torch.bfloat16, device=dev)
         self.part = torch.empty((L, d.hidden), dtype=torch.bfloat16, device=dev)
         self.h_txt = torch.empty((T, ml), dtype=torch.bfloat16, device=dev)
@@ -147,15 +150,24 @@ class TPScratch:
         self.cat = torch.empty((L, HDl + ml), dtype=torch.bfloat16, device=dev)
 
 
+def _qkv_attention_double(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, pe, mask,
+                          s: TPScratch) -> None:
+    """The rank's heads: qkv projections with qk_norm and RoPE in the epilogue (txt rows take
+    pe rows [0, T), img rows [T, L)), then attention over the txt + img sequence into s.attn."""
+    T, HDl = txt_mod1.shape[0], s.HDl
+    ops.qkv_rope([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T], pe=pe[:T],
+                       q_norm=txt_w.q_norm, k_norm=txt_w.k_norm),
+                  dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:], pe=pe[T:],
+                       q_norm=img_w.q_norm, k_norm=img_w.k_norm)], s.hl)
+    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
+    ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.attn)
+
+
 def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, txt_mod2, img_mod2, txt,
                     img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask, s: TPScratch) -> None:
     """This rank's share of double_block (chroma.cuh:808-964); txt, img replicated F32 streams."""
     T, HDl = txt.shape[0], s.HDl
-    ops.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
-                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
-    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
-    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm, q_norm2=img_w.q_norm,
-                  k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s)
     ops.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, out=s.part[:T]),
                     dict(x=s.attn[T:], w=img_w.proj_w, out=s.part[T:])])
     ops.all_reduce(s.part)
@@ -173,10 +185,11 @@ def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod
 def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch) -> None:
     """This rank's share of single_block (chroma.cuh:1101-1157); x the replicated F32 stream."""
     HDl = s.HDl
-    ops.gemm(x_mod, w.linear1_w[:3 * HDl], w.linear1_b[:3 * HDl], out=s.qkv)
+    ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
+                       q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
     ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
-    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask, out=s.cat[:, :HDl])
+    ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
     ops.gemm(s.cat, w.linear2_w, out=s.part)
     ops.all_reduce(s.part)
     ops.bias_gated_residual(s.part, w.linear2_b, gate, x)
@@ -253,11 +266,7 @@ def tp_double_block_fused(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_
     """tp_double_block with each row-split layer's all-reduce fused into its GEMM: the
     replicated txt and img streams are comm.res_double[:T] and [T:]."""
     T, HDl = txt_mod1.shape[0], s.HDl
-    ops.gemm_group([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T]),
-                    dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:])])
-    q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
-    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=txt_w.q_norm, k_norm=txt_w.k_norm, q_norm2=img_w.q_norm,
-                  k_norm2=img_w.k_norm, norm_split=T, attn_mask=mask, out=s.attn)
+    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s)
     comm.reduce("double", [dict(x=s.attn[:T], w=txt_w.proj_w, bias=txt_w.proj_b, gate=txt_gate1),
                            dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, gate=img_gate1)], [0, T])
     ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
@@ -270,8 +279,9 @@ def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, g
     """tp_single_block with linear2's all-reduce fused into its GEMM: the replicated stream is
     comm.res_single."""
     HDl = s.HDl
-    ops.gemm(x_mod, w.linear1_w[:3 * HDl], w.linear1_b[:3 * HDl], out=s.qkv)
+    ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
+                       q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
     ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
-    ops.attention(q, k, v, pe, s.hl, s.d.dhead, q_norm=w.q_norm, k_norm=w.k_norm, attn_mask=mask, out=s.cat[:, :HDl])
+    ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
     comm.reduce("single", [dict(x=s.cat, w=w.linear2_w, bias=w.linear2_b, gate=gate)], [0])

@@ -224,6 +224,35 @@ b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, i
  * is bounded (2 s): on timeout the device error word gets bit 8 (b2g_check_device_error). */
 b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream);
 
+/* Attention input projection with qk_norm and RoPE fused into the GEMM epilogue.  The
+ * reference runs these as three linears into F32 q, k, v, then qk_norm (rms_norm per head with
+ * a learned scale) on q and k (chroma.cuh:822-842 double block, chroma.cuh:1108-1116 single
+ * block), then RoPE + bf16 inside attention_with_rope (apply_rope_fused_bf16,
+ * cudnn_attention.cuh:449-476).  descs[i]: bf16/fp16 x [M,K] . w[N,K]^T + bias (F32) with
+ * N = 3 * n_head * 128 ([q | k | v] weight rows, as the reference's fused qkv weight stores
+ * them), epilogue B2G_EPI_NONE, bf16 output d [M, ldd] (16-byte aligned rows).  In the output
+ * the q and k heads are RMSNorm'd with rope[i].q_norm / k_norm ([128] F32 each, NULL: no norm;
+ * x * rsqrt(mean(x^2) + eps) * scale) and rotated by the pe table rows rope[i].pe (F32
+ * [M][64][4], the rows of problem i's tokens in the attention sequence); v is the plain
+ * product.  count 1 or 2 (the txt and img streams: one launch). */
+typedef struct {
+  const float* pe;       /* RoPE rows of this problem's first token, 16-byte aligned */
+  const float* q_norm;   /* [128] or NULL */
+  const float* k_norm;   /* [128] or NULL */
+} b2g_qkv_rope_desc;
+b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
+                             float eps, void* stream);
+
+/* The fused attention on bf16 operands that are already normed and rotated, e.g. the three
+ * sections of a b2g_gemm_qkv_rope output: q = d, k = d + H*D, v = d + 2*H*D, all with row
+ * stride ldd.  softmax(Q K^T / sqrt(d_head) + key_bias[key]) V per head (key_bias [L] F32 or
+ * NULL), out [L, ldo] F32 or BF16 with head h at columns h*d_head.  Replaces the cuDNN SDPA
+ * call of cudnn_attention_with_rope (cudnn_attention.cuh:408-443, 466-471), whose operands are
+ * bf16 at that point.  Q/K/V bases 16-byte aligned, row strides multiples of 8 elements. */
+b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                              int64_t L, int n_head, int d_head, const float* key_bias, void* out,
+                              b2g_dtype out_dtype, int64_t ldo, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

@@ -376,6 +376,22 @@ void oracle_rms_norm(const float* x, const float* scale, float* out, int64_t row
   }
 }
 
+/* RoPE on rows of heads, the rotation of apply_rope_fused_bf16 (rope.cuh:180-221) kept in
+ * fp32: x [L, H*D], pair j of a head -> (x_e*p0 + x_o*p1, x_e*p2 + x_o*p3) with p = pe[l][j]
+ * ([L, D/2, 4]: cos, -sin, sin, cos). */
+void oracle_rope(const float* x, const float* pe, float* out, int64_t L, int64_t H, int64_t D) {
+  const int64_t half = D / 2;
+  for (int64_t l = 0; l < L; ++l)
+    for (int64_t h = 0; h < H; ++h)
+      for (int64_t j = 0; j < half; ++j) {
+        const float* p = pe + (l * half + j) * 4;
+        const int64_t i = l * H * D + h * D + 2 * j;
+        const float e = x[i], o = x[i + 1];
+        out[i] = e * p[0] + o * p[1];
+        out[i + 1] = e * p[2] + o * p[3];
+      }
+}
+
 /*
  * Attention with RoPE, restating cudnn_attention_with_rope (cudnn_attention.cuh:449-476):
  *   Qr, Kr = RoPE(Q), RoPE(K) rounded to bf16 (apply_rope_fused_bf16, rope.cuh:180-221:

@@ -50,6 +50,7 @@ class Oracle:
         lib.oracle_gated_residual.argtypes = [_c_p, _c_p, _c_p, _c_p, _i64, _i64]
         lib.oracle_modulate.argtypes = [_c_p, _c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
         lib.oracle_rms_norm.argtypes = [_c_p, _c_p, _c_p, _i64, _i64, ctypes.c_float]
+        lib.oracle_rope.argtypes = [_c_p, _c_p, _c_p, _i64, _i64, _i64]
         lib.oracle_round.argtypes = [_c_p, ctypes.c_int, _c_p, _i64]
         lib.oracle_f32_to_e4m3_array.argtypes = [_c_p, _c_p, _i64]
         lib.oracle_e4m3_to_f32_array.argtypes = [_c_p, _c_p, _i64]
@@ -188,6 +189,15 @@ class Oracle:
         out = acc * sa.astype(np.float64)[:, None] * sb.astype(np.float64)[None, :]
         if bias is not None:
             out = out + bias.astype(np.float64)[None, :]
+        return out
+
+    def rope(self, x, pe, n_head):
+        """RoPE rotation of F32 [L, H*D] rows by pe [L, D/2, 4], kept in fp32."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        pe = np.ascontiguousarray(pe, dtype=np.float32)
+        L, HD = x.shape
+        out = np.empty_like(x)
+        self.lib.oracle_rope(_np_ptr(x), _np_ptr(pe), _np_ptr(out), L, n_head, HD // n_head)
         return out
 
     def rms_norm(self, x, scale, eps=1e-6):

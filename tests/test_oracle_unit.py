@@ -150,3 +150,23 @@ def test_e4m3_quantisation_error_is_inherent(oracle):
     rms = np.sqrt(np.mean((y8 - y) ** 2) / np.mean(y ** 2))
     assert 0.024 < per_elem < 0.029
     assert 0.033 < rms < 0.041
+
+
+def test_rope_is_the_attention_rotation(oracle):
+    """oracle.rope rotates each (even, odd) pair by its pe row: pair norms are kept, the
+    inverse table (cos, sin, -sin, cos) undoes it, and it agrees with the pair formula of
+    apply_rope_fused_bf16 in numpy (to an fp32 ulp: the C code may contract into FMAs)."""
+    rng = np.random.default_rng(5)
+    L, H, D = 9, 3, 16
+    x = rng.standard_normal((L, H * D)).astype(np.float32)
+    ang = rng.uniform(0, 2 * np.pi, (L, D // 2))
+    pe = np.stack([np.cos(ang), -np.sin(ang), np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+    inv = np.stack([np.cos(ang), np.sin(ang), -np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+    y = oracle.rope(x, pe, H)
+    pairs = lambda a: np.hypot(a[:, 0::2], a[:, 1::2])
+    assert np.allclose(pairs(y), pairs(x), rtol=1e-6, atol=1e-6)
+    assert np.allclose(oracle.rope(y, inv, H), x, rtol=1e-5, atol=1e-5)
+    e, o = x.reshape(L, H, D // 2, 2)[..., 0], x.reshape(L, H, D // 2, 2)[..., 1]
+    p = pe[:, None]
+    want = np.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(L, H * D)
+    assert np.allclose(y, want, rtol=1e-6, atol=1e-6)

@@ -1,0 +1,198 @@
+"""The block's attention input path: the qkv GEMM with qk_norm and RoPE in its epilogue
+(b2g_gemm_qkv_rope, bf16 [q | k | v] out) and the fused attention reading that buffer
+(b2g_attention_bf16), against the oracle's linear, rms_norm, rope and attention on the same
+seeded inputs.
+
+Tolerances: the epilogue's output is bf16, so each element may differ from the fp32 oracle by
+half a bf16 ulp (2^-8 relative) plus fp32 rounding noise; attention as in the other attention
+tests (max|d|/max|ref| < 1e-2 against the oracle, which rounds P and O to bf16 as cuDNN does).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+DH = 128
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def pe_table(L: int, D: int, seed: int) -> np.ndarray:
+    g = np.random.default_rng(seed)
+    ang = g.uniform(0, 2 * np.pi, (L, D // 2))
+    return np.stack([np.cos(ang), -np.sin(ang), np.sin(ang), np.cos(ang)], -1).astype(np.float32)
+
+
+def identity_pe(L: int, D: int) -> np.ndarray:
+    pe = np.zeros((L, D // 2, 4), np.float32)
+    pe[..., 0] = 1.0
+    pe[..., 3] = 1.0
+    return pe
+
+
+def qkv_oracle(oracle, x, w, bias, pe, H, qn, kn):
+    """linear -> per-head rms_norm (when a scale is given) -> rope on q and k; v plain."""
+    y = oracle.linear(bits(x), 2, bits(w), 2, bias.cpu().numpy())
+    HD = H * DH
+
+    def nr(a, s):
+        a = np.ascontiguousarray(a)
+        if s is not None:
+            a = oracle.rms_norm(a.reshape(-1, DH), s.cpu().numpy()).reshape(a.shape)
+        return oracle.rope(a, pe, H)
+
+    return np.concatenate([nr(y[:, :HD], qn), nr(y[:, HD:2 * HD], kn), y[:, 2 * HD:]], 1)
+
+
+def assert_bf16_of(got: torch.Tensor, want: np.ndarray):
+    g = got.float().cpu().numpy().astype(np.float64)
+    w = want.astype(np.float64)
+    assert np.isfinite(g).all()
+    slack = 2.0 ** -8 * np.abs(w) + 1e-5 * np.abs(w).max()
+    bad = np.abs(g - w) > slack
+    assert not bad.any(), f"{bad.sum()} elements off, worst {np.abs(g - w).max():.3e}"
+
+
+def seeded(shape, seed, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+@pytest.mark.parametrize("M0,M1,H,K,norms,variant", [(40, 200, 2, 256, True, -1), (333, 0, 3, 200, False, -1),
+                                                      (130, 260, 2, 320, True, 1), (64, 64, 4, 128, True, 0)])
+def test_gemm_qkv_rope_vs_oracle(engine, oracle, M0, M1, H, K, norms, variant):
+    """Two problems (txt rows take pe rows [0, M0), img rows [M0, M0+M1)) in one launch, their
+    own norm scales; ragged M, K not a multiple of 64, H*128 not a multiple of the 256-column
+    tile (a tile then spans two sections), no norm; every kernel variant (the 128-column one
+    is promoted to 256 columns)."""
+    N = 3 * H * DH
+    L = M0 + M1
+    pe = pe_table(L, DH, L + K)
+    pe_d = torch.from_numpy(pe).to(DEV)
+    probs, wants = [], []
+    for i, (m, r0) in enumerate(((M0, 0), (M1, M0))):
+        if m == 0:
+            continue
+        x = seeded((m, K), 10 * i + 1)
+        w = seeded((N, K), 10 * i + 2, 0.05)
+        b = seeded((N,), 10 * i + 3, 0.05, torch.float32)
+        qn = (1 + 0.2 * seeded((DH,), 10 * i + 4, 1.0, torch.float32)) if norms else None
+        kn = (1 + 0.2 * seeded((DH,), 10 * i + 5, 1.0, torch.float32)) if norms else None
+        probs.append(dict(x=x.to(DEV), w=w.to(DEV), bias=b.to(DEV), pe=pe_d[r0:r0 + m],
+                          q_norm=qn.to(DEV) if norms else None, k_norm=kn.to(DEV) if norms else None))
+        wants.append(qkv_oracle(oracle, x, w, b, pe[r0:r0 + m], H, qn, kn))
+    engine.set_gemm_variant(variant)
+    try:
+        outs = engine.gemm_qkv_rope(probs, H)
+        torch.cuda.synchronize()
+    finally:
+        engine.set_gemm_variant(-1)
+    for got, want in zip(outs, wants):
+        assert got.dtype == torch.bfloat16 and got.shape == want.shape
+        assert_bf16_of(got, want)
+
+
+def test_gemm_qkv_rope_config2_shape(engine):
+    """The double block's qkv layer at 512^2 (txt 512 + img 1024 rows, 24 heads, K 3072) into
+    row views of one [1536, 9216] buffer, against a float64 torch restatement on the GPU."""
+    T, I, H, K = 512, 1024, 24, 3072
+    N = 3 * H * DH
+    L = T + I
+    pe = torch.from_numpy(pe_table(L, DH, 11)).to(DEV)
+    buf = torch.zeros((L, N), dtype=torch.bfloat16, device=DEV)
+    probs, refs = [], []
+    for i, (m, r0) in enumerate(((T, 0), (I, T))):
+        x = seeded((m, K), 50 + i).to(DEV)
+        w = seeded((N, K), 60 + i, 0.02).to(DEV)
+        b = seeded((N,), 70 + i, 0.02, torch.float32).to(DEV)
+        qn = (1 + 0.2 * seeded((DH,), 80 + i, 1.0, torch.float32)).to(DEV)
+        kn = (1 + 0.2 * seeded((DH,), 90 + i, 1.0, torch.float32)).to(DEV)
+        probs.append(dict(x=x, w=w, bias=b, out=buf[r0:r0 + m], pe=pe[r0:r0 + m], q_norm=qn, k_norm=kn))
+        y = (x.double() @ w.double().t() + b.double()).reshape(m, 3, H, DH)
+        p = pe[r0:r0 + m].double().reshape(m, 1, DH // 2, 4)
+
+        def nr(a, s):
+            a = a * torch.rsqrt((a * a).mean(-1, keepdim=True) + 1e-6) * s.double()
+            e, o = a[..., 0::2], a[..., 1::2]
+            return torch.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(m, H, DH)
+
+        refs.append(torch.stack([nr(y[:, 0], qn), nr(y[:, 1], kn), y[:, 2]], 1).reshape(m, N))
+    engine.gemm_qkv_rope(probs, H)
+    torch.cuda.synchronize()
+    want = torch.cat(refs).cpu().numpy()
+    assert_bf16_of(buf, want)
+
+
+def test_gemm_qkv_rope_rejects_bad_arguments(engine):
+    x = torch.zeros((8, 64), dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros((3 * 2 * DH, 64), dtype=torch.bfloat16, device=DEV)
+    pe = torch.zeros((8, 64, 4), device=DEV)
+    with pytest.raises(engine.B2GError):
+        engine.gemm_qkv_rope([dict(x=x, w=w, pe=pe)], 3)   # N != 3 * n_head * 128
+    with pytest.raises(engine.B2GError):
+        engine.gemm_qkv_rope([dict(x=x, w=w, pe=pe, out=torch.zeros((8, 768), device=DEV))], 2)  # F32 out
+
+
+@pytest.mark.parametrize("L,H,D,mask_kind,out_bf16", [(131, 2, 128, "pad", False), (256, 3, 64, "none", True),
+                                                       (300, 2, 128, "general", False), (1, 1, 64, "none", False)])
+def test_attention_bf16_vs_oracle(engine, oracle, L, H, D, mask_kind, out_bf16):
+    """q, k, v as column sections of one bf16 [L, 3*H*D] buffer (row stride 3*H*D); L not a
+    multiple of 8 or of the 128-key block; padding mask, general bias with -inf keys, none;
+    output into a column view of a wider buffer."""
+    HD = H * D
+    qkv = seeded((L, 3 * HD), L + D, 1.0)
+    mask = np.zeros(L, np.float32)
+    if mask_kind == "pad":
+        mask[L // 3:L // 3 + 21] = -np.inf
+    elif mask_kind == "general":
+        mask = (np.random.default_rng(L).standard_normal(L) * 2.0).astype(np.float32)
+        mask[5:17] = -np.inf
+    dq = qkv.to(DEV)
+    out_w = torch.zeros((L, HD + 16), dtype=torch.bfloat16 if out_bf16 else torch.float32, device=DEV)
+    m = torch.from_numpy(mask).to(DEV) if mask_kind != "none" else None
+    engine.attention_bf16(dq[:, :HD], dq[:, HD:2 * HD], dq[:, 2 * HD:], H, D, attn_mask=m, out=out_w[:, 8:8 + HD])
+    torch.cuda.synchronize()
+    f = qkv.float().numpy()
+    want = oracle.attention_rope(f[:, :HD].reshape(L, H, D), f[:, HD:2 * HD].reshape(L, H, D),
+                                 f[:, 2 * HD:].reshape(L, H, D), identity_pe(L, D),
+                                 mask if mask_kind != "none" else None)
+    got_w = out_w.float().cpu().numpy()
+    assert np.all(got_w[:, :8] == 0) and np.all(got_w[:, 8 + HD:] == 0)
+    got = got_w[:, 8:8 + HD]
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) < 1e-2
+
+
+def test_fused_path_matches_the_separate_one(engine):
+    """The block's new path (qkv GEMM with norm + RoPE epilogue, attention on bf16) against the
+    engine's separate path (F32 qkv GEMM, attention_qknorm_rope prologue + the same kernel) at
+    config-2 size: both round q, k, v to bf16 once, so they agree to bf16 rounding of inputs."""
+    T, I, H, K = 512, 1024, 24, 3072
+    HD, N, L = H * DH, 3 * H * DH, T + I
+    pe = torch.from_numpy(pe_table(L, DH, 5)).to(DEV)
+    mask = torch.zeros(L, device=DEV)
+    mask[100:512] = float("-inf")
+    xs = [seeded((m, K), 100 + i).to(DEV) for i, m in enumerate((T, I))]
+    ws = [seeded((N, K), 110 + i, 0.02).to(DEV) for i in range(2)]
+    bs = [seeded((N,), 120 + i, 0.02, torch.float32).to(DEV) for i in range(2)]
+    ns = [(1 + 0.2 * seeded((DH,), 130 + i, 1.0, torch.float32)).to(DEV) for i in range(4)]
+    buf = torch.empty((L, N), dtype=torch.bfloat16, device=DEV)
+    engine.gemm_qkv_rope([dict(x=xs[0], w=ws[0], bias=bs[0], out=buf[:T], pe=pe[:T], q_norm=ns[0], k_norm=ns[1]),
+                          dict(x=xs[1], w=ws[1], bias=bs[1], out=buf[T:], pe=pe[T:], q_norm=ns[2], k_norm=ns[3])], H)
+    fused = engine.attention_bf16(buf[:, :HD], buf[:, HD:2 * HD], buf[:, 2 * HD:], H, DH, attn_mask=mask)
+    f32 = torch.empty((L, N), device=DEV)
+    engine.gemm(xs[0], ws[0], bs[0], out=f32[:T])
+    engine.gemm(xs[1], ws[1], bs[1], out=f32[T:])
+    sep = engine.attention_qknorm_rope(f32[:, :HD], f32[:, HD:2 * HD], f32[:, 2 * HD:], pe, H, DH, q_norm=ns[0],
+                                       k_norm=ns[1], q_norm2=ns[2], k_norm2=ns[3], norm_split=T, attn_mask=mask)
+    torch.cuda.synchronize()
+    a, b = fused.double().cpu().numpy().ravel(), sep.double().cpu().numpy().ravel()
+    assert rel_err(a, b) < 1e-2
+    assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999

@@ -43,23 +43,27 @@ class TorchOps:
             out.copy_(y.to(out.dtype))
         return out
 
-    def attention(self, q, k, v, pe, n_head, d_head, q_norm=None, k_norm=None, q_norm2=None, k_norm2=None,
-                  norm_split=-1, attn_mask=None, out=None, eps=1e-6):
-        L = q.shape[0]
+    def qkv_rope(self, problems, n_head, eps=1e-6):
+        for pr in problems:
+            y = pr["x"].float() @ pr["w"].float().t() + pr["bias"]
+            M = y.shape[0]
+            dh = y.shape[1] // (3 * n_head)
+            q, k, v = y.reshape(M, 3, n_head, dh).unbind(1)
+            p = pr["pe"].reshape(M, 1, dh // 2, 4)
 
-        def prep(x, n1, n2, rope):
-            x = x.float().reshape(L, n_head, d_head)
-            if n1 is not None:
-                scale = torch.stack([n1 if (norm_split < 0 or l < norm_split) else n2 for l in range(L)])
-                x = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * scale[:, None, :]
-            if rope:
-                p = pe.reshape(L, 1, d_head // 2, 4)
+            def norm_rope(x, scale):
+                if scale is not None:
+                    x = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * scale
                 e, o = x[..., 0::2], x[..., 1::2]
-                x = torch.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(L, n_head,
-                                                                                                          d_head)
-            return x.to(torch.bfloat16).float()
+                return torch.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(
+                    M, n_head, dh)
 
-        qq, kk, vv = prep(q, q_norm, q_norm2, True), prep(k, k_norm, k_norm2, True), prep(v, None, None, False)
+            y = torch.stack([norm_rope(q, pr["q_norm"]), norm_rope(k, pr["k_norm"]), v], 1).reshape(M, -1)
+            pr["out"].copy_(y.to(pr["out"].dtype))
+
+    def attention_bf16(self, q, k, v, n_head, d_head, attn_mask=None, out=None):
+        L = q.shape[0]
+        qq, kk, vv = (t.float().reshape(L, n_head, d_head) for t in (q, k, v))
         s = torch.einsum("lhd,mhd->hlm", qq, kk) / d_head ** 0.5
         if attn_mask is not None:
             s = s + attn_mask[None, None, :]
