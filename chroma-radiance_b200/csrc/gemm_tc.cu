@@ -110,6 +110,7 @@ struct TcParams {
   float* const* tp_res;    // [world] F32 residual copies
   long long tp_ld_part, tp_ld_res;
   int* tp_counters;        // rank 0's per-slot arrival counters (epoch counting, never reset)
+  int n_outer;             // tiles column-major over all groups' m-blocks (batch 1), see tile_coords
   int hd;                  // kEpiQkvRope: H * 128, the width of each of the q, k, v sections
   float eps;               // kEpiQkvRope: RMSNorm epsilon
   TcGroup g[kMaxGroups];
@@ -121,6 +122,19 @@ __host__ __device__ constexpr size_t smem_bytes(int a_bytes, int b_bytes, int st
 }
 
 __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi, int& bz, int& mb, int& nb) {
+  if (p.n_outer) {
+    // Column-major over the m-blocks of all groups: the last tiles are the last columns.  The
+    // qkv projection uses it so that the final wave holds v tiles, whose epilogue (no norm,
+    // no RoPE) is the short one and is not hidden behind a next mainloop.
+    const int nmb0 = p.g[0].num_m_blocks;
+    const int nmb_all = nmb0 + (p.groups > 1 ? p.g[1].num_m_blocks : 0);
+    nb = tile / nmb_all;
+    const int r = tile - nb * nmb_all;
+    gi = (p.groups > 1 && r >= nmb0) ? 1 : 0;
+    mb = r - (gi ? nmb0 : 0);
+    bz = 0;
+    return;
+  }
   gi = (p.groups > 1 && tile >= p.g[1].tile0) ? 1 : 0;
   const int nmb = p.g[gi].num_m_blocks;
   const int t = tile - p.g[gi].tile0;
@@ -1400,6 +1414,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     }
     prm.hd = static_cast<int>(r.heads * 128);
     prm.eps = r.eps;
+    prm.n_outer = 1;
   }
   if (p.tp) {
     const TpReduce& t = *p.tp;
