@@ -14,8 +14,10 @@ RoPE, QK^T and PV over 24 heads, 0/-inf key mask on 400 of the 512 text tokens).
             The engine replays the step as two CUDA graphs; weights (680 MB) are larger than
             L2, and a 256 MB buffer is also written before every step, outside the events.
   roofline  dominant kernel = the engine's tcgen05 GEMM (the linear layers): GEMM FLOPs /
-            summed GEMM launch time, from events recorded between the launches inside the
-            graphs during the timed steps; peak = MEASURED_PEAKS.json bf16_tflops.
+            summed GEMM launch time, from events recorded between the launches inside a
+            second copy of the graphs replayed after the timed steps (the timed graphs carry
+            no events between launches, so that consecutive kernels overlap their set-up and
+            tail); peak = MEASURED_PEAKS.json bf16_tflops.
   e2e       the same step through the public API with host buffers: the step's activations
             (modulated bf16 inputs, F32 residual streams, gates) copied from pinned host
             memory and the updated residual streams copied back, inside the event pair; the
@@ -424,18 +426,28 @@ def run_engine_config2(args) -> None:
     run_single()  # sizes the engine's workspaces before capture
     torch.cuda.synchronize(dev)
     cap = torch.cuda.Stream(dev)
+
+    def capture(with_marks):
+        gs, ms = [], []
+        for fn in (run_double, run_single):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(cap):
+                mk = _Marks(torch, cap) if with_marks else None
+                with torch.cuda.graph(g, stream=cap):
+                    if mk:
+                        mk.begin()
+                    fn(mk)
+            gs.append(g)
+            ms.append(mk)
+        return gs, ms
+
+    # The timed graphs hold only the engine's launches (consecutive kernels overlap set-up and
+    # tail through programmatic dependent launch); a second pair of graphs with timing events
+    # between the launches gives the per-operation breakdown.
     n0 = b2g.launch_count()
-    graphs, marks = [], []
-    for fn in (run_double, run_single):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(cap):
-            mk = _Marks(torch, cap)
-            with torch.cuda.graph(g, stream=cap):
-                mk.begin()
-                fn(mk)
-        graphs.append(g)
-        marks.append(mk)
+    graphs, _ = capture(False)
     launches_per_step = b2g.launch_count() - n0
+    marked, marks = capture(True)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -459,11 +471,16 @@ def run_engine_config2(args) -> None:
             b.record(stream)
             b.synchronize()
             per_step.append(a.elapsed_time(b))
-            for mk in marks:
-                for lab, ms in mk.durations().items():
-                    per_op.setdefault(lab, []).append(ms)
         barrier()
     total_ms = sum(per_step)
+    for i in range(max(3, min(args.steps, 20))):
+        flush.fill_(i & 0xFF)
+        for g in marked:
+            g.replay()
+        torch.cuda.synchronize(dev)
+        for mk in marks:
+            for lab, ms in mk.durations().items():
+                per_op.setdefault(lab, []).append(ms)
     b2g.check_device_error()
 
     # End to end with host buffers: inputs in on one side stream, outputs back on another.
@@ -555,7 +572,7 @@ def run_engine_config2(args) -> None:
         line["cpu_baseline"] = cpu_baseline(o, x_h, w_h, bias_h)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graphs
+    del graphs, marked
     if world > 1:
         torch.distributed.destroy_process_group()
 

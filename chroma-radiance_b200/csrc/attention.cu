@@ -138,6 +138,8 @@ __device__ __forceinline__ void prep_rows(const PrepArgs& a, long long row0, int
 
 template <int D>
 __global__ void __launch_bounds__(256, 4) attn_prep_kernel(const PrepArgs a) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   prep_rows<D>(a, (static_cast<long long>(blockIdx.x) * 8 + warp) * kRowsPerWarp, lane);
 }
@@ -269,6 +271,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // the set-up above overlapped the previous kernel's tail
+  griddep_launch_dependents();
 
   if (warp < 4) {
    regs_dec<kFaRegsIdle>();
@@ -546,9 +550,7 @@ b2g_status launch_flash(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16
                       "cudaFuncSetAttribute(flash_attn)")) != B2G_OK)
     return s;
   const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows)), static_cast<unsigned>(H));
-  flash_attn_kernel<D><<<grid, kFaThreads, smem, st>>>(tq, tk, tv, fp);
-  note_launch();
-  return check_cuda(cudaGetLastError(), "flash_attn launch");
+  return launch_pdl(flash_attn_kernel<D>, grid, dim3(kFaThreads), smem, st, "flash_attn launch", tq, tk, tv, fp);
 }
 
 // Shared checks and launch of the fused kernel on bf16 operands.
@@ -621,10 +623,9 @@ b2g_status attention_rope_ex(const AttnArgs& a, cudaStream_t st) {
   pa.pe = a.pe;
   pa.L = static_cast<int>(L); pa.H = static_cast<int>(H);
   const unsigned blocks = static_cast<unsigned>((3 * L * H + 8 * kRowsPerWarp - 1) / (8 * kRowsPerWarp));
-  if (D == 128) attn_prep_kernel<128><<<blocks, 256, 0, st>>>(pa);
-  else attn_prep_kernel<64><<<blocks, 256, 0, st>>>(pa);
-  note_launch();
-  if ((s = check_cuda(cudaGetLastError(), "attention prologue kernel")) != B2G_OK) return s;
+  s = D == 128 ? launch_pdl(attn_prep_kernel<128>, dim3(blocks), dim3(256), 0, st, "attention prologue kernel", pa)
+               : launch_pdl(attn_prep_kernel<64>, dim3(blocks), dim3(256), 0, st, "attention prologue kernel", pa);
+  if (s != B2G_OK) return s;
 
   AttnBf16Args f;
   f.q = qb; f.k = kb; f.v = vb;

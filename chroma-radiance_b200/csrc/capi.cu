@@ -55,6 +55,14 @@ b2g_status check_cuda(cudaError_t e, const char* what) {
 
 void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B2G_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 b2g_status device_info(DeviceInfo** out) {
   int dev = -1;
   b2g_status s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");

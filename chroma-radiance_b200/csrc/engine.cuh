@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <string>
+#include <utility>
 #include "../../include/b2g.h"
 
 namespace b2g {
@@ -71,6 +72,30 @@ b2g_status device_info(DeviceInfo** out);
 
 // Counts launches of this library's kernels (reported by b2g_launch_count).
 void note_launch(uint64_t n = 1);
+
+// Programmatic dependent launch for the hot kernels (B2G_PDL=0 in the environment turns it
+// off): a kernel launched this way may start while the previous kernel on the stream is
+// still finishing, so it runs its set-up (barriers, TMEM, descriptor prefetch) early and then
+// executes griddep_wait() in every CTA before it reads or writes any memory that an earlier
+// kernel may still use.
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+b2g_status launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  b2g_status s = check_cuda(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+  if (s == B2G_OK) note_launch();
+  return s;
+}
 
 // Workspaces (device memory owned by the library, grown on demand, never shrunk), one per
 // purpose so that one call can use several.  kWsCounters is zero-filled when (re)allocated

@@ -755,6 +755,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // the set-up above overlapped the previous kernel's tail
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -955,6 +957,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // barrier inits and the TMEM allocation are visible pair-wide
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // the set-up above overlapped the previous kernel's tail
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -1182,9 +1186,7 @@ b2g_status launch_kernel(Kern kern, size_t smem, const TcMaps& maps, const TcPar
   b2g_status s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "cudaFuncSetAttribute(tc_gemm)");
   if (s != B2G_OK) return s;
-  kern<<<grid, kThreads, smem, st>>>(maps, prm);
-  note_launch();
-  return check_cuda(cudaGetLastError(), "tc_gemm launch");
+  return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, st, "tc_gemm launch", maps, prm);
 }
 
 // Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.

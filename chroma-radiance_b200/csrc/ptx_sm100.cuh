@@ -403,6 +403,14 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw128(uint32_t saddr) {
   return d;
 }
 
+// Programmatic dependent launch: wait until the preceding kernel on the stream has completed
+// with its memory visible (returns at once when the kernel was launched without the
+// attribute), and let the next kernel's CTAs be scheduled.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor for an MN-major operand with 128-byte swizzle (16-bit
 // types): each 128-byte row holds 64 consecutive M/N elements of one K index, as a TMA box of
 // 64 elements x rows writes it; 8-row groups (1024 bytes, the stride byte offset) step K by 8,
