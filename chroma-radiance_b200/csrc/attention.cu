@@ -158,8 +158,11 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 //               S = Q K_j^T (M=128, N=128, K=D, both from shared memory) goes to the tile's
 //               TMEM S columns; P (bf16 pairs) overwrites the first 64 of them and is the A
 //               operand of P.V read straight from TMEM, V_j the MN-major B operand; O
-//               accumulates in TMEM.  S(j+1) is issued once P(j).V_j has retired (it
-//               overwrites P(j)).
+//               accumulates in TMEM.  S(j+1) overwrites P(j) but is issued right behind
+//               P(j).V_j without waiting for it: tcgen05.mma operations issued by one thread
+//               execute in issue order, so P.V has read P before S is written.  The softmax
+//               hands P over in two parts (keys 0-95, then 96-127), so P.V starts on the
+//               first 96 keys while the last 32 are still being exponentiated.
 //   warp 3      idle (completes the first warpgroup, which runs on 64 registers per thread)
 //   warps 4-7   softmax of tile A, warps 8-11 of tile B (216 registers per thread); warp w
 //               reads TMEM lanes 32*(w%4)..,
@@ -171,8 +174,8 @@ int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 //               At the end O / l is written in the caller's layout.
 // TMEM: tile t at columns [256t, 256t+128) S/P and [256t+128, +D) O: 512 columns.
 // Barriers: q_full; k_full[3], k_empty[3] (commit after S_B(j)); v_full[2], v_empty[2]
-// (commit after P_B(j).V_j); per tile s_full (commit after S), p_full (4 softmax warps),
-// pv_done (commit after P.V).  Every wait is bounded; on timeout the kernel records the error
+// (commit after P_B(j).V_j); per tile s_full (commit after S), p_part and p_full (4 softmax
+// warps each: keys 0-95 / 96-127 of P written), pv_done (commit after P.V).  Every wait is bounded; on timeout the kernel records the error
 // word and winds down.
 constexpr int kFaThreads = 384;  // 3 warpgroups
 // Registers: launched at 168 per thread (64,512 per CTA); the producer/MMA warpgroup gives
@@ -234,7 +237,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint64_t* p_full = s_full + kFaTiles;
   uint64_t* pv_done = p_full + kFaTiles;
   uint64_t* drain_bar = pv_done + kFaTiles;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* p_part = drain_bar + 1;    // [tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_part + kFaTiles);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -255,6 +259,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     for (int t = 0; t < kFaTiles; ++t) {
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
+      mbar_init(&p_part[t], 4);
       mbar_init(&pv_done[t], 1);
     }
     mbar_init(drain_bar, 1);
@@ -345,21 +350,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       for (int j = 0; j < nkb && ok; ++j) {
         const int vs = j % VS;
         for (int t = 0; t < kFaTiles && ok; ++t) {
-          if (!(ok = mbar_wait(&p_full[t], j & 1, p.err, kErrWaitMma))) break;
+          const uint32_t v0 = smem_u32(sV + vs * Ly::kVBytes);
+          // 16 keys per MMA: P columns 8k.., V rows 16k.. (2 KB step).  Keys 0-95 as soon as the
+          // softmax has written them, keys 96-127 when all of P is there.
+          if (!(ok = mbar_wait(&p_part[t], j & 1, p.err, kErrWaitMma))) break;
           if (t == 0 && !(ok = mbar_wait(&v_full[vs], (j / VS) & 1, p.err, kErrWaitMma))) break;
           tc_fence_after();
-          const uint32_t v0 = smem_u32(sV + vs * Ly::kVBytes);
 #pragma unroll
-          for (int k = 0; k < 8; ++k)  // 16 keys per MMA: P columns 8k.., V rows 16k.. (2 KB step)
+          for (int k = 0; k < 6; ++k)
             umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k, smem_desc_mn_sw128(v0 + k * 2048, kFaBox),
                         idesc_o, (j | k) != 0 ? 1u : 0u);
+          if (!(ok = mbar_wait(&p_full[t], j & 1, p.err, kErrWaitMma))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int k = 6; k < 8; ++k)
+            umma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + 8 * k, smem_desc_mn_sw128(v0 + k * 2048, kFaBox),
+                        idesc_o, 1u);
           umma_commit(&pv_done[t]);
           if (t == kFaTiles - 1) umma_commit(&v_empty[vs]);  // both tiles have read V_j
           if (j + 1 < nkb) {
             if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, p.err, kErrWaitMma))) break;
-            // S(j+1) overwrites P(j): wait until P(j).V_j has retired.
-            if (!(ok = mbar_wait(&pv_done[t], j & 1, p.err, kErrWaitMma))) break;
-            tc_fence_after();
+            // S(j+1) overwrites P(j); issued behind P(j).V_j, which reads P first (issue order).
             issue_s(t, j + 1);
           }
         }
@@ -476,6 +487,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
         }
         tmem_st_32x32b_x16(sbase + c * 16, pk);
+        if (c == 2) {  // keys 0-95 of P are in TMEM: P.V can start on them
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_part[t]);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
