@@ -113,6 +113,10 @@ _SIGNATURES = {
     "b2g_attention_bf16": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                                    ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
+    "b2g_modulate_to_bf16": ([ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p],
+                             ctypes.c_int),
+    "b2g_modulate_to_e4m3": ([ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p],
+                             ctypes.c_int),
     "b2g_attention_with_rope": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p,
                                  ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
 }
@@ -510,6 +514,44 @@ def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_head: in
                                   L, n_head, d_head, _ptr(attn_mask), out.data_ptr(), _TORCH_TO_B2G[out.dtype],
                                   out.stride(0), ctypes.c_void_p(s)))
     return out
+
+
+def _modulate_args(x, shift, scale):
+    _require_cuda(x, shift, scale)
+    for t in (x, shift, scale):
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise B2GError("modulate: contiguous F32 x, shift and scale expected")
+    if x.dim() != 2 or shift.numel() != x.shape[1] or scale.numel() != x.shape[1]:
+        raise B2GError("modulate: x [M, C] with shift and scale [C]")
+    return x.shape
+
+
+def modulate_to_bf16(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6,
+                     out: torch.Tensor | None = None, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """modulate_to_bf16 (kernels.cu:552-599): bf16(LayerNorm(x) * (1 + scale) + shift), x [M, C] F32."""
+    lib = load()
+    M, C = _modulate_args(x, shift, scale)
+    if out is None:
+        out = torch.empty((M, C), dtype=torch.bfloat16, device=x.device)
+    if out.dtype != torch.bfloat16 or not out.is_contiguous() or out.shape != (M, C):
+        raise B2GError("modulate_to_bf16: contiguous bf16 out [M, C] expected")
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_modulate_to_bf16(x.data_ptr(), shift.data_ptr(), scale.data_ptr(), out.data_ptr(), M, C, eps,
+                                    ctypes.c_void_p(s)))
+    return out
+
+
+def modulate_to_e4m3(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6,
+                     stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """The modulated rows quantised per row to E4M3: (codes uint8 [M, C], row scales f32 [M])."""
+    lib = load()
+    M, C = _modulate_args(x, shift, scale)
+    codes = torch.empty((M, C), dtype=torch.uint8, device=x.device)
+    rs = torch.empty(M, dtype=torch.float32, device=x.device)
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_modulate_to_e4m3(x.data_ptr(), shift.data_ptr(), scale.data_ptr(), codes.data_ptr(),
+                                    rs.data_ptr(), M, C, eps, ctypes.c_void_p(s)))
+    return codes, rs
 
 
 def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None:

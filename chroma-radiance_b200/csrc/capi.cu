@@ -544,6 +544,22 @@ b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t
   return attention_bf16(a, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_modulate_to_bf16(const float* x, const float* shift, const float* scale, void* out, int64_t M,
+                                int64_t C, float eps, void* stream) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return modulate_rows(x, shift, scale, out, B2G_BF16, nullptr, M, C, eps, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_modulate_to_e4m3(const float* x, const float* shift, const float* scale, uint8_t* out,
+                                float* row_scale, int64_t M, int64_t C, float eps, void* stream) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return modulate_rows(x, shift, scale, out, B2G_E4M3, row_scale, M, C, eps, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_check_device_error(int* code) {
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);

@@ -6,9 +6,16 @@
 // and only then may bias and gate be applied, once.  This is the reference's gated_residual
 // (kernels.cu:942-968, x + gate * y) with the linear's bias (added in linear_lt's cuBLASLt
 // epilogue, cublas_ops.cuh:214-288) folded in.  y is bf16 (the all-reduced partials) or F32.
+//
+// Also the A-operand producer of the block GEMMs, modulate_to_bf16 (kernels.cu:552-599):
+// out = bf16(LN(x) * (1 + scale[c]) + shift[c]), LayerNorm without affine, eps 1e-6, its mean
+// and variance in two passes as the reference takes them; and the same values quantised per
+// token to E4M3 for the FP8 linears (scale absmax/448, the quantize_rows_e4m3 recipe of fp8.cu).
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cstdint>
 #include "engine.cuh"
+#include "ptx_sm100.cuh"
 
 namespace b2g {
 
@@ -53,7 +60,130 @@ __global__ void __launch_bounds__(256) bias_gated_residual_kernel(const void* __
   r[1] = r1;
 }
 
+// One 128-thread block per row of x [M, C] (16-byte aligned rows, C % 4 == 0,
+// C <= 128 * 4 * NV): the row is read from memory once into registers (NV float4 per thread),
+// then mean, variance about the mean and the modulated output; the block sums go through
+// four warp shuffles and a 4-entry shared array.  OUT 0: bf16; 1: E4M3 with a per-row scale.
+constexpr int kModThreads = 128;
+
+__device__ __forceinline__ float block_sum4(float v, float* red, int warp, int lane) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const float t = (red[0] + red[1]) + (red[2] + red[3]);
+  __syncthreads();  // red is reused by the next reduction
+  return t;
+}
+
+template <int NV, int OUT>
+__global__ void __launch_bounds__(kModThreads) modulate_rows_kernel(const float* __restrict__ x,
+                                                                    const float* __restrict__ shift,
+                                                                    const float* __restrict__ scale,
+                                                                    void* __restrict__ out,
+                                                                    float* __restrict__ row_scale, int M, int C,
+                                                                    float eps) {
+  __shared__ float red[4];
+  griddep_wait();
+  griddep_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * C);
+  const int nv4 = C >> 2;
+  float4 v[NV];
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = k * kModThreads + threadIdx.x;
+    v[k] = i < nv4 ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);  // streamed: read once
+    sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+  }
+  const float mean = block_sum4(sum, red, warp, lane) / static_cast<float>(C);
+  float var = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    if (k * kModThreads + static_cast<int>(threadIdx.x) < nv4) {
+      const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
+      var += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+  const float inv_std = rsqrtf(block_sum4(var, red, warp, lane) / static_cast<float>(C) + eps);
+  const float4* sc = reinterpret_cast<const float4*>(scale);
+  const float4* sh = reinterpret_cast<const float4*>(shift);
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = k * kModThreads + threadIdx.x;
+    if (i < nv4) {
+      const float4 a = __ldg(sc + i), b = __ldg(sh + i);
+      v[k].x = (v[k].x - mean) * inv_std * (1.0f + a.x) + b.x;
+      v[k].y = (v[k].y - mean) * inv_std * (1.0f + a.y) + b.y;
+      v[k].z = (v[k].z - mean) * inv_std * (1.0f + a.z) + b.z;
+      v[k].w = (v[k].w - mean) * inv_std * (1.0f + a.w) + b.w;
+      if constexpr (OUT == 0) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(v[k].x, v[k].y), hi = __floats2bfloat162_rn(v[k].z, v[k].w);
+        reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + row * C)[i] =
+            make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+      } else {
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+      }
+    }
+  }
+  if constexpr (OUT == 1) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[warp] = amax;
+    __syncthreads();
+    amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float inv = amax > 0.f ? 448.0f / amax : 1.0f;
+    if (threadIdx.x == 0) row_scale[row] = amax > 0.f ? amax / 448.0f : 1.0f;
+    uint32_t* orow = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(out) + row * C);
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int i = k * kModThreads + threadIdx.x;
+      if (i < nv4) {
+        const __nv_fp8x2_storage_t lo =
+            __nv_cvt_float2_to_fp8x2(make_float2(v[k].x * inv, v[k].y * inv), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t hi =
+            __nv_cvt_float2_to_fp8x2(make_float2(v[k].z * inv, v[k].w * inv), __NV_SATFINITE, __NV_E4M3);
+        orow[i] = static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+      }
+    }
+  }
+}
+
+template <int OUT>
+b2g_status launch_modulate(const float* x, const float* shift, const float* scale, void* out, float* row_scale,
+                           int64_t M, int64_t C, float eps, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>(M);
+  const int nv = static_cast<int>((C / 4 + kModThreads - 1) / kModThreads);
+  const int m = static_cast<int>(M), c = static_cast<int>(C);
+  auto kern = nv <= 2 ? modulate_rows_kernel<2, OUT>
+              : nv <= 4 ? modulate_rows_kernel<4, OUT>
+              : nv <= 6 ? modulate_rows_kernel<6, OUT> : modulate_rows_kernel<8, OUT>;
+  return launch_pdl(kern, dim3(grid), dim3(kModThreads), 0, st, "modulate launch", x, shift, scale, out, row_scale, m,
+                    c, eps);
+}
+
 }  // namespace
+
+b2g_status modulate_rows(const float* x, const float* shift, const float* scale, void* out, b2g_dtype out_dtype,
+                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st) {
+  if (M < 0 || C < 0) return set_error(B2G_ERR_INVALID, "modulate: negative size");
+  if (M == 0 || C == 0) return B2G_OK;
+  if (!x || !shift || !scale || !out) return set_error(B2G_ERR_INVALID, "modulate: null pointer");
+  if (out_dtype != B2G_BF16 && out_dtype != B2G_E4M3) return set_error(B2G_ERR_UNSUPPORTED, "modulate: bf16 or E4M3 out");
+  if (out_dtype == B2G_E4M3 && !row_scale) return set_error(B2G_ERR_INVALID, "modulate: E4M3 needs row scales");
+  if (C % 4 != 0 || C > 4096 || M > (1ll << 31) - 1)
+    return set_error(B2G_ERR_UNSUPPORTED, "modulate: C must be a multiple of 4 and at most 4096");
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(shift) |
+                         reinterpret_cast<uintptr_t>(scale);
+  const uintptr_t obits = reinterpret_cast<uintptr_t>(out);
+  if ((bits & 15u) || (obits & (out_dtype == B2G_BF16 ? 7u : 3u)))
+    return set_error(B2G_ERR_UNSUPPORTED, "modulate: x, shift, scale 16-byte and out 8/4-byte aligned");
+  if (out_dtype == B2G_BF16) return launch_modulate<0>(x, shift, scale, out, nullptr, M, C, eps, st);
+  return launch_modulate<1>(x, shift, scale, out, row_scale, M, C, eps, st);
+}
 
 b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias, const float* gate,
                                float* residual, int64_t ldr, int64_t M, int64_t N, cudaStream_t st) {

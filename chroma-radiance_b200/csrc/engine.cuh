@@ -170,6 +170,11 @@ struct AttnBf16Args {
   int64_t L = 0, H = 0, D = 0;
 };
 b2g_status attention_bf16(const AttnBf16Args& a, cudaStream_t st);
+
+// out = LN(x) * (1 + scale) + shift per row of x [M, C] F32 (no-affine LayerNorm, two-pass
+// statistics), written as bf16 or as per-row E4M3 with row_scale[M] (absmax / 448).
+b2g_status modulate_rows(const float* x, const float* shift, const float* scale, void* out, b2g_dtype out_dtype,
+                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st);
 // Contiguous F32 [L, H*D] form of the above (no norm), the reference's attention_with_rope.
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,
                           float* out, int64_t L, int64_t H, int64_t D, cudaStream_t st);

@@ -253,6 +253,24 @@ b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t
                               int64_t L, int n_head, int d_head, const float* key_bias, void* out,
                               b2g_dtype out_dtype, int64_t ldo, void* stream);
 
+/* The block GEMMs' A-operand producer.  Same arguments and meaning as the reference's
+ *   void modulate_to_bf16_cuda(const float* x, const float* shift, const float* scale,
+ *                              __nv_bfloat16* out, int64_t M, int64_t C, float eps)
+ *                                                       kernels.cu:592-599 (kernel :552-590)
+ * called before every block GEMM group (chroma.cuh:824, 835, 920, ...): out[m, c] =
+ * bf16((x[m, c] - mean_m) * rsqrt(var_m + eps) * (1 + scale[c]) + shift[c]), mean and variance
+ * of row m over its C values (variance about the mean, two passes).  x, shift, scale 16-byte
+ * aligned, out 8-byte aligned, C % 4 == 0 and C <= 4096 (else B2G_ERR_UNSUPPORTED). */
+b2g_status b2g_modulate_to_bf16(const float* x, const float* shift, const float* scale, void* out, int64_t M,
+                                int64_t C, float eps, void* stream);
+
+/* The same modulated values quantised per row to E4M3 for b2g_gemm_fp8's activations (no
+ * reference counterpart: the reference's quantised producers are INT8,
+ * kernels.cu:1988-2125): row_scale[m] = absmax_m / 448 (1 for an all-zero row), out = E4M3 of
+ * the fp32 modulated values times 448 / absmax_m, round to nearest even, saturating. */
+b2g_status b2g_modulate_to_e4m3(const float* x, const float* shift, const float* scale, uint8_t* out,
+                                float* row_scale, int64_t M, int64_t C, float eps, void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the
