@@ -555,7 +555,7 @@ def run_engine_config2(args) -> None:
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "traffic": profile_traffic("block_pair_config2_launches.md"),
                      "peak_source": peaks["source"] + " (burst bf16)",
-                     "kernel": "tc_gemm: the block pair's 7 linear-layer launches, FLOP-weighted",
+                     "kernel": "tc_gemm: the block pair's 6 linear-layer launches, FLOP-weighted",
                      "gemm_ms_per_step": round(gemm_ms, 5)},
         "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
         "breakdown_tflops": {lab: round(f / (mean_op[lab] * 1e-3) / 1e12, 1) for lab, _, f in ops},

@@ -67,7 +67,8 @@ class TpReduceDesc(ctypes.Structure):
 
 class QkvRopeDesc(ctypes.Structure):
     """b2g_qkv_rope_desc: RoPE rows and RMSNorm scales of one qkv projection problem."""
-    _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+    _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+                ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64)]
 
 
 _lib = None
@@ -467,15 +468,28 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
     view with 16-byte aligned rows; allocated when absent), pe (F32 RoPE rows of the
     problem's tokens, [M, 64, 4] or [M, 256]), q_norm / k_norm ([128] F32 or None).  Output
     columns [q | k | v]: q and k heads normed and rotated, v the plain product (+ bias).
-    Two problems (txt and img streams) run as one launch.
+    Two problems (txt and img streams) run as one launch.  One problem may carry gelu_out (a
+    bf16 [M, N - 3*n_head*128] view): w then has more rows, and those columns get bias + GELU
+    into gelu_out (the single block's linear1 in one launch); out holds the qkv columns.
     """
     lib = load()
     descs, ropes, outs, keep = [], [], [], []
     for pr in problems:
         out = pr.get("out")
+        qkv_cols = 3 * n_head * 128
+        tail = pr.get("gelu_out")
         if out is None:
-            out = torch.empty((pr["x"].shape[0], pr["w"].shape[0]), device=pr["x"].device, dtype=torch.bfloat16)
-        d, out = _gemm_desc(pr["x"], pr["w"], pr.get("bias"), out, None, "none", None)
+            out = torch.empty((pr["x"].shape[0], qkv_cols if tail is not None else pr["w"].shape[0]),
+                              device=pr["x"].device, dtype=torch.bfloat16)
+        if tail is not None:
+            _require_cuda(tail)
+            if (tail.dtype != torch.bfloat16 or tail.stride(1) != 1 or
+                    tail.shape != (pr["x"].shape[0], pr["w"].shape[0] - qkv_cols)):
+                raise B2GError("gemm_qkv_rope: gelu_out must be a bf16 [M, N - 3*n_head*128] view")
+            d, _ = _gemm_desc(pr["x"], pr["w"][:qkv_cols], pr.get("bias"), out, None, "none", None)
+            d.N = pr["w"].shape[0]
+        else:
+            d, out = _gemm_desc(pr["x"], pr["w"], pr.get("bias"), out, None, "none", None)
         pe = pr["pe"]
         qn, kn = pr.get("q_norm"), pr.get("k_norm")
         _require_cuda(pe, qn, kn)
@@ -485,7 +499,8 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
         if pe.numel() < pr["x"].shape[0] * 256:
             raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x")
         descs.append(d)
-        ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn)))
+        ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn), _ptr(tail),
+                                 tail.stride(0) if tail is not None else 0))
         outs.append(out)
         keep.append(pe)
     arr = (GemmDesc * len(descs))(*descs)

@@ -135,12 +135,11 @@ def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1,
 def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=None) -> None:
     """Updates x [L, 3072] (F32 residual stream) in place.  `mark` as in double_block."""
     mark = mark or _no_mark
-    n_qkv = 3 * HIDDEN
-    b2g.gemm_qkv_rope([dict(x=x_mod, w=w.linear1_w[:n_qkv], bias=w.linear1_b[:n_qkv], out=s.qkv, pe=pe,
-                            q_norm=w.q_norm, k_norm=w.k_norm)], HEADS)
-    mark("single.linear1_qkv")
-    b2g.gemm(x_mod, w.linear1_w[n_qkv:], w.linear1_b[n_qkv:], out=s.cat[:, HIDDEN:], epilogue="gelu")
-    mark("single.linear1_mlp")
+    # linear1 in one launch (its weight rows are [q | k | v | mlp]): the qkv columns get qk_norm
+    # + RoPE into s.qkv, the MLP columns bias + GELU straight into the linear2 concat buffer.
+    b2g.gemm_qkv_rope([dict(x=x_mod, w=w.linear1_w, bias=w.linear1_b, out=s.qkv, pe=pe, q_norm=w.q_norm,
+                            k_norm=w.k_norm, gelu_out=s.cat[:, HIDDEN:])], HEADS)
+    mark("single.linear1")
     q, k, v = s.qkv[:, :HIDDEN], s.qkv[:, HIDDEN:2 * HIDDEN], s.qkv[:, 2 * HIDDEN:]
     b2g.attention_bf16(q, k, v, HEADS, DHEAD, attn_mask=mask, out=s.cat[:, :HIDDEN])
     mark("single.attention")
@@ -163,7 +162,7 @@ def block_pair_ops(T: int, I: int) -> list[tuple[str, str, float]]:
     return [("double.qkv", "gemm", 2.0 * L * H3 * H), ("double.attention", "attention", att),
             ("double.proj", "gemm", 2.0 * L * H * H), ("double.mlp0", "gemm", 2.0 * L * MLP * H),
             ("double.mlp2", "gemm", 2.0 * L * H * MLP),
-            ("single.linear1_qkv", "gemm", 2.0 * L * H3 * H), ("single.linear1_mlp", "gemm", 2.0 * L * MLP * H),
+            ("single.linear1", "gemm", 2.0 * L * (H3 + MLP) * H),
             ("single.attention", "attention", att), ("single.linear2", "gemm", 2.0 * L * H * (H + MLP))]
 
 

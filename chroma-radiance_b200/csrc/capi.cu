@@ -497,21 +497,30 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     const b2g_gemm_desc* d = descs + i;
     if (d->epilogue != B2G_EPI_NONE) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: epilogue must be NONE");
     if (d->d_dtype != B2G_BF16) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 output");
-    if (d->N != 3ll * n_head * 128) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: N must be 3 * n_head * 128");
+    const int64_t qkv_cols = 3ll * n_head * 128;
+    const bool tail = rope[i].gelu_out != nullptr;
+    if (tail ? (count != 1 || d->N <= qkv_cols) : d->N != qkv_cols)
+      return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: N must be 3 * n_head * 128 (more, with one problem, for "
+                                        "a GELU tail)");
     if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16))
       return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 or fp16 operands of one type");
     if (!rope[i].pe) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe is required");
     GemmProblem p;
     bool empty = false;
-    b2g_status s = desc_to_problem(d, "b2g_gemm_qkv_rope", &p, &empty);
+    b2g_gemm_desc dq = *d;  // d holds the [q | k | v] columns only; the tail goes to gelu_out
+    dq.N = qkv_cols;
+    b2g_status s = desc_to_problem(&dq, "b2g_gemm_qkv_rope", &p, &empty);
     if (s != B2G_OK) return s;
     if (empty) continue;
+    p.N = d->N;
     if (p.K == 0) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: K must be positive");
     rs[n].heads = n_head;
     rs[n].eps = eps;
     rs[n].pe = rope[i].pe;
     rs[n].q_norm = rope[i].q_norm;
     rs[n].k_norm = rope[i].k_norm;
+    rs[n].gelu_out = rope[i].gelu_out;
+    rs[n].gelu_ld = rope[i].gelu_ld;
     p.rope = &rs[n];
     p.epilogue = static_cast<b2g_epilogue>(kEpiQkvRope);
     std::string why;

@@ -43,6 +43,8 @@ struct QkvRope {
   const float* pe = nullptr;        // RoPE table rows of this problem's first token [M][64][4]
   const float* q_norm = nullptr;    // RMSNorm scales [128] of the q heads (NULL: no norm)
   const float* k_norm = nullptr;    // and of the k heads
+  void* gelu_out = nullptr;         // optional: columns past 3 * heads * 128 -> bias + GELU, bf16 here
+  int64_t gelu_ld = 0;
 };
 
 // Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *

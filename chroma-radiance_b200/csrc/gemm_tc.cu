@@ -112,6 +112,8 @@ struct TcParams {
   int* tp_counters;        // rank 0's per-slot arrival counters (epoch counting, never reset)
   int n_outer;             // tiles column-major over all groups' m-blocks (batch 1), see tile_coords
   int hd;                  // kEpiQkvRope: H * 128, the width of each of the q, k, v sections
+  int split;               // kEpiQkvRope with a GELU tail: columns >= split (= 3 * hd) are bias +
+                           // GELU, stored through the tensor map after the group's (0: no tail)
   float eps;               // kEpiQkvRope: RMSNorm epsilon
   TcGroup g[kMaxGroups];
 };
@@ -559,7 +561,9 @@ __device__ __forceinline__ void prefetch_residual(const TcParams& p, const TcGro
 // passes through.  Everything leaves as bf16 through the TMA store path: the attention kernel
 // reads its operands from this buffer, so the fp32 projection never goes to memory.
 // Pass 1 reads the head's 128 accumulator columns from TMEM for the sum of squares, pass 2
-// reads them again and writes the result.
+// reads them again and writes the result.  With a GELU tail (the single block's linear1: its
+// weight rows are [q | k | v | mlp]), 128-column halves at or past p.split take bias + GELU
+// and leave through the tensor map that follows tmD (the launch then has one group).
 template <int BN, typename Release>
 __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
                                               uint32_t tacc, Release release, const CUtensorMap* tmD, int m,
@@ -568,6 +572,23 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
   const int c0 = e.half * 4;           // this warp's first 32-column chunk in the tile
   const int col = n_base + c0 * 32;    // first column of the head (uniform across the warp)
   const int m_warp0 = m - e.lane;
+  if (p.split && col >= p.split) {
+    const float* sbg = p.bias_kind ? e.sbias + c0 * 32 : nullptr;
+    uint32_t r[2][32];
+    tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      tmem_wait_ld();
+      if (i + 1 < 4) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);
+      if (i == 3) release();
+      float v[32];
+      chunk_values<B2G_EPI_GELU>(r[i & 1], sbg ? sbg + i * 32 : nullptr, p.alpha, v);
+      if (m_warp0 < G.M && col + i * 32 < p.N)
+        stage_store_values<false, OUT_BF16>(tmD + 1, e.buf, obuf, 0, m_warp0, col - p.split + i * 32, v, e.lane);
+    }
+    named_bar_sync(1, kEpiThreads);  // the staged bias is reused next item
+    return;
+  }
   const int sec = col / p.hd;          // 0 q, 1 k, 2 v
   const float* norm = sec == 0 ? G.qn : (sec == 1 ? G.kn : nullptr);
   const float* sb = p.bias_kind ? e.sbias + c0 * 32 : nullptr;
@@ -1406,8 +1427,12 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     const QkvRope& r = *p.rope;
     if (kind != 0 || p.d_dtype != B2G_BF16 || p.batch != 1)
       return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: bf16/fp16 operands, bf16 output, no batch");
-    if (r.heads < 1 || p.N != 3 * r.heads * 128)
-      return set_error(B2G_ERR_INVALID, "qkv rope epilogue: N must be 3 * heads * 128");
+    const bool tail = r.gelu_out != nullptr;
+    if (r.heads < 1 || (tail ? p.N <= 3 * r.heads * 128 : p.N != 3 * r.heads * 128))
+      return set_error(B2G_ERR_INVALID, "qkv rope epilogue: N must be 3 * heads * 128 (more with a GELU tail)");
+    if (tail && (count != 1 || (reinterpret_cast<uintptr_t>(r.gelu_out) & 15u) || (r.gelu_ld * 2) % 16 != 0 ||
+                 r.gelu_ld < p.N - 3 * r.heads * 128))
+      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: GELU tail needs one problem and 16-byte aligned rows");
     if (!prm.tma_store) return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: 16-byte aligned output rows required");
     for (int i = 0; i < count; ++i) {
       const QkvRope& ri = *ps[i].rope;
@@ -1417,6 +1442,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     prm.hd = static_cast<int>(r.heads * 128);
     prm.eps = r.eps;
     prm.n_outer = 1;
+    prm.split = tail ? 3 * prm.hd : 0;
   }
   if (p.tp) {
     const TpReduce& t = *p.tp;
@@ -1445,7 +1471,14 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     if ((s = make_operand_map(&maps.b[i], q.b, q.b_dtype, q.K, q.N, q.ldb, q.batch, b_bs, b_box)) != B2G_OK) return s;
     if (prm.tma_store && q.d) {
       const int64_t d_bs = q.batch > 1 ? q.d_bstride : q.ldd * q.M;
-      if ((s = make_output_map(&maps.d[i], q.d, q.d_dtype, q.N, q.M, q.ldd, q.batch, d_bs)) != B2G_OK) return s;
+      const int64_t n_d = prm.split ? prm.split : q.N;  // a GELU tail has its own map, next
+      if ((s = make_output_map(&maps.d[i], q.d, q.d_dtype, n_d, q.M, q.ldd, q.batch, d_bs)) != B2G_OK) return s;
+      if (prm.split) {
+        const QkvRope& r = *q.rope;
+        if ((s = make_output_map(&maps.d[i + 1], r.gelu_out, B2G_BF16, q.N - prm.split, q.M, r.gelu_ld, 1,
+                                 r.gelu_ld * q.M)) != B2G_OK)
+          return s;
+      }
     }
   }
 

@@ -196,3 +196,30 @@ def test_fused_path_matches_the_separate_one(engine):
     a, b = fused.double().cpu().numpy().ravel(), sep.double().cpu().numpy().ravel()
     assert rel_err(a, b) < 1e-2
     assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
+
+
+@pytest.mark.parametrize("M,H,MLPC,K", [(200, 2, 512, 256), (131, 2, 200, 192)])
+def test_gemm_qkv_rope_with_gelu_tail(engine, oracle, M, H, MLPC, K):
+    """The single block's linear1 in one launch: weight rows [q | k | v | mlp]; the qkv columns
+    come out normed and rotated, the MLP columns as bias + tanh-GELU (bf16) in a column view of
+    a wider concat buffer, nothing written outside it."""
+    QKV = 3 * H * DH
+    N = QKV + MLPC
+    x = seeded((M, K), 5)
+    w = seeded((N, K), 6, 0.05)
+    b = seeded((N,), 7, 0.05, torch.float32)
+    qn = 1 + 0.2 * seeded((DH,), 8, 1.0, torch.float32)
+    kn = 1 + 0.2 * seeded((DH,), 9, 1.0, torch.float32)
+    pe = pe_table(M, DH, 17)
+    cat = torch.zeros((M, 64 + MLPC + 40), dtype=torch.bfloat16, device=DEV)
+    outs = engine.gemm_qkv_rope([dict(x=x.to(DEV), w=w.to(DEV), bias=b.to(DEV), pe=torch.from_numpy(pe).to(DEV),
+                                      q_norm=qn.to(DEV), k_norm=kn.to(DEV), gelu_out=cat[:, 64:64 + MLPC])], H)
+    torch.cuda.synchronize()
+    want_qkv = qkv_oracle(oracle, x, w[:QKV], b[:QKV], pe, H, qn, kn)
+    assert outs[0].shape == (M, QKV)
+    assert_bf16_of(outs[0], want_qkv)
+    y = oracle.linear(bits(x), 2, bits(w[QKV:]), 2, b[QKV:].numpy())
+    want_mlp = oracle.gelu(y)
+    got = cat.float().cpu().numpy()
+    assert np.all(got[:, :64] == 0) and np.all(got[:, 64 + MLPC:] == 0)
+    assert_bf16_of(cat[:, 64:64 + MLPC], want_mlp)
