@@ -442,12 +442,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int i = 0; i < 32; ++i)
               if ((words[c] >> i) & 1u) r[c][i] = 0xFF800000u;  // -inf
         }
+        // three-input max: two scores per instruction, 16 chains
+        float m16[16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int q = 0; q < 16; ++q) m16[q] = fmaxf(__uint_as_float(r[0][q]), __uint_as_float(r[0][q + 16]));
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
+        for (int c = 1; c < 4; ++c)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) mx4[q] = fmaxf(mx4[q], __uint_as_float(r[c][i + q]));
+          for (int q = 0; q < 16; ++q) m16[q] = max3f(m16[q], __uint_as_float(r[c][q]), __uint_as_float(r[c][q + 16]));
+#pragma unroll
+        for (int q = 0; q < 4; ++q) mx4[q] = max3f(max3f(m16[4 * q], m16[4 * q + 1], m16[4 * q + 2]), m16[4 * q + 3], mx4[q]);
       }
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       if (!biased) mx *= p.scale_log2;  // scale > 0: the max commutes with it
@@ -473,16 +477,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
       // P chunk by chunk from the registers: keys 32c..32c+31 become bf16 pairs in columns
       // 16c..16c+15 (S has been read in full above).
-      const float ua = biased ? 1.f : p.scale_log2;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // Packed fp32 pairs (fma/add .f32x2) for the exponent arguments and the row sum: half the
+      // instructions of the scalar forms, same per-element rounding.
+      const uint64_t ua2 = f2_splat(biased ? 1.f : p.scale_log2), nm2 = f2_splat(neg_m);
+      uint64_t ls2[2] = {f2_splat(0.f), f2_splat(0.f)};
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float e0 = fast_exp2(fmaf(__uint_as_float(r[c][i]), ua, neg_m));
-          const float e1 = fast_exp2(fmaf(__uint_as_float(r[c][i + 1]), ua, neg_m));
-          ls[(i >> 1) & 3] += e0 + e1;
+          const float2 xx = f2_unpack(f2_fma(f2_pack(r[c][i], r[c][i + 1]), ua2, nm2));
+          const float e0 = fast_exp2(xx.x);
+          const float e1 = fast_exp2(xx.y);
+          uint32_t eb0 = __float_as_uint(e0), eb1 = __float_as_uint(e1);
+          ls2[(i >> 1) & 1] = f2_add(ls2[(i >> 1) & 1], f2_pack(eb0, eb1));
           __nv_bfloat162 hh = __floats2bfloat162_rn(e0, e1);
           pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hh);
         }
@@ -498,7 +506,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t]);
-      l_sum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      const float2 la = f2_unpack(ls2[0]), lb = f2_unpack(ls2[1]);
+      l_sum += (la.x + la.y) + (lb.x + lb.y);
     }
     // Final: wait for the last P.Vt of this tile, write O / l.
     if (good)

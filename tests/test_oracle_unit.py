@@ -170,3 +170,4 @@ def test_rope_is_the_attention_rotation(oracle):
     p = pe[:, None]
     want = np.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(L, H * D)
     assert np.allclose(y, want, rtol=1e-6, atol=1e-6)
+
