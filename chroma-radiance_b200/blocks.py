@@ -102,6 +102,13 @@ def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1,
 
     `mark(label)`, when given, is called after each operation (labels and FLOPs in
     block_pair_ops order) so a caller can record events between the launches."""
+    double_block_attention(txt_w, img_w, txt_mod1, img_mod1, txt, img, txt_gate1, img_gate1, pe, mask, s, mark)
+    double_block_mlp(txt_w, img_w, txt_mod2, img_mod2, txt, img, txt_gate2, img_gate2, s, mark)
+
+
+def double_block_attention(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1, txt, img, txt_gate1,
+                           img_gate1, pe, mask, s: Scratch, mark=None) -> None:
+    """The attention half of a double block (chroma.cuh:808-905): qkv, attention, proj."""
     mark = mark or _no_mark
     T = txt.shape[0]
     # Each layer's txt and img GEMMs share one launch (b2g_gemm_group): together their tiles
@@ -122,6 +129,12 @@ def double_block(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1, img_mod1,
                     dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, out=img, epilogue="gated_residual",
                          gate=img_gate1)])
     mark("double.proj")
+
+
+def double_block_mlp(txt_w: StreamWeights, img_w: StreamWeights, txt_mod2, img_mod2, txt, img, txt_gate2,
+                     img_gate2, s: Scratch, mark=None) -> None:
+    """The MLP half of a double block (chroma.cuh:906-964): mlp0 + GELU, mlp2 + gated residual."""
+    mark = mark or _no_mark
     b2g.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
                     dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
     mark("double.mlp0")
@@ -149,6 +162,67 @@ def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=No
 
 def _no_mark(label: str) -> None:
     pass
+
+
+# ---------------------------------------------------------------------------- transformer pass
+DOUBLE_BLOCKS, SINGLE_BLOCKS = 19, 38  # Chroma's layout (chroma.cuh:1499-1584)
+
+
+@dataclass
+class PassWeights:
+    """Weights of every block of one transformer pass, and the modulation vectors the
+    approximator would produce for it: per double block and stream [6, 3072] F32 (shift1,
+    scale1, gate1, shift2, scale2, gate2), per single block [3, 3072] (shift, scale, gate)."""
+    double: list          # [(txt StreamWeights, img StreamWeights)]
+    single: list          # [SingleWeights]
+    mods: torch.Tensor    # [DOUBLE_BLOCKS * 2 * 6 + SINGLE_BLOCKS * 3, 3072] F32
+
+
+def random_pass(gen: torch.Generator, dev, n_double: int = DOUBLE_BLOCKS, n_single: int = SINGLE_BLOCKS) -> PassWeights:
+    """Random-init weights of a whole pass (about 17 GB of bf16 for Chroma's 19 + 38 blocks)."""
+    double = [(random_stream(gen, dev), random_stream(gen, dev)) for _ in range(n_double)]
+    single = [random_single(gen, dev) for _ in range(n_single)]
+    return PassWeights(double, single, mods=torch.zeros((n_double * 12 + n_single * 3, HIDDEN), device=dev))
+
+
+class PassScratch(Scratch):
+    """Scratch of a pass: the block buffers plus the modulated activations."""
+
+    def __init__(self, T: int, I: int, dev):
+        super().__init__(T, I, dev)
+        L = T + I
+        self.mod = torch.empty((L, HIDDEN), dtype=torch.bfloat16, device=dev)
+
+
+def forward_pass(pw: PassWeights, x, pe, mask, s: PassScratch, T: int) -> None:
+    """The transformer blocks of one denoising step (forward, chroma.cuh:1345-1493, without the
+    embedders, approximator and final layer): the double blocks on the txt rows x[:T] and img
+    rows x[T:] of the F32 stream x [L, 3072], then the single blocks on x, every block
+    modulating its inputs on the device (modulate_to_bf16, kernels.cu:552-599) as the
+    reference's blocks do.  x is updated in place; txt and img are row views of it, so the
+    double-to-single concatenation costs nothing."""
+    txt, img = x[:T], x[T:]
+    for i, (tw, iw) in enumerate(pw.double):
+        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        b2g.modulate_to_bf16(txt, mt[0], mt[1], out=s.mod[:T])
+        b2g.modulate_to_bf16(img, mi[0], mi[1], out=s.mod[T:])
+        double_block_attention(tw, iw, s.mod[:T], s.mod[T:], txt, img, mt[2], mi[2], pe, mask, s)
+        b2g.modulate_to_bf16(txt, mt[3], mt[4], out=s.mod[:T])
+        b2g.modulate_to_bf16(img, mi[3], mi[4], out=s.mod[T:])
+        double_block_mlp(tw, iw, s.mod[:T], s.mod[T:], txt, img, mt[5], mi[5], s)
+    base = 12 * len(pw.double)
+    for i, sw in enumerate(pw.single):
+        m = pw.mods[base + 3 * i:base + 3 * i + 3]
+        b2g.modulate_to_bf16(x, m[0], m[1], out=s.mod)
+        single_block(sw, s.mod, x, m[2], pe, mask, s)
+
+
+def pass_flops(T: int, I: int, n_double: int = DOUBLE_BLOCKS, n_single: int = SINGLE_BLOCKS) -> float:
+    """GEMM + attention (unmasked) FLOPs of forward_pass; the modulations are not counted."""
+    ops = block_pair_ops(T, I)
+    dbl = sum(f for lab, _, f in ops if lab.startswith("double."))
+    sgl = sum(f for lab, _, f in ops if lab.startswith("single."))
+    return n_double * dbl + n_single * sgl
 
 
 def block_pair_ops(T: int, I: int) -> list[tuple[str, str, float]]:
