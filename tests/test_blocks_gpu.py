@@ -133,3 +133,42 @@ def test_block_pair_in_cuda_graph_matches_eager(engine, setup):
     torch.cuda.synchronize()
     for k in state:
         assert torch.equal(state[k], eager[k]), k
+
+
+def test_forward_pass_is_the_blocks_in_sequence(engine):
+    """blocks.forward_pass over a short pass (2 double + 2 single blocks, txt/img as row views
+    of the single blocks' stream, every block modulating its inputs on the device) gives the
+    same bits as calling modulate_to_bf16 and the block functions one by one, and stays finite."""
+    import blocks
+
+    T, I = 128, 256
+    L = T + I
+    g = torch.Generator(device=DEV).manual_seed(5)
+    pw = blocks.random_pass(g, DEV, n_double=2, n_single=2)
+    pw.mods.copy_(torch.randn(tuple(pw.mods.shape), generator=g, device=DEV) * 0.1)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=DEV) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    mask = torch.zeros(L, device=DEV)
+    mask[T - 40:T] = float("-inf")
+    x0 = torch.randn((L, blocks.HIDDEN), generator=g, device=DEV)
+
+    x = x0.clone()
+    blocks.forward_pass(pw, x, pe, mask, blocks.PassScratch(T, I, DEV), T)
+
+    y = x0.clone()
+    s = blocks.PassScratch(T, I, DEV)
+    txt, img = y[:T], y[T:]
+    for i, (tw, iw) in enumerate(pw.double):
+        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        m1t, m1i = engine.modulate_to_bf16(txt, mt[0], mt[1]), engine.modulate_to_bf16(img, mi[0], mi[1])
+        blocks.double_block_attention(tw, iw, m1t, m1i, txt, img, mt[2], mi[2], pe, mask, s)
+        m2t, m2i = engine.modulate_to_bf16(txt, mt[3], mt[4]), engine.modulate_to_bf16(img, mi[3], mi[4])
+        blocks.double_block_mlp(tw, iw, m2t, m2i, txt, img, mt[5], mi[5], s)
+    for i, sw in enumerate(pw.single):
+        m = pw.mods[24 + 3 * i:24 + 3 * i + 3]
+        blocks.single_block(sw, engine.modulate_to_bf16(y, m[0], m[1]), y, m[2], pe, mask, s)
+    torch.cuda.synchronize()
+    assert torch.isfinite(x).all()
+    assert torch.equal(x, y)
+    assert not torch.equal(x, x0)
+    assert blocks.pass_flops(T, I, 2, 2) > 0
