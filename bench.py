@@ -305,6 +305,9 @@ def run_engine_config1(args) -> None:
 
 
 T_TXT, I_IMG, MASKED = 512, 1024, 400
+CFG_HALVES = 2         # conditional + unconditional (forward_cfg)
+UNCOND_TEXT_KEYS = 2   # the unconditional half's live text keys (an empty prompt)
+
 WORKLOAD2 = ("config2: one double-stream + one single-stream Chroma block at 512^2 (T=512 txt + I=1024 img "
              "tokens, hidden 3072, 24x128 heads, MLP 12288, key mask on 400 of 512 txt tokens)")
 
@@ -534,25 +537,29 @@ def run_engine_config2(args) -> None:
     del graphs, marked
 
     # End to end over the transformer blocks of one denoising step, the way the model runs
-    # them: Chroma's 19 double + 38 single blocks, each with its own weights (17 GB), inputs
-    # modulated on the device; in from pinned host memory the hidden states and the step's
-    # modulation vectors, out the image hidden states.
+    # them under classifier-free guidance (forward_cfg's block loop): both
+    # halves through Chroma's 19 double + 38 single blocks, each block with its own weights
+    # (17 GB), inputs modulated on the device; in from pinned host memory the hidden states of
+    # both halves and the step's modulation vectors, out both halves' image hidden states.
     pw = blocks.random_pass(gdev, dev)
-    ps = blocks.PassScratch(T, I, dev)
+    ps = blocks.PassScratch(T, I, dev, halves=CFG_HALVES)
     gp = torch.Generator().manual_seed(2)
-    x_h = torch.randn((L, H), generator=gp).pin_memory()
+    x_h = torch.randn((CFG_HALVES * L, H), generator=gp).pin_memory()
     mods_h = (torch.randn(tuple(pw.mods.shape), generator=gp) * 0.1).pin_memory()
-    img_h = torch.empty((I, H)).pin_memory()
-    x_d = torch.empty((L, H), device=dev)
+    img_h = torch.empty((CFG_HALVES, I, H)).pin_memory()
+    x_d = torch.empty((CFG_HALVES * L, H), device=dev)
     x_d.copy_(x_h)
     pw.mods.copy_(mods_h)
-    blocks.forward_pass(pw, x_d, pe, mask, ps, T)  # sizes the workspaces before capture
+    masks = torch.zeros((CFG_HALVES, L), device=dev)
+    masks[0] = mask
+    masks[1:, UNCOND_TEXT_KEYS:T] = float("-inf")
+    blocks.forward_pass(pw, x_d, pe, masks, ps, T)  # sizes the workspaces before capture
     torch.cuda.synchronize(dev)
     n0 = b2g.launch_count()
     pass_graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(cap):
         with torch.cuda.graph(pass_graph, stream=cap):
-            blocks.forward_pass(pw, x_d, pe, mask, ps, T)
+            blocks.forward_pass(pw, x_d, pe, masks, ps, T)
     pass_launches = b2g.launch_count() - n0
 
     def pass_step():
@@ -561,7 +568,8 @@ def run_engine_config2(args) -> None:
         x_d.copy_(x_h, non_blocking=True)
         pw.mods.copy_(mods_h, non_blocking=True)
         pass_graph.replay()
-        img_h.copy_(x_d[T:], non_blocking=True)
+        for h in range(CFG_HALVES):
+            img_h[h].copy_(x_d[h * L + T:(h + 1) * L], non_blocking=True)
         b.record(stream)
         b.synchronize()
         return a.elapsed_time(b)
@@ -572,6 +580,7 @@ def run_engine_config2(args) -> None:
     pass_ms = sum(pass_step() for _ in range(pass_steps)) / pass_steps
     pass_h2d = x_h.numel() * 4 + mods_h.numel() * 4
     pass_d2h = img_h.numel() * 4
+    pass_flop = blocks.pass_flops(T, I, halves=CFG_HALVES)
     del pass_graph, pw, ps
 
     if world > 1:
@@ -609,15 +618,17 @@ def run_engine_config2(args) -> None:
                      "gemm_ms_per_step": round(gemm_ms, 5)},
         "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
         "breakdown_tflops": {lab: round(f / (mean_op[lab] * 1e-3) / 1e12, 1) for lab, _, f in ops},
-        "e2e": {"value": round(blocks.pass_flops(T, I) * world / (pass_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "e2e": {"value": round(pass_flop * world / (pass_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": pass_h2d, "d2h_bytes_per_step": pass_d2h, "ms_per_step": round(pass_ms, 4),
-                "workload": f"the transformer blocks of one denoising step at 512^2 through the public API: "
-                            f"{blocks.DOUBLE_BLOCKS} double + {blocks.SINGLE_BLOCKS} single blocks with their own "
-                            f"weights, every block's inputs modulated on the device (modulate_to_bf16); hidden "
-                            f"states and the step's modulation vectors copied in from pinned host memory and the "
-                            f"image hidden states copied back inside the events; one CUDA graph of "
-                            f"{pass_launches} launches; FLOPs = GEMMs + attention (unmasked), modulations not "
-                            f"counted", "flop_per_step": blocks.pass_flops(T, I)},
+                "workload": f"config3's block loop (forward_cfg) at 512^2 through the public API: both guidance "
+                            f"halves (conditional: {T - MASKED} of {T} text keys live; unconditional: "
+                            f"{UNCOND_TEXT_KEYS}) through {blocks.DOUBLE_BLOCKS} double + {blocks.SINGLE_BLOCKS} "
+                            f"single blocks with their own weights, every block's inputs modulated on the device "
+                            f"(modulate_to_bf16); hidden states of both halves and the step's modulation vectors "
+                            f"copied in from pinned host memory and both halves' image hidden states copied back "
+                            f"inside the events; one CUDA graph of {pass_launches} launches; FLOPs = GEMMs + "
+                            f"attention (unmasked), modulations not counted; embedders, approximator, NeRF decoder "
+                            f"and cfg_blend not included", "flop_per_step": pass_flop},
         "e2e_block_pair": {"value": round(flop_step * world / (e2e_per * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_per, 4),
                            "workload": "the timed block pair with all of its activations (modulated inputs, "

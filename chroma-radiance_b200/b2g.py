@@ -68,7 +68,7 @@ class TpReduceDesc(ctypes.Structure):
 class QkvRopeDesc(ctypes.Structure):
     """b2g_qkv_rope_desc: RoPE rows and RMSNorm scales of one qkv projection problem."""
     _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
-                ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64)]
+                ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64), ("pe_period", ctypes.c_int64)]
 
 
 _lib = None
@@ -224,7 +224,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
 
 def gemm_group(problems: list[dict], stream: torch.cuda.Stream | None = None) -> list[torch.Tensor]:
     """Several gemm() problems (dicts of gemm's keyword arguments, x and w required) in one
-    call; two that share N, K, dtypes and epilogue run as one tensor-core launch."""
+    call; two to four that share N, K, dtypes and epilogue run as one tensor-core launch."""
     lib = load()
     descs, outs = [], []
     for pr in problems:
@@ -466,9 +466,11 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
 
     Each problem: x [M, K] and w [3*n_head*128, K] (bf16/fp16), bias (F32), out (bf16 [M, N]
     view with 16-byte aligned rows; allocated when absent), pe (F32 RoPE rows of the
-    problem's tokens, [M, 64, 4] or [M, 256]), q_norm / k_norm ([128] F32 or None).  Output
-    columns [q | k | v]: q and k heads normed and rotated, v the plain product (+ bias).
-    Two problems (txt and img streams) run as one launch.  One problem may carry gelu_out (a
+    problem's tokens, [M, 64, 4] or [M, 256]), q_norm / k_norm ([128] F32 or None), and
+    optionally pe_period P (row m uses pe row m % P; pe then needs P rows only: stacked
+    guidance halves of one sequence).  Output columns [q | k | v]: q and k heads normed and
+    rotated, v the plain product (+ bias).  Up to four problems (txt and img streams, times
+    the guidance halves) run as one launch.  One problem may carry gelu_out (a
     bf16 [M, N - 3*n_head*128] view): w then has more rows, and those columns get bias + GELU
     into gelu_out (the single block's linear1 in one launch); out holds the qkv columns.
     """
@@ -496,11 +498,14 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
         for t in (pe, qn, kn):
             if t is not None and (t.dtype != torch.float32 or not t.is_contiguous()):
                 raise B2GError("gemm_qkv_rope: pe and norm scales must be contiguous F32")
-        if pe.numel() < pr["x"].shape[0] * 256:
-            raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x")
+        period = int(pr.get("pe_period") or 0)
+        if period < 0:
+            raise B2GError("gemm_qkv_rope: pe_period must be 0 or positive")
+        if pe.numel() < (period or pr["x"].shape[0]) * 256:
+            raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x (per pe_period row)")
         descs.append(d)
         ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn), _ptr(tail),
-                                 tail.stride(0) if tail is not None else 0))
+                                 tail.stride(0) if tail is not None else 0, period))
         outs.append(out)
         keep.append(pe)
     arr = (GemmDesc * len(descs))(*descs)

@@ -233,7 +233,7 @@ b2g_status b2g_gemm(const b2g_gemm_desc* d, void* stream) {
 
 b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
   if (count < 0 || (count > 0 && !descs)) return set_error(B2G_ERR_INVALID, "b2g_gemm_group: bad descriptor array");
-  GemmProblem ps[2];
+  GemmProblem ps[kMaxGemmGroups];
   int n = 0;
   bool all_empty = true;
   for (int i = 0; i < count; ++i) {
@@ -243,7 +243,7 @@ b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
     if (s != B2G_OK) return s;
     if (!empty) {
       all_empty = false;
-      if (n < 2) ps[n] = p;
+      if (n < kMaxGemmGroups) ps[n] = p;
       ++n;
     }
   }
@@ -252,12 +252,13 @@ b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // One launch when the (at most two) non-empty problems run on the tensor cores without an
+  // One launch when the (two to four) non-empty problems run on the tensor cores without an
   // activation cast and agree on everything but M and their pointers; otherwise one GEMM
   // after the other on the stream.
-  if (n == 2 && ps[0].K > 0 && tc_gemm_supported(ps[0], nullptr) && tc_gemm_supported(ps[1], nullptr) &&
-      tc_gemm_groupable(ps[0], ps[1]))
-    return tc_gemm_launch_group(ps, 2, st);
+  bool one_launch = n >= 2 && n <= kMaxGemmGroups && ps[0].K > 0;
+  for (int i = 0; one_launch && i < n; ++i)
+    one_launch = tc_gemm_supported(ps[i], nullptr) && tc_gemm_groupable(ps[0], ps[i]);
+  if (one_launch) return tc_gemm_launch_group(ps, n, st);
   for (int i = 0; i < count; ++i) {
     GemmProblem p;
     bool empty = false;
@@ -488,10 +489,10 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
 
 b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
                              float eps, void* stream) {
-  if (!descs || !rope || count < 1 || count > 2 || n_head < 1)
-    return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: 1 or 2 descriptors with rope descriptors, n_head >= 1");
-  GemmProblem ps[2];
-  QkvRope rs[2];
+  if (!descs || !rope || count < 1 || count > kMaxGemmGroups || n_head < 1)
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: 1 to 4 descriptors with rope descriptors, n_head >= 1");
+  GemmProblem ps[kMaxGemmGroups];
+  QkvRope rs[kMaxGemmGroups];
   int n = 0;
   for (int i = 0; i < count; ++i) {
     const b2g_gemm_desc* d = descs + i;
@@ -505,6 +506,8 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16))
       return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 or fp16 operands of one type");
     if (!rope[i].pe) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe is required");
+    if (rope[i].pe_period < 0 || rope[i].pe_period > (1ll << 30))
+      return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe_period must be 0 or a positive row count");
     GemmProblem p;
     bool empty = false;
     b2g_gemm_desc dq = *d;  // d holds the [q | k | v] columns only; the tail goes to gelu_out
@@ -521,6 +524,7 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     rs[n].k_norm = rope[i].k_norm;
     rs[n].gelu_out = rope[i].gelu_out;
     rs[n].gelu_ld = rope[i].gelu_ld;
+    rs[n].pe_period = rope[i].pe_period;
     p.rope = &rs[n];
     p.epilogue = static_cast<b2g_epilogue>(kEpiQkvRope);
     std::string why;
@@ -532,7 +536,9 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (n == 2 && tc_gemm_groupable(ps[0], ps[1])) return tc_gemm_launch_group(ps, 2, st);
+  bool one_launch = n >= 2;
+  for (int i = 1; one_launch && i < n; ++i) one_launch = tc_gemm_groupable(ps[0], ps[i]);
+  if (one_launch) return tc_gemm_launch_group(ps, n, st);
   for (int i = 0; i < n; ++i)
     if ((s = tc_gemm_launch_group(ps + i, 1, st)) != B2G_OK) return s;
   return B2G_OK;

@@ -10,6 +10,9 @@
 
 namespace b2g {
 
+// Most problems one tensor-core launch computes together (tc_gemm_launch_group).
+constexpr int kMaxGemmGroups = 4;
+
 // Normalised problem handed from the C ABI to a kernel launcher.  All pointers are device
 // pointers; strides are in elements.  A GEMM with batch > 1 uses the *_bstride fields.
 struct GemmProblem {
@@ -45,6 +48,7 @@ struct QkvRope {
   const float* k_norm = nullptr;    // and of the k heads
   void* gelu_out = nullptr;         // optional: columns past 3 * heads * 128 -> bias + GELU, bf16 here
   int64_t gelu_ld = 0;
+  int64_t pe_period = 0;            // rows per sequence when one problem stacks several (0: M)
 };
 
 // Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *

@@ -63,8 +63,9 @@ constexpr int kScaleBytes = KIND == 2 ? kBiasBytes : 0;
 
 // A launch computes up to kMaxGroups independent problems that share N, K, dtypes and the
 // epilogue (the txt and img streams of a double block: same layer shapes, their own rows,
-// weights, biases and gates).  Their tiles are numbered one group after the other.
-constexpr int kMaxGroups = 2;
+// weights, biases and gates; with classifier-free guidance, each stream's conditional and
+// unconditional rows as well).  Their tiles are numbered one group after the other.
+constexpr int kMaxGroups = kMaxGemmGroups;
 
 struct TcGroup {
   int M;                   // rows of A and D
@@ -81,6 +82,7 @@ struct TcGroup {
   const float* pe;         // kEpiQkvRope: RoPE table rows of the group's first token [M][64][4]
   const float* qn;         // kEpiQkvRope: RMSNorm scales of q and k heads [128] (NULL: none)
   const float* kn;
+  int pe_period;           // kEpiQkvRope: the RoPE row of row m is m % pe_period (0: m)
 };
 
 // Tensor maps of every group (kernel parameter; indexed by group at run time).
@@ -128,16 +130,19 @@ __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi
     // Column-major over the m-blocks of all groups: the last tiles are the last columns.  The
     // qkv projection uses it so that the final wave holds v tiles, whose epilogue (no norm,
     // no RoPE) is the short one and is not hidden behind a next mainloop.
-    const int nmb0 = p.g[0].num_m_blocks;
-    const int nmb_all = nmb0 + (p.groups > 1 ? p.g[1].num_m_blocks : 0);
+    int nmb_all = 0;
+    for (int i = 0; i < p.groups; ++i) nmb_all += p.g[i].num_m_blocks;
     nb = tile / nmb_all;
-    const int r = tile - nb * nmb_all;
-    gi = (p.groups > 1 && r >= nmb0) ? 1 : 0;
-    mb = r - (gi ? nmb0 : 0);
+    int r = tile - nb * nmb_all;
+    gi = 0;
+    while (gi + 1 < p.groups && r >= p.g[gi].num_m_blocks) r -= p.g[gi++].num_m_blocks;
+    mb = r;
     bz = 0;
     return;
   }
-  gi = (p.groups > 1 && tile >= p.g[1].tile0) ? 1 : 0;
+  gi = 0;
+  for (int i = 1; i < p.groups; ++i)
+    if (tile >= p.g[i].tile0) gi = i;
   const int nmb = p.g[gi].num_m_blocks;
   const int t = tile - p.g[gi].tile0;
   const int per_batch = nmb * p.num_n_blocks;
@@ -607,7 +612,9 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
     }
     inv = rsqrtf(ss / 128.0f + p.eps);
   }
-  const float4* pe_row = reinterpret_cast<const float4*>(G.pe) + static_cast<long long>(m < G.M ? m : G.M - 1) * 64;
+  const int pe_m = m < G.M ? m : G.M - 1;
+  const float4* pe_row =
+      reinterpret_cast<const float4*>(G.pe) + static_cast<long long>(G.pe_period ? pe_m % G.pe_period : pe_m) * 64;
   uint32_t r[2][32];
   tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
 #pragma unroll
@@ -1304,7 +1311,7 @@ bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
 b2g_status tc_gemm_launch(const GemmProblem& p, cudaStream_t st) { return tc_gemm_launch_group(&p, 1, st); }
 
 b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t st) {
-  if (count < 1 || count > kMaxGroups) return set_error(B2G_ERR_INVALID, "tc_gemm: 1 or 2 problems per launch");
+  if (count < 1 || count > kMaxGroups) return set_error(B2G_ERR_INVALID, "tc_gemm: 1 to 4 problems per launch");
   for (int i = 1; i < count; ++i)
     if (!tc_gemm_groupable(ps[0], ps[i])) return set_error(B2G_ERR_INVALID, "tc_gemm: problems cannot share a launch");
   const GemmProblem& p = ps[0];
@@ -1391,6 +1398,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     G.pe = q.rope ? q.rope->pe : nullptr;
     G.qn = q.rope ? q.rope->q_norm : nullptr;
     G.kn = q.rope ? q.rope->k_norm : nullptr;
+    G.pe_period = q.rope ? static_cast<int>(q.rope->pe_period) : 0;
     G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
                (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
     all_vec = all_vec && G.vec_ok;

@@ -234,7 +234,8 @@ b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int 
  * the q and k heads are RMSNorm'd with rope[i].q_norm / k_norm ([128] F32 each, NULL: no norm;
  * x * rsqrt(mean(x^2) + eps) * scale) and rotated by the pe table rows rope[i].pe (F32
  * [M][64][4], the rows of problem i's tokens in the attention sequence); v is the plain
- * product.  count 1 or 2 (the txt and img streams: one launch).
+ * product.  count 1 to 4 (the txt and img streams, and with classifier-free guidance their
+ * conditional and unconditional rows: one launch).
  * GELU tail (the single block's linear1, whose weight rows are [q | k | v | mlp],
  * chroma.cuh:1109-1113): with gelu_out set (count 1), N may exceed 3 * n_head * 128; columns
  * past it get bias + tanh-GELU and are written bf16 to gelu_out [M, gelu_ld] (e.g. the
@@ -246,6 +247,9 @@ typedef struct {
   const float* k_norm;   /* [128] or NULL */
   void* gelu_out;        /* NULL, or the GELU tail's bf16 output (16-byte aligned rows) */
   int64_t gelu_ld;       /* its row stride in elements */
+  int64_t pe_period;     /* 0, or P > 0: row m rotates by pe row m % P (several sequences of
+                            P tokens stacked in one problem, e.g. the conditional and
+                            unconditional halves of a guidance batch; pe then holds P rows) */
 } b2g_qkv_rope_desc;
 b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
                              float eps, void* stream);

@@ -172,3 +172,45 @@ def test_forward_pass_is_the_blocks_in_sequence(engine):
     assert torch.equal(x, y)
     assert not torch.equal(x, x0)
     assert blocks.pass_flops(T, I, 2, 2) > 0
+
+
+def test_cfg_pass_equals_each_half_alone(engine):
+    """forward_pass over two guidance halves stacked half-major (each with its own key mask:
+    the conditional prompt and an almost empty unconditional one) against the same pass on each
+    half alone.  With one GEMM variant forced (2-CTA tiles, no split-K) every tile runs the same
+    instructions on the same data in both, so the results are bit-identical; with the
+    variants the cost model picks (the CFG launches have twice the tiles, and may get another
+    variant) they agree to bf16 rounding of the activations, as check_delta states."""
+    import blocks
+
+    T, I = 128, 256
+    L = T + I
+    g = torch.Generator(device=DEV).manual_seed(9)
+    pw = blocks.random_pass(g, DEV, n_double=2, n_single=2)
+    pw.mods.copy_(torch.randn(tuple(pw.mods.shape), generator=g, device=DEV) * 0.1)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=DEV) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    masks = torch.zeros((2, L), device=DEV)
+    masks[0, T - 40:T] = float("-inf")
+    masks[1, 1:T] = float("-inf")
+    x0 = torch.randn((2 * L, blocks.HIDDEN), generator=g, device=DEV)
+    for variant in (2, -1):
+        engine.set_gemm_variant(variant, 0)
+        try:
+            x = x0.clone()
+            blocks.forward_pass(pw, x, pe, masks, blocks.PassScratch(T, I, DEV, halves=2), T)
+            ys = []
+            for b in range(2):
+                y = x0[b * L:(b + 1) * L].clone()
+                blocks.forward_pass(pw, y, pe, masks[b], blocks.PassScratch(T, I, DEV), T)
+                ys.append(y)
+            torch.cuda.synchronize()
+        finally:
+            engine.set_gemm_variant(-1, 0)
+        assert torch.isfinite(x).all()
+        for b in range(2):
+            if variant == 2:
+                assert torch.equal(x[b * L:(b + 1) * L], ys[b]), f"half {b}"
+            else:
+                check_delta(x[b * L:(b + 1) * L], ys[b], x0[b * L:(b + 1) * L])
+    assert not torch.equal(x[:L], x[L:])

@@ -1,0 +1,159 @@
+"""Classifier-free guidance layout of blocks.py on CPU (no GPU): the engine calls are replaced
+by an fp32 torch stand-in with the same signatures, and a pass over two guidance halves
+stacked half-major ([txt_c, img_c | txt_u, img_u], each half with its own key mask) must equal
+the same pass run on each half alone.  This checks the row views, the per-half attention and
+masks and the single block's RoPE row period that forward_cfg's block loop
+(chroma.cuh:1540-1563) needs.  Tolerance: max|d|/max|x| <= 1e-5 (the stand-in is fp32 and
+rounds the bf16 activations at the same points in both runs; matrix products over different
+row counts may round differently in the last bits)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import b2g as engine_b2g
+import blocks
+
+
+class FakeEngine:
+    """fp32 CPU stand-in for the b2g calls blocks.py makes."""
+
+    B2GError = engine_b2g.B2GError
+
+    def __init__(self):
+        self.calls = []
+
+    def gemm(self, x, w, bias=None, out=None, epilogue="none", gate=None, out_dtype=None):
+        self.calls.append(("gemm", 1))
+        return self._gemm(x, w, bias, out, epilogue, gate)
+
+    @staticmethod
+    def _gemm(x, w, bias, out, epilogue, gate):
+        y = x.float() @ w.float().t()
+        if bias is not None:
+            y = y + bias
+        if epilogue == "gelu":
+            y = 0.5 * y * (1 + torch.tanh(0.7978845608 * (y + 0.044715 * y ** 3)))
+        if epilogue == "gated_residual":
+            out += gate * y
+        else:
+            out.copy_(y.to(out.dtype))
+        return out
+
+    def gemm_group(self, problems):
+        assert 1 <= len(problems) <= 4
+        self.calls.append(("gemm_group", len(problems)))
+        return [self._gemm(p["x"], p["w"], p.get("bias"), p.get("out"), p.get("epilogue", "none"), p.get("gate"))
+                for p in problems]
+
+    def gemm_qkv_rope(self, problems, n_head, eps=1e-6):
+        assert 1 <= len(problems) <= 4
+        self.calls.append(("gemm_qkv_rope", len(problems)))
+        for pr in problems:
+            y = pr["x"].float() @ pr["w"].float().t() + pr["bias"]
+            M = y.shape[0]
+            qkv = 3 * n_head * blocks.DHEAD
+            if pr.get("gelu_out") is not None:
+                t = y[:, qkv:]
+                pr["gelu_out"].copy_((0.5 * t * (1 + torch.tanh(0.7978845608 * (t + 0.044715 * t ** 3)))).to(
+                    torch.bfloat16))
+                y = y[:, :qkv]
+            period = pr.get("pe_period") or M
+            rows = torch.arange(M) % period
+            p = pr["pe"].reshape(-1, blocks.DHEAD // 2, 4)[rows].reshape(M, 1, blocks.DHEAD // 2, 4)
+            q, k, v = y.reshape(M, 3, n_head, blocks.DHEAD).unbind(1)
+
+            def norm_rope(a, scale):
+                a = a * torch.rsqrt((a * a).mean(-1, keepdim=True) + eps) * scale
+                e, o = a[..., 0::2], a[..., 1::2]
+                return torch.stack([e * p[..., 0] + o * p[..., 1], e * p[..., 2] + o * p[..., 3]], -1).reshape(
+                    M, n_head, blocks.DHEAD)
+
+            out = torch.stack([norm_rope(q, pr["q_norm"]), norm_rope(k, pr["k_norm"]), v], 1).reshape(M, -1)
+            pr["out"].copy_(out.to(torch.bfloat16))
+
+    def attention_bf16(self, q, k, v, n_head, d_head, attn_mask=None, out=None):
+        self.calls.append(("attention_bf16", 1))
+        L = q.shape[0]
+        qq, kk, vv = (t.float().reshape(L, n_head, d_head) for t in (q, k, v))
+        s = torch.einsum("lhd,mhd->hlm", qq, kk) / d_head ** 0.5
+        if attn_mask is not None:
+            s = s + attn_mask[None, None, :]
+        o = torch.einsum("hlm,mhd->lhd", torch.softmax(s, -1), vv).reshape(L, n_head * d_head)
+        out.copy_(o.to(out.dtype))
+        return out
+
+    def modulate_to_bf16(self, x, shift, scale, out=None, eps=1e-6):
+        self.calls.append(("modulate", 1))
+        xf = x.float()
+        mu = xf.mean(-1, keepdim=True)
+        var = ((xf - mu) ** 2).mean(-1, keepdim=True)
+        out.copy_(((xf - mu) * torch.rsqrt(var + eps) * (1 + scale) + shift).to(torch.bfloat16))
+        return out
+
+
+T, I = 8, 16
+L = T + I
+
+
+@pytest.fixture(scope="module")
+def pass_inputs():
+    g = torch.Generator().manual_seed(11)
+    pw = blocks.random_pass(g, "cpu", n_double=1, n_single=1)
+    pw.mods.copy_(torch.randn(tuple(pw.mods.shape), generator=g) * 0.1)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    masks = torch.zeros((2, L))
+    masks[0, T - 3:T] = float("-inf")
+    masks[1, 1:T] = float("-inf")      # the unconditional half: an (almost) empty prompt
+    x0 = torch.randn((2 * L, blocks.HIDDEN), generator=g)
+    return pw, pe, masks, x0
+
+
+def test_cfg_pass_equals_each_half_alone(pass_inputs, monkeypatch):
+    pw, pe, masks, x0 = pass_inputs
+    fake = FakeEngine()
+    monkeypatch.setattr(blocks, "b2g", fake)
+    x = x0.clone()
+    blocks.forward_pass(pw, x, pe, masks, blocks.PassScratch(T, I, "cpu", halves=2), T)
+    # one launch per double-block GEMM layer over the four row blocks, one linear1 over both
+    # halves, one attention per half and block
+    assert ("gemm_qkv_rope", 4) in fake.calls and ("gemm_group", 4) in fake.calls
+    assert ("gemm_qkv_rope", 1) in fake.calls
+    assert sum(1 for c in fake.calls if c[0] == "attention_bf16") == 2 * 2
+    for b in range(2):
+        y = x0[b * L:(b + 1) * L].clone()
+        blocks.forward_pass(pw, y, pe, masks[b], blocks.PassScratch(T, I, "cpu"), T)
+        d = (x[b * L:(b + 1) * L] - y).abs().max() / y.abs().max()
+        assert d <= 1e-5, f"half {b}: {d:.3e}"
+    assert not torch.equal(x[:L], x[L:])
+    assert torch.isfinite(x).all()
+
+
+def test_single_block_rope_period_and_per_half_masks(pass_inputs, monkeypatch):
+    """single_block on two stacked halves rotates each half's rows by pe rows 0..L-1 and masks
+    each half with its own key bias."""
+    pw, pe, masks, x0 = pass_inputs
+    monkeypatch.setattr(blocks, "b2g", FakeEngine())
+    sw = pw.single[0]
+    g = torch.Generator().manual_seed(2)
+    x_mod = torch.randn((2 * L, blocks.HIDDEN), generator=g).to(torch.bfloat16)
+    gate = torch.randn(blocks.HIDDEN, generator=g)
+    x = x0.clone()
+    blocks.single_block(sw, x_mod, x, gate, pe, masks, blocks.Scratch(T, I, "cpu", halves=2))
+    for b in range(2):
+        y = x0[b * L:(b + 1) * L].clone()
+        blocks.single_block(sw, x_mod[b * L:(b + 1) * L], y, gate, pe, masks[b], blocks.Scratch(T, I, "cpu"))
+        assert (x[b * L:(b + 1) * L] - y).abs().max() / y.abs().max() <= 1e-5
+
+
+def test_masks_per_half_are_checked():
+    with pytest.raises(AssertionError):
+        blocks._masks(torch.zeros((3, L)), 2)
+    assert blocks._masks(None, 2) == [None, None]
+    m = torch.zeros(L)
+    assert all(t is m for t in blocks._masks(m, 2))
+
+
+def test_cfg_flops_double():
+    assert blocks.pass_flops(T, I, 1, 1, halves=2) == 2 * blocks.pass_flops(T, I, 1, 1)

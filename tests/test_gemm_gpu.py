@@ -344,6 +344,62 @@ def test_gemm_group_one_launch(engine, variant, M0, M1, N, K, epilogue, out_dtyp
     engine.check_device_error()
 
 
+FOUR = [
+    # (Ms, N, K): the double block's layers with guidance halves at 512^2 ([txt_c, txt_u, img_c,
+    # img_u] row blocks), then ragged rows and K
+    ((512, 512, 1024, 1024), 3072, 3072), ((3, 130, 257, 64), 640, 200),
+]
+
+
+@pytest.mark.parametrize("variant", [-1, 0, 1, 2])
+@pytest.mark.parametrize("Ms,N,K", FOUR)
+@pytest.mark.parametrize("epilogue,out_dtype", [("none", torch.float32), ("gelu", torch.bfloat16),
+                                                ("gated_residual", torch.float32)])
+def test_gemm_group_four_problems_one_launch(engine, variant, Ms, N, K, epilogue, out_dtype):
+    """Four problems (problems 0/1 and 2/3 share a weight, as the guidance halves of one stream
+    do) in one launch; every variant; the outputs are row views of one buffer."""
+    engine.set_gemm_variant(variant, 0)
+    try:
+        ws = [seeded((N, K), 31 * K + j, 0.02) for j in range(2)]
+        bs = [seeded((N,), 37 * K + j, 0.02, torch.float32) for j in range(2)]
+        gate = seeded((N,), 41, 1.0, torch.float32) if epilogue == "gated_residual" else None
+        rows = sum(Ms)
+        buf = (seeded((rows, N), 43, 1.0, torch.float32) if gate is not None
+               else torch.zeros((rows, N), dtype=out_dtype, device=DEV))
+        probs, refs, r0 = [], [], 0
+        for i, M in enumerate(Ms):
+            x = seeded((M, K), 47 * M + i)
+            out = buf[r0:r0 + M]
+            y = fp32_ref(x, ws[i // 2], bs[i // 2])
+            if epilogue == "gelu":
+                y = gelu_t(y)
+            elif gate is not None:
+                y = out.double() + gate.double() * y
+            refs.append(y)
+            probs.append(dict(x=x, w=ws[i // 2], bias=bs[i // 2], out=out, epilogue=epilogue, gate=gate))
+            r0 += M
+        n0 = engine.launch_count()
+        engine.gemm_group(probs)
+        torch.cuda.synchronize()
+        assert engine.launch_count() - n0 == 1
+        for pr, y in zip(probs, refs):
+            check(pr["out"], y)
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    engine.check_device_error()
+
+
+def test_gemm_group_five_problems_run_one_by_one(engine):
+    xs = [seeded((64 + 8 * i, 256), 60 + i) for i in range(5)]
+    w = seeded((384, 256), 70, 0.02)
+    n0 = engine.launch_count()
+    outs = engine.gemm_group([dict(x=x, w=w) for x in xs])
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 5
+    for x, o in zip(xs, outs):
+        check(o, fp32_ref(x, w))
+
+
 def test_gemm_group_split_k(engine):
     engine.set_gemm_variant(2, 3)
     try:

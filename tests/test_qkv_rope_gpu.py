@@ -223,3 +223,54 @@ def test_gemm_qkv_rope_with_gelu_tail(engine, oracle, M, H, MLPC, K):
     got = cat.float().cpu().numpy()
     assert np.all(got[:, :64] == 0) and np.all(got[:, 64 + MLPC:] == 0)
     assert_bf16_of(cat[:, 64:64 + MLPC], want_mlp)
+
+
+@pytest.mark.parametrize("L,H,K,halves", [(200, 2, 256, 2), (131, 2, 192, 3)])
+def test_gemm_qkv_rope_pe_period(engine, oracle, L, H, K, halves):
+    """Guidance halves stacked in one problem (the single block's linear1 under forward_cfg):
+    row r is rotated by pe row r % L, with pe holding L rows only; a GELU tail as well."""
+    QKV, MLPC = 3 * H * DH, 192
+    N = QKV + MLPC
+    M = halves * L
+    x = seeded((M, K), 21)
+    w = seeded((N, K), 22, 0.05)
+    b = seeded((N,), 23, 0.05, torch.float32)
+    qn = 1 + 0.2 * seeded((DH,), 24, 1.0, torch.float32)
+    kn = 1 + 0.2 * seeded((DH,), 25, 1.0, torch.float32)
+    pe = pe_table(L, DH, 29)
+    tail = torch.zeros((M, MLPC), dtype=torch.bfloat16, device=DEV)
+    outs = engine.gemm_qkv_rope([dict(x=x.to(DEV), w=w.to(DEV), bias=b.to(DEV), pe=torch.from_numpy(pe).to(DEV),
+                                      pe_period=L, q_norm=qn.to(DEV), k_norm=kn.to(DEV), gelu_out=tail)], H)
+    torch.cuda.synchronize()
+    want = qkv_oracle(oracle, x, w[:QKV], b[:QKV], np.concatenate([pe] * halves), H, qn, kn)
+    assert_bf16_of(outs[0], want)
+    y = oracle.linear(bits(x), 2, bits(w[QKV:]), 2, b[QKV:].numpy())
+    assert_bf16_of(tail, oracle.gelu(y))
+
+
+def test_gemm_qkv_rope_four_problems(engine, oracle):
+    """The double block's qkv layer with guidance halves: txt_c, txt_u (txt weights, pe rows
+    [0, T)), img_c, img_u (img weights, pe rows [T, L)) in one launch into the half-major
+    [L_c | L_u] rows of one buffer."""
+    T, I, H, K = 70, 130, 2, 192
+    N, L = 3 * H * DH, T + I
+    pe = pe_table(L, DH, 31)
+    pe_d = torch.from_numpy(pe).to(DEV)
+    buf = torch.zeros((2 * L, N), dtype=torch.bfloat16, device=DEV)
+    ws = [seeded((N, K), 32 + j, 0.05) for j in range(2)]
+    bs = [seeded((N,), 34 + j, 0.05, torch.float32) for j in range(2)]
+    ns = [1 + 0.2 * seeded((DH,), 36 + j, 1.0, torch.float32) for j in range(4)]
+    probs, wants = [], []
+    for j, (m, p0) in enumerate(((T, 0), (I, T))):          # stream: txt, img
+        for h in range(2):                                   # guidance half
+            x = seeded((m, K), 40 + 2 * j + h)
+            r0 = h * L + p0
+            probs.append(dict(x=x.to(DEV), w=ws[j].to(DEV), bias=bs[j].to(DEV), out=buf[r0:r0 + m],
+                              pe=pe_d[p0:p0 + m], q_norm=ns[2 * j].to(DEV), k_norm=ns[2 * j + 1].to(DEV)))
+            wants.append((r0, m, qkv_oracle(oracle, x, ws[j], bs[j], pe[p0:p0 + m], H, ns[2 * j], ns[2 * j + 1])))
+    n0 = engine.launch_count()
+    engine.gemm_qkv_rope(probs, H)
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 1
+    for r0, m, want in wants:
+        assert_bf16_of(buf[r0:r0 + m], want)
