@@ -68,7 +68,8 @@ class TpReduceDesc(ctypes.Structure):
 class QkvRopeDesc(ctypes.Structure):
     """b2g_qkv_rope_desc: RoPE rows and RMSNorm scales of one qkv projection problem."""
     _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
-                ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64), ("pe_period", ctypes.c_int64)]
+                ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64), ("pe_period", ctypes.c_int64),
+                ("a_scale", ctypes.c_void_p), ("b_scale", ctypes.c_void_p)]
 
 
 _lib = None
@@ -85,6 +86,8 @@ _SIGNATURES = {
                                                                                    ctypes.c_void_p, ctypes.c_void_p],
                           ctypes.c_int),
     "b2g_gemm_fp8": ([ctypes.POINTER(GemmDesc), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "b2g_gemm_fp8_group": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                            ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_gemm_tp_reduce": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int64), ctypes.c_int,
                             ctypes.POINTER(TpReduceDesc), ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
@@ -178,6 +181,11 @@ def _require_cuda(*ts: torch.Tensor | None) -> None:
             raise B2GError("all tensors must be CUDA tensors")
 
 
+def _operand_dtype(t: torch.Tensor) -> int:
+    """b2g dtype of a GEMM operand: uint8 tensors hold E4M3 codes."""
+    return E4M3 if t.dtype == torch.uint8 else _TORCH_TO_B2G[t.dtype]
+
+
 def _gemm_desc(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out: torch.Tensor | None,
                out_dtype: torch.dtype | None, epilogue: str, gate: torch.Tensor | None) -> tuple[GemmDesc, torch.Tensor]:
     _require_cuda(x, w, bias, out, gate)
@@ -196,8 +204,8 @@ def _gemm_desc(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, out:
         raise B2GError("gemm: out must be [M, N] with unit column stride")
     d = GemmDesc()
     d.M, d.N, d.K = M, N, K
-    d.a, d.a_dtype, d.lda = x.data_ptr(), _TORCH_TO_B2G[x.dtype], x.stride(0) if M > 1 else K
-    d.b, d.b_dtype, d.ldb = w.data_ptr(), _TORCH_TO_B2G[w.dtype], w.stride(0) if N > 1 else K
+    d.a, d.a_dtype, d.lda = x.data_ptr(), _operand_dtype(x), x.stride(0) if M > 1 else K
+    d.b, d.b_dtype, d.ldb = w.data_ptr(), _operand_dtype(w), w.stride(0) if N > 1 else K
     d.bias = _ptr(bias)
     d.bias_dtype = _TORCH_TO_B2G[bias.dtype] if bias is not None else F32
     d.d, d.d_dtype, d.ldd = out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0) if M > 1 else N
@@ -239,19 +247,31 @@ def gemm_group(problems: list[dict], stream: torch.cuda.Stream | None = None) ->
     return outs
 
 
-def quantize_e4m3(x: torch.Tensor, stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+def _q8_outputs(rows: int, cols: int, dev, out, scales, who: str) -> tuple[torch.Tensor, torch.Tensor]:
+    """Caller-given (or new) uint8 [rows, cols] code and F32 [rows] scale buffers."""
+    q = out if out is not None else torch.empty((rows, cols), dtype=torch.uint8, device=dev)
+    sc = scales if scales is not None else torch.empty(rows, dtype=torch.float32, device=dev)
+    _require_cuda(q, sc)
+    if (q.dtype != torch.uint8 or q.shape != (rows, cols) or q.stride(1) != 1 or sc.dtype != torch.float32 or
+            sc.shape != (rows,) or not sc.is_contiguous()):
+        raise B2GError(f"{who}: out must be uint8 [rows, cols] (unit column stride), scales F32 [rows]")
+    return q, sc
+
+
+def quantize_e4m3(x: torch.Tensor, out: torch.Tensor | None = None, scales: torch.Tensor | None = None,
+                  stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-row E4M3 quantisation of a 2-D F32/BF16/F16 CUDA tensor: (codes uint8 [rows, cols],
-    scales f32 [rows]) with scales = absmax/448 and codes = E4M3(x * 448/absmax)."""
+    scales f32 [rows]) with scales = absmax/448 and codes = E4M3(x * 448/absmax); into `out` and
+    `scales` when given."""
     lib = load()
     _require_cuda(x)
     if x.dim() != 2 or x.stride(1) != 1:
         raise B2GError("quantize_e4m3: 2-D tensor with unit column stride expected")
     rows, cols = x.shape
-    q = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
-    sc = torch.empty(rows, dtype=torch.float32, device=x.device)
+    q, sc = _q8_outputs(rows, cols, x.device, out, scales, "quantize_e4m3")
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_quantize_e4m3(x.data_ptr(), _TORCH_TO_B2G[x.dtype], rows, cols, x.stride(0) if rows > 1 else cols,
-                                 q.data_ptr(), cols, sc.data_ptr(), ctypes.c_void_p(s)))
+                                 q.data_ptr(), q.stride(0) if rows > 1 else cols, sc.data_ptr(), ctypes.c_void_p(s)))
     return q, sc
 
 
@@ -289,6 +309,32 @@ def gemm_fp8(x: torch.Tensor, wq: torch.Tensor, w_scale: torch.Tensor, bias: tor
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_gemm_fp8(ctypes.byref(d), _ptr(x_scale), w_scale.data_ptr(), ctypes.c_void_p(s)))
     return out
+
+
+def gemm_fp8_group(problems: list[dict], stream: torch.cuda.Stream | None = None) -> list[torch.Tensor]:
+    """Up to four FP8 linears in one call (b2g_gemm_fp8_group): dicts with x (uint8 E4M3 codes),
+    x_scale, w (uint8 codes), w_scale and gemm()'s bias / out / out_dtype / epilogue / gate;
+    those that share N, K and epilogue run as one tensor-core launch."""
+    lib = load()
+    descs, outs, a_sc, b_sc = [], [], [], []
+    for pr in problems:
+        x, w = pr["x"], pr["w"]
+        if x.dtype != torch.uint8 or w.dtype != torch.uint8:
+            raise B2GError("gemm_fp8_group: uint8 E4M3 x and w expected")
+        _require_cuda(pr["x_scale"], pr["w_scale"])
+        d, out = _gemm_desc(x, w, pr.get("bias"), pr.get("out"), pr.get("out_dtype"), pr.get("epilogue", "none"),
+                            pr.get("gate"))
+        descs.append(d)
+        outs.append(out)
+        a_sc.append(pr["x_scale"].data_ptr())
+        b_sc.append(pr["w_scale"].data_ptr())
+    n = len(descs)
+    arr = (GemmDesc * n)(*descs)
+    dev = problems[0]["x"].device if problems else torch.device("cuda")
+    s = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    _check(lib.b2g_gemm_fp8_group(arr, (ctypes.c_void_p * n)(*a_sc), (ctypes.c_void_p * n)(*b_sc), n,
+                                  ctypes.c_void_p(s)))
+    return outs
 
 
 def gemm_tp_reduce(problems: list[dict], row0: list[int], tp: TpReduceDesc,
@@ -470,7 +516,8 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
     optionally pe_period P (row m uses pe row m % P; pe then needs P rows only: stacked
     guidance halves of one sequence).  Output columns [q | k | v]: q and k heads normed and
     rotated, v the plain product (+ bias).  Up to four problems (txt and img streams, times
-    the guidance halves) run as one launch.  One problem may carry gelu_out (a
+    the guidance halves) run as one launch.  FP8 form: x and w uint8 E4M3 codes with x_scale
+    (per row) and w_scale (per output channel, from quantize_e4m3).  One problem may carry gelu_out (a
     bf16 [M, N - 3*n_head*128] view): w then has more rows, and those columns get bias + GELU
     into gelu_out (the single block's linear1 in one launch); out holds the qkv columns.
     """
@@ -503,9 +550,14 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
             raise B2GError("gemm_qkv_rope: pe_period must be 0 or positive")
         if pe.numel() < (period or pr["x"].shape[0]) * 256:
             raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x (per pe_period row)")
+        xs, ws = pr.get("x_scale"), pr.get("w_scale")
+        if pr["x"].dtype == torch.uint8:
+            _require_cuda(xs, ws)
+            if xs is None or ws is None or pr["w"].dtype != torch.uint8:
+                raise B2GError("gemm_qkv_rope: E4M3 x needs x_scale, and uint8 w with w_scale")
         descs.append(d)
         ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn), _ptr(tail),
-                                 tail.stride(0) if tail is not None else 0, period))
+                                 tail.stride(0) if tail is not None else 0, period, _ptr(xs), _ptr(ws)))
         outs.append(out)
         keep.append(pe)
     arr = (GemmDesc * len(descs))(*descs)
@@ -562,12 +614,15 @@ def modulate_to_bf16(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, 
 
 
 def modulate_to_e4m3(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6,
+                     out: torch.Tensor | None = None, scales: torch.Tensor | None = None,
                      stream: torch.cuda.Stream | None = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """The modulated rows quantised per row to E4M3: (codes uint8 [M, C], row scales f32 [M])."""
+    """The modulated rows quantised per row to E4M3: (codes uint8 [M, C], row scales f32 [M]),
+    into `out` (contiguous) and `scales` when given."""
     lib = load()
     M, C = _modulate_args(x, shift, scale)
-    codes = torch.empty((M, C), dtype=torch.uint8, device=x.device)
-    rs = torch.empty(M, dtype=torch.float32, device=x.device)
+    codes, rs = _q8_outputs(M, C, x.device, out, scales, "modulate_to_e4m3")
+    if not codes.is_contiguous():
+        raise B2GError("modulate_to_e4m3: out must be contiguous")
     s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
     _check(lib.b2g_modulate_to_e4m3(x.data_ptr(), shift.data_ptr(), scale.data_ptr(), codes.data_ptr(),
                                     rs.data_ptr(), M, C, eps, ctypes.c_void_p(s)))

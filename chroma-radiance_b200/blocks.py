@@ -106,8 +106,9 @@ class Scratch:
         B = halves
         self.qkv = torch.empty((B * L, 3 * HIDDEN), dtype=torch.bfloat16, device=dev)  # normed, rotated
         self.attn = torch.empty((B * L, HIDDEN), dtype=torch.bfloat16, device=dev)
-        self.h_img = torch.empty((B * I, MLP), dtype=torch.bfloat16, device=dev)
-        self.h_txt = torch.empty((B * T, MLP), dtype=torch.bfloat16, device=dev)
+        self.h = torch.empty((B * L, MLP), dtype=torch.bfloat16, device=dev)  # txt rows of all halves, then img
+        self.h_txt = self.h[:B * T]
+        self.h_img = self.h[B * T:]
         self.cat = torch.empty((B * L, HIDDEN + MLP), dtype=torch.bfloat16, device=dev)
 
 
@@ -310,3 +311,227 @@ def block_pair_flops(T: int, I: int) -> tuple[float, float]:
     """(linear FLOPs, attention FLOPs counted unmasked) of one double + one single block."""
     ops = block_pair_ops(T, I)
     return (sum(f for _, kind, f in ops if kind == "gemm"), sum(f for _, kind, f in ops if kind == "attention"))
+
+
+# ---------------------------------------------------------------------------- FP8 variant
+# BASELINE config 5's transformer: every linear on E4M3 weights with one fp32 scale per output
+# channel (absmax / 448, made once at load) and E4M3 activations with one scale per token.
+# The reference's quantised path is INT8 (linear_prequant / quantize_act, kernels.cu:1988-2125,
+# 2504-2644) and has no FP8 form; the producers here follow its structure: the modulation
+# writes the quantised A operand of qkv / mlp0 / linear1 directly (modulate_to_e4m3), and the
+# bf16 attention output, MLP hidden state and single-block concat buffer are quantised per
+# token before proj / mlp2 / linear2 (one launch each).  Epilogues are those of the bf16 path.
+
+
+@dataclass
+class QLinear:
+    """E4M3 weight codes [N, K] (uint8) with one fp32 scale per output channel [N]."""
+    q: torch.Tensor
+    s: torch.Tensor
+
+
+@dataclass
+class Q8:
+    """Per-token E4M3 activations: codes [M, K] (uint8) and one fp32 scale per row [M]."""
+    q: torch.Tensor
+    s: torch.Tensor
+
+    def rows(self, a: int, b: int) -> "Q8":
+        return Q8(self.q[a:b], self.s[a:b])
+
+
+@dataclass
+class StreamWeightsFP8:
+    qkv: QLinear
+    qkv_b: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    proj: QLinear
+    proj_b: torch.Tensor
+    mlp0: QLinear
+    mlp0_b: torch.Tensor
+    mlp2: QLinear
+    mlp2_b: torch.Tensor
+
+
+@dataclass
+class SingleWeightsFP8:
+    linear1: QLinear
+    linear1_b: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    linear2: QLinear
+    linear2_b: torch.Tensor
+
+
+def quantize_weight(w: torch.Tensor) -> QLinear:
+    """The load-time FP8 transform of one linear's weight (per output channel)."""
+    return QLinear(*b2g.quantize_e4m3(w))
+
+
+def quantize_stream(w: StreamWeights) -> StreamWeightsFP8:
+    return StreamWeightsFP8(quantize_weight(w.qkv_w), w.qkv_b, w.q_norm, w.k_norm, quantize_weight(w.proj_w),
+                            w.proj_b, quantize_weight(w.mlp0_w), w.mlp0_b, quantize_weight(w.mlp2_w), w.mlp2_b)
+
+
+def quantize_single(w: SingleWeights) -> SingleWeightsFP8:
+    return SingleWeightsFP8(quantize_weight(w.linear1_w), w.linear1_b, w.q_norm, w.k_norm,
+                            quantize_weight(w.linear2_w), w.linear2_b)
+
+
+def _q8(rows: int, cols: int, dev) -> Q8:
+    return Q8(torch.empty((rows, cols), dtype=torch.uint8, device=dev), torch.empty(rows, device=dev))
+
+
+class ScratchFP8(Scratch):
+    """The bf16 scratch plus the E4M3 forms of the quantised activations."""
+
+    def __init__(self, T: int, I: int, dev, halves: int = 1):
+        super().__init__(T, I, dev, halves)
+        R = halves * (T + I)
+        self.mod8 = _q8(R, HIDDEN, dev)          # modulated block inputs
+        self.attn8 = _q8(R, HIDDEN, dev)         # double-block attention output (proj input)
+        self.h8 = _q8(R, MLP, dev)               # GELU'd MLP hidden state (mlp2 input)
+        self.cat8 = _q8(R, HIDDEN + MLP, dev)    # single-block [attn | mlp] (linear2 input)
+
+
+def double_block_attention_fp8(txt_w: StreamWeightsFP8, img_w: StreamWeightsFP8, txt_mod1, img_mod1, txt, img,
+                               txt_gate1, img_gate1, pe, mask, s: ScratchFP8, mark=None) -> None:
+    """double_block_attention on E4M3 weights: txt_mod1 / img_mod1 are Q8 (or lists of Q8, one
+    per guidance half) from modulate_to_e4m3; the rest as in double_block_attention."""
+    mark = mark or _no_mark
+    txt_m, img_m, txts, imgs = _halves(txt_mod1), _halves(img_mod1), _halves(txt), _halves(img)
+    B, T = len(txts), txts[0].shape[0]
+    L = T + imgs[0].shape[0]
+    b2g.gemm_qkv_rope([dict(x=txt_m[b].q, x_scale=txt_m[b].s, w=txt_w.qkv.q, w_scale=txt_w.qkv.s, bias=txt_w.qkv_b,
+                            out=s.qkv[b * L:b * L + T], pe=pe[:T], q_norm=txt_w.q_norm, k_norm=txt_w.k_norm)
+                       for b in range(B)] +
+                      [dict(x=img_m[b].q, x_scale=img_m[b].s, w=img_w.qkv.q, w_scale=img_w.qkv.s, bias=img_w.qkv_b,
+                            out=s.qkv[b * L + T:(b + 1) * L], pe=pe[T:L], q_norm=img_w.q_norm,
+                            k_norm=img_w.k_norm) for b in range(B)], HEADS)
+    mark("double.qkv")
+    for b, mb in enumerate(_masks(mask, B)):
+        rows = s.qkv[b * L:(b + 1) * L]
+        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
+                           attn_mask=mb, out=s.attn[b * L:(b + 1) * L])
+    mark("double.attention")
+    b2g.quantize_e4m3(s.attn[:B * L], out=s.attn8.q[:B * L], scales=s.attn8.s[:B * L])
+    mark("double.quantize_attn")
+    a8 = s.attn8
+    b2g.gemm_fp8_group([dict(x=a8.q[b * L:b * L + T], x_scale=a8.s[b * L:b * L + T], w=txt_w.proj.q,
+                             w_scale=txt_w.proj.s, bias=txt_w.proj_b, out=txts[b], epilogue="gated_residual",
+                             gate=txt_gate1) for b in range(B)] +
+                       [dict(x=a8.q[b * L + T:(b + 1) * L], x_scale=a8.s[b * L + T:(b + 1) * L], w=img_w.proj.q,
+                             w_scale=img_w.proj.s, bias=img_w.proj_b, out=imgs[b], epilogue="gated_residual",
+                             gate=img_gate1) for b in range(B)])
+    mark("double.proj")
+
+
+def double_block_mlp_fp8(txt_w: StreamWeightsFP8, img_w: StreamWeightsFP8, txt_mod2, img_mod2, txt, img,
+                         txt_gate2, img_gate2, s: ScratchFP8, mark=None) -> None:
+    """double_block_mlp on E4M3 weights (modulated inputs as Q8, one per half or a list)."""
+    mark = mark or _no_mark
+    txt_m, img_m, txts, imgs = _halves(txt_mod2), _halves(img_mod2), _halves(txt), _halves(img)
+    B, T, I = len(txts), txts[0].shape[0], imgs[0].shape[0]
+    # h rows: every half's txt rows, then every half's img rows (one quantisation launch)
+    ht = [(b * T, (b + 1) * T) for b in range(B)]
+    hi = [(B * T + b * I, B * T + (b + 1) * I) for b in range(B)]
+    b2g.gemm_fp8_group([dict(x=txt_m[b].q, x_scale=txt_m[b].s, w=txt_w.mlp0.q, w_scale=txt_w.mlp0.s,
+                             bias=txt_w.mlp0_b, out=s.h[r0:r1], epilogue="gelu") for b, (r0, r1) in enumerate(ht)] +
+                       [dict(x=img_m[b].q, x_scale=img_m[b].s, w=img_w.mlp0.q, w_scale=img_w.mlp0.s,
+                             bias=img_w.mlp0_b, out=s.h[r0:r1], epilogue="gelu") for b, (r0, r1) in enumerate(hi)])
+    mark("double.mlp0")
+    R = B * (T + I)
+    b2g.quantize_e4m3(s.h[:R], out=s.h8.q[:R], scales=s.h8.s[:R])
+    mark("double.quantize_h")
+    h8 = s.h8
+    b2g.gemm_fp8_group([dict(x=h8.q[r0:r1], x_scale=h8.s[r0:r1], w=txt_w.mlp2.q, w_scale=txt_w.mlp2.s,
+                             bias=txt_w.mlp2_b, out=txts[b], epilogue="gated_residual", gate=txt_gate2)
+                        for b, (r0, r1) in enumerate(ht)] +
+                       [dict(x=h8.q[r0:r1], x_scale=h8.s[r0:r1], w=img_w.mlp2.q, w_scale=img_w.mlp2.s,
+                             bias=img_w.mlp2_b, out=imgs[b], epilogue="gated_residual", gate=img_gate2)
+                        for b, (r0, r1) in enumerate(hi)])
+    mark("double.mlp2")
+
+
+def single_block_fp8(w: SingleWeightsFP8, x_mod: Q8, x, gate, pe, mask, s: ScratchFP8, mark=None) -> None:
+    """single_block on E4M3 weights; x_mod is the Q8 of all B*L rows (modulate_to_e4m3)."""
+    mark = mark or _no_mark
+    L = pe.shape[0]
+    B = x.shape[0] // L
+    assert B * L == x.shape[0], "x must hold whole guidance halves of pe.shape[0] rows"
+    R = B * L
+    b2g.gemm_qkv_rope([dict(x=x_mod.q, x_scale=x_mod.s, w=w.linear1.q, w_scale=w.linear1.s, bias=w.linear1_b,
+                            out=s.qkv[:R], pe=pe, pe_period=L, q_norm=w.q_norm, k_norm=w.k_norm,
+                            gelu_out=s.cat[:R, HIDDEN:])], HEADS)
+    mark("single.linear1")
+    for b, mb in enumerate(_masks(mask, B)):
+        rows = s.qkv[b * L:(b + 1) * L]
+        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
+                           attn_mask=mb, out=s.cat[b * L:(b + 1) * L, :HIDDEN])
+    mark("single.attention")
+    b2g.quantize_e4m3(s.cat[:R], out=s.cat8.q[:R], scales=s.cat8.s[:R])
+    mark("single.quantize_cat")
+    b2g.gemm_fp8_group([dict(x=s.cat8.q[:R], x_scale=s.cat8.s[:R], w=w.linear2.q, w_scale=w.linear2.s,
+                             bias=w.linear2_b, out=x, epilogue="gated_residual", gate=gate)])
+    mark("single.linear2")
+
+
+def block_pair_ops_fp8(T: int, I: int) -> list[tuple[str, str, float]]:
+    """block_pair_ops with the FP8 path's per-token quantisations (kind "quantize", 0 FLOPs)."""
+    out = []
+    for lab, kind, f in block_pair_ops(T, I):
+        out.append((lab, kind, f))
+        if lab == "double.attention":
+            out.append(("double.quantize_attn", "quantize", 0.0))
+        elif lab == "double.mlp0":
+            out.append(("double.quantize_h", "quantize", 0.0))
+        elif lab == "single.attention":
+            out.append(("single.quantize_cat", "quantize", 0.0))
+    return out
+
+
+@dataclass
+class PassWeightsFP8:
+    """PassWeights with every linear in E4M3 (quantize_pass)."""
+    double: list          # [(txt StreamWeightsFP8, img StreamWeightsFP8)]
+    single: list          # [SingleWeightsFP8]
+    mods: torch.Tensor
+
+
+def quantize_pass(pw: PassWeights) -> PassWeightsFP8:
+    """The load-time FP8 transform of a whole pass (8.6 GB of codes for Chroma's 57 blocks)."""
+    return PassWeightsFP8([(quantize_stream(t), quantize_stream(i)) for t, i in pw.double],
+                          [quantize_single(w) for w in pw.single], pw.mods)
+
+
+def forward_pass_fp8(pw: PassWeightsFP8, x, pe, mask, s: ScratchFP8, T: int) -> None:
+    """forward_pass on E4M3 weights: every block's modulation writes the E4M3 A operand with
+    per-token scales (modulate_to_e4m3); layout, guidance halves and masks as forward_pass."""
+    L = pe.shape[0]
+    B = x.shape[0] // L
+    assert B * L == x.shape[0] and 0 < T < L, "x must hold whole guidance halves of pe.shape[0] rows"
+    txts = [x[b * L:b * L + T] for b in range(B)]
+    imgs = [x[b * L + T:(b + 1) * L] for b in range(B)]
+    mod_t = [s.mod8.rows(b * L, b * L + T) for b in range(B)]
+    mod_i = [s.mod8.rows(b * L + T, (b + 1) * L) for b in range(B)]
+
+    def modulate(src, shift, scale, dst: Q8):
+        b2g.modulate_to_e4m3(src, shift, scale, out=dst.q, scales=dst.s)
+
+    for i, (tw, iw) in enumerate(pw.double):
+        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        for b in range(B):
+            modulate(txts[b], mt[0], mt[1], mod_t[b])
+            modulate(imgs[b], mi[0], mi[1], mod_i[b])
+        double_block_attention_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[2], mi[2], pe, mask, s)
+        for b in range(B):
+            modulate(txts[b], mt[3], mt[4], mod_t[b])
+            modulate(imgs[b], mi[3], mi[4], mod_i[b])
+        double_block_mlp_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[5], mi[5], s)
+    base = 12 * len(pw.double)
+    for i, sw in enumerate(pw.single):
+        m = pw.mods[base + 3 * i:base + 3 * i + 3]
+        x8 = s.mod8.rows(0, B * L)
+        modulate(x, m[0], m[1], x8)
+        single_block_fp8(sw, x8, x, m[2], pe, mask, s)

@@ -216,6 +216,27 @@ b2g_status desc_to_problem(const b2g_gemm_desc* d, const char* who, GemmProblem*
   return B2G_OK;
 }
 
+// desc_to_problem for a problem on E4M3 operands: both a and b E4M3 (activations already
+// quantised per row) with their per-row (a_scale) and per-output-channel (b_scale) scales.
+b2g_status fp8_desc_to_problem(const b2g_gemm_desc* d, const float* a_scale, const float* b_scale, const char* who,
+                               GemmProblem* p, bool* empty) {
+  const std::string w(who);
+  if (!d) return set_error(B2G_ERR_INVALID, w + ": null descriptor");
+  if (d->a_dtype != B2G_E4M3 || d->b_dtype != B2G_E4M3)
+    return set_error(B2G_ERR_UNSUPPORTED, w + ": E4M3 activations and weights expected");
+  if (!a_scale || !b_scale) return set_error(B2G_ERR_INVALID, w + ": E4M3 operands need row and column scales");
+  if (d->d_dtype == B2G_E4M3) return set_error(B2G_ERR_UNSUPPORTED, w + ": E4M3 output is not implemented");
+  b2g_gemm_desc dd = *d;  // the checks of the 16-bit path, on a descriptor with bf16 operand tags
+  dd.a_dtype = dd.b_dtype = B2G_BF16;
+  b2g_status s = desc_to_problem(&dd, who, p, empty);
+  if (s != B2G_OK || *empty) return s;
+  if (p->K == 0) return set_error(B2G_ERR_INVALID, w + ": K must be positive");
+  p->a_dtype = p->b_dtype = B2G_E4M3;
+  p->a_scale = a_scale;
+  p->b_scale = b_scale;
+  return B2G_OK;
+}
+
 }  // namespace
 }  // namespace b2g
 
@@ -374,6 +395,40 @@ b2g_status b2g_gemm_fp8(const b2g_gemm_desc* d, const float* a_scale, const floa
   return tc_gemm_launch(p, st);
 }
 
+b2g_status b2g_gemm_fp8_group(const b2g_gemm_desc* descs, const float* const* a_scales,
+                              const float* const* b_scales, int count, void* stream) {
+  if (count < 0 || (count > 0 && (!descs || !a_scales || !b_scales)))
+    return set_error(B2G_ERR_INVALID, "b2g_gemm_fp8_group: bad descriptor or scale arrays");
+  GemmProblem ps[kMaxGemmGroups];
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    GemmProblem p;
+    bool empty = false;
+    b2g_status s = fp8_desc_to_problem(descs + i, a_scales[i], b_scales[i], "b2g_gemm_fp8_group", &p, &empty);
+    if (s != B2G_OK) return s;
+    std::string why;
+    if (!empty && !tc_gemm_supported(p, &why)) return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_fp8_group: " + why);
+    if (!empty && n < kMaxGemmGroups) ps[n] = p;
+    if (!empty) ++n;
+  }
+  if (n == 0) return B2G_OK;
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bool one_launch = n >= 2 && n <= kMaxGemmGroups;
+  for (int i = 1; one_launch && i < n; ++i) one_launch = tc_gemm_groupable(ps[0], ps[i]);
+  if (one_launch) return tc_gemm_launch_group(ps, n, st);
+  for (int i = 0; i < count; ++i) {
+    GemmProblem p;
+    bool empty = false;
+    if ((s = fp8_desc_to_problem(descs + i, a_scales[i], b_scales[i], "b2g_gemm_fp8_group", &p, &empty)) != B2G_OK)
+      return s;
+    if (!empty && (s = tc_gemm_launch(p, st)) != B2G_OK) return s;
+  }
+  return B2G_OK;
+}
+
 b2g_status b2g_bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias,
                                    const float* gate, float* residual, int64_t ldr, int64_t M, int64_t N,
                                    void* stream) {
@@ -503,8 +558,9 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     if (tail ? (count != 1 || d->N <= qkv_cols) : d->N != qkv_cols)
       return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: N must be 3 * n_head * 128 (more, with one problem, for "
                                         "a GELU tail)");
-    if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16))
-      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16 or fp16 operands of one type");
+    const bool fp8 = d->a_dtype == B2G_E4M3;
+    if (d->a_dtype != d->b_dtype || (d->a_dtype != B2G_BF16 && d->a_dtype != B2G_F16 && !fp8))
+      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_qkv_rope: bf16, fp16 or E4M3 operands of one type");
     if (!rope[i].pe) return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe is required");
     if (rope[i].pe_period < 0 || rope[i].pe_period > (1ll << 30))
       return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe_period must be 0 or a positive row count");
@@ -512,7 +568,8 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     bool empty = false;
     b2g_gemm_desc dq = *d;  // d holds the [q | k | v] columns only; the tail goes to gelu_out
     dq.N = qkv_cols;
-    b2g_status s = desc_to_problem(&dq, "b2g_gemm_qkv_rope", &p, &empty);
+    b2g_status s = fp8 ? fp8_desc_to_problem(&dq, rope[i].a_scale, rope[i].b_scale, "b2g_gemm_qkv_rope", &p, &empty)
+                       : desc_to_problem(&dq, "b2g_gemm_qkv_rope", &p, &empty);
     if (s != B2G_OK) return s;
     if (empty) continue;
     p.N = d->N;

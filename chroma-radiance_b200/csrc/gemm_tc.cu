@@ -568,8 +568,10 @@ __device__ __forceinline__ void prefetch_residual(const TcParams& p, const TcGro
 // Pass 1 reads the head's 128 accumulator columns from TMEM for the sum of squares, pass 2
 // reads them again and writes the result.  With a GELU tail (the single block's linear1: its
 // weight rows are [q | k | v | mlp]), 128-column halves at or past p.split take bias + GELU
-// and leave through the tensor map that follows tmD (the launch then has one group).
-template <int BN, typename Release>
+// and leave through the tensor map that follows tmD (the launch then has one group).  With
+// E4M3 operands (KIND 2) every accumulator chunk is first scaled by the row's activation scale
+// and the columns' weight scales, as in the other epilogues.
+template <int BN, int KIND, typename Release>
 __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
                                               uint32_t tacc, Release release, const CUtensorMap* tmD, int m,
                                               int n_base) {
@@ -577,6 +579,8 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
   const int c0 = e.half * 4;           // this warp's first 32-column chunk in the tile
   const int col = n_base + c0 * 32;    // first column of the head (uniform across the warp)
   const int m_warp0 = m - e.lane;
+  float rs = 0.f;                      // E4M3: this row's activation scale
+  if constexpr (KIND == 2) rs = m < G.M ? __ldg(G.a_scale + m) : 0.f;
   if (p.split && col >= p.split) {
     const float* sbg = p.bias_kind ? e.sbias + c0 * 32 : nullptr;
     uint32_t r[2][32];
@@ -586,6 +590,7 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
       tmem_wait_ld();
       if (i + 1 < 4) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);
       if (i == 3) release();
+      if constexpr (KIND == 2) scale_chunk(r[i & 1], rs, e.sscale + (c0 + i) * 32);
       float v[32];
       chunk_values<B2G_EPI_GELU>(r[i & 1], sbg ? sbg + i * 32 : nullptr, p.alpha, v);
       if (m_warp0 < G.M && col + i * 32 < p.N)
@@ -606,6 +611,7 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
       float v[32];
       tmem_ld_32x32b_x32(tacc + (c0 + i) * 32, r);
       tmem_wait_ld();
+      if constexpr (KIND == 2) scale_chunk(r, rs, e.sscale + (c0 + i) * 32);
       chunk_values<B2G_EPI_NONE>(r, sb ? sb + i * 32 : nullptr, p.alpha, v);
 #pragma unroll
       for (int j = 0; j < 32; ++j) ss += v[j] * v[j];
@@ -622,6 +628,7 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
     tmem_wait_ld();
     if (i + 1 < 4) tmem_ld_32x32b_x32(tacc + (c0 + i + 1) * 32, r[(i + 1) & 1]);
     if (i == 3) release();
+    if constexpr (KIND == 2) scale_chunk(r[i & 1], rs, e.sscale + (c0 + i) * 32);
     float v[32];
     chunk_values<B2G_EPI_NONE>(r[i & 1], sb ? sb + i * 32 : nullptr, p.alpha, v);
     if (sec < 2) {
@@ -662,7 +669,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
     tp_epilogue_item<BN>(p, G, e, tacc, release, m, n_base, slot);
     return;
   } else if constexpr (EPI == kEpiQkvRope) {
-    if constexpr (BN == 256) qkv_rope_item<BN>(p, G, e, obuf, tacc, release, tmD, m, n_base);
+    if constexpr (BN == 256) qkv_rope_item<BN, KIND>(p, G, e, obuf, tacc, release, tmD, m, n_base);
     return;
   }
   float rs = 0.f;  // E4M3: this row's activation scale
@@ -1238,10 +1245,10 @@ b2g_status dispatch_out(const TcMaps& maps, const TcParams& prm, int grid, b2g_e
   if constexpr (KIND == 0) {
     if (static_cast<int>(epi) == kEpiTpReduce)
       return launch_one<PAIR, BN, STAGES, kEpiTpReduce, OUT_F32, 0>(maps, prm, grid, st);
-    if (static_cast<int>(epi) == kEpiQkvRope) {
-      if constexpr (BN == 256) return launch_one<PAIR, BN, STAGES, kEpiQkvRope, OUT_BF16, 0>(maps, prm, grid, st);
-      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: 256-column tiles only");
-    }
+  }
+  if (static_cast<int>(epi) == kEpiQkvRope) {
+    if constexpr (BN == 256) return launch_one<PAIR, BN, STAGES, kEpiQkvRope, OUT_BF16, KIND>(maps, prm, grid, st);
+    return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: 256-column tiles only");
   }
   if (epi == B2G_EPI_GATED_RESIDUAL)
     return launch_one<PAIR, BN, STAGES, B2G_EPI_GATED_RESIDUAL, OUT_F32, KIND>(maps, prm, grid, st);
@@ -1433,8 +1440,8 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   prm.tma_store = all_vec && g_tma_store && !p.tp ? 1 : 0;
   if (p.rope) {
     const QkvRope& r = *p.rope;
-    if (kind != 0 || p.d_dtype != B2G_BF16 || p.batch != 1)
-      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: bf16/fp16 operands, bf16 output, no batch");
+    if (kind == 1 || p.d_dtype != B2G_BF16 || p.batch != 1)
+      return set_error(B2G_ERR_UNSUPPORTED, "qkv rope epilogue: bf16/fp16/E4M3 operands, bf16 output, no batch");
     const bool tail = r.gelu_out != nullptr;
     if (r.heads < 1 || (tail ? p.N <= 3 * r.heads * 128 : p.N != 3 * r.heads * 128))
       return set_error(B2G_ERR_INVALID, "qkv rope epilogue: N must be 3 * heads * 128 (more with a GELU tail)");

@@ -187,6 +187,15 @@ b2g_status b2g_quantize_e4m3(const void* src, b2g_dtype src_dtype, int64_t rows,
  * same epilogues and output types as b2g_gemm.  K % 16 == 0 (16-byte rows). */
 b2g_status b2g_gemm_fp8(const b2g_gemm_desc* desc, const float* a_scale, const float* b_scale, void* stream);
 
+/* `count` (up to 4) b2g_gemm_fp8 problems on E4M3 activations (already quantised per row)
+ * and E4M3 weights, a_scales[i] / b_scales[i] their scales.  Problems that share N, K, bias
+ * presence, output dtype and epilogue run as one tensor-core launch (the FP8 form of
+ * b2g_gemm_group: the txt and img streams of a double-block layer, and with guidance both
+ * halves of each); otherwise one after the other.  No reference counterpart (the reference's
+ * quantised linears are INT8, cublas_ops.cuh:294-791). */
+b2g_status b2g_gemm_fp8_group(const b2g_gemm_desc* descs, const float* const* a_scales,
+                              const float* const* b_scales, int count, void* stream);
+
 /* residual[m, n] (F32, row stride ldr) += gate[n] * (y[m, n] + bias[n]) for the tensor-parallel
  * path: the reference's gated_residual (kernels.cu:942-968) with the linear's bias folded in,
  * applied once after the all-reduce of the row-split layer's partial sums (which carry no
@@ -228,7 +237,9 @@ b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int 
  * reference runs these as three linears into F32 q, k, v, then qk_norm (rms_norm per head with
  * a learned scale) on q and k (chroma.cuh:822-842 double block, chroma.cuh:1108-1116 single
  * block), then RoPE + bf16 inside attention_with_rope (apply_rope_fused_bf16,
- * cudnn_attention.cuh:449-476).  descs[i]: bf16/fp16 x [M,K] . w[N,K]^T + bias (F32) with
+ * cudnn_attention.cuh:449-476).  descs[i]: bf16/fp16 x [M,K] . w[N,K]^T + bias (F32), or on
+ * E4M3 x and w with rope[i].a_scale / b_scale (the FP8 variant: acc * a_scale[m] * b_scale[n]
+ * before the bias), with
  * N = 3 * n_head * 128 ([q | k | v] weight rows, as the reference's fused qkv weight stores
  * them), epilogue B2G_EPI_NONE, bf16 output d [M, ldd] (16-byte aligned rows).  In the output
  * the q and k heads are RMSNorm'd with rope[i].q_norm / k_norm ([128] F32 each, NULL: no norm;
@@ -250,6 +261,8 @@ typedef struct {
   int64_t pe_period;     /* 0, or P > 0: row m rotates by pe row m % P (several sequences of
                             P tokens stacked in one problem, e.g. the conditional and
                             unconditional halves of a guidance batch; pe then holds P rows) */
+  const float* a_scale;  /* E4M3 operands only: per-row activation scales [M] */
+  const float* b_scale;  /* E4M3 operands only: per-output-channel weight scales [N] */
 } b2g_qkv_rope_desc;
 b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
                              float eps, void* stream);

@@ -23,13 +23,28 @@ def test_block_pair_flops_match_baseline():
 def test_bench_help_lists_workloads():
     r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--help"], capture_output=True, text=True)
     assert r.returncode == 0
-    for w in ("config1", "config2", "config4"):
+    for w in ("config1", "config2", "config4", "config5"):
         assert w in r.stdout
 
 
 def test_reference_arm_without_gpu_reports_unavailable_or_runs():
-    """The config4 reference arm has no counterpart in the reference: one JSON line saying so."""
-    r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--workload", "config4"],
-                       capture_output=True, text=True, timeout=120)
-    assert r.returncode == 0
-    assert '"unavailable"' in r.stdout
+    """The config4 and config5 reference arms have no counterpart in the reference (no TP, no
+    FP8 path): one JSON line saying so."""
+    for w in ("config4", "config5"):
+        r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--workload", w],
+                           capture_output=True, text=True, timeout=120)
+        assert r.returncode == 0
+        assert '"unavailable"' in r.stdout
+
+
+def test_fp8_block_pair_ops():
+    """The FP8 block pair has the bf16 pair's FLOPs plus three zero-FLOP quantisation steps, each
+    right after the operation whose output it quantises."""
+    ops8 = blocks.block_pair_ops_fp8(512, 1024)
+    ops = blocks.block_pair_ops(512, 1024)
+    assert sum(f for _, _, f in ops8) == sum(f for _, _, f in ops)
+    labels = [lab for lab, _, _ in ops8]
+    assert [lab for lab, kind, _ in ops8 if kind == "quantize"] == ["double.quantize_attn", "double.quantize_h",
+                                                                    "single.quantize_cat"]
+    assert labels.index("double.quantize_attn") == labels.index("double.attention") + 1
+    assert labels.index("single.quantize_cat") == labels.index("single.attention") + 1

@@ -214,3 +214,72 @@ def test_cfg_pass_equals_each_half_alone(engine):
             else:
                 check_delta(x[b * L:(b + 1) * L], ys[b], x0[b * L:(b + 1) * L])
     assert not torch.equal(x[:L], x[L:])
+
+
+def test_fp8_block_pair_close_to_bf16(engine, setup):
+    """Config 5's transformer block pair (E4M3 weights per channel, per-token E4M3 activations,
+    the bf16 path's epilogues) against the bf16 block pair on the same weights and inputs:
+    the difference is E4M3 rounding of both operands of every linear (2.65% relative per
+    element on Gaussian operands), so the residual-stream update agrees to max|d|/max|ref|
+    <= 0.1 and cosine >= 0.998."""
+    import blocks
+
+    s = setup
+    a, gt = s["acts"], s["gates"]
+    T, I, L = s["T"], s["I"], s["L"]
+    tw8, iw8 = blocks.quantize_stream(s["txt_w"]), blocks.quantize_stream(s["img_w"])
+    sw8 = blocks.quantize_single(s["sw"])
+    s8 = blocks.ScratchFP8(T, I, DEV)
+    q8 = {k: blocks.Q8(*engine.quantize_e4m3(a[k])) for k in ("txt_mod1", "img_mod1", "txt_mod2", "img_mod2",
+                                                              "x_mod")}
+    txt, img, x = a["txt"].clone(), a["img"].clone(), a["x"].clone()
+    blocks.double_block_attention_fp8(tw8, iw8, q8["txt_mod1"], q8["img_mod1"], txt, img, gt[0], gt[1], s["pe"],
+                                      s["mask"], s8)
+    blocks.double_block_mlp_fp8(tw8, iw8, q8["txt_mod2"], q8["img_mod2"], txt, img, gt[2], gt[3], s8)
+    blocks.single_block_fp8(sw8, q8["x_mod"], x, gt[4], s["pe"], s["mask"], s8)
+    rtxt, rimg, rx = a["txt"].clone(), a["img"].clone(), a["x"].clone()
+    blocks.double_block(s["txt_w"], s["img_w"], a["txt_mod1"], a["img_mod1"], a["txt_mod2"], a["img_mod2"], rtxt,
+                        rimg, gt[0], gt[1], gt[2], gt[3], s["pe"], s["mask"], s["scratch"])
+    blocks.single_block(s["sw"], a["x_mod"], rx, gt[4], s["pe"], s["mask"], s["scratch"])
+    torch.cuda.synchronize()
+    engine.check_device_error()
+    for mine, ref, x0 in ((txt, rtxt, a["txt"]), (img, rimg, a["img"]), (x, rx, a["x"])):
+        dm, dr = (mine - x0).double(), (ref - x0).double()
+        err = float((dm - dr).abs().max() / dr.abs().max())
+        c = cos(dm, dr)
+        print(f"fp8 vs bf16: max rel {err:.4f} cos {c:.6f}")
+        assert err <= 0.1 and c >= 0.998
+
+
+def test_fp8_cfg_pass_equals_each_half_alone(engine):
+    """forward_pass_fp8 over two stacked guidance halves is bit-identical to each half alone
+    with the GEMM variant fixed (the quantisations are per row, so they see the same rows)."""
+    import blocks
+
+    T, I = 128, 256
+    L = T + I
+    g = torch.Generator(device=DEV).manual_seed(13)
+    pw = blocks.random_pass(g, DEV, n_double=2, n_single=2)
+    pw.mods.copy_(torch.randn(tuple(pw.mods.shape), generator=g, device=DEV) * 0.1)
+    pw8 = blocks.quantize_pass(pw)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=DEV) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    masks = torch.zeros((2, L), device=DEV)
+    masks[0, T - 40:T] = float("-inf")
+    masks[1, 1:T] = float("-inf")
+    x0 = torch.randn((2 * L, blocks.HIDDEN), generator=g, device=DEV)
+    engine.set_gemm_variant(2, 0)
+    try:
+        x = x0.clone()
+        blocks.forward_pass_fp8(pw8, x, pe, masks, blocks.ScratchFP8(T, I, DEV, halves=2), T)
+        ys = []
+        for b in range(2):
+            y = x0[b * L:(b + 1) * L].clone()
+            blocks.forward_pass_fp8(pw8, y, pe, masks[b], blocks.ScratchFP8(T, I, DEV), T)
+            ys.append(y)
+        torch.cuda.synchronize()
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    assert torch.isfinite(x).all()
+    for b in range(2):
+        assert torch.equal(x[b * L:(b + 1) * L], ys[b]), f"half {b}"

@@ -46,11 +46,45 @@ class FakeEngine:
         return [self._gemm(p["x"], p["w"], p.get("bias"), p.get("out"), p.get("epilogue", "none"), p.get("gate"))
                 for p in problems]
 
+    @staticmethod
+    def _deq(t, sc):
+        if t.dtype != torch.uint8:
+            return t.float()
+        return t.view(torch.float8_e4m3fn).float() * sc[:, None]
+
+    def quantize_e4m3(self, x, out=None, scales=None):
+        self.calls.append(("quantize", 1))
+        xf = x.float()
+        amax = xf.abs().amax(1)
+        sc = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+        q = (xf / sc[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+        out = out if out is not None else torch.empty_like(q)
+        scales = scales if scales is not None else torch.empty_like(sc)
+        out.copy_(q)
+        scales.copy_(sc)
+        return out, scales
+
+    def modulate_to_e4m3(self, x, shift, scale, out=None, scales=None, eps=1e-6):
+        self.calls.append(("modulate", 1))
+        xf = x.float()
+        mu = xf.mean(-1, keepdim=True)
+        var = ((xf - mu) ** 2).mean(-1, keepdim=True)
+        calls = len(self.calls)
+        r = self.quantize_e4m3((xf - mu) * torch.rsqrt(var + eps) * (1 + scale) + shift, out, scales)
+        del self.calls[calls:]
+        return r
+
+    def gemm_fp8_group(self, problems):
+        assert 1 <= len(problems) <= 4
+        self.calls.append(("gemm_fp8_group", len(problems)))
+        return [self._gemm(self._deq(p["x"], p["x_scale"]), self._deq(p["w"], p["w_scale"]), p.get("bias"),
+                           p.get("out"), p.get("epilogue", "none"), p.get("gate")) for p in problems]
+
     def gemm_qkv_rope(self, problems, n_head, eps=1e-6):
         assert 1 <= len(problems) <= 4
         self.calls.append(("gemm_qkv_rope", len(problems)))
         for pr in problems:
-            y = pr["x"].float() @ pr["w"].float().t() + pr["bias"]
+            y = self._deq(pr["x"], pr.get("x_scale")) @ self._deq(pr["w"], pr.get("w_scale")).t() + pr["bias"]
             M = y.shape[0]
             qkv = 3 * n_head * blocks.DHEAD
             if pr.get("gelu_out") is not None:
@@ -157,3 +191,29 @@ def test_masks_per_half_are_checked():
 
 def test_cfg_flops_double():
     assert blocks.pass_flops(T, I, 1, 1, halves=2) == 2 * blocks.pass_flops(T, I, 1, 1)
+
+
+def test_fp8_cfg_pass_equals_each_half_alone(pass_inputs, monkeypatch):
+    """The FP8 pass (E4M3 weights, per-token E4M3 activations) over two stacked guidance
+    halves equals each half alone, and launches the FP8 layers as the bf16 pass does."""
+    pw, pe, masks, x0 = pass_inputs
+    fake = FakeEngine()
+    monkeypatch.setattr(blocks, "b2g", fake)
+    pw8 = blocks.quantize_pass(pw)
+    x = x0.clone()
+    blocks.forward_pass_fp8(pw8, x, pe, masks, blocks.ScratchFP8(T, I, "cpu", halves=2), T)
+    assert ("gemm_qkv_rope", 4) in fake.calls and ("gemm_fp8_group", 4) in fake.calls
+    # the 10 weights (4 per stream, 2 single), then one attention output, one MLP hidden state
+    # and one concat buffer per pass over both halves
+    assert sum(1 for c in fake.calls if c[0] == "quantize") == 10 + 3
+    for b in range(2):
+        y = x0[b * L:(b + 1) * L].clone()
+        blocks.forward_pass_fp8(pw8, y, pe, masks[b], blocks.ScratchFP8(T, I, "cpu"), T)
+        d = (x[b * L:(b + 1) * L] - y).abs().max() / y.abs().max()
+        assert d <= 1e-5, f"half {b}: {d:.3e}"
+    # close to the bf16 pass (E4M3 rounding of weights and activations)
+    z = x0.clone()
+    blocks.forward_pass(pw, z, pe, masks, blocks.PassScratch(T, I, "cpu", halves=2), T)
+    dz, dx = (z - x0).double(), (x - x0).double()
+    assert (dz - dx).abs().max() / dz.abs().max() < 0.2
+    assert float((dz * dx).sum() / (dz.norm() * dx.norm())) > 0.99

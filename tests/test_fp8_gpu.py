@@ -130,3 +130,45 @@ def test_gemm_fp8_rejects_bad_input(engine):
     xq, xs = engine.quantize_e4m3(x)
     with pytest.raises(engine.B2GError):
         engine.gemm_fp8(xq, wq, ws)                             # E4M3 activations without scales
+
+
+@pytest.mark.parametrize("variant", [-1, 2])
+@pytest.mark.parametrize("epilogue", ["none", "gated_residual"])
+def test_gemm_fp8_group_four_problems(engine, oracle, variant, epilogue):
+    """b2g_gemm_fp8_group: four E4M3 problems (0/1 and 2/3 share a weight, as the guidance
+    halves of one stream do) in one launch, against the oracle's exact-product GEMM."""
+    N, K = 640, 512
+    Ms = (64, 200, 130, 256)
+    ws_ = [fp8_operands(engine, 8, N, K, 90 + j)[4:] for j in range(2)]
+    bias = [seeded((N,), 95 + j, 0.02, torch.float32) for j in range(2)]
+    gate = seeded((N,), 97, 1.0, torch.float32) if epilogue == "gated_residual" else None
+    probs, wants = [], []
+    for i, M in enumerate(Ms):
+        xq, xs = engine.quantize_e4m3(seeded((M, K), 100 + i))
+        wq, wsc = ws_[i // 2]
+        out = seeded((M, N), 110 + i, 1.0, torch.float32)
+        y = oracle.gemm_fp8(xq.cpu().numpy(), xs.cpu().numpy(), wq.cpu().numpy(), wsc.cpu().numpy(),
+                            bias[i // 2].cpu().numpy())
+        if gate is not None:
+            y = out.double().cpu().numpy() + gate.double().cpu().numpy() * y
+        wants.append(y)
+        probs.append(dict(x=xq, x_scale=xs, w=wq, w_scale=wsc, bias=bias[i // 2], out=out, epilogue=epilogue,
+                          gate=gate))
+    engine.set_gemm_variant(variant, 0)
+    try:
+        n0 = engine.launch_count()
+        engine.gemm_fp8_group(probs)
+        torch.cuda.synchronize()
+        assert engine.launch_count() - n0 == 1
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    for pr, want in zip(probs, wants):
+        assert rel_err(pr["out"].cpu().numpy(), want) <= 1e-5
+    engine.check_device_error()
+
+
+def test_gemm_fp8_group_rejects_16bit_operands(engine):
+    x = seeded((8, 64), 1)
+    w = seeded((64, 64), 2)
+    with pytest.raises(engine.B2GError):
+        engine.gemm_fp8_group([dict(x=x, x_scale=torch.ones(8, device=DEV), w=w, w_scale=torch.ones(64, device=DEV))])

@@ -274,3 +274,60 @@ def test_gemm_qkv_rope_four_problems(engine, oracle):
     assert engine.launch_count() - n0 == 1
     for r0, m, want in wants:
         assert_bf16_of(buf[r0:r0 + m], want)
+
+
+def rope_oracle_from(oracle, y, pe, H, qn, kn):
+    """norm + rope on q and k of an already computed [M, 3*H*128] projection."""
+    HD = H * DH
+
+    def nr(a, sc):
+        a = np.ascontiguousarray(a)
+        if sc is not None:
+            a = oracle.rms_norm(a.reshape(-1, DH), sc.cpu().numpy()).reshape(a.shape)
+        return oracle.rope(a, pe, H)
+
+    return np.concatenate([nr(y[:, :HD], qn), nr(y[:, HD:2 * HD], kn), y[:, 2 * HD:]], 1)
+
+
+@pytest.mark.parametrize("tail,halves", [(False, 1), (True, 2)])
+def test_gemm_qkv_rope_fp8_vs_oracle(engine, oracle, tail, halves):
+    """The E4M3 form (config 5's qkv / linear1): per-token E4M3 x and per-channel E4M3 w, the
+    accumulator scaled by both before the bias, then norm + RoPE, against the oracle's
+    exact-product E4M3 GEMM on the same codes; with two problems in one launch, or one problem
+    with a GELU tail over two stacked guidance halves (pe_period)."""
+    H, K, L = 2, 320, 150
+    QKV = 3 * H * DH
+    MLPC = 256 if tail else 0
+    N = QKV + MLPC
+    pe = pe_table(L, DH, 41)
+    pe_d = torch.from_numpy(pe).to(DEV)
+    qn = (1 + 0.2 * seeded((DH,), 42, 1.0, torch.float32)).to(DEV)
+    kn = (1 + 0.2 * seeded((DH,), 43, 1.0, torch.float32)).to(DEV)
+    specs = [(halves * L, 0)] if tail else [(70, 0), (L - 70, 70)]
+    probs, wants = [], []
+    for i, (m, r0) in enumerate(specs):
+        x = seeded((m, K), 50 + i, 1.0, torch.float32).to(DEV)
+        w = seeded((N, K), 60 + i, 0.05).to(DEV)
+        b = seeded((N,), 70 + i, 0.05, torch.float32).to(DEV)
+        xq, xs = engine.quantize_e4m3(x)
+        wq, ws = engine.quantize_e4m3(w)
+        pr = dict(x=xq, x_scale=xs, w=wq, w_scale=ws, bias=b, q_norm=qn, k_norm=kn)
+        if tail:
+            pr.update(pe=pe_d, pe_period=L, gelu_out=torch.zeros((m, MLPC), dtype=torch.bfloat16, device=DEV))
+            rows_pe = np.concatenate([pe] * halves)
+        else:
+            pr.update(pe=pe_d[r0:r0 + m])
+            rows_pe = pe[r0:r0 + m]
+        y = oracle.gemm_fp8(xq.cpu().numpy(), xs.cpu().numpy(), wq.cpu().numpy(), ws.cpu().numpy(), b.cpu().numpy())
+        probs.append(pr)
+        wants.append((rope_oracle_from(oracle, np.ascontiguousarray(y[:, :QKV]), rows_pe, H, qn, kn),
+                      oracle.gelu(np.ascontiguousarray(y[:, QKV:])) if tail else None))
+    n0 = engine.launch_count()
+    outs = engine.gemm_qkv_rope(probs, H)
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 1
+    for pr, out, (want, want_tail) in zip(probs, outs, wants):
+        assert_bf16_of(out, want)
+        if tail:
+            assert_bf16_of(pr["gelu_out"], want_tail)
+    engine.check_device_error()
