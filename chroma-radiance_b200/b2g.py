@@ -119,6 +119,9 @@ _SIGNATURES = {
                                                                    ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_modulate_to_bf16": ([ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p],
                              ctypes.c_int),
+    "b2g_modulate_streams": ([ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int,
+                                                       ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+                                                       ctypes.c_void_p], ctypes.c_int),
     "b2g_modulate_to_e4m3": ([ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p],
                              ctypes.c_int),
     "b2g_attention_with_rope": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p,
@@ -642,3 +645,31 @@ def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None
     if not all(t.dtype == torch.float32 and t.is_contiguous() for t in (A, B, C)):
         raise B2GError("batched_matmul_Bt: contiguous F32 tensors expected")
     _check(lib.b2g_batched_matmul_Bt(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, K, N))
+
+
+def modulate_streams(x: torch.Tensor, txt_shift: torch.Tensor, txt_scale: torch.Tensor, img_shift: torch.Tensor,
+                     img_scale: torch.Tensor, seq: int, txt_rows: int, out: torch.Tensor | None = None,
+                     scales: torch.Tensor | None = None, fp8: bool = False, eps: float = 1e-6,
+                     stream: torch.cuda.Stream | None = None):
+    """Both streams of a double block in one launch (b2g_modulate_streams): x [M, C] F32 holds
+    whole sequences of `seq` rows, the first `txt_rows` of each modulated with the txt vectors,
+    the rest with the img vectors.  Returns bf16 [M, C], or (codes, row scales) with fp8."""
+    lib = load()
+    M, C = _modulate_args(x, txt_shift, txt_scale)
+    _modulate_args(x, img_shift, img_scale)
+    if fp8:
+        codes, rs = _q8_outputs(M, C, x.device, out, scales, "modulate_streams")
+        dst, dt, rsp = codes, E4M3, rs.data_ptr()
+    else:
+        codes = out if out is not None else torch.empty((M, C), dtype=torch.bfloat16, device=x.device)
+        _require_cuda(codes)
+        if codes.dtype != torch.bfloat16 or codes.shape != (M, C):
+            raise B2GError("modulate_streams: out must be bf16 [M, C]")
+        dst, dt, rsp, rs = codes, BF16, None, None
+    if not dst.is_contiguous():
+        raise B2GError("modulate_streams: out must be contiguous")
+    s = (stream or torch.cuda.current_stream(x.device)).cuda_stream
+    _check(lib.b2g_modulate_streams(x.data_ptr(), txt_shift.data_ptr(), txt_scale.data_ptr(), img_shift.data_ptr(),
+                                    img_scale.data_ptr(), seq, txt_rows, dst.data_ptr(), dt, rsp, M, C, eps,
+                                    ctypes.c_void_p(s)))
+    return (codes, rs) if fp8 else codes

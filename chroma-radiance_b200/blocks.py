@@ -256,7 +256,8 @@ def forward_pass(pw: PassWeights, x, pe, mask, s: PassScratch, T: int) -> None:
     F32 stream x [B*L, 3072] (B = x rows / pe rows guidance halves, half-major: half b's txt
     rows at [b*L, b*L + T), its img rows after them), then the single blocks on x, every block
     modulating its inputs on the device (modulate_to_bf16, kernels.cu:552-599) as the
-    reference's blocks do.  x is updated in place; txt and img are row views of it, so the
+    reference's blocks do (a double block's txt and img rows of all halves in one launch,
+    modulate_streams).  x is updated in place; txt and img are row views of it, so the
     double-to-single concatenation costs nothing.  mask: one [L] key bias for every half, or
     one per half ([B, L] or a list)."""
     L = pe.shape[0]
@@ -268,13 +269,10 @@ def forward_pass(pw: PassWeights, x, pe, mask, s: PassScratch, T: int) -> None:
     mod_i = [s.mod[b * L + T:(b + 1) * L] for b in range(B)]
     for i, (tw, iw) in enumerate(pw.double):
         mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
-        for b in range(B):
-            b2g.modulate_to_bf16(txts[b], mt[0], mt[1], out=mod_t[b])
-            b2g.modulate_to_bf16(imgs[b], mi[0], mi[1], out=mod_i[b])
+        # both streams of every half in one launch (each row as modulate_to_bf16 writes it)
+        b2g.modulate_streams(x, mt[0], mt[1], mi[0], mi[1], L, T, out=s.mod[:B * L])
         double_block_attention(tw, iw, mod_t, mod_i, txts, imgs, mt[2], mi[2], pe, mask, s)
-        for b in range(B):
-            b2g.modulate_to_bf16(txts[b], mt[3], mt[4], out=mod_t[b])
-            b2g.modulate_to_bf16(imgs[b], mi[3], mi[4], out=mod_i[b])
+        b2g.modulate_streams(x, mt[3], mt[4], mi[3], mi[4], L, T, out=s.mod[:B * L])
         double_block_mlp(tw, iw, mod_t, mod_i, txts, imgs, mt[5], mi[5], s)
     base = 12 * len(pw.double)
     for i, sw in enumerate(pw.single):
@@ -519,19 +517,15 @@ def forward_pass_fp8(pw: PassWeightsFP8, x, pe, mask, s: ScratchFP8, T: int) -> 
     def modulate(src, shift, scale, dst: Q8):
         b2g.modulate_to_e4m3(src, shift, scale, out=dst.q, scales=dst.s)
 
+    x8 = s.mod8.rows(0, B * L)
     for i, (tw, iw) in enumerate(pw.double):
         mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
-        for b in range(B):
-            modulate(txts[b], mt[0], mt[1], mod_t[b])
-            modulate(imgs[b], mi[0], mi[1], mod_i[b])
+        b2g.modulate_streams(x, mt[0], mt[1], mi[0], mi[1], L, T, out=x8.q, scales=x8.s, fp8=True)
         double_block_attention_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[2], mi[2], pe, mask, s)
-        for b in range(B):
-            modulate(txts[b], mt[3], mt[4], mod_t[b])
-            modulate(imgs[b], mi[3], mi[4], mod_i[b])
+        b2g.modulate_streams(x, mt[3], mt[4], mi[3], mi[4], L, T, out=x8.q, scales=x8.s, fp8=True)
         double_block_mlp_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[5], mi[5], s)
     base = 12 * len(pw.double)
     for i, sw in enumerate(pw.single):
         m = pw.mods[base + 3 * i:base + 3 * i + 3]
-        x8 = s.mod8.rows(0, B * L)
         modulate(x, m[0], m[1], x8)
         single_block_fp8(sw, x8, x, m[2], pe, mask, s)

@@ -632,6 +632,19 @@ b2g_status b2g_modulate_to_e4m3(const float* x, const float* shift, const float*
   return modulate_rows(x, shift, scale, out, B2G_E4M3, row_scale, M, C, eps, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_modulate_streams(const float* x, const float* txt_shift, const float* txt_scale,
+                                const float* img_shift, const float* img_scale, int64_t seq, int64_t txt_rows,
+                                void* out, b2g_dtype out_dtype, float* row_scale, int64_t M, int64_t C, float eps,
+                                void* stream) {
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  if (seq <= 0 || txt_rows < 0 || txt_rows > seq || M % seq != 0)
+    return set_error(B2G_ERR_INVALID, "b2g_modulate_streams: M must be whole sequences of seq >= txt_rows rows");
+  return modulate_rows(x, txt_shift, txt_scale, out, out_dtype, row_scale, M, C, eps,
+                       static_cast<cudaStream_t>(stream), img_shift, img_scale, seq, txt_rows);
+}
+
 b2g_status b2g_check_device_error(int* code) {
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);

@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(256) bias_gated_residual_kernel(const void* __
 // C <= 128 * 4 * NV): the row is read from memory once into registers (NV float4 per thread),
 // then mean, variance about the mean and the modulated output; the block sums go through
 // four warp shuffles and a 4-entry shared array.  OUT 0: bf16; 1: E4M3 with a per-row scale.
+// With period > 0, rows whose index modulo `period` is >= `split` take (shift2, scale2): the
+// img rows of a half-major [txt | img] stream (period = T + I, split = T), so one launch
+// modulates both streams of a double block for every guidance half.
 constexpr int kModThreads = 128;
 
 __device__ __forceinline__ float block_sum4(float v, float* red, int warp, int lane) {
@@ -80,7 +83,9 @@ template <int NV, int OUT>
 __global__ void __launch_bounds__(kModThreads) modulate_rows_kernel(const float* __restrict__ x,
                                                                     const float* __restrict__ shift,
                                                                     const float* __restrict__ scale,
-                                                                    void* __restrict__ out,
+                                                                    const float* __restrict__ shift2,
+                                                                    const float* __restrict__ scale2, int period,
+                                                                    int split, void* __restrict__ out,
                                                                     float* __restrict__ row_scale, int M, int C,
                                                                     float eps) {
   __shared__ float red[4];
@@ -88,6 +93,10 @@ __global__ void __launch_bounds__(kModThreads) modulate_rows_kernel(const float*
   griddep_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long row = blockIdx.x;
+  if (period > 0 && static_cast<int>(row % period) >= split) {
+    shift = shift2;
+    scale = scale2;
+  }
   const float4* xr = reinterpret_cast<const float4*>(x + row * C);
   const int nv4 = C >> 2;
   float4 v[NV];
@@ -153,36 +162,44 @@ __global__ void __launch_bounds__(kModThreads) modulate_rows_kernel(const float*
 }
 
 template <int OUT>
-b2g_status launch_modulate(const float* x, const float* shift, const float* scale, void* out, float* row_scale,
-                           int64_t M, int64_t C, float eps, cudaStream_t st) {
+b2g_status launch_modulate(const float* x, const float* shift, const float* scale, const float* shift2,
+                           const float* scale2, int period, int split, void* out, float* row_scale, int64_t M,
+                           int64_t C, float eps, cudaStream_t st) {
   const unsigned grid = static_cast<unsigned>(M);
   const int nv = static_cast<int>((C / 4 + kModThreads - 1) / kModThreads);
   const int m = static_cast<int>(M), c = static_cast<int>(C);
   auto kern = nv <= 2 ? modulate_rows_kernel<2, OUT>
               : nv <= 4 ? modulate_rows_kernel<4, OUT>
               : nv <= 6 ? modulate_rows_kernel<6, OUT> : modulate_rows_kernel<8, OUT>;
-  return launch_pdl(kern, dim3(grid), dim3(kModThreads), 0, st, "modulate launch", x, shift, scale, out, row_scale, m,
-                    c, eps);
+  return launch_pdl(kern, dim3(grid), dim3(kModThreads), 0, st, "modulate launch", x, shift, scale, shift2, scale2,
+                    period, split, out, row_scale, m, c, eps);
 }
 
 }  // namespace
 
 b2g_status modulate_rows(const float* x, const float* shift, const float* scale, void* out, b2g_dtype out_dtype,
-                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st) {
+                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st, const float* shift2,
+                         const float* scale2, int64_t period, int64_t split) {
   if (M < 0 || C < 0) return set_error(B2G_ERR_INVALID, "modulate: negative size");
   if (M == 0 || C == 0) return B2G_OK;
   if (!x || !shift || !scale || !out) return set_error(B2G_ERR_INVALID, "modulate: null pointer");
+  if (period < 0 || period > (1ll << 30) || (period > 0 && (split < 0 || split > period || !shift2 || !scale2)))
+    return set_error(B2G_ERR_INVALID, "modulate: second parameter set needs 0 <= split <= period and its vectors");
+  if (period == 0) shift2 = shift, scale2 = scale;
   if (out_dtype != B2G_BF16 && out_dtype != B2G_E4M3) return set_error(B2G_ERR_UNSUPPORTED, "modulate: bf16 or E4M3 out");
   if (out_dtype == B2G_E4M3 && !row_scale) return set_error(B2G_ERR_INVALID, "modulate: E4M3 needs row scales");
   if (C % 4 != 0 || C > 4096 || M > (1ll << 31) - 1)
     return set_error(B2G_ERR_UNSUPPORTED, "modulate: C must be a multiple of 4 and at most 4096");
   const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(shift) |
-                         reinterpret_cast<uintptr_t>(scale);
+                         reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(shift2) |
+                         reinterpret_cast<uintptr_t>(scale2);
   const uintptr_t obits = reinterpret_cast<uintptr_t>(out);
   if ((bits & 15u) || (obits & (out_dtype == B2G_BF16 ? 7u : 3u)))
     return set_error(B2G_ERR_UNSUPPORTED, "modulate: x, shift, scale 16-byte and out 8/4-byte aligned");
-  if (out_dtype == B2G_BF16) return launch_modulate<0>(x, shift, scale, out, nullptr, M, C, eps, st);
-  return launch_modulate<1>(x, shift, scale, out, row_scale, M, C, eps, st);
+  const int per = static_cast<int>(period), spl = static_cast<int>(split);
+  if (out_dtype == B2G_BF16)
+    return launch_modulate<0>(x, shift, scale, shift2, scale2, per, spl, out, nullptr, M, C, eps, st);
+  return launch_modulate<1>(x, shift, scale, shift2, scale2, per, spl, out, row_scale, M, C, eps, st);
 }
 
 b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias, const float* gate,

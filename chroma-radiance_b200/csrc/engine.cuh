@@ -178,9 +178,12 @@ struct AttnBf16Args {
 b2g_status attention_bf16(const AttnBf16Args& a, cudaStream_t st);
 
 // out = LN(x) * (1 + scale) + shift per row of x [M, C] F32 (no-affine LayerNorm, two-pass
-// statistics), written as bf16 or as per-row E4M3 with row_scale[M] (absmax / 448).
+// statistics), written as bf16 or as per-row E4M3 with row_scale[M] (absmax / 448).  With
+// period > 0, rows r with r % period >= split use (shift2, scale2) instead.
 b2g_status modulate_rows(const float* x, const float* shift, const float* scale, void* out, b2g_dtype out_dtype,
-                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st);
+                         float* row_scale, int64_t M, int64_t C, float eps, cudaStream_t st,
+                         const float* shift2 = nullptr, const float* scale2 = nullptr, int64_t period = 0,
+                         int64_t split = 0);
 // Contiguous F32 [L, H*D] form of the above (no norm), the reference's attention_with_rope.
 b2g_status attention_rope(const float* q, const float* k, const float* v, const float* pe, const float* key_bias,
                           float* out, int64_t L, int64_t H, int64_t D, cudaStream_t st);

@@ -295,6 +295,18 @@ b2g_status b2g_modulate_to_bf16(const float* x, const float* shift, const float*
 b2g_status b2g_modulate_to_e4m3(const float* x, const float* shift, const float* scale, uint8_t* out,
                                 float* row_scale, int64_t M, int64_t C, float eps, void* stream);
 
+/* Both streams of a double block modulated in one launch.  The reference modulates each
+ * stream with its own vectors (modulate_to_bf16_cuda on txt and on img, chroma.cuh:824, 835,
+ * 920, 955; with guidance each stream holds both halves' rows).  Here x [M, C] is the F32 stream
+ * in the half-major layout: whole sequences of `seq` rows, the first txt_rows of each being
+ * text tokens (txt_shift / txt_scale) and the rest image tokens (img_shift / img_scale).  out
+ * bf16 (out_dtype B2G_BF16, row_scale NULL) or per-row E4M3 (B2G_E4M3, row_scale [M]), each row
+ * as b2g_modulate_to_bf16 / b2g_modulate_to_e4m3 writes it.  M % seq == 0. */
+b2g_status b2g_modulate_streams(const float* x, const float* txt_shift, const float* txt_scale,
+                                const float* img_shift, const float* img_scale, int64_t seq, int64_t txt_rows,
+                                void* out, b2g_dtype out_dtype, float* row_scale, int64_t M, int64_t C, float eps,
+                                void* stream);
+
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).
  * Synchronises the device.  Returns B2G_OK or B2G_ERR_DEVICE_TIMEOUT; *code gets the

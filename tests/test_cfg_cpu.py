@@ -117,6 +117,24 @@ class FakeEngine:
         out.copy_(o.to(out.dtype))
         return out
 
+    def modulate_streams(self, x, txt_shift, txt_scale, img_shift, img_scale, seq, txt_rows, out=None,
+                         scales=None, fp8=False, eps=1e-6):
+        self.calls.append(("modulate", 1))
+        img = ((torch.arange(x.shape[0]) % seq) >= txt_rows)[:, None]
+        shift = torch.where(img, img_shift, txt_shift)
+        scale = torch.where(img, img_scale, txt_scale)
+        xf = x.float()
+        mu = xf.mean(-1, keepdim=True)
+        var = ((xf - mu) ** 2).mean(-1, keepdim=True)
+        y = (xf - mu) * torch.rsqrt(var + eps) * (1 + scale) + shift
+        if fp8:
+            calls = len(self.calls)
+            r = self.quantize_e4m3(y, out, scales)
+            del self.calls[calls:]
+            return r
+        out.copy_(y.to(torch.bfloat16))
+        return out
+
     def modulate_to_bf16(self, x, shift, scale, out=None, eps=1e-6):
         self.calls.append(("modulate", 1))
         xf = x.float()

@@ -80,3 +80,32 @@ def test_modulate_rejects_unsupported(engine):
     v = torch.zeros(6, device=DEV)
     with pytest.raises(engine.B2GError):
         engine.modulate_to_bf16(x, v, v)  # C % 4 != 0
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_modulate_streams_equals_per_stream_calls(engine, fp8):
+    """b2g_modulate_streams over two half-major sequences of [txt | img] rows gives, row for
+    row, the same bits as modulate_to_bf16 / modulate_to_e4m3 on each stream's rows with that
+    stream's vectors."""
+    T, I, C = 40, 88, 3072
+    L = T + I
+    g = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn((2 * L, C), generator=g, device=DEV) * 3 + 0.5
+    vec = [torch.randn(C, generator=g, device=DEV) * 0.3 for _ in range(4)]
+    got = engine.modulate_streams(x, vec[0], vec[1], vec[2], vec[3], L, T, fp8=fp8)
+    torch.cuda.synchronize()
+    one = engine.modulate_to_e4m3 if fp8 else engine.modulate_to_bf16
+    for b in range(2):
+        for r0, r1, sh, sc in ((b * L, b * L + T, vec[0], vec[1]), (b * L + T, (b + 1) * L, vec[2], vec[3])):
+            want = one(x[r0:r1].contiguous(), sh, sc)
+            if fp8:
+                assert torch.equal(got[0][r0:r1], want[0]) and torch.equal(got[1][r0:r1], want[1])
+            else:
+                assert torch.equal(got[r0:r1], want)
+
+
+def test_modulate_streams_rejects_partial_sequences(engine):
+    x = torch.zeros((100, 64), device=DEV)
+    v = torch.zeros(64, device=DEV)
+    with pytest.raises(engine.B2GError):
+        engine.modulate_streams(x, v, v, v, v, 64, 10)      # 100 rows are not whole sequences of 64
