@@ -273,6 +273,33 @@ b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream) {
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Problems that read the same F32 activations against 16-bit weights (the T5 layer's q, k,
+  // v and its wi_0, wi_1 linears, t5.cuh:233-275, each of which linear() casts on its own) share
+  // one cast into the workspace, then run as 16-bit problems.
+  bool shared_cast = n >= 2 && n <= kMaxGemmGroups && ps[0].a_dtype == B2G_F32 && ps[0].K > 0 &&
+                     (ps[0].b_dtype == B2G_BF16 || ps[0].b_dtype == B2G_F16) && ps[0].batch == 1;
+  for (int i = 1; shared_cast && i < n; ++i)
+    shared_cast = ps[i].a == ps[0].a && ps[i].a_dtype == B2G_F32 && ps[i].lda == ps[0].lda && ps[i].M == ps[0].M &&
+                  ps[i].K == ps[0].K && ps[i].b_dtype == ps[0].b_dtype && ps[i].batch == 1;
+  if (shared_cast) {
+    const int64_t kp = round_up(ps[0].K, 8);
+    void* ws = nullptr;
+    if ((s = workspace_get(static_cast<size_t>(ps[0].M * kp) * 2, &ws)) != B2G_OK) return s;
+    if ((s = cast_f32_to_16(static_cast<const float*>(ps[0].a), ws, ps[0].b_dtype, 1, ps[0].M, ps[0].K, ps[0].lda,
+                            0, kp, ps[0].M * kp, st)) != B2G_OK)
+      return s;
+    for (int i = 0; i < n; ++i) {
+      ps[i].a = ws;
+      ps[i].a_dtype = ps[0].b_dtype;
+      ps[i].lda = kp;
+    }
+    bool one = true;
+    for (int i = 0; one && i < n; ++i) one = tc_gemm_supported(ps[i], nullptr) && tc_gemm_groupable(ps[0], ps[i]);
+    if (one) return tc_gemm_launch_group(ps, n, st);
+    for (int i = 0; i < n; ++i)
+      if ((s = run_gemm(ps[i], st)) != B2G_OK) return s;
+    return B2G_OK;
+  }
   // One launch when the (two to four) non-empty problems run on the tensor cores without an
   // activation cast and agree on everything but M and their pointers; otherwise one GEMM
   // after the other on the stream.

@@ -400,6 +400,27 @@ def test_gemm_group_five_problems_run_one_by_one(engine):
         check(o, fp32_ref(x, w))
 
 
+def test_gemm_group_shares_the_activation_cast(engine):
+    """Problems on one F32 input against fp16 weights (the T5 layer's q, k, v) cast it once and
+    run as one launch; with different epilogues (wi_0 GELU, wi_1 none) the cast is still shared.
+    Results equal each problem run alone (same fp16 operands)."""
+    x = seeded((200, 512), 1, 1.0, torch.float32)
+    ws = [seeded((384, 512), 2 + i, 0.02, torch.float16) for i in range(3)]
+    alone = [engine.gemm(x, w) for w in ws]
+    n0 = engine.launch_count()
+    grouped = engine.gemm_group([dict(x=x, w=w) for w in ws])
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 2            # one cast + one GEMM launch
+    for a, b in zip(alone, grouped):
+        assert rel_err(b.cpu().numpy(), a.cpu().numpy()) <= 1e-6
+    n0 = engine.launch_count()
+    g2 = engine.gemm_group([dict(x=x, w=ws[0], epilogue="gelu"), dict(x=x, w=ws[1])])
+    torch.cuda.synchronize()
+    assert engine.launch_count() - n0 == 3            # one cast + two GEMM launches
+    assert rel_err(g2[1].cpu().numpy(), alone[1].cpu().numpy()) <= 1e-6
+    check(g2[0], gelu_t(fp32_ref(x.to(torch.float16), ws[0])))
+
+
 def test_gemm_group_split_k(engine):
     engine.set_gemm_variant(2, 3)
     try:
