@@ -991,7 +991,8 @@ def run_engine_config5(args) -> None:
                    "l2": "E4M3 weights 340 MB > L2; 256 MB buffer written before every step, outside the events",
                    "execution": "one CUDA graph per step"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
-                     "frac": round(achieved / fp8_peak, 4), "traffic": None,
+                     "frac": round(achieved / fp8_peak, 4),
+                     "traffic": profile_traffic("fp8_block_pair_config5_launches.md"),
                      "peak_source": "derived: 2 x " + peaks["source"] + " bf16 burst (kind::f8f6f4 issues twice the "
                                     "bf16 rate; no FP8 figure is measured)",
                      "kernel": "tc_gemm E4M3: the block pair's 6 linear-layer launches, FLOP-weighted",
