@@ -1016,13 +1016,193 @@ def run_engine_config5(args) -> None:
         torch.distributed.destroy_process_group()
 
 
+NERF_P, NERF_S, NERF_HID, NERF_MLP, NERF_COND = 1024, 256, 64, 256, 3072
+NERF_PARAMS = 3 * NERF_HID * NERF_MLP  # 49152 param_gen outputs per patch: w_gate, w_value, w_fc2
+WORKLOAD_NERF = ("nerf: the GEMMs of one NeRF decoder GLU block at 512^2 (nerf_glu_block, chroma.cuh:1253-1302), "
+                 "P=1024 patches x 256 pixels x 64 channels: param_gen linear F32 s [1024, 3072] x bf16 W "
+                 "[49152, 3072]^T + F32 bias -> F32 params (linear(): activations rounded to bf16), then "
+                 "batched_matmul_Bt x3 (x [P,256,64] . w_gate/w_value [P,256,64]^T -> [P,256,256]; h [P,256,256] "
+                 ". w_fc2 [P,64,256]^T -> [P,256,64], F32, operands rounded as cuBLAS's FAST_16BF mode does)")
+
+
+def nerf_inputs(torch, dev):
+    """Seeded inputs of one NeRF GLU block's GEMMs (weights ~N(0, 0.02), activations ~N(0, 1))."""
+    g = torch.Generator(device=dev).manual_seed(7)
+    P, S, D, F = NERF_P, NERF_S, NERF_HID, NERF_MLP
+    t = {"s": torch.randn((P, NERF_COND), generator=g, device=dev),
+         "w": (torch.randn((NERF_PARAMS, NERF_COND), generator=g, device=dev) * 0.02).to(torch.bfloat16),
+         "b": torch.randn(NERF_PARAMS, generator=g, device=dev) * 0.02,
+         "x": torch.randn((P, S, D), generator=g, device=dev),
+         "wg": torch.randn((P, F, D), generator=g, device=dev) * 0.125,
+         "wv": torch.randn((P, F, D), generator=g, device=dev) * 0.125,
+         "w2": torch.randn((P, D, F), generator=g, device=dev) * 0.0625}
+    t["params"] = torch.empty((P, NERF_PARAMS), device=dev)
+    t["x1"] = torch.empty((P, S, F), device=dev)
+    t["x2"] = torch.empty((P, S, F), device=dev)
+    t["out"] = torch.empty((P, S, D), device=dev)
+    return t
+
+
+def nerf_flops() -> dict:
+    P, S, D, F = NERF_P, NERF_S, NERF_HID, NERF_MLP
+    return {"param_gen": 2.0 * P * NERF_PARAMS * NERF_COND, "gate": 2.0 * P * S * F * D, "value": 2.0 * P * S * F * D,
+            "fc2": 2.0 * P * S * D * F}
+
+
+def nerf_step_ops(t, linear, bmm) -> list:
+    """The four GEMMs of the block, as (label, callable) in the reference's order."""
+    P, S, D, F = NERF_P, NERF_S, NERF_HID, NERF_MLP
+    return [("param_gen", lambda: linear(t["s"], t["w"], t["b"], t["params"])),
+            ("gate", lambda: bmm(t["x"], t["wg"], t["x1"])),
+            ("value", lambda: bmm(t["x"], t["wv"], t["x2"])),
+            ("fc2", lambda: bmm(t["x1"], t["w2"], t["out"]))]
+
+
+def time_ops(torch, ops, steps, warmup, flush, graph: bool) -> tuple[float, dict]:
+    """Mean ms of the whole step (the ops in order) and of each op alone, CUDA events on the
+    current stream, L2 flushed before every timed step; graph=True replays CUDA graphs."""
+    def runner(fns):
+        if not graph:
+            return lambda: [f() for f in fns]
+        g = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                for f in fns:
+                    f()
+        return g.replay
+
+    def timed(run, n):
+        for _ in range(warmup):
+            run()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for i in range(n):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            run()
+            b.record()
+            b.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / n
+
+    fns = [f for _, f in ops]
+    for f in fns:
+        f()  # sizes any workspace before capture
+    torch.cuda.synchronize()
+    step = timed(runner(fns), steps)
+    per = {lab: timed(runner([f]), max(3, steps // 4)) for lab, f in ops}
+    return step, per
+
+
+def nerf_line(impl, args, step_ms, per_ms, extra) -> dict:
+    fl = nerf_flops()
+    total = sum(fl.values())
+    line = {"metric": METRIC, "value": round(total / (step_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (param_gen), tf32-rounded f32 (batched)",
+            "data": "synthetic (torch Philox generator, seed 7)",
+            "config": {"workload": WORKLOAD_NERF, "flop_per_step": total,
+                       "l2": "256 MB buffer written before every step, outside the events"},
+            "breakdown_us": {k: round(v * 1e3, 1) for k, v in per_ms.items()},
+            "breakdown_tflops": {k: round(fl[k] / (per_ms[k] * 1e-3) / 1e12, 1) for k in per_ms}}
+    if impl == "reference":
+        line["impl"] = "reference"
+    line.update(extra)
+    return line
+
+
+def run_engine_nerf(args) -> None:
+    import torch
+
+    import b2g
+
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b2g.init()
+    t = nerf_inputs(torch, dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    ops = nerf_step_ops(t, b2g.linear, b2g.batched_matmul_Bt)
+    n0 = b2g.launch_count()
+    for _, f in ops:
+        f()
+    launches = b2g.launch_count() - n0
+    # Eager on stream 0, as the reference arm: linear() and batched_matmul_Bt mirror the
+    # reference's stream-0 calls.
+    with ClockSampler(local) as clk:
+        step_ms, per = time_ops(torch, ops, args.steps, args.warmup, flush, graph=False)
+    b2g.check_device_error()
+    peaks = measured_peaks()
+    fl = nerf_flops()
+    ach = fl["param_gen"] / (per["param_gen"] * 1e-3) / 1e12
+    # End to end: s copied in from pinned host memory and the block's output copied back.
+    s_h = t["s"].cpu().pin_memory()
+    out_h = torch.empty(t["out"].shape).pin_memory()
+    ops_e2e = [("in", lambda: t["s"].copy_(s_h, non_blocking=True))] + ops + \
+              [("out", lambda: out_h.copy_(t["out"], non_blocking=True))]
+    e2e_ms, _ = time_ops(torch, ops_e2e, max(3, args.steps // 2), args.warmup, flush, graph=False)
+    line = nerf_line("b2g", args, step_ms, per, {
+        "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": None,
+                     "peak_source": peaks["source"] + " (burst bf16)",
+                     "kernel": "tc_gemm: the param_gen linear (92% of the step's FLOPs)"},
+        "e2e": {"value": round(sum(fl.values()) / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": s_h.numel() * 4, "d2h_bytes_per_step": out_h.numel() * 4,
+                "ms_per_step": round(e2e_ms, 4)},
+        "clocks": clk.summary(), "gpu_launches": int(launches * args.steps)})
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_nerf(args) -> None:
+    """The reference's own linear() and batched_matmul_Bt (cuBLASLt / cuBLAS, built from its
+    sources into oracle/_ref) on the same inputs, eager on stream 0 as the reference runs them."""
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    import oracle as oracle_mod
+    import torch
+
+    if not oracle_mod.REF_PATH.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_cublaslt.so was not built "
+                          "(the reference sources were absent at build time)"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ref = oracle_mod.Ref()
+    t = nerf_inputs(torch, dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def linear(x, w, b, out):
+        ref.linear(x.data_ptr(), 0, w.data_ptr(), 2, b.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1], w.shape[0])
+
+    def bmm(a, b, c):
+        ref.batched_matmul_Bt(a.data_ptr(), b.data_ptr(), c.data_ptr(), a.shape[0], a.shape[1], a.shape[2], b.shape[1])
+
+    ops = nerf_step_ops(t, linear, bmm)
+    with ClockSampler(local) as clk:
+        step_ms, per = time_ops(torch, ops, args.steps, args.warmup, flush, graph=False)
+    line = nerf_line("reference", args, step_ms, per, {
+        "cpu_baseline": {"kind": "reference", "cores": 0, "value": round(sum(nerf_flops().values()) /
+                                                                         (step_ms * 1e-3) / 1e12, 2),
+                         "unit": "TFLOP/s", "sample": "the reference has no CPU path; this arm is its own linear() "
+                                                      "and batched_matmul_Bt (cublas_ops.cuh:359, 558) on the B200"},
+        "e2e": {"value": round(sum(nerf_flops().values()) / (step_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "clocks": clk.summary(), "cublaslt_version": int(ref.cublaslt_version())})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100 for config2, 200 config1)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
-    ap.add_argument("--workload", choices=["config2", "config1", "config4", "config5"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config1", "config4", "config5", "nerf"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",
                     help="config4: reduction of the row-split layers (fused into the GEMM, or NCCL)")
@@ -1030,10 +1210,11 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = {"config2": 100, "config1": 200, "config4": 30, "config5": 100}[args.workload]
+        args.steps = {"config2": 100, "config1": 200, "config4": 30, "config5": 100, "nerf": 40}[args.workload]
     fn = {("b2g", "config1"): run_engine_config1, ("reference", "config1"): run_reference_config1,
           ("b2g", "config2"): run_engine_config2, ("reference", "config2"): run_reference_config2,
           ("b2g", "config4"): run_engine_config4, ("b2g", "config5"): run_engine_config5,
+          ("b2g", "nerf"): run_engine_nerf, ("reference", "nerf"): run_reference_nerf,
           ("reference", "config5"): lambda a: print(json.dumps({
               "impl": "reference", "unavailable": "the reference has no FP8 path (its quantised linears are INT8, "
                                                   "cublas_ops.cuh:294-791); its bf16 block code is the config2 "

@@ -514,7 +514,21 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
   // CUBLAS_COMPUTE_32F_FAST_16BF as cuBLAS runs it on B200: operands rounded to TF32 (round
-  // to nearest even), TF32 products, fp32 accumulation -> kind::tf32 tensor-core MMAs.
+  // to nearest even), TF32 products, fp32 accumulation -> kind::tf32 tensor-core MMAs.  With
+  // 16-byte operand rows (K % 4 == 0, aligned bases) the operands go to the kernel as they are
+  // and it rounds each shared-memory stage; otherwise a pass rounds them into padded copies.
+  cudaStream_t st = nullptr;
+  GemmProblem p;
+  p.M = M; p.N = N; p.K = K; p.batch = batch;
+  p.d = C; p.d_dtype = B2G_F32; p.ldd = N; p.d_bstride = M * N;
+  p.allow_tf32 = true;
+  p.a_dtype = p.b_dtype = B2G_F32;
+  if (K > 0 && K % 4 == 0 && (reinterpret_cast<uintptr_t>(A) & 15u) == 0 && (reinterpret_cast<uintptr_t>(B) & 15u) == 0) {
+    p.a = A; p.lda = K; p.a_bstride = M * K;
+    p.b = B; p.ldb = K; p.b_bstride = N * K;
+    p.round_tf32 = true;
+    return run_gemm(p, st);
+  }
   const int64_t kp = round_up(K > 0 ? K : 1, 4);  // 16-byte rows for TMA
   const size_t a_bytes = static_cast<size_t>(round_up(batch * M * kp * 4, 256));
   const size_t b_bytes = static_cast<size_t>(batch * N * kp * 4);
@@ -522,15 +536,10 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64
   if ((s = workspace_get(a_bytes + b_bytes, &ws)) != B2G_OK) return s;
   void* wa = ws;
   void* wb = static_cast<char*>(ws) + a_bytes;
-  cudaStream_t st = nullptr;
   if ((s = cast_f32_to_16(A, wa, B2G_F32, batch, M, K, K, M * K, kp, M * kp, st)) != B2G_OK) return s;
   if ((s = cast_f32_to_16(B, wb, B2G_F32, batch, N, K, K, N * K, kp, N * kp, st)) != B2G_OK) return s;
-  GemmProblem p;
-  p.M = M; p.N = N; p.K = K; p.batch = batch;
-  p.a = wa; p.a_dtype = B2G_F32; p.lda = kp; p.a_bstride = M * kp;
-  p.b = wb; p.b_dtype = B2G_F32; p.ldb = kp; p.b_bstride = N * kp;
-  p.d = C; p.d_dtype = B2G_F32; p.ldd = N; p.d_bstride = M * N;
-  p.allow_tf32 = true;
+  p.a = wa; p.lda = kp; p.a_bstride = M * kp;
+  p.b = wb; p.ldb = kp; p.b_bstride = N * kp;
   return run_gemm(p, st);
 }
 

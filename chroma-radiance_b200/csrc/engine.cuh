@@ -24,6 +24,8 @@ struct GemmProblem {
   b2g_epilogue epilogue = B2G_EPI_NONE;
   const float* gate = nullptr;
   bool allow_tf32 = false;  // F32 x F32 may run as TF32 products (batched_matmul_Bt only)
+  bool round_tf32 = false;  // TF32 operands still plain fp32: the kernel rounds each shared-memory
+                            // stage to nearest TF32 before the MMAs read it (1-CTA kernels)
   float alpha = 1.0f;       // D = epilogue(alpha * A.B^T + bias); internal (attention scores)
   bool allow_split = true;  // false: never split K (split-K needs workspace; b2g_gemm_noalloc)
   // E4M3 operands: D = (sum_k A.B) * a_scale[m] * b_scale[n] + bias, before the epilogue.

@@ -9,6 +9,7 @@
 #include <cuda_fp16.h>
 #include <type_traits>
 #include "engine.cuh"
+#include "ptx_sm100.cuh"
 
 namespace b2g {
 
@@ -95,19 +96,6 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
       }
     }
   }
-}
-
-// fp32 -> fp32 rounded to TF32 precision (10 explicit mantissa bits), round to nearest even;
-// Inf/NaN pass through.  This is the operand rounding cuBLAS applies in the reference's
-// batched_matmul_Bt (CUBLAS_COMPUTE_32F_FAST_16BF runs as TF32 on B200; verified against the
-// reference's own outputs to 2e-7).
-__device__ __forceinline__ float round_tf32(float v) {
-  uint32_t u = __float_as_uint(v);
-  if ((u & 0x7F800000u) != 0x7F800000u) {
-    u += 0xFFFu + ((u >> 13) & 1u);
-    u &= 0xFFFFE000u;
-  }
-  return __uint_as_float(u);
 }
 
 // F32 -> bf16/fp16 copy with round-to-nearest-even, as f32_to_bf16_kernel /

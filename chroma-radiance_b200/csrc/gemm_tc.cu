@@ -117,6 +117,7 @@ struct TcParams {
   int split;               // kEpiQkvRope with a GELU tail: columns >= split (= 3 * hd) are bias +
                            // GELU, stored through the tensor map after the group's (0: no tail)
   float eps;               // kEpiQkvRope: RMSNorm epsilon
+  int round_tf32;          // kind::tf32: round each landed stage to TF32 in shared memory first
   TcGroup g[kMaxGroups];
 };
 
@@ -158,6 +159,21 @@ __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi
   r -= g * group_size;
   mb = first_m + r % gm;
   nb = r / gm;
+}
+
+// Rounds one shared-memory operand stage (bytes a multiple of 512) to TF32 in place, the 32
+// lanes of a warp striding over it in 16-byte words; the values' positions (swizzle) are
+// irrelevant to an elementwise rounding.
+__device__ __forceinline__ void round_stage_tf32(uint8_t* stage, uint32_t bytes, int lane) {
+  float4* q = reinterpret_cast<float4*>(stage);
+  for (uint32_t i = lane; i < bytes / 16; i += 32) {
+    float4 v = q[i];
+    v.x = round_tf32_cvt(v.x);
+    v.y = round_tf32_cvt(v.y);
+    v.z = round_tf32_cvt(v.z);
+    v.w = round_tf32_cvt(v.w);
+    q[i] = v;
+  }
 }
 
 // Work item -> (tile, split, k-block range).  Items are split-major so the CTAs running at
@@ -832,7 +848,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    bool round_stages = false;
+    if constexpr (KIND == 1) round_stages = p.round_tf32 != 0;
+    if (round_stages) {
+      // kind::tf32 on operands that are still plain fp32 (batched_matmul_Bt): the whole warp
+      // rounds every landed stage to nearest TF32 in place, makes its shared-memory writes
+      // visible to the tensor core (proxy fence), and lane 0 then issues the stage's MMAs.
+      // This replaces a rounding pass over both operands in global memory.
+      int stage = 0;
+      uint32_t phase = 0, local = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x, ++local) {
+        int tile, split, kb0, kb1;
+        item_coords(item, p, tile, split, kb0, kb1);
+        const uint32_t acc = local & 1u;
+        const uint32_t acc_phase = (local >> 1) & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kErrWaitMma));
+        if (!ok) break;
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma));
+          if (!ok) break;
+          round_stage_tf32(sA + stage * A_BYTES, A_BYTES, lane);
+          round_stage_tf32(sB + stage * B_BYTES, B_BYTES, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tc_fence_after();
+            const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
+            const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
+              umma_tf32(d_tmem, ad, bd, p.idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            }
+            umma_commit(&empty_bar[stage]);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok && lane == 0) umma_commit(&tfull_bar[acc]);
+      }
+      if (!ok && lane == 0) {
+        umma_commit(drain_bar);
+        mbar_wait_drain(drain_bar, 0);
+      }
+    } else if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0, local = 0;
       bool ok = true;
@@ -1348,6 +1412,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     if (cand == VPAIR && !g_allow_pair) continue;
     if (cand != V128 && p.N <= 128) continue;
     if (cand == V128 && p.rope) continue;  // the rope epilogue needs a whole head per thread
+    if (cand == VPAIR && p.round_tf32) continue;  // in-kernel TF32 rounding: 1-CTA kernels only
     const long long tm = cand == VPAIR ? 256 : 128, tn = cand == V128 ? 128 : 256;
     long long tiles = 0;
     for (int i = 0; i < count; ++i) tiles += ps[i].batch * ((ps[i].M + tm - 1) / tm) * ((p.N + tn - 1) / tn);
@@ -1372,6 +1437,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
   if (nkb == 0 || !p.allow_split || p.tp || p.rope) splits = 1;
   if (p.rope && v == V128) v = g_allow_pair ? VPAIR : V256;
+  if (p.round_tf32 && v == VPAIR) v = V256;
   const bool pair = v == VPAIR;
   const int bn = v == V128 ? 128 : 256;
   const int tile_m = pair ? 256 : kBM;
@@ -1418,6 +1484,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   prm.d_bstride = p.batch > 1 ? p.d_bstride : 0;
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.alpha = p.alpha;
+  prm.round_tf32 = (kind == 1 && p.round_tf32) ? 1 : 0;
   prm.err = dev->err_word;
   prm.idesc = idesc_make(kind == 1 ? kFmtTF32 : (kind == 2 ? kFmtE4M3 : (p.a_dtype == B2G_BF16 ? kFmtBF16 : kFmtF16)),
                          tile_m, bn);

@@ -18,6 +18,28 @@ enum : int {
 // Upper bound on any single pipeline wait.  Legitimate waits are micro- to milliseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// fp32 -> fp32 rounded to TF32 precision (10 explicit mantissa bits), round to nearest even;
+// Inf/NaN pass through.  This is the operand rounding cuBLAS applies in the reference's
+// batched_matmul_Bt (CUBLAS_COMPUTE_32F_FAST_16BF runs as TF32 on B200; verified against the
+// reference's own outputs to 2e-7), and the hi/lo split of the T5 attention's operands.
+__device__ __forceinline__ float round_tf32(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u & 0x7F800000u) != 0x7F800000u) {
+    u += 0xFFFu + ((u >> 13) & 1u);
+    u &= 0xFFFFE000u;
+  }
+  return __uint_as_float(u);
+}
+
+// The same rounding in one instruction (cvt.rn.tf32.f32: round to nearest even, the result
+// an fp32 bit pattern whose 13 low mantissa bits are zero); equal to round_tf32 for every
+// non-NaN fp32 input.
+__device__ __forceinline__ float round_tf32_cvt(float v) {
+  uint32_t r;
+  asm("cvt.rn.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

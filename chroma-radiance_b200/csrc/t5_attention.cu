@@ -19,21 +19,12 @@
 //   5. GEMM (kind::tf32, batch H)   out[:, h*D:(h+1)*D] = P_h Vt_h^T.
 #include <cstdint>
 #include "engine.cuh"
+#include "ptx_sm100.cuh"
 
 namespace b2g {
 
 namespace {
 
-// fp32 -> fp32 holding a TF32 value (10 explicit mantissa bits), round to nearest even;
-// Inf/NaN pass through.
-__device__ __forceinline__ float to_tf32(float v) {
-  uint32_t u = __float_as_uint(v);
-  if ((u & 0x7F800000u) != 0x7F800000u) {
-    u += 0xFFFu + ((u >> 13) & 1u);
-    u &= 0xFFFFE000u;
-  }
-  return __uint_as_float(u);
-}
 
 // x [L, H, D] (row stride H*D) -> dst [H, L, 3D]: pattern 0 = [hi | hi | lo], 1 = [hi | lo | hi].
 __global__ void t5_split_qk_kernel(const float* __restrict__ x, float* __restrict__ dst, int L, int H, int D,
@@ -45,7 +36,7 @@ __global__ void t5_split_qk_kernel(const float* __restrict__ x, float* __restric
   const long long lh = i / D;
   const int h = static_cast<int>(lh % H), l = static_cast<int>(lh / H);
   const float v = x[i];
-  const float hi = to_tf32(v), lo = to_tf32(v - hi);
+  const float hi = round_tf32(v), lo = round_tf32(v - hi);
   float* o = dst + (static_cast<long long>(h) * L + l) * (3 * D);
   o[d] = hi;
   o[D + d] = pattern == 0 ? hi : lo;
@@ -63,7 +54,7 @@ __global__ void t5_vt_kernel(const float* __restrict__ v, float* __restrict__ vt
   __syncthreads();
   for (int r = threadIdx.y; r < 32; r += blockDim.y) {
     const int c = c0 + r, l = l0 + threadIdx.x;
-    if (c < HD && l < L) vt[static_cast<long long>(c) * L + l] = to_tf32(tile[threadIdx.x][r]);
+    if (c < HD && l < L) vt[static_cast<long long>(c) * L + l] = round_tf32(tile[threadIdx.x][r]);
   }
 }
 
@@ -108,7 +99,7 @@ __global__ void t5_softmax_kernel(float* __restrict__ S, const float* __restrict
   for (int c = lane * 4; c < L; c += 128) {
     float4 v = *reinterpret_cast<const float4*>(s + c);
     *reinterpret_cast<float4*>(s + c) =
-        make_float4(to_tf32(v.x * inv), to_tf32(v.y * inv), to_tf32(v.z * inv), to_tf32(v.w * inv));
+        make_float4(round_tf32(v.x * inv), round_tf32(v.y * inv), round_tf32(v.z * inv), round_tf32(v.w * inv));
   }
 }
 

@@ -23,7 +23,7 @@ def test_block_pair_flops_match_baseline():
 def test_bench_help_lists_workloads():
     r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--help"], capture_output=True, text=True)
     assert r.returncode == 0
-    for w in ("config1", "config2", "config4", "config5"):
+    for w in ("config1", "config2", "config4", "config5", "nerf"):
         assert w in r.stdout
 
 
@@ -48,3 +48,16 @@ def test_fp8_block_pair_ops():
                                                                     "single.quantize_cat"]
     assert labels.index("double.quantize_attn") == labels.index("double.attention") + 1
     assert labels.index("single.quantize_cat") == labels.index("single.attention") + 1
+
+
+def test_nerf_step_flops():
+    """One NeRF GLU block's GEMMs at 512^2: param_gen 2*1024*49152*3072 and three batched
+    products of 2*1024*256*256*64 each (chroma.cuh:1262-1302)."""
+    sys.argv = ["bench.py"]
+    sys.path.insert(0, str(REPO))
+    import bench
+
+    fl = bench.nerf_flops()
+    assert bench.NERF_PARAMS == 3 * 64 * 256
+    assert fl["param_gen"] == 2.0 * 1024 * 49152 * 3072
+    assert fl["gate"] == fl["value"] == fl["fc2"] == 2.0 * 1024 * 256 * 256 * 64

@@ -608,3 +608,31 @@ def test_attention_vs_reference_cudnn(engine, L, text_masked):
     a, b = mine.double().cpu().numpy().ravel(), theirs.double().cpu().numpy().ravel()
     assert rel_err(a, b) < 1e-2
     assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
+
+
+def test_nerf_block_gemms_vs_reference(engine, ref):
+    """One NeRF GLU block's GEMMs at 512^2 (chroma.cuh:1262-1302) at their real sizes, engine
+    against the reference's own linear() and batched_matmul_Bt on the same inputs: param_gen
+    (F32 s [1024, 3072] x bf16 W [49152, 3072]^T + bias), then the gate, value and fc2 batched
+    products over 1024 patches."""
+    g = torch.Generator(device=DEV).manual_seed(17)
+    P = 1024
+    s = torch.randn((P, 3072), generator=g, device=DEV)
+    w = (torch.randn((49152, 3072), generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    b = torch.randn(49152, generator=g, device=DEV) * 0.02
+    mine, theirs = torch.empty((P, 49152), device=DEV), torch.empty((P, 49152), device=DEV)
+    engine.linear(s, w, b, mine)
+    ref.linear(s.data_ptr(), 0, w.data_ptr(), 2, b.data_ptr(), theirs.data_ptr(), P, 3072, 49152)
+    torch.cuda.synchronize()
+    assert rel_err(mine.cpu().numpy(), theirs.cpu().numpy()) <= TOL_F32_OUT
+    x = torch.randn((P, 256, 64), generator=g, device=DEV)
+    wg = torch.randn((P, 256, 64), generator=g, device=DEV) * 0.125
+    w2 = torch.randn((P, 64, 256), generator=g, device=DEV) * 0.0625
+    for a, bb, n in ((x, wg, 256), (torch.randn((P, 256, 256), generator=g, device=DEV), w2, 64)):
+        c_mine = torch.empty((P, a.shape[1], n), device=DEV)
+        c_ref = torch.empty((P, a.shape[1], n), device=DEV)
+        engine.batched_matmul_Bt(a, bb, c_mine)
+        ref.batched_matmul_Bt(a.data_ptr(), bb.data_ptr(), c_ref.data_ptr(), P, a.shape[1], a.shape[2], n)
+        torch.cuda.synchronize()
+        assert rel_err(c_mine.cpu().numpy(), c_ref.cpu().numpy()) <= TOL_F32_OUT
+    engine.check_device_error()
