@@ -44,6 +44,12 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;          // 64 x 2 B = one 128-byte swizzle row (16-bit operands)
 constexpr int kThreads = 320;    // producer, MMA, 8 epilogue warps
+// kind::tf32 1-CTA kernels add warps that round each landed operand stage to TF32 in shared
+// memory (batched_matmul_Bt's fp32 operands): the conversion runs at a quarter of the FP32
+// rate, so one warp (one scheduler) cannot keep up with the MMAs; four spread it over all four.
+constexpr int kRoundWarps = 4;
+template <int KIND>
+constexpr int kThreadsK = KIND == 1 ? kThreads + 32 * kRoundWarps : kThreads;
 constexpr int kEpiThreads = 256;
 constexpr int kEpiWarps = 8;
 // K elements per 128-byte stage row: 64 for bf16/fp16 (KIND 0), 32 for tf32 (KIND 1), 128
@@ -161,18 +167,27 @@ __device__ __forceinline__ void tile_coords(int tile, const TcParams& p, int& gi
   nb = r / gm;
 }
 
-// Rounds one shared-memory operand stage (bytes a multiple of 512) to TF32 in place, the 32
-// lanes of a warp striding over it in 16-byte words; the values' positions (swizzle) are
-// irrelevant to an elementwise rounding.
-__device__ __forceinline__ void round_stage_tf32(uint8_t* stage, uint32_t bytes, int lane) {
-  float4* q = reinterpret_cast<float4*>(stage);
-  for (uint32_t i = lane; i < bytes / 16; i += 32) {
-    float4 v = q[i];
-    v.x = round_tf32_cvt(v.x);
-    v.y = round_tf32_cvt(v.y);
-    v.z = round_tf32_cvt(v.z);
-    v.w = round_tf32_cvt(v.w);
-    q[i] = v;
+// Rounds one shared-memory operand stage of BYTES (a multiple of 4 KB) to TF32 in place, the
+// 32 lanes of a warp striding over it in 16-byte words, eight words per lane in flight at a
+// time (one at a time, each load's latency made the rounding 5x slower than the MMAs); the
+// values' positions (swizzle) are irrelevant to an elementwise rounding.
+template <uint32_t BYTES>
+__device__ __forceinline__ void round_stage_tf32(uint8_t* stage, int lane) {
+  static_assert(BYTES % 4096 == 0, "whole groups of 8 x 32 words");
+  float4* q = reinterpret_cast<float4*>(stage) + lane;
+#pragma unroll 1
+  for (uint32_t g = 0; g < BYTES / 4096; ++g, q += 256) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = q[j * 32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      v[j].x = round_tf32_cvt(v[j].x);
+      v[j].y = round_tf32_cvt(v[j].y);
+      v[j].z = round_tf32_cvt(v[j].z);
+      v[j].w = round_tf32_cvt(v[j].w);
+      q[j * 32] = v[j];
+    }
   }
 }
 
@@ -756,7 +771,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
 
 // ---------------------------------------------------------------------------- 1-CTA kernel
 template <int BN, int STAGES, int EPI, int OUT, int KIND>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsK<KIND>, 1)
     tc_gemm_kernel(const __grid_constant__ TcMaps maps, const __grid_constant__ TcParams p) {
   constexpr uint32_t A_BYTES = kBM * kBK * 2;
   constexpr uint32_t B_BYTES = BN * kBK * 2;
@@ -775,16 +790,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
   uint64_t* drain_bar = tempty_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* rnd_bar = drain_bar + 1;  // kind::tf32 with round_tf32: stage s rounded (kRoundWarps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rnd_bar + STAGES);
   volatile int* bcast = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  bool round_stages = false;
+  if constexpr (KIND == 1) round_stages = p.round_tf32 != 0;
+  uint64_t* ready_bar = round_stages ? rnd_bar : full_bar;  // what the MMA waits for per stage
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
+      if (round_stages) mbar_init(&rnd_bar[s], kRoundWarps);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
@@ -848,55 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    bool round_stages = false;
-    if constexpr (KIND == 1) round_stages = p.round_tf32 != 0;
-    if (round_stages) {
-      // kind::tf32 on operands that are still plain fp32 (batched_matmul_Bt): the whole warp
-      // rounds every landed stage to nearest TF32 in place, makes its shared-memory writes
-      // visible to the tensor core (proxy fence), and lane 0 then issues the stage's MMAs.
-      // This replaces a rounding pass over both operands in global memory.
-      int stage = 0;
-      uint32_t phase = 0, local = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x, ++local) {
-        int tile, split, kb0, kb1;
-        item_coords(item, p, tile, split, kb0, kb1);
-        const uint32_t acc = local & 1u;
-        const uint32_t acc_phase = (local >> 1) & 1u;
-        ok = __all_sync(0xffffffffu, mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.err, kErrWaitMma));
-        if (!ok) break;
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          ok = __all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma));
-          if (!ok) break;
-          round_stage_tf32(sA + stage * A_BYTES, A_BYTES, lane);
-          round_stage_tf32(sB + stage * B_BYTES, B_BYTES, lane);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            tc_fence_after();
-            const uint32_t a0 = smem_u32(sA + stage * A_BYTES);
-            const uint32_t b0 = smem_u32(sB + stage * B_BYTES);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint64_t ad = smem_desc_k_sw128(a0 + k * 32), bd = smem_desc_k_sw128(b0 + k * 32);
-              umma_tf32(d_tmem, ad, bd, p.idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-            }
-            umma_commit(&empty_bar[stage]);
-          }
-          __syncwarp();
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (ok && lane == 0) umma_commit(&tfull_bar[acc]);
-      }
-      if (!ok && lane == 0) {
-        umma_commit(drain_bar);
-        mbar_wait_drain(drain_bar, 0);
-      }
-    } else if (lane == 0) {
+    if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0, local = 0;
       bool ok = true;
@@ -912,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma)) {
+          if (!mbar_wait(&ready_bar[stage], phase, p.err, kErrWaitMma)) {
             ok = false;
             break;
           }
@@ -941,6 +913,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         // MMAs already issued must retire before TMEM is released.
         umma_commit(drain_bar);
         mbar_wait_drain(drain_bar, 0);
+      }
+    }
+  } else if (warp >= 2 + kEpiWarps) {
+    // ------------------------------------------------------------ TF32 rounders (warps 10..13)
+    // Every landed stage is rounded to TF32 in place, each warp a quarter of A and of B; the
+    // warp's shared-memory writes are made visible to the tensor core (proxy fence) before its
+    // arrival on the stage's rounded barrier, which the MMA issuer waits for.
+    if (round_stages) {
+      const int r = warp - 2 - kEpiWarps;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < p.num_items && ok; item += gridDim.x) {
+        int tile, split, kb0, kb1;
+        item_coords(item, p, tile, split, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&full_bar[stage], phase, p.err, kErrWaitMma));
+          if (!ok) break;
+          round_stage_tf32<A_BYTES / kRoundWarps>(sA + stage * A_BYTES + r * (A_BYTES / kRoundWarps), lane);
+          round_stage_tf32<B_BYTES / kRoundWarps>(sB + stage * B_BYTES + r * (B_BYTES / kRoundWarps), lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&rnd_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
       }
     }
   } else {
@@ -1281,11 +1281,12 @@ b2g_status make_output_map(CUtensorMap* map, void* base, b2g_dtype dt, int64_t N
 }
 
 template <typename Kern>
-b2g_status launch_kernel(Kern kern, size_t smem, const TcMaps& maps, const TcParams& prm, int grid, cudaStream_t st) {
+b2g_status launch_kernel(Kern kern, size_t smem, const TcMaps& maps, const TcParams& prm, int grid, int threads,
+                         cudaStream_t st) {
   b2g_status s = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                             "cudaFuncSetAttribute(tc_gemm)");
   if (s != B2G_OK) return s;
-  return launch_pdl(kern, dim3(grid), dim3(kThreads), smem, st, "tc_gemm launch", maps, prm);
+  return launch_pdl(kern, dim3(grid), dim3(threads), smem, st, "tc_gemm launch", maps, prm);
 }
 
 // Variant selector: PAIR = 2-CTA 256x256 kernel, else 1-CTA 128xBN kernel.
@@ -1294,11 +1295,11 @@ b2g_status launch_one(const TcMaps& maps, const TcParams& prm, int grid, cudaStr
   if constexpr (PAIR) {
     constexpr size_t smem = smem_bytes(kBM * kBK * 2, 128 * kBK * 2, STAGES, kScaleBytes<KIND>);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
+    return launch_kernel(tc_gemm_pair_kernel<STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, kThreads, st);
   } else {
     constexpr size_t smem = smem_bytes(kBM * kBK * 2, BN * kBK * 2, STAGES, kScaleBytes<KIND>);
     static_assert(smem <= 227 * 1024, "shared memory budget");
-    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, st);
+    return launch_kernel(tc_gemm_kernel<BN, STAGES, EPI, OUT, KIND>, smem, maps, prm, grid, kThreadsK<KIND>, st);
   }
 }
 
