@@ -117,6 +117,11 @@ _SIGNATURES = {
     "b2g_attention_bf16": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_int64, ctypes.c_int, ctypes.c_int,
                                                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                                                    ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
+    "b2g_attention_bf16_batched": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                                                           ctypes.c_int, ctypes.c_void_p,
+                                                                           ctypes.c_int64, ctypes.c_void_p, ctypes.c_int,
+                                                                           ctypes.c_int64, ctypes.c_void_p],
+                                   ctypes.c_int),
     "b2g_modulate_to_bf16": ([ctypes.c_void_p] * 4 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p],
                              ctypes.c_int),
     "b2g_modulate_streams": ([ctypes.c_void_p] * 5 + [ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int,
@@ -588,6 +593,42 @@ def attention_bf16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_head: in
     _check(lib.b2g_attention_bf16(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
                                   L, n_head, d_head, _ptr(attn_mask), out.data_ptr(), _TORCH_TO_B2G[out.dtype],
                                   out.stride(0), ctypes.c_void_p(s)))
+    return out
+
+
+def attention_bf16_batched(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, n_head: int, d_head: int,
+                           batch: int, attn_mask: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                           out_dtype: torch.dtype = torch.float32,
+                           stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """attention_bf16 over `batch` sequences stacked in the rows of q, k, v (and out): sequence
+    b is rows [b*L, (b+1)*L) with L = rows / batch and attends only within itself.  attn_mask:
+    None, one [L] bias for every sequence, or [batch, L] (contiguous)."""
+    lib = load()
+    _require_cuda(q, k, v, attn_mask, out)
+    R = q.shape[0]
+    if batch < 1 or R % batch != 0:
+        raise B2GError("attention_bf16_batched: rows must be whole sequences")
+    L = R // batch
+    for t in (q, k, v):
+        if t.dtype != torch.bfloat16 or t.stride(1) != 1 or t.shape[0] != R:
+            raise B2GError("attention_bf16_batched: bf16 [batch*L, H*D] views with unit column stride expected")
+    stride = 0
+    if attn_mask is not None:
+        if attn_mask.dtype != torch.float32 or not attn_mask.is_contiguous():
+            raise B2GError("attention_bf16_batched: attn_mask must be contiguous F32")
+        if attn_mask.dim() == 2:
+            if tuple(attn_mask.shape) != (batch, L):
+                raise B2GError("attention_bf16_batched: attn_mask must be [L] or [batch, L]")
+            stride = L
+        elif attn_mask.numel() != L:
+            raise B2GError("attention_bf16_batched: attn_mask must be [L] or [batch, L]")
+    if out is None:
+        out = torch.empty((R, n_head * d_head), dtype=out_dtype, device=q.device)
+    s = (stream or torch.cuda.current_stream(q.device)).cuda_stream
+    _check(lib.b2g_attention_bf16_batched(q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(),
+                                          v.stride(0), L, batch, n_head, d_head, _ptr(attn_mask), stride,
+                                          out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0),
+                                          ctypes.c_void_p(s)))
     return out
 
 

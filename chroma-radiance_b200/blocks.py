@@ -117,6 +117,24 @@ def _halves(t) -> list:
     return list(t) if isinstance(t, (list, tuple)) else [t]
 
 
+def _attention(qkv, mask, B: int, L: int, out) -> None:
+    """The attention of every guidance half over the half-major [q | k | v] rows of qkv into
+    the same rows of out: one launch for all halves (attention_bf16_batched) when the key
+    biases are one [L] tensor or a contiguous [B, L] tensor, else one launch per half."""
+    R = B * L
+    q, k, v = qkv[:R, :HIDDEN], qkv[:R, HIDDEN:2 * HIDDEN], qkv[:R, 2 * HIDDEN:]
+    if B == 1:
+        b2g.attention_bf16(q, k, v, HEADS, DHEAD, attn_mask=_masks(mask, 1)[0], out=out[:R])
+        return
+    if mask is None or (torch.is_tensor(mask) and mask.is_contiguous() and
+                        (mask.dim() == 1 or tuple(mask.shape) == (B, L))):
+        b2g.attention_bf16_batched(q, k, v, HEADS, DHEAD, B, attn_mask=mask, out=out[:R])
+        return
+    for b, mb in enumerate(_masks(mask, B)):
+        rows = slice(b * L, (b + 1) * L)
+        b2g.attention_bf16(q[rows], k[rows], v[rows], HEADS, DHEAD, attn_mask=mb, out=out[rows])
+
+
 def _masks(mask, B: int) -> list:
     """Key bias per half: None, one [L] tensor shared by all halves, a [B, L] tensor or a list."""
     if mask is None:
@@ -160,10 +178,7 @@ def double_block_attention(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1,
                       [dict(x=img_m[b], w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[b * L + T:(b + 1) * L],
                             pe=pe[T:L], q_norm=img_w.q_norm, k_norm=img_w.k_norm) for b in range(B)], HEADS)
     mark("double.qkv")
-    for b, mb in enumerate(_masks(mask, B)):
-        rows = s.qkv[b * L:(b + 1) * L]
-        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
-                           attn_mask=mb, out=s.attn[b * L:(b + 1) * L])
+    _attention(s.qkv, mask, B, L, s.attn)
     mark("double.attention")
     b2g.gemm_group([dict(x=s.attn[b * L:b * L + T], w=txt_w.proj_w, bias=txt_w.proj_b, out=txts[b],
                          epilogue="gated_residual", gate=txt_gate1) for b in range(B)] +
@@ -206,10 +221,7 @@ def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=No
     b2g.gemm_qkv_rope([dict(x=x_mod, w=w.linear1_w, bias=w.linear1_b, out=s.qkv[:B * L], pe=pe, pe_period=L,
                             q_norm=w.q_norm, k_norm=w.k_norm, gelu_out=s.cat[:B * L, HIDDEN:])], HEADS)
     mark("single.linear1")
-    for b, mb in enumerate(_masks(mask, B)):
-        rows = s.qkv[b * L:(b + 1) * L]
-        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
-                           attn_mask=mb, out=s.cat[b * L:(b + 1) * L, :HIDDEN])
+    _attention(s.qkv, mask, B, L, s.cat[:, :HIDDEN])
     mark("single.attention")
     b2g.gemm(s.cat[:B * L], w.linear2_w, w.linear2_b, out=x, epilogue="gated_residual", gate=gate)
     mark("single.linear2")
@@ -408,10 +420,7 @@ def double_block_attention_fp8(txt_w: StreamWeightsFP8, img_w: StreamWeightsFP8,
                             out=s.qkv[b * L + T:(b + 1) * L], pe=pe[T:L], q_norm=img_w.q_norm,
                             k_norm=img_w.k_norm) for b in range(B)], HEADS)
     mark("double.qkv")
-    for b, mb in enumerate(_masks(mask, B)):
-        rows = s.qkv[b * L:(b + 1) * L]
-        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
-                           attn_mask=mb, out=s.attn[b * L:(b + 1) * L])
+    _attention(s.qkv, mask, B, L, s.attn)
     mark("double.attention")
     b2g.quantize_e4m3(s.attn[:B * L], out=s.attn8.q[:B * L], scales=s.attn8.s[:B * L])
     mark("double.quantize_attn")
@@ -463,10 +472,7 @@ def single_block_fp8(w: SingleWeightsFP8, x_mod: Q8, x, gate, pe, mask, s: Scrat
                             out=s.qkv[:R], pe=pe, pe_period=L, q_norm=w.q_norm, k_norm=w.k_norm,
                             gelu_out=s.cat[:R, HIDDEN:])], HEADS)
     mark("single.linear1")
-    for b, mb in enumerate(_masks(mask, B)):
-        rows = s.qkv[b * L:(b + 1) * L]
-        b2g.attention_bf16(rows[:, :HIDDEN], rows[:, HIDDEN:2 * HIDDEN], rows[:, 2 * HIDDEN:], HEADS, DHEAD,
-                           attn_mask=mb, out=s.cat[b * L:(b + 1) * L, :HIDDEN])
+    _attention(s.qkv, mask, B, L, s.cat[:, :HIDDEN])
     mark("single.attention")
     b2g.quantize_e4m3(s.cat[:R], out=s.cat8.q[:R], scales=s.cat8.s[:R])
     mark("single.quantize_cat")

@@ -210,6 +210,7 @@ struct FaParams {
   int num_kb;             // key blocks of 128
   float scale_log2;       // log2(e) / sqrt(D)
   const float* bias;      // [L] additive key bias (0 / -inf mask or general), NULL: none
+  long long bias_stride;  // floats between consecutive sequences' biases (0: one shared bias)
   void* out;
   long long ldo;
   int out_bf16;
@@ -244,6 +245,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int lane = threadIdx.x & 31;
   const int qpair = blockIdx.x;
   const int head = blockIdx.y;
+  // Sequence blockIdx.z of a batch stored one after another (rows [z*L, (z+1)*L) of q, k, v
+  // and out; keys past L of the last block are masked like any key past L).
+  const int row0 = static_cast<int>(blockIdx.z) * p.L;
+  const float* key_bias = p.bias ? p.bias + static_cast<long long>(blockIdx.z) * p.bias_stride : nullptr;
   const int nkb = p.num_kb;
 
   if (warp == 0 && lane == 0) {
@@ -297,7 +302,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
             tma_load_3d(sQ + t * Ly::kQTileBytes + c * kFaBox, &tmQ, q_full, c * 64,
-                        (qpair * kFaTiles + t) * kFaRows, head, once);
+                        row0 + (qpair * kFaTiles + t) * kFaRows, head, once);
       }
       int issued = 0;
       for (int j = 0; j < nkb; ++j) {
@@ -307,12 +312,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           mbar_arrive_expect_tx(&full[st], Ly::kKBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, j * kFaKeys, head, shared_kv);
+            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, row0 + j * kFaKeys, head,
+                        shared_kv);
         } else {
           mbar_arrive_expect_tx(&full[st], Ly::kVBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, j * kFaKeys, head, shared_kv);
+            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, row0 + j * kFaKeys, head,
+                        shared_kv);
         }
         ++issued;
       }
@@ -398,7 +405,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int key = j * kFaKeys + c * 32 + lane;
-        kb2[c] = key < p.L ? (p.bias ? __ldg(p.bias + key) * 1.4426950408889634f : 0.f) : -INFINITY;
+        kb2[c] = key < p.L ? (key_bias ? __ldg(key_bias + key) * 1.4426950408889634f : 0.f) : -INFINITY;
       }
       good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
       if (!good) break;
@@ -524,7 +531,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tmem_wait_ld();
         if (q < p.L) {
           if (p.out_bf16) {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + q * p.ldo + col0 + c * 32);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
+                                               static_cast<long long>(row0 + q) * p.ldo + col0 + c * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               __nv_bfloat162 a0 = __floats2bfloat162_rn(__uint_as_float(o[8 * i]) * inv,
@@ -539,7 +547,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                                   *reinterpret_cast<uint32_t*>(&a2), *reinterpret_cast<uint32_t*>(&a3));
             }
           } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + q * p.ldo + col0 + c * 32);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                    static_cast<long long>(row0 + q) * p.ldo + col0 + c * 32);
 #pragma unroll
             for (int i = 0; i < 8; ++i)
               dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
@@ -563,19 +572,21 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 template <int D>
 b2g_status launch_flash(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16* k, int64_t ldk,
                         const __nv_bfloat16* v, int64_t ldv, const FaParams& fp, int64_t L, int64_t H,
-                        cudaStream_t st) {
+                        int64_t batch, cudaStream_t st) {
   CUtensorMap tq, tk, tv;
   b2g_status s;
-  if ((s = make_operand_map(&tq, q, B2G_BF16, D, L, ldq, H, D, kFaRows)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tk, k, B2G_BF16, D, L, ldk, H, D, kFaKeys)) != B2G_OK) return s;
-  if ((s = make_operand_map(&tv, v, B2G_BF16, D, L, ldv, H, D, kFaKeys)) != B2G_OK) return s;
+  const int64_t rows = L * batch;  // the batch's sequences, one after another
+  if ((s = make_operand_map(&tq, q, B2G_BF16, D, rows, ldq, H, D, kFaRows)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tk, k, B2G_BF16, D, rows, ldk, H, D, kFaKeys)) != B2G_OK) return s;
+  if ((s = make_operand_map(&tv, v, B2G_BF16, D, rows, ldv, H, D, kFaKeys)) != B2G_OK) return s;
   constexpr uint32_t smem = FaLayout<D>::kSmem;
   static_assert(smem <= 227 * 1024, "shared memory budget");
   if ((s = check_cuda(cudaFuncSetAttribute(flash_attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem)),
                       "cudaFuncSetAttribute(flash_attn)")) != B2G_OK)
     return s;
-  const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows)), static_cast<unsigned>(H));
+  const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows)), static_cast<unsigned>(H),
+                  static_cast<unsigned>(batch));
   return launch_pdl(flash_attn_kernel<D>, grid, dim3(kFaThreads), smem, st, "flash_attn launch", tq, tk, tv, fp);
 }
 
@@ -599,12 +610,15 @@ b2g_status flash_checked(const AttnBf16Args& a, cudaStream_t st) {
   fp.num_kb = static_cast<int>((L + kFaKeys - 1) / kFaKeys);
   fp.scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   fp.bias = a.key_bias;
+  fp.bias_stride = a.bias_stride;
   fp.out = a.out;
   fp.ldo = a.ldo;
   fp.out_bf16 = a.out_dtype == B2G_BF16 ? 1 : 0;
   fp.err = dev->err_word;
-  if (D == 128) return launch_flash<128>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, st);
-  return launch_flash<64>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, st);
+  if (a.batch < 1 || a.batch > 65535 || L * a.batch > (1ll << 30) || a.bias_stride < 0)
+    return set_error(B2G_ERR_INVALID, "attention: batch in [1, 65535], batch * L < 2^30, bias stride >= 0");
+  if (D == 128) return launch_flash<128>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, a.batch, st);
+  return launch_flash<64>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, a.batch, st);
 }
 
 }  // namespace

@@ -652,6 +652,23 @@ b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t
   return attention_bf16(a, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_attention_bf16_batched(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                      int64_t ldv, int64_t L, int64_t batch, int n_head, int d_head,
+                                      const float* key_bias, int64_t bias_stride, void* out, b2g_dtype out_dtype,
+                                      int64_t ldo, void* stream) {
+  if (n_head < 0 || d_head < 0 || L < 0 || batch < 0)
+    return set_error(B2G_ERR_INVALID, "b2g_attention_bf16_batched: negative size");
+  if (L == 0 || n_head == 0 || batch == 0) return B2G_OK;
+  AttnBf16Args a;
+  a.q = static_cast<const __nv_bfloat16*>(q); a.ldq = ldq;
+  a.k = static_cast<const __nv_bfloat16*>(k); a.ldk = ldk;
+  a.v = static_cast<const __nv_bfloat16*>(v); a.ldv = ldv;
+  a.key_bias = key_bias; a.bias_stride = bias_stride;
+  a.out = out; a.out_dtype = out_dtype; a.ldo = ldo;
+  a.L = L; a.H = n_head; a.D = d_head; a.batch = batch;
+  return attention_bf16(a, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_modulate_to_bf16(const float* x, const float* shift, const float* scale, void* out, int64_t M,
                                 int64_t C, float eps, void* stream) {
   DeviceInfo* dev = nullptr;

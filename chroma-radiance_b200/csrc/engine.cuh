@@ -176,6 +176,8 @@ struct AttnBf16Args {
   b2g_dtype out_dtype = B2G_F32;
   int64_t ldo = 0;
   int64_t L = 0, H = 0, D = 0;
+  int64_t batch = 1;        // sequences of L rows stored one after another, each attending within itself
+  int64_t bias_stride = 0;  // floats between consecutive sequences' key biases (0: shared)
 };
 b2g_status attention_bf16(const AttnBf16Args& a, cudaStream_t st);
 

@@ -277,6 +277,17 @@ b2g_status b2g_attention_bf16(const void* q, int64_t ldq, const void* k, int64_t
                               int64_t L, int n_head, int d_head, const float* key_bias, void* out,
                               b2g_dtype out_dtype, int64_t ldo, void* stream);
 
+/* b2g_attention_bf16 over `batch` sequences of L rows stored one after another in q, k, v and
+ * out (sequence b at rows [b*L, (b+1)*L), each attending only within itself), in one launch;
+ * sequence b's key bias starts at key_bias + b * bias_stride (bias_stride 0: one bias for all).
+ * The guidance halves of forward_cfg (chroma.cuh:1540-1563), which the reference runs as one
+ * cuDNN SDPA call per half after gathering each half's [txt; img] rows (chroma.cuh:851-876,
+ * 1118-1136), stored here half-major.  batch <= 65535, batch * L < 2^30. */
+b2g_status b2g_attention_bf16_batched(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                      int64_t ldv, int64_t L, int64_t batch, int n_head, int d_head,
+                                      const float* key_bias, int64_t bias_stride, void* out, b2g_dtype out_dtype,
+                                      int64_t ldo, void* stream);
+
 /* The block GEMMs' A-operand producer.  Same arguments and meaning as the reference's
  *   void modulate_to_bf16_cuda(const float* x, const float* shift, const float* scale,
  *                              __nv_bfloat16* out, int64_t M, int64_t C, float eps)

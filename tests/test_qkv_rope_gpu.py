@@ -331,3 +331,38 @@ def test_gemm_qkv_rope_fp8_vs_oracle(engine, oracle, tail, halves):
         if tail:
             assert_bf16_of(pr["gelu_out"], want_tail)
     engine.check_device_error()
+
+
+@pytest.mark.parametrize("L,batch,shared_mask,out_bf16", [(200, 2, False, True), (131, 3, True, False),
+                                                           (1536, 2, False, True)])
+def test_attention_bf16_batched_equals_one_call_per_sequence(engine, L, batch, shared_mask, out_bf16):
+    """Sequences stacked in the rows of one [batch*L, 3*H*D] buffer (the guidance halves of
+    forward_cfg, half-major) in one launch: bit-identical to one attention_bf16 call per
+    sequence, including L not a multiple of the 128-key block (the last key block of a
+    sequence overlaps the next one's rows, which its mask must exclude) and a bias per
+    sequence or one shared bias."""
+    H, D = 2, 128
+    HD = H * D
+    qkv = seeded((batch * L, 3 * HD), L + batch, 1.0).to(DEV)
+    g = torch.Generator().manual_seed(batch)
+    if shared_mask:
+        mask = torch.zeros(L)
+        mask[3:40] = float("-inf")
+    else:
+        mask = torch.randn((batch, L), generator=g) * 2.0
+        mask[:, 5:17] = float("-inf")
+        mask[1, 20:L // 2] = float("-inf")
+    mask = mask.contiguous().to(DEV)
+    dt = torch.bfloat16 if out_bf16 else torch.float32
+    got = torch.zeros((batch * L, HD), dtype=dt, device=DEV)
+    engine.attention_bf16_batched(qkv[:, :HD], qkv[:, HD:2 * HD], qkv[:, 2 * HD:], H, D, batch, attn_mask=mask,
+                                  out=got)
+    want = torch.zeros_like(got)
+    for b in range(batch):
+        r = slice(b * L, (b + 1) * L)
+        engine.attention_bf16(qkv[r, :HD], qkv[r, HD:2 * HD], qkv[r, 2 * HD:], H, D,
+                              attn_mask=mask if shared_mask else mask[b], out=want[r])
+    torch.cuda.synchronize()
+    assert torch.isfinite(got.float()).all()
+    assert torch.equal(got, want)
+    engine.check_device_error()
