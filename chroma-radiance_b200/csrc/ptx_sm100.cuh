@@ -95,38 +95,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
-// Non-blocking probe of a phase (mbarrier.test_wait never suspends the thread).
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait for latency-critical hand-overs: polls with test_wait instead of letting
-// try_wait suspend the thread, so it resumes within a few cycles of the phase completing
-// (at the price of issue slots on its sub-partition).  Same limit and error handling.
-__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err, int code) {
-  const uint32_t addr = smem_u32(bar);
-  if (mbar_test_wait(addr, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_test_wait(addr, parity)) return true;
-    if ((it & 4095u) == 0) {
-      if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        atomicOr(err, code);
-        return false;
-      }
-    }
-  }
-}
-
 // Bounded wait used only on the abort path: never records anything, just stops.
 __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
   const uint32_t addr = smem_u32(bar);
