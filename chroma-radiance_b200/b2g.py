@@ -69,7 +69,7 @@ class QkvRopeDesc(ctypes.Structure):
     """b2g_qkv_rope_desc: RoPE rows and RMSNorm scales of one qkv projection problem."""
     _fields_ = [("pe", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
                 ("gelu_out", ctypes.c_void_p), ("gelu_ld", ctypes.c_int64), ("pe_period", ctypes.c_int64),
-                ("a_scale", ctypes.c_void_p), ("b_scale", ctypes.c_void_p)]
+                ("a_scale", ctypes.c_void_p), ("b_scale", ctypes.c_void_p), ("pe_compact", ctypes.c_int64)]
 
 
 _lib = None
@@ -521,7 +521,9 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
     Each problem: x [M, K] and w [3*n_head*128, K] (bf16/fp16), bias (F32), out (bf16 [M, N]
     view with 16-byte aligned rows; allocated when absent), pe (F32 RoPE rows of the
     problem's tokens, [M, 64, 4] or [M, 256]), q_norm / k_norm ([128] F32 or None), and
-    optionally pe_period P (row m uses pe row m % P; pe then needs P rows only: stacked
+    pe may also be [M, 64, 2] (cos, sin) per pair, for tables of the rotation form (cos, -sin,
+    sin, cos): the same result from half the bytes (compact_rope_table).  Optionally
+    pe_period P (row m uses pe row m % P; pe then needs P rows only: stacked
     guidance halves of one sequence).  Output columns [q | k | v]: q and k heads normed and
     rotated, v the plain product (+ bias).  Up to four problems (txt and img streams, times
     the guidance halves) run as one launch.  FP8 form: x and w uint8 E4M3 codes with x_scale
@@ -556,8 +558,10 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
         period = int(pr.get("pe_period") or 0)
         if period < 0:
             raise B2GError("gemm_qkv_rope: pe_period must be 0 or positive")
-        if pe.numel() < (period or pr["x"].shape[0]) * 256:
-            raise B2GError("gemm_qkv_rope: pe must hold 256 floats per row of x (per pe_period row)")
+        compact = pe.dim() == 3 and pe.shape[-1] == 2
+        if pe.numel() < (period or pr["x"].shape[0]) * (128 if compact else 256):
+            raise B2GError("gemm_qkv_rope: pe must hold 256 floats ([64, 4]), or 128 ([64, 2] cos/sin), per row "
+                           "of x (per pe_period row)")
         xs, ws = pr.get("x_scale"), pr.get("w_scale")
         if pr["x"].dtype == torch.uint8:
             _require_cuda(xs, ws)
@@ -565,7 +569,8 @@ def gemm_qkv_rope(problems: list[dict], n_head: int, eps: float = 1e-6,
                 raise B2GError("gemm_qkv_rope: E4M3 x needs x_scale, and uint8 w with w_scale")
         descs.append(d)
         ropes.append(QkvRopeDesc(pe.data_ptr(), _ptr(qn), _ptr(kn), _ptr(tail),
-                                 tail.stride(0) if tail is not None else 0, period, _ptr(xs), _ptr(ws)))
+                                 tail.stride(0) if tail is not None else 0, period, _ptr(xs), _ptr(ws),
+                                 1 if compact else 0))
         outs.append(out)
         keep.append(pe)
     arr = (GemmDesc * len(descs))(*descs)
@@ -714,3 +719,12 @@ def modulate_streams(x: torch.Tensor, txt_shift: torch.Tensor, txt_scale: torch.
                                     img_scale.data_ptr(), seq, txt_rows, dst.data_ptr(), dt, rsp, M, C, eps,
                                     ctypes.c_void_p(s)))
     return (codes, rs) if fp8 else codes
+
+
+def compact_rope_table(pe: torch.Tensor) -> torch.Tensor | None:
+    """[L, 64, 2] (cos, sin) form of a RoPE table [L, 64, 4] = (cos, -sin, sin, cos) per pair,
+    for gemm_qkv_rope; None if the table is not of that form (then pass it as it is)."""
+    p = pe.reshape(pe.shape[0], -1, 4)
+    if not (torch.equal(p[..., 0], p[..., 3]) and torch.equal(p[..., 1], -p[..., 2])):
+        return None
+    return torch.stack([p[..., 0], p[..., 2]], -1).contiguous()

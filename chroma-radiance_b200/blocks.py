@@ -117,6 +117,16 @@ def _halves(t) -> list:
     return list(t) if isinstance(t, (list, tuple)) else [t]
 
 
+def _rope_table(pe, s):
+    """pe in its compact (cos, sin) form when it has the rotation form (every RoPE table does):
+    the qkv epilogue then reads half the bytes.  Made once per table and kept on the scratch,
+    so a captured graph reuses the same tensor."""
+    if getattr(s, "_pe_src", None) is not pe:
+        s._pe_src = pe
+        s._pe_c = b2g.compact_rope_table(pe)
+    return s._pe_c if s._pe_c is not None else pe
+
+
 def _attention(qkv, mask, B: int, L: int, out) -> None:
     """The attention of every guidance half over the half-major [q | k | v] rows of qkv into
     the same rows of out: one launch for all halves (attention_bf16_batched) when the key
@@ -168,6 +178,7 @@ def double_block_attention(txt_w: StreamWeights, img_w: StreamWeights, txt_mod1,
     txt_m, img_m, txts, imgs = _halves(txt_mod1), _halves(img_mod1), _halves(txt), _halves(img)
     B, T = len(txts), txts[0].shape[0]
     L = T + imgs[0].shape[0]
+    pe = _rope_table(pe, s)
     # Each layer's GEMMs over all row blocks share one launch (b2g_gemm_group): together their
     # tiles fill the SMs where the txt GEMM alone (M=512) would leave most of them idle.  The
     # qkv projection applies qk_norm and RoPE in its epilogue (txt rows take pe rows [0, T),
@@ -215,6 +226,7 @@ def single_block(w: SingleWeights, x_mod, x, gate, pe, mask, s: Scratch, mark=No
     L = pe.shape[0]
     B = x.shape[0] // L
     assert B * L == x.shape[0], "x must hold whole guidance halves of pe.shape[0] rows"
+    pe = _rope_table(pe, s)
     # linear1 in one launch over all halves (its weight rows are [q | k | v | mlp]): the qkv
     # columns get qk_norm + RoPE (row r rotated by pe row r % L) into s.qkv, the MLP columns
     # bias + GELU straight into the linear2 concat buffer.
@@ -413,6 +425,7 @@ def double_block_attention_fp8(txt_w: StreamWeightsFP8, img_w: StreamWeightsFP8,
     txt_m, img_m, txts, imgs = _halves(txt_mod1), _halves(img_mod1), _halves(txt), _halves(img)
     B, T = len(txts), txts[0].shape[0]
     L = T + imgs[0].shape[0]
+    pe = _rope_table(pe, s)
     b2g.gemm_qkv_rope([dict(x=txt_m[b].q, x_scale=txt_m[b].s, w=txt_w.qkv.q, w_scale=txt_w.qkv.s, bias=txt_w.qkv_b,
                             out=s.qkv[b * L:b * L + T], pe=pe[:T], q_norm=txt_w.q_norm, k_norm=txt_w.k_norm)
                        for b in range(B)] +
@@ -467,6 +480,7 @@ def single_block_fp8(w: SingleWeightsFP8, x_mod: Q8, x, gate, pe, mask, s: Scrat
     L = pe.shape[0]
     B = x.shape[0] // L
     assert B * L == x.shape[0], "x must hold whole guidance halves of pe.shape[0] rows"
+    pe = _rope_table(pe, s)
     R = B * L
     b2g.gemm_qkv_rope([dict(x=x_mod.q, x_scale=x_mod.s, w=w.linear1.q, w_scale=w.linear1.s, bias=w.linear1_b,
                             out=s.qkv[:R], pe=pe, pe_period=L, q_norm=w.q_norm, k_norm=w.k_norm,

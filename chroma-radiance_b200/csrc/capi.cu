@@ -618,6 +618,9 @@ b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc
     rs[n].gelu_out = rope[i].gelu_out;
     rs[n].gelu_ld = rope[i].gelu_ld;
     rs[n].pe_period = rope[i].pe_period;
+    if (rope[i].pe_compact != 0 && rope[i].pe_compact != 1)
+      return set_error(B2G_ERR_INVALID, "b2g_gemm_qkv_rope: pe_compact must be 0 or 1");
+    rs[n].pe_compact = rope[i].pe_compact == 1;
     p.rope = &rs[n];
     p.epilogue = static_cast<b2g_epilogue>(kEpiQkvRope);
     std::string why;

@@ -51,6 +51,7 @@ struct QkvRope {
   void* gelu_out = nullptr;         // optional: columns past 3 * heads * 128 -> bias + GELU, bf16 here
   int64_t gelu_ld = 0;
   int64_t pe_period = 0;            // rows per sequence when one problem stacks several (0: M)
+  bool pe_compact = false;          // pe rows [64][2] (cos, sin) instead of [64][4]
 };
 
 // Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *

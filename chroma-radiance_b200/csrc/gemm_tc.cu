@@ -89,6 +89,7 @@ struct TcGroup {
   const float* qn;         // kEpiQkvRope: RMSNorm scales of q and k heads [128] (NULL: none)
   const float* kn;
   int pe_period;           // kEpiQkvRope: the RoPE row of row m is m % pe_period (0: m)
+  int pe_compact;          // kEpiQkvRope: pe rows are [64][2] (cos, sin) instead of [64][4]
 };
 
 // Tensor maps of every group (kernel parameter; indexed by group at run time).
@@ -649,9 +650,14 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
     }
     inv = rsqrtf(ss / 128.0f + p.eps);
   }
+  // The table row of the token: [64][4] (c0, c1, c2, c3) per pair, or compact [64][2] (cos, sin)
+  // for the rotation form (cos, -sin, sin, cos), half the bytes (the reads compete with the
+  // L2-bound mainloop for L2 bandwidth).  Both forms go through the same roundings:
+  // x0' = fma(x0, c0, x1 * c1), x1' = fma(x0, c2, x1 * c3).
   const int pe_m = m < G.M ? m : G.M - 1;
-  const float4* pe_row =
-      reinterpret_cast<const float4*>(G.pe) + static_cast<long long>(G.pe_period ? pe_m % G.pe_period : pe_m) * 64;
+  const bool compact = G.pe_compact != 0;
+  const float4* pe_row = reinterpret_cast<const float4*>(G.pe) +
+                         static_cast<long long>(G.pe_period ? pe_m % G.pe_period : pe_m) * (compact ? 32 : 64);
   uint32_t r[2][32];
   tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
 #pragma unroll
@@ -673,12 +679,26 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
           v[j + 3] = v[j + 3] * inv * w.w;
         }
       }
+      if (compact) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {  // pair i*16 + j of the head
-        const float4 c = __ldg(pe_row + i * 16 + j);
-        const float x0 = v[2 * j], x1 = v[2 * j + 1];
-        v[2 * j] = x0 * c.x + x1 * c.y;
-        v[2 * j + 1] = x0 * c.z + x1 * c.w;
+        for (int j = 0; j < 8; ++j) {  // pairs i*16 + 2j and 2j + 1 of the head
+          const float4 cs = __ldg(pe_row + i * 8 + j);
+          float x0 = v[4 * j], x1 = v[4 * j + 1];
+          v[4 * j] = __fmaf_rn(x0, cs.x, __fmul_rn(x1, -cs.y));
+          v[4 * j + 1] = __fmaf_rn(x0, cs.y, __fmul_rn(x1, cs.x));
+          x0 = v[4 * j + 2];
+          x1 = v[4 * j + 3];
+          v[4 * j + 2] = __fmaf_rn(x0, cs.z, __fmul_rn(x1, -cs.w));
+          v[4 * j + 3] = __fmaf_rn(x0, cs.w, __fmul_rn(x1, cs.z));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {  // pair i*16 + j of the head
+          const float4 c = __ldg(pe_row + i * 16 + j);
+          const float x0 = v[2 * j], x1 = v[2 * j + 1];
+          v[2 * j] = __fmaf_rn(x0, c.x, __fmul_rn(x1, c.y));
+          v[2 * j + 1] = __fmaf_rn(x0, c.z, __fmul_rn(x1, c.w));
+        }
       }
     }
     if (m_warp0 < G.M && col < p.N) stage_store_values<false, OUT_BF16>(tmD, e.buf, obuf, 0, m_warp0, col + i * 32, v,
@@ -1473,6 +1493,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     G.qn = q.rope ? q.rope->q_norm : nullptr;
     G.kn = q.rope ? q.rope->k_norm : nullptr;
     G.pe_period = q.rope ? static_cast<int>(q.rope->pe_period) : 0;
+    G.pe_compact = q.rope ? (q.rope->pe_compact ? 1 : 0) : 0;
     G.vec_ok = aligned16(q.d) && ((q.ldd * out_bytes) % 16 == 0) &&
                (q.batch <= 1 || (q.d_bstride * out_bytes) % 16 == 0);
     all_vec = all_vec && G.vec_ok;

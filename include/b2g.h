@@ -263,6 +263,10 @@ typedef struct {
                             unconditional halves of a guidance batch; pe then holds P rows) */
   const float* a_scale;  /* E4M3 operands only: per-row activation scales [M] */
   const float* b_scale;  /* E4M3 operands only: per-output-channel weight scales [N] */
+  int64_t pe_compact;    /* 0: pe rows are the reference's [64][4] (c0, c1, c2, c3) per pair;
+                            1: [64][2] (cos, sin) per pair for tables of the rotation form
+                            (cos, -sin, sin, cos), which every RoPE table is: the same values
+                            from half the table bytes */
 } b2g_qkv_rope_desc;
 b2g_status b2g_gemm_qkv_rope(const b2g_gemm_desc* descs, const b2g_qkv_rope_desc* rope, int count, int n_head,
                              float eps, void* stream);

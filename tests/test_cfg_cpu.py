@@ -94,7 +94,10 @@ class FakeEngine:
                 y = y[:, :qkv]
             period = pr.get("pe_period") or M
             rows = torch.arange(M) % period
-            p = pr["pe"].reshape(-1, blocks.DHEAD // 2, 4)[rows].reshape(M, 1, blocks.DHEAD // 2, 4)
+            pe = pr["pe"]
+            if pe.dim() == 3 and pe.shape[-1] == 2:   # compact (cos, sin) form
+                pe = torch.stack([pe[..., 0], -pe[..., 1], pe[..., 1], pe[..., 0]], -1)
+            p = pe.reshape(-1, blocks.DHEAD // 2, 4)[rows].reshape(M, 1, blocks.DHEAD // 2, 4)
             q, k, v = y.reshape(M, 3, n_head, blocks.DHEAD).unbind(1)
 
             def norm_rope(a, scale):
@@ -120,6 +123,8 @@ class FakeEngine:
         o = torch.einsum("hlm,mhd->lhd", torch.softmax(s, -1), vv).reshape(L, n_head * d_head)
         out.copy_(o.to(out.dtype))
         return out
+
+    compact_rope_table = staticmethod(engine_b2g.compact_rope_table)
 
     def attention_bf16_batched(self, q, k, v, n_head, d_head, batch, attn_mask=None, out=None):
         self.calls.append(("attention_bf16_batched", batch))
@@ -262,3 +267,15 @@ def test_per_half_mask_list_falls_back_to_one_launch_per_half(pass_inputs, monke
     blocks.forward_pass(pw, y, pe, [masks[0], masks[1]], blocks.PassScratch(T, I, "cpu", halves=2), T)
     assert ("attention_bf16", 1) in fake.calls
     assert torch.allclose(x, y, rtol=0, atol=1e-5 * float(y.abs().max()))
+
+
+def test_compact_rope_table():
+    """compact_rope_table keeps (cos, sin) of a rotation-form table and refuses other tables."""
+    ang = torch.rand((5, 64), generator=torch.Generator().manual_seed(4)) * 6.28
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    c = engine_b2g.compact_rope_table(pe)
+    assert c.shape == (5, 64, 2) and c.is_contiguous()
+    assert torch.equal(c[..., 0], ang.cos()) and torch.equal(c[..., 1], ang.sin())
+    general = pe.clone()
+    general[2, 7, 1] += 0.5
+    assert engine_b2g.compact_rope_table(general) is None

@@ -366,3 +366,41 @@ def test_attention_bf16_batched_equals_one_call_per_sequence(engine, L, batch, s
     assert torch.isfinite(got.float()).all()
     assert torch.equal(got, want)
     engine.check_device_error()
+
+
+@pytest.mark.parametrize("fp8,tail", [(False, False), (True, False), (False, True)])
+def test_gemm_qkv_rope_compact_table_equals_full(engine, fp8, tail):
+    """The compact (cos, sin) RoPE table gives the same outputs as the reference's [64][4]
+    table it was made from: bf16 and E4M3 operands, two problems, and one problem over two
+    stacked sequences (pe_period) with a GELU tail."""
+    H, K = 2, 256
+    QKV = 3 * H * DH
+    N = QKV + (192 if tail else 0)
+    pe = torch.from_numpy(pe_table(160, DH, 51)).to(DEV)
+    pe_c = engine.compact_rope_table(pe)
+    assert pe_c is not None
+    qn = (1 + 0.2 * seeded((DH,), 52, 1.0, torch.float32)).to(DEV)
+    kn = (1 + 0.2 * seeded((DH,), 53, 1.0, torch.float32)).to(DEV)
+    specs = [(320, 0, 160)] if tail else [(60, 0, 0), (100, 60, 0)]
+    results = []
+    for table in (pe, pe_c):
+        probs = []
+        for i, (m, r0, period) in enumerate(specs):
+            x = seeded((m, K), 60 + i).to(DEV)
+            w = seeded((N, K), 70 + i, 0.05).to(DEV)
+            b = seeded((N,), 80 + i, 0.05, torch.float32).to(DEV)
+            pr = dict(x=x, w=w, bias=b, q_norm=qn, k_norm=kn, pe=table if period else table[r0:r0 + m],
+                      pe_period=period)
+            if fp8:
+                xq, xs = engine.quantize_e4m3(x)
+                wq, wsc = engine.quantize_e4m3(w)
+                pr.update(x=xq, x_scale=xs, w=wq, w_scale=wsc)
+            if tail:
+                pr["gelu_out"] = torch.zeros((m, N - QKV), dtype=torch.bfloat16, device=DEV)
+            probs.append(pr)
+        outs = engine.gemm_qkv_rope(probs, H)
+        torch.cuda.synchronize()
+        results.append([o.clone() for o in outs] + [p["gelu_out"].clone() for p in probs if "gelu_out" in p])
+    for full, comp in zip(*results):
+        assert torch.equal(full, comp)
+    engine.check_device_error()
