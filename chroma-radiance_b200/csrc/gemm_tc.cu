@@ -730,7 +730,11 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
   const int m_warp0 = m - e.lane;
   const float* sb = p.bias_kind ? e.sbias : nullptr;
   const bool splitk = p.splits > 1;
-  float* part = splitk ? p.ws + ((static_cast<size_t>(slot) * p.splits + split) * 128 + e.row) * BN : nullptr;
+  // Split-K partials: one 128 x BN fp32 block per (slot, split), stored so that a warp's 32
+  // rows of one 4-column group are 32 consecutive 16-byte words (float4 index
+  // (chunk * 8 + j) * 128 + row): every store and fixup load of a warp is one coalesced 512 bytes.
+  float4* part = splitk ? reinterpret_cast<float4*>(p.ws + (static_cast<size_t>(slot) * p.splits + split) * 128 * BN)
+                        : nullptr;
   uint32_t r[2][32];
   tmem_ld_32x32b_x32(tacc + c0 * 32, r[0]);
 #pragma unroll
@@ -744,11 +748,11 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
       emit_chunk<EPI, OUT>(p, G, tmD, e.buf, obuf, bz, m, m_warp0, n_base + c * 32, r[i & 1],
                            sb ? sb + c * 32 : nullptr, e.lane);
     } else {
-      float4* dst = reinterpret_cast<float4*>(part + c * 32);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        dst[j] = make_float4(__uint_as_float(r[i & 1][4 * j]), __uint_as_float(r[i & 1][4 * j + 1]),
-                             __uint_as_float(r[i & 1][4 * j + 2]), __uint_as_float(r[i & 1][4 * j + 3]));
+        part[(c * 8 + j) * 128 + e.row] =
+            make_float4(__uint_as_float(r[i & 1][4 * j]), __uint_as_float(r[i & 1][4 * j + 1]),
+                        __uint_as_float(r[i & 1][4 * j + 2]), __uint_as_float(r[i & 1][4 * j + 3]));
     }
   }
   if (splitk) {
@@ -758,7 +762,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
     named_bar_sync(1, kEpiThreads);
     if (*e.bcast == p.splits - 1) {
       __threadfence();
-      const float* base = p.ws + (static_cast<size_t>(slot) * p.splits * 128 + e.row) * BN;
+      const float4* base = reinterpret_cast<const float4*>(p.ws + static_cast<size_t>(slot) * p.splits * 128 * BN);
 #pragma unroll 1
       for (int i = 0; i < NCH; ++i) {
         const int c = c0 + i;
@@ -766,10 +770,10 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.f;
         for (int sp = 0; sp < p.splits; ++sp) {
-          const float4* src = reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * 128 * BN + c * 32);
+          const float4* src = base + static_cast<size_t>(sp) * 32 * BN;  // 128 * BN floats per split
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const float4 v = __ldcg(src + j);
+            const float4 v = __ldcg(src + (c * 8 + j) * 128 + e.row);
             acc[4 * j] += v.x;
             acc[4 * j + 1] += v.y;
             acc[4 * j + 2] += v.z;
