@@ -266,11 +266,14 @@ class AttnRef:
         lib.ref_bench_attention.restype = ctypes.c_int
         pp = ctypes.POINTER(ctypes.c_void_p)
         lib.ref_double_block.argtypes = [pp, _i64, _i64]
+        lib.ref_double_block_attn.argtypes = [pp, _i64, _i64]
+        lib.ref_double_block_mlp.argtypes = [pp, _i64, _i64]
         lib.ref_single_block.argtypes = [pp, _i64]
         lib.ref_alloc_blocks.argtypes = [ctypes.c_ulonglong, _i64, _i64, _i64, pp, pp]
         lib.ref_bench_blocks.argtypes = [pp, pp, _i64, _i64, ctypes.c_int, ctypes.c_int, _i64,
                                          ctypes.POINTER(ctypes.c_double)]
-        for f in ("ref_double_block", "ref_single_block", "ref_alloc_blocks", "ref_bench_blocks"):
+        for f in ("ref_double_block", "ref_double_block_attn", "ref_double_block_mlp", "ref_single_block",
+                  "ref_alloc_blocks", "ref_bench_blocks"):
             getattr(lib, f).restype = ctypes.c_int
         lib.ref_t5_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, ctypes.c_float, _c_p, _c_p]
         lib.ref_t5_attention.restype = ctypes.c_int
@@ -287,6 +290,12 @@ class AttnRef:
 
     def double_block(self, ptrs, T, I):
         return self.lib.ref_double_block(self.ptr_array(ptrs), T, I)
+
+    def double_block_attn(self, ptrs, T, I):
+        return self.lib.ref_double_block_attn(self.ptr_array(ptrs), T, I)
+
+    def double_block_mlp(self, ptrs, T, I):
+        return self.lib.ref_double_block_mlp(self.ptr_array(ptrs), T, I)
 
     def single_block(self, ptrs, L):
         return self.lib.ref_single_block(self.ptr_array(ptrs), L)

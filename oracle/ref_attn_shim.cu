@@ -134,7 +134,8 @@ static Tensor bview(void* base, int64_t off, int64_t n) {
   return Tensor::wrap_gpu(static_cast<float*>(base) + off, {n}, DType::F32);
 }
 
-int ref_double_block(void** p, int64_t T, int64_t I) {
+// The attention half (qkv, qk_norm, attention, proj + gated residual; chroma.cuh:808-905).
+int ref_double_block_attn(void** p, int64_t T, int64_t I) {
   const int64_t L = T + I;
   Tensor all_q = Tensor::alloc({L, kH}, DType::F32, true);
   Tensor all_k = Tensor::alloc({L, kH}, DType::F32, true);
@@ -168,6 +169,12 @@ int ref_double_block(void** p, int64_t T, int64_t I) {
     Tensor bp = bview(w[5], 0, kH);
     linear_gated_residual(a, wp, &bp, x, static_cast<float*>(p[26 + s]), M, kH);
   }
+  return 0;
+}
+
+// The MLP half (mlp0, GELU, mlp2 + gated residual; chroma.cuh:906-964), on inputs modulated
+// from the residual streams the attention half updated.
+int ref_double_block_mlp(void** p, int64_t T, int64_t I) {
   for (int s = 0; s < 2; ++s) {
     void** w = p + 10 * s;
     const int64_t M = s == 0 ? I : T;
@@ -182,6 +189,11 @@ int ref_double_block(void** p, int64_t T, int64_t I) {
     gated_residual_cuda(x, o.f32(), static_cast<float*>(p[28 + s]), x, M, kH);
   }
   return 0;
+}
+
+int ref_double_block(void** p, int64_t T, int64_t I) {
+  const int r = ref_double_block_attn(p, T, I);
+  return r != 0 ? r : ref_double_block_mlp(p, T, I);
 }
 
 int ref_single_block(void** p, int64_t L) {
