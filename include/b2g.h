@@ -77,11 +77,14 @@ const char* b2g_version(void);
 /* General fused GEMM.  New entry point (no reference counterpart beyond linear_lt). */
 b2g_status b2g_gemm(const b2g_gemm_desc* desc, void* stream);
 
-/* `count` independent b2g_gemm problems in stream order.  When two of them share N, K,
- * dtypes, bias presence and epilogue (the txt and img streams of one double-block layer:
+/* `count` independent b2g_gemm problems in stream order.  When two to four of them share N,
+ * K, dtypes, bias presence and epilogue (the txt and img streams of one double-block layer:
  * chroma.cuh:826-839 qkv, :888-892 proj, :923-927 / :958-962 MLP, each run by the reference
- * as a separate linear() per stream) they run as one persistent tensor-core launch whose
- * tiles fill the SMs together; otherwise one after the other.  New entry point. */
+ * as a separate linear() per stream; with classifier-free guidance also each stream's
+ * conditional and unconditional rows) they run as one persistent tensor-core launch whose
+ * tiles fill the SMs together; otherwise one after the other.  Problems that read the same
+ * F32 activations against 16-bit weights (the T5 layer's q, k, v: t5.cuh:233-275) share one
+ * cast of them.  New entry point. */
 b2g_status b2g_gemm_group(const b2g_gemm_desc* descs, int count, void* stream);
 
 /* out[M,N] (F32) = x[M,K] . w[N,K]^T + bias[N] (F32, may be NULL).
