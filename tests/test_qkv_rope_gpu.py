@@ -404,3 +404,18 @@ def test_gemm_qkv_rope_compact_table_equals_full(engine, fp8, tail):
     for full, comp in zip(*results):
         assert torch.equal(full, comp)
     engine.check_device_error()
+
+
+def test_attention_bf16_batched_rejects_bad_arguments(engine):
+    """Rows that are not whole sequences, and a mask whose rows do not match the batch, are
+    errors rather than silent reads past a sequence."""
+    H, D = 2, 128
+    qkv = torch.zeros((10, 3 * H * D), dtype=torch.bfloat16, device=DEV)
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
+    with pytest.raises(engine.B2GError):
+        engine.attention_bf16_batched(q, k, v, H, D, 3)                    # 10 rows, 3 sequences
+    with pytest.raises(engine.B2GError):
+        engine.attention_bf16_batched(q, k, v, H, D, 2, attn_mask=torch.zeros((3, 5), device=DEV))
+    out = engine.attention_bf16_batched(q, k, v, H, D, 2, attn_mask=torch.zeros((2, 5), device=DEV))
+    torch.cuda.synchronize()
+    assert out.shape == (10, H * D) and torch.isfinite(out).all()
