@@ -162,6 +162,7 @@ b2g_status b2g_init(void) {
 
 b2g_status b2g_shutdown(void) {
   workspace_release();
+  noalloc_forget();
   return B2G_OK;
 }
 
@@ -181,7 +182,6 @@ b2g_status b2g_set_gemm_variant(int variant, int splits) {
 }  // extern "C"
 
 namespace b2g {
-namespace {
 
 // Checks one descriptor (the rules of b2g_gemm) and fills the internal problem.
 // *empty = true for an M == 0 or N == 0 problem (nothing to do).
@@ -215,6 +215,8 @@ b2g_status desc_to_problem(const b2g_gemm_desc* d, const char* who, GemmProblem*
   p->gate = d->gate;
   return B2G_OK;
 }
+
+namespace {
 
 // desc_to_problem for a problem on E4M3 operands: both a and b E4M3 (activations already
 // quantised per row) with their per-row (a_scale) and per-output-channel (b_scale) scales.

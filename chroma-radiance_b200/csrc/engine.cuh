@@ -66,6 +66,12 @@ struct TpReduce {
   int64_t counter_slots;    // capacity of `counters`
 };
 
+// The checks of b2g_gemm on one descriptor (`who` names the entry point in error messages);
+// fills *p, and sets *empty for an M == 0 or N == 0 problem (nothing to do).
+b2g_status desc_to_problem(const b2g_gemm_desc* d, const char* who, GemmProblem* p, bool* empty);
+// Forgets b2g_gemm_noalloc's cached per-device scratch addresses (b2g_shutdown).
+void noalloc_forget();
+
 // Records a message for b2g_last_error() and returns `st`.
 b2g_status set_error(b2g_status st, const std::string& msg);
 b2g_status check_cuda(cudaError_t e, const char* what);

@@ -12,8 +12,11 @@
 // The array is shared by every call on a device: calls whose kernels may overlap (other
 // streams, other host threads) race on it and must be serialised by the caller.  The first
 // call on each device resolves the array's address (cudaGetSymbolAddress) with that device
-// current; make that first call before capturing any stream on the device.
+// current; make that first call before capturing any stream on the device.  b2g_shutdown
+// forgets the resolved addresses, so after a device reset (a new primary context) call
+// b2g_shutdown before the next call.
 #include <cuda_runtime.h>
+#include <atomic>
 #include <string>
 #include "engine.cuh"
 
@@ -24,7 +27,9 @@ constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
+// Device address of each device's copy of the array, resolved on first use.  Two host threads
+// resolving the same device at once store the same value, so plain atomics suffice.
+std::atomic<void*> g_scratch_addr[kMaxDevices];
 
 // Device address of this device's copy of g_noalloc_scratch, resolved once per device.
 b2g_status scratch_address(void** out) {
@@ -32,55 +37,40 @@ b2g_status scratch_address(void** out) {
   b2g_status s = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
   if (s != B2G_OK) return s;
   if (dev < 0 || dev >= kMaxDevices) return set_error(B2G_ERR_NO_DEVICE, "device ordinal out of range");
-  if (!g_scratch_addr[dev]) {
-    void* p = nullptr;
+  void* p = g_scratch_addr[dev].load(std::memory_order_acquire);
+  if (!p) {
     if ((s = check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)")) !=
         B2G_OK)
       return s;
-    g_scratch_addr[dev] = p;
+    g_scratch_addr[dev].store(p, std::memory_order_release);
   }
-  *out = g_scratch_addr[dev];
+  *out = p;
   return B2G_OK;
 }
 
 int64_t round_up8(int64_t v) { return (v + 7) / 8 * 8; }
 
 }  // namespace
+
+void noalloc_forget() {
+  for (auto& a : g_scratch_addr) a.store(nullptr, std::memory_order_release);
+}
+
 }  // namespace b2g
 
 using namespace b2g;
 
 extern "C" b2g_status b2g_gemm_noalloc(const b2g_gemm_desc* d, void* stream) {
-  if (!d) return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: null descriptor");
-  if (d->M < 0 || d->N < 0 || d->K < 0) return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: negative size");
-  if (d->M == 0 || d->N == 0) return B2G_OK;
-  if (!d->d || (d->K > 0 && (!d->a || !d->b))) return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: null operand");
-  if (d->K > 0 && (d->lda < d->K || d->ldb < d->K))
-    return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: lda/ldb < K");
-  if (d->ldd < d->N) return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: ldd < N");
-  if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_GATED_RESIDUAL)
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_noalloc: unknown epilogue");
-  if (d->epilogue == B2G_EPI_GATED_RESIDUAL && (!d->gate || d->d_dtype != B2G_F32))
-    return set_error(B2G_ERR_INVALID, "b2g_gemm_noalloc: gated residual needs a gate and an F32 output");
-  if (d->a_dtype == B2G_E4M3 || d->b_dtype == B2G_E4M3 || d->d_dtype == B2G_E4M3)
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_noalloc: E4M3 operands are not implemented");
-  const bool w16 = d->b_dtype == B2G_BF16 || d->b_dtype == B2G_F16;
-  if (!(d->a_dtype == d->b_dtype || (d->a_dtype == B2G_F32 && w16)))
-    return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_noalloc: unsupported operand dtype combination");
-  DeviceInfo* dev = nullptr;
-  b2g_status s = device_info(&dev);
-  if (s != B2G_OK) return s;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-
   GemmProblem p;
-  p.M = d->M; p.N = d->N; p.K = d->K;
-  p.a = d->a; p.a_dtype = d->a_dtype; p.lda = d->lda;
-  p.b = d->b; p.b_dtype = d->b_dtype; p.ldb = d->ldb;
-  p.bias = d->bias; p.bias_dtype = d->bias_dtype;
-  p.d = d->d; p.d_dtype = d->d_dtype; p.ldd = d->ldd;
-  p.epilogue = d->epilogue;
-  p.gate = d->gate;
+  bool empty = false;
+  // The same checks as b2g_gemm, so the two entry points accept exactly the same descriptors.
+  b2g_status s = desc_to_problem(d, "b2g_gemm_noalloc", &p, &empty);
+  if (s != B2G_OK || empty) return s;
+  DeviceInfo* dev = nullptr;
+  if ((s = device_info(&dev)) != B2G_OK) return s;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
   p.allow_split = false;
+  const bool w16 = p.b_dtype == B2G_BF16 || p.b_dtype == B2G_F16;
   if (p.a_dtype == B2G_F32 && w16 && p.K > 0) {
     const int64_t kp = round_up8(p.K);  // 16-byte rows for TMA
     const double need = static_cast<double>(p.M) * static_cast<double>(kp) * 2.0;

@@ -1,6 +1,6 @@
 // cublas_ops.cuh — drop-in replacement for the reference's GEMM layer header.
 //
-// Integration (see INTEGRATION.md): in the reference tree, rename its original
+// Integration: in the reference tree, rename its original
 // cublas_ops.cuh to cublas_ops_cublaslt.cuh, put this file in its place, add the engine's
 // include/ directory to the include path and link libb2g.so.  chroma.cuh, t5.cuh,
 // attention.cuh and main.cu then compile unchanged: every function, global and macro the

@@ -157,9 +157,12 @@ b2g_status b2g_attention_qknorm_rope(const float* q, int64_t ldq, const float* k
  * b2g_gemm's workspace growth (cudaMalloc, cudaFree) brings.  F32 activations with 16-bit
  * weights are cast into an 8 MiB array compiled into the library, so M*round_up(K,8)*2 must be
  * <= 8388608 bytes (else B2G_ERR_INVALID, nothing launched); K is never split.  Otherwise the
- * same arguments, rules and results as b2g_gemm.  The array is shared per device: calls whose
- * kernels can overlap race on it.  The first call on a device must come before any stream
- * capture on it (it looks up the array's device address). */
+ * same arguments and rules as b2g_gemm, and the same results up to fp32 accumulation order
+ * (b2g_gemm may split K).  The array is shared per device: calls whose kernels can overlap
+ * race on it.  The first call on a device must come before any stream capture on it (it looks
+ * up the array's device address); after a device reset, call b2g_shutdown first so the
+ * address is looked up again.  Loading the library reserves the 8 MiB on every device it
+ * runs on, whether or not this entry point is called. */
 b2g_status b2g_gemm_noalloc(const b2g_gemm_desc* desc, void* stream);
 
 /* T5 attention.  Same arguments and meaning as the reference's

@@ -1,13 +1,20 @@
 """b2g_gemm_noalloc (F32 activations cast into the library's static scratch, K never split)
-against b2g_gemm, the entry point that casts into its growable workspace.  Collected last so
-it also runs after every other test has used the library.
+against b2g_gemm, the entry point that casts into its growable workspace, and against the C
+oracle.  Collected last so it also runs after every other test has used the library.
 
 Both paths cast the same way and run the same tensor-core kernels, so they agree to
-max|d|/max|ref| <= 1e-6 (the kernel variant may differ only in accumulation order).
+max|d|/max|ref| <= 1e-6 (the kernel variant may differ only in accumulation order).  The
+entry point exists for callers that cannot let a library allocate device memory, so one test
+runs in a fresh process, forces split-K (which makes b2g_gemm allocate partial sums) and
+checks that the device's free memory does not move across no-alloc calls.
 """
 from __future__ import annotations
 
 import ctypes
+import os
+import subprocess
+import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -76,3 +83,71 @@ def test_noalloc_rejects_oversize_before_launching(engine):
     assert engine.launch_count() == n0
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)
+
+
+def test_noalloc_matches_oracle(engine, oracle):
+    """The no-alloc path against the C restatement of linear(): F32 activations rounded to
+    bf16 as the reference's linear() casts them, bf16 weights, F32 bias and output."""
+    lib = lib_and_desc(engine)
+    M, K, N = 200, 768, 384
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn((M, K), generator=g)
+    w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g) * 0.02
+    xb = oracle.to_bf16_bits(x.numpy())
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    want = oracle.linear(xb, 2, wb, 2, bias.numpy())
+    xd, wd, bd = x.to(DEV), w.to(DEV), bias.to(DEV)
+    out = torch.empty((M, N), device=DEV)
+    for _ in range(2):
+        out.fill_(float("nan"))
+        d = desc(engine, xd, wd, bd, out)
+        assert lib.b2g_gemm_noalloc(ctypes.byref(d), None) == 0, engine.load().b2g_last_error()
+        torch.cuda.synchronize()
+        assert rel_err(out.cpu().numpy(), want) <= 1e-4
+
+
+def _fresh_process_worker() -> int:
+    """Run as a script: a process in which nothing has used the library yet."""
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "chroma-radiance_b200"))
+    import b2g
+
+    b2g.init()
+    lib = lib_and_desc(b2g)
+    b2g.set_gemm_variant(-1, 4)   # force 4-way split-K: b2g_gemm then needs partial-sum workspace
+    M, K, N = 512, 3072, 3072
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn((M, K), generator=g).to(DEV)           # F32 activations: the cast path
+    w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    bias = (torch.randn(N, generator=g) * 0.02).to(DEV)
+    got, want = torch.empty((M, N), device=DEV), torch.empty((M, N), device=DEV)
+    dg, dw = desc(b2g, x, w, bias, got), desc(b2g, x, w, bias, want)
+    # The first call loads the kernels' module and looks up the array's address.
+    assert lib.b2g_gemm_noalloc(ctypes.byref(dg), None) == 0, lib.b2g_last_error()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for _ in range(3):
+        assert lib.b2g_gemm_noalloc(ctypes.byref(dg), None) == 0, lib.b2g_last_error()
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, f"b2g_gemm_noalloc changed free device memory by {free0 - free1} bytes"
+    # The same request through b2g_gemm grows its workspaces (cast operand, split-K partials):
+    # the measurement above would have seen an allocation.
+    assert lib.b2g_gemm(ctypes.byref(dw), None) == 0, lib.b2g_last_error()
+    torch.cuda.synchronize()
+    free2 = torch.cuda.mem_get_info()[0]
+    assert free2 < free1, "b2g_gemm was expected to allocate its workspace in a fresh process"
+    assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-6
+    b2g.check_device_error()
+    print("no-alloc fresh process ok", free0 - free2)
+    return 0
+
+
+def test_noalloc_allocates_nothing_in_fresh_process():
+    r = subprocess.run([sys.executable, os.path.abspath(__file__)], capture_output=True, text=True, timeout=600)
+    print(r.stdout[-2000:], r.stderr[-2000:])
+    assert r.returncode == 0 and "no-alloc fresh process ok" in r.stdout
+
+
+if __name__ == "__main__":
+    sys.exit(_fresh_process_worker())
