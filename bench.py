@@ -312,42 +312,91 @@ WORKLOAD2 = ("config2: one double-stream + one single-stream Chroma block at 512
              "tokens, hidden 3072, 24x128 heads, MLP 12288, key mask on 400 of 512 txt tokens)")
 
 
+def _ref_blocks_ms(ref, T: int, I: int, steps: int, warmup: int, seed: int = 0) -> float:
+    """ms per step of the reference's block pair (double + single block) at T txt + I img tokens."""
+    import ctypes
+
+    dp, sp = (ctypes.c_void_p * 32)(), (ctypes.c_void_p * 11)()
+    rc = ref.lib.ref_alloc_blocks(seed, T, I, MASKED, dp, sp)
+    if rc != 0:
+        raise RuntimeError(f"ref_alloc_blocks failed: {rc}")
+    ms = ctypes.c_double(0)
+    rc = ref.lib.ref_bench_blocks(dp, sp, T, I, steps, warmup, FLUSH_BYTES, ctypes.byref(ms))
+    if rc != 0:
+        raise RuntimeError(f"ref_bench_blocks failed: CUDA error {rc}")
+    return ms.value / steps
+
+
+def _no_gpu_line(speak: bool = True) -> bool:
+    """True when no GPU is visible; then prints the reference arm's `unavailable` line (when
+    `speak`, i.e. on rank 0)."""
+    import torch
+
+    if torch.cuda.device_count() > 0:
+        return False
+    if speak:
+        print(json.dumps({"impl": "reference", "unavailable": "no CUDA device visible: the reference's path is its "
+                      "GPU code (cuBLASLt, cuDNN and its own kernels); it has no CPU implementation"}))
+    return True
+
+
+def _ref_world_max(world: int, vals: list) -> list:
+    """Max over ranks of host floats, over a gloo group (the reference arm never touches the
+    engine or torch's CUDA state)."""
+    if world == 1:
+        return vals
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    t = torch.tensor(vals, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def run_reference_config2(args) -> None:
     """The reference's block code (oracle/_ref/libref_attention.so): its own linear(),
     linear_gated_residual(), rms_norm, cuDNN attention and elementwise kernels in its own call
-    order, on inputs from its own Philox generator; timed with CUDA events in C."""
-    import ctypes
-
+    order, on inputs from its own Philox generator; timed with CUDA events in C.  With N ranks
+    every rank runs one replica on its own GPU (as the engine arm does), and the value is the
+    aggregate over ranks from the slowest rank's time.  Rank 0 also times the reference's block
+    pair at 1024^2 (L=4608) on its GPU: the single-GPU baseline of the tensor-parallel leg."""
     import oracle as oracle_mod
 
     world, rank, local = dist_setup()
-    if rank != 0:
-        return
     os.environ.setdefault("CUDA_VISIBLE_DEVICES", str(local))
     if not oracle_mod.ATTN_REF_PATH.exists():
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_attention.so was not built "
-                          "(the reference sources were absent at build time)"}))
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_attention.so was not built "
+                              "(the reference sources were absent at build time)"}))
+        return
+    if _no_gpu_line(rank == 0):
         return
     import blocks
 
     ref = oracle_mod.AttnRef()
-    dp, sp = (ctypes.c_void_p * 32)(), (ctypes.c_void_p * 11)()
-    rc = ref.lib.ref_alloc_blocks(0, T_TXT, I_IMG, MASKED, dp, sp)
-    if rc != 0:
-        raise RuntimeError(f"ref_alloc_blocks failed: {rc}")
-    ms = ctypes.c_double(0)
     with ClockSampler(local) as clk:
-        rc = ref.lib.ref_bench_blocks(dp, sp, T_TXT, I_IMG, args.steps, args.warmup, FLUSH_BYTES, ctypes.byref(ms))
-    if rc != 0:
-        raise RuntimeError(f"ref_bench_blocks failed: CUDA error {rc}")
+        per = _ref_blocks_ms(ref, T_TXT, I_IMG, args.steps, args.warmup)
+    per = _ref_world_max(world, [per])[0]
+    tp_ref = None
+    if rank == 0 and not args.no_tp1024:
+        lin4, att4 = blocks.block_pair_flops(T_1024, I_1024)
+        per4 = _ref_blocks_ms(ref, T_1024, I_1024, args.steps, max(3, args.warmup), seed=4)
+        tp_ref = {"workload": WORKLOAD_TP1024.split(";")[0] + " (the reference has no tensor-parallel path: its "
+                  "block code on one GPU)", "n_gpus": 1, "ms_per_step": round(per4, 5),
+                  "tflops": round((lin4 + att4) / (per4 * 1e-3) / 1e12, 2)}
     lin, att = blocks.block_pair_flops(T_TXT, I_IMG)
-    per = ms.value / args.steps
-    value = (lin + att) / (per * 1e-3) / 1e12
+    value = (lin + att) * world / (per * 1e-3) / 1e12
+    if rank != 0:
+        return
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (reference Philox, seed 0)",
-        "config": {"workload": WORKLOAD2, "flop_per_step": lin + att,
+        "config": {"workload": WORKLOAD2, "flop_per_step": lin + att, "parallelism": f"replicas x{world}",
                    "l2": "weights 680 MB > L2; 256 MB buffer written before every step, outside the events"},
         "cpu_baseline": {"kind": "reference", "cores": 0, "value": round(value, 2), "unit": "TFLOP/s",
                          "sample": "the reference has no CPU path; this arm is its own block code (chroma.cuh "
@@ -355,7 +404,8 @@ def run_reference_config2(args) -> None:
                                    "built from its sources and run on the B200"},
         "e2e": {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "clocks": clk.summary(),
-    }))
+        "tp1024": tp_ref,
+    }), flush=True)
 
 
 class _Marks:
@@ -582,6 +632,8 @@ def run_engine_config2(args) -> None:
     pass_d2h = img_h.numel() * 4
     pass_flop = blocks.pass_flops(T, I, halves=CFG_HALVES)
     del pass_graph, pw, ps
+    torch.cuda.empty_cache()
+    tp_leg = tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) if not args.no_tp1024 else None
 
     if world > 1:
         import torch.distributed as dist
@@ -637,6 +689,7 @@ def run_engine_config2(args) -> None:
         "clocks": clk.summary(),
         "gpu_launches": int(launches_per_step * args.steps),
         "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
+        "tp1024": tp_leg,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as oracle_mod
@@ -649,37 +702,73 @@ def run_engine_config2(args) -> None:
         torch.distributed.destroy_process_group()
 
 
-WORKLOAD4 = ("config4: one double-stream + one single-stream block at 1024^2 (T=512 txt + I=4096 img tokens), "
-             "tensor-parallel over all ranks (column-split qkv/linear1/mlp0, row-split proj/linear2/mlp2, "
-             "3 bf16 NCCL all-reduces of [4608, 3072] per step)")
+
+# ---------------------------------------------------------------------------- 1024^2 TP leg
+T_1024, I_1024 = 512, 4096
+WORKLOAD_TP1024 = ("config4's block pair at 1024^2: one double-stream + one single-stream block, T=512 txt + "
+                   "I=4096 img tokens (L=4608), hidden 3072, 24x128 heads, MLP 12288, key mask on 400 of 512 txt "
+                   "tokens; 1 GPU: the unsharded block pair; N GPUs: tensor parallel (column-split qkv/linear1/mlp0 "
+                   "by heads and MLP columns, row-split proj/mlp2/linear2 with the all-rank reduction fused into the "
+                   "GEMM over NVLink peer memory, one cross-rank barrier kernel per row-split layer)")
 
 
-def run_engine_config4(args) -> None:
-    """Tensor-parallel block pair at 1024^2: every rank runs its shard; strong scaling."""
+class _EagerMarks:
+    """Events recorded between eagerly launched operations (per-operation time split)."""
+
+    def __init__(self, torch, stream):
+        self.torch, self.stream = torch, stream
+        self.start = torch.cuda.Event(enable_timing=True)
+        self.items = []
+
+    def begin(self):
+        self.start.record(self.stream)
+
+    def __call__(self, label):
+        ev = self.torch.cuda.Event(enable_timing=True)
+        ev.record(self.stream)
+        self.items.append((label, ev))
+
+    def durations(self) -> dict:
+        out, prev = {}, self.start
+        for lab, ev in self.items:
+            out[lab] = out.get(lab, 0.0) + prev.elapsed_time(ev)
+            prev = ev
+        return out
+
+
+def _tp_categories(us: dict) -> dict:
+    """Sums of a per-operation split: column-split GEMMs, attention, row-split GEMMs (with the
+    fused all-rank reduction at N > 1) and cross-rank barriers."""
+    cat = {"column_gemms": 0.0, "attention": 0.0, "row_gemms_with_reduction": 0.0, "barriers": 0.0}
+    for lab, v in us.items():
+        if lab.endswith(".barrier"):
+            cat["barriers"] += v
+        elif "attention" in lab:
+            cat["attention"] += v
+        elif lab.split(".")[-1] in ("proj", "mlp2", "linear2"):
+            cat["row_gemms_with_reduction"] += v
+        else:
+            cat["column_gemms"] += v
+    return {k: round(v, 1) for k, v in cat.items()}
+
+
+def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
+    """BASELINE config 4's block pair at 1024^2 on every rank of this run (chroma.cuh:808-1157 at
+    L=4608).  One GPU: the unsharded block pair.  N GPUs: tp.py's fused tensor-parallel path, and
+    on rank 0 also the unsharded block pair on its own GPU (the 1-GPU time the speed-up is taken
+    against, and the parity reference: the replicated residual streams after one step from the
+    same seeded inputs, max|d|/max|ref| and cosine of the update).  The NCCL all-reduce variant
+    is timed beside the fused one.  Eager launches (the fused path's barrier epochs change every
+    call); an L2 flush (256 MB write) and, at N > 1, a barrier before every step, outside the
+    events; device time, max over ranks."""
     import datetime
 
-    import torch
-    import torch.distributed as dist
-
-    import b2g
     import blocks
     import tp
 
-    world, rank, local = dist_setup()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    b2g.init()
-    T, I = 512, 4096
+    T, I = T_1024, I_1024
     L, H = T + I, blocks.HIDDEN
-    g = torch.Generator(device=dev).manual_seed(0)
-    txt_w, img_w = blocks.random_stream(g, dev), blocks.random_stream(g, dev)
-    sw = blocks.random_single(g, dev)
-    tw, iw, ts = tp.shard_stream(txt_w, rank, world), tp.shard_stream(img_w, rank, world), tp.shard_single(sw, rank,
-                                                                                                          world)
-    del txt_w, img_w, sw  # keep only this rank's shard resident
-    torch.cuda.empty_cache()
+    g = torch.Generator(device=dev).manual_seed(4)   # identical inputs on every rank
     act = {k: torch.randn((n, H), generator=g, device=dev).to(torch.bfloat16) for k, n in
            (("txt_mod1", T), ("img_mod1", I), ("txt_mod2", T), ("img_mod2", I), ("x_mod", L))}
     res = {k: torch.randn((n, H), generator=g, device=dev) for k, n in (("txt", T), ("img", I), ("x", L))}
@@ -688,79 +777,216 @@ def run_engine_config4(args) -> None:
     pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
     mask = torch.zeros(L, device=dev)
     mask[T - MASKED:T] = float("-inf")
-    scratch = tp.TPScratch(T, I, world, dev)
-    ops = tp.EngineOps()
-    fused = world > 1 and args.tp_comm == "fused"
-    if fused:
-        comm = tp.SymmetricComm(L, H, None, dev)
-        comm.res_double[:T].copy_(res["txt"])
-        comm.res_double[T:].copy_(res["img"])
-        comm.res_single.copy_(res["x"])
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
-
-    def step():
-        if fused:
-            tp.tp_double_block_fused(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"],
-                                     act["img_mod2"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
-            tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gt[4], pe, mask, scratch)
-            return
-        tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
-                           res["txt"], res["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
-        tp.tp_single_block(ops, ts, act["x_mod"], res["x"], gt[4], pe, mask, scratch)
+    steps, warm = args.steps, max(3, args.warmup)
+    lin, att = blocks.block_pair_flops(T, I)
+    if world > 1:
+        import torch.distributed as dist
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    for _ in range(args.warmup):
-        step()
-    barrier()
-    n0 = b2g.launch_count()
-    per_step = []
-    with ClockSampler(local) as clk:
-        for i in range(args.steps):
-            flush.fill_(i & 0xFF)
+    def timed(fn, sync_ranks: bool) -> list:
+        if sync_ranks:
             barrier()
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize(dev)
+        out = []
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            if sync_ranks:
+                barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            step()
+            fn()
             b.record(stream)
             b.synchronize()
-            per_step.append(a.elapsed_time(b))
-    launches = b2g.launch_count() - n0
-    b2g.check_device_error()
-    total_ms = sum(per_step)
-    if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t[0])
-    lin, att = blocks.block_pair_flops(T, I)
-    per = total_ms / args.steps
+            out.append(a.elapsed_time(b))
+        return out
+
+    def split(fn) -> dict:
+        torch.cuda.synchronize(dev)
+        mk = _EagerMarks(torch, stream)
+        mk.begin()
+        fn(mk)
+        torch.cuda.synchronize(dev)
+        return {k: 1e3 * v for k, v in mk.durations().items()}
+
+    def delta(a, b):
+        return (a - b).double().flatten()
+
+    out = {"workload": WORKLOAD_TP1024, "n_gpus": world, "steps": steps, "warmup": warm,
+           "flop_per_step": lin + att}
+    # --- the unsharded block pair (the whole leg at N = 1; rank 0's reference at N > 1)
+    uns_ms, uns_split, ref = None, None, None
+    if rank == 0:
+        s1 = blocks.Scratch(T, I, dev)
+        ures = {k: v.clone() for k, v in res.items()}
+
+        def unsharded(mark=None):
+            blocks.double_block(txt_w, img_w, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                                ures["txt"], ures["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, s1, mark)
+            blocks.single_block(sw, act["x_mod"], ures["x"], gt[4], pe, mask, s1, mark)
+
+        unsharded()
+        torch.cuda.synchronize(dev)
+        ref = {k: delta(ures[k], res[k]) for k in res}
+        per = timed(unsharded, False)
+        uns_ms = sum(per) / steps
+        uns_split = split(unsharded)
+        del s1, ures
+    if world == 1:
+        out.update({"mode": "unsharded block pair, 1 GPU", "ms_per_step": round(uns_ms, 5),
+                    "tflops": round((lin + att) / (uns_ms * 1e-3) / 1e12, 2),
+                    "breakdown_us": {k: round(v, 1) for k, v in uns_split.items()},
+                    "categories_us": _tp_categories(uns_split), "unsharded_ms_per_step": round(uns_ms, 5),
+                    "speedup_vs_1gpu": 1.0, "parity": None})
+        return out
+    barrier()
+    # --- the tensor-parallel block pair (every rank)
+    ops = tp.EngineOps()
+    tw, iw, ts = tp.shard_stream(txt_w, rank, world), tp.shard_stream(img_w, rank, world), tp.shard_single(sw, rank,
+                                                                                                          world)
+    scratch = tp.TPScratch(T, I, world, dev)
+    comm = tp.SymmetricComm(L, H, None, dev)
+
+    def load_res():
+        comm.res_double[:T].copy_(res["txt"])
+        comm.res_double[T:].copy_(res["img"])
+        comm.res_single.copy_(res["x"])
+
+    def fused(mark=None):
+        tp.tp_double_block_fused(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"],
+                                 act["img_mod2"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch, mark)
+        tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gt[4], pe, mask, scratch, mark)
+
+    load_res()
+    barrier()
+    fused()
+    barrier()
+    parity = None
+    if rank == 0:
+        got = {"txt": delta(comm.res_double[:T], res["txt"]), "img": delta(comm.res_double[T:], res["img"]),
+               "x": delta(comm.res_single, res["x"])}
+        parity = {}
+        for k in got:
+            parity[k] = {"max_rel": float((got[k] - ref[k]).abs().max() / ref[k].abs().max()),
+                         "cosine": float((got[k] @ ref[k]) / (got[k].norm() * ref[k].norm()))}
+        parity["against"] = ("the unsharded block pair on rank 0's GPU, same seeded weights and inputs: the update "
+                             "of the replicated residual streams (txt, img, single-block x) after one step")
+        parity["within_tolerance"] = all(v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999
+                                         for k, v in parity.items() if isinstance(v, dict))
+    per_f = timed(fused, True)
+    sp = split(fused)
+    nres = {k: v.clone() for k, v in res.items()}
+
+    def nccl(mark=None):
+        tp.tp_double_block(ops, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                           nres["txt"], nres["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch)
+        tp.tp_single_block(ops, ts, act["x_mod"], nres["x"], gt[4], pe, mask, scratch)
+
+    per_n = timed(nccl, True)
+    b2g_mod = __import__("b2g")
+    b2g_mod.check_device_error()
+    labels = sorted(sp)
+    t = torch.tensor([sum(per_f), sum(per_n)] + [sp[k] for k in labels], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    f_ms, n_ms = float(t[0]) / steps, float(t[1]) / steps
+    sp = {k: float(v) for k, v in zip(labels, t[2:].tolist())}
+    u = torch.tensor([uns_ms or 0.0], device=dev, dtype=torch.float64)
+    dist.all_reduce(u, op=dist.ReduceOp.MAX)   # rank 0's 1-GPU time, on every rank
+    uns_ms = float(u[0])
+    out.update({"mode": f"tp{world}, reduction fused into the row-split GEMMs over NVLink peer memory",
+                "ms_per_step": round(f_ms, 5), "tflops": round((lin + att) / (f_ms * 1e-3) / 1e12, 2),
+                "breakdown_us": {k: round(v, 1) for k, v in sp.items()}, "categories_us": _tp_categories(sp),
+                "unsharded_ms_per_step": round(uns_ms, 5), "speedup_vs_1gpu": round(uns_ms / f_ms, 3),
+                "unsharded_breakdown_us": ({k: round(v, 1) for k, v in uns_split.items()} if uns_split else None),
+                "nccl_ms_per_step": round(n_ms, 5),
+                "allreduce_bytes_per_step": 3 * L * H * 2, "parity": parity})
+    del comm
+    return out
+
+
+def run_reference_config4(args) -> None:
+    """The reference's block pair at 1024^2 on one GPU (it has no tensor-parallel path): rank 0
+    runs it; other ranks exit without work."""
+    import oracle as oracle_mod
+
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    os.environ.setdefault("CUDA_VISIBLE_DEVICES", str(local))
+    if not oracle_mod.ATTN_REF_PATH.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_attention.so was not built"}))
+        return
+    if _no_gpu_line():
+        return
+    import blocks
+
+    ref = oracle_mod.AttnRef()
+    with ClockSampler(local) as clk:
+        per = _ref_blocks_ms(ref, T_1024, I_1024, args.steps, args.warmup, seed=4)
+    lin, att = blocks.block_pair_flops(T_1024, I_1024)
     value = (lin + att) / (per * 1e-3) / 1e12
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (reference Philox, seed 4)",
+        "config": {"workload": WORKLOAD_TP1024, "flop_per_step": lin + att, "parallelism": "none (1 GPU)"},
+        "cpu_baseline": {"kind": "reference", "cores": 0, "value": round(value, 2), "unit": "TFLOP/s",
+                         "sample": "the reference has no CPU path; its own block code on one B200"},
+        "e2e": {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "clocks": clk.summary()}), flush=True)
+
+
+def run_engine_config4(args) -> None:
+    """Config 4's block pair at 1024^2 on its own: tp1024_leg as the headline (1 GPU: unsharded;
+    N GPUs: the fused tensor-parallel path, strong scaling)."""
+    import datetime
+
+    import torch
+
+    import b2g
+    import blocks
+
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    b2g.init()
+    g = torch.Generator(device=dev).manual_seed(0)
+    txt_w, img_w = blocks.random_stream(g, dev), blocks.random_stream(g, dev)
+    sw = blocks.random_single(g, dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n0 = b2g.launch_count()
+    with ClockSampler(local) as clk:
+        leg = tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush)
+    launches = b2g.launch_count() - n0
     peaks = measured_peaks()
-    per_gpu = value / world
+    per = leg["ms_per_step"]
+    value = leg["tflops"]
     line = {
-        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox generator, seed 0)",
-        "config": {"workload": WORKLOAD4, "flop_per_step": lin + att, "parallelism": f"tp{world}",
-                   "tp_comm": ("reduction fused into the row-split GEMMs over NVLink peer memory" if fused else
-                               "NCCL bf16 all-reduce" if world > 1 else "none"),
-                   "allreduce_bytes_per_step": 3 * L * H * 2 if world > 1 else 0,
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": leg["warmup"], "ms_per_step": per, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox generator, seeds 0/4)",
+        "config": {"workload": WORKLOAD_TP1024, "flop_per_step": leg["flop_per_step"], "parallelism": f"tp{world}",
                    "l2": "256 MB buffer written before every step, outside the events"},
-        "roofline": {"bound": "tensor", "achieved": round(per_gpu, 2), "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": round(per_gpu / peaks["bf16_tflops"], 4), "traffic": None,
+        "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(value / world / peaks["bf16_tflops"], 4), "traffic": None,
                      "peak_source": peaks["source"] + " (burst bf16)",
-                     "kernel": "whole step per GPU (GEMMs, attention, all-reduces)"},
-        "clocks": clk.summary(), "gpu_launches": int(launches),
-        "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
+                     "kernel": "whole step per GPU (GEMMs, attention, fused reductions, barriers)"},
+        "clocks": clk.summary(), "gpu_launches": int(launches), "tp1024": leg,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        dist.destroy_process_group()
+        torch.distributed.destroy_process_group()
 
 
 WORKLOAD5 = ("config5: the FP8 transformer at 512^2, one independent job per GPU: one double-stream + one "
@@ -1197,6 +1423,9 @@ def run_reference_nerf(args) -> None:
 
 
 def main():
+    # The fused tensor-parallel path needs plain peer mappings only; keep torch's symmetric
+    # memory from binding its buffers to an NVLink multicast object.
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100 for config2, 200 config1)")
@@ -1204,8 +1433,7 @@ def main():
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
     ap.add_argument("--workload", choices=["config2", "config1", "config4", "config5", "nerf"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--tp-comm", choices=["fused", "nccl"], default="fused",
-                    help="config4: reduction of the row-split layers (fused into the GEMM, or NCCL)")
+    ap.add_argument("--no-tp1024", action="store_true", help="skip the 1024^2 tensor-parallel leg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1219,9 +1447,7 @@ def main():
               "impl": "reference", "unavailable": "the reference has no FP8 path (its quantised linears are INT8, "
                                                   "cublas_ops.cuh:294-791); its bf16 block code is the config2 "
                                                   "reference arm"})),
-          ("reference", "config4"): lambda a: print(json.dumps({
-              "impl": "reference", "unavailable": "the reference has no tensor-parallel path; its single-GPU "
-                                                  "block code is the config2 reference arm"}))}
+          ("reference", "config4"): run_reference_config4}
     fn[(args.impl, args.workload)](args)
 
 

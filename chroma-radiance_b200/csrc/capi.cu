@@ -715,8 +715,12 @@ b2g_status b2g_check_device_error(int* code) {
   if (v != 0) {
     const int zero = 0;
     cudaMemcpy(dev->err_word, &zero, sizeof(int), cudaMemcpyHostToDevice);
-    return set_error(B2G_ERR_DEVICE_TIMEOUT, "a tensor-core kernel gave up waiting on its pipeline (code " +
-                                                 std::to_string(v) + ")");
+    std::string who;
+    const char* names[] = {"TMA producer", "MMA issuer", "epilogue", "tensor-parallel barrier (another rank)"};
+    for (int b = 0; b < 4; ++b)
+      if (v & (1 << b)) who += (who.empty() ? "" : ", ") + std::string(names[b]);
+    return set_error(B2G_ERR_DEVICE_TIMEOUT, "a kernel gave up on a bounded wait (code " + std::to_string(v) +
+                                                 ": " + (who.empty() ? "unknown" : who) + ")");
   }
   return B2G_OK;
 }

@@ -21,6 +21,10 @@ the CPU tests substitute an fp32 torch stand-in with gloo ranks to check the sha
 """
 from __future__ import annotations
 
+import collections
+import datetime
+import threading
+import time
 from dataclasses import dataclass
 
 import torch
@@ -38,14 +42,127 @@ class Dims:
     mlp: int = MLP
 
 
+# ---------------------------------------------------------------------------- failure handling
+# The reference is single-GPU and exits on any error; the tensor-parallel path adds ranks that
+# can fail independently.  Three layers keep a failure from turning into a hang:
+#   * on the device, every wait of the engine's kernels (pipeline barriers, the cross-rank
+#     barrier kernel) gives up after 2 s and reports through b2g_check_device_error;
+#   * between steps, StepWatch: each rank posts its step number to the process group's store
+#     and checks that every peer reached the previous one before launching the next, so a rank
+#     that left is noticed on the host before any kernel waits for it;
+#   * for NCCL collectives, a non-blocking communicator (nccl_options) and CollectiveWatchdog,
+#     a host thread that aborts the communicator (ncclCommAbort) when a collective outlives its
+#     deadline, so the pending all-reduce ends with an error instead of waiting for good.
+
+
+class RankLost(RuntimeError):
+    """A peer rank did not reach a step within the deadline (it left or stalled)."""
+
+
+class CollectiveTimeout(RuntimeError):
+    """A collective did not complete within the watchdog's deadline; its group was aborted."""
+
+
+class StepWatch:
+    """Host-side liveness check between tensor-parallel steps over a c10d store.
+
+    arrive(step) posts this rank's arrival at `step`; check(step) waits (at most `timeout_s`)
+    until every rank has posted `step` and raises RankLost naming the ranks that have not."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "b2g/step"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout = datetime.timedelta(seconds=timeout_s)
+        self.prefix = prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def arrive(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), "1")
+
+    def check(self, step: int) -> None:
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.timeout)
+        except Exception as e:  # the store raises on timeout; name who is missing
+            missing = [r for r, k in enumerate(keys) if not self.store.check([k])]
+            raise RankLost(f"rank(s) {missing} did not reach step {step} within "
+                           f"{self.timeout.total_seconds():.1f} s") from e
+
+
+def nccl_options(blocking: bool = False):
+    """ProcessGroupNCCL options with a non-blocking communicator (ncclCommInitRankConfig with
+    blocking = 0): NCCL calls return at once, and an abort can end an in-flight collective."""
+    import torch.distributed as dist
+
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.config.blocking = 1 if blocking else 0
+    return opts
+
+
+class CollectiveWatchdog:
+    """Tracks asynchronous collectives (objects with is_completed()) and calls `abort` once
+    when one has been outstanding longer than `deadline_s`; the next track()/check() then
+    raises CollectiveTimeout.  `poll()` does one pass (tests drive it with their own clock);
+    start() runs it every `poll_s` seconds in a daemon thread."""
+
+    def __init__(self, abort, deadline_s: float = 30.0, poll_s: float = 0.005, clock=time.monotonic):
+        self.abort, self.deadline, self.poll_s, self.clock = abort, deadline_s, poll_s, clock
+        self.pending = collections.deque()
+        self.error: CollectiveTimeout | None = None
+        self._lock = threading.Lock()
+        self._stop = threading.Event()
+        self._thread = None
+
+    def track(self, work, label: str = "collective"):
+        self.check()
+        with self._lock:
+            self.pending.append((work, self.clock(), label))
+        return work
+
+    def check(self) -> None:
+        if self.error is not None:
+            raise self.error
+
+    def poll(self) -> None:
+        with self._lock:
+            while self.pending and self.pending[0][0].is_completed():
+                self.pending.popleft()
+            late = next(((lab, t) for w, t, lab in self.pending
+                         if not w.is_completed() and self.clock() - t > self.deadline), None)
+            if late is None or self.error is not None:
+                return
+            self.error = CollectiveTimeout(f"{late[0]} did not complete within {self.deadline:.1f} s; "
+                                           f"the process group was aborted")
+            self.pending.clear()
+        self.abort()
+
+    def _run(self) -> None:
+        while not self._stop.wait(self.poll_s):
+            self.poll()
+
+    def start(self) -> "CollectiveWatchdog":
+        self._thread = threading.Thread(target=self._run, name="b2g-collective-watchdog", daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+
 class EngineOps:
     """The product path: libb2g's tensor-core GEMMs, fused attention and bias/gate kernel,
-    and an all-reduce over the default process group (NCCL on GPUs)."""
+    and an all-reduce over the default process group (NCCL on GPUs).  With a watchdog, each
+    all-reduce is issued asynchronously and tracked, so a collective that never completes
+    aborts the group instead of hanging the step."""
 
-    def __init__(self):
+    def __init__(self, watchdog: CollectiveWatchdog | None = None):
         import b2g
 
         self.b2g = b2g
+        self.watchdog = watchdog
 
     def gemm_group(self, problems):
         return self.b2g.gemm_group(problems)
@@ -66,7 +183,10 @@ class EngineOps:
         import torch.distributed as dist
 
         if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
-            dist.all_reduce(t)
+            if self.watchdog is None:
+                dist.all_reduce(t)
+            else:
+                self.watchdog.track(dist.all_reduce(t, async_op=True), "all_reduce")
 
 
 @dataclass
@@ -150,8 +270,12 @@ class TPScratch:
         self.cat = torch.empty((L, HDl + ml), dtype=torch.bfloat16, device=dev)
 
 
+def _no_mark(label: str) -> None:
+    pass
+
+
 def _qkv_attention_double(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, pe, mask,
-                          s: TPScratch) -> None:
+                          s: TPScratch, mark=_no_mark) -> None:
     """The rank's heads: qkv projections with qk_norm and RoPE in the epilogue (txt rows take
     pe rows [0, T), img rows [T, L)), then attention over the txt + img sequence into s.attn."""
     T, HDl = txt_mod1.shape[0], s.HDl
@@ -159,8 +283,10 @@ def _qkv_attention_double(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, t
                        q_norm=txt_w.q_norm, k_norm=txt_w.k_norm),
                   dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:], pe=pe[T:],
                        q_norm=img_w.q_norm, k_norm=img_w.k_norm)], s.hl)
+    mark("double.qkv")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.attn)
+    mark("double.attention")
 
 
 def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, txt_mod2, img_mod2, txt,
@@ -250,9 +376,15 @@ class SymmetricComm:
             d.counter_slots = self.COUNTER_SLOTS
             self.desc[name] = d
 
-    def reduce(self, which: str, problems: list[dict], row0: list[int]) -> None:
+    def reduce(self, which: str, problems: list[dict], row0: list[int], mark=None, label: str = "") -> None:
+        """One row-split layer with its all-rank reduction fused into the GEMM, then the
+        cross-rank barrier.  `mark(label)`, when given, is called after each of the two."""
         self.b2g.gemm_tp_reduce(problems, row0, self.desc[which])
+        if mark:
+            mark(label)
         self.barrier()
+        if mark:
+            mark(label + ".barrier")
 
     def barrier(self) -> None:
         """All ranks' fused layers are done (bounded wait in libb2g's own barrier kernel)."""
@@ -262,26 +394,35 @@ class SymmetricComm:
 
 def tp_double_block_fused(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1,
                           img_mod1, txt_mod2, img_mod2, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask,
-                          s: TPScratch) -> None:
+                          s: TPScratch, mark=None) -> None:
     """tp_double_block with each row-split layer's all-reduce fused into its GEMM: the
-    replicated txt and img streams are comm.res_double[:T] and [T:]."""
+    replicated txt and img streams are comm.res_double[:T] and [T:].  `mark(label)`, when
+    given, is called after every launch (for timing events between them)."""
     T, HDl = txt_mod1.shape[0], s.HDl
-    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s)
+    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s, mark or _no_mark)
     comm.reduce("double", [dict(x=s.attn[:T], w=txt_w.proj_w, bias=txt_w.proj_b, gate=txt_gate1),
-                           dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, gate=img_gate1)], [0, T])
+                           dict(x=s.attn[T:], w=img_w.proj_w, bias=img_w.proj_b, gate=img_gate1)], [0, T],
+                mark, "double.proj")
     ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
                     dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
+    (mark or _no_mark)("double.mlp0")
     comm.reduce("double", [dict(x=s.h_txt, w=txt_w.mlp2_w, bias=txt_w.mlp2_b, gate=txt_gate2),
-                           dict(x=s.h_img, w=img_w.mlp2_w, bias=img_w.mlp2_b, gate=img_gate2)], [0, T])
+                           dict(x=s.h_img, w=img_w.mlp2_w, bias=img_w.mlp2_b, gate=img_gate2)], [0, T],
+                mark, "double.mlp2")
 
 
-def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, gate, pe, mask, s: TPScratch) -> None:
+def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, gate, pe, mask, s: TPScratch,
+                          mark=None) -> None:
     """tp_single_block with linear2's all-reduce fused into its GEMM: the replicated stream is
-    comm.res_single."""
+    comm.res_single.  `mark` as in tp_double_block_fused."""
     HDl = s.HDl
+    mk = mark or _no_mark
     ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
                        q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
+    mk("single.linear1_qkv")
     ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
+    mk("single.linear1_mlp")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
-    comm.reduce("single", [dict(x=s.cat, w=w.linear2_w, bias=w.linear2_b, gate=gate)], [0])
+    mk("single.attention")
+    comm.reduce("single", [dict(x=s.cat, w=w.linear2_w, bias=w.linear2_b, gate=gate)], [0], mark, "single.linear2")

@@ -28,9 +28,9 @@ def test_bench_help_lists_workloads():
 
 
 def test_reference_arm_without_gpu_reports_unavailable_or_runs():
-    """The config4 and config5 reference arms have no counterpart in the reference (no TP, no
-    FP8 path): one JSON line saying so."""
-    for w in ("config4", "config5"):
+    """Without a GPU the reference arms print one `unavailable` JSON line (the reference's path
+    is GPU code only; config5 has no counterpart at all: no FP8 path)."""
+    for w in ("config2", "config4", "config5"):
         r = subprocess.run([sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--workload", w],
                            capture_output=True, text=True, timeout=120)
         assert r.returncode == 0
