@@ -137,9 +137,12 @@ def _fresh_process_worker() -> int:
     torch.cuda.synchronize()
     free2 = torch.cuda.mem_get_info()[0]
     assert free2 < free1, "b2g_gemm was expected to allocate its workspace in a fresh process"
-    assert rel_err(got.cpu().numpy(), want.cpu().numpy()) <= 1e-6
+    # b2g_gemm summed K in 4 split parts, the no-alloc call in one: fp32 accumulation order
+    # differs, so the tolerance is the F32-output one of the GEMM tests (1e-4 of max|ref|).
+    err = rel_err(got.cpu().numpy(), want.cpu().numpy())
+    assert err <= 1e-4, err
     b2g.check_device_error()
-    print("no-alloc fresh process ok", free0 - free2)
+    print("no-alloc fresh process ok", free0 - free2, err)
     return 0
 
 
