@@ -29,11 +29,11 @@ F32, F16, BF16, E4M3 = 0, 1, 2, 3
 # cudaDataType_t values used by linear_lt's signature
 CUDA_R_32F, CUDA_R_16F, CUDA_R_16BF = 0, 2, 14
 # b2g_epilogue
-EPI_NONE, EPI_GELU, EPI_GATED_RESIDUAL = 0, 1, 2
+EPI_NONE, EPI_GELU, EPI_GATED_RESIDUAL, EPI_SILU = 0, 1, 2, 3
 
 _TORCH_TO_B2G = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
 _TORCH_TO_CUDA = {torch.float32: CUDA_R_32F, torch.float16: CUDA_R_16F, torch.bfloat16: CUDA_R_16BF}
-_EPILOGUES = {"none": EPI_NONE, "gelu": EPI_GELU, "gated_residual": EPI_GATED_RESIDUAL}
+_EPILOGUES = {"none": EPI_NONE, "gelu": EPI_GELU, "gated_residual": EPI_GATED_RESIDUAL, "silu": EPI_SILU}
 
 
 class B2GError(RuntimeError):
@@ -105,6 +105,22 @@ _SIGNATURES = {
                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
                                    ctypes.c_int64], ctypes.c_int),
     "b2g_batched_matmul_Bt": ([ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4, ctypes.c_int),
+    "b2g_batched_matmul_Bt_stream": ([ctypes.c_void_p] * 3 + [ctypes.c_int64] * 4 + [ctypes.c_void_p], ctypes.c_int),
+    "b2g_patchify_bf16": ([ctypes.c_void_p] + [ctypes.c_int] * 4 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p],
+                          ctypes.c_int),
+    "b2g_timestep_vec": ([ctypes.c_void_p, ctypes.c_float, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p],
+                         ctypes.c_int),
+    "b2g_rms_norm": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                      ctypes.c_int64, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p], ctypes.c_int),
+    "b2g_nerf_input_bf16": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                             ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
+    "b2g_nerf_glu_weights": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64] + [ctypes.c_void_p] * 4, ctypes.c_int),
+    "b2g_convert_f32": ([ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
+                                                                 ctypes.c_void_p], ctypes.c_int),
+    "b2g_silu_mul": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
+    "b2g_add_inplace": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
+    "b2g_nerf_final": ([ctypes.c_void_p] * 5 + [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
     "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
@@ -228,7 +244,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, out
     """out[M, N] = epilogue(x[M, K] . w[N, K]^T + bias) on the tensor-core path.
 
     x, w: 2-D, unit stride along K (row strides may exceed K).  epilogue: "none", "gelu"
-    (tanh GELU) or "gated_residual" (out is an F32 residual updated in place:
+    (tanh GELU), "silu" or "gated_residual" (out is an F32 residual updated in place:
     out += gate * (x.w^T + bias)).  Runs on `stream` (default: torch's current stream).
     """
     lib = load()
@@ -678,8 +694,11 @@ def modulate_to_e4m3(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, 
     return codes, rs
 
 
-def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None:
-    """batched_matmul_Bt (cublas_ops.cuh:558): C[b] = A[b] . B[b]^T, F32, operands rounded to bf16."""
+def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                      stream: torch.cuda.Stream | None = None) -> None:
+    """batched_matmul_Bt (cublas_ops.cuh:558): C[b] = A[b] . B[b]^T, F32, operands rounded to TF32
+    (as cuBLAS runs the reference's CUBLAS_COMPUTE_32F_FAST_16BF on B200), fp32 accumulation.
+    On `stream` (default: torch's current stream)."""
     lib = load()
     _require_cuda(A, B, C)
     if A.dim() != 3 or B.dim() != 3 or C.dim() != 3:
@@ -690,7 +709,9 @@ def batched_matmul_Bt(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor) -> None
         raise B2GError("batched_matmul_Bt: shape mismatch")
     if not all(t.dtype == torch.float32 and t.is_contiguous() for t in (A, B, C)):
         raise B2GError("batched_matmul_Bt: contiguous F32 tensors expected")
-    _check(lib.b2g_batched_matmul_Bt(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, K, N))
+    s = (stream or torch.cuda.current_stream(A.device)).cuda_stream
+    _check(lib.b2g_batched_matmul_Bt_stream(A.data_ptr(), B.data_ptr(), C.data_ptr(), batch, M, K, N,
+                                            ctypes.c_void_p(s)))
 
 
 def modulate_streams(x: torch.Tensor, txt_shift: torch.Tensor, txt_scale: torch.Tensor, img_shift: torch.Tensor,
@@ -728,3 +749,98 @@ def compact_rope_table(pe: torch.Tensor) -> torch.Tensor | None:
     if not (torch.equal(p[..., 0], p[..., 3]) and torch.equal(p[..., 1], -p[..., 2])):
         return None
     return torch.stack([p[..., 0], p[..., 2]], -1).contiguous()
+
+
+# ---------------------------------------------------------------------------- rest of the step
+def _stream(t: torch.Tensor, stream: torch.cuda.Stream | None) -> ctypes.c_void_p:
+    return ctypes.c_void_p((stream or torch.cuda.current_stream(t.device)).cuda_stream)
+
+
+def patchify_bf16(x: torch.Tensor, p: int, out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """im2col of conv2d_img_in + linear()'s cast (chroma.cuh:1311-1327): x F32 [C, H, W] (or
+    [1, C, H, W]) -> out bf16 [(H/p)(W/p), >= C*p*p]."""
+    _require_cuda(x, out)
+    C, H, W = x.shape[-3:]
+    if x.dtype != torch.float32 or not x.is_contiguous() or out.dtype != torch.bfloat16 or out.stride(1) != 1:
+        raise B2GError("patchify_bf16: contiguous F32 image and a bf16 output with unit column stride")
+    _check(load().b2g_patchify_bf16(x.data_ptr(), C, H, W, p, out.data_ptr(), out.stride(0), _stream(x, stream)))
+    return out
+
+
+def timestep_vec(timestep: torch.Tensor, guidance: float, out: torch.Tensor,
+                 stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """compute_modulation's approximator input (chroma.cuh:467-505) into out F32 [rows, 64];
+    timestep: a one-element F32 device tensor."""
+    _require_cuda(timestep, out)
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.shape[-1] != 64:
+        raise B2GError("timestep_vec: contiguous F32 [rows, 64] output")
+    _check(load().b2g_timestep_vec(timestep.data_ptr(), float(guidance), out.data_ptr(), out.shape[0],
+                                   _stream(out, stream)))
+    return out
+
+
+def rms_norm(x: torch.Tensor, scale: torch.Tensor, out: torch.Tensor, eps: float = 1e-6,
+             stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """rms_norm_cuda (kernels.cu:174-212) over the last dim of x [rows, C] (F32, row stride any)
+    into out (F32 or bf16)."""
+    _require_cuda(x, scale, out)
+    rows, C = x.shape
+    if x.dtype != torch.float32 or x.stride(1) != 1 or out.stride(1) != 1 or out.shape != x.shape:
+        raise B2GError("rms_norm: F32 x and an output of the same shape, unit column strides")
+    _check(load().b2g_rms_norm(x.data_ptr(), x.stride(0), scale.data_ptr(), out.data_ptr(), _operand_dtype(out),
+                               out.stride(0), rows, C, eps, _stream(x, stream)))
+    return out
+
+
+def nerf_input_bf16(x: torch.Tensor, dct: torch.Tensor, out: torch.Tensor,
+                    stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """The NeRF embedder's input rows [pixel rgb | DCT features | zeros] (chroma.cuh:1170-1200)."""
+    _require_cuda(x, dct, out)
+    H, W = x.shape[-2:]
+    _check(load().b2g_nerf_input_bf16(x.data_ptr(), dct.data_ptr(), H, W, out.data_ptr(), out.stride(0),
+                                      _stream(x, stream)))
+    return out
+
+
+def nerf_glu_weights(params: torch.Tensor, gate: torch.Tensor, value: torch.Tensor, fc2: torch.Tensor,
+                     stream: torch.cuda.Stream | None = None) -> None:
+    """slice_transpose + l2_norm of one NeRF GLU block's generated weights (chroma.cuh:1264-1281):
+    params F32 [P, 49152] -> gate, value [P, 256, 64], fc2 [P, 64, 256]."""
+    _require_cuda(params, gate, value, fc2)
+    _check(load().b2g_nerf_glu_weights(params.data_ptr(), params.stride(0), params.shape[0], gate.data_ptr(),
+                                       value.data_ptr(), fc2.data_ptr(), _stream(params, stream)))
+
+
+def convert_f32(src: torch.Tensor, out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """out (bf16 or fp16) = src (F32 [rows, cols]) rounded to nearest, as linear() casts
+    activations (f32_to_bf16_cuda); unit column strides, any row strides."""
+    _require_cuda(src, out)
+    if src.dtype != torch.float32 or src.shape != out.shape or src.stride(1) != 1 or out.stride(1) != 1:
+        raise B2GError("convert_f32: F32 source and an output of the same 2-D shape")
+    _check(load().b2g_convert_f32(src.data_ptr(), src.stride(0), src.shape[0], src.shape[1], out.data_ptr(),
+                                  _operand_dtype(out), out.stride(0), _stream(src, stream)))
+    return out
+
+
+def silu_mul(a: torch.Tensor, b: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+    """a = silu(a) * b (silu_mul_cuda), F32, contiguous."""
+    _require_cuda(a, b)
+    _check(load().b2g_silu_mul(a.data_ptr(), b.data_ptr(), a.numel(), _stream(a, stream)))
+
+
+def add_inplace(x: torch.Tensor, y: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+    """x += y (add_cuda), F32, contiguous."""
+    _require_cuda(x, y)
+    _check(load().b2g_add_inplace(x.data_ptr(), y.data_ptr(), x.numel(), _stream(x, stream)))
+
+
+def nerf_final(feat_cond: torch.Tensor, feat_uncond: torch.Tensor | None, norm_scale: torch.Tensor,
+               conv_w: torch.Tensor, conv_b: torch.Tensor, cfg_scale: float, H: int, W: int, tmp: torch.Tensor,
+               out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """NeRF final layer of both guidance halves + cfg_blend (chroma.cuh:1225-1250, 1581) into out
+    F32 [3, H, W]; tmp F32 scratch of halves * H * W * 64 floats."""
+    _require_cuda(feat_cond, norm_scale, conv_w, conv_b, tmp, out)
+    _check(load().b2g_nerf_final(feat_cond.data_ptr(), _ptr(feat_uncond), norm_scale.data_ptr(), conv_w.data_ptr(),
+                                 conv_b.data_ptr(), float(cfg_scale), H, W, tmp.data_ptr(), out.data_ptr(),
+                                 _stream(out, stream)))
+    return out

@@ -247,21 +247,37 @@ def _no_mark(label: str) -> None:
 DOUBLE_BLOCKS, SINGLE_BLOCKS = 19, 38  # Chroma's layout (chroma.cuh:1499-1584)
 
 
+def single_mods(mods: torch.Tensor, i: int) -> torch.Tensor:
+    """Rows (shift, scale, gate) of single block i in the approximator's output: 3i
+    (chroma.cuh:980-984)."""
+    return mods[3 * i:3 * i + 3]
+
+
+def double_mods(mods: torch.Tensor, i: int, n_double: int, n_single: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rows (shift1, scale1, gate1, shift2, scale2, gate2) of double block i, txt then img, in the
+    approximator's output: img at 6i + 3*n_single, txt at 6i + 6*n_double + 3*n_single
+    (chroma.cuh:535-553)."""
+    img = 6 * i + 3 * n_single
+    txt = 6 * i + 6 * n_double + 3 * n_single
+    return mods[txt:txt + 6], mods[img:img + 6]
+
+
 @dataclass
 class PassWeights:
     """Weights of every block of one transformer pass, and the modulation vectors the
-    approximator would produce for it: per double block and stream [6, 3072] F32 (shift1,
-    scale1, gate1, shift2, scale2, gate2), per single block [3, 3072] (shift, scale, gate)."""
+    approximator produces for it, in its own row order (single_mods, double_mods): per double
+    block and stream 6 rows (shift1, scale1, gate1, shift2, scale2, gate2), per single block 3
+    (shift, scale, gate)."""
     double: list          # [(txt StreamWeights, img StreamWeights)]
     single: list          # [SingleWeights]
-    mods: torch.Tensor    # [DOUBLE_BLOCKS * 2 * 6 + SINGLE_BLOCKS * 3, 3072] F32
+    mods: torch.Tensor    # [SINGLE_BLOCKS * 3 + DOUBLE_BLOCKS * 12 (+ unused rows), 3072] F32
 
 
 def random_pass(gen: torch.Generator, dev, n_double: int = DOUBLE_BLOCKS, n_single: int = SINGLE_BLOCKS) -> PassWeights:
     """Random-init weights of a whole pass (about 17 GB of bf16 for Chroma's 19 + 38 blocks)."""
     double = [(random_stream(gen, dev), random_stream(gen, dev)) for _ in range(n_double)]
     single = [random_single(gen, dev) for _ in range(n_single)]
-    return PassWeights(double, single, mods=torch.zeros((n_double * 12 + n_single * 3, HIDDEN), device=dev))
+    return PassWeights(double, single, mods=torch.zeros((n_single * 3 + n_double * 12, HIDDEN), device=dev))
 
 
 class PassScratch(Scratch):
@@ -291,16 +307,16 @@ def forward_pass(pw: PassWeights, x, pe, mask, s: PassScratch, T: int) -> None:
     imgs = [x[b * L + T:(b + 1) * L] for b in range(B)]
     mod_t = [s.mod[b * L:b * L + T] for b in range(B)]
     mod_i = [s.mod[b * L + T:(b + 1) * L] for b in range(B)]
+    nd, ns = len(pw.double), len(pw.single)
     for i, (tw, iw) in enumerate(pw.double):
-        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        mt, mi = double_mods(pw.mods, i, nd, ns)
         # both streams of every half in one launch (each row as modulate_to_bf16 writes it)
         b2g.modulate_streams(x, mt[0], mt[1], mi[0], mi[1], L, T, out=s.mod[:B * L])
         double_block_attention(tw, iw, mod_t, mod_i, txts, imgs, mt[2], mi[2], pe, mask, s)
         b2g.modulate_streams(x, mt[3], mt[4], mi[3], mi[4], L, T, out=s.mod[:B * L])
         double_block_mlp(tw, iw, mod_t, mod_i, txts, imgs, mt[5], mi[5], s)
-    base = 12 * len(pw.double)
     for i, sw in enumerate(pw.single):
-        m = pw.mods[base + 3 * i:base + 3 * i + 3]
+        m = single_mods(pw.mods, i)
         b2g.modulate_to_bf16(x, m[0], m[1], out=s.mod[:B * L])
         single_block(sw, s.mod[:B * L], x, m[2], pe, mask, s)
 
@@ -538,14 +554,14 @@ def forward_pass_fp8(pw: PassWeightsFP8, x, pe, mask, s: ScratchFP8, T: int) -> 
         b2g.modulate_to_e4m3(src, shift, scale, out=dst.q, scales=dst.s)
 
     x8 = s.mod8.rows(0, B * L)
+    nd, ns = len(pw.double), len(pw.single)
     for i, (tw, iw) in enumerate(pw.double):
-        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        mt, mi = double_mods(pw.mods, i, nd, ns)
         b2g.modulate_streams(x, mt[0], mt[1], mi[0], mi[1], L, T, out=x8.q, scales=x8.s, fp8=True)
         double_block_attention_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[2], mi[2], pe, mask, s)
         b2g.modulate_streams(x, mt[3], mt[4], mi[3], mi[4], L, T, out=x8.q, scales=x8.s, fp8=True)
         double_block_mlp_fp8(tw, iw, mod_t, mod_i, txts, imgs, mt[5], mi[5], s)
-    base = 12 * len(pw.double)
     for i, sw in enumerate(pw.single):
-        m = pw.mods[base + 3 * i:base + 3 * i + 3]
+        m = single_mods(pw.mods, i)
         modulate(x, m[0], m[1], x8)
         single_block_fp8(sw, x8, x, m[2], pe, mask, s)

@@ -29,6 +29,11 @@ NVCC_FLAGS = ARCH + [
 ]
 
 
+# Per-file extra flags.  model_fastmath.cu reproduces a computation the reference compiles with
+# --use_fast_math, and has to be built the same way to give the same values.
+FILE_FLAGS = {"model_fastmath.cu": ["--use_fast_math"]}
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
         if cand and Path(cand).exists():
@@ -59,7 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     for src in sources():
         obj = BUILD / (src.stem + ".o")
         if force or _stale(obj, [src] + hdrs):
-            cmd = [nvcc()] + NVCC_FLAGS + ["-c", str(src), "-o", str(obj)]
+            cmd = [nvcc()] + NVCC_FLAGS + FILE_FLAGS.get(src.name, []) + ["-c", str(src), "-o", str(obj)]
             jobs.append((src, obj, cmd))
 
     def run(job):

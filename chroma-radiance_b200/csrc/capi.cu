@@ -199,7 +199,7 @@ b2g_status desc_to_problem(const b2g_gemm_desc* d, const char* who, GemmProblem*
   if (d->ldd < d->N) return set_error(B2G_ERR_INVALID, w + ": ldd < N");
   if (d->epilogue == B2G_EPI_GATED_RESIDUAL && (!d->gate || d->d_dtype != B2G_F32))
     return set_error(B2G_ERR_INVALID, w + ": gated residual needs a gate and an F32 output");
-  if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_GATED_RESIDUAL)
+  if (d->epilogue < B2G_EPI_NONE || d->epilogue > B2G_EPI_SILU)
     return set_error(B2G_ERR_UNSUPPORTED, w + ": unknown epilogue");
   if (d->a_dtype == B2G_E4M3 || d->b_dtype == B2G_E4M3 || d->d_dtype == B2G_E4M3)
     return set_error(B2G_ERR_UNSUPPORTED, w + ": E4M3 operands are not implemented");
@@ -507,8 +507,24 @@ b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type, const
   return b2g_gemm(&d, nullptr);
 }
 
+b2g_status b2g_convert_f32(const float* src, int64_t lds, int64_t rows, int64_t cols, void* dst, b2g_dtype dst_dtype,
+                           int64_t ldd, void* stream) {
+  if (rows <= 0 || cols <= 0) return B2G_OK;
+  if (!src || !dst || lds < cols || ldd < cols || (dst_dtype != B2G_BF16 && dst_dtype != B2G_F16))
+    return set_error(B2G_ERR_INVALID, "b2g_convert_f32: arguments");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  return cast_f32_to_16(src, dst, dst_dtype, 1, rows, cols, lds, 0, ldd, 0, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
                                  int64_t N) {
+  return b2g_batched_matmul_Bt_stream(A, B, C, batch, M, K, N, nullptr);
+}
+
+b2g_status b2g_batched_matmul_Bt_stream(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
+                                        int64_t N, void* stream) {
   if (batch < 0 || M < 0 || K < 0 || N < 0) return set_error(B2G_ERR_INVALID, "b2g_batched_matmul_Bt: negative size");
   if (batch == 0 || M == 0 || N == 0) return B2G_OK;
   if (!A || !B || !C) return set_error(B2G_ERR_INVALID, "b2g_batched_matmul_Bt: null operand");
@@ -519,7 +535,7 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C, int64
   // to nearest even), TF32 products, fp32 accumulation -> kind::tf32 tensor-core MMAs.  With
   // 16-byte operand rows (K % 4 == 0, aligned bases) the operands go to the kernel as they are
   // and it rounds each shared-memory stage; otherwise a pass rounds them into padded copies.
-  cudaStream_t st = nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   GemmProblem p;
   p.M = M; p.N = N; p.K = K; p.batch = batch;
   p.d = C; p.d_dtype = B2G_F32; p.ldd = N; p.d_bstride = M * N;

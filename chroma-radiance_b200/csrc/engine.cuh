@@ -41,7 +41,7 @@ struct GemmProblem {
 
 // Internal epilogue: D = [q | k | v] (N = 3 * heads * 128, bf16 out) with per-head RMSNorm
 // (when scales are given) and RoPE applied to the q and k heads inside the GEMM.
-constexpr int kEpiQkvRope = 4;
+constexpr int kEpiQkvRope = 17;
 struct QkvRope {
   int64_t heads = 0;                // H; head_dim is 128
   float eps = 1e-6f;
@@ -56,7 +56,7 @@ struct QkvRope {
 
 // Internal epilogue: bf16 partial -> all-rank sum (fixed rank order) -> residual += gate *
 // (sum + bias), the residual updated in every rank's copy.  All buffers are peer-mapped.
-constexpr int kEpiTpReduce = 3;
+constexpr int kEpiTpReduce = 16;
 struct TpReduce {
   int world, rank;
   void* const* part_ptrs;   // device array [world]: each rank's bf16 partial buffer [rows, ld_part]

@@ -40,6 +40,8 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return 0.5f * v * (1.0f + tanhf(inner));
 }
 
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
 // 64x64 output tile per 256-thread block, 4x4 outputs per thread, K staged 16 at a time.
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
   __shared__ float As[kTileK][kTile + 4];
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p) {
       else if (p.bias_kind == 2) v += __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[n]);
       const long long o = dbase + static_cast<long long>(m) * p.ldd + n;
       if (p.epilogue == B2G_EPI_GELU) v = gelu_tanh(v);
+      if (p.epilogue == B2G_EPI_SILU) v = silu(v);
       if (p.epilogue == B2G_EPI_GATED_RESIDUAL) {
         float* dp = static_cast<float*>(p.d);
         dp[o] = dp[o] + p.gate[n] * v;

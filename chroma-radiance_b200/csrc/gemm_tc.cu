@@ -213,7 +213,14 @@ __device__ __forceinline__ float gelu_tanh(float v) {
   return __fdividef(v, 1.0f + e);
 }
 
-// alpha * acc + bias (bias staged in shared memory, zero past N), then GELU if asked.
+// SiLU, the formula of the reference's silu_val (kernels.cu): v / (1 + e^-v), with e^-v from
+// the hardware base-2 exponential (capped at 2^126, where the quotient is -0 to fp32
+// precision) and a fast division.
+__device__ __forceinline__ float silu_fast(float v) {
+  return __fdividef(v, 1.0f + fast_exp2(fminf(-1.4426950408889634f * v, 126.0f)));
+}
+
+// alpha * acc + bias (bias staged in shared memory, zero past N), then GELU or SiLU if asked.
 template <int EPI>
 __device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], const float* sb, float alpha, float (&v)[32]) {
 #pragma unroll
@@ -235,6 +242,10 @@ __device__ __forceinline__ void chunk_values(const uint32_t (&r)[32], const floa
   if constexpr (EPI == B2G_EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  }
+  if constexpr (EPI == B2G_EPI_SILU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu_fast(v[j]);
   }
 }
 
@@ -1345,6 +1356,13 @@ b2g_status dispatch_out(const TcMaps& maps, const TcParams& prm, int grid, b2g_e
     if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F32, KIND>(maps, prm, grid, st);
     if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_BF16, KIND>(maps, prm, grid, st);
     return launch_one<PAIR, BN, STAGES, B2G_EPI_GELU, OUT_F16, KIND>(maps, prm, grid, st);
+  }
+  if constexpr (KIND == 0) {
+    if (epi == B2G_EPI_SILU) {
+      if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_SILU, OUT_F32, KIND>(maps, prm, grid, st);
+      if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_SILU, OUT_BF16, KIND>(maps, prm, grid, st);
+      return launch_one<PAIR, BN, STAGES, B2G_EPI_SILU, OUT_F16, KIND>(maps, prm, grid, st);
+    }
   }
   if (out == B2G_F32) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_F32, KIND>(maps, prm, grid, st);
   if (out == B2G_BF16) return launch_one<PAIR, BN, STAGES, B2G_EPI_NONE, OUT_BF16, KIND>(maps, prm, grid, st);

@@ -1,8 +1,9 @@
 // ab_check.cu — compiled inside the reference tree by build_reference_with_b2g.sh.  It
-// includes the reference's model headers unchanged (through the drop-in cublas_ops.cuh),
-// then runs each routed GEMM entry point twice on the same device buffers: once through the
-// engine (the names the model code calls) and once through the original cuBLASLt code
-// (renamed ref_cublaslt_*), and prints max|diff|/max|ref| per entry point.
+// includes the reference's model headers unchanged (through the drop-in cublas_ops.cuh,
+// cudnn_attention.cuh and attention.cuh), then runs each routed entry point twice on the
+// same device buffers: once through the engine (the names the model code calls) and once
+// through the original code (renamed ref_cublaslt_*, ref_cudnn_attention_with_rope,
+// ref_cublas_t5_attention), and prints max|diff|/max|ref| per entry point.
 #include <functional>
 #include "tensor.cuh"
 #include "cublas_ops.cuh"
@@ -71,6 +72,35 @@ int main() {
     linear_gated_residual(x, w, &b, r1.f32(), g.f32(), 1024, 3072);
     ref_cublaslt_linear_gated_residual(x, w, &b, r2.f32(), g.f32(), 1024, 3072);
     report("linear_gated_residual", rel_diff(r1, r2), 2e-3);
+  }
+  // cudnn_attention_with_rope (the double block's attention at 512^2, F32 Q/K/V, RoPE table
+  // and a key mask): engine kernel against the original cuDNN SDPA path
+  {
+    const int L = 1536, H = 24, D = 128;
+    Tensor q = randn({L, H, D}, DType::F32, 1.0f, 13), k = randn({L, H, D}, DType::F32, 1.0f, 14);
+    Tensor v = randn({L, H, D}, DType::F32, 1.0f, 15);
+    std::vector<int> axes = {16, 56, 56};
+    std::vector<float> pe_h = RoPE::gen_pe(512, 512, 16, 512, 10000, axes);
+    Tensor pe = Tensor::alloc({L, D / 2 * 4}, DType::F32, true);
+    CHECK_CUDA(cudaMemcpy(pe.data, pe_h.data(), pe_h.size() * 4, cudaMemcpyHostToDevice));
+    std::vector<float> mask_h(L, 0.f);
+    for (int i = 112; i < 512; ++i) mask_h[i] = -INFINITY;
+    Tensor mask = Tensor::alloc({L}, DType::F32, true);
+    CHECK_CUDA(cudaMemcpy(mask.data, mask_h.data(), L * 4, cudaMemcpyHostToDevice));
+    init_cudnn();
+    Tensor o1 = cudnn_attention_with_rope(q, k, v, pe, H, D, mask.f32());
+    Tensor o2 = ref_cudnn_attention_with_rope(q, k, v, pe, H, D, mask.f32());
+    report("cudnn_attention_with_rope", rel_diff(o1, o2), 1e-2);
+  }
+  // t5_attention (one T5-XXL layer: 512 tokens, 64 heads x 64, relative bias, scale 1)
+  {
+    const int L = 512, H = 64, D = 64;
+    Tensor q = randn({L, H, D}, DType::F32, 1.0f, 16), k = randn({L, H, D}, DType::F32, 1.0f, 17);
+    Tensor v = randn({L, H, D}, DType::F32, 1.0f, 18);
+    Tensor bias = randn({H, L, L}, DType::F32, 1.0f, 19);
+    Tensor o1 = t5_attention(q, k, v, bias.f32(), H, D, 1.0f, nullptr);
+    Tensor o2 = ref_cublas_t5_attention(q, k, v, bias.f32(), H, D, 1.0f, nullptr);
+    report("t5_attention", rel_diff(o1, o2), 2e-3);
   }
   // batched_matmul_Bt (NeRF GLU shape)
   {

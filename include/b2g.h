@@ -48,7 +48,9 @@ typedef enum {
 typedef enum {
   B2G_EPI_NONE = 0,           /* D = acc (+ bias)                                   */
   B2G_EPI_GELU = 1,           /* D = gelu_tanh(acc (+ bias))                        */
-  B2G_EPI_GATED_RESIDUAL = 2  /* D[m,n] (F32, read-modify-write) += gate[n] * (acc (+ bias)) */
+  B2G_EPI_GATED_RESIDUAL = 2, /* D[m,n] (F32, read-modify-write) += gate[n] * (acc (+ bias)) */
+  B2G_EPI_SILU = 3            /* D = silu(acc (+ bias)) = v / (1 + e^-v): the approximator's
+                                 in_layer -> silu_cuda (chroma.cuh:201-203, kernels.cu:346) */
 } b2g_epilogue;
 
 /* One GEMM with a fused epilogue.  a/b dtypes: (BF16,BF16), (F16,F16) run on the
@@ -126,6 +128,9 @@ b2g_status b2g_linear_gated_residual(const void* x, cudaDataType_t x_type,
  * reference's own outputs); this engine does the same on kind::tf32 tensor cores.  Stream 0. */
 b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
                                  int64_t batch, int64_t M, int64_t K, int64_t N);
+/* The same on an explicit stream (the NeRF decoder's GLU products inside a captured step). */
+b2g_status b2g_batched_matmul_Bt_stream(const float* A, const float* B, float* C, int64_t batch, int64_t M, int64_t K,
+                                        int64_t N, void* stream);
 
 /* out[L, n_head*d_head] (F32) = softmax(rope(Q) rope(K)^T / sqrt(d_head) + mask) V per head.
  * Q, K, V: F32 [L, n_head, d_head] (Q and K already RMS-normed), pe: F32 [L, d_head/2, 4]
@@ -134,8 +139,10 @@ b2g_status b2g_batched_matmul_Bt(const float* A, const float* B, float* C,
  *   static Tensor attention_with_rope(const Tensor& Q, const Tensor& K, const Tensor& V,
  *       const Tensor& pe, int n_head, int d_head, const float* attn_mask)  attention.cuh:23-28
  * i.e. cudnn_attention_with_rope (cudnn_attention.cuh:449-476): RoPE + bf16 operands, fp32
- * softmax, bf16 probabilities; here QK^T and PV are tcgen05 batched GEMMs.  Requires L and
- * d_head to be multiples of 8.  Uses a library workspace of about n_head*L*L*6 bytes. */
+ * softmax, bf16 probabilities.  Here a prologue kernel rotates Q and K and writes bf16 Q, K, V
+ * into a library workspace (3*L*n_head*d_head*2 bytes), then one fused tcgen05 attention
+ * kernel keeps scores and probabilities on chip (no [n_head, L, L] matrix).  d_head 64 or 128;
+ * Q, K, V and pe 16-byte aligned. */
 b2g_status b2g_attention_with_rope(const float* Q, const float* K, const float* V, const float* pe, int n_head,
                                    int d_head, int64_t L, const float* attn_mask, float* out, void* stream);
 
@@ -327,6 +334,61 @@ b2g_status b2g_modulate_streams(const float* x, const float* txt_shift, const fl
                                 const float* img_shift, const float* img_scale, int64_t seq, int64_t txt_rows,
                                 void* out, b2g_dtype out_dtype, float* row_scale, int64_t M, int64_t C, float eps,
                                 void* stream);
+
+/* ---- The rest of the denoising step (ChromaRadiance::forward_cfg, chroma.cuh:1499-1584) ----
+ * The operand producers and element-wise steps around the embedder, approximator and NeRF
+ * GEMMs; all stream-ordered on `stream`, no allocation. */
+
+/* im2col of conv2d_img_in (chroma.cuh:1311-1327, patchify_kernel kernels.cu:975-1019) fused
+ * with linear()'s F32 -> bf16 activation cast: x F32 [C, H, W] -> out bf16 [(H/p)(W/p), ldo],
+ * column c*p*p + py*p + px of patch (ph, pw) = x[c, ph*p + py, pw*p + px].  p even, H and W
+ * multiples of p, x 8-byte and out 4-byte aligned. */
+b2g_status b2g_patchify_bf16(const float* x, int C, int H, int W, int p, void* out, int64_t ldo, void* stream);
+
+/* The approximator's input of compute_modulation (chroma.cuh:467-505): rows i < rows of
+ * [timestep_embedding(*timestep, 16) | timestep_embedding(guidance, 16) |
+ *  timestep_embedding(i, 32)] with time factor 1000 and period 10000 (kernels.cu:608-631,
+ * evaluated with the same fast-math functions), F32 [rows, 64].  The timestep is read from
+ * device memory, so a captured step can be replayed at another timestep. */
+b2g_status b2g_timestep_vec(const float* timestep, float guidance, float* out, int rows, void* stream);
+
+/* rms_norm_cuda (kernels.cu:174-212): out[r, c] = x[r, c] * rsqrt(mean_c(x[r]^2) + eps) *
+ * scale[c], rows of C values (row strides ldx / ldo), F32 or BF16 out (the bf16 form is the
+ * approximator's norm followed by linear()'s cast).  C a multiple of 4, 16-byte aligned x and
+ * scale; C <= 256 and a multiple of 64 takes one warp per row. */
+b2g_status b2g_rms_norm(const float* x, int64_t ldx, const float* scale, void* out, b2g_dtype out_dtype, int64_t ldo,
+                        int64_t rows, int64_t C, float eps, void* stream);
+
+/* NeRF decoder input (nerf_decode steps 1-3, chroma.cuh:1170-1200): row patch*256 + pix =
+ * [x[0..2] at the pixel | dct[pix, 0..63] | zeros], bf16 [P*256, ldo], ldo >= 67 and a
+ * multiple of 8 (72 pads the embedder's K = 67 to 16-byte rows; its weight is padded with
+ * zero columns to match, which changes no product).  x F32 [3, H, W], dct F32 [256, 64]. */
+b2g_status b2g_nerf_input_bf16(const float* x, const float* dct, int H, int W, void* out, int64_t ldo, void* stream);
+
+/* The per-patch weights of one NeRF GLU block from its param_generator output params [P, ldp]
+ * (slice_transpose x3 + l2_norm x3, chroma.cuh:1264-1281): gate, value F32 [P, 256, 64] (the
+ * [64, 256] slices 0 and 1 transposed, rows L2-normalised), fc2 F32 [P, 64, 256] (slice 2
+ * [256, 64] transposed, rows L2-normalised), norms floored at 1e-12. */
+b2g_status b2g_nerf_glu_weights(const float* params, int64_t ldp, int64_t patches, float* gate, float* value,
+                                float* fc2, void* stream);
+
+/* dst[r, c] = round-to-nearest bf16 / fp16 of src[r, c] (f32_to_bf16_cuda / f32_to_fp16_cuda,
+ * kernels.cu:40-92, the activation cast inside linear()), rows x cols with row strides lds/ldd. */
+b2g_status b2g_convert_f32(const float* src, int64_t lds, int64_t rows, int64_t cols, void* dst, b2g_dtype dst_dtype,
+                           int64_t ldd, void* stream);
+
+/* a = silu(a) * b (silu_mul_cuda) and x += y (add_cuda), F32, n % 4 == 0, 16-byte aligned. */
+b2g_status b2g_silu_mul(float* a, const float* b, int64_t n, void* stream);
+b2g_status b2g_add_inplace(float* x, const float* y, int64_t n, void* stream);
+
+/* The NeRF final layer and the guidance blend (chroma.cuh:1225-1250, 1581): each half's decoder
+ * state feat [P, 256, 64] is un-patchified, RMS-normed over its 64 channels at every pixel
+ * (scale norm_scale, eps 1e-6) and convolved 3x3 (conv_w [3, 64, 3, 3], conv_b [3], zero
+ * padding); out F32 [3, H, W] = uncond + cfg_scale * (cond - uncond), or the conditional
+ * result alone when feat_uncond is NULL.  tmp: F32 scratch of halves * H * W * 64 floats. */
+b2g_status b2g_nerf_final(const float* feat_cond, const float* feat_uncond, const float* norm_scale,
+                          const float* conv_w, const float* conv_b, float cfg_scale, int H, int W, float* tmp,
+                          float* out, void* stream);
 
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).

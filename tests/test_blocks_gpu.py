@@ -159,13 +159,13 @@ def test_forward_pass_is_the_blocks_in_sequence(engine):
     s = blocks.PassScratch(T, I, DEV)
     txt, img = y[:T], y[T:]
     for i, (tw, iw) in enumerate(pw.double):
-        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        mt, mi = blocks.double_mods(pw.mods, i, len(pw.double), len(pw.single))
         m1t, m1i = engine.modulate_to_bf16(txt, mt[0], mt[1]), engine.modulate_to_bf16(img, mi[0], mi[1])
         blocks.double_block_attention(tw, iw, m1t, m1i, txt, img, mt[2], mi[2], pe, mask, s)
         m2t, m2i = engine.modulate_to_bf16(txt, mt[3], mt[4]), engine.modulate_to_bf16(img, mi[3], mi[4])
         blocks.double_block_mlp(tw, iw, m2t, m2i, txt, img, mt[5], mi[5], s)
     for i, sw in enumerate(pw.single):
-        m = pw.mods[24 + 3 * i:24 + 3 * i + 3]
+        m = blocks.single_mods(pw.mods, i)
         blocks.single_block(sw, engine.modulate_to_bf16(y, m[0], m[1]), y, m[2], pe, mask, s)
     torch.cuda.synchronize()
     assert torch.isfinite(x).all()
@@ -328,7 +328,7 @@ def test_short_pass_chained_vs_reference(engine, ref):
                 w.mlp2_w.data_ptr(), w.mlp2_b.data_ptr()]
 
     for i, (tw, iw) in enumerate(pw.double):
-        mt, mi = pw.mods[12 * i:12 * i + 6], pw.mods[12 * i + 6:12 * i + 12]
+        mt, mi = blocks.double_mods(pw.mods, i, len(pw.double), len(pw.single))
         ptrs = wptrs(iw) + wptrs(tw) + [m1i.data_ptr(), m1t.data_ptr(), m2i.data_ptr(), m2t.data_ptr(),
                                         img.data_ptr(), txt.data_ptr(), mi[2].data_ptr(), mt[2].data_ptr(),
                                         mi[5].data_ptr(), mt[5].data_ptr(), pe.data_ptr(), mask.data_ptr()]
@@ -339,7 +339,7 @@ def test_short_pass_chained_vs_reference(engine, ref):
         modulate(img, mi[3], mi[4], m2i)
         assert attn.double_block_mlp(ptrs, T, I) == 0
     for j, sw in enumerate(pw.single):
-        m = pw.mods[24 + 3 * j:24 + 3 * j + 3]
+        m = blocks.single_mods(pw.mods, j)
         modulate(xr, m[0], m[1], xm)
         assert attn.single_block([sw.linear1_w.data_ptr(), sw.linear1_b.data_ptr(), sw.q_norm.data_ptr(),
                                   sw.k_norm.data_ptr(), sw.linear2_w.data_ptr(), sw.linear2_b.data_ptr(),
