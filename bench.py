@@ -19,12 +19,17 @@ RoPE, QK^T and PV over 24 heads, 0/-inf key mask on 400 of the 512 text tokens).
             so they sum to the timed step (the timed graphs carry no events between launches,
             so consecutive kernels overlap their set-up and tail; the events in the copy stop
             that overlap); peak = MEASURED_PEAKS.json bf16_tflops.
-  e2e       through the public API with host buffers, the way the model runs its blocks: one
-            denoising step's 19 double + 38 single blocks (own weights, 17 GB), each block
-            modulating its inputs on the device; the hidden states and the step's modulation
-            vectors copied in from pinned host memory and the image hidden states copied back
-            inside the event pair.  e2e_block_pair is the timed block pair with all of its
-            activations copied in and out every step (PCIe-bound, 104 MB per step).
+  e2e       the whole denoising step at 512^2 through the public API (
+            model.ChromaRadiance.forward_cfg, chroma.cuh:1499-1584): img_in, txt_in, the
+            approximator, 19 double + 38 single blocks over both guidance halves, two NeRF
+            decodes and cfg_blend, as one CUDA graph; per step the noise, both T5 contexts and
+            the timestep copied in from pinned host memory and the velocity copied back inside
+            the events.  The reference arm times its own forward_cfg the same way.  Beside it,
+            dropin_forward_cfg: the reference's forward_cfg built through the drop-in headers.
+            e2e_block_pair is the timed block pair with all of its activations copied in and out
+            every step (PCIe-bound, 104 MB per step).
+  tp1024    config 4's block pair at 1024^2: unsharded on one GPU, tensor-parallel over N GPUs
+            (speed-up over rank 0's unsharded time, per-operation split, on-box parity).
 config1: one GEMM, the single-stream linear1 at 512^2 (M=1536 K=3072 N=21504, bias, bf16 out),
 inputs from numpy PCG64 seed 0, identical for both arms.
 cpu_baseline  the fp32 C oracle (oracle/oracle.c, OpenMP, all host cores) on a bounded row
@@ -388,6 +393,17 @@ def run_reference_config2(args) -> None:
         tp_ref = {"workload": WORKLOAD_TP1024.split(";")[0] + " (the reference has no tensor-parallel path: its "
                   "block code on one GPU)", "n_gpus": 1, "ms_per_step": round(per4, 5),
                   "tflops": round((lin4 + att4) / (per4 * 1e-3) / 1e12, 2)}
+    # The whole denoising step: the reference's own forward_cfg (its harness build), the same
+    # workload, copies and timing as the engine arm's e2e.
+    import harness
+    import model
+
+    h = harness.ForwardCfgHarness(oracle_mod.MODEL_REF_PATH)
+    h.setup(42, FC_H, FC_W, *FC_REAL)
+    n_fc = max(3, min(args.steps, 20))
+    fc_dev, fc_e2e = h.bench(FC_TIMESTEP, FC_CFG, n_fc, 3, FLUSH_BYTES)
+    fc_dev, fc_e2e = _ref_world_max(world, [fc_dev, fc_e2e])
+    fc_flop = model.step_flops(FC_H, FC_W)["total"]
     lin, att = blocks.block_pair_flops(T_TXT, I_IMG)
     value = (lin + att) * world / (per * 1e-3) / 1e12
     if rank != 0:
@@ -402,7 +418,14 @@ def run_reference_config2(args) -> None:
                          "sample": "the reference has no CPU path; this arm is its own block code (chroma.cuh "
                                    "double/single block GEMM + attention calls, cublas_ops.cuh, cuDNN SDPA) "
                                    "built from its sources and run on the B200"},
-        "e2e": {"value": round(value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": round(fc_flop * world / (fc_e2e * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": (3 * FC_H * FC_W + 2 * 512 * 4096) * 4, "d2h_bytes_per_step": 3 * FC_H * FC_W * 4,
+                "ms_per_step": round(fc_e2e, 4), "device_ms_per_step": round(fc_dev, 4), "flop_per_step": fc_flop,
+                "steps": n_fc,
+                "workload": WORKLOAD3 + "; the reference's own ChromaRadiance::forward_cfg (cuBLASLt, cuDNN, its "
+                            "kernels) on stream 0, weights in its Tensor fields from its own Philox generator; per "
+                            "step the noise and both T5 contexts copied in from pinned host memory and the velocity "
+                            "copied back inside the events"},
         "clocks": clk.summary(),
         "tp1024": tp_ref,
     }), flush=True)
@@ -586,61 +609,15 @@ def run_engine_config2(args) -> None:
     e2e_per = e2e_ms / e2e_steps
     del graphs, marked
 
-    # End to end over the transformer blocks of one denoising step, the way the model runs
-    # them under classifier-free guidance (forward_cfg's block loop): both
-    # halves through Chroma's 19 double + 38 single blocks, each block with its own weights
-    # (17 GB), inputs modulated on the device; in from pinned host memory the hidden states of
-    # both halves and the step's modulation vectors, out both halves' image hidden states.
-    pw = blocks.random_pass(gdev, dev)
-    ps = blocks.PassScratch(T, I, dev, halves=CFG_HALVES)
-    gp = torch.Generator().manual_seed(2)
-    x_h = torch.randn((CFG_HALVES * L, H), generator=gp).pin_memory()
-    mods_h = (torch.randn(tuple(pw.mods.shape), generator=gp) * 0.1).pin_memory()
-    img_h = torch.empty((CFG_HALVES, I, H)).pin_memory()
-    x_d = torch.empty((CFG_HALVES * L, H), device=dev)
-    x_d.copy_(x_h)
-    pw.mods.copy_(mods_h)
-    masks = torch.zeros((CFG_HALVES, L), device=dev)
-    masks[0] = mask
-    masks[1:, UNCOND_TEXT_KEYS:T] = float("-inf")
-    blocks.forward_pass(pw, x_d, pe, masks, ps, T)  # sizes the workspaces before capture
-    torch.cuda.synchronize(dev)
-    n0 = b2g.launch_count()
-    pass_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(cap):
-        with torch.cuda.graph(pass_graph, stream=cap):
-            blocks.forward_pass(pw, x_d, pe, masks, ps, T)
-    pass_launches = b2g.launch_count() - n0
-
-    def pass_step():
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        x_d.copy_(x_h, non_blocking=True)
-        pw.mods.copy_(mods_h, non_blocking=True)
-        pass_graph.replay()
-        for h in range(CFG_HALVES):
-            img_h[h].copy_(x_d[h * L + T:(h + 1) * L], non_blocking=True)
-        b.record(stream)
-        b.synchronize()
-        return a.elapsed_time(b)
-
-    for _ in range(2):
-        pass_step()
-    pass_steps = 5
-    pass_ms = sum(pass_step() for _ in range(pass_steps)) / pass_steps
-    pass_h2d = x_h.numel() * 4 + mods_h.numel() * 4
-    pass_d2h = img_h.numel() * 4
-    pass_flop = blocks.pass_flops(T, I, halves=CFG_HALVES)
-    del pass_graph, pw, ps
-    torch.cuda.empty_cache()
+    fc = forward_cfg_leg(args, torch, dev, flush, dropin=(world == 1 and not args.no_dropin))
     tp_leg = tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) if not args.no_tp1024 else None
 
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([total_ms, e2e_per, pass_ms], device=dev, dtype=torch.float64)
+        t = torch.tensor([total_ms, e2e_per, fc["ms_per_step"]], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_per, pass_ms = float(t[0]), float(t[1]), float(t[2])
+        total_ms, e2e_per, fc["ms_per_step"] = float(t[0]), float(t[1]), float(t[2])
     ops = blocks.block_pair_ops(T, I)
     flop_step = sum(f for _, _, f in ops)
     per = total_ms / args.steps
@@ -670,17 +647,8 @@ def run_engine_config2(args) -> None:
                      "gemm_ms_per_step": round(gemm_ms, 5)},
         "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
         "breakdown_tflops": {lab: round(f / (mean_op[lab] * 1e-3) / 1e12, 1) for lab, _, f in ops},
-        "e2e": {"value": round(pass_flop * world / (pass_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": pass_h2d, "d2h_bytes_per_step": pass_d2h, "ms_per_step": round(pass_ms, 4),
-                "workload": f"config3's block loop (forward_cfg) at 512^2 through the public API: both guidance "
-                            f"halves (conditional: {T - MASKED} of {T} text keys live; unconditional: "
-                            f"{UNCOND_TEXT_KEYS}) through {blocks.DOUBLE_BLOCKS} double + {blocks.SINGLE_BLOCKS} "
-                            f"single blocks with their own weights, every block's inputs modulated on the device "
-                            f"(modulate_to_bf16); hidden states of both halves and the step's modulation vectors "
-                            f"copied in from pinned host memory and both halves' image hidden states copied back "
-                            f"inside the events; one CUDA graph of {pass_launches} launches; FLOPs = GEMMs + "
-                            f"attention (unmasked), modulations not counted; embedders, approximator, NeRF decoder "
-                            f"and cfg_blend not included", "flop_per_step": pass_flop},
+        "e2e": dict(fc, value=round(fc["flop_per_step"] * world / (fc["ms_per_step"] * 1e-3) / 1e12, 3),
+                    ms_per_step=round(fc["ms_per_step"], 4)),
         "e2e_block_pair": {"value": round(flop_step * world / (e2e_per * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_per, 4),
                            "workload": "the timed block pair with all of its activations (modulated inputs, "
@@ -701,6 +669,127 @@ def run_engine_config2(args) -> None:
     if world > 1:
         torch.distributed.destroy_process_group()
 
+
+
+# ---------------------------------------------------------------------------- the whole step
+WORKLOAD3 = ("config3: one denoising step at 512^2, ChromaRadiance::forward_cfg (chroma.cuh:1499-1584): img_in, "
+             "txt_in, the approximator, 19 double + 38 single blocks over both guidance halves (conditional: "
+             "112 of 512 text keys live, unconditional: 2), two NeRF decodes and cfg_blend (scale 4), timestep "
+             "0.7, random-init weights (19 GB)")
+FC_H = FC_W = 512
+FC_REAL = (111, 1)
+FC_TIMESTEP, FC_CFG = 0.7, 4.0
+
+
+def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
+    """The engine's whole denoising step (model.ChromaRadiance.forward_cfg) through the public API,
+    captured in one CUDA graph; every step copies its inputs (noise, both T5 contexts, the
+    timestep) in from pinned host memory and the velocity back, inside the events.  After the
+    timed steps, one eager step is split by part.  With `dropin`, the reference's own
+    forward_cfg built through the drop-in headers (every GEMM and attention in libb2g.so) is
+    timed beside it, on its own random weights."""
+    import b2g
+    import model
+
+    g = torch.Generator(device=dev).manual_seed(42)
+    m = model.ChromaRadiance(model.random_weights(g, dev), dev)
+    s = model.ForwardScratch(FC_H, FC_W, dev)
+    gh = torch.Generator().manual_seed(3)
+    host = {"x": torch.randn((1, 3, FC_H, FC_W), generator=gh).pin_memory(),
+            "cc": torch.randn((model.TXT_TOKENS, model.CTX_DIM), generator=gh).pin_memory(),
+            "cu": torch.randn((model.TXT_TOKENS, model.CTX_DIM), generator=gh).pin_memory(),
+            "t": torch.tensor([FC_TIMESTEP]).pin_memory()}
+    d = {k: torch.empty_like(v, device=dev) for k, v in host.items() if k != "t"}
+    vel_h = torch.empty((1, 3, FC_H, FC_W)).pin_memory()
+    pe = torch.from_numpy(model.rope_table(FC_H, FC_W)).to(dev)
+    dct = torch.from_numpy(model.dct_features()).to(dev)
+    masks = torch.from_numpy(model.key_masks(list(FC_REAL), FC_H, FC_W)).to(dev)
+    for k in d:
+        d[k].copy_(host[k])
+    s.timestep.copy_(host["t"])
+
+    def run():
+        m.forward_cfg(s, d["x"], d["cc"], d["cu"], pe, dct, masks, FC_CFG)
+
+    run()  # sizes the library's workspaces before capture
+    torch.cuda.synchronize(dev)
+    cap = torch.cuda.Stream(dev)
+    n0 = b2g.launch_count()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            run()
+    launches = b2g.launch_count() - n0
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for k in d:
+            d[k].copy_(host[k], non_blocking=True)
+        s.timestep.copy_(host["t"], non_blocking=True)
+        graph.replay()
+        vel_h.copy_(s.velocity, non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    for _ in range(max(3, min(args.warmup, 5))):
+        step()
+    n = max(3, min(args.steps, 20))
+    times = []
+    for i in range(n):
+        flush.fill_(i & 0xFF)
+        torch.cuda.synchronize(dev)
+        times.append(step())
+    b2g.check_device_error()
+    ms = sum(times) / n
+
+    def timed(fn) -> float:
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b)
+
+    import blocks as blocks_mod
+
+    parts = {"embed": timed(lambda: m.embed(s, d["x"], d["cc"], d["cu"])),
+             "approximator": timed(lambda: m.compute_modulation(s)),
+             "blocks": timed(lambda: blocks_mod.forward_pass(m.blocks, s.x, pe, masks, s.blocks, s.T)),
+             "nerf_decode": timed(lambda: m.nerf_decode(s, d["x"], dct)),
+             "nerf_final_cfg_blend": timed(lambda: b2g.nerf_final(s.nx[0], s.nx[1], m.final_norm, m.conv_w, m.conv_b,
+                                                                  FC_CFG, FC_H, FC_W, s.tmp,
+                                                                  s.velocity.view(3, FC_H, FC_W)))}
+    flops = model.step_flops(FC_H, FC_W)
+    out = {"unit": "TFLOP/s", "ms_per_step": ms, "flop_per_step": flops["total"],
+           "h2d_bytes_per_step": sum(host[k].numel() * host[k].element_size() for k in host),
+           "d2h_bytes_per_step": vel_h.numel() * 4, "steps": n,
+           "workload": WORKLOAD3 + "; through the public API (model.ChromaRadiance.forward_cfg), one CUDA graph of "
+                       f"{launches} engine launches; per step the noise, both T5 contexts and the timestep are "
+                       "copied in from pinned host memory and the velocity copied back inside the events; FLOPs "
+                       "= every GEMM and attention of the step (unmasked), the element-wise work not counted",
+           "parts_ms_eager": {k: round(v, 3) for k, v in parts.items()},
+           "parts_tflop": {k: round(flops[k] / 1e12, 4) for k in ("embed", "approximator", "blocks", "nerf")},
+           "launches_per_step": launches, "step_ms_min_median": [round(min(times), 4),
+                                                                 round(statistics.median(times), 4)]}
+    del graph, m, s
+    torch.cuda.empty_cache()
+    if dropin:
+        import harness
+
+        if harness.DROPIN_PATH.exists():
+            h = harness.ForwardCfgHarness(harness.DROPIN_PATH)
+            h.setup(42, FC_H, FC_W, *FC_REAL)
+            dev_ms, e2e_ms = h.bench(FC_TIMESTEP, FC_CFG, n, 3, FLUSH_BYTES)
+            out["dropin_forward_cfg"] = {
+                "ms_per_step": round(e2e_ms, 4), "device_ms_per_step": round(dev_ms, 4),
+                "what": "the reference's own ChromaRadiance::forward_cfg, unchanged, built through the drop-in "
+                        "headers (cublas_ops.cuh, cudnn_attention.cuh, attention.cuh): every GEMM and attention "
+                        "in libb2g.so, everything else the reference's own kernels; same copies as this e2e"}
+    return out
 
 
 # ---------------------------------------------------------------------------- 1024^2 TP leg
@@ -1434,6 +1523,7 @@ def main():
     ap.add_argument("--workload", choices=["config2", "config1", "config4", "config5", "nerf"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp1024", action="store_true", help="skip the 1024^2 tensor-parallel leg")
+    ap.add_argument("--no-dropin", action="store_true", help="skip the drop-in build's forward_cfg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -249,6 +249,9 @@ class Ref:
 
 
 ATTN_REF_PATH = HERE / "_ref" / "libref_attention.so"
+# The reference's whole forward_cfg, stock (oracle/Makefile builds it from the drop-in
+# directory's harness and the reference's own headers); bound by chroma-radiance_b200/harness.py.
+MODEL_REF_PATH = HERE / "_ref" / "libref_model.so"
 
 
 class AttnRef:
