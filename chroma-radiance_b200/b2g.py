@@ -117,6 +117,8 @@ _SIGNATURES = {
     "b2g_nerf_glu_weights": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64] + [ctypes.c_void_p] * 4, ctypes.c_int),
     "b2g_convert_f32": ([ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64,
                                                                  ctypes.c_void_p], ctypes.c_int),
+    "b2g_nerf_glu_block": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                            ctypes.c_void_p], ctypes.c_int),
     "b2g_silu_mul": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_add_inplace": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_nerf_final": ([ctypes.c_void_p] * 5 + [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
@@ -820,6 +822,20 @@ def convert_f32(src: torch.Tensor, out: torch.Tensor, stream: torch.cuda.Stream 
     _check(load().b2g_convert_f32(src.data_ptr(), src.stride(0), src.shape[0], src.shape[1], out.data_ptr(),
                                   _operand_dtype(out), out.stride(0), _stream(src, stream)))
     return out
+
+
+def nerf_glu_block(params: torch.Tensor, norm_scale: torch.Tensor, x: torch.Tensor,
+                   stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """One NeRF GLU block fused (chroma.cuh:1253-1306): params F32 [P, >= 49152] (the
+    param_generator output), x F32 [P, 256, 64] updated in place."""
+    _require_cuda(params, norm_scale, x)
+    P = params.shape[0]
+    if params.dtype != torch.float32 or params.stride(1) != 1 or x.dtype != torch.float32 or not x.is_contiguous() \
+            or x.numel() != P * 256 * 64:
+        raise B2GError("nerf_glu_block: F32 params [P, >= 49152] and a contiguous F32 state [P, 256, 64]")
+    _check(load().b2g_nerf_glu_block(params.data_ptr(), params.stride(0), norm_scale.data_ptr(), x.data_ptr(), P,
+                                     _stream(x, stream)))
+    return x
 
 
 def silu_mul(a: torch.Tensor, b: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:

@@ -11,9 +11,9 @@ checkpoint names its load() reads, chroma.cuh:375-462) and the same inputs:
      residual with a gate of ones).
   4. 19 double + 38 single blocks (blocks.forward_pass), both halves in one half-major stream.
   5. nerf_decode for both halves at once (chroma.cuh:1163-1306): the embedder input in one
-     kernel, then per GLU block one param_generator GEMM over both halves' patches, the weight
-     preparation, RMSNorm, the three batched products (TF32, as the reference's cuBLAS runs
-     them), SiLU * mul and the residual add.
+     kernel, then per GLU block one param_generator GEMM over both halves' patches and one
+     fused tcgen05 kernel (b2g.nerf_glu_block) for the weight preparation, RMSNorm, the three
+     TF32 products, SiLU * mul and the residual add, intermediates kept on chip.
   6. the final norm + 3x3 conv of both halves and cfg_blend (chroma.cuh:1225-1250, 1581).
 
 Everything runs on the current stream and allocates nothing after ForwardScratch is made, so a
@@ -266,16 +266,23 @@ class ChromaRadiance:
         b2g.gemm_group([dict(x=s.emb_in, w=self.emb_w, bias=self.emb_b, out=s.nx[b]) for b in range(2)])
         for b in range(2):
             b2g.convert_f32(s.x[b * L + T:(b + 1) * L], s.img16[b * P:(b + 1) * P])
-        xn, nx = s.xn.view(2 * P * 256, NERF_HID), s.nx.view(2 * P * 256, NERF_HID)
         for blk in self.nerf:
             b2g.gemm(s.img16, blk.param_w, blk.param_b, out=s.params)
-            b2g.nerf_glu_weights(s.params, s.gate, s.value, s.fc2)
-            b2g.rms_norm(nx, blk.norm, xn)
-            b2g.batched_matmul_Bt(s.xn, s.gate, s.x1)
-            b2g.batched_matmul_Bt(s.xn, s.value, s.x2)
-            b2g.silu_mul(s.x1, s.x2)
-            b2g.batched_matmul_Bt(s.x1, s.fc2, s.xo)
-            b2g.add_inplace(s.nx, s.xo)
+            b2g.nerf_glu_block(s.params, blk.norm, s.nx)
+
+    def nerf_glu_block_unfused(self, s: ForwardScratch, blk: NerfBlock) -> None:
+        """The GLU block after its param_generator GEMM as the reference sequences it (weight
+        preparation, rms_norm, three batched products, silu_mul, add), each step its own launch
+        through HBM: the comparison for the fused b2g.nerf_glu_block."""
+        P = s.P
+        xn, nx = s.xn.view(2 * P * 256, NERF_HID), s.nx.view(2 * P * 256, NERF_HID)
+        b2g.nerf_glu_weights(s.params, s.gate, s.value, s.fc2)
+        b2g.rms_norm(nx, blk.norm, xn)
+        b2g.batched_matmul_Bt(s.xn, s.gate, s.x1)
+        b2g.batched_matmul_Bt(s.xn, s.value, s.x2)
+        b2g.silu_mul(s.x1, s.x2)
+        b2g.batched_matmul_Bt(s.x1, s.fc2, s.xo)
+        b2g.add_inplace(s.nx, s.xo)
 
     def forward_cfg(self, s: ForwardScratch, x_img: torch.Tensor, ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor,
                     pe: torch.Tensor, dct: torch.Tensor, masks: torch.Tensor, cfg_scale: float) -> torch.Tensor:

@@ -377,6 +377,16 @@ b2g_status b2g_nerf_glu_weights(const float* params, int64_t ldp, int64_t patche
 b2g_status b2g_convert_f32(const float* src, int64_t lds, int64_t rows, int64_t cols, void* dst, b2g_dtype dst_dtype,
                            int64_t ldd, void* stream);
 
+/* One whole NeRF GLU block (NerfGLUBlock::forward, chroma.cuh:1253-1306) for `patches` patches in
+ * one persistent tcgen05 kernel: from each patch's param_generator output row params[p] (ldp >=
+ * 49152 floats) the L2-normalised gate / value / fc2 weights, rms_norm of the state x[p]
+ * [256, 64] (norm_scale [64], eps 1e-6), the three TF32 products with silu * mul between them,
+ * and x[p] += the result, in place.  Replaces b2g_nerf_glu_weights + b2g_rms_norm + three
+ * b2g_batched_matmul_Bt + b2g_silu_mul + b2g_add_inplace with no intermediate in HBM.  x
+ * 16-byte aligned; each kernel wait is bounded (b2g_check_device_error). */
+b2g_status b2g_nerf_glu_block(const float* params, int64_t ldp, const float* norm_scale, float* x, int64_t patches,
+                              void* stream);
+
 /* a = silu(a) * b (silu_mul_cuda) and x += y (add_cuda), F32, n % 4 == 0, 16-byte aligned. */
 b2g_status b2g_silu_mul(float* a, const float* b, int64_t n, void* stream);
 b2g_status b2g_add_inplace(float* x, const float* y, int64_t n, void* stream);

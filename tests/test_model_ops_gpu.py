@@ -131,3 +131,52 @@ def test_gemm_silu_epilogue(engine):
     torch.cuda.synchronize()
     assert rel_err(got32.cpu().numpy(), want.cpu().numpy()) <= 1e-5
     assert rel_err(got.float().cpu().numpy(), want.cpu().numpy()) <= 2.0 ** -8
+
+
+def _tf32(t: torch.Tensor) -> torch.Tensor:
+    """Round fp32 values to TF32 (10 mantissa bits), nearest even (finite inputs)."""
+    i = t.float().contiguous().view(torch.int32)
+    return ((i + (((i >> 13) & 1) + 0x0FFF)) & ~0x1FFF).view(torch.float32)
+
+
+def test_nerf_glu_block_fused(engine):
+    """The fused GLU block against fp64 with the operands rounded to TF32 where the reference's
+    cuBLAS rounds them (normalised weights, normed state, silu * mul), and against the engine's
+    own unfused sequence (weights, rms_norm, three batched products, silu_mul, add)."""
+    P = 301                                     # more patches than SMs: the persistent loop wraps
+    params = torch.randn((P, 49152), generator=gen(40), device=DEV) * 0.05
+    x = torch.randn((P, 256, 64), generator=gen(41), device=DEV)
+    scale = torch.randn(64, generator=gen(42), device=DEV) * 0.1 + 1
+    x0 = x.clone()
+    engine.nerf_glu_block(params, scale, x)
+    # unfused engine sequence
+    gate, value = (torch.empty((P, 256, 64), device=DEV) for _ in range(2))
+    fc2 = torch.empty((P, 64, 256), device=DEV)
+    xn, x1, x2, xo = (torch.empty(s, device=DEV) for s in ((P, 256, 64), (P, 256, 256), (P, 256, 256), (P, 256, 64)))
+    y = x0.clone()
+    engine.nerf_glu_weights(params, gate, value, fc2)
+    engine.rms_norm(y.view(-1, 64), scale, xn.view(-1, 64))
+    engine.batched_matmul_Bt(xn, gate, x1)
+    engine.batched_matmul_Bt(xn, value, x2)
+    engine.silu_mul(x1, x2)
+    engine.batched_matmul_Bt(x1, fc2, xo)
+    engine.add_inplace(y, xo)
+    torch.cuda.synchronize()
+    engine.check_device_error()
+    # fp64 with TF32 operand rounding
+    pd = params.double()
+
+    def l2(t):
+        return t / t.norm(dim=-1, keepdim=True).clamp_min(1e-12)
+
+    wg = _tf32(l2(pd[:, :16384].view(P, 64, 256).transpose(1, 2))).double()
+    wv = _tf32(l2(pd[:, 16384:32768].view(P, 64, 256).transpose(1, 2))).double()
+    wf = _tf32(l2(pd[:, 32768:].view(P, 256, 64).transpose(1, 2))).double()
+    xd = x0.double()
+    n = _tf32(xd * torch.rsqrt((xd * xd).mean(-1, keepdim=True) + 1e-6) * scale.double()).double()
+    a1, a2 = n @ wg.transpose(1, 2), n @ wv.transpose(1, 2)
+    h = _tf32((a1 / (1 + torch.exp(-a1))) * a2).double()
+    want = xd + h @ wf.transpose(1, 2)
+    d = want - xd
+    assert ((x.double() - want).abs().max() / d.abs().max()).item() <= 2e-3
+    assert ((x.double() - y.double()).abs().max() / d.abs().max()).item() <= 2e-3
