@@ -761,7 +761,7 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
              "blocks": timed(lambda: blocks_mod.forward_pass(m.blocks, s.x, pe, masks, s.blocks, s.T)),
              "nerf_decode": timed(lambda: m.nerf_decode(s, d["x"], dct)),
              "nerf_final_cfg_blend": timed(lambda: b2g.nerf_final(s.nx[0], s.nx[1], m.final_norm, m.conv_w, m.conv_b,
-                                                                  FC_CFG, FC_H, FC_W, s.tmp,
+                                                                  FC_CFG, FC_H, FC_W,
                                                                   s.velocity.view(3, FC_H, FC_W)))}
     flops = model.step_flops(FC_H, FC_W)
     out = {"unit": "TFLOP/s", "ms_per_step": ms, "flop_per_step": flops["total"],

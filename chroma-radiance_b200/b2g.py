@@ -122,7 +122,7 @@ _SIGNATURES = {
     "b2g_silu_mul": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_add_inplace": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p], ctypes.c_int),
     "b2g_nerf_final": ([ctypes.c_void_p] * 5 + [ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
-                                                 ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+                                                 ctypes.c_void_p], ctypes.c_int),
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
     "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
@@ -851,12 +851,11 @@ def add_inplace(x: torch.Tensor, y: torch.Tensor, stream: torch.cuda.Stream | No
 
 
 def nerf_final(feat_cond: torch.Tensor, feat_uncond: torch.Tensor | None, norm_scale: torch.Tensor,
-               conv_w: torch.Tensor, conv_b: torch.Tensor, cfg_scale: float, H: int, W: int, tmp: torch.Tensor,
+               conv_w: torch.Tensor, conv_b: torch.Tensor, cfg_scale: float, H: int, W: int,
                out: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
     """NeRF final layer of both guidance halves + cfg_blend (chroma.cuh:1225-1250, 1581) into out
-    F32 [3, H, W]; tmp F32 scratch of halves * H * W * 64 floats."""
-    _require_cuda(feat_cond, norm_scale, conv_w, conv_b, tmp, out)
+    F32 [3, H, W], one kernel."""
+    _require_cuda(feat_cond, norm_scale, conv_w, conv_b, out)
     _check(load().b2g_nerf_final(feat_cond.data_ptr(), _ptr(feat_uncond), norm_scale.data_ptr(), conv_w.data_ptr(),
-                                 conv_b.data_ptr(), float(cfg_scale), H, W, tmp.data_ptr(), out.data_ptr(),
-                                 _stream(out, stream)))
+                                 conv_b.data_ptr(), float(cfg_scale), H, W, out.data_ptr(), _stream(out, stream)))
     return out

@@ -250,83 +250,135 @@ __global__ void add_inplace_kernel(float* __restrict__ x, const float* __restric
   }
 }
 
-// NeRF final layer, step 1: for pixel (h, w) of half z, the 64 channels of the decoder state
-// feat_z[patch][pix][0..63] (patch = (h/16)*(W/16) + w/16, pix = (h%16)*16 + w%16), RMS-normed
-// over the channels and scaled, into tmp[z][h][w][64].  One warp per pixel.
-__global__ void nerf_final_norm_kernel(const float* __restrict__ feat0, const float* __restrict__ feat1,
-                                       const float* __restrict__ scale, int H, int W, float eps,
-                                       float* __restrict__ tmp) {
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
-  const int64_t HW = static_cast<int64_t>(H) * W;
+// NeRF final layer (chroma.cuh:1225-1250) and cfg_blend (chroma.cuh:1581) in one kernel: for
+// each half z, the decoder state feat_z[patch][pix][64] (patch = (h/16)*(W/16) + w/16,
+// pix = (h%16)*16 + w%16) is RMS-normed over its 64 channels (eps, scale), convolved 3x3 to
+// 3 channels (zero padding), and the halves blended: out = uncond + cfg * (cond - uncond), or
+// cond alone with one half.
+//
+// A block owns a 16 x 16 pixel tile.  Its 18 x 18 halo cells, normed, sit in shared memory
+// channel-major (plane stride kFinPlane, odd, so that the 16 lanes that store one cell's
+// channels spread over the banks); the 64 x 27 conv weights sit beside them as [c][28] rows
+// read as broadcast float4s.  Loading: each half-warp takes one cell per step (16 lanes x
+// float4 = the cell's 64 channels, its sum of squares reduced over the half-warp), with
+// kFinUnroll cells' loads in flight before any is used.  Convolution: the 256 threads are two
+// groups of 128, one per 32-channel half; a thread computes two vertically adjacent pixels, so
+// one channel costs it 12 tile loads and 7 weight loads for 54 FMAs; the second group's sums
+// are added through shared memory.  HBM sees the state once (plus the halo rows, mostly L2
+// hits) and the 3-channel output once.
+constexpr int kFinTile = 16, kFinHalo = kFinTile + 2, kFinCells = kFinHalo * kFinHalo;
+constexpr int kFinPlane = kFinCells + 1, kFinThreads = 256, kFinWRow = 28, kFinUnroll = 7;
+constexpr int kFinSmem = (64 * kFinPlane + 64 * kFinWRow + 128 * 6) * 4;
+
+__global__ void __launch_bounds__(kFinThreads) nerf_final_kernel(const float* __restrict__ feat0,
+                                                                 const float* __restrict__ feat1,
+                                                                 const float* __restrict__ scale,
+                                                                 const float* __restrict__ wgt,
+                                                                 const float* __restrict__ bias, float cfg, int H,
+                                                                 int W, float eps, float* __restrict__ out) {
+  extern __shared__ float4 fin_smem4[];
+  float* tile = reinterpret_cast<float*>(fin_smem4);
+  float* ws = tile + 64 * kFinPlane;  // [c][28]: co * 9 + kh * 3 + kw, one pad
+  float* red = ws + 64 * kFinWRow;    // [6][128]: the second channel group's sums
+  for (int i = threadIdx.x; i < 64 * kFinWRow; i += kFinThreads) {
+    const int c = i / kFinWRow, j = i % kFinWRow;
+    ws[i] = j < 27 ? wgt[((j / 9) * 64 + c) * 9 + j % 9] : 0.0f;
+  }
+  const int t = threadIdx.x, hl = t & 15, hw = t >> 4;  // half-warp lane / half-warp index
+  const int grp = t >> 7, tt = t & 127;                  // channel group, thread within it
+  const int tx = tt & 15, ty = tt >> 4;                  // pixels (2ty, tx) and (2ty + 1, tx)
+  const int h0 = blockIdx.y * kFinTile, w0 = blockIdx.x * kFinTile;
+  const int PW = W / 16;
+  const float4 sc = reinterpret_cast<const float4*>(scale)[hl];
+  float res[2][2][3];
   const int halves = feat1 ? 2 : 1;
-  if (gw >= halves * HW) return;
-  const int z = static_cast<int>(gw / HW);
-  const int64_t hw = gw % HW;
-  const int h = static_cast<int>(hw / W), w = static_cast<int>(hw % W);
-  const int64_t patch = static_cast<int64_t>(h / 16) * (W / 16) + w / 16;
-  const int pix = (h % 16) * 16 + (w % 16);
-  const float* src = (z ? feat1 : feat0) + (patch * 256 + pix) * 64;
-  const float2 v = reinterpret_cast<const float2*>(src)[lane];
-  float ss = v.x * v.x + v.y * v.y;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float r = rsqrtf(ss / 64.0f + eps);
-  const float2 s = reinterpret_cast<const float2*>(scale)[lane];
-  reinterpret_cast<float2*>(tmp + (z * HW + hw) * 64)[lane] = make_float2(v.x * r * s.x, v.y * r * s.y);
-}
-
-// NeRF final layer, step 2: 3x3 conv (64 -> 3 channels, zero padding) of each half's normed
-// state, then out = uncond + cfg * (cond - uncond) (one half: out = cond).  A 16 x 16 pixel
-// tile per block; each 16-channel slice of the halo tile passes through shared memory once.
-constexpr int kConvTile = 16, kConvHalo = kConvTile + 2, kConvSlice = 16;
-
-__global__ void __launch_bounds__(256) nerf_final_conv_kernel(const float* __restrict__ tmp, int halves,
-                                                              const float* __restrict__ wgt,
-                                                              const float* __restrict__ bias, float cfg, int H, int W,
-                                                              float* __restrict__ out) {
-  __shared__ float ws[3 * 64 * 9];
-  __shared__ float tile[kConvHalo * kConvHalo * kConvSlice];
-  for (int i = threadIdx.x; i < 3 * 64 * 9; i += 256) ws[i] = wgt[i];
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int h0 = blockIdx.y * kConvTile, w0 = blockIdx.x * kConvTile;
-  const int h = h0 + ty, w = w0 + tx;
-  const int64_t HW = static_cast<int64_t>(H) * W;
-  float res[2][3];
   for (int z = 0; z < halves; ++z) {
-    float acc[3] = {bias[0], bias[1], bias[2]};
-    for (int c0 = 0; c0 < 64; c0 += kConvSlice) {
-      __syncthreads();
-      for (int i = threadIdx.x; i < kConvHalo * kConvHalo * (kConvSlice / 4); i += 256) {
-        const int q = i % (kConvSlice / 4), cell = i / (kConvSlice / 4);
-        const int ih = h0 - 1 + cell / kConvHalo, iw = w0 - 1 + cell % kConvHalo;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ih >= 0 && ih < H && iw >= 0 && iw < W)
-          v = *reinterpret_cast<const float4*>(tmp + (z * HW + static_cast<int64_t>(ih) * W + iw) * 64 + c0 + 4 * q);
-        *reinterpret_cast<float4*>(tile + cell * kConvSlice + 4 * q) = v;
+    const float* feat = z ? feat1 : feat0;
+    __syncthreads();  // the previous half's reads of the tile are done
+    for (int base = hw; base < kFinCells; base += 16 * kFinUnroll) {
+      float4 v[kFinUnroll];
+#pragma unroll
+      for (int u = 0; u < kFinUnroll; ++u) {
+        const int cell = base + 16 * u;
+        const int ih = h0 - 1 + cell / kFinHalo, iw = w0 - 1 + cell % kFinHalo;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (cell < kFinCells && ih >= 0 && ih < H && iw >= 0 && iw < W) {
+          const int64_t patch = static_cast<int64_t>(ih >> 4) * PW + (iw >> 4);
+          const int pix = (ih & 15) * 16 + (iw & 15);
+          v[u] = __ldg(reinterpret_cast<const float4*>(feat + (patch * 256 + pix) * 64) + hl);
+        }
       }
-      __syncthreads();
-      if (h < H && w < W) {
-        for (int c = 0; c < kConvSlice; ++c) {
 #pragma unroll
-          for (int kh = 0; kh < 3; ++kh) {
+      for (int u = 0; u < kFinUnroll; ++u) {
+        const int cell = base + 16 * u;
+        float ss = v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
 #pragma unroll
-            for (int kw = 0; kw < 3; ++kw) {
-              const float v = tile[((ty + kh) * kConvHalo + tx + kw) * kConvSlice + c];
-#pragma unroll
-              for (int co = 0; co < 3; ++co) acc[co] += v * ws[((co * 64 + c0 + c) * 3 + kh) * 3 + kw];
-            }
-          }
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (cell < kFinCells) {
+          // Zero padding: outside cells load as 0 and stay 0 (r is finite for eps > 0).
+          const float r = rsqrtf(ss / 64.0f + eps);
+          tile[(4 * hl) * kFinPlane + cell] = v[u].x * r * sc.x;
+          tile[(4 * hl + 1) * kFinPlane + cell] = v[u].y * r * sc.y;
+          tile[(4 * hl + 2) * kFinPlane + cell] = v[u].z * r * sc.z;
+          tile[(4 * hl + 3) * kFinPlane + cell] = v[u].w * r * sc.w;
         }
       }
     }
+    __syncthreads();
+    float acc[2][3];
 #pragma unroll
-    for (int co = 0; co < 3; ++co) res[z][co] = acc[co];
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int co = 0; co < 3; ++co) acc[p][co] = grp ? 0.0f : bias[co];
+#pragma unroll 4
+    for (int c = 32 * grp; c < 32 * grp + 32; ++c) {
+      const float* tc = tile + c * kFinPlane + (2 * ty) * kFinHalo + tx;
+      float v[4][3];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int q = 0; q < 3; ++q) v[r][q] = tc[r * kFinHalo + q];
+      const float4* wc = reinterpret_cast<const float4*>(ws + c * kFinWRow);
+      float wk[28];
+#pragma unroll
+      for (int q = 0; q < 7; ++q) {
+        const float4 f = wc[q];
+        wk[4 * q] = f.x;
+        wk[4 * q + 1] = f.y;
+        wk[4 * q + 2] = f.z;
+        wk[4 * q + 3] = f.w;
+      }
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw)
+#pragma unroll
+            for (int co = 0; co < 3; ++co) acc[p][co] += v[p + kh][kw] * wk[co * 9 + kh * 3 + kw];
+    }
+    if (grp) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int co = 0; co < 3; ++co) red[(p * 3 + co) * 128 + tt] = acc[p][co];
+    }
+    __syncthreads();
+    if (!grp) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p)
+#pragma unroll
+        for (int co = 0; co < 3; ++co) res[z][p][co] = acc[p][co] + red[(p * 3 + co) * 128 + tt];
+    }
   }
-  if (h < H && w < W) {
+  if (grp) return;
+  const int64_t HW = static_cast<int64_t>(H) * W;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int h = h0 + 2 * ty + p, w = w0 + tx;
 #pragma unroll
     for (int co = 0; co < 3; ++co) {
-      const float v = halves == 2 ? res[1][co] + cfg * (res[0][co] - res[1][co]) : res[0][co];
+      const float v = halves == 2 ? res[1][p][co] + cfg * (res[0][p][co] - res[1][p][co]) : res[0][p][co];
       out[co * HW + static_cast<int64_t>(h) * W + w] = v;
     }
   }
@@ -450,24 +502,25 @@ b2g_status b2g_add_inplace(float* x, const float* y, int64_t n, void* stream) {
 }
 
 b2g_status b2g_nerf_final(const float* feat_cond, const float* feat_uncond, const float* norm_scale,
-                          const float* conv_w, const float* conv_b, float cfg_scale, int H, int W, float* tmp,
-                          float* out, void* stream) {
-  if (!feat_cond || !norm_scale || !conv_w || !conv_b || !tmp || !out || H % 16 || W % 16 || H <= 0 || W <= 0 ||
-      !aligned16(tmp) || (reinterpret_cast<uintptr_t>(feat_cond) & 7u) ||
-      (feat_uncond && (reinterpret_cast<uintptr_t>(feat_uncond) & 7u)) || (reinterpret_cast<uintptr_t>(norm_scale) & 7u))
+                          const float* conv_w, const float* conv_b, float cfg_scale, int H, int W, float* out,
+                          void* stream) {
+  if (!feat_cond || !norm_scale || !conv_w || !conv_b || !out || H % 16 || W % 16 || H <= 0 || W <= 0 ||
+      !aligned16(feat_cond) || (feat_uncond && !aligned16(feat_uncond)) || !aligned16(norm_scale))
     return set_error(B2G_ERR_INVALID, "b2g_nerf_final: arguments / alignment");
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int halves = feat_uncond ? 2 : 1;
-  const int64_t warps = static_cast<int64_t>(halves) * H * W;
-  nerf_final_norm_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
-      feat_cond, feat_uncond, norm_scale, H, W, 1e-6f, tmp);
-  if ((s = launched("nerf final norm launch")) != B2G_OK) return s;
-  nerf_final_conv_kernel<<<dim3(W / kConvTile, H / kConvTile), 256, 0, st>>>(tmp, halves, conv_w, conv_b, cfg_scale,
-                                                                              H, W, out);
-  return launched("nerf final conv launch");
+  static bool attr_set[64] = {};
+  if (dev->device < 64 && !attr_set[dev->device]) {
+    if ((s = check_cuda(cudaFuncSetAttribute(nerf_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kFinSmem),
+                        "nerf final smem attribute")) != B2G_OK)
+      return s;
+    attr_set[dev->device] = true;
+  }
+  nerf_final_kernel<<<dim3(W / kFinTile, H / kFinTile), kFinThreads, kFinSmem, static_cast<cudaStream_t>(stream)>>>(
+      feat_cond, feat_uncond, norm_scale, conv_w, conv_b, cfg_scale, H, W, 1e-6f, out);
+  return launched("nerf final launch");
 }
 
 }  // extern "C"

@@ -180,7 +180,6 @@ class ForwardScratch:
         self.x1 = torch.empty((2 * P, 256, NERF_MLP), dtype=f, device=dev)
         self.x2 = torch.empty_like(self.x1)
         self.xo = torch.empty((2 * P, 256, NERF_HID), dtype=f, device=dev)
-        self.tmp = torch.empty((2, H, W, NERF_HID), dtype=f, device=dev)
         self.velocity = torch.empty((1, 3, H, W), dtype=f, device=dev)
 
 
@@ -293,7 +292,7 @@ class ChromaRadiance:
         self.blocks.mods = self.compute_modulation(s)
         blocks.forward_pass(self.blocks, s.x, pe, masks, s.blocks, s.T)
         self.nerf_decode(s, x_img, dct)
-        b2g.nerf_final(s.nx[0], s.nx[1], self.final_norm, self.conv_w, self.conv_b, cfg_scale, s.H, s.W, s.tmp,
+        b2g.nerf_final(s.nx[0], s.nx[1], self.final_norm, self.conv_w, self.conv_b, cfg_scale, s.H, s.W,
                        s.velocity.view(3, s.H, s.W))
         return s.velocity
 

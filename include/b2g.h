@@ -395,10 +395,11 @@ b2g_status b2g_add_inplace(float* x, const float* y, int64_t n, void* stream);
  * state feat [P, 256, 64] is un-patchified, RMS-normed over its 64 channels at every pixel
  * (scale norm_scale, eps 1e-6) and convolved 3x3 (conv_w [3, 64, 3, 3], conv_b [3], zero
  * padding); out F32 [3, H, W] = uncond + cfg_scale * (cond - uncond), or the conditional
- * result alone when feat_uncond is NULL.  tmp: F32 scratch of halves * H * W * 64 floats. */
+ * result alone when feat_uncond is NULL.  One kernel: the normed state never leaves shared
+ * memory.  feat_cond, feat_uncond and norm_scale 16-byte aligned; H and W multiples of 16. */
 b2g_status b2g_nerf_final(const float* feat_cond, const float* feat_uncond, const float* norm_scale,
-                          const float* conv_w, const float* conv_b, float cfg_scale, int H, int W, float* tmp,
-                          float* out, void* stream);
+                          const float* conv_w, const float* conv_b, float cfg_scale, int H, int W, float* out,
+                          void* stream);
 
 /* Reads and clears the device-side error word that the tensor-core kernels set when a
  * pipeline wait exceeds its time limit (they then drain and return instead of hanging).

@@ -107,7 +107,7 @@ def test_nerf_decode_matches_reference(stock, engine_model):
     s.x[s.L + s.T:].copy_(img)
     m.nerf_decode(s, stock.tensor("x").view(1, 3, H, W), stock.tensor("dct").view(256, 64))
     got = torch.empty((3, H, W), device="cuda")
-    b2g.nerf_final(s.nx[0], None, m.final_norm, m.conv_w, m.conv_b, 1.0, H, W, s.tmp, got)
+    b2g.nerf_final(s.nx[0], None, m.final_norm, m.conv_w, m.conv_b, 1.0, H, W, got)
     torch.cuda.synchronize()
     cos, rel = compare(got, want)
     print(f"nerf_decode vs reference: cosine {cos:.8f}, max|d|/max|ref| {rel:.3e}")

@@ -91,9 +91,8 @@ def test_nerf_final(engine, halves):
     scale = torch.randn(64, generator=gen(20), device=DEV) * 0.1 + 1
     cw = torch.randn((3, 64, 3, 3), generator=gen(21), device=DEV) * 0.05
     cb = torch.randn(3, generator=gen(22), device=DEV) * 0.05
-    tmp = torch.empty((2, H, W, 64), device=DEV)
     out = torch.empty((3, H, W), device=DEV)
-    engine.nerf_final(feats[0], feats[1] if halves == 2 else None, scale, cw, cb, cfg, H, W, tmp, out)
+    engine.nerf_final(feats[0], feats[1] if halves == 2 else None, scale, cw, cb, cfg, H, W, out)
 
     def ref(f):   # unpatchify to [64, H, W], RMS norm over channels, 3x3 conv with zero padding
         img = f.double().view(H // 16, W // 16, 16, 16, 64).permute(4, 0, 2, 1, 3).reshape(64, H, W)
