@@ -362,6 +362,66 @@ def _ref_world_max(world: int, vals: list) -> list:
     return t.tolist()
 
 
+def attention_leg(torch, dev, flush, steps: int, warmup: int, ref=None) -> dict:
+    """The attention kernel alone, engine against the reference's cuDNN SDPA, at the config-2
+    and config-4 sequence lengths (L = 1536 and 4608; 24 heads x 128, key bias -inf on 400 of
+    the 512 text keys).  The operands are bf16 with identical values in both arms, each in its
+    own layout: the engine reads q, k, v as column views of the [L, 3 * 3072] buffer its qkv
+    epilogue writes and writes bf16 [L, 3072] (flash_attn_kernel); the reference's
+    cudnn_sdpa_forward (cudnn_attention.cuh:408-443, graph->execute) reads [24, L, 128] and
+    writes [24, L, 128].  Per call: CUDA events around it, a 256 MB L2 flush before it outside
+    the events; the median over `steps` calls.  FLOPs: 4 L^2 H D (unmasked), and 4 L (L - 400)
+    H D for the live keys."""
+    H, D = 24, 128
+    out = {}
+    for T, I in ((T_TXT, I_IMG), (T_1024, I_1024)):
+        L = T + I
+        g = torch.Generator(device=dev).manual_seed(11)
+        qkv = torch.randn((L, 3, H, D), generator=g, device=dev).to(torch.bfloat16)
+        mask = torch.zeros(L, device=dev)
+        mask[T - MASKED:T] = float("-inf")
+        flop, live = 4.0 * L * L * H * D, 4.0 * L * (L - MASKED) * H * D
+        if ref is None:
+            import b2g
+
+            flat = qkv.view(L, 3 * H * D)
+            q, k, v = flat[:, :H * D], flat[:, H * D:2 * H * D], flat[:, 2 * H * D:]
+            o = torch.empty((L, H * D), dtype=torch.bfloat16, device=dev)
+            stream = torch.cuda.current_stream(dev)
+
+            def call():
+                b2g.attention_bf16(q, k, v, H, D, attn_mask=mask, out=o)
+
+            for _ in range(warmup):
+                call()
+            torch.cuda.synchronize(dev)
+            ms = []
+            for i in range(steps):
+                flush.fill_(i & 0xFF)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call()
+                b.record(stream)
+                b.synchronize()
+                ms.append(a.elapsed_time(b))
+            what = "flash_attn_kernel (b2g_attention_bf16), bf16 out"
+        else:
+            q, k, v = (qkv[:, j].permute(1, 0, 2).contiguous() for j in range(3))
+            o = torch.empty((H, L, D), dtype=torch.bfloat16, device=dev)
+            torch.cuda.synchronize(dev)
+            ms = ref.bench_sdpa_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), mask.data_ptr(), o.data_ptr(), H, L, D,
+                                     steps, warmup, flush.data_ptr(), flush.numel())
+            what = "cuDNN SDPA (cudnn_sdpa_forward: graph->execute), bf16 out"
+        med = statistics.median(ms)
+        out[f"L{L}"] = {"us": round(1e3 * med, 1), "tflops": round(flop / (med * 1e-3) / 1e12, 1),
+                        "tflops_live_keys": round(live / (med * 1e-3) / 1e12, 1), "kernel": what}
+        del qkv, q, k, v, o
+    out["workload"] = ("attention alone, 24 heads x 128, bf16 operands with identical values in both arms, key "
+                       "bias -inf on 400 of 512 text keys; median of per-call CUDA-event times, L2 flushed before "
+                       "each call")
+    return out
+
+
 def run_reference_config2(args) -> None:
     """The reference's block code (oracle/_ref/libref_attention.so): its own linear(),
     linear_gated_residual(), rms_norm, cuDNN attention and elementwise kernels in its own call
@@ -408,6 +468,11 @@ def run_reference_config2(args) -> None:
     value = (lin + att) * world / (per * 1e-3) / 1e12
     if rank != 0:
         return
+    import torch
+
+    dev = torch.device("cuda", 0)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup), ref=ref)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
@@ -428,6 +493,7 @@ def run_reference_config2(args) -> None:
                             "copied back inside the events"},
         "clocks": clk.summary(),
         "tp1024": tp_ref,
+        "attention": attn,
     }), flush=True)
 
 
@@ -610,6 +676,7 @@ def run_engine_config2(args) -> None:
     del graphs, marked
 
     fc = forward_cfg_leg(args, torch, dev, flush, dropin=(world == 1 and not args.no_dropin))
+    attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup)) if rank == 0 else None
     tp_leg = tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) if not args.no_tp1024 else None
 
     if world > 1:
@@ -658,6 +725,7 @@ def run_engine_config2(args) -> None:
         "gpu_launches": int(launches_per_step * args.steps),
         "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
         "tp1024": tp_leg,
+        "attention": attn,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as oracle_mod

@@ -283,6 +283,11 @@ class AttnRef:
         lib.ref_bench_t5_attention.argtypes = [_c_p] * 4 + [ctypes.c_int, ctypes.c_int, _i64, ctypes.c_float, _c_p,
                                                             ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
         lib.ref_bench_t5_attention.restype = ctypes.c_int
+        lib.ref_sdpa_bf16.argtypes = [_c_p] * 5 + [ctypes.c_int] * 3
+        lib.ref_sdpa_bf16.restype = ctypes.c_int
+        lib.ref_bench_sdpa_bf16.argtypes = [_c_p] * 5 + [ctypes.c_int] * 5 + [_c_p, _i64,
+                                                                            ctypes.POINTER(ctypes.c_double)]
+        lib.ref_bench_sdpa_bf16.restype = ctypes.c_int
         lib.ref_attn_init()
         self.lib = lib
 
@@ -305,6 +310,19 @@ class AttnRef:
 
     def attention_with_rope(self, Q, K, V, pe, n_head, d_head, L, mask, out):
         return self.lib.ref_attention_with_rope(Q, K, V, pe, n_head, d_head, L, mask, out)
+
+    def sdpa_bf16(self, Q, K, V, bias, O, n_head, L, d_head):
+        """cudnn_sdpa_forward on bf16 [n_head, L, d_head] device buffers (addresses)."""
+        return self.lib.ref_sdpa_bf16(Q, K, V, bias, O, n_head, L, d_head)
+
+    def bench_sdpa_bf16(self, Q, K, V, bias, O, n_head, L, d_head, iters, warmup, flush, flush_bytes):
+        """Per-call milliseconds of cudnn_sdpa_forward alone (events on stream 0, L2 flushed
+        before each call outside the events)."""
+        ms = (ctypes.c_double * iters)()
+        rc = self.lib.ref_bench_sdpa_bf16(Q, K, V, bias, O, n_head, L, d_head, iters, warmup, flush, flush_bytes, ms)
+        if rc != 0:
+            raise RuntimeError(f"ref_bench_sdpa_bf16: CUDA error {rc}")
+        return list(ms)
 
 
 def available() -> dict:

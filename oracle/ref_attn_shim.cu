@@ -112,6 +112,41 @@ int ref_bench_attention(const float* Q, const float* K, const float* V, const fl
   return 0;
 }
 
+// The reference's SDPA call alone (cudnn_sdpa_forward, cudnn_attention.cuh:408-443): Q, K, V
+// bf16 [n_head, L, d_head] contiguous, bias F32 [L] or null, O bf16 [n_head, L, d_head].  This
+// is the kernel under attention_with_rope once its RoPE and permute kernels have run.
+int ref_sdpa_bf16(const void* Q, const void* K, const void* V, const float* bias, void* O, int n_head, int L,
+                  int d_head) {
+  cudnn_sdpa_forward(static_cast<const __nv_bfloat16*>(Q), static_cast<const __nv_bfloat16*>(K),
+                     static_cast<const __nv_bfloat16*>(V), bias, static_cast<__nv_bfloat16*>(O), n_head, L, d_head);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// Times ref_sdpa_bf16 with CUDA events around each call on stream 0; before each call (outside
+// the events) `flush_bytes` of `flush` are rewritten so that the operands start out of L2.
+// ms[i] gets call i's time.
+int ref_bench_sdpa_bf16(const void* Q, const void* K, const void* V, const float* bias, void* O, int n_head, int L,
+                        int d_head, int iters, int warmup, void* flush, int64_t flush_bytes, double* ms) {
+  for (int i = 0; i < warmup; ++i) ref_sdpa_bf16(Q, K, V, bias, O, n_head, L, d_head);
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int i = 0; i < iters; ++i) {
+    if (flush && flush_bytes > 0) cudaMemsetAsync(flush, i & 0xFF, static_cast<size_t>(flush_bytes), 0);
+    cudaEventRecord(e0, 0);
+    ref_sdpa_bf16(Q, K, V, bias, O, n_head, L, d_head);
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float t = 0;
+    cudaEventElapsedTime(&t, e0, e1);
+    ms[i] = t;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  return static_cast<int>(cudaGetLastError());
+}
+
 // ---------------------------------------------------------------------------------------
 // One double-stream and one single-stream block from the modulated bf16 inputs to the
 // updated residual streams, with exactly the reference's BF16-path calls

@@ -610,6 +610,32 @@ def test_attention_vs_reference_cudnn(engine, L, text_masked):
     assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
 
 
+@pytest.mark.parametrize("T,I", [(512, 1024), (512, 4096)])
+def test_attention_bf16_vs_reference_sdpa(engine, T, I):
+    """The block path's attention (bf16 q, k, v column views of the qkv buffer, bf16 out)
+    against the reference's cudnn_sdpa_forward (cudnn_attention.cuh:408-443) on the same bf16
+    values in its [24, L, 128] layout, at L = 1536 and 4608 with -inf on 400 of 512 text keys:
+    the pair the bench's attention leg times."""
+    ref = attn_ref_or_skip()
+    H, D, L = 24, 128, T + I
+    g = torch.Generator(device=DEV).manual_seed(11)
+    qkv = torch.randn((L, 3, H, D), generator=g, device=DEV).to(torch.bfloat16)
+    mask = torch.zeros(L, device=DEV)
+    mask[T - 400:T] = float("-inf")
+    flat = qkv.view(L, 3 * H * D)
+    mine = engine.attention_bf16(flat[:, :H * D], flat[:, H * D:2 * H * D], flat[:, 2 * H * D:], H, D,
+                                 attn_mask=mask, out_dtype=torch.bfloat16)
+    q, k, v = (qkv[:, j].permute(1, 0, 2).contiguous() for j in range(3))
+    o = torch.empty((H, L, D), dtype=torch.bfloat16, device=DEV)
+    assert ref.sdpa_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), mask.data_ptr(), o.data_ptr(), H, L, D) == 0
+    torch.cuda.synchronize()
+    theirs = o.permute(1, 0, 2).reshape(L, H * D)
+    a, b = mine.double().cpu().numpy().ravel(), theirs.double().cpu().numpy().ravel()
+    # Both round O to bf16 (½ ulp = 2^-9 relative each); the softmax is fp32 in both.
+    assert rel_err(a, b) < 1e-2
+    assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.99999
+
+
 def test_nerf_block_gemms_vs_reference(engine, ref):
     """One NeRF GLU block's GEMMs at 512^2 (chroma.cuh:1262-1302) at their real sizes, engine
     against the reference's own linear() and batched_matmul_Bt on the same inputs: param_gen
