@@ -351,3 +351,37 @@ def test_short_pass_chained_vs_reference(engine, ref):
     c = cos(dm, dr)
     print(f"chained 2+2 blocks: cosine {c:.6f}, max rel {err:.4f}")
     assert torch.isfinite(x).all() and c >= 0.999 and err <= 5e-3
+
+
+def test_fp8_full_pass_close_to_bf16(engine):
+    """Config 5's FP8 transformer over a whole pass (Chroma's 19 double + 38 single blocks at
+    512^2, both guidance halves, E4M3 weights per channel and per-token E4M3 activations)
+    against the bf16 pass on the same random weights, modulation vectors and inputs.  Every
+    linear of every block rounds both operands to E4M3 (3.7% RMS relative error per K=3072
+    product on Gaussian operands), and the residual streams carry it through 57 blocks: the
+    update x_out - x_in agrees to cosine >= 0.995 (the measured value is printed)."""
+    import blocks
+
+    T, I = 512, 1024
+    L = T + I
+    g = torch.Generator(device=DEV).manual_seed(21)
+    pw = blocks.random_pass(g, DEV)
+    pw.mods.copy_(torch.randn(tuple(pw.mods.shape), generator=g, device=DEV) * 0.1)
+    pw8 = blocks.quantize_pass(pw)
+    ang = torch.rand((L, blocks.DHEAD // 2), generator=g, device=DEV) * 6.2831853
+    pe = torch.stack([ang.cos(), -ang.sin(), ang.sin(), ang.cos()], -1).contiguous()
+    masks = torch.zeros((2, L), device=DEV)
+    masks[0, 112:T] = float("-inf")
+    masks[1, 2:T] = float("-inf")
+    x0 = torch.randn((2 * L, blocks.HIDDEN), generator=g, device=DEV)
+    x16, x8 = x0.clone(), x0.clone()
+    blocks.forward_pass(pw, x16, pe, masks, blocks.PassScratch(T, I, DEV, halves=2), T)
+    blocks.forward_pass_fp8(pw8, x8, pe, masks, blocks.ScratchFP8(T, I, DEV, halves=2), T)
+    torch.cuda.synchronize()
+    engine.check_device_error()
+    d16, d8 = (x16 - x0).double(), (x8 - x0).double()
+    c = float((d16.flatten() @ d8.flatten()) / (d16.norm() * d8.norm()))
+    err = float((d8 - d16).abs().max() / d16.abs().max())
+    print(f"fp8 vs bf16 57-block pass: cosine {c:.6f}, max|d|/max|ref| {err:.4f}")
+    assert torch.isfinite(x8).all()
+    assert c >= 0.995
