@@ -462,6 +462,7 @@ def run_reference_config2(args) -> None:
     h.setup(42, FC_H, FC_W, *FC_REAL)
     n_fc = max(3, min(args.steps, 20))
     fc_dev, fc_e2e = h.bench(FC_TIMESTEP, FC_CFG, n_fc, 3, FLUSH_BYTES)
+    approx_ms = h.bench_modulation(FC_TIMESTEP, max(5, min(args.steps, 30)), 3, FLUSH_BYTES)
     fc_dev, fc_e2e = _ref_world_max(world, [fc_dev, fc_e2e])
     fc_flop = model.step_flops(FC_H, FC_W)["total"]
     lin, att = blocks.block_pair_flops(T_TXT, I_IMG)
@@ -473,6 +474,13 @@ def run_reference_config2(args) -> None:
     dev = torch.device("cuda", 0)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup), ref=ref)
+    approx = approximator_leg(torch, dev, flush, None, None, 0, ms_list=approx_ms)
+    approx["workload"] += "; the reference's own ChromaApproximator (linear() on cuBLASLt) in its forward_cfg build"
+    t5_ms = ref.bench_t5_leg(T5_LAYERS, T5_TOKENS, T5_D, T5_FF, T5_HEADS, 5, 2, flush.data_ptr(), flush.numel())
+    t5 = t5_line(statistics.median(t5_ms), "the reference's own calls in t5.cuh's order: linear() on fp16 weights "
+                 "for q, k, v, o, wi_0, wi_1, wo (each casting its F32 input to fp16), t5_attention (fp32 cuBLAS "
+                 "SGEMMs), gelu_cuda on the gate; RMSNorms, gate product and residual adds left out, as in the "
+                 "engine's leg; L2 flushed before each of 5 passes (median)")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per, 5), "higher_is_better": True,
@@ -494,6 +502,8 @@ def run_reference_config2(args) -> None:
         "clocks": clk.summary(),
         "tp1024": tp_ref,
         "attention": attn,
+        "approximator": approx,
+        "t5": t5,
     }), flush=True)
 
 
@@ -677,6 +687,8 @@ def run_engine_config2(args) -> None:
 
     fc = forward_cfg_leg(args, torch, dev, flush, dropin=(world == 1 and not args.no_dropin))
     attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup)) if rank == 0 else None
+    t5 = (t5_encoder_leg(torch, b2g, dev, torch.Generator(device=dev).manual_seed(5), torch.cuda.current_stream(dev),
+                         flush) if rank == 0 else None)
     tp_leg = tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) if not args.no_tp1024 else None
 
     if world > 1:
@@ -726,6 +738,7 @@ def run_engine_config2(args) -> None:
         "step_ms_min_median": [round(min(per_step), 5), round(statistics.median(per_step), 5)],
         "tp1024": tp_leg,
         "attention": attn,
+        "t5": t5,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle as oracle_mod
@@ -747,6 +760,69 @@ WORKLOAD3 = ("config3: one denoising step at 512^2, ChromaRadiance::forward_cfg 
 FC_H = FC_W = 512
 FC_REAL = (111, 1)
 FC_TIMESTEP, FC_CFG = 0.7, 4.0
+
+
+def approximator_shapes() -> list:
+    """(label, M, N, K) of the approximator's GEMMs (chroma.cuh:188-212, 467-508)."""
+    import model
+
+    M, A = model.MOD_ROWS, model.APPROX_DIM
+    out = [("in_proj", M, A, 64)]
+    for i in range(model.APPROX_LAYERS):
+        out += [(f"layer{i}.in", M, A, A), (f"layer{i}.out", M, A, A)]
+    return out + [("out_proj", M, model.HIDDEN, A)]
+
+
+def approximator_bytes(M: int, N: int, K: int) -> int:
+    """Algorithmic HBM bytes of one approximator GEMM: the bf16 weight, the F32 activations in
+    (cast to bf16 by linear(), cublas_ops.cuh:486-490) and the F32 output."""
+    return N * K * 2 + M * K * 4 + M * N * 4
+
+
+def approximator_leg(torch, dev, flush, stream, run, steps: int, ms_list=None) -> dict:
+    """The approximator alone (compute_modulation: 12 GEMMs at M=344, 556 MB of bf16 weights, the
+    weight-streaming 'skinny' shape): median per-call time over `steps` calls (CUDA events, L2
+    flushed before each), TFLOP/s and achieved HBM GB/s of its algorithmic bytes against
+    MEASURED_PEAKS.json hbm_gbs; with `run(mark)` also a per-GEMM split of one eager call.
+    `ms_list` (the reference arm) gives the per-call times instead of running anything."""
+    shapes = approximator_shapes()
+    flop = sum(2.0 * M * N * K for _, M, N, K in shapes)
+    byts = sum(approximator_bytes(M, N, K) for _, M, N, K in shapes)
+    if ms_list is None:
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize(dev)
+        ms_list = []
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            run()
+            b.record(stream)
+            b.synchronize()
+            ms_list.append(a.elapsed_time(b))
+    med = statistics.median(ms_list)
+    peaks = measured_peaks()
+    out = {"us": round(1e3 * med, 1), "tflops": round(flop / (med * 1e-3) / 1e12, 1),
+           "hbm_gbs": round(byts / (med * 1e-3) / 1e9, 1), "hbm_frac": round(byts / (med * 1e-3) / 1e9 /
+                                                                            peaks["hbm_gbs"], 3),
+           "flop": flop, "bytes": byts,
+           "workload": "the approximator (compute_modulation, guidance 0): 12 GEMMs at M=344 (64->5120, 10 x "
+                       "5120->5120, 5120->3072) with their RMSNorms; median of per-call CUDA-event times, L2 "
+                       "flushed before each call; bytes = bf16 weights + F32 activations in + F32 outputs"}
+    if run is not None:
+        flush.fill_(0)
+        torch.cuda.synchronize(dev)
+        mk = _EagerMarks(torch, stream)
+        mk.begin()
+        run(mk)
+        torch.cuda.synchronize(dev)
+        per = mk.durations()
+        out["per_gemm"] = {lab: {"us": round(1e3 * per[lab], 1),
+                                 "hbm_gbs": round(approximator_bytes(M, N, K) / (per[lab] * 1e-3) / 1e9, 1),
+                                 "tflops": round(2.0 * M * N * K / (per[lab] * 1e-3) / 1e12, 1)}
+                           for lab, M, N, K in shapes if lab in per}
+    return out
 
 
 def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
@@ -831,6 +907,8 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
              "nerf_final_cfg_blend": timed(lambda: b2g.nerf_final(s.nx[0], s.nx[1], m.final_norm, m.conv_w, m.conv_b,
                                                                   FC_CFG, FC_H, FC_W,
                                                                   s.velocity.view(3, FC_H, FC_W)))}
+    approx = approximator_leg(torch, dev, flush, stream, lambda mark=None: m.compute_modulation(s, mark),
+                              max(5, min(args.steps, 30)))
     flops = model.step_flops(FC_H, FC_W)
     out = {"unit": "TFLOP/s", "ms_per_step": ms, "flop_per_step": flops["total"],
            "h2d_bytes_per_step": sum(host[k].numel() * host[k].element_size() for k in host),
@@ -842,7 +920,8 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
            "parts_ms_eager": {k: round(v, 3) for k, v in parts.items()},
            "parts_tflop": {k: round(flops[k] / 1e12, 4) for k in ("embed", "approximator", "blocks", "nerf")},
            "launches_per_step": launches, "step_ms_min_median": [round(min(times), 4),
-                                                                 round(statistics.median(times), 4)]}
+                                                                 round(statistics.median(times), 4)],
+           "approximator": approx}
     del graph, m, s
     torch.cuda.empty_cache()
     if dropin:
@@ -1154,6 +1233,24 @@ WORKLOAD5 = ("config5: the FP8 transformer at 512^2, one independent job per GPU
 T5_LAYERS, T5_TOKENS, T5_D, T5_HEADS, T5_FF = 24, 512, 4096, 64, 10240
 
 
+def t5_shapes() -> list:
+    """(label, GEMMs in the launch, M, N, K) of one T5 layer's linears (t5.cuh:233-275)."""
+    d, ff, L = T5_D, T5_FF, T5_TOKENS
+    return [("qkv", 3, L, d, d), ("o", 1, L, d, d), ("wi0_wi1", 2, L, ff, d), ("wo", 1, L, d, ff)]
+
+
+def t5_line(ms: float, what: str) -> dict:
+    """The T5 leg's summary from its per-pass time."""
+    d, ff, L = T5_D, T5_FF, T5_TOKENS
+    gemm_flop = T5_LAYERS * 2.0 * L * (4 * d * d + 2 * ff * d + d * ff)
+    att_flop = T5_LAYERS * 4.0 * L * L * d
+    return {"ms": round(ms, 4), "tflops": round((gemm_flop + att_flop) / (ms * 1e-3) / 1e12, 2),
+            "flop": gemm_flop + att_flop, "gemm_flop": gemm_flop,
+            "workload": f"T5-XXL encoder GEMMs and attention for one prompt, {T5_LAYERS} layers x (7 linears + "
+                        f"attention), {L} tokens, d_model {d}, FFN {ff}, 64 heads x 64, fp16 weights ~N(0, 0.02); "
+                        + what}
+
+
 def t5_encoder_leg(torch, b2g, dev, gen, stream, flush) -> dict:
     """The T5-XXL encoder's GEMMs and attention for one prompt (t5.cuh:233-275): per layer the
     reference's 7 linears (q, k, v, o 4096x4096; wi_0, wi_1 10240x4096; wo 4096x10240) on fp16
@@ -1202,14 +1299,42 @@ def t5_encoder_leg(torch, b2g, dev, gen, stream, flush) -> dict:
         b.synchronize()
         times.append(a.elapsed_time(b))
     del g
-    gemm_flop = T5_LAYERS * 2.0 * L * (4 * d * d + 2 * ff * d + d * ff)
-    att_flop = T5_LAYERS * 4.0 * L * L * d
-    ms = statistics.median(times)
-    return {"ms": round(ms, 4), "tflops": round((gemm_flop + att_flop) / (ms * 1e-3) / 1e12, 2),
-            "flop": gemm_flop + att_flop, "gemm_flop": gemm_flop, "launches": launches,
-            "workload": f"T5-XXL encoder, {T5_LAYERS} layers x (7 linears + attention), {L} tokens, fp16 weights, "
-                        f"F32 activations cast to fp16 (q/k/v and wi_0/wi_1 share their input's cast; q/k/v one "
-                        f"launch); one CUDA graph; L2 flushed before each of 5 timed passes (median)"}
+    # Per-launch split: every layer's launches eagerly, events between them, median over layers.
+    w0 = ws[0]
+    ops = {"qkv": lambda: b2g.gemm_group([dict(x=x, w=w0["q"], out=q), dict(x=x, w=w0["k"], out=k),
+                                          dict(x=x, w=w0["v"], out=v)]),
+           "attention": lambda: b2g.t5_attention(q.view(L, H, d // H), k.view(L, H, d // H), v.view(L, H, d // H),
+                                                 bias, H, d // H, out=att),
+           "o": lambda: b2g.gemm(att, w0["o"], out=o),
+           "wi0_wi1": lambda: b2g.gemm_group([dict(x=x, w=w0["wi0"], out=h0, epilogue="gelu"),
+                                              dict(x=x, w=w0["wi1"], out=h1)]),
+           "wo": lambda: b2g.gemm(h0, w0["wo"], out=y)}
+    per = {}
+    for lab, fn in ops.items():
+        ts = []
+        for i in range(9):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        per[lab] = statistics.median(ts)
+    hbm = measured_peaks()["hbm_gbs"]
+    split = {}
+    for lab, n, M, N, K in t5_shapes():
+        byts = n * N * K * 2 + M * K * 4 + n * M * N * 4  # fp16 weights, the F32 input once, F32 outputs
+        gbs = byts / (per[lab] * 1e-3) / 1e9
+        split[lab] = {"us": round(1e3 * per[lab], 1), "tflops": round(n * 2.0 * M * N * K / (per[lab] * 1e-3) / 1e12, 1),
+                      "hbm_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3)}
+    split["attention"] = {"us": round(1e3 * per["attention"], 1)}
+    out = t5_line(statistics.median(times),
+                  "F32 activations cast to fp16 (q/k/v and wi_0/wi_1 share their input's cast; q/k/v one launch); "
+                  "one CUDA graph; L2 flushed before each of 5 timed passes (median); per_launch: each launch "
+                  "alone, eager, L2 flushed, median of 9")
+    out.update({"launches": launches, "per_launch": split})
+    return out
 
 
 def run_engine_config5(args) -> None:

@@ -305,6 +305,36 @@ int fc_modulation(float timestep) {
   return static_cast<int>(cudaGetLastError());
 }
 
+// Times compute_modulation (the approximator, chroma.cuh:467-508: timestep embedding, in_proj,
+// 5 residual MLP layers of 5120, out_proj to the [344, 3072] modulation vectors) with CUDA
+// events on stream 0, `iters` calls after `warmup`; ms[i] is call i's time, a `flush_bytes`
+// buffer rewritten before each call outside the events.
+int fc_bench_modulation(float timestep, int iters, int warmup, int64_t flush_bytes, double* ms) {
+  for (int i = 0; i < warmup; ++i) Tensor m = g_model->compute_modulation(timestep, 0.0f);
+  void* flush = nullptr;
+  if (flush_bytes > 0) CHECK_CUDA(cudaMalloc(&flush, flush_bytes));
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int i = 0; i < iters; ++i) {
+    if (flush) cudaMemsetAsync(flush, i & 0xFF, flush_bytes, 0);
+    cudaEventRecord(e0, 0);
+    {
+      Tensor m = g_model->compute_modulation(timestep, 0.0f);
+    }
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float t = 0;
+    cudaEventElapsedTime(&t, e0, e1);
+    ms[i] = t;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (flush) cudaFree(flush);
+  return static_cast<int>(cudaGetLastError());
+}
+
 // One NeRF decode (nerf_decode, chroma.cuh:1163-1251) of transformer image rows img [P, 3072]
 // (a device pointer) into out [1,3,H,W] (a device pointer).
 int fc_nerf_decode(const float* img, float* out) {

@@ -41,6 +41,8 @@ class ForwardCfgHarness:
         lib.fc_forward.argtypes = [ctypes.c_float, ctypes.c_float]
         lib.fc_modulation.argtypes = [ctypes.c_float]
         lib.fc_nerf_decode.argtypes = [vp, vp]
+        lib.fc_bench_modulation.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int, i64,
+                                            ctypes.POINTER(ctypes.c_double)]
         lib.fc_bench.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, i64,
                                  ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
         self.lib = lib
@@ -90,3 +92,9 @@ class ForwardCfgHarness:
         self._check(self.lib.fc_bench(timestep, cfg_scale, iters, warmup, flush_bytes, ctypes.byref(d),
                                       ctypes.byref(e)), "fc_bench")
         return d.value / iters, e.value / iters
+
+    def bench_modulation(self, timestep: float, iters: int, warmup: int, flush_bytes: int) -> list:
+        """Per-call milliseconds of compute_modulation (the approximator), CUDA events on stream 0."""
+        ms = (ctypes.c_double * iters)()
+        self._check(self.lib.fc_bench_modulation(timestep, iters, warmup, flush_bytes, ms), "fc_bench_modulation")
+        return list(ms)

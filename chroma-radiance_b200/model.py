@@ -233,16 +233,22 @@ class ChromaRadiance:
                                g(f"nerf_blocks.{i}.norm.scale")) for i in range(NERF_DEPTH)]
 
     # ------------------------------------------------------------------ pieces of the step
-    def compute_modulation(self, s: ForwardScratch) -> torch.Tensor:
+    def compute_modulation(self, s: ForwardScratch, mark=None) -> torch.Tensor:
         """ChromaApproximator on the timestep in s.timestep (guidance 0, as forward_cfg calls it)
-        into s.mod [344, 3072]."""
+        into s.mod [344, 3072].  `mark(label)`, when given, is called after each GEMM (with the
+        RMSNorm and timestep embedding before it counted in)."""
+        mk = mark or (lambda label: None)
         b2g.timestep_vec(s.timestep, 0.0, s.vec)
         b2g.gemm(s.vec, self.in_proj_w, self.in_proj_b, out=s.ax)
-        for layer in self.approx:
+        mk("in_proj")
+        for i, layer in enumerate(self.approx):
             b2g.rms_norm(s.ax, layer.norm, s.an)
             b2g.gemm(s.an, layer.in_w, layer.in_b, out=s.ah, epilogue="silu")
+            mk(f"layer{i}.in")
             b2g.gemm(s.ah, layer.out_w, layer.out_b, out=s.ax, epilogue="gated_residual", gate=self.ones)
+            mk(f"layer{i}.out")
         b2g.gemm(s.ax, self.out_proj_w, self.out_proj_b, out=s.mod)
+        mk("out_proj")
         return s.mod
 
     def embed(self, s: ForwardScratch, x_img: torch.Tensor, ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor) -> None:

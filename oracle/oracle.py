@@ -288,6 +288,9 @@ class AttnRef:
         lib.ref_bench_sdpa_bf16.argtypes = [_c_p] * 5 + [ctypes.c_int] * 5 + [_c_p, _i64,
                                                                             ctypes.POINTER(ctypes.c_double)]
         lib.ref_bench_sdpa_bf16.restype = ctypes.c_int
+        lib.ref_bench_t5_leg.argtypes = [ctypes.c_int, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         _c_p, _i64, ctypes.POINTER(ctypes.c_double)]
+        lib.ref_bench_t5_leg.restype = ctypes.c_int
         lib.ref_attn_init()
         self.lib = lib
 
@@ -314,6 +317,14 @@ class AttnRef:
     def sdpa_bf16(self, Q, K, V, bias, O, n_head, L, d_head):
         """cudnn_sdpa_forward on bf16 [n_head, L, d_head] device buffers (addresses)."""
         return self.lib.ref_sdpa_bf16(Q, K, V, bias, O, n_head, L, d_head)
+
+    def bench_t5_leg(self, layers, L, d, ff, heads, iters, warmup, flush, flush_bytes):
+        """Per-pass milliseconds of the reference's T5 GEMMs + t5_attention leg (ref_bench_t5_leg)."""
+        ms = (ctypes.c_double * iters)()
+        rc = self.lib.ref_bench_t5_leg(layers, L, d, ff, heads, iters, warmup, flush, flush_bytes, ms)
+        if rc != 0:
+            raise RuntimeError(f"ref_bench_t5_leg: CUDA error {rc}")
+        return list(ms)
 
     def bench_sdpa_bf16(self, Q, K, V, bias, O, n_head, L, d_head, iters, warmup, flush, flush_bytes):
         """Per-call milliseconds of cudnn_sdpa_forward alone (events on stream 0, L2 flushed

@@ -276,7 +276,10 @@ static void* fill(int64_t n, DType dt, float scale, float shift, unsigned long l
   if (dt == DType::F32) return f;
   void* b = nullptr;
   CHECK_CUDA(cudaMalloc(&b, n * 2));
-  f32_to_bf16_cuda(f, static_cast<__nv_bfloat16*>(b), n);
+  if (dt == DType::FP16)
+    f32_to_fp16_cuda(f, static_cast<__half*>(b), n);
+  else
+    f32_to_bf16_cuda(f, static_cast<__nv_bfloat16*>(b), n);
   CHECK_CUDA(cudaDeviceSynchronize());
   cudaFree(f);
   return b;
@@ -367,6 +370,76 @@ int ref_bench_blocks(void** dp, void** sp, int64_t T, int64_t I, int iters, int 
   cudaEventDestroy(e1);
   if (flush) cudaFree(flush);
   return static_cast<int>(cudaGetLastError());
+}
+
+// The T5-XXL encoder's GEMMs and attention for one prompt with the reference's own calls, in
+// t5.cuh's order (t5.cuh:229-275): per layer linear() on fp16 weights for q, k, v (each casting
+// its F32 input to fp16, cublas_ops.cuh:491-495), t5_attention (attention.cuh:34-91, scale 1,
+// relative bias [heads, L, L]), o, wi_0, wi_1, gelu_cuda on the gate, wo.  The RMSNorms, the
+// gate product and the residual adds are left out, as the engine's T5 leg leaves them out;
+// every layer reads the same F32 input.  Weights ~N(0, 0.02) fp16, x ~N(0, 1), bias
+// ~N(0, 0.5).  ms[i]: pass i's time (CUDA events on stream 0, `flush_bytes` rewritten before
+// each pass outside the events).
+int ref_bench_t5_leg(int layers, int64_t L, int64_t d, int64_t ff, int heads, int iters, int warmup, void* flush,
+                     int64_t flush_bytes, double* ms) {
+  unsigned long long seed = 500;
+  std::vector<Tensor> wq, wk, wv, wo_, wi0, wi1, wo2;
+  auto weight = [&](int64_t rows, int64_t cols) {
+    return Tensor::wrap_gpu(fill(rows * cols, DType::FP16, 0.02f, 0.f, ++seed), {rows, cols}, DType::FP16);
+  };
+  for (int l = 0; l < layers; ++l) {
+    wq.push_back(weight(d, d));
+    wk.push_back(weight(d, d));
+    wv.push_back(weight(d, d));
+    wo_.push_back(weight(d, d));
+    wi0.push_back(weight(ff, d));
+    wi1.push_back(weight(ff, d));
+    wo2.push_back(weight(d, ff));
+  }
+  Tensor x = Tensor::wrap_gpu(fill(L * d, DType::F32, 1.f, 0.f, ++seed), {L, d}, DType::F32);
+  float* bias = static_cast<float*>(fill(static_cast<int64_t>(heads) * L * L, DType::F32, 0.5f, 0.f, ++seed));
+  Tensor q = Tensor::alloc({L, d}, DType::F32, true), k = Tensor::alloc({L, d}, DType::F32, true);
+  Tensor v = Tensor::alloc({L, d}, DType::F32, true), o = Tensor::alloc({L, d}, DType::F32, true);
+  Tensor g = Tensor::alloc({L, ff}, DType::F32, true), u = Tensor::alloc({L, ff}, DType::F32, true);
+  Tensor y = Tensor::alloc({L, d}, DType::F32, true);
+  const int dh = static_cast<int>(d / heads);
+  auto pass = [&]() {
+    for (int l = 0; l < layers; ++l) {
+      linear(x, wq[l], nullptr, q);
+      linear(x, wk[l], nullptr, k);
+      linear(x, wv[l], nullptr, v);
+      Tensor a = t5_attention(q.reshape({L, (int64_t)heads, (int64_t)dh}), k.reshape({L, (int64_t)heads, (int64_t)dh}),
+                              v.reshape({L, (int64_t)heads, (int64_t)dh}), bias, heads, dh, 1.0f, nullptr);
+      linear(a, wo_[l], nullptr, o);
+      linear(x, wi0[l], nullptr, g);
+      linear(x, wi1[l], nullptr, u);
+      gelu_cuda(g.f32(), g.f32(), L * ff);
+      linear(g, wo2[l], nullptr, y);
+    }
+  };
+  for (int i = 0; i < warmup; ++i) pass();
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int i = 0; i < iters; ++i) {
+    if (flush && flush_bytes > 0) cudaMemsetAsync(flush, i & 0xFF, static_cast<size_t>(flush_bytes), 0);
+    cudaEventRecord(e0, 0);
+    pass();
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float t = 0;
+    cudaEventElapsedTime(&t, e0, e1);
+    ms[i] = t;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  const int rc = static_cast<int>(cudaGetLastError());
+  for (auto* vec : {&wq, &wk, &wv, &wo_, &wi0, &wi1, &wo2})
+    for (auto& t : *vec) cudaFree(t.data);
+  cudaFree(x.data);
+  cudaFree(bias);
+  return rc;
 }
 
 }  // extern "C"
