@@ -126,6 +126,7 @@ _SIGNATURES = {
     "b2g_check_device_error": ([ctypes.POINTER(ctypes.c_int)], ctypes.c_int),
     "b2g_launch_count": ([], ctypes.c_uint64),
     "b2g_set_gemm_variant": ([ctypes.c_int, ctypes.c_int], ctypes.c_int),
+    "b2g_set_attention_splits": ([ctypes.c_int], ctypes.c_int),
     "b2g_attention_qknorm_rope": ([ctypes.c_void_p, ctypes.c_int64] * 3 + [ctypes.c_void_p] * 4 +
                                   [ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                    ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
@@ -187,8 +188,14 @@ def launch_count() -> int:
 
 def set_gemm_variant(variant: int, splits: int = 0) -> None:
     """variant -1 automatic, 0 = 1-CTA 128x128, 1 = 1-CTA 128x256, 2 = 2-CTA 256x256 tiles;
-    splits 0 automatic, else the split-K factor."""
+    splits 0 automatic, > 0 the split-K factor of every tile, < 0 (-S) only the tiles of the
+    last, partial wave split S ways."""
     _check(load().b2g_set_gemm_variant(variant, splits))
+
+
+def set_attention_splits(splits: int) -> None:
+    """Fused-attention key splits: 0 automatic, -1 never, > 0 that many slices."""
+    _check(load().b2g_set_attention_splits(splits))
 
 
 def check_device_error() -> None:

@@ -21,6 +21,10 @@
 
 namespace b2g {
 
+// Key-split override for the fused attention (b2g_set_attention_splits): 0 automatic, -1
+// never, > 0 that many slices.
+int g_attn_splits = 0;
+
 namespace {
 
 // Attention prologue (256 threads per block): Q, K and V rows, each warp 2 (token l, head h)
@@ -215,6 +219,14 @@ struct FaParams {
   long long ldo;
   int out_bf16;
   int* err;
+  // Key splits (kv_splits > 1, for launches too small to fill the GPU): CTA x covers query
+  // pair x / kv_splits and the x % kv_splits-th slice of the key blocks, and stores its
+  // unnormalised O and its row statistics (running max m in log2 units, row sum l) instead of
+  // the output; attn_combine_kernel then merges the slices.
+  int kv_splits;
+  int lpad;               // rows per (sequence, head, split) in the partial buffers
+  float* part_o;          // [batch][H][kv_splits][lpad][D]
+  float2* part_ml;        // [batch][H][kv_splits][lpad]: (m, l)
 };
 
 template <int D>
@@ -243,13 +255,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qpair = blockIdx.x;
+  const int qpair = static_cast<int>(blockIdx.x) / p.kv_splits;
+  const int kslice = static_cast<int>(blockIdx.x) % p.kv_splits;
   const int head = blockIdx.y;
   // Sequence blockIdx.z of a batch stored one after another (rows [z*L, (z+1)*L) of q, k, v
   // and out; keys past L of the last block are masked like any key past L).
   const int row0 = static_cast<int>(blockIdx.z) * p.L;
   const float* key_bias = p.bias ? p.bias + static_cast<long long>(blockIdx.z) * p.bias_stride : nullptr;
-  const int nkb = p.num_kb;
+  // This CTA's key blocks: [kb0, kb0 + nkb).
+  const int kb0 = static_cast<int>(static_cast<long long>(kslice) * p.num_kb / p.kv_splits);
+  const int nkb = static_cast<int>(static_cast<long long>(kslice + 1) * p.num_kb / p.kv_splits) - kb0;
 
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
@@ -312,13 +327,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           mbar_arrive_expect_tx(&full[st], Ly::kKBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, row0 + j * kFaKeys, head,
+            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, row0 + (kb0 + j) * kFaKeys, head,
                         shared_kv);
         } else {
           mbar_arrive_expect_tx(&full[st], Ly::kVBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, row0 + j * kFaKeys, head,
+            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, row0 + (kb0 + j) * kFaKeys, head,
                         shared_kv);
         }
         ++issued;
@@ -404,7 +419,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       float kb2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int key = j * kFaKeys + c * 32 + lane;
+        const int key = (kb0 + j) * kFaKeys + c * 32 + lane;
         kb2[c] = key < p.L ? (key_bias ? __ldg(key_bias + key) * 1.4426950408889634f : 0.f) : -INFINITY;
       }
       good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
@@ -519,7 +534,26 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // Final: wait for the last P.Vt of this tile, write O / l.
     if (good)
       good = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (nkb - 1) & 1, p.err, kErrWaitEpilogue));
-    if (good) {
+    if (good && p.kv_splits > 1) {
+      // One key slice: the unnormalised O and (m, l) of each row go to the partial buffers.
+      tc_fence_after();
+      const int q = (qpair * kFaTiles + t) * kFaRows + row;
+      const long long prow = ((static_cast<long long>(blockIdx.z) * gridDim.y + head) * p.kv_splits + kslice) * p.lpad + q;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(obase + c * 32, o);
+        tmem_wait_ld();
+        if (q < p.L) {
+          float4* dst = reinterpret_cast<float4*>(p.part_o + prow * D + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                                 __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+        }
+      }
+      if (q < p.L) p.part_ml[prow] = make_float2(m_used, l_sum);
+    } else if (good) {
       tc_fence_after();
       const int q = (qpair * kFaTiles + t) * kFaRows + row;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
@@ -567,6 +601,55 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   }
 }
 
+// Merges the key slices of a split launch: for query row q of head h, with slice s holding
+// (m_s, l_s) and O_s = sum over its keys of 2^(t - m_s) v, the output is
+// sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s, M = max_s m_s (rows with no live key: 0).
+// One warp per (sequence, row, head); lane i covers columns [4i, 4i + 4) (D = 128) or
+// [2i, 2i + 2) (D = 64).
+template <int D>
+__global__ void attn_combine_kernel(FaParams p, int H, int batch) {
+  griddep_wait();  // launched dependent on the attention kernel: its partials must be complete
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long total = static_cast<long long>(batch) * p.L * H;
+  if (w >= total) return;
+  const int h = static_cast<int>(w % H);
+  const long long zq = w / H;
+  const int q = static_cast<int>(zq % p.L), z = static_cast<int>(zq / p.L);
+  const long long base = (static_cast<long long>(z) * H + h) * p.kv_splits * p.lpad + q;
+  float M = -INFINITY;
+  for (int s = 0; s < p.kv_splits; ++s) M = fmaxf(M, p.part_ml[base + static_cast<long long>(s) * p.lpad].x);
+  constexpr int kPer = D / 32;
+  float acc[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) acc[i] = 0.f;
+  float den = 0.f;
+  if (M != -INFINITY) {
+    for (int s = 0; s < p.kv_splits; ++s) {
+      const long long r = base + static_cast<long long>(s) * p.lpad;
+      const float2 ml = p.part_ml[r];
+      const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      den += wgt * ml.y;
+      const float* src = p.part_o + r * D + lane * kPer;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) acc[i] += wgt * src[i];
+    }
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  const long long orow = static_cast<long long>(z) * p.L + q;
+  const long long col = static_cast<long long>(h) * D + lane * kPer;
+  if (p.out_bf16) {
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + orow * p.ldo + col;
+#pragma unroll
+    for (int i = 0; i < kPer; i += 2)
+      *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(acc[i] * inv, acc[i + 1] * inv);
+  } else {
+    float* dst = static_cast<float*>(p.out) + orow * p.ldo + col;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) dst[i] = acc[i] * inv;
+  }
+}
+
 // Q, K, V bf16 [L, ld] with head h at columns [h*D, (h+1)*D): one 3-D tensor map each
 // (D-wide rows, head stride D); rows past L are zero-filled by TMA.
 template <int D>
@@ -585,9 +668,15 @@ b2g_status launch_flash(const __nv_bfloat16* q, int64_t ldq, const __nv_bfloat16
                                            static_cast<int>(smem)),
                       "cudaFuncSetAttribute(flash_attn)")) != B2G_OK)
     return s;
-  const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows)), static_cast<unsigned>(H),
-                  static_cast<unsigned>(batch));
-  return launch_pdl(flash_attn_kernel<D>, grid, dim3(kFaThreads), smem, st, "flash_attn launch", tq, tk, tv, fp);
+  const dim3 grid(static_cast<unsigned>((L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows) * fp.kv_splits),
+                  static_cast<unsigned>(H), static_cast<unsigned>(batch));
+  if ((s = launch_pdl(flash_attn_kernel<D>, grid, dim3(kFaThreads), smem, st, "flash_attn launch", tq, tk, tv, fp)) !=
+      B2G_OK)
+    return s;
+  if (fp.kv_splits <= 1) return B2G_OK;
+  const long long warps = batch * L * H;
+  return launch_pdl(attn_combine_kernel<D>, dim3(static_cast<unsigned>((warps * 32 + 255) / 256)), dim3(256), 0, st,
+                    "attention combine launch", fp, static_cast<int>(H), static_cast<int>(batch));
 }
 
 // Shared checks and launch of the fused kernel on bf16 operands.
@@ -617,6 +706,27 @@ b2g_status flash_checked(const AttnBf16Args& a, cudaStream_t st) {
   fp.err = dev->err_word;
   if (a.batch < 1 || a.batch > 65535 || L * a.batch > (1ll << 30) || a.bias_stride < 0)
     return set_error(B2G_ERR_INVALID, "attention: batch in [1, 65535], batch * L < 2^30, bias stride >= 0");
+  // Key splits when the launch fills under half of the SMs (a tensor-parallel rank's few heads):
+  // as many slices as keep every CTA on the GPU at once, each of at least 4 key blocks.
+  const long long ctas = (L + kFaTiles * kFaRows - 1) / (kFaTiles * kFaRows) * H * a.batch;
+  int splits = 1;
+  if (g_attn_splits > 0) {
+    splits = g_attn_splits;
+  } else if (g_attn_splits == 0 && 2 * ctas <= dev->num_sms) {
+    splits = static_cast<int>(dev->num_sms / ctas);
+  }
+  if (splits > fp.num_kb / 4) splits = fp.num_kb / 4;
+  if (splits < 1) splits = 1;
+  fp.kv_splits = splits;
+  if (splits > 1) {
+    fp.lpad = static_cast<int>(round_up(L, kFaTiles * kFaRows));
+    const size_t rows = static_cast<size_t>(a.batch) * H * splits * fp.lpad;
+    const size_t o_bytes = round_up(static_cast<int64_t>(rows * D * sizeof(float)), 256);
+    void* ws = nullptr;
+    if ((s = workspace_get(o_bytes + rows * sizeof(float2), &ws, kWsAttnSplit)) != B2G_OK) return s;
+    fp.part_o = static_cast<float*>(ws);
+    fp.part_ml = reinterpret_cast<float2*>(static_cast<char*>(ws) + o_bytes);
+  }
   if (D == 128) return launch_flash<128>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, a.batch, st);
   return launch_flash<64>(a.q, a.ldq, a.k, a.ldk, a.v, a.ldv, fp, L, H, a.batch, st);
 }

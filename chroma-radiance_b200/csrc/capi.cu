@@ -172,9 +172,15 @@ const char* b2g_version(void) { return "b2g 0.1 (sm_100a tcgen05)"; }
 
 uint64_t b2g_launch_count(void) { return g_launches.load(); }
 
+b2g_status b2g_set_attention_splits(int splits) {
+  if (splits < -1 || splits > 16) return set_error(B2G_ERR_INVALID, "b2g_set_attention_splits: splits in [-1, 16]");
+  g_attn_splits = splits;
+  return B2G_OK;
+}
+
 b2g_status b2g_set_gemm_variant(int variant, int splits) {
   if (variant < -1 || variant > 2) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: variant in [-1, 2]");
-  if (splits < 0 || splits > 16) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: splits in [0, 16]");
+  if (splits < -16 || splits > 16) return set_error(B2G_ERR_INVALID, "b2g_set_gemm_variant: splits in [-16, 16]");
   tc_gemm_set_variant(variant, 1, splits);
   return B2G_OK;
 }

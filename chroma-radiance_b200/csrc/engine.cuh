@@ -115,7 +115,7 @@ b2g_status launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 // Workspaces (device memory owned by the library, grown on demand, never shrunk), one per
 // purpose so that one call can use several.  kWsCounters is zero-filled when (re)allocated
 // and kernels leave it zero.
-enum WorkspaceSlot { kWsOperands = 0, kWsSplitK = 1, kWsCounters = 2, kWsAttention = 3, kWsSlots = 4 };
+enum WorkspaceSlot { kWsOperands = 0, kWsSplitK = 1, kWsCounters = 2, kWsAttention = 3, kWsAttnSplit = 4, kWsSlots = 5 };
 b2g_status workspace_get(size_t bytes, void** ptr, int slot = kWsOperands);
 void workspace_release();
 
@@ -153,6 +153,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
 // Kernel variant override for tests/tuning: -1 automatic, 0 = 1-CTA 128x128 tiles,
 // 1 = 1-CTA 128x256 tiles, 2 = 2-CTA 256x256 tiles.
 void tc_gemm_set_variant(int force_variant, int allow_pair, int force_splits);
+extern int g_attn_splits;  // fused attention key splits: 0 automatic, -1 never, > 0 forced
 
 // Attention with RoPE (attention.cu).  q, k, v F32 rows of H*D (row strides ldq/ldk/ldv);
 // q_norm/k_norm: optional per-head RMSNorm scales [D] (eps) fused into the Q/K producer;

@@ -107,9 +107,10 @@ struct TcParams {
   int* err;
   uint32_t idesc;
   int a_keep;              // 1: keep A in L2 (evict_last), stream B (evict_first); 0: reverse
-  int splits;              // split-K factor S (1 = none); work item = (split, tile)
-  int num_items;           // num_tiles * splits
-  float* ws;               // split-K partials [slot][split][128][BN] fp32
+  int splits;              // split-K factor S of the split tiles (1 = none)
+  int dp_tiles;            // tiles [0, dp_tiles) run whole; tiles [dp_tiles, num_tiles) split S ways
+  int num_items;           // dp_tiles + (num_tiles - dp_tiles) * splits
+  float* ws;               // split-K partials [slot][split][128][BN] fp32 (slots of the split tiles)
   int* counters;           // split-K arrival counter per slot (zero between launches)
   int tma_store;           // 1: outputs leave through smem staging + TMA bulk tensor stores
   float alpha;             // accumulator scale before the bias (1 for every linear layer)
@@ -192,11 +193,24 @@ __device__ __forceinline__ void round_stage_tf32(uint8_t* stage, int lane) {
   }
 }
 
-// Work item -> (tile, split, k-block range).  Items are split-major so the CTAs running at
-// the same time share K ranges (and therefore A/B panels in L2).
+// Work item -> (tile, split, k-block range).  Items [0, dp_tiles) are whole tiles (split -1);
+// the rest cover the split tiles split-major, so the CTAs running at the same time share K
+// ranges (and therefore A/B panels in L2).  dp_tiles = 0 is plain split-K over every tile;
+// dp_tiles = num_tiles, no split.  A launch whose tiles fill some whole waves plus a partial
+// one splits only the partial wave's tiles: their pieces fill the last wave instead of leaving
+// most SMs idle through it.
 __device__ __forceinline__ void item_coords(int item, const TcParams& p, int& tile, int& split, int& kb0, int& kb1) {
-  split = item / p.num_tiles;
-  tile = item - split * p.num_tiles;
+  if (item < p.dp_tiles) {
+    tile = item;
+    split = -1;
+    kb0 = 0;
+    kb1 = p.num_k_blocks;
+    return;
+  }
+  const int rest = p.num_tiles - p.dp_tiles;
+  const int j = item - p.dp_tiles;
+  split = j / rest;
+  tile = p.dp_tiles + (j - split * rest);
   kb0 = static_cast<int>(static_cast<long long>(split) * p.num_k_blocks / p.splits);
   kb1 = static_cast<int>(static_cast<long long>(split + 1) * p.num_k_blocks / p.splits);
 }
@@ -720,9 +734,10 @@ __device__ __forceinline__ void qkv_rope_item(const TcParams& p, const TcGroup& 
 
 // Epilogue of one work item by the 8 epilogue warps of a CTA.  `tacc` addresses the
 // accumulator's column 0 at this warp's lane quarter; `release()` hands the accumulator back
-// after this warp's last chunk is read.  With split-K, each split stores its raw fp32
-// partial; the split arriving last on the slot's counter sums all partials in split order
-// (deterministic), runs the epilogue and re-arms the counter for the next launch.
+// after this warp's last chunk is read.  For a piece of a split tile (split >= 0), each split
+// stores its raw fp32 partial; the split arriving last on the slot's counter sums all partials
+// in split order (deterministic), runs the epilogue and re-arms the counter for the next
+// launch.  `slot` numbers the split tiles' CTA-tiles (and, for the TP epilogue, every tile's).
 template <int BN, int EPI, int OUT, int KIND, typename Release>
 __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& G, const EpiCtx& e, int& obuf,
                                               uint32_t tacc, Release release, const CUtensorMap* tmD, int bz, int m,
@@ -740,7 +755,7 @@ __device__ __forceinline__ void epilogue_item(const TcParams& p, const TcGroup& 
   const int c0 = e.half * NCH;
   const int m_warp0 = m - e.lane;
   const float* sb = p.bias_kind ? e.sbias : nullptr;
-  const bool splitk = p.splits > 1;
+  const bool splitk = split >= 0 && p.splits > 1;
   // Split-K partials: one 128 x BN fp32 block per (slot, split), stored so that a warp's 32
   // rows of one 4-column group are 32 consecutive 16-byte words (float4 index
   // (chunk * 8 + j) * 128 + row): every store and fixup load of a warp is one coalesced 512 bytes.
@@ -1012,7 +1027,7 @@ __global__ void __launch_bounds__(kThreadsK<KIND>, 1)
         if (lane == 0) mbar_arrive(&tempty_bar[acc]);
       };
       epilogue_item<BN, EPI, OUT, KIND>(p, G, e, obuf, tacc, release, &maps.d[gi], bz, mb * kBM + e.row, nb * BN,
-                                        tile, split);
+                                        split >= 0 ? tile - p.dp_tiles : tile, split);
     }
     if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
@@ -1217,7 +1232,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       };
       epilogue_item<BN, EPI, OUT, KIND>(p, G, e, obuf, tacc, release, &maps.d[gi], bz,
                                   mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN,
-                                  tile * 2 + static_cast<int>(rank), split);
+                                  (split >= 0 ? tile - p.dp_tiles : tile) * 2 + static_cast<int>(rank), split);
     }
     if (lane == 0) bulk_wait_group_all();
   }
@@ -1244,12 +1259,17 @@ constexpr double kCostPair = 1.0;
 // Measured: the reduction is latency-bound and rarely pays, so automatic selection only
 // splits when it removes at least this much time.
 constexpr double kSplitOverhead = 24.0;
+// A launch that splits only the tiles of its last, partial wave (their pieces fill that wave):
+// a fixed cost plus one per split (each piece stores a 128 x BN fp32 partial; the last sums
+// them all), fitted to B200 timings of such launches at S = 2, 4, 8.
+constexpr double kTailFixed = 17.0;
+constexpr double kTailPerSplit = 5.0;
 // Shared-memory ring depth (6 x 32 KB measured slightly faster than 7 on B200).
 constexpr int kPairStages = 6;
 constexpr int kStages128 = 6;
 constexpr int kStages256 = 4;  // 4 x 48 KB
 int g_force_variant = -1;  // -1 auto, 0 = 1-CTA 128, 1 = 1-CTA 256, 2 = 2-CTA pair
-int g_force_splits = 0;    // 0 auto, else split-K factor
+int g_force_splits = 0;    // 0 auto, > 0 split-K factor of every tile, < 0 split factor of the last wave's tiles
 bool g_allow_pair = true;
 int g_tma_store = -1;      // stage outputs through smem and TMA stores (B2G_TMA_STORE=0 disables)
 
@@ -1450,6 +1470,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   // reduction overhead.  The tiles of all problems of the launch form one pool of work.
   enum { V128 = 0, V256 = 1, VPAIR = 2 };
   int v = VPAIR, splits = 1;
+  bool tail_only = false;  // split only the tiles of the last, partial wave
   double best = 1e300;
   for (int cand = 0; cand < 3; ++cand) {
     if (cand == VPAIR && !g_allow_pair) continue;
@@ -1470,14 +1491,33 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
         best = cost;
         v = cand;
         splits = sk;
+        tail_only = false;
+      }
+    }
+    // Whole tiles for the full waves, the partial wave's tiles split to fill one wave.
+    const long long full = tiles / slots, rest = tiles % slots;
+    if (full >= 1 && rest > 0) {
+      for (long long sk = 2; sk <= 8 && sk <= nkb && rest * sk <= slots; ++sk) {
+        const double last = static_cast<double>((nkb + sk - 1) / sk);
+        const double cost = kb_cost * (static_cast<double>(full) * nkb + last + kTailFixed + kTailPerSplit * sk);
+        if (cost < best - 1e-9) {
+          best = cost;
+          v = cand;
+          splits = static_cast<int>(sk);
+          tail_only = true;
+        }
       }
     }
   }
   if (g_force_variant >= 0) {
     v = g_force_variant;
-    if (g_force_splits <= 0) splits = 1;
+    if (g_force_splits == 0) splits = 1;
   }
-  if (g_force_splits > 0) splits = static_cast<int>(g_force_splits < nkb ? g_force_splits : nkb);
+  if (g_force_splits != 0) {
+    const int f = g_force_splits > 0 ? g_force_splits : -g_force_splits;
+    splits = static_cast<int>(f < nkb ? f : nkb);
+    tail_only = g_force_splits < 0;
+  }
   if (nkb == 0 || !p.allow_split || p.tp || p.rope) splits = 1;
   if (p.rope && v == V128) v = g_allow_pair ? VPAIR : V256;
   if (p.round_tf32 && v == VPAIR) v = V256;
@@ -1523,8 +1563,15 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     b_bytes += static_cast<double>(q.N) * q.K;
   }
   prm.num_tiles = tiles;
+  {
+    // Split tiles: all of them, or (tail_only) those of the last wave when it is partial.
+    const int slots = pair ? pairs : sms;
+    const int rest = tiles % slots;
+    prm.dp_tiles = splits <= 1 ? tiles : (tail_only ? (rest == 0 ? tiles : (tiles < slots ? 0 : tiles - rest)) : 0);
+    if (splits > 1 && prm.dp_tiles == tiles) splits = 1;
+  }
   prm.splits = splits;
-  prm.num_items = prm.num_tiles * splits;
+  prm.num_items = prm.dp_tiles + (prm.num_tiles - prm.dp_tiles) * splits;
   prm.d_bstride = p.batch > 1 ? p.d_bstride : 0;
   prm.bias_kind = p.bias ? (p.bias_dtype == B2G_F32 ? 1 : 2) : 0;
   prm.alpha = p.alpha;
@@ -1536,7 +1583,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   if (prm.num_tiles == 0) return B2G_OK;
 
   if (splits > 1) {
-    const size_t slots = static_cast<size_t>(prm.num_tiles) * (pair ? 2 : 1);
+    const size_t slots = static_cast<size_t>(prm.num_tiles - prm.dp_tiles) * (pair ? 2 : 1);
     void* ws = nullptr;
     void* ctr = nullptr;
     if ((s = workspace_get(slots * splits * 128 * bn * sizeof(float), &ws, kWsSplitK)) != B2G_OK) return s;

@@ -412,9 +412,16 @@ uint64_t b2g_launch_count(void);
 
 /* Tensor-core kernel selection for tests and tuning (no reference counterpart):
  * variant -1 automatic (default), 0 = one CTA per 128x128 tile, 1 = one CTA per 128x256
- * tile, 2 = a 2-CTA cluster per 256x256 tile; splits 0 automatic, else the split-K factor
- * (partials reduced in a fixed order by the last split).  Affects later calls. */
+ * tile, 2 = a 2-CTA cluster per 256x256 tile; splits 0 automatic, > 0 the split-K factor of
+ * every tile, < 0 (-S) whole tiles for the full waves and the last, partial wave's tiles split
+ * S ways (partials reduced in a fixed order by the last split).  Affects later calls. */
 b2g_status b2g_set_gemm_variant(int variant, int splits);
+
+/* Fused-attention key splits for tests and tuning (no reference counterpart): 0 automatic
+ * (a launch that fills under half of the SMs, e.g. a tensor-parallel rank's few heads, splits
+ * its key blocks into slices run by separate CTAs and merged by a second kernel), -1 never,
+ * > 0 that many slices (at most one per 4 key blocks).  Affects later calls. */
+b2g_status b2g_set_attention_splits(int splits);
 
 #ifdef __cplusplus
 }

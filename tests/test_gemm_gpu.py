@@ -105,6 +105,33 @@ def test_every_kernel_variant(engine, variant, M, N, K):
     check(out16, gelu_t(ref))
 
 
+@pytest.mark.parametrize("splits", [-2, -5, -8])
+@pytest.mark.parametrize("variant,M,N,K", [(2, 512, 10240, 1024), (0, 1024, 2560, 512), (1, 1024, 5120, 640)])
+def test_split_last_wave(engine, variant, splits, M, N, K):
+    """Whole tiles for the full waves and the last, partial wave's tiles split (80 pair tiles
+    on 74 SM pairs, 160 tiles on 148 SMs): every epilogue kind, twice in a row."""
+    x = seeded((M, K), 5 * M + K)
+    w = seeded((N, K), 3 * N + K, 0.02)
+    bias = seeded((N,), 23, 0.02, torch.float32)
+    gate = seeded((N,), 24, 1.0, torch.float32)
+    r0 = seeded((M, N), 25, 1.0, torch.float32)
+    ref = fp32_ref(x, w, bias)
+    try:
+        engine.set_gemm_variant(variant, splits)
+        for _ in range(2):
+            out = engine.gemm(x, w, bias, out_dtype=torch.float32)
+            g16 = engine.gemm(x, w, bias, out_dtype=torch.bfloat16, epilogue="gelu")
+            res = r0.clone()
+            engine.gemm(x, w, bias, out=res, epilogue="gated_residual", gate=gate)
+            torch.cuda.synchronize()
+            check(out, ref)
+            check(g16, gelu_t(ref))
+            assert rel_err(res.cpu().numpy(), (r0.double() + gate.double() * ref).cpu().numpy()) <= TOL_F32_OUT
+    finally:
+        engine.set_gemm_variant(-1, 0)
+    engine.check_device_error()
+
+
 @pytest.mark.parametrize("variant", [0, 1, 2])
 @pytest.mark.parametrize("splits", [2, 3, 5])
 @pytest.mark.parametrize("M,N,K", [(512, 3072, 3072), (300, 700, 2000), (1024, 3072, 12288)])
@@ -634,6 +661,51 @@ def test_attention_bf16_vs_reference_sdpa(engine, T, I):
     # Both round O to bf16 (½ ulp = 2^-9 relative each); the softmax is fp32 in both.
     assert rel_err(a, b) < 1e-2
     assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.99999
+
+
+@pytest.mark.parametrize("L,H,splits,batch", [(4608, 3, 0, 1), (4608, 3, 3, 1), (1536, 2, 2, 2), (640, 1, 0, 1)])
+def test_attention_key_splits(engine, L, H, splits, batch):
+    """Key-split attention (a launch too small to fill the GPU, e.g. a tensor-parallel rank's 3
+    heads: slices of the key blocks in separate CTAs, merged by a second kernel; splits 0 =
+    the automatic choice) against the one-pass kernel on the same bf16 inputs, bf16 and F32
+    out, with a key mask, twice in a row."""
+    D, T = 128, 512
+    g = torch.Generator(device=DEV).manual_seed(17)
+    qkv = torch.randn((batch * L, 3 * H * D), generator=g, device=DEV).to(torch.bfloat16)
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
+    mask = torch.zeros((batch, L), device=DEV)
+    mask[:, min(T, L) - 100:min(T, L)] = float("-inf")
+    mask = mask if batch > 1 else mask[0]
+    run = (lambda dt: engine.attention_bf16_batched(q, k, v, H, D, batch, attn_mask=mask, out_dtype=dt)) \
+        if batch > 1 else (lambda dt: engine.attention_bf16(q, k, v, H, D, attn_mask=mask, out_dtype=dt))
+    # fp64 softmax(q k^T / sqrt(D) + mask) v per sequence and head
+    want = torch.empty((batch * L, H * D), dtype=torch.float64, device=DEV)
+    mrow = mask.view(batch, L).double()
+    for z in range(batch):
+        rows = slice(z * L, (z + 1) * L)
+        for h in range(H):
+            cols = slice(h * D, (h + 1) * D)
+            sc = q[rows, cols].double() @ k[rows, cols].double().t() / np.sqrt(D) + mrow[z][None, :]
+            want[rows, cols] = torch.softmax(sc, dim=-1) @ v[rows, cols].double()
+    b = want.cpu().numpy().ravel()
+    try:
+        engine.set_attention_splits(-1)
+        one_pass = run(torch.float32).double().cpu().numpy().ravel()
+        engine.set_attention_splits(splits)
+        for _ in range(2):
+            for dt in (torch.float32, torch.bfloat16):
+                got = run(dt)
+                torch.cuda.synchronize()
+                a = got.double().cpu().numpy().ravel()
+                # P is rounded to bf16 against each slice's own running max, so the slices' sums
+                # differ from the one-pass kernel's at bf16 precision; both are held to the fp64
+                # result by the block-path attention tolerance.
+                assert rel_err(a, b) < 1e-2
+                assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
+                assert rel_err(a, one_pass) < 1e-2
+    finally:
+        engine.set_attention_splits(0)
+    engine.check_device_error()
 
 
 def test_nerf_block_gemms_vs_reference(engine, ref):
