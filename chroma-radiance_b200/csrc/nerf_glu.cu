@@ -12,15 +12,19 @@
 // 512^2).  Here each patch's intermediates live in shared memory and TMEM; HBM sees the
 // param_generator row once (192 KB) and the state once in and once out (64 KB each).
 //
-// Per patch, the 256 MLP columns go in 4 chunks of 64:
+// A work item is one half of a patch (128 of its 256 pixel rows); the two halves of a patch
+// are consecutive items, so two CTAs read its parameter row at about the same time (one from
+// HBM, one from L2).  Two CTAs share an SM (84 KB of shared memory and 256 TMEM columns each),
+// so one CTA's loads and normalisation overlap the other's MMAs and SiLU.  Per item, the 256
+// MLP columns go in 4 chunks of 64:
 //   threads   load the chunk's gate / value / fc2 slices, normalise (the fc2 norms, which
 //             span all 256 columns, come from one pass before the chunks), round to TF32 and
 //             write them as K-major operands with the 128-byte swizzle of the UMMA descriptors;
-//   thread 0  issues x1, x2 (M = 128 x 2 row tiles, N = 64, K = 64) into TMEM;
-//   threads   read x1, x2 from TMEM (warp w: row tile w/4, lanes 32(w%4)..), write
+//   thread 0  issues x1, x2 (M = 128, N = 64, K = 64) into TMEM;
+//   threads   read x1, x2 from TMEM (warp w: lanes 32(w%4).., columns 32(w/4)..), write
 //             TF32(silu(x1) * x2) as the A operand of the fc2 product;
 //   thread 0  issues x_out += h . w_fc2^T (N = 64, K = 64 of this chunk) into TMEM.
-// Then every thread adds its row of x_out to the state and stores it.
+// Then every thread adds its part of x_out to the state and stores it.
 //
 // TF32 rounding (round to nearest even) happens where cuBLAS rounds the reference's
 // CUBLAS_COMPUTE_32F_FAST_16BF operands: the normalised weights, the normed state and the
@@ -33,21 +37,26 @@
 namespace b2g {
 namespace {
 
-constexpr int kHid = 64, kMlp = 256, kRows = 256, kChunk = 64, kChunks = kMlp / kChunk;
+constexpr int kHid = 64, kMlp = 256, kRows = 128, kChunk = 64, kChunks = kMlp / kChunk;
+constexpr int kPatchRows = 256;     // pixel rows of a patch; a work item is kRows of them
 constexpr int kGluThreads = 256;
-constexpr int kTmemCols = 512;       // D1 [0,128), D2 [128,256), D3 [256,384): two 64-column row tiles each
+constexpr int kTmemCols = 256;       // D1 [0,64), D2 [64,128), D3 [128,192)
 // Shared memory (bytes from a 1024-aligned base): K-major fp32 operands, 128-byte swizzle,
 // one "atom" = 32 fp32 of K (128 bytes) per row, 8-row groups of 1024 bytes.
-constexpr int kOffA1 = 0;                          // xn       [256 rows][K = 64 h]   2 atoms x 32 KB
-constexpr int kOffA3 = kOffA1 + kRows * kHid * 4;  // h chunk  [256 rows][K = 64 m]   2 atoms x 32 KB
-constexpr int kOffB1 = kOffA3 + kRows * kChunk * 4;  // gate    [64 m rows][K = 64 h] 2 atoms x 8 KB
+// The h chunk (A3) takes the place of the gate and value chunks (B1, B2): those are free once
+// the x1, x2 MMAs have completed, and the next chunk's weights are written only after the fc2
+// MMA that reads A3 has completed.
+constexpr int kOffA1 = 0;                            // xn       [128 rows][K = 64 h]   2 atoms x 16 KB
+constexpr int kOffB1 = kOffA1 + kRows * kHid * 4;    // gate    [64 m rows][K = 64 h] 2 atoms x 8 KB
 constexpr int kOffB2 = kOffB1 + kChunk * kHid * 4;   // value   [64 m rows][K = 64 h]
+constexpr int kOffA3 = kOffB1;                       // h chunk  [128 rows][K = 64 m]   2 atoms x 16 KB
 constexpr int kOffB3 = kOffB2 + kChunk * kHid * 4;   // fc2     [64 h rows][K = 64 m]
+static_assert(kRows * kChunk * 4 == 2 * kChunk * kHid * 4, "A3 fills exactly B1 and B2");
 constexpr int kOffPart = kOffB3 + kHid * kChunk * 4;  // float [2][4][64] partial sums of squares
 constexpr int kOffInvF = kOffPart + 2 * 4 * 64 * 4;   // float [64] fc2 inverse norms
 constexpr int kOffBar = kOffInvF + 64 * 4;            // 3 mbarriers + TMEM slot
 constexpr int kGluSmem = kOffBar + 64 + 1024;         // + alignment slack
-static_assert(kGluSmem <= 227 * 1024, "shared memory");
+static_assert(2 * kGluSmem <= 227 * 1024, "shared memory for two CTAs per SM");
 
 // Byte offset of fp32 element (r, k) in a K-major operand of `rows` rows and K = 64.
 __device__ __forceinline__ uint32_t sw_off(int rows, int r, int k) {
@@ -61,9 +70,10 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-__global__ void __launch_bounds__(kGluThreads, 1)
+__global__ void __launch_bounds__(kGluThreads, 2)
     nerf_glu_kernel(const float* __restrict__ params, int64_t ldp, const float* __restrict__ scale,
                     float* __restrict__ x, int64_t patches, float eps, int* err) {
+  const int64_t items = 2 * patches;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* part = reinterpret_cast<float*>(sm + kOffPart);
@@ -90,28 +100,30 @@ __global__ void __launch_bounds__(kGluThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   constexpr uint32_t idesc = idesc_make(kFmtTF32, 128, kChunk);
-  const int tile = warp >> 2, quarter = warp & 3;
-  const int my_row = tile * 128 + quarter * 32 + lane;  // the row this thread owns in the epilogues
+  const int colh = warp >> 2, quarter = warp & 3;
+  const int my_row = quarter * 32 + lane;  // the row this thread owns in the epilogues (columns 32 colh..)
   const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
   uint32_t ph12 = 0, ph3 = 0;
   bool ok = true;
 
-  for (int64_t b = blockIdx.x; b < patches && ok; b += gridDim.x) {
+  for (int64_t item = blockIdx.x; item < items && ok; item += gridDim.x) {
+    const int64_t b = item >> 1;
     const float* prm = params + b * ldp;
-    float* xb = x + b * (kRows * kHid);
-    // The next patch's parameter row and state (256 KB) start moving into L2 now, so that its
-    // loads, which this CTA issues in a few dependent rounds, are L2 hits rather than DRAM trips.
-    if (b + gridDim.x < patches) {
-      const char* np = reinterpret_cast<const char*>(params + (b + gridDim.x) * ldp);
-      const char* nx = reinterpret_cast<const char*>(x + (b + gridDim.x) * (kRows * kHid));
+    float* xb = x + (b * kPatchRows + (item & 1) * kRows) * kHid;
+    // The next item's parameter row and state start moving into L2 now, so that its loads,
+    // which this CTA issues in a few dependent rounds, are L2 hits rather than DRAM trips.
+    if (item + gridDim.x < items) {
+      const int64_t ni = item + gridDim.x;
+      const char* np = reinterpret_cast<const char*>(params + (ni >> 1) * ldp);
+      const char* nx = reinterpret_cast<const char*>(x + ((ni >> 1) * kPatchRows + (ni & 1) * kRows) * kHid);
       for (int i = t; i < 3 * kHid * kMlp * 4 / 128; i += kGluThreads) prefetch_l2(np + i * 128);
       for (int i = t; i < kRows * kHid * 4 / 128; i += kGluThreads) prefetch_l2(nx + i * 128);
     }
-    // ---- normed state -> A1 (each warp 32 rows, each lane 2 columns)
+    // ---- normed state -> A1 (each warp 16 rows, each lane 2 columns)
     const float2 sc = reinterpret_cast<const float2*>(scale)[lane];
 #pragma unroll 8
-    for (int i = 0; i < 32; ++i) {
-      const int r = warp * 32 + i;
+    for (int i = 0; i < kRows / 8; ++i) {
+      const int r = warp * (kRows / 8) + i;
       const float2 v = reinterpret_cast<const float2*>(xb + r * kHid)[lane];
       float ss = v.x * v.x + v.y * v.y;
 #pragma unroll
@@ -181,18 +193,13 @@ __global__ void __launch_bounds__(kGluThreads, 1)
       if (t == 0) {
         tc_fence_after();
 #pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
+        for (int ka = 0; ka < 2; ++ka) {
 #pragma unroll
-          for (int ka = 0; ka < 2; ++ka) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t acc = (ka | k) ? 1u : 0u;
-              const uint64_t ad = smem_desc_k_sw128(sbase + kOffA1 + ka * kRows * 128 + tt * 128 * 128 + k * 32);
-              umma_tf32(tmem + tt * kChunk, ad, smem_desc_k_sw128(sbase + kOffB1 + ka * kChunk * 128 + k * 32), idesc,
-                        acc);
-              umma_tf32(tmem + 128 + tt * kChunk, ad,
-                        smem_desc_k_sw128(sbase + kOffB2 + ka * kChunk * 128 + k * 32), idesc, acc);
-            }
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (ka | k) ? 1u : 0u;
+            const uint64_t ad = smem_desc_k_sw128(sbase + kOffA1 + ka * kRows * 128 + k * 32);
+            umma_tf32(tmem, ad, smem_desc_k_sw128(sbase + kOffB1 + ka * kChunk * 128 + k * 32), idesc, acc);
+            umma_tf32(tmem + kChunk, ad, smem_desc_k_sw128(sbase + kOffB2 + ka * kChunk * 128 + k * 32), idesc, acc);
           }
         }
         umma_commit(bar12);
@@ -203,11 +210,10 @@ __global__ void __launch_bounds__(kGluThreads, 1)
       if (!ok) break;
       tc_fence_after();
       // ---- h = TF32(silu(x1) * x2) -> A3 (this thread's row, the chunk's 64 columns)
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
+      {
         uint32_t r1[32], r2[32];
-        tmem_ld_32x32b_x32(tmem + lane_addr + tile * kChunk + half * 32, r1);
-        tmem_ld_32x32b_x32(tmem + lane_addr + 128 + tile * kChunk + half * 32, r2);
+        tmem_ld_32x32b_x32(tmem + lane_addr + colh * 32, r1);
+        tmem_ld_32x32b_x32(tmem + lane_addr + kChunk + colh * 32, r2);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kGluThreads, 1)
           hv.y = round_tf32_cvt(silu_f(__uint_as_float(r1[4 * j + 1])) * __uint_as_float(r2[4 * j + 1]));
           hv.z = round_tf32_cvt(silu_f(__uint_as_float(r1[4 * j + 2])) * __uint_as_float(r2[4 * j + 2]));
           hv.w = round_tf32_cvt(silu_f(__uint_as_float(r1[4 * j + 3])) * __uint_as_float(r2[4 * j + 3]));
-          *reinterpret_cast<float4*>(sm + kOffA3 + sw_off(kRows, my_row, half * 32 + 4 * j)) = hv;
+          *reinterpret_cast<float4*>(sm + kOffA3 + sw_off(kRows, my_row, colh * 32 + 4 * j)) = hv;
         }
       }
       fence_proxy_async_smem();
@@ -226,16 +232,11 @@ __global__ void __launch_bounds__(kGluThreads, 1)
       if (t == 0) {
         tc_fence_after();
 #pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
+        for (int ka = 0; ka < 2; ++ka) {
 #pragma unroll
-          for (int ka = 0; ka < 2; ++ka) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              umma_tf32(tmem + 256 + tt * kHid,
-                        smem_desc_k_sw128(sbase + kOffA3 + ka * kRows * 128 + tt * 128 * 128 + k * 32),
-                        smem_desc_k_sw128(sbase + kOffB3 + ka * kHid * 128 + k * 32), idesc,
-                        (c | ka | k) ? 1u : 0u);
-            }
+          for (int k = 0; k < 4; ++k) {
+            umma_tf32(tmem + 2 * kChunk, smem_desc_k_sw128(sbase + kOffA3 + ka * kRows * 128 + k * 32),
+                      smem_desc_k_sw128(sbase + kOffB3 + ka * kHid * 128 + k * 32), idesc, (c | ka | k) ? 1u : 0u);
           }
         }
         umma_commit(bar3);
@@ -246,21 +247,20 @@ __global__ void __launch_bounds__(kGluThreads, 1)
       tc_fence_after();
     }
     if (!ok) break;
-    // ---- x += x_out for this thread's row
-    float* xr = xb + my_row * kHid;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
+    // ---- x += x_out for this thread's row, columns 32 colh ..
+    {
+      float* xr = xb + my_row * kHid + colh * 32;
       uint32_t r3[32];
-      tmem_ld_32x32b_x32(tmem + lane_addr + 256 + tile * kHid + half * 32, r3);
+      tmem_ld_32x32b_x32(tmem + lane_addr + 2 * kChunk + colh * 32, r3);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float4 v = reinterpret_cast<const float4*>(xr + half * 32)[j];
+        float4 v = reinterpret_cast<const float4*>(xr)[j];
         v.x += __uint_as_float(r3[4 * j]);
         v.y += __uint_as_float(r3[4 * j + 1]);
         v.z += __uint_as_float(r3[4 * j + 2]);
         v.w += __uint_as_float(r3[4 * j + 3]);
-        reinterpret_cast<float4*>(xr + half * 32)[j] = v;
+        reinterpret_cast<float4*>(xr)[j] = v;
       }
     }
     tc_fence_before();
@@ -300,7 +300,7 @@ extern "C" b2g_status b2g_nerf_glu_block(const float* params, int64_t ldp, const
       return s;
     attr_set[dev->device] = true;
   }
-  const int64_t grid = patches < dev->num_sms ? patches : dev->num_sms;
+  const int64_t grid = 2 * patches < 2 * dev->num_sms ? 2 * patches : 2 * dev->num_sms;
   nerf_glu_kernel<<<static_cast<unsigned>(grid), kGluThreads, kGluSmem, static_cast<cudaStream_t>(stream)>>>(
       params, ldp, norm_scale, x, patches, 1e-6f, dev->err_word);
   note_launch();

@@ -290,35 +290,52 @@ def _qkv_attention_double(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, t
 
 
 def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1, txt_mod2, img_mod2, txt,
-                    img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask, s: TPScratch) -> None:
-    """This rank's share of double_block (chroma.cuh:808-964); txt, img replicated F32 streams."""
+                    img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask, s: TPScratch, mark=None) -> None:
+    """This rank's share of double_block (chroma.cuh:808-964); txt, img replicated F32 streams.
+    `mark(label)`, when given, is called after every step (timing events between them)."""
     T, HDl = txt.shape[0], s.HDl
-    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s)
+    mk = mark or _no_mark
+    _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s, mk)
     ops.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, out=s.part[:T]),
                     dict(x=s.attn[T:], w=img_w.proj_w, out=s.part[T:])])
+    mk("double.proj")
     ops.all_reduce(s.part)
+    mk("double.proj.all_reduce")
     ops.bias_gated_residual(s.part[:T], txt_w.proj_b, txt_gate1, txt)
     ops.bias_gated_residual(s.part[T:], img_w.proj_b, img_gate1, img)
+    mk("double.proj.residual")
     ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
                     dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
+    mk("double.mlp0")
     ops.gemm_group([dict(x=s.h_txt, w=txt_w.mlp2_w, out=s.part[:T]),
                     dict(x=s.h_img, w=img_w.mlp2_w, out=s.part[T:])])
+    mk("double.mlp2")
     ops.all_reduce(s.part)
+    mk("double.mlp2.all_reduce")
     ops.bias_gated_residual(s.part[:T], txt_w.mlp2_b, txt_gate2, txt)
     ops.bias_gated_residual(s.part[T:], img_w.mlp2_b, img_gate2, img)
+    mk("double.mlp2.residual")
 
 
-def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch) -> None:
-    """This rank's share of single_block (chroma.cuh:1101-1157); x the replicated F32 stream."""
+def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch, mark=None) -> None:
+    """This rank's share of single_block (chroma.cuh:1101-1157); x the replicated F32 stream.
+    `mark` as in tp_double_block."""
     HDl = s.HDl
+    mk = mark or _no_mark
     ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
                        q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
+    mk("single.linear1_qkv")
     ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
+    mk("single.linear1_mlp")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
+    mk("single.attention")
     ops.gemm(s.cat, w.linear2_w, out=s.part)
+    mk("single.linear2")
     ops.all_reduce(s.part)
+    mk("single.linear2.all_reduce")
     ops.bias_gated_residual(s.part, w.linear2_b, gate, x)
+    mk("single.linear2.residual")
 
 
 # ---------------------------------------------------------------------------- fused reduction
