@@ -21,6 +21,12 @@ namespace b2g {
 
 namespace {
 
+// res[m][n] += gate[n] * (y[m][n] + bias[n]).  A thread owns 8 columns (one 16-byte bf16 or
+// two float4 loads of y, two float4 of the residual) of kBgrRows consecutive rows: the bias and
+// gate are loaded once (as float4s) for all of them, and every row's loads are issued before
+// any is used.
+constexpr int kBgrRows = 4;
+
 template <bool BF16>
 __global__ void __launch_bounds__(256) bias_gated_residual_kernel(const void* __restrict__ y, long long ldy,
                                                                   const float* __restrict__ bias,
@@ -29,35 +35,58 @@ __global__ void __launch_bounds__(256) bias_gated_residual_kernel(const void* __
                                                                   int N) {
   const int groups = N / 8;  // 8 columns per thread
   const long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-  if (idx >= static_cast<long long>(M) * groups) return;
-  const int m = static_cast<int>(idx / groups), n = static_cast<int>(idx % groups) * 8;
-  float v[8];
-  if constexpr (BF16) {
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(y) + m * ldy + n);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 f = __bfloat1622float2(h[i]);
-      v[2 * i] = f.x;
-      v[2 * i + 1] = f.y;
-    }
-  } else {
-    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(y) + m * ldy + n);
-    const float4 a = p[0], b = p[1];
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-  float4* r = reinterpret_cast<float4*>(res + m * ldr + n);
-  float4 r0 = r[0], r1 = r[1];
+  const long long row_groups = (M + kBgrRows - 1) / kBgrRows;
+  if (idx >= row_groups * groups) return;
+  const int m0 = static_cast<int>(idx / groups) * kBgrRows, n = static_cast<int>(idx % groups) * 8;
   float b[8], g[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    b[i] = bias ? __ldg(bias + n + i) : 0.f;
-    g[i] = __ldg(gate + n + i);
+  {
+    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gate + n)), g1 = __ldg(reinterpret_cast<const float4*>(gate + n) + 1);
+    g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+    float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+    if (bias) {
+      b0 = __ldg(reinterpret_cast<const float4*>(bias + n));
+      b1 = __ldg(reinterpret_cast<const float4*>(bias + n) + 1);
+    }
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
   }
-  r0.x += g[0] * (v[0] + b[0]); r0.y += g[1] * (v[1] + b[1]); r0.z += g[2] * (v[2] + b[2]); r0.w += g[3] * (v[3] + b[3]);
-  r1.x += g[4] * (v[4] + b[4]); r1.y += g[5] * (v[5] + b[5]); r1.z += g[6] * (v[6] + b[6]); r1.w += g[7] * (v[7] + b[7]);
-  r[0] = r0;
-  r[1] = r1;
+  float v[kBgrRows][8];
+  float4 r[kBgrRows][2];
+#pragma unroll
+  for (int k = 0; k < kBgrRows; ++k) {
+    const int m = m0 + k;
+    if (m >= M) break;
+    if constexpr (BF16) {
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(y) + m * ldy + n));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[k][2 * i] = f.x;
+        v[k][2 * i + 1] = f.y;
+      }
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(y) + m * ldy + n);
+      const float4 a = __ldcs(p), c = __ldcs(p + 1);
+      v[k][0] = a.x; v[k][1] = a.y; v[k][2] = a.z; v[k][3] = a.w;
+      v[k][4] = c.x; v[k][5] = c.y; v[k][6] = c.z; v[k][7] = c.w;
+    }
+    const float4* rp = reinterpret_cast<const float4*>(res + m * ldr + n);
+    r[k][0] = rp[0];
+    r[k][1] = rp[1];
+  }
+#pragma unroll
+  for (int k = 0; k < kBgrRows; ++k) {
+    const int m = m0 + k;
+    if (m >= M) break;
+    float4 r0 = r[k][0], r1 = r[k][1];
+    r0.x += g[0] * (v[k][0] + b[0]); r0.y += g[1] * (v[k][1] + b[1]);
+    r0.z += g[2] * (v[k][2] + b[2]); r0.w += g[3] * (v[k][3] + b[3]);
+    r1.x += g[4] * (v[k][4] + b[4]); r1.y += g[5] * (v[k][5] + b[5]);
+    r1.z += g[6] * (v[k][6] + b[6]); r1.w += g[7] * (v[k][7] + b[7]);
+    float4* rp = reinterpret_cast<float4*>(res + m * ldr + n);
+    rp[0] = r0;
+    rp[1] = r1;
+  }
 }
 
 // One 128-thread block per row of x [M, C] (16-byte aligned rows, C % 4 == 0,
@@ -215,7 +244,9 @@ b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, co
       (reinterpret_cast<uintptr_t>(residual) & 15u))
     return set_error(B2G_ERR_UNSUPPORTED, "bias_gated_residual: N % 8 and 16-byte aligned rows required");
   if (M * (N / 8) > (1ll << 40)) return set_error(B2G_ERR_UNSUPPORTED, "bias_gated_residual: size");
-  const long long threads = M * (N / 8);
+  if ((reinterpret_cast<uintptr_t>(gate) & 15u) || (bias && (reinterpret_cast<uintptr_t>(bias) & 15u)))
+    return set_error(B2G_ERR_UNSUPPORTED, "bias_gated_residual: bias and gate must be 16-byte aligned");
+  const long long threads = (M + kBgrRows - 1) / kBgrRows * (N / 8);
   const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
   if (y_dtype == B2G_BF16)
     bias_gated_residual_kernel<true><<<blocks, 256, 0, st>>>(y, ldy, bias, gate, residual, ldr, static_cast<int>(M),

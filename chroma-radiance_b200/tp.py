@@ -29,7 +29,7 @@ from dataclasses import dataclass
 
 import torch
 
-from blocks import DHEAD, HEADS, HIDDEN, MLP, SingleWeights, StreamWeights
+from blocks import DHEAD, HEADS, HIDDEN, MLP, SingleWeights, StreamWeights, _rope_table
 
 
 @dataclass(frozen=True)
@@ -279,6 +279,7 @@ def _qkv_attention_double(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, t
     """The rank's heads: qkv projections with qk_norm and RoPE in the epilogue (txt rows take
     pe rows [0, T), img rows [T, L)), then attention over the txt + img sequence into s.attn."""
     T, HDl = txt_mod1.shape[0], s.HDl
+    pe = _rope_table(pe, s)
     ops.qkv_rope([dict(x=txt_mod1, w=txt_w.qkv_w, bias=txt_w.qkv_b, out=s.qkv[:T], pe=pe[:T],
                        q_norm=txt_w.q_norm, k_norm=txt_w.k_norm),
                   dict(x=img_mod1, w=img_w.qkv_w, bias=img_w.qkv_b, out=s.qkv[T:], pe=pe[T:],
@@ -317,16 +318,21 @@ def tp_double_block(ops, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod
     mk("double.mlp2.residual")
 
 
+def _linear1(ops, w: TPSingleWeights, x_mod, pe, s: TPScratch) -> None:
+    """The rank's linear1 in one launch, as the unsharded block runs it: its q, k, v columns get
+    qk_norm + RoPE into s.qkv, its MLP columns bias + GELU straight into the linear2 input
+    s.cat[:, HDl:] (the split falls on a head boundary at every TP degree)."""
+    ops.qkv_rope([dict(x=x_mod, w=w.linear1_w, bias=w.linear1_b, out=s.qkv, pe=_rope_table(pe, s),
+                       q_norm=w.q_norm, k_norm=w.k_norm, gelu_out=s.cat[:, s.HDl:])], s.hl)
+
+
 def tp_single_block(ops, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch, mark=None) -> None:
     """This rank's share of single_block (chroma.cuh:1101-1157); x the replicated F32 stream.
     `mark` as in tp_double_block."""
     HDl = s.HDl
     mk = mark or _no_mark
-    ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
-                       q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
-    mk("single.linear1_qkv")
-    ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
-    mk("single.linear1_mlp")
+    _linear1(ops, w, x_mod, pe, s)
+    mk("single.linear1")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
     mk("single.attention")
@@ -434,11 +440,8 @@ def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, g
     comm.res_single.  `mark` as in tp_double_block_fused."""
     HDl = s.HDl
     mk = mark or _no_mark
-    ops.qkv_rope([dict(x=x_mod, w=w.linear1_w[:3 * HDl], bias=w.linear1_b[:3 * HDl], out=s.qkv, pe=pe,
-                       q_norm=w.q_norm, k_norm=w.k_norm)], s.hl)
-    mk("single.linear1_qkv")
-    ops.gemm(x_mod, w.linear1_w[3 * HDl:], w.linear1_b[3 * HDl:], out=s.cat[:, HDl:], epilogue="gelu")
-    mk("single.linear1_mlp")
+    _linear1(ops, w, x_mod, pe, s)
+    mk("single.linear1")
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
     mk("single.attention")

@@ -212,7 +212,8 @@ b2g_status b2g_gemm_fp8_group(const b2g_gemm_desc* descs, const float* const* a_
 /* residual[m, n] (F32, row stride ldr) += gate[n] * (y[m, n] + bias[n]) for the tensor-parallel
  * path: the reference's gated_residual (kernels.cu:942-968) with the linear's bias folded in,
  * applied once after the all-reduce of the row-split layer's partial sums (which carry no
- * bias).  y BF16 or F32 (row stride ldy); bias may be NULL.  N % 8 == 0, 16-byte rows. */
+ * bias).  y BF16 or F32 (row stride ldy); bias may be NULL.  N % 8 == 0, 16-byte rows,
+ * 16-byte aligned bias and gate. */
 b2g_status b2g_bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, const float* bias,
                                    const float* gate, float* residual, int64_t ldr, int64_t M, int64_t N,
                                    void* stream);

@@ -47,9 +47,18 @@ class TorchOps:
         for pr in problems:
             y = pr["x"].float() @ pr["w"].float().t() + pr["bias"]
             M = y.shape[0]
-            dh = y.shape[1] // (3 * n_head)
+            dh = D.dhead
+            if pr.get("gelu_out") is not None:   # linear1's MLP columns: bias + GELU
+                t = y[:, 3 * n_head * dh:]
+                pr["gelu_out"].copy_((0.5 * t * (1 + torch.tanh(0.7978845608 * (t + 0.044715 * t ** 3)))).to(
+                    pr["gelu_out"].dtype))
+                y = y[:, :3 * n_head * dh]
             q, k, v = y.reshape(M, 3, n_head, dh).unbind(1)
-            p = pr["pe"].reshape(M, 1, dh // 2, 4)
+            pe = pr["pe"]
+            if pe.shape[-1] == 2:                # compact (cos, sin) table
+                c, sn = pe[..., 0], pe[..., 1]
+                pe = torch.stack([c, -sn, sn, c], -1)
+            p = pe.reshape(M, 1, dh // 2, 4)
 
             def norm_rope(x, scale):
                 if scale is not None:

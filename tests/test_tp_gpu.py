@@ -55,13 +55,17 @@ def test_tp_world1_matches_blocks(engine):
         assert ((d1 @ d0) / (d1.norm() * d0.norm())).item() >= 0.9999, k
 
 
-def test_bias_gated_residual_kernel(engine):
+@pytest.mark.parametrize("M,dtype,with_bias", [(300, torch.bfloat16, True), (301, torch.bfloat16, False),
+                                                (7, torch.float32, True), (4608, torch.bfloat16, True)])
+def test_bias_gated_residual_kernel(engine, M, dtype, with_bias):
+    """residual += gate * (y + bias) after a tensor-parallel all-reduce (gated_residual,
+    kernels.cu:942-968), rows not a multiple of the kernel's 4-row groups included."""
     g = torch.Generator(device=DEV).manual_seed(9)
-    y = torch.randn((300, 3072), generator=g, device=DEV).to(torch.bfloat16)
-    b = torch.randn(3072, generator=g, device=DEV)
+    y = torch.randn((M, 3072), generator=g, device=DEV).to(dtype)
+    b = torch.randn(3072, generator=g, device=DEV) if with_bias else None
     gate = torch.randn(3072, generator=g, device=DEV)
-    r = torch.randn((300, 3072), generator=g, device=DEV)
-    want = r + gate * (y.float() + b)
+    r = torch.randn((M, 3072), generator=g, device=DEV)
+    want = r + gate * (y.float() + (b if with_bias else 0.0))
     engine.bias_gated_residual(y, b, gate, r)
     torch.cuda.synchronize()
     assert torch.allclose(r, want, rtol=1e-6, atol=1e-5)
