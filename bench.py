@@ -463,6 +463,10 @@ def run_reference_config2(args) -> None:
     n_fc = max(3, min(args.steps, 20))
     fc_dev, fc_e2e = h.bench(FC_TIMESTEP, FC_CFG, n_fc, 3, FLUSH_BYTES)
     approx_ms = h.bench_modulation(FC_TIMESTEP, max(5, min(args.steps, 30)), 3, FLUSH_BYTES)
+    import torch
+
+    glu = nerf_glu_leg(torch, torch.device("cuda", 0), None, None, (FC_H // 16) * (FC_W // 16),
+                       max(5, min(args.steps, 30)), h=h)
     fc_dev, fc_e2e = _ref_world_max(world, [fc_dev, fc_e2e])
     fc_flop = model.step_flops(FC_H, FC_W)["total"]
     lin, att = blocks.block_pair_flops(T_TXT, I_IMG)
@@ -503,6 +507,7 @@ def run_reference_config2(args) -> None:
         "tp1024": tp_ref,
         "attention": attn,
         "approximator": approx,
+        "nerf_glu_block": glu,
         "t5": t5,
     }), flush=True)
 
@@ -825,6 +830,49 @@ def approximator_leg(torch, dev, flush, stream, run, steps: int, ms_list=None) -
     return out
 
 
+def nerf_glu_leg(torch, dev, flush, stream, P: int, steps: int, m=None, h=None) -> dict:
+    """One NeRF GLU block (nerf_glu_block, chroma.cuh:1253-1306) alone at one guidance half's
+    P patches, both arms on their own block-0 weights and the same seeded x [P, 256, 64] and
+    s [P, 3072]: the reference's whole block (param_generator linear, weight slices and L2
+    norms, rms_norm, three cuBLAS batched products, silu_mul, residual add; `h`, its harness),
+    or the engine's cast of s, param_generator GEMM and fused GLU kernel (`m`).  Median per call
+    (CUDA events, L2 flushed before each)."""
+    g = torch.Generator(device=dev).manual_seed(31)
+    x = torch.randn((P, 256, 64), generator=g, device=dev)
+    sv = torch.randn((P, 3072), generator=g, device=dev)
+    if h is not None:
+        ms = h.bench_nerf_glu_block(0, x, sv, steps, 3, FLUSH_BYTES)
+        what = "the reference's nerf_glu_block: 14 launches (cuBLASLt linear, cuBLAS batched products, its kernels)"
+    else:
+        import b2g
+
+        blk = m.nerf[0]
+        s16 = torch.empty((P, 3072), dtype=torch.bfloat16, device=dev)
+        params = torch.empty((P, blk.param_w.shape[0]), device=dev)
+
+        def run():
+            b2g.convert_f32(sv, s16)
+            b2g.gemm(s16, blk.param_w, blk.param_b, out=params)
+            b2g.nerf_glu_block(params, blk.norm, x)
+
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize(dev)
+        ms = []
+        for i in range(steps):
+            flush.fill_(i & 0xFF)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            run()
+            b.record(stream)
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        what = "the engine: cast of s, param_generator GEMM (tc_gemm), nerf_glu_kernel (3 launches)"
+    return {"us": round(1e3 * statistics.median(ms), 1), "patches": P, "kernels": what,
+            "workload": "one NeRF GLU block at 512^2 for one guidance half (1024 patches), block 0's weights, "
+                        "seeded x and s; median of per-call CUDA-event times, L2 flushed before each"}
+
+
 def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
     """The engine's whole denoising step (model.ChromaRadiance.forward_cfg) through the public API,
     captured in one CUDA graph; every step copies its inputs (noise, both T5 contexts, the
@@ -909,6 +957,7 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
                                                                   s.velocity.view(3, FC_H, FC_W)))}
     approx = approximator_leg(torch, dev, flush, stream, lambda mark=None: m.compute_modulation(s, mark),
                               max(5, min(args.steps, 30)))
+    glu = nerf_glu_leg(torch, dev, flush, stream, s.P, max(5, min(args.steps, 30)), m=m)
     flops = model.step_flops(FC_H, FC_W)
     out = {"unit": "TFLOP/s", "ms_per_step": ms, "flop_per_step": flops["total"],
            "h2d_bytes_per_step": sum(host[k].numel() * host[k].element_size() for k in host),
@@ -921,7 +970,7 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
            "parts_tflop": {k: round(flops[k] / 1e12, 4) for k in ("embed", "approximator", "blocks", "nerf")},
            "launches_per_step": launches, "step_ms_min_median": [round(min(times), 4),
                                                                  round(statistics.median(times), 4)],
-           "approximator": approx}
+           "approximator": approx, "nerf_glu_block": glu}
     del graph, m, s
     torch.cuda.empty_cache()
     if dropin:
@@ -976,12 +1025,12 @@ def _tp_categories(us: dict) -> dict:
     """Sums of a per-operation split: column-split GEMMs, attention, row-split GEMMs (with the
     fused all-rank reduction at N > 1) and cross-rank barriers."""
     cat = {"column_gemms": 0.0, "attention": 0.0, "row_gemms_with_reduction": 0.0, "barriers": 0.0,
-           "nccl_all_reduce": 0.0, "bias_gated_residual": 0.0}
+           "all_reduce": 0.0, "bias_gated_residual": 0.0}
     for lab, v in us.items():
         if lab.endswith(".barrier"):
             cat["barriers"] += v
-        elif lab.endswith(".all_reduce"):
-            cat["nccl_all_reduce"] += v
+        elif lab.endswith(".all_reduce") or lab.endswith(".reduce"):
+            cat["all_reduce"] += v
         elif lab.endswith(".residual"):
             cat["bias_gated_residual"] += v
         elif "attention" in lab:
@@ -1131,35 +1180,55 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
 
     per_n = timed(nccl, True)
     sp_n = split(nccl)
+    pres = {k: v.clone() for k, v in res.items()}
+
+    def p2p(mark=None):
+        tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                               pres["txt"], pres["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch, mark)
+        tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], pres["x"], gt[4], pe, mask, scratch, mark)
+
+    p2p()
+    barrier()
+    if rank == 0:
+        got = {k: delta(pres[k], res[k]) for k in res}
+        parity["p2p"] = {k: {"max_rel": float((got[k] - ref[k]).abs().max() / ref[k].abs().max()),
+                             "cosine": float((got[k] @ ref[k]) / (got[k].norm() * ref[k].norm()))} for k in got}
+        parity["within_tolerance"] = parity["within_tolerance"] and all(
+            v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999 for v in parity["p2p"].values())
+    per_p = timed(p2p, True)
+    sp_p = split(p2p)
     b2g_mod = __import__("b2g")
     b2g_mod.check_device_error()
-    labels, labels_n = sorted(sp), sorted(sp_n)
-    t = torch.tensor([sum(per_f), sum(per_n)] + [sp[k] for k in labels] + [sp_n[k] for k in labels_n], device=dev,
-                     dtype=torch.float64)
+    labels, labels_n, labels_p = sorted(sp), sorted(sp_n), sorted(sp_p)
+    t = torch.tensor([sum(per_f), sum(per_n), sum(per_p)] + [sp[k] for k in labels] + [sp_n[k] for k in labels_n] +
+                     [sp_p[k] for k in labels_p], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    f_ms, n_ms = float(t[0]) / steps, float(t[1]) / steps
-    vals = t[2:].tolist()
+    f_ms, n_ms, p_ms = float(t[0]) / steps, float(t[1]) / steps, float(t[2]) / steps
+    vals = t[3:].tolist()
     sp = {k: float(v) for k, v in zip(labels, vals[:len(labels)])}
-    sp_n = {k: float(v) for k, v in zip(labels_n, vals[len(labels):])}
+    sp_n = {k: float(v) for k, v in zip(labels_n, vals[len(labels):len(labels) + len(labels_n)])}
+    sp_p = {k: float(v) for k, v in zip(labels_p, vals[len(labels) + len(labels_n):])}
     u = torch.tensor([uns_ms or 0.0], device=dev, dtype=torch.float64)
     dist.all_reduce(u, op=dist.ReduceOp.MAX)   # rank 0's 1-GPU time, on every rank
     uns_ms = float(u[0])
     fused_mode = f"tp{world}, reduction fused into the row-split GEMMs over NVLink peer memory"
     nccl_mode = (f"tp{world}, NCCL all-reduce (bf16) of each row-split GEMM's partial, then bias + gated residual "
                  "(b2g_bias_gated_residual)")
-    # The headline is the faster of the two communication paths, both measured in this run.
-    use_nccl = n_ms < f_ms
-    ms, split_us = (n_ms, sp_n) if use_nccl else (f_ms, sp)
-    out.update({"mode": nccl_mode if use_nccl else fused_mode,
+    p2p_mode = (f"tp{world}, two-phase all-reduce over NVLink peer memory (each rank sums its shard of rows from "
+                "every rank's partial, then every rank applies the bias + gated residual from the owners' sums)")
+    # The headline is the fastest of the three communication paths, all measured in this run.
+    paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p)], key=lambda x: x[0])
+    ms, mode, split_us = paths[0]
+    out.update({"mode": mode,
                 "ms_per_step": round(ms, 5), "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 2),
                 "breakdown_us": {k: round(v, 1) for k, v in split_us.items()}, "categories_us": _tp_categories(split_us),
                 "unsharded_ms_per_step": round(uns_ms, 5), "speedup_vs_1gpu": round(uns_ms / ms, 3),
                 "unsharded_breakdown_us": ({k: round(v, 1) for k, v in uns_split.items()} if uns_split else None),
-                "other_mode": {"mode": fused_mode if use_nccl else nccl_mode,
-                               "ms_per_step": round(f_ms if use_nccl else n_ms, 5),
-                               "breakdown_us": {k: round(v, 1) for k, v in (sp if use_nccl else sp_n).items()}},
+                "other_modes": [{"mode": md, "ms_per_step": round(t_, 5),
+                                 "breakdown_us": {k: round(v, 1) for k, v in sp_.items()}} for t_, md, sp_ in paths[1:]],
                 "allreduce_bytes_per_step": 3 * L * H * 2, "parity": parity,
-                "parity_of": "the fused path (the NCCL path's sums differ from it only in summation order)"})
+                "parity_of": "the fused path (top level) and the peer-memory path ('p2p'); the NCCL path's sums "
+                             "differ from the peer-memory path's only in summation order"})
     del comm
     return out
 
@@ -1355,6 +1424,33 @@ def t5_encoder_leg(torch, b2g, dev, gen, stream, flush) -> dict:
     return out
 
 
+def fp8_library_peak(torch, dev, n: int = 8192, reps: int = 10) -> dict | None:
+    """A measured FP8 denominator, made the way MEASURED_PEAKS.json's bf16 one is (a library GEMM
+    timed in a burst): torch._scaled_mm (cuBLASLt) on E4M3 [n, n] x [n, n]^T with unit scales,
+    bf16 out, best of `reps` CUDA-event timings.  None where torch has no FP8 GEMM."""
+    if not hasattr(torch, "_scaled_mm") or not hasattr(torch, "float8_e4m3fn"):
+        return None
+    g = torch.Generator(device=dev).manual_seed(5)
+    a = torch.randn((n, n), generator=g, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn((n, n), generator=g, device=dev).to(torch.float8_e4m3fn)
+    one = torch.ones((), device=dev)
+    try:
+        for _ in range(3):
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+    except (RuntimeError, TypeError):
+        return None
+    return {"tflops": round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1),
+            "how": f"torch._scaled_mm (cuBLASLt) E4M3 {n}^3, unit scales, bf16 out, best of {reps} (burst)"}
+
+
 def run_engine_config5(args) -> None:
     """Config 5 per GPU (data-parallel replicas, weak scaling): the FP8 block pair timed like
     config 2, the T5 encoder leg, and end to end the FP8 57-block pass over both guidance
@@ -1506,7 +1602,10 @@ def run_engine_config5(args) -> None:
     gemm_flop = sum(f for _, kind, f in ops if kind == "gemm")
     gemm_ms = sum(mean_op[lab] for lab, kind, _ in ops if kind == "gemm")
     peaks = measured_peaks()
-    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    lib8 = fp8_library_peak(torch, dev)
+    fp8_peak = lib8["tflops"] if lib8 else 2.0 * peaks["bf16_tflops"]
+    fp8_src = (f"measured in this run: {lib8['how']}" if lib8 else
+               "derived: 2 x " + peaks["source"] + " bf16 burst (kind::f8f6f4 issues twice the bf16 rate)")
     achieved = gemm_flop / (gemm_ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": round(flop_step * args.steps * world / (total_ms * 1e-3) / 1e12, 2),
@@ -1519,8 +1618,7 @@ def run_engine_config5(args) -> None:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(fp8_peak, 1), "unit": "TFLOP/s",
                      "frac": round(achieved / fp8_peak, 4),
                      "traffic": profile_traffic("fp8_block_pair_config5_launches.md"),
-                     "peak_source": "derived: 2 x " + peaks["source"] + " bf16 burst (kind::f8f6f4 issues twice the "
-                                    "bf16 rate; no FP8 figure is measured)",
+                     "peak_source": fp8_src, "derived_peak_2x_bf16": round(2.0 * peaks["bf16_tflops"], 1),
                      "kernel": "tc_gemm E4M3: the block pair's 6 linear-layer launches, FLOP-weighted",
                      "gemm_ms_per_step": round(gemm_ms, 5)},
         "breakdown_us": {lab: round(1e3 * mean_op[lab], 1) for lab, _, _ in ops},
@@ -1640,6 +1738,8 @@ def nerf_line(impl, args, step_ms, per_ms, extra) -> dict:
 
 
 def run_engine_nerf(args) -> None:
+    import types
+
     import torch
 
     import b2g
@@ -1671,7 +1771,13 @@ def run_engine_nerf(args) -> None:
     ops_e2e = [("in", lambda: t["s"].copy_(s_h, non_blocking=True))] + ops + \
               [("out", lambda: out_h.copy_(t["out"], non_blocking=True))]
     e2e_ms, _ = time_ops(torch, ops_e2e, max(3, args.steps // 2), args.warmup, flush, graph=False)
+    # The engine's own path for the whole block: the cast of s, param_gen and nerf_glu_kernel
+    # (weight preparation, rms_norm, the three products, silu_mul and the residual add fused).
+    blk = types.SimpleNamespace(param_w=t["w"], param_b=t["b"], norm=torch.ones(NERF_HID, device=dev))
+    glu = nerf_glu_leg(torch, dev, flush, torch.cuda.current_stream(dev), NERF_P, args.steps,
+                       m=types.SimpleNamespace(nerf=[blk]))
     line = nerf_line("b2g", args, step_ms, per, {
+        "glu_block": glu,
         "roofline": {"bound": "tensor", "achieved": round(ach, 2), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": round(ach / peaks["bf16_tflops"], 4), "traffic": None,
                      "peak_source": peaks["source"] + " (burst bf16)",
@@ -1722,6 +1828,92 @@ def run_reference_nerf(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_engine_skinny(args) -> None:
+    """The approximator alone (the weight-streaming M=344 GEMMs, 556 MB of bf16 weights) on
+    random weights of its shapes, through model.ChromaRadiance.compute_modulation's own code:
+    approximator_leg's median, HBM GB/s and per-GEMM split.  Small enough for a full ncu
+    capture of its GEMMs."""
+    import types
+
+    import torch
+
+    import b2g
+    import model
+
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b2g.init()
+    g = torch.Generator(device=dev).manual_seed(42)
+    A, Hd, R = model.APPROX_DIM, model.HIDDEN, model.MOD_ROWS
+
+    def w(n, k):
+        return (torch.randn((n, k), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+
+    def b(n):
+        return torch.randn(n, generator=g, device=dev) * 0.02
+
+    ap = types.SimpleNamespace(in_proj_w=w(A, 64), in_proj_b=b(A), out_proj_w=w(Hd, A), out_proj_b=b(Hd),
+                               ones=torch.ones(A, device=dev),
+                               approx=[model.ApproxLayer(1 + b(A), w(A, A), b(A), w(A, A), b(A))
+                                       for _ in range(model.APPROX_LAYERS)])
+    sc = types.SimpleNamespace(timestep=torch.full((1,), FC_TIMESTEP, device=dev),
+                               vec=torch.empty((R, 64), device=dev), ax=torch.empty((R, A), device=dev),
+                               an=torch.empty((R, A), dtype=torch.bfloat16, device=dev),
+                               ah=torch.empty((R, A), dtype=torch.bfloat16, device=dev),
+                               mod=torch.empty((R, Hd), device=dev))
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    n0 = b2g.launch_count()
+    with ClockSampler(local) as clk:
+        leg = approximator_leg(torch, dev, flush, stream,
+                               lambda mark=None: model.ChromaRadiance.compute_modulation(ap, sc, mark), args.steps)
+    launches = b2g.launch_count() - n0
+    b2g.check_device_error()
+    peaks = measured_peaks()
+    print(json.dumps({
+        "metric": METRIC, "value": leg["tflops"], "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": 3, "ms_per_step": round(leg["us"] / 1e3, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox, seed 42)",
+        "config": {"workload": "skinny: " + leg["workload"], "parallelism": "none (1 GPU)",
+                   "l2": "256 MB buffer written before every call, outside the events"},
+        "roofline": {"bound": "hbm", "achieved": leg["hbm_gbs"], "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": leg["hbm_frac"], "traffic": None, "peak_source": peaks["source"] + " (copy GB/s)",
+                     "kernel": "tc_gemm_kernel: the approximator's 12 GEMMs"},
+        "approximator": leg, "clocks": clk.summary(), "gpu_launches": int(launches)}), flush=True)
+
+
+def run_engine_config3(args) -> None:
+    """Config 3 alone: the whole denoising step at 512^2 (forward_cfg_leg) on rank 0, the e2e of
+    the default line without the block-pair, TP and drop-in legs."""
+    import torch
+
+    import b2g
+
+    world, rank, local = dist_setup()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    b2g.init()
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    n0 = b2g.launch_count()
+    with ClockSampler(local) as clk:
+        fc = forward_cfg_leg(args, torch, dev, flush, dropin=False)
+    launches = b2g.launch_count() - n0
+    value = fc["flop_per_step"] / (fc["ms_per_step"] * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": 1, "steps": fc["steps"],
+        "warmup": args.warmup, "ms_per_step": round(fc["ms_per_step"], 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (torch Philox, seed 42)",
+        "config": {"workload": WORKLOAD3, "flop_per_step": fc["flop_per_step"], "parallelism": "none (1 GPU)",
+                   "l2": "256 MB buffer written before every step, outside the events"},
+        "e2e": dict(fc, value=round(value, 3)), "clocks": clk.summary(), "gpu_launches": int(launches)}),
+        flush=True)
+
+
 def main():
     # The fused tensor-parallel path needs plain peer mappings only; keep torch's symmetric
     # memory from binding its buffers to an NVLink multicast object.
@@ -1731,7 +1923,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default 100 for config2, 200 config1)")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["b2g", "reference"], default="b2g")
-    ap.add_argument("--workload", choices=["config2", "config1", "config4", "config5", "nerf"], default="config2")
+    ap.add_argument("--workload", choices=["config2", "config1", "config3", "config4", "config5", "nerf", "skinny"], default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp1024", action="store_true", help="skip the 1024^2 tensor-parallel leg")
     ap.add_argument("--no-dropin", action="store_true", help="skip the drop-in build's forward_cfg")
@@ -1739,9 +1931,18 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = {"config2": 100, "config1": 200, "config4": 30, "config5": 100, "nerf": 40}[args.workload]
+        args.steps = {"config2": 100, "config1": 200, "config3": 10, "config4": 30, "skinny": 30, "config5": 100, "nerf": 40}[args.workload]
     fn = {("b2g", "config1"): run_engine_config1, ("reference", "config1"): run_reference_config1,
           ("b2g", "config2"): run_engine_config2, ("reference", "config2"): run_reference_config2,
+          ("b2g", "config3"): run_engine_config3,
+          ("b2g", "skinny"): run_engine_skinny,
+          ("reference", "skinny"): lambda a: print(json.dumps({
+              "impl": "reference", "unavailable": "the reference's approximator runs inside its forward_cfg build; "
+                                                  "its time is the 'approximator' object of the default reference "
+                                                  "line"})),
+          ("reference", "config3"): lambda a: print(json.dumps({
+              "impl": "reference", "unavailable": "config 3 alone has no reference line: the reference's forward_cfg "
+                                                  "is the e2e of the default (config2) reference arm"})),
           ("b2g", "config4"): run_engine_config4, ("b2g", "config5"): run_engine_config5,
           ("b2g", "nerf"): run_engine_nerf, ("reference", "nerf"): run_reference_nerf,
           ("reference", "config5"): lambda a: print(json.dumps({

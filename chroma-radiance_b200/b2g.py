@@ -54,6 +54,13 @@ class GemmDesc(ctypes.Structure):
     ]
 
 
+class TpResidualSeg(ctypes.Structure):
+    """Mirror of b2g_tp_residual_seg."""
+
+    _fields_ = [("row0", ctypes.c_int64), ("rows", ctypes.c_int64), ("bias", ctypes.c_void_p),
+                ("gate", ctypes.c_void_p), ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64)]
+
+
 class TpReduceDesc(ctypes.Structure):
     """Mirror of b2g_tp_reduce_desc."""
 
@@ -92,6 +99,10 @@ _SIGNATURES = {
                             ctypes.POINTER(TpReduceDesc), ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
                        ctypes.c_int),
+    "b2g_tp_reduce_shard": ([ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_int,
+                                                                                       ctypes.c_void_p], ctypes.c_int),
+    "b2g_tp_gather_residual": ([ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p,
+                                                                          ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_t5_attention": ([ctypes.c_void_p] * 4 + [ctypes.c_int, ctypes.c_int, ctypes.c_int64, ctypes.c_float,
                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "b2g_bias_gated_residual": ([ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
@@ -396,6 +407,32 @@ def gemm_tp_reduce(problems: list[dict], row0: list[int], tp: TpReduceDesc,
     rows = (ctypes.c_int64 * len(row0))(*row0)
     s = (stream or torch.cuda.current_stream(problems[0]["x"].device)).cuda_stream
     _check(lib.b2g_gemm_tp_reduce(arr, rows, len(descs), ctypes.byref(tp), ctypes.c_void_p(s)))
+
+
+def tp_reduce_shard(part_ptrs: torch.Tensor, sum_buf: torch.Tensor, world: int, rank: int,
+                    stream: torch.cuda.Stream | None = None) -> None:
+    """Phase 1 of the peer-memory all-reduce (b2g_tp_reduce_shard): part_ptrs an int64 CUDA
+    tensor of every rank's bf16 partial [rows, N] address; sum_buf this rank's bf16 [rows, N]."""
+    rows, N = sum_buf.shape
+    s = (stream or torch.cuda.current_stream(sum_buf.device)).cuda_stream
+    _check(load().b2g_tp_reduce_shard(part_ptrs.data_ptr(), sum_buf.data_ptr(), sum_buf.stride(0), rows, N, world,
+                                      rank, ctypes.c_void_p(s)))
+
+
+def tp_gather_residual(sum_ptrs: torch.Tensor, sum_buf: torch.Tensor, world: int, segments: list[dict],
+                       stream: torch.cuda.Stream | None = None) -> None:
+    """Phase 2 (b2g_tp_gather_residual): segments of dict(row0, bias, gate, residual) with the
+    residual F32 [rows, N] of sum rows [row0, row0 + rows)."""
+    rows, N = sum_buf.shape
+    segs = (TpResidualSeg * len(segments))()
+    for i, g in enumerate(segments):
+        r = g["residual"]
+        _require_cuda(r, g["gate"], g.get("bias"))
+        segs[i] = TpResidualSeg(g["row0"], r.shape[0], _ptr(g.get("bias")), g["gate"].data_ptr(), r.data_ptr(),
+                                r.stride(0))
+    s = (stream or torch.cuda.current_stream(sum_buf.device)).cuda_stream
+    _check(load().b2g_tp_gather_residual(sum_ptrs.data_ptr(), sum_buf.stride(0), rows, N, world, segs, len(segments),
+                                         ctypes.c_void_p(s)))
 
 
 def tp_barrier(flag_ptrs: torch.Tensor, own_flags: torch.Tensor, world: int, rank: int, epoch: int,

@@ -150,6 +150,14 @@ __global__ void __launch_bounds__(256, 4) attn_prep_kernel(const PrepArgs a) {
 
 int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
+// A shared-memory int read afresh at every use (volatile asm is neither hoisted nor merged), so
+// that a value set once per CTA need not occupy a register across long loops.
+__device__ __forceinline__ int ld_shared_volatile(const int* p) {
+  int v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+  return v;
+}
+
 // ---------------------------------------------------------------------------- fused attention
 //
 // CTA = (two query tiles A and B of 128 rows = 256 queries, head h), 384 threads:
@@ -195,6 +203,11 @@ constexpr int kFaKStages = 3;
 constexpr int kFaVStages = 2;
 constexpr uint32_t kFaBox = 128 * 128;  // bytes of one 128-row x 128-byte swizzled box
 constexpr float kFaRescaleLog2 = 8.0f;
+// Key blocks whose 128 keys are all masked (bias -inf, or past L) contribute nothing: P = 0
+// there, and the running max ignores them.  A CTA lists its live blocks once and runs its loads,
+// MMAs and softmax over those only, which gives the same result.  A CTA covers at most
+// kFaMaxLive key blocks (64K keys): longer sequences are split into key slices (kv_splits).
+constexpr int kFaMaxLive = 512;
 
 template <int D>
 struct FaLayout {
@@ -205,7 +218,8 @@ struct FaLayout {
   static constexpr uint32_t kK = kQ + kFaTiles * kQTileBytes;
   static constexpr uint32_t kV = kK + kFaKStages * kKBytes;
   static constexpr uint32_t kBars = kV + kFaVStages * kVBytes;
-  static constexpr uint32_t kSmem = 1024 + kBars + 256;
+  static constexpr uint32_t kLive = kBars + 256;  // live key-block list (kFaMaxLive uint16) + count
+  static constexpr uint32_t kSmem = 1024 + kLive + 2 * kFaMaxLive + 16;
   static constexpr uint32_t kTmemCols = 512;
 };
 
@@ -299,6 +313,43 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   griddep_wait();  // the set-up above overlapped the previous kernel's tail
   griddep_launch_dependents();
 
+  // ---- live key blocks of [kb0, kb0 + nkb): warp w checks blocks w, w + 12, .. (4 keys a lane)
+  uint16_t* live = reinterpret_cast<uint16_t*>(smem + Ly::kLive);
+  int* live_count = reinterpret_cast<int*>(smem + Ly::kLive + 2 * kFaMaxLive);
+  {
+    for (int j = warp; j < nkb; j += kFaThreads / 32) {
+      bool any = key_bias == nullptr;
+      if (!any) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int k = (kb0 + j) * kFaKeys + 32 * c + lane;
+          any |= k < p.L && __ldg(key_bias + k) != -INFINITY;
+        }
+      }
+      any = __any_sync(0xffffffffu, any);
+      if (lane == 0) live[j] = any ? 1 : 0;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int count = 0;
+      for (int base = 0; base < nkb; base += 32) {
+        const int j = base + lane;
+        const bool f = j < nkb && live[j] != 0;
+        const uint32_t m = __ballot_sync(0xffffffffu, f);
+        __syncwarp();  // every lane has read its flag before any slot below it is overwritten
+        if (f) live[count + __popc(m & ((1u << lane) - 1u))] = static_cast<uint16_t>(j);
+        count += __popc(m);
+        __syncwarp();
+      }
+      if (lane == 0) *live_count = count;
+    }
+    __syncthreads();
+  }
+  // The number of blocks this CTA runs (read where used: nothing keeps it in a register across
+  // the roles' loops); local index j is key block KBLOCK(j).
+#define NRUN ld_shared_volatile(live_count)
+#define KBLOCK(j) (kb0 + static_cast<int>(live[(j)]))
+
   if (warp < 4) {
    regs_dec<kFaRegsIdle>();
    if (warp == 0 || warp == 2) {
@@ -320,20 +371,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                         row0 + (qpair * kFaTiles + t) * kFaRows, head, once);
       }
       int issued = 0;
-      for (int j = 0; j < nkb; ++j) {
+      for (int j = 0; j < NRUN; ++j) {
         const int st = j % stages;
         if (!mbar_wait(&empty[st], ((j / stages) & 1) ^ 1u, p.err, kErrWaitProducer)) break;
         if (is_k) {
           mbar_arrive_expect_tx(&full[st], Ly::kKBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, row0 + (kb0 + j) * kFaKeys, head,
+            tma_load_3d(sK + st * Ly::kKBytes + c * kFaBox, &tmK, &full[st], c * 64, row0 + KBLOCK(j) * kFaKeys, head,
                         shared_kv);
         } else {
           mbar_arrive_expect_tx(&full[st], Ly::kVBytes);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c)
-            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, row0 + (kb0 + j) * kFaKeys, head,
+            tma_load_3d(sV + st * Ly::kVBytes + c * kFaBox, &tmV, &full[st], c * 64, row0 + KBLOCK(j) * kFaKeys, head,
                         shared_kv);
         }
         ++issued;
@@ -361,7 +412,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         umma_commit(&s_full[t]);
         if (t == kFaTiles - 1) umma_commit(&k_empty[j % KS]);  // both tiles have read K_j
       };
-      if (ok) {
+      if (ok && NRUN > 0) {  // (a range with no live key block issues nothing)
         tc_fence_after();
         ok = mbar_wait(&k_full[0], 0, p.err, kErrWaitMma);
         if (ok) {
@@ -369,7 +420,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           for (int t = 0; t < kFaTiles; ++t) issue_s(t, 0);
         }
       }
-      for (int j = 0; j < nkb && ok; ++j) {
+      for (int j = 0; j < NRUN && ok; ++j) {
         const int vs = j % VS;
         for (int t = 0; t < kFaTiles && ok; ++t) {
           const uint32_t v0 = smem_u32(sV + vs * Ly::kVBytes);
@@ -390,7 +441,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                         idesc_o, 1u);
           umma_commit(&pv_done[t]);
           if (t == kFaTiles - 1) umma_commit(&v_empty[vs]);  // both tiles have read V_j
-          if (j + 1 < nkb) {
+          if (j + 1 < NRUN) {
             if (t == 0 && !(ok = mbar_wait(&k_full[(j + 1) % KS], ((j + 1) / KS) & 1, p.err, kErrWaitMma))) break;
             // S(j+1) overwrites P(j); issued behind P(j).V_j, which reads P first (issue order).
             issue_s(t, j + 1);
@@ -413,13 +464,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const uint32_t obase = sbase + 128;
     float m_used = -INFINITY, l_sum = 0.f;
     bool good = true;
-    for (int j = 0; j < nkb && good; ++j) {
+    for (int j = 0; j < NRUN && good; ++j) {
       // The block's key bias, key 32c + lane in kb2[c], in base-2 exponent units (keys past L
       // are -inf); loaded before the wait, which hides the latency.
       float kb2[4];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        const int key = (kb0 + j) * kFaKeys + c * 32 + lane;
+        const int key = KBLOCK(j) * kFaKeys + c * 32 + lane;
         kb2[c] = key < p.L ? (key_bias ? __ldg(key_bias + key) * 1.4426950408889634f : 0.f) : -INFINITY;
       }
       good = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, p.err, kErrWaitEpilogue));
@@ -533,10 +584,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
     // Final: wait for the last P.Vt of this tile, write O / l.
     if (good)
-      good = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (nkb - 1) & 1, p.err, kErrWaitEpilogue));
+      good = NRUN == 0 || __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (NRUN - 1) & 1, p.err, kErrWaitEpilogue));
     if (good && p.kv_splits > 1) {
       // One key slice: the unnormalised O and (m, l) of each row go to the partial buffers.
       tc_fence_after();
+      const bool none = NRUN == 0;
       const int q = (qpair * kFaTiles + t) * kFaRows + row;
       const long long prow = ((static_cast<long long>(blockIdx.z) * gridDim.y + head) * p.kv_splits + kslice) * p.lpad + q;
 #pragma unroll
@@ -544,6 +596,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         uint32_t o[32];
         tmem_ld_32x32b_x32(obase + c * 32, o);
         tmem_wait_ld();
+        if (none) {  // no live key block: O was never written (its TMEM holds anything)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
         if (q < p.L) {
           float4* dst = reinterpret_cast<float4*>(p.part_o + prow * D + c * 32);
 #pragma unroll
@@ -558,11 +614,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const int q = (qpair * kFaTiles + t) * kFaRows + row;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
       const long long col0 = static_cast<long long>(head) * D;
+      const bool none = NRUN == 0;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(obase + c * 32, o);
         tmem_wait_ld();
+        if (none) {  // no live key block: O was never written (its TMEM holds anything)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
         if (q < p.L) {
           if (p.out_bf16) {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) +
@@ -599,6 +660,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Ly::kTmemCols);
   }
+#undef KBLOCK
+#undef NRUN
 }
 
 // Merges the key slices of a split launch: for query row q of head h, with slice s holding
@@ -628,7 +691,8 @@ __global__ void attn_combine_kernel(FaParams p, int H, int batch) {
     for (int s = 0; s < p.kv_splits; ++s) {
       const long long r = base + static_cast<long long>(s) * p.lpad;
       const float2 ml = p.part_ml[r];
-      const float wgt = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      if (ml.x == -INFINITY) continue;  // a slice without a live key holds no information
+      const float wgt = exp2f(ml.x - M);
       den += wgt * ml.y;
       const float* src = p.part_o + r * D + lane * kPer;
 #pragma unroll
@@ -717,6 +781,8 @@ b2g_status flash_checked(const AttnBf16Args& a, cudaStream_t st) {
   }
   if (splits > fp.num_kb / 4) splits = fp.num_kb / 4;
   if (splits < 1) splits = 1;
+  // A CTA lists at most kFaMaxLive key blocks: longer sequences always split.
+  if ((fp.num_kb + splits - 1) / splits > kFaMaxLive) splits = (fp.num_kb + kFaMaxLive - 1) / kFaMaxLive;
   fp.kv_splits = splits;
   if (splits > 1) {
     fp.lpad = static_cast<int>(round_up(L, kFaTiles * kFaRows));

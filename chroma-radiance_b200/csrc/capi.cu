@@ -366,6 +366,16 @@ b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int 
   return tp_barrier(flag_ptrs, own_flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t ld, int64_t rows, int64_t N,
+                               int world, int rank, void* stream) {
+  return tp_reduce_shard(part_ptrs, sum, ld, rows, N, world, rank, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,
+                                  const b2g_tp_residual_seg* segs, int nsegs, void* stream) {
+  return tp_gather_residual(sum_ptrs, ld, rows, N, world, segs, nsegs, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_t5_attention(const float* Q, const float* K, const float* V, const float* rel_bias, int n_head,
                             int d_head, int64_t L, float scale, const float* attn_mask, float* out, void* stream) {
   return t5_attention(Q, K, V, rel_bias, n_head, d_head, L, scale, attn_mask, out, static_cast<cudaStream_t>(stream));

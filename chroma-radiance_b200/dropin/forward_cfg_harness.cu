@@ -335,6 +335,40 @@ int fc_bench_modulation(float timestep, int iters, int warmup, int64_t flush_byt
   return static_cast<int>(cudaGetLastError());
 }
 
+// Times NeRF GLU block `blk` (nerf_glu_block, chroma.cuh:1253-1306: the param_generator linear,
+// the weight slices and L2 norms, rms_norm, three batched products, silu_mul and the residual
+// add) on x [P, 256, 64] (updated in place by every call) and s [P, 3072], both F32 device
+// pointers; CUDA events on stream 0 around each call, a `flush_bytes` buffer rewritten before
+// each outside them; ms[i] is call i's time.
+int fc_bench_nerf_glu_block(int blk, float* x, const float* s, int64_t P, int iters, int warmup, int64_t flush_bytes,
+                            double* ms) {
+  if (blk < 0 || blk >= static_cast<int>(g_model->nerf_block_weights.size())) return -1;
+  Tensor tx = Tensor::wrap_gpu(x, {P, 256, 64}, DType::F32);
+  Tensor ts = Tensor::wrap_gpu(const_cast<float*>(s), {P, (int64_t)ChromaRadiance::hidden_size}, DType::F32);
+  const auto& w = g_model->nerf_block_weights[blk];
+  for (int i = 0; i < warmup; ++i) g_model->nerf_glu_block(tx, ts, w);
+  void* flush = nullptr;
+  if (flush_bytes > 0) CHECK_CUDA(cudaMalloc(&flush, flush_bytes));
+  CHECK_CUDA(cudaDeviceSynchronize());
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  for (int i = 0; i < iters; ++i) {
+    if (flush) cudaMemsetAsync(flush, i & 0xFF, flush_bytes, 0);
+    cudaEventRecord(e0, 0);
+    g_model->nerf_glu_block(tx, ts, w);
+    cudaEventRecord(e1, 0);
+    cudaEventSynchronize(e1);
+    float t = 0;
+    cudaEventElapsedTime(&t, e0, e1);
+    ms[i] = t;
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (flush) cudaFree(flush);
+  return static_cast<int>(cudaGetLastError());
+}
+
 // One NeRF decode (nerf_decode, chroma.cuh:1163-1251) of transformer image rows img [P, 3072]
 // (a device pointer) into out [1,3,H,W] (a device pointer).
 int fc_nerf_decode(const float* img, float* out) {

@@ -41,6 +41,8 @@ class ForwardCfgHarness:
         lib.fc_forward.argtypes = [ctypes.c_float, ctypes.c_float]
         lib.fc_modulation.argtypes = [ctypes.c_float]
         lib.fc_nerf_decode.argtypes = [vp, vp]
+        lib.fc_bench_nerf_glu_block.argtypes = [ctypes.c_int, vp, vp, i64, ctypes.c_int, ctypes.c_int, i64,
+                                                ctypes.POINTER(ctypes.c_double)]
         lib.fc_bench_modulation.argtypes = [ctypes.c_float, ctypes.c_int, ctypes.c_int, i64,
                                             ctypes.POINTER(ctypes.c_double)]
         lib.fc_bench.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, i64,
@@ -97,4 +99,12 @@ class ForwardCfgHarness:
         """Per-call milliseconds of compute_modulation (the approximator), CUDA events on stream 0."""
         ms = (ctypes.c_double * iters)()
         self._check(self.lib.fc_bench_modulation(timestep, iters, warmup, flush_bytes, ms), "fc_bench_modulation")
+        return list(ms)
+
+    def bench_nerf_glu_block(self, blk: int, x, s, iters: int, warmup: int, flush_bytes: int) -> list:
+        """Per-call milliseconds of the reference's nerf_glu_block `blk` on x F32 [P, 256, 64]
+        (updated in place) and s F32 [P, 3072] (device tensors)."""
+        ms = (ctypes.c_double * iters)()
+        self._check(self.lib.fc_bench_nerf_glu_block(blk, x.data_ptr(), s.data_ptr(), x.shape[0], iters, warmup,
+                                                     flush_bytes, ms), "fc_bench_nerf_glu_block")
         return list(ms)

@@ -247,6 +247,29 @@ b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, i
  * is bounded (2 s): on timeout the device error word gets bit 8 (b2g_check_device_error). */
 b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream);
 
+/* Two-phase all-reduce of a row-split layer's bf16 partial over NVLink peer memory, with the
+ * residual update folded in (no reference counterpart: it replaces the ncclAllReduce +
+ * gated_residual (kernels.cu:942-968) of the tensor-parallel path).  Rows [0, rows) are split
+ * into world shards of ceil(rows / world); rank q owns shard q.
+ *   b2g_tp_reduce_shard: sums, in rank order, the world partials [rows, N] (part_ptrs: device
+ *     array [world] of peer-mapped bf16 buffers, row stride ld) over this rank's shard, rounds
+ *     to bf16 and stores it at the same rows of `sum` (this rank's peer-mapped buffer).
+ *   b2g_tp_gather_residual: for every row m of each segment, residual[m - row0] += gate *
+ *     (sums[owner(m)][m] + bias) (sum_ptrs: device array [world] of the ranks' sum buffers).
+ * A cross-rank barrier (b2g_tp_barrier) must precede each call: the partials, then the sums,
+ * must be complete on every rank.  world <= 8, N % 8 == 0, 16-byte aligned rows, gate, bias. */
+typedef struct {
+  int64_t row0, rows;        /* rows [row0, row0 + rows) of the sum buffers */
+  const float* bias;         /* [N] or NULL */
+  const float* gate;         /* [N] */
+  float* residual;           /* F32 [rows, ldr], this rank's replicated residual */
+  int64_t ldr;
+} b2g_tp_residual_seg;
+b2g_status b2g_tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t ld, int64_t rows, int64_t N,
+                               int world, int rank, void* stream);
+b2g_status b2g_tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,
+                                  const b2g_tp_residual_seg* segs, int nsegs, void* stream);
+
 /* Attention input projection with qk_norm and RoPE fused into the GEMM epilogue.  The
  * reference runs these as three linears into F32 q, k, v, then qk_norm (rms_norm per head with
  * a learned scale) on q and k (chroma.cuh:822-842 double block, chroma.cuh:1108-1116 single

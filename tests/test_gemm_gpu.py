@@ -708,6 +708,51 @@ def test_attention_key_splits(engine, L, H, splits, batch):
     engine.check_device_error()
 
 
+@pytest.mark.parametrize("case", ["middle_blocks", "one_key_live", "per_sequence"])
+@pytest.mark.parametrize("splits", [-1, 2])
+def test_attention_skips_masked_key_blocks(engine, case, splits):
+    """Key blocks whose 128 keys are all -inf are skipped (no loads, MMAs or softmax): the
+    result must equal softmax(q k^T / sqrt(D) + mask) v in fp64 where whole blocks, all but
+    one key, or different blocks per stacked sequence are masked; one pass and key-split."""
+    H, D, L = 4, 128, 1536
+    batch = 2 if case == "per_sequence" else 1
+    g = torch.Generator(device=DEV).manual_seed(23)
+    qkv = torch.randn((batch * L, 3 * H * D), generator=g, device=DEV).to(torch.bfloat16)
+    q, k, v = qkv[:, :H * D], qkv[:, H * D:2 * H * D], qkv[:, 2 * H * D:]
+    mask = torch.zeros((batch, L), device=DEV)
+    if case == "middle_blocks":
+        mask[0, 100:1400] = float("-inf")        # blocks 1..9 dead, 0 and 10 partly live
+    elif case == "one_key_live":
+        mask[0, :] = float("-inf")
+        mask[0, 700] = 0.0                        # one live block holding one live key
+    else:
+        mask[0, 256:1024] = float("-inf")
+        mask[1, :512] = float("-inf")
+        mask[1, 1280:] = float("-inf")
+    want = torch.empty((batch * L, H * D), dtype=torch.float64, device=DEV)
+    for z in range(batch):
+        rows = slice(z * L, (z + 1) * L)
+        for h in range(H):
+            cols = slice(h * D, (h + 1) * D)
+            sc = q[rows, cols].double() @ k[rows, cols].double().t() / np.sqrt(D) + mask[z].double()[None, :]
+            want[rows, cols] = torch.softmax(sc, dim=-1) @ v[rows, cols].double()
+    b = want.cpu().numpy().ravel()
+    try:
+        engine.set_attention_splits(splits)
+        for dt in (torch.float32, torch.bfloat16):
+            if batch > 1:
+                got = engine.attention_bf16_batched(q, k, v, H, D, batch, attn_mask=mask, out_dtype=dt)
+            else:
+                got = engine.attention_bf16(q, k, v, H, D, attn_mask=mask[0], out_dtype=dt)
+            torch.cuda.synchronize()
+            a = got.double().cpu().numpy().ravel()
+            assert rel_err(a, b) < 1e-2
+            assert a @ b / np.sqrt((a @ a) * (b @ b)) > 0.9999
+    finally:
+        engine.set_attention_splits(0)
+    engine.check_device_error()
+
+
 def test_nerf_block_gemms_vs_reference(engine, ref):
     """One NeRF GLU block's GEMMs at 512^2 (chroma.cuh:1262-1302) at their real sizes, engine
     against the reference's own linear() and batched_matmul_Bt on the same inputs: param_gen

@@ -1,6 +1,6 @@
 """Worker for tests/test_tp_gpu.py, launched with torchrun (one process per GPU, NCCL).
-Runs both the NCCL all-reduce path and the fused path (reduction inside the GEMM over
-peer-mapped memory).
+Runs the NCCL all-reduce path, the fused path (reduction inside the GEMM over peer-mapped
+memory) and the two-phase peer-memory all-reduce with the residual update folded in.
 
 Every rank builds the same block-pair weights and inputs (seeded), shards them with tp.py,
 runs the tensor-parallel double + single block, and compares its replicated residual
@@ -70,6 +70,11 @@ def main() -> int:
                              gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
     tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gates[4], pe, mask, scratch)
     fused = {"txt": comm.res_double[:T], "img": comm.res_double[T:], "x": comm.res_single}
+    # And with the two-phase peer-memory all-reduce (b2g_tp_reduce_shard + b2g_tp_gather_residual).
+    p2p = {k: v.clone() for k, v in res.items()}
+    tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                           p2p["txt"], p2p["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
+    tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], p2p["x"], gates[4], pe, mask, scratch)
     torch.cuda.synchronize()
     b2g.check_device_error()
     ok = True
@@ -85,6 +90,11 @@ def main() -> int:
         same = torch.equal(fused[k], got[k])
         print(f"rank {rank}/{world} {k} fused: err {err2:.3e} cos {cos2:.6f} identical-to-nccl {same}", flush=True)
         ok = ok and err2 <= 1e-2 and cos2 >= 0.9999
+        d3 = (p2p[k] - res[k]).double().flatten()
+        err3 = ((d3 - d0).abs().max() / d0.abs().max()).item()
+        cos3 = ((d3 @ d0) / (d3.norm() * d0.norm())).item()
+        print(f"rank {rank}/{world} {k} p2p: err {err3:.3e} cos {cos3:.6f}", flush=True)
+        ok = ok and err3 <= 1e-2 and cos3 >= 0.9999
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
