@@ -1187,34 +1187,41 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
 
     per_n = timed(nccl, True)
     sp_n = split(nccl)
-    pres = {k: v.clone() for k, v in res.items()}
+    runs = {}
+    for name, push in (("p2p", False), ("push", True)):
+        pres = {k: v.clone() for k, v in res.items()}
 
-    def p2p(mark=None):
-        tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
-                               pres["txt"], pres["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch, mark)
-        tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], pres["x"], gt[4], pe, mask, scratch, mark)
+        def path(mark=None, pres=pres, push=push):
+            tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"],
+                                   act["img_mod2"], pres["txt"], pres["img"], gt[0], gt[1], gt[2], gt[3], pe, mask,
+                                   scratch, mark, push=push)
+            tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], pres["x"], gt[4], pe, mask, scratch, mark, push=push)
 
-    p2p()
-    barrier()
-    if rank == 0:
-        got = {k: delta(pres[k], res[k]) for k in res}
-        parity["p2p"] = {k: {"max_rel": float((got[k] - ref[k]).abs().max() / ref[k].abs().max()),
-                             "cosine": float((got[k] @ ref[k]) / (got[k].norm() * ref[k].norm()))} for k in got}
-        parity["within_tolerance"] = parity["within_tolerance"] and all(
-            v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999 for v in parity["p2p"].values())
-    per_p = timed(p2p, True)
-    sp_p = split(p2p)
+        path()
+        barrier()
+        if rank == 0:
+            got = {k: delta(pres[k], res[k]) for k in res}
+            parity[name] = {k: {"max_rel": float((got[k] - ref[k]).abs().max() / ref[k].abs().max()),
+                                "cosine": float((got[k] @ ref[k]) / (got[k].norm() * ref[k].norm()))} for k in got}
+            parity["within_tolerance"] = parity["within_tolerance"] and all(
+                v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999 for v in parity[name].values())
+        runs[name] = (timed(path, True), split(path))
+    per_p, sp_p = runs["p2p"]
+    per_q, sp_q = runs["push"]
     b2g_mod = __import__("b2g")
     b2g_mod.check_device_error()
-    labels, labels_n, labels_p = sorted(sp), sorted(sp_n), sorted(sp_p)
-    t = torch.tensor([sum(per_f), sum(per_n), sum(per_p)] + [sp[k] for k in labels] + [sp_n[k] for k in labels_n] +
-                     [sp_p[k] for k in labels_p], device=dev, dtype=torch.float64)
+    labels, labels_n, labels_p, labels_q = sorted(sp), sorted(sp_n), sorted(sp_p), sorted(sp_q)
+    t = torch.tensor([sum(per_f), sum(per_n), sum(per_p), sum(per_q)] + [sp[k] for k in labels] +
+                     [sp_n[k] for k in labels_n] + [sp_p[k] for k in labels_p] + [sp_q[k] for k in labels_q],
+                     device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    f_ms, n_ms, p_ms = float(t[0]) / steps, float(t[1]) / steps, float(t[2]) / steps
-    vals = t[3:].tolist()
-    sp = {k: float(v) for k, v in zip(labels, vals[:len(labels)])}
-    sp_n = {k: float(v) for k, v in zip(labels_n, vals[len(labels):len(labels) + len(labels_n)])}
-    sp_p = {k: float(v) for k, v in zip(labels_p, vals[len(labels) + len(labels_n):])}
+    f_ms, n_ms, p_ms, q_ms = (float(t[i]) / steps for i in range(4))
+    vals = t[4:].tolist()
+    splits_out = []
+    for lab in (labels, labels_n, labels_p, labels_q):
+        splits_out.append({k: float(v) for k, v in zip(lab, vals[:len(lab)])})
+        vals = vals[len(lab):]
+    sp, sp_n, sp_p, sp_q = splits_out
     u = torch.tensor([uns_ms or 0.0], device=dev, dtype=torch.float64)
     dist.all_reduce(u, op=dist.ReduceOp.MAX)   # rank 0's 1-GPU time, on every rank
     uns_ms = float(u[0])
@@ -1224,7 +1231,11 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
     p2p_mode = (f"tp{world}, two-phase all-reduce over NVLink peer memory (each rank sums its shard of rows from "
                 "every rank's partial, then every rank applies the bias + gated residual from the owners' sums)")
     # The headline is the fastest of the three communication paths, all measured in this run.
-    paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p)], key=lambda x: x[0])
+    push_mode = (f"tp{world}, reduce-scatter from the row-split GEMMs' epilogues (each output row stored over "
+                 "NVLink into its owner rank's receive slot while the GEMM runs), a local sum of the slots, then "
+                 "every rank applies the bias + gated residual from the owners' sums")
+    paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p), (q_ms, push_mode, sp_q)],
+                   key=lambda x: x[0])
     ms, mode, split_us = paths[0]
     out.update({"mode": mode,
                 "ms_per_step": round(ms, 5), "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 2),
@@ -1234,8 +1245,8 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                 "other_modes": [{"mode": md, "ms_per_step": round(t_, 5),
                                  "breakdown_us": {k: round(v, 1) for k, v in sp_.items()}} for t_, md, sp_ in paths[1:]],
                 "allreduce_bytes_per_step": 3 * L * H * 2, "parity": parity,
-                "parity_of": "the fused path (top level) and the peer-memory path ('p2p'); the NCCL path's sums "
-                             "differ from the peer-memory path's only in summation order"})
+                "parity_of": "the fused path (top level) and the peer-memory paths ('p2p', 'push'); the NCCL path's "
+                             "sums differ from the peer-memory paths' only in summation order"})
     del comm
     return out
 

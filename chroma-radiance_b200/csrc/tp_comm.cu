@@ -89,6 +89,40 @@ __global__ void __launch_bounds__(256) tp_reduce_shard_kernel(const __nv_bfloat1
   }
 }
 
+// Phase 1 of the reduce-scatter form: the row-split GEMMs have stored every rank's partial of
+// this rank's rows into this rank's receive buffer [world slots][shard rows][N]; sum the slots in
+// rank order (local reads only) into this rank's rows of `sum`.
+__global__ void __launch_bounds__(256) tp_reduce_slots_kernel(const __nv_bfloat16* __restrict__ recv, int world,
+                                                               long long shard, __nv_bfloat16* __restrict__ sum,
+                                                               long long ld, long long r0, long long nrows, int N) {
+  const int groups = N / 8;
+  const long long total = nrows * groups;
+  const long long slot = shard * ld;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / groups;
+    const int n = static_cast<int>(i % groups) * 8;
+    uint4 u[kTpMaxWorld];
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q)
+      if (q < world) u[q] = __ldcg(reinterpret_cast<const uint4*>(recv + q * slot + r * ld + n));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q) {
+      if (q >= world) break;
+      float v[8];
+      bf16x8_to_f32(u[q], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+    uint4 o;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(sum + (r0 + r) * ld + n) = o;
+  }
+}
+
 struct TpSegs {
   int count;
   long long row0[2], rows[2], ldr[2];
@@ -150,6 +184,27 @@ b2g_status tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t ld, 
       static_cast<int>(N));
   note_launch();
   return check_cuda(cudaGetLastError(), "tp_reduce_shard launch");
+}
+
+b2g_status tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
+                           cudaStream_t st) {
+  if (world < 1 || world > kTpMaxWorld || rank < 0 || rank >= world || !recv || !sum || rows < 0 || N <= 0 || N % 8 ||
+      (reinterpret_cast<uintptr_t>(recv) & 15u) || (reinterpret_cast<uintptr_t>(sum) & 15u))
+    return set_error(B2G_ERR_INVALID, "tp_reduce_slots: world in [1, 8], N % 8 == 0, 16-byte aligned buffers");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const int64_t shard = (rows + world - 1) / world;
+  const int64_t r0 = rank * shard < rows ? rank * shard : rows;
+  const int64_t r1 = r0 + shard < rows ? r0 + shard : rows;
+  if (r1 <= r0) return B2G_OK;
+  const int64_t work = (r1 - r0) * (N / 8);
+  const int64_t blocks = (work + 255) / 256 < 8 * dev->num_sms ? (work + 255) / 256 : 8 * dev->num_sms;
+  tp_reduce_slots_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(recv), world, shard, static_cast<__nv_bfloat16*>(sum), N, r0, r1 - r0,
+      static_cast<int>(N));
+  note_launch();
+  return check_cuda(cudaGetLastError(), "tp_reduce_slots launch");
 }
 
 b2g_status tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,

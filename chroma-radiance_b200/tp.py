@@ -368,12 +368,16 @@ class SymmetricComm:
         self.res_single = symm.empty((rows, hidden), dtype=torch.float32, device=dev)
         self.counters = symm.empty(self.COUNTER_SLOTS, dtype=torch.int32, device=dev)
         self.sums = symm.empty((rows, hidden), dtype=torch.bfloat16, device=dev)
+        self.rows = rows
+        shard = (rows + self.world - 1) // self.world
+        self.recv = symm.empty((self.world, shard, hidden), dtype=torch.bfloat16, device=dev)
         self.flags = symm.empty(self.world, dtype=torch.int32, device=dev)
         self.counters.zero_()
         self.flags.zero_()
         name = group.group_name if group is not None else dist.group.WORLD.group_name
         self._handles = [symm.rendezvous(t, name) for t in
-                         (self.part, self.res_double, self.res_single, self.counters, self.flags, self.sums)]
+                         (self.part, self.res_double, self.res_single, self.counters, self.flags, self.sums,
+                          self.recv)]
         torch.cuda.synchronize(dev)
         dist.barrier(group)  # every rank's zeroed counters and flags are in place
 
@@ -389,6 +393,7 @@ class SymmetricComm:
         counters0 = peers(self.counters, self._handles[3])[0]
         self._flag_ptrs = torch.tensor(peers(self.flags, self._handles[4]), dtype=torch.int64, device=dev)
         self._sum_ptrs = torch.tensor(peers(self.sums, self._handles[5]), dtype=torch.int64, device=dev)
+        self._recv_ptrs = torch.tensor(peers(self.recv, self._handles[6]), dtype=torch.int64, device=dev)
         self.epoch = 0
         self.desc = {}
         for name, t in (("double", self.res_double), ("single", self.res_single)):
@@ -419,6 +424,29 @@ class SymmetricComm:
         segments (b2g_tp_gather_residual; dict(row0, bias, gate, residual))."""
         self.barrier()
         self.b2g.tp_reduce_shard(self._part_ptrs, self.sums, self.world, self.rank)
+        if mark:
+            mark(label + ".reduce")
+        self.barrier()
+        self.b2g.tp_gather_residual(self._sum_ptrs, self.sums, self.world, segments)
+        if mark:
+            mark(label + ".residual")
+
+    def gemm_push(self, problems: list[dict], row0: list[int], mark=None, label: str = "") -> None:
+        """A row-split layer whose GEMM stores each output row's bf16 partial straight into the
+        owning rank's slot of self.recv (b2g_gemm_scatter_rows): the NVLink transfer overlaps
+        the GEMM.  problems = [dict(x=, w=)]; row0 = their first rows among self.rows."""
+        self.b2g.gemm_scatter_rows([dict(x=p["x"], w=p["w"], out=self.part[r:r + p["x"].shape[0]])
+                                    for p, r in zip(problems, row0)], row0, self._recv_ptrs, self.rows, self.world,
+                                   self.rank)
+        if mark:
+            mark(label)
+
+    def reduce_push(self, segments: list[dict], mark=None, label: str = "") -> None:
+        """After gemm_push: barrier, sum this rank's rows from its receive slots (local reads,
+        b2g_tp_reduce_slots), barrier, then the residual update from every rank's sums
+        (b2g_tp_gather_residual)."""
+        self.barrier()
+        self.b2g.tp_reduce_slots(self.recv, self.sums, self.world, self.rank)
         if mark:
             mark(label + ".reduce")
         self.barrier()
@@ -465,33 +493,44 @@ def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, g
     comm.reduce("single", [dict(x=s.cat, w=w.linear2_w, bias=w.linear2_b, gate=gate)], [0], mark, "single.linear2")
 
 
+def _row_split_p2p(ops, comm: SymmetricComm, problems: list[dict], row0: list[int], segments: list[dict], mk,
+                   label: str, push: bool) -> None:
+    """One row-split layer and its all-reduce + residual update over peer memory: pull form (the
+    GEMM writes comm.part, phase 1 reads every rank's) or push form (the GEMM stores each row
+    into its owner's receive slot, phase 1 reads local slots)."""
+    if push:
+        comm.gemm_push(problems, row0, mk, label)
+        comm.reduce_push(segments, mk, label)
+    else:
+        ops.gemm_group([dict(x=p["x"], w=p["w"], out=comm.part[r:r + p["x"].shape[0]]) for p, r in zip(problems, row0)])
+        mk(label)
+        comm.reduce_p2p(segments, mk, label)
+
+
 def tp_double_block_p2p(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1,
                         txt_mod2, img_mod2, txt, img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask,
-                        s: TPScratch, mark=None) -> None:
+                        s: TPScratch, mark=None, push: bool = False) -> None:
     """tp_double_block with each row-split layer's all-reduce and residual update done by the
-    two-phase peer-memory kernels (SymmetricComm.reduce_p2p): the row-split GEMMs write their
-    partial into comm.part; txt, img are this rank's replicated F32 streams."""
+    two-phase peer-memory kernels (_row_split_p2p, pull or push form); txt, img are this rank's
+    replicated F32 streams."""
     T = txt_mod1.shape[0]
     mk = mark or _no_mark
     _qkv_attention_double(ops, txt_w, img_w, txt_mod1, img_mod1, pe, mask, s, mk)
-    part = comm.part
-    ops.gemm_group([dict(x=s.attn[:T], w=txt_w.proj_w, out=part[:T]), dict(x=s.attn[T:], w=img_w.proj_w, out=part[T:])])
-    mk("double.proj")
-    comm.reduce_p2p([dict(row0=0, bias=txt_w.proj_b, gate=txt_gate1, residual=txt),
-                     dict(row0=T, bias=img_w.proj_b, gate=img_gate1, residual=img)], mark, "double.proj")
+    _row_split_p2p(ops, comm, [dict(x=s.attn[:T], w=txt_w.proj_w), dict(x=s.attn[T:], w=img_w.proj_w)], [0, T],
+                   [dict(row0=0, bias=txt_w.proj_b, gate=txt_gate1, residual=txt),
+                    dict(row0=T, bias=img_w.proj_b, gate=img_gate1, residual=img)], mk, "double.proj", push)
     ops.gemm_group([dict(x=txt_mod2, w=txt_w.mlp0_w, bias=txt_w.mlp0_b, out=s.h_txt, epilogue="gelu"),
                     dict(x=img_mod2, w=img_w.mlp0_w, bias=img_w.mlp0_b, out=s.h_img, epilogue="gelu")])
     mk("double.mlp0")
-    ops.gemm_group([dict(x=s.h_txt, w=txt_w.mlp2_w, out=part[:T]), dict(x=s.h_img, w=img_w.mlp2_w, out=part[T:])])
-    mk("double.mlp2")
-    comm.reduce_p2p([dict(row0=0, bias=txt_w.mlp2_b, gate=txt_gate2, residual=txt),
-                     dict(row0=T, bias=img_w.mlp2_b, gate=img_gate2, residual=img)], mark, "double.mlp2")
+    _row_split_p2p(ops, comm, [dict(x=s.h_txt, w=txt_w.mlp2_w), dict(x=s.h_img, w=img_w.mlp2_w)], [0, T],
+                   [dict(row0=0, bias=txt_w.mlp2_b, gate=txt_gate2, residual=txt),
+                    dict(row0=T, bias=img_w.mlp2_b, gate=img_gate2, residual=img)], mk, "double.mlp2", push)
 
 
 def tp_single_block_p2p(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch,
-                        mark=None) -> None:
+                        mark=None, push: bool = False) -> None:
     """tp_single_block with linear2's all-reduce and residual update by the two-phase
-    peer-memory kernels; x this rank's replicated F32 stream."""
+    peer-memory kernels (pull or push form); x this rank's replicated F32 stream."""
     HDl = s.HDl
     mk = mark or _no_mark
     _linear1(ops, w, x_mod, pe, s)
@@ -499,6 +538,5 @@ def tp_single_block_p2p(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, x, 
     q, k, v = s.qkv[:, :HDl], s.qkv[:, HDl:2 * HDl], s.qkv[:, 2 * HDl:]
     ops.attention_bf16(q, k, v, s.hl, s.d.dhead, attn_mask=mask, out=s.cat[:, :HDl])
     mk("single.attention")
-    ops.gemm(s.cat, w.linear2_w, out=comm.part)
-    mk("single.linear2")
-    comm.reduce_p2p([dict(row0=0, bias=w.linear2_b, gate=gate, residual=x)], mark, "single.linear2")
+    _row_split_p2p(ops, comm, [dict(x=s.cat, w=w.linear2_w)], [0],
+                   [dict(row0=0, bias=w.linear2_b, gate=gate, residual=x)], mk, "single.linear2", push)

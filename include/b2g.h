@@ -270,6 +270,18 @@ b2g_status b2g_tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t 
 b2g_status b2g_tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,
                                   const b2g_tp_residual_seg* segs, int nsegs, void* stream);
 
+/* The reduce-scatter form of the same all-reduce (no reference counterpart): the row-split GEMM
+ * itself stores each output row's bf16 partial into the receive buffer of the rank that owns
+ * the row (recv_ptrs: device array [world] of peer-mapped bf16 [world][shard][N] buffers,
+ * shard = ceil(rows / world); row r of problem i is row0[i] + m; this rank's slot), so the
+ * transfer over NVLink overlaps the GEMM; b2g_tp_reduce_slots then sums the world slots of this
+ * rank's rows (local reads) into its rows of `sum` [rows, N].  A b2g_tp_barrier goes between
+ * them, and before b2g_tp_gather_residual.  Descriptors: bf16 out, no bias, no epilogue. */
+b2g_status b2g_gemm_scatter_rows(const b2g_gemm_desc* descs, const int64_t* row0, int count, void* const* recv_ptrs,
+                                 int64_t rows, int world, int rank, void* stream);
+b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
+                               void* stream);
+
 /* Attention input projection with qk_norm and RoPE fused into the GEMM epilogue.  The
  * reference runs these as three linears into F32 q, k, v, then qk_norm (rms_norm per head with
  * a learned scale) on q and k (chroma.cuh:822-842 double block, chroma.cuh:1108-1116 single

@@ -70,11 +70,17 @@ def main() -> int:
                              gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
     tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gates[4], pe, mask, scratch)
     fused = {"txt": comm.res_double[:T], "img": comm.res_double[T:], "x": comm.res_single}
-    # And with the two-phase peer-memory all-reduce (b2g_tp_reduce_shard + b2g_tp_gather_residual).
+    # And with the two-phase peer-memory all-reduce (b2g_tp_reduce_shard + b2g_tp_gather_residual),
+    # and its reduce-scatter form (b2g_gemm_scatter_rows + b2g_tp_reduce_slots).
     p2p = {k: v.clone() for k, v in res.items()}
     tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
                            p2p["txt"], p2p["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
     tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], p2p["x"], gates[4], pe, mask, scratch)
+    push = {k: v.clone() for k, v in res.items()}
+    tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                           push["txt"], push["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch,
+                           push=True)
+    tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], push["x"], gates[4], pe, mask, scratch, push=True)
     torch.cuda.synchronize()
     b2g.check_device_error()
     ok = True
@@ -95,6 +101,12 @@ def main() -> int:
         cos3 = ((d3 @ d0) / (d3.norm() * d0.norm())).item()
         print(f"rank {rank}/{world} {k} p2p: err {err3:.3e} cos {cos3:.6f}", flush=True)
         ok = ok and err3 <= 1e-2 and cos3 >= 0.9999
+        d4 = (push[k] - res[k]).double().flatten()
+        err4 = ((d4 - d0).abs().max() / d0.abs().max()).item()
+        cos4 = ((d4 @ d0) / (d4.norm() * d0.norm())).item()
+        print(f"rank {rank}/{world} {k} push: err {err4:.3e} cos {cos4:.6f} identical-to-p2p "
+              f"{torch.equal(push[k], p2p[k])}", flush=True)
+        ok = ok and err4 <= 1e-2 and cos4 >= 0.9999
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
