@@ -1231,9 +1231,9 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
     p2p_mode = (f"tp{world}, two-phase all-reduce over NVLink peer memory (each rank sums its shard of rows from "
                 "every rank's partial, then every rank applies the bias + gated residual from the owners' sums)")
     # The headline is the fastest of the three communication paths, all measured in this run.
-    push_mode = (f"tp{world}, reduce-scatter from the row-split GEMMs' epilogues (each output row stored over "
-                 "NVLink into its owner rank's receive slot while the GEMM runs), a local sum of the slots, then "
-                 "every rank applies the bias + gated residual from the owners' sums")
+    push_mode = (f"tp{world}, all-reduce by copy-engine copies over NVLink (each shard of partial rows into its "
+                 "owner's receive slot, the owner's local sum of its slots copied to every rank), then the bias + "
+                 "gated residual from each rank's own sums")
     paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p), (q_ms, push_mode, sp_q)],
                    key=lambda x: x[0])
     ms, mode, split_us = paths[0]

@@ -97,9 +97,10 @@ _SIGNATURES = {
                             ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_gemm_tp_reduce": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int64), ctypes.c_int,
                             ctypes.POINTER(TpReduceDesc), ctypes.c_void_p], ctypes.c_int),
-    "b2g_gemm_scatter_rows": ([ctypes.POINTER(GemmDesc), ctypes.POINTER(ctypes.c_int64), ctypes.c_int,
-                               ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
-                              ctypes.c_int),
+    "b2g_tp_push_rows": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                          ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
+    "b2g_tp_push_sums": ([ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                          ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_reduce_slots": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
                              ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
@@ -414,28 +415,24 @@ def gemm_tp_reduce(problems: list[dict], row0: list[int], tp: TpReduceDesc,
     _check(lib.b2g_gemm_tp_reduce(arr, rows, len(descs), ctypes.byref(tp), ctypes.c_void_p(s)))
 
 
-def gemm_scatter_rows(problems: list[dict], row0: list[int], recv_ptrs: torch.Tensor, rows: int, world: int,
-                      rank: int, stream: torch.cuda.Stream | None = None) -> None:
-    """Row-split layer storing each bf16 output row into its owner's receive buffer
-    (b2g_gemm_scatter_rows): problems = [dict(x=, w=, out=)] with `out` a local bf16 [M, N] view
-    (the problem's nominal output, not written), row0 = their first rows among `rows`."""
-    lib = load()
-    descs = []
-    for pr in problems:
-        x, w, out = pr["x"], pr["w"], pr["out"]
-        _require_cuda(x, w, out)
-        d = GemmDesc()
-        d.M, d.K, d.N = x.shape[0], x.shape[1], w.shape[0]
-        d.a, d.a_dtype, d.lda = x.data_ptr(), _TORCH_TO_B2G[x.dtype], x.stride(0) if x.shape[0] > 1 else x.shape[1]
-        d.b, d.b_dtype, d.ldb = w.data_ptr(), _TORCH_TO_B2G[w.dtype], w.stride(0)
-        d.bias, d.bias_dtype = None, F32
-        d.d, d.d_dtype, d.ldd = out.data_ptr(), _TORCH_TO_B2G[out.dtype], out.stride(0) if out.shape[0] > 1 else d.N
-        d.epilogue = EPI_NONE
-        descs.append(d)
-    arr = (GemmDesc * len(descs))(*descs)
-    r0 = (ctypes.c_int64 * len(row0))(*row0)
-    s = (stream or torch.cuda.current_stream(problems[0]["x"].device)).cuda_stream
-    _check(lib.b2g_gemm_scatter_rows(arr, r0, len(descs), recv_ptrs.data_ptr(), rows, world, rank, ctypes.c_void_p(s)))
+def tp_push_rows(part: torch.Tensor, recv_ptrs: list[int], world: int, rank: int,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """Push form, step 1 (b2g_tp_push_rows): this rank's bf16 partial [rows, N] (contiguous) into
+    every owner's receive slot `rank` by copy-engine copies (recv_ptrs: the ranks' addresses)."""
+    rows, N = part.shape
+    arr = (ctypes.c_void_p * world)(*recv_ptrs)
+    s = (stream or torch.cuda.current_stream(part.device)).cuda_stream
+    _check(load().b2g_tp_push_rows(part.data_ptr(), arr, rows, N, world, rank, ctypes.c_void_p(s)))
+
+
+def tp_push_sums(sum_ptrs: list[int], sum_buf: torch.Tensor, world: int, rank: int,
+                 stream: torch.cuda.Stream | None = None) -> None:
+    """Push form, step 3 (b2g_tp_push_sums): this rank's rows of its sums into every other rank's
+    by copy-engine copies (sum_ptrs: the ranks' addresses)."""
+    rows, N = sum_buf.shape
+    arr = (ctypes.c_void_p * world)(*sum_ptrs)
+    s = (stream or torch.cuda.current_stream(sum_buf.device)).cuda_stream
+    _check(load().b2g_tp_push_sums(arr, rows, N, world, rank, ctypes.c_void_p(s)))
 
 
 def tp_reduce_slots(recv: torch.Tensor, sum_buf: torch.Tensor, world: int, rank: int,

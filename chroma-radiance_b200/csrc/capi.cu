@@ -362,33 +362,13 @@ b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, i
   return tc_gemm_launch_group(ps, count, static_cast<cudaStream_t>(stream));
 }
 
-b2g_status b2g_gemm_scatter_rows(const b2g_gemm_desc* descs, const int64_t* row0, int count, void* const* recv_ptrs,
-                                 int64_t rows, int world, int rank, void* stream) {
-  if (!descs || !row0 || !recv_ptrs || count < 1 || count > 2 || world < 1 || world > 8 || rank < 0 || rank >= world ||
-      rows <= 0)
-    return set_error(B2G_ERR_INVALID, "b2g_gemm_scatter_rows: 1 or 2 descriptors, row offsets, world in [1, 8]");
-  GemmProblem ps[2];
-  TpScatter sc;
-  sc.recv_ptrs = recv_ptrs;
-  sc.shard = (rows + world - 1) / world;
-  sc.ld = descs[0].N;
-  sc.slot_off = rank * sc.shard * sc.ld;
-  for (int i = 0; i < count; ++i) {
-    const b2g_gemm_desc* d = descs + i;
-    bool empty = false;
-    b2g_status s = desc_to_problem(d, "b2g_gemm_scatter_rows", &ps[i], &empty);
-    if (s != B2G_OK) return s;
-    if (empty || d->N != sc.ld || d->d_dtype != B2G_BF16 || d->epilogue != B2G_EPI_NONE || d->bias ||
-        row0[i] < 0 || row0[i] + d->M > rows)
-      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_scatter_rows: bf16 out, no bias or epilogue, one N, rows in range");
-    ps[i].scatter = &sc;
-    ps[i].tp_row0 = row0[i];
-    ps[i].allow_split = false;
-  }
-  for (int i = 0; i < count; ++i)
-    if (!tc_gemm_supported(ps[i], nullptr))
-      return set_error(B2G_ERR_UNSUPPORTED, "b2g_gemm_scatter_rows: operands not supported by the tensor-core path");
-  return tc_gemm_launch_group(ps, count, static_cast<cudaStream_t>(stream));
+b2g_status b2g_tp_push_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                            void* stream) {
+  return tp_push_rows(part, recv_ptrs, rows, N, world, rank, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int world, int rank, void* stream) {
+  return tp_push_sums(sum_ptrs, rows, N, world, rank, static_cast<cudaStream_t>(stream));
 }
 
 b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,

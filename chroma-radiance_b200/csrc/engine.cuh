@@ -35,9 +35,6 @@ struct GemmProblem {
   // summed with the other ranks' over NVLink inside the GEMM, see TpReduce.
   const struct TpReduce* tp = nullptr;
   int64_t tp_row0 = 0;      // first row of this problem in the partial / residual buffers
-  // Tensor-parallel row-split layer, reduce-scatter form: the bf16 output row r (= tp_row0 + m)
-  // goes to the receive buffer of the rank that owns it, see TpScatter.
-  const struct TpScatter* scatter = nullptr;
   // Attention input projection (epilogue kEpiQkvRope), see QkvRope.
   const struct QkvRope* rope = nullptr;
 };
@@ -67,14 +64,6 @@ struct TpReduce {
   int64_t ld_part, ld_res;
   int* counters;            // rank 0's arrival counters (one per output tile slot), peer-mapped
   int64_t counter_slots;    // capacity of `counters`
-};
-
-// Row owners of a reduce-scatter: row r belongs to rank r / shard; this rank's partial of it is
-// stored at recv_ptrs[r / shard] + slot_off + (r % shard) * ld (bf16), i.e. in the owner's
-// buffer [world slots][shard rows][ld], slot = this rank.
-struct TpScatter {
-  void* const* recv_ptrs;   // device array [world] of peer-mapped bf16 receive buffers
-  int64_t shard, slot_off, ld;
 };
 
 // The checks of b2g_gemm on one descriptor (`who` names the entry point in error messages);
@@ -155,6 +144,9 @@ b2g_status tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t r
                               const b2g_tp_residual_seg* segs, int nsegs, cudaStream_t st);
 b2g_status tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
                            cudaStream_t st);
+b2g_status tp_push_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                        cudaStream_t st);
+b2g_status tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int world, int rank, cudaStream_t st);
 
 // T5 attention (t5_attention.cu): Q, K, V [L, H, D] F32, rel_bias [H, L, L] or NULL, key mask
 // [L] or NULL, out [L, H*D] F32.

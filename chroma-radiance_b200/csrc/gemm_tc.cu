@@ -120,10 +120,6 @@ struct TcParams {
   float* const* tp_res;    // [world] F32 residual copies
   long long tp_ld_part, tp_ld_res;
   int* tp_counters;        // rank 0's per-slot arrival counters (epoch counting, never reset)
-  // reduce-scatter store of the bf16 output (TpScatter): row r = g.tp_row0 + m goes to
-  // scat_ptrs[r / scat_shard] + scat_slot + (r % scat_shard) * scat_ld
-  void* const* scat_ptrs;
-  long long scat_shard, scat_slot, scat_ld;
   int n_outer;             // tiles column-major over all groups' m-blocks (batch 1), see tile_coords
   int hd;                  // kEpiQkvRope: H * 128, the width of each of the q, k, v sections
   int split;               // kEpiQkvRope with a GELU tail: columns >= split (= 3 * hd) are bias +
@@ -327,10 +323,6 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, const TcGroup& G,
     uint32_t packed[16];
     pack16<OUT>(v, packed);
     uint16_t* dp = static_cast<uint16_t*>(G.d) + off;
-    if (p.scat_ptrs) {  // the owner's receive buffer, perhaps on another GPU (NVLink)
-      const long long r = G.tp_row0 + m;
-      dp = static_cast<uint16_t*>(p.scat_ptrs[r / p.scat_shard]) + p.scat_slot + (r % p.scat_shard) * p.scat_ld + n0;
-    }
     if (full && G.vec_ok) {
 #pragma unroll
       for (int j = 0; j < 4; ++j)
@@ -1037,7 +1029,6 @@ __global__ void __launch_bounds__(kThreadsK<KIND>, 1)
       epilogue_item<BN, EPI, OUT, KIND>(p, G, e, obuf, tacc, release, &maps.d[gi], bz, mb * kBM + e.row, nb * BN,
                                         split >= 0 ? tile - p.dp_tiles : tile, split);
     }
-    if (p.scat_ptrs) __threadfence_system();  // reduce-scatter stores to peers performed before exit
     if (lane == 0) bulk_wait_group_all();  // staged stores done before the CTA's smem goes away
   }
 
@@ -1243,7 +1234,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                   mb * 256 + static_cast<int>(rank) * 128 + e.row, nb * BN,
                                   (split >= 0 ? tile - p.dp_tiles : tile) * 2 + static_cast<int>(rank), split);
     }
-    if (p.scat_ptrs) __threadfence_system();  // reduce-scatter stores to peers performed before exit
     if (lane == 0) bulk_wait_group_all();
   }
 
@@ -1447,7 +1437,7 @@ bool tc_gemm_groupable(const GemmProblem& a, const GemmProblem& b) {
   return a.N == b.N && a.K == b.K && a.batch == 1 && b.batch == 1 && a.a_dtype == b.a_dtype &&
          a.b_dtype == b.b_dtype && a.d_dtype == b.d_dtype && a.epilogue == b.epilogue && a.alpha == b.alpha &&
          (a.bias == nullptr) == (b.bias == nullptr) && (!a.bias || a.bias_dtype == b.bias_dtype) &&
-         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr) && a.tp == b.tp && a.scatter == b.scatter &&
+         a.allow_split == b.allow_split && (a.a_scale == nullptr) == (b.a_scale == nullptr) && a.tp == b.tp &&
          (a.rope == nullptr) == (b.rope == nullptr) &&
          (!a.rope || (a.rope->heads == b.rope->heads && a.rope->eps == b.rope->eps));
 }
@@ -1528,7 +1518,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
     splits = static_cast<int>(f < nkb ? f : nkb);
     tail_only = g_force_splits < 0;
   }
-  if (nkb == 0 || !p.allow_split || p.tp || p.rope || p.scatter) splits = 1;
+  if (nkb == 0 || !p.allow_split || p.tp || p.rope) splits = 1;
   if (p.rope && v == V128) v = g_allow_pair ? VPAIR : V256;
   if (p.round_tf32 && v == VPAIR) v = V256;
   const bool pair = v == VPAIR;
@@ -1605,16 +1595,7 @@ b2g_status tc_gemm_launch_group(const GemmProblem* ps, int count, cudaStream_t s
   TcMaps maps;
   memset(&maps, 0, sizeof(maps));
   const uint32_t b_box = v == V256 ? 256u : 128u;
-  prm.tma_store = all_vec && g_tma_store && !p.tp && !p.scatter ? 1 : 0;
-  if (p.scatter) {
-    if (p.d_dtype != B2G_BF16 || p.epilogue != B2G_EPI_NONE || p.batch != 1 || !p.scatter->recv_ptrs ||
-        p.scatter->shard <= 0 || p.scatter->ld < p.N || p.scatter->ld % 8 || p.scatter->slot_off % 8)
-      return set_error(B2G_ERR_UNSUPPORTED, "reduce-scatter store: bf16 output, no epilogue, ld and slot % 8 == 0");
-    prm.scat_ptrs = p.scatter->recv_ptrs;
-    prm.scat_shard = p.scatter->shard;
-    prm.scat_slot = p.scatter->slot_off;
-    prm.scat_ld = p.scatter->ld;
-  }
+  prm.tma_store = all_vec && g_tma_store && !p.tp ? 1 : 0;
   if (p.rope) {
     const QkvRope& r = *p.rope;
     if (kind == 1 || p.d_dtype != B2G_BF16 || p.batch != 1)

@@ -207,6 +207,47 @@ b2g_status tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N,
   return check_cuda(cudaGetLastError(), "tp_reduce_slots launch");
 }
 
+// Push form with the copy engines: each transfer is one cudaMemcpyAsync of whole rows between
+// this device and a peer's mapped buffer (peer addresses given in host arrays), so the moves run
+// on the DMA engines, not the SMs.  Stream-ordered: the barrier kernel that follows starts after
+// they have completed.
+b2g_status tp_push_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                        cudaStream_t st) {
+  if (world < 1 || world > kTpMaxWorld || rank < 0 || rank >= world || !part || !recv_ptrs || rows <= 0 || N <= 0)
+    return set_error(B2G_ERR_INVALID, "tp_push_rows: world in [1, 8], rows and N positive");
+  const int64_t shard = (rows + world - 1) / world;
+  for (int k = 0; k < world; ++k) {
+    const int q = (rank + k) % world;  // each rank starts on a different peer
+    const int64_t r0 = q * shard < rows ? q * shard : rows;
+    const int64_t r1 = r0 + shard < rows ? r0 + shard : rows;
+    if (r1 <= r0) continue;
+    char* dst = static_cast<char*>(recv_ptrs[q]) + rank * shard * N * 2;
+    const char* src = static_cast<const char*>(part) + r0 * N * 2;
+    b2g_status s = check_cuda(cudaMemcpyAsync(dst, src, static_cast<size_t>((r1 - r0) * N * 2),
+                                              cudaMemcpyDeviceToDevice, st), "tp_push_rows copy");
+    if (s != B2G_OK) return s;
+  }
+  return B2G_OK;
+}
+
+b2g_status tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int world, int rank, cudaStream_t st) {
+  if (world < 1 || world > kTpMaxWorld || rank < 0 || rank >= world || !sum_ptrs || rows <= 0 || N <= 0)
+    return set_error(B2G_ERR_INVALID, "tp_push_sums: world in [1, 8], rows and N positive");
+  const int64_t shard = (rows + world - 1) / world;
+  const int64_t r0 = rank * shard < rows ? rank * shard : rows;
+  const int64_t r1 = r0 + shard < rows ? r0 + shard : rows;
+  if (r1 <= r0) return B2G_OK;
+  const char* src = static_cast<const char*>(sum_ptrs[rank]) + r0 * N * 2;
+  for (int k = 1; k < world; ++k) {
+    const int q = (rank + k) % world;
+    b2g_status s = check_cuda(cudaMemcpyAsync(static_cast<char*>(sum_ptrs[q]) + r0 * N * 2, src,
+                                              static_cast<size_t>((r1 - r0) * N * 2), cudaMemcpyDeviceToDevice, st),
+                              "tp_push_sums copy");
+    if (s != B2G_OK) return s;
+  }
+  return B2G_OK;
+}
+
 b2g_status tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,
                               const b2g_tp_residual_seg* segs, int nsegs, cudaStream_t st) {
   if (world < 1 || world > kTpMaxWorld || !sum_ptrs || !segs || nsegs < 1 || nsegs > 2 || rows <= 0 || N <= 0 ||

@@ -394,6 +394,8 @@ class SymmetricComm:
         self._flag_ptrs = torch.tensor(peers(self.flags, self._handles[4]), dtype=torch.int64, device=dev)
         self._sum_ptrs = torch.tensor(peers(self.sums, self._handles[5]), dtype=torch.int64, device=dev)
         self._recv_ptrs = torch.tensor(peers(self.recv, self._handles[6]), dtype=torch.int64, device=dev)
+        self._recv_host = peers(self.recv, self._handles[6])     # for the copy-engine pushes
+        self._sum_host = peers(self.sums, self._handles[5])
         self.epoch = 0
         self.desc = {}
         for name, t in (("double", self.res_double), ("single", self.res_single)):
@@ -431,26 +433,23 @@ class SymmetricComm:
         if mark:
             mark(label + ".residual")
 
-    def gemm_push(self, problems: list[dict], row0: list[int], mark=None, label: str = "") -> None:
-        """A row-split layer whose GEMM stores each output row's bf16 partial straight into the
-        owning rank's slot of self.recv (b2g_gemm_scatter_rows): the NVLink transfer overlaps
-        the GEMM.  problems = [dict(x=, w=)]; row0 = their first rows among self.rows."""
-        self.b2g.gemm_scatter_rows([dict(x=p["x"], w=p["w"], out=self.part[r:r + p["x"].shape[0]])
-                                    for p, r in zip(problems, row0)], row0, self._recv_ptrs, self.rows, self.world,
-                                   self.rank)
-        if mark:
-            mark(label)
-
     def reduce_push(self, segments: list[dict], mark=None, label: str = "") -> None:
-        """After gemm_push: barrier, sum this rank's rows from its receive slots (local reads,
-        b2g_tp_reduce_slots), barrier, then the residual update from every rank's sums
-        (b2g_tp_gather_residual)."""
+        """The all-reduce of self.part (written by a plain row-split GEMM) in the push form, every
+        NVLink transfer a copy-engine copy: each shard of partial rows into its owner's receive
+        slot (b2g_tp_push_rows), barrier, the owner sums its slots (b2g_tp_reduce_slots, local)
+        and copies its sums to every rank (b2g_tp_push_sums), barrier, then each rank applies
+        bias + gate from its own sum buffer (b2g_bias_gated_residual per segment:
+        dict(row0, bias, gate, residual))."""
+        self.b2g.tp_push_rows(self.part, self._recv_host, self.world, self.rank)
         self.barrier()
         self.b2g.tp_reduce_slots(self.recv, self.sums, self.world, self.rank)
+        self.b2g.tp_push_sums(self._sum_host, self.sums, self.world, self.rank)
         if mark:
             mark(label + ".reduce")
         self.barrier()
-        self.b2g.tp_gather_residual(self._sum_ptrs, self.sums, self.world, segments)
+        for g in segments:
+            r = g["residual"]
+            self.b2g.bias_gated_residual(self.sums[g["row0"]:g["row0"] + r.shape[0]], g.get("bias"), g["gate"], r)
         if mark:
             mark(label + ".residual")
 
@@ -495,16 +494,12 @@ def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, g
 
 def _row_split_p2p(ops, comm: SymmetricComm, problems: list[dict], row0: list[int], segments: list[dict], mk,
                    label: str, push: bool) -> None:
-    """One row-split layer and its all-reduce + residual update over peer memory: pull form (the
-    GEMM writes comm.part, phase 1 reads every rank's) or push form (the GEMM stores each row
-    into its owner's receive slot, phase 1 reads local slots)."""
-    if push:
-        comm.gemm_push(problems, row0, mk, label)
-        comm.reduce_push(segments, mk, label)
-    else:
-        ops.gemm_group([dict(x=p["x"], w=p["w"], out=comm.part[r:r + p["x"].shape[0]]) for p, r in zip(problems, row0)])
-        mk(label)
-        comm.reduce_p2p(segments, mk, label)
+    """One row-split layer (its GEMM writes comm.part) and its all-reduce + residual update over
+    peer memory: pull form (SymmetricComm.reduce_p2p, loads from the peers) or push form
+    (SymmetricComm.reduce_push, stores to the peers)."""
+    ops.gemm_group([dict(x=p["x"], w=p["w"], out=comm.part[r:r + p["x"].shape[0]]) for p, r in zip(problems, row0)])
+    mk(label)
+    (comm.reduce_push if push else comm.reduce_p2p)(segments, mk, label)
 
 
 def tp_double_block_p2p(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1,

@@ -270,15 +270,22 @@ b2g_status b2g_tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t 
 b2g_status b2g_tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,
                                   const b2g_tp_residual_seg* segs, int nsegs, void* stream);
 
-/* The reduce-scatter form of the same all-reduce (no reference counterpart): the row-split GEMM
- * itself stores each output row's bf16 partial into the receive buffer of the rank that owns
- * the row (recv_ptrs: device array [world] of peer-mapped bf16 [world][shard][N] buffers,
- * shard = ceil(rows / world); row r of problem i is row0[i] + m; this rank's slot), so the
- * transfer over NVLink overlaps the GEMM; b2g_tp_reduce_slots then sums the world slots of this
- * rank's rows (local reads) into its rows of `sum` [rows, N].  A b2g_tp_barrier goes between
- * them, and before b2g_tp_gather_residual.  Descriptors: bf16 out, no bias, no epilogue. */
-b2g_status b2g_gemm_scatter_rows(const b2g_gemm_desc* descs, const int64_t* row0, int count, void* const* recv_ptrs,
-                                 int64_t rows, int world, int rank, void* stream);
+/* The push form of the same all-reduce (no reference counterpart): every transfer over NVLink
+ * is a copy-engine copy of whole rows (cudaMemcpyAsync on `stream`), none an SM load.  Rows
+ * [0, rows) are split into world shards of ceil(rows / world) as above; peer addresses are
+ * HOST arrays here.
+ *   b2g_tp_push_rows: this rank's bf16 partial [rows, N] (local, row stride N) goes, shard by
+ *     shard, into the owning rank's receive buffer, slot `rank` (recv_ptrs: host array [world] of
+ *     peer-mapped bf16 [world][shard][N] buffers).
+ *   b2g_tp_reduce_slots: sums the world slots of this rank's receive buffer (local reads) in rank
+ *     order into its rows of `sum` [rows, N] (bf16).
+ *   b2g_tp_push_sums: this rank's rows of the sums go into every other rank's sum buffer
+ *     (sum_ptrs: host array [world]); each rank then applies b2g_bias_gated_residual from its
+ *     own, now complete, sum buffer.
+ * A b2g_tp_barrier goes before b2g_tp_reduce_slots and after b2g_tp_push_sums. */
+b2g_status b2g_tp_push_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                            void* stream);
+b2g_status b2g_tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int world, int rank, void* stream);
 b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
                                void* stream);
 
