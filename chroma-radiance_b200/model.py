@@ -173,13 +173,6 @@ class ForwardScratch:
         self.emb_in = torch.empty((P * 256, EMB_K), dtype=bf, device=dev)
         self.nx = torch.empty((2, P * 256, NERF_HID), dtype=f, device=dev)  # decoder state per half
         self.params = torch.empty((2 * P, NERF_PARAMS), dtype=f, device=dev)
-        self.gate = torch.empty((2 * P, NERF_MLP, NERF_HID), dtype=f, device=dev)
-        self.value = torch.empty_like(self.gate)
-        self.fc2 = torch.empty((2 * P, NERF_HID, NERF_MLP), dtype=f, device=dev)
-        self.xn = torch.empty((2 * P, 256, NERF_HID), dtype=f, device=dev)
-        self.x1 = torch.empty((2 * P, 256, NERF_MLP), dtype=f, device=dev)
-        self.x2 = torch.empty_like(self.x1)
-        self.xo = torch.empty((2 * P, 256, NERF_HID), dtype=f, device=dev)
         self.velocity = torch.empty((1, 3, H, W), dtype=f, device=dev)
 
 
@@ -274,20 +267,6 @@ class ChromaRadiance:
         for blk in self.nerf:
             b2g.gemm(s.img16, blk.param_w, blk.param_b, out=s.params)
             b2g.nerf_glu_block(s.params, blk.norm, s.nx)
-
-    def nerf_glu_block_unfused(self, s: ForwardScratch, blk: NerfBlock) -> None:
-        """The GLU block after its param_generator GEMM as the reference sequences it (weight
-        preparation, rms_norm, three batched products, silu_mul, add), each step its own launch
-        through HBM: the comparison for the fused b2g.nerf_glu_block."""
-        P = s.P
-        xn, nx = s.xn.view(2 * P * 256, NERF_HID), s.nx.view(2 * P * 256, NERF_HID)
-        b2g.nerf_glu_weights(s.params, s.gate, s.value, s.fc2)
-        b2g.rms_norm(nx, blk.norm, xn)
-        b2g.batched_matmul_Bt(s.xn, s.gate, s.x1)
-        b2g.batched_matmul_Bt(s.xn, s.value, s.x2)
-        b2g.silu_mul(s.x1, s.x2)
-        b2g.batched_matmul_Bt(s.x1, s.fc2, s.xo)
-        b2g.add_inplace(s.nx, s.xo)
 
     def forward_cfg(self, s: ForwardScratch, x_img: torch.Tensor, ctx_cond: torch.Tensor, ctx_uncond: torch.Tensor,
                     pe: torch.Tensor, dct: torch.Tensor, masks: torch.Tensor, cfg_scale: float) -> torch.Tensor:

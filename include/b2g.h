@@ -463,7 +463,8 @@ b2g_status b2g_set_gemm_variant(int variant, int splits);
 /* Fused-attention key splits for tests and tuning (no reference counterpart): 0 automatic
  * (a launch that fills under half of the SMs, e.g. a tensor-parallel rank's few heads, splits
  * its key blocks into slices run by separate CTAs and merged by a second kernel), -1 never,
- * > 0 that many slices (at most one per 4 key blocks).  Affects later calls. */
+ * > 0 that many slices (at most one per 4 key blocks).  Sequences of over 64K keys always
+ * split (a CTA covers at most 512 key blocks).  Affects later calls. */
 b2g_status b2g_set_attention_splits(int splits);
 
 #ifdef __cplusplus
