@@ -534,7 +534,7 @@ class _Marks:
     def durations(self):
         out, prev = {}, self.start
         for lab, ev in zip(self.labels, self.events):
-            out[lab] = prev.elapsed_time(ev)
+            out[lab] = out.get(lab, 0.0) + prev.elapsed_time(ev)
             prev = ev
         return out
 
@@ -1054,10 +1054,13 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
     L=4608).  One GPU: the unsharded block pair.  N GPUs: tp.py's fused tensor-parallel path, and
     on rank 0 also the unsharded block pair on its own GPU (the 1-GPU time the speed-up is taken
     against, and the parity reference: the replicated residual streams after one step from the
-    same seeded inputs, max|d|/max|ref| and cosine of the update).  The NCCL all-reduce variant
-    is timed beside the fused one.  Eager launches (the fused path's barrier epochs change every
-    call); an L2 flush (256 MB write) and, at N > 1, a barrier before every step, outside the
-    events; device time, max over ranks."""
+    same seeded inputs, max|d|/max|ref| and cosine of the update).  The NCCL all-reduce, pull
+    and push variants are timed beside the fused one.  Every path (the unsharded one included)
+    is timed as a CUDA graph replay of its whole block pair, captured after an eager run (the
+    cross-rank barriers keep their epoch on the device, so replays stay in step); the
+    per-operation split comes from a second capture with timing events between the launches.
+    An L2 flush (256 MB write) and, at N > 1, a barrier before every step, outside the events;
+    device time, max over ranks."""
     import datetime
 
     import blocks
@@ -1104,11 +1107,29 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
             out.append(a.elapsed_time(b))
         return out
 
-    def split(fn) -> dict:
+    cap = torch.cuda.Stream(dev)
+    held = []   # every captured graph; released before the leg returns (NCCL's among them)
+
+    def graphed(fn):
+        """fn (already run eagerly: every workspace exists) captured in a CUDA graph, and again
+        with timing events between its launches; returns (replay, marked graph, marks)."""
         torch.cuda.synchronize(dev)
-        mk = _EagerMarks(torch, stream)
-        mk.begin()
-        fn(mk)
+        g, gm = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        mk = _Marks(torch, cap)
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(g, stream=cap):
+                fn()
+            with torch.cuda.graph(gm, stream=cap):
+                mk.begin()
+                fn(mk)
+        held.extend([g, gm])
+        return g.replay, gm, mk
+
+    def split(captured, sync_ranks: bool) -> dict:
+        _, gm, mk = captured
+        if sync_ranks:
+            barrier()
+        gm.replay()
         torch.cuda.synchronize(dev)
         return {k: 1e3 * v for k, v in mk.durations().items()}
 
@@ -1131,10 +1152,12 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
         unsharded()
         torch.cuda.synchronize(dev)
         ref = {k: delta(ures[k], res[k]) for k in res}
-        per = timed(unsharded, False)
+        cu = graphed(unsharded)
+        per = timed(cu[0], False)
         uns_ms = sum(per) / steps
-        uns_split = split(unsharded)
-        del s1, ures
+        uns_split = split(cu, False)
+        del cu, s1, ures
+        held.clear()
     if world == 1:
         out.update({"mode": "unsharded block pair, 1 GPU", "ms_per_step": round(uns_ms, 5),
                     "tflops": round((lin + att) / (uns_ms * 1e-3) / 1e12, 2),
@@ -1176,8 +1199,9 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                              "of the replicated residual streams (txt, img, single-block x) after one step")
         parity["within_tolerance"] = all(v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999
                                          for k, v in parity.items() if isinstance(v, dict))
-    per_f = timed(fused, True)
-    sp = split(fused)
+    cf = graphed(fused)
+    per_f = timed(cf[0], True)
+    sp = split(cf, True)
     nres = {k: v.clone() for k, v in res.items()}
 
     def nccl(mark=None):
@@ -1185,8 +1209,11 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                            nres["txt"], nres["img"], gt[0], gt[1], gt[2], gt[3], pe, mask, scratch, mark)
         tp.tp_single_block(ops, ts, act["x_mod"], nres["x"], gt[4], pe, mask, scratch, mark)
 
-    per_n = timed(nccl, True)
-    sp_n = split(nccl)
+    nccl()   # eager first (NCCL's communicator and the workspaces), then captured
+    barrier()
+    cn = graphed(nccl)
+    per_n = timed(cn[0], True)
+    sp_n = split(cn, True)
     runs = {}
     for name, push in (("p2p", False), ("push", True)):
         pres = {k: v.clone() for k, v in res.items()}
@@ -1205,7 +1232,8 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                                 "cosine": float((got[k] @ ref[k]) / (got[k].norm() * ref[k].norm()))} for k in got}
             parity["within_tolerance"] = parity["within_tolerance"] and all(
                 v["max_rel"] <= 1e-2 and v["cosine"] >= 0.9999 for v in parity[name].values())
-        runs[name] = (timed(path, True), split(path))
+        cp = graphed(path)
+        runs[name] = (timed(cp[0], True), split(cp, True))
     per_p, sp_p = runs["p2p"]
     per_q, sp_q = runs["push"]
     b2g_mod = __import__("b2g")
@@ -1246,7 +1274,12 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                                  "breakdown_us": {k: round(v, 1) for k, v in sp_.items()}} for t_, md, sp_ in paths[1:]],
                 "allreduce_bytes_per_step": 3 * L * H * 2, "parity": parity,
                 "parity_of": "the fused path (top level) and the peer-memory paths ('p2p', 'push'); the NCCL path's "
-                             "sums differ from the peer-memory paths' only in summation order"})
+                             "sums differ from the peer-memory paths' only in summation order",
+                "launch": "CUDA graph replay of the whole block pair (every path, the unsharded one included)"})
+    del cf, cn, cp
+    held.clear()
+    torch.cuda.synchronize(dev)
+    barrier()
     del comm
     return out
 

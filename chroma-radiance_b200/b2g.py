@@ -105,6 +105,8 @@ _SIGNATURES = {
                              ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
                        ctypes.c_int),
+    "b2g_tp_barrier_next": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                             ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_reduce_shard": ([ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_int,
                                                                                        ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_gather_residual": ([ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_void_p,
@@ -477,6 +479,16 @@ def tp_barrier(flag_ptrs: torch.Tensor, own_flags: torch.Tensor, world: int, ran
     lib = load()
     s = (stream or torch.cuda.current_stream(own_flags.device)).cuda_stream
     _check(lib.b2g_tp_barrier(flag_ptrs.data_ptr(), own_flags.data_ptr(), world, rank, epoch, ctypes.c_void_p(s)))
+
+
+def tp_barrier_next(flag_ptrs: torch.Tensor, own_flags: torch.Tensor, epoch_counter: torch.Tensor, world: int,
+                    rank: int, stream: torch.cuda.Stream | None = None) -> None:
+    """The cross-rank barrier with its epoch held in device memory (b2g_tp_barrier_next):
+    epoch_counter this rank's own int32 [1] CUDA tensor, zero before the first call.  Safe to
+    capture in a CUDA graph: every replay waits on the next epoch."""
+    s = (stream or torch.cuda.current_stream(own_flags.device)).cuda_stream
+    _check(load().b2g_tp_barrier_next(flag_ptrs.data_ptr(), own_flags.data_ptr(), epoch_counter.data_ptr(), world,
+                                      rank, ctypes.c_void_p(s)))
 
 
 def t5_attention(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, rel_bias: torch.Tensor | None, n_head: int,

@@ -377,7 +377,13 @@ b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_
 }
 
 b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream) {
-  return tp_barrier(flag_ptrs, own_flags, world, rank, epoch, static_cast<cudaStream_t>(stream));
+  return tp_barrier(flag_ptrs, own_flags, world, rank, epoch, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_tp_barrier_next(int* const* flag_ptrs, int* own_flags, int* epoch_counter, int world, int rank,
+                               void* stream) {
+  if (!epoch_counter) return set_error(B2G_ERR_INVALID, "tp_barrier_next: epoch_counter is NULL");
+  return tp_barrier(flag_ptrs, own_flags, world, rank, 0, epoch_counter, static_cast<cudaStream_t>(stream));
 }
 
 b2g_status b2g_tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t ld, int64_t rows, int64_t N,

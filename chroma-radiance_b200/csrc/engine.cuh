@@ -137,7 +137,8 @@ b2g_status bias_gated_residual(const void* y, b2g_dtype y_dtype, int64_t ldy, co
                                float* residual, int64_t ldr, int64_t M, int64_t N, cudaStream_t st);
 
 // Cross-rank barrier over peer-mapped flag arrays (tp_comm.cu), bounded wait.
-b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, cudaStream_t st);
+b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, int* epoch_ctr,
+                      cudaStream_t st);
 b2g_status tp_reduce_shard(const void* const* part_ptrs, void* sum, int64_t ld, int64_t rows, int64_t N, int world,
                            int rank, cudaStream_t st);
 b2g_status tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t rows, int64_t N, int world,

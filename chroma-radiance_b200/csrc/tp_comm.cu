@@ -16,8 +16,15 @@ namespace b2g {
 
 namespace {
 
-__global__ void tp_barrier_kernel(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, int* err) {
+__global__ void tp_barrier_kernel(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch,
+                                  int* epoch_ctr, int* err) {
   const int q = threadIdx.x;
+  // Device-held epoch (epoch_ctr != nullptr): this barrier's epoch is the previous one + 1,
+  // read by every thread before thread 0 stores it back, so a CUDA graph that captured the
+  // launch waits on a fresh epoch at every replay.
+  if (epoch_ctr) epoch = *epoch_ctr + 1;
+  __syncthreads();
+  if (epoch_ctr && q == 0) *epoch_ctr = epoch;
   if (q >= world) return;
   __threadfence_system();
   int* slot = flag_ptrs[q] + rank;
@@ -281,13 +288,16 @@ b2g_status tp_gather_residual(const void* const* sum_ptrs, int64_t ld, int64_t r
   return check_cuda(cudaGetLastError(), "tp_gather_residual launch");
 }
 
-b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, cudaStream_t st) {
+b2g_status tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, int* epoch_ctr,
+                      cudaStream_t st) {
   if (world < 1 || world > 1024 || rank < 0 || rank >= world || !flag_ptrs || !own_flags)
     return set_error(B2G_ERR_INVALID, "tp_barrier: world/rank/pointers");
+  if (!epoch_ctr && epoch < 1) return set_error(B2G_ERR_INVALID, "tp_barrier: epoch must be >= 1");
   DeviceInfo* dev = nullptr;
   b2g_status s = device_info(&dev);
   if (s != B2G_OK) return s;
-  tp_barrier_kernel<<<1, 32 * ((world + 31) / 32), 0, st>>>(flag_ptrs, own_flags, world, rank, epoch, dev->err_word);
+  tp_barrier_kernel<<<1, 32 * ((world + 31) / 32), 0, st>>>(flag_ptrs, own_flags, world, rank, epoch, epoch_ctr,
+                                                                    dev->err_word);
   note_launch();
   return check_cuda(cudaGetLastError(), "tp_barrier launch");
 }

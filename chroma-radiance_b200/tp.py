@@ -351,7 +351,7 @@ class SymmetricComm:
     residual copies (the double block's txt rows then img rows, and the single block's
     stream), and the tile arrival counters (rank 0's copy is the one used).  `barrier()` is the
     cross-rank barrier each fused layer needs before its outputs are read or its partial buffer
-    is reused (b2g_tp_barrier on a peer-mapped flag array)."""
+    is reused (b2g_tp_barrier_next on a peer-mapped flag array)."""
 
     COUNTER_SLOTS = 8192
 
@@ -396,7 +396,7 @@ class SymmetricComm:
         self._recv_ptrs = torch.tensor(peers(self.recv, self._handles[6]), dtype=torch.int64, device=dev)
         self._recv_host = peers(self.recv, self._handles[6])     # for the copy-engine pushes
         self._sum_host = peers(self.sums, self._handles[5])
-        self.epoch = 0
+        self.epoch_ctr = torch.zeros(1, dtype=torch.int32, device=dev)   # the barrier's epoch, kept on the device
         self.desc = {}
         for name, t in (("double", self.res_double), ("single", self.res_single)):
             d = b2g.TpReduceDesc()
@@ -454,9 +454,10 @@ class SymmetricComm:
             mark(label + ".residual")
 
     def barrier(self) -> None:
-        """All ranks' fused layers are done (bounded wait in libb2g's own barrier kernel)."""
-        self.epoch += 1
-        self.b2g.tp_barrier(self._flag_ptrs, self.flags, self.world, self.rank, self.epoch)
+        """All ranks' fused layers are done (bounded wait in libb2g's own barrier kernel).  The
+        epoch lives in device memory (b2g_tp_barrier_next), so a CUDA graph of a step that
+        holds barriers replays correctly."""
+        self.b2g.tp_barrier_next(self._flag_ptrs, self.flags, self.epoch_ctr, self.world, self.rank)
 
 
 def tp_double_block_fused(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1,

@@ -246,6 +246,14 @@ b2g_status b2g_gemm_tp_reduce(const b2g_gemm_desc* descs, const int64_t* row0, i
  * of its own array reach `epoch`.  Call with the same increasing epoch on every rank.  The wait
  * is bounded (2 s): on timeout the device error word gets bit 8 (b2g_check_device_error). */
 b2g_status b2g_tp_barrier(int* const* flag_ptrs, int* own_flags, int world, int rank, int epoch, void* stream);
+/* The same barrier with the epoch kept in device memory: epoch_counter (this rank's own int,
+ * zero before the first call, not peer-mapped) holds the last epoch; the kernel waits on
+ * *epoch_counter + 1 and stores it back.  Because the host passes no epoch, a CUDA graph that
+ * captured the call replays with a fresh epoch each time (b2g_tp_barrier bakes its argument
+ * into the graph).  Every rank makes the same sequence of calls; do not mix the two forms on
+ * one flag array. */
+b2g_status b2g_tp_barrier_next(int* const* flag_ptrs, int* own_flags, int* epoch_counter, int world, int rank,
+                               void* stream);
 
 /* Two-phase all-reduce of a row-split layer's bf16 partial over NVLink peer memory, with the
  * residual update folded in (no reference counterpart: it replaces the ncclAllReduce +

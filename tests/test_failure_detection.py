@@ -235,3 +235,31 @@ def test_tp_barrier_wait_expires_and_reports(engine, oracle):
     torch.cuda.synchronize()
     engine.check_device_error()
     assert rel_err(got.cpu().numpy(), want) <= 1e-4
+
+
+@pytest.mark.gpu
+def test_tp_barrier_next_keeps_its_epoch_on_the_device(engine):
+    """b2g_tp_barrier_next at world 1 (its own arrival completes it): the device counter advances
+    once per call, eager and under CUDA graph replay alike, and the flag array follows it."""
+    dev = "cuda:0"
+    own = torch.zeros(1, dtype=torch.int32, device=dev)
+    ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+    ptrs = torch.tensor([own.data_ptr()], dtype=torch.int64, device=dev)
+    for _ in range(3):
+        engine.tp_barrier_next(ptrs, own, ctr, 1, 0)
+    torch.cuda.synchronize()
+    assert ctr.item() == 3 and own.item() == 3
+    g = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(dev)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(g, stream=cap):
+            engine.tp_barrier_next(ptrs, own, ctr, 1, 0)
+            engine.tp_barrier_next(ptrs, own, ctr, 1, 0)
+    torch.cuda.synchronize()
+    assert ctr.item() == 3          # capture launches nothing
+    for _ in range(4):
+        g.replay()
+    torch.cuda.synchronize()
+    engine.check_device_error()
+    assert ctr.item() == 11 and own.item() == 11
+    del g
