@@ -790,21 +790,36 @@ def approximator_leg(torch, dev, flush, stream, run, steps: int, ms_list=None) -
     """The approximator alone (compute_modulation: 12 GEMMs at M=344, 556 MB of bf16 weights, the
     weight-streaming 'skinny' shape): median per-call time over `steps` calls (CUDA events, L2
     flushed before each), TFLOP/s and achieved HBM GB/s of its algorithmic bytes against
-    MEASURED_PEAKS.json hbm_gbs; with `run(mark)` also a per-GEMM split of one eager call.
-    `ms_list` (the reference arm) gives the per-call times instead of running anything."""
+    MEASURED_PEAKS.json hbm_gbs.  The engine's call is captured once in a CUDA graph and
+    replayed (forward_cfg runs it inside its step graph); with `run(mark)` also a per-GEMM
+    split from a second capture with timing events between the launches.  `ms_list` (the
+    reference arm) gives the per-call times instead of running anything."""
     shapes = approximator_shapes()
     flop = sum(2.0 * M * N * K for _, M, N, K in shapes)
     byts = sum(approximator_bytes(M, N, K) for _, M, N, K in shapes)
+    graph = marked = marks = None
     if ms_list is None:
         for _ in range(3):
             run()
+        torch.cuda.synchronize(dev)
+        cap = torch.cuda.Stream(dev)
+        graph, marked = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        marks = _Marks(torch, cap)
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                run()
+            with torch.cuda.graph(marked, stream=cap):
+                marks.begin()
+                run(marks)
+        for _ in range(3):
+            graph.replay()
         torch.cuda.synchronize(dev)
         ms_list = []
         for i in range(steps):
             flush.fill_(i & 0xFF)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            run()
+            graph.replay()
             b.record(stream)
             b.synchronize()
             ms_list.append(a.elapsed_time(b))
@@ -816,15 +831,15 @@ def approximator_leg(torch, dev, flush, stream, run, steps: int, ms_list=None) -
            "flop": flop, "bytes": byts,
            "workload": "the approximator (compute_modulation, guidance 0): 12 GEMMs at M=344 (64->5120, 10 x "
                        "5120->5120, 5120->3072) with their RMSNorms; median of per-call CUDA-event times, L2 "
-                       "flushed before each call; bytes = bf16 weights + F32 activations in + F32 outputs"}
-    if run is not None:
+                       "flushed before each call; bytes = bf16 weights + F32 activations in + F32 outputs"
+                       + ("" if run is None else "; the engine's call replayed as a CUDA graph")}
+    if marked is not None:
         flush.fill_(0)
         torch.cuda.synchronize(dev)
-        mk = _EagerMarks(torch, stream)
-        mk.begin()
-        run(mk)
+        marked.replay()
         torch.cuda.synchronize(dev)
-        per = mk.durations()
+        per = marks.durations()
+        del graph, marked
         out["per_gemm"] = {lab: {"us": round(1e3 * per[lab], 1),
                                  "hbm_gbs": round(approximator_bytes(M, N, K) / (per[lab] * 1e-3) / 1e9, 1),
                                  "tflops": round(2.0 * M * N * K / (per[lab] * 1e-3) / 1e12, 1)}
