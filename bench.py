@@ -1230,7 +1230,7 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
     per_n = timed(cn[0], True)
     sp_n = split(cn, True)
     runs = {}
-    for name, push in (("p2p", False), ("push", True)):
+    for name, push in (("p2p", False), ("push", True), ("store", "store")):
         pres = {k: v.clone() for k, v in res.items()}
 
         def path(mark=None, pres=pres, push=push):
@@ -1251,20 +1251,21 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
         runs[name] = (timed(cp[0], True), split(cp, True))
     per_p, sp_p = runs["p2p"]
     per_q, sp_q = runs["push"]
+    per_s, sp_s = runs["store"]
     b2g_mod = __import__("b2g")
     b2g_mod.check_device_error()
-    labels, labels_n, labels_p, labels_q = sorted(sp), sorted(sp_n), sorted(sp_p), sorted(sp_q)
-    t = torch.tensor([sum(per_f), sum(per_n), sum(per_p), sum(per_q)] + [sp[k] for k in labels] +
-                     [sp_n[k] for k in labels_n] + [sp_p[k] for k in labels_p] + [sp_q[k] for k in labels_q],
-                     device=dev, dtype=torch.float64)
+    labels, labels_n, labels_p, labels_q, labels_s = sorted(sp), sorted(sp_n), sorted(sp_p), sorted(sp_q), sorted(sp_s)
+    t = torch.tensor([sum(per_f), sum(per_n), sum(per_p), sum(per_q), sum(per_s)] + [sp[k] for k in labels] +
+                     [sp_n[k] for k in labels_n] + [sp_p[k] for k in labels_p] + [sp_q[k] for k in labels_q] +
+                     [sp_s[k] for k in labels_s], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    f_ms, n_ms, p_ms, q_ms = (float(t[i]) / steps for i in range(4))
-    vals = t[4:].tolist()
+    f_ms, n_ms, p_ms, q_ms, s_ms = (float(t[i]) / steps for i in range(5))
+    vals = t[5:].tolist()
     splits_out = []
-    for lab in (labels, labels_n, labels_p, labels_q):
+    for lab in (labels, labels_n, labels_p, labels_q, labels_s):
         splits_out.append({k: float(v) for k, v in zip(lab, vals[:len(lab)])})
         vals = vals[len(lab):]
-    sp, sp_n, sp_p, sp_q = splits_out
+    sp, sp_n, sp_p, sp_q, sp_s = splits_out
     u = torch.tensor([uns_ms or 0.0], device=dev, dtype=torch.float64)
     dist.all_reduce(u, op=dist.ReduceOp.MAX)   # rank 0's 1-GPU time, on every rank
     uns_ms = float(u[0])
@@ -1273,12 +1274,15 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                  "(b2g_bias_gated_residual)")
     p2p_mode = (f"tp{world}, two-phase all-reduce over NVLink peer memory (each rank sums its shard of rows from "
                 "every rank's partial, then every rank applies the bias + gated residual from the owners' sums)")
-    # The headline is the fastest of the three communication paths, all measured in this run.
+    # The headline is the fastest of the communication paths, all measured in this run.
     push_mode = (f"tp{world}, all-reduce by copy-engine copies over NVLink (each shard of partial rows into its "
                  "owner's receive slot, the owner's local sum of its slots copied to every rank), then the bias + "
                  "gated residual from each rank's own sums")
-    paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p), (q_ms, push_mode, sp_q)],
-                   key=lambda x: x[0])
+    store_mode = (f"tp{world}, all-reduce by SM stores over NVLink (each partial row stored into its owner's "
+                  "receive slot, the owner's sum of its slots stored into every rank's sum buffer), then the bias + "
+                  "gated residual from each rank's own sums")
+    paths = sorted([(f_ms, fused_mode, sp), (n_ms, nccl_mode, sp_n), (p_ms, p2p_mode, sp_p), (q_ms, push_mode, sp_q),
+                    (s_ms, store_mode, sp_s)], key=lambda x: x[0])
     ms, mode, split_us = paths[0]
     out.update({"mode": mode,
                 "ms_per_step": round(ms, 5), "tflops": round((lin + att) / (ms * 1e-3) / 1e12, 2),
@@ -1288,7 +1292,7 @@ def tp1024_leg(args, torch, world, rank, dev, txt_w, img_w, sw, flush) -> dict:
                 "other_modes": [{"mode": md, "ms_per_step": round(t_, 5),
                                  "breakdown_us": {k: round(v, 1) for k, v in sp_.items()}} for t_, md, sp_ in paths[1:]],
                 "allreduce_bytes_per_step": 3 * L * H * 2, "parity": parity,
-                "parity_of": "the fused path (top level) and the peer-memory paths ('p2p', 'push'); the NCCL path's "
+                "parity_of": "the fused path (top level) and the peer-memory paths ('p2p', 'push', 'store'); the NCCL path's "
                              "sums differ from the peer-memory paths' only in summation order",
                 "launch": "CUDA graph replay of the whole block pair (every path, the unsharded one included)"})
     del cf, cn, cp

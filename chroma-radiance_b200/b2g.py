@@ -105,6 +105,10 @@ _SIGNATURES = {
                              ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p],
                        ctypes.c_int),
+    "b2g_tp_scatter_rows": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                             ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
+    "b2g_tp_reduce_slots_bcast": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int,
+                                   ctypes.c_int, ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_barrier_next": ([ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                              ctypes.c_void_p], ctypes.c_int),
     "b2g_tp_reduce_shard": ([ctypes.c_void_p, ctypes.c_void_p] + [ctypes.c_int64] * 3 + [ctypes.c_int, ctypes.c_int,
@@ -444,6 +448,27 @@ def tp_reduce_slots(recv: torch.Tensor, sum_buf: torch.Tensor, world: int, rank:
     rows, N = sum_buf.shape
     s = (stream or torch.cuda.current_stream(sum_buf.device)).cuda_stream
     _check(load().b2g_tp_reduce_slots(recv.data_ptr(), sum_buf.data_ptr(), rows, N, world, rank, ctypes.c_void_p(s)))
+
+
+def tp_scatter_rows(part: torch.Tensor, recv_ptrs: torch.Tensor, world: int, rank: int,
+                    stream: torch.cuda.Stream | None = None) -> None:
+    """Store form, step 1 (b2g_tp_scatter_rows): this rank's bf16 partial [rows, N] (contiguous)
+    into every owner's receive slot `rank` by SM stores; recv_ptrs an int64 CUDA tensor of the
+    ranks' receive-buffer addresses."""
+    rows, N = part.shape
+    s = (stream or torch.cuda.current_stream(part.device)).cuda_stream
+    _check(load().b2g_tp_scatter_rows(part.data_ptr(), recv_ptrs.data_ptr(), rows, N, world, rank,
+                                      ctypes.c_void_p(s)))
+
+
+def tp_reduce_slots_bcast(recv: torch.Tensor, sum_ptrs: torch.Tensor, rows: int, N: int, world: int, rank: int,
+                          stream: torch.cuda.Stream | None = None) -> None:
+    """Store form, step 2 (b2g_tp_reduce_slots_bcast): the sum of this rank's receive slots
+    (recv bf16 [world, shard, N]) stored into every rank's sum buffer [rows, N] (sum_ptrs an
+    int64 CUDA tensor of their addresses)."""
+    s = (stream or torch.cuda.current_stream(recv.device)).cuda_stream
+    _check(load().b2g_tp_reduce_slots_bcast(recv.data_ptr(), sum_ptrs.data_ptr(), rows, N, world, rank,
+                                            ctypes.c_void_p(s)))
 
 
 def tp_reduce_shard(part_ptrs: torch.Tensor, sum_buf: torch.Tensor, world: int, rank: int,

@@ -371,6 +371,16 @@ b2g_status b2g_tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int 
   return tp_push_sums(sum_ptrs, rows, N, world, rank, static_cast<cudaStream_t>(stream));
 }
 
+b2g_status b2g_tp_scatter_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world,
+                               int rank, void* stream) {
+  return tp_scatter_rows(part, recv_ptrs, rows, N, world, rank, static_cast<cudaStream_t>(stream));
+}
+
+b2g_status b2g_tp_reduce_slots_bcast(const void* recv, void* const* sum_ptrs, int64_t rows, int64_t N, int world,
+                                     int rank, void* stream) {
+  return tp_reduce_slots_bcast(recv, sum_ptrs, rows, N, world, rank, static_cast<cudaStream_t>(stream));
+}
+
 b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
                                void* stream) {
   return tp_reduce_slots(recv, sum, rows, N, world, rank, static_cast<cudaStream_t>(stream));

@@ -148,6 +148,10 @@ b2g_status tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N,
 b2g_status tp_push_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
                         cudaStream_t st);
 b2g_status tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int world, int rank, cudaStream_t st);
+b2g_status tp_scatter_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                           cudaStream_t st);
+b2g_status tp_reduce_slots_bcast(const void* recv, void* const* sum_ptrs, int64_t rows, int64_t N, int world,
+                                 int rank, cudaStream_t st);
 
 // T5 attention (t5_attention.cu): Q, K, V [L, H, D] F32, rel_bias [H, L, L] or NULL, key mask
 // [L] or NULL, out [L, H*D] F32.

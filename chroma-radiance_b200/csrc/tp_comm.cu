@@ -130,6 +130,63 @@ __global__ void __launch_bounds__(256) tp_reduce_slots_kernel(const __nv_bfloat1
   }
 }
 
+// The store form: every NVLink transfer is an SM store (16 bytes a thread, consecutive threads on
+// consecutive bytes of a row), none a load and none a copy-engine copy.
+//   tp_scatter_rows_kernel: row m of this rank's bf16 partial goes to its owner q = m / shard,
+//     slot `rank`, row m - q * shard of q's receive buffer [world][shard][N].
+//   tp_reduce_slots_bcast_kernel: this rank sums its receive slots in rank order (local reads,
+//     bf16 rounding as a bf16 all-reduce rounds) and stores each sum row into every rank's sum
+//     buffer (its own included) at the same row.
+__global__ void __launch_bounds__(256) tp_scatter_rows_kernel(const __nv_bfloat16* __restrict__ part,
+                                                               __nv_bfloat16* const* recv, int rank,
+                                                               long long rows, long long shard, int N) {
+  const int groups = N / 8;
+  const long long total = rows * groups;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long m = i / groups;
+    const int n = static_cast<int>(i % groups) * 8;
+    const long long q = m / shard;
+    const uint4 u = __ldcs(reinterpret_cast<const uint4*>(part + m * N + n));
+    *reinterpret_cast<uint4*>(recv[q] + (rank * shard + (m - q * shard)) * N + n) = u;
+  }
+}
+
+__global__ void __launch_bounds__(256) tp_reduce_slots_bcast_kernel(const __nv_bfloat16* __restrict__ recv,
+                                                                     __nv_bfloat16* const* sums, int world,
+                                                                     long long shard, long long r0,
+                                                                     long long nrows, int N) {
+  const int groups = N / 8;
+  const long long total = nrows * groups;
+  const long long slot = shard * N;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / groups;
+    const int n = static_cast<int>(i % groups) * 8;
+    uint4 u[kTpMaxWorld];
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q)
+      if (q < world) u[q] = __ldcs(reinterpret_cast<const uint4*>(recv + q * slot + r * N + n));
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q) {
+      if (q >= world) break;
+      float v[8];
+      bf16x8_to_f32(u[q], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+    uint4 o;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    const long long off = (r0 + r) * N + n;
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q)
+      if (q < world) *reinterpret_cast<uint4*>(sums[q] + off) = o;
+  }
+}
+
 struct TpSegs {
   int count;
   long long row0[2], rows[2], ldr[2];
@@ -212,6 +269,45 @@ b2g_status tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N,
       static_cast<int>(N));
   note_launch();
   return check_cuda(cudaGetLastError(), "tp_reduce_slots launch");
+}
+
+b2g_status tp_scatter_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world, int rank,
+                           cudaStream_t st) {
+  if (world < 1 || world > kTpMaxWorld || rank < 0 || rank >= world || !part || !recv_ptrs || rows <= 0 || N <= 0 ||
+      N % 8 || (reinterpret_cast<uintptr_t>(part) & 15u))
+    return set_error(B2G_ERR_INVALID, "tp_scatter_rows: world in [1, 8], N % 8 == 0, 16-byte aligned partial");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const int64_t shard = (rows + world - 1) / world;
+  const int64_t work = rows * (N / 8);
+  const int64_t blocks = (work + 255) / 256 < 8 * dev->num_sms ? (work + 255) / 256 : 8 * dev->num_sms;
+  tp_scatter_rows_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(part), reinterpret_cast<__nv_bfloat16* const*>(recv_ptrs), rank, rows, shard,
+      static_cast<int>(N));
+  note_launch();
+  return check_cuda(cudaGetLastError(), "tp_scatter_rows launch");
+}
+
+b2g_status tp_reduce_slots_bcast(const void* recv, void* const* sum_ptrs, int64_t rows, int64_t N, int world,
+                                 int rank, cudaStream_t st) {
+  if (world < 1 || world > kTpMaxWorld || rank < 0 || rank >= world || !recv || !sum_ptrs || rows <= 0 || N <= 0 ||
+      N % 8 || (reinterpret_cast<uintptr_t>(recv) & 15u))
+    return set_error(B2G_ERR_INVALID, "tp_reduce_slots_bcast: world in [1, 8], N % 8 == 0, 16-byte aligned buffers");
+  DeviceInfo* dev = nullptr;
+  b2g_status s = device_info(&dev);
+  if (s != B2G_OK) return s;
+  const int64_t shard = (rows + world - 1) / world;
+  const int64_t r0 = rank * shard < rows ? rank * shard : rows;
+  const int64_t r1 = r0 + shard < rows ? r0 + shard : rows;
+  if (r1 <= r0) return B2G_OK;
+  const int64_t work = (r1 - r0) * (N / 8);
+  const int64_t blocks = (work + 255) / 256 < 8 * dev->num_sms ? (work + 255) / 256 : 8 * dev->num_sms;
+  tp_reduce_slots_bcast_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(
+      static_cast<const __nv_bfloat16*>(recv), reinterpret_cast<__nv_bfloat16* const*>(sum_ptrs), world, shard, r0,
+      r1 - r0, static_cast<int>(N));
+  note_launch();
+  return check_cuda(cudaGetLastError(), "tp_reduce_slots_bcast launch");
 }
 
 // Push form with the copy engines: each transfer is one cudaMemcpyAsync of whole rows between

@@ -453,6 +453,25 @@ class SymmetricComm:
         if mark:
             mark(label + ".residual")
 
+    def reduce_store(self, segments: list[dict], mark=None, label: str = "") -> None:
+        """The all-reduce of self.part in the store form, every NVLink transfer an SM store: each
+        row of the partial into its owner's receive slot (b2g_tp_scatter_rows), barrier, the
+        owner sums its slots and stores the sums into every rank's sum buffer
+        (b2g_tp_reduce_slots_bcast), barrier, then each rank applies bias + gate from its own
+        sums (b2g_bias_gated_residual per segment: dict(row0, bias, gate, residual))."""
+        self.b2g.tp_scatter_rows(self.part, self._recv_ptrs, self.world, self.rank)
+        self.barrier()
+        self.b2g.tp_reduce_slots_bcast(self.recv, self._sum_ptrs, self.rows, self.part.shape[1], self.world,
+                                       self.rank)
+        if mark:
+            mark(label + ".reduce")
+        self.barrier()
+        for g in segments:
+            r = g["residual"]
+            self.b2g.bias_gated_residual(self.sums[g["row0"]:g["row0"] + r.shape[0]], g.get("bias"), g["gate"], r)
+        if mark:
+            mark(label + ".residual")
+
     def barrier(self) -> None:
         """All ranks' fused layers are done (bounded wait in libb2g's own barrier kernel).  The
         epoch lives in device memory (b2g_tp_barrier_next), so a CUDA graph of a step that
@@ -494,20 +513,21 @@ def tp_single_block_fused(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, g
 
 
 def _row_split_p2p(ops, comm: SymmetricComm, problems: list[dict], row0: list[int], segments: list[dict], mk,
-                   label: str, push: bool) -> None:
+                   label: str, push) -> None:
     """One row-split layer (its GEMM writes comm.part) and its all-reduce + residual update over
-    peer memory: pull form (SymmetricComm.reduce_p2p, loads from the peers) or push form
-    (SymmetricComm.reduce_push, stores to the peers)."""
+    peer memory: pull form (push False: SymmetricComm.reduce_p2p, loads from the peers), push
+    form by copy engines (push True: reduce_push) or by SM stores (push "store": reduce_store)."""
     ops.gemm_group([dict(x=p["x"], w=p["w"], out=comm.part[r:r + p["x"].shape[0]]) for p, r in zip(problems, row0)])
     mk(label)
-    (comm.reduce_push if push else comm.reduce_p2p)(segments, mk, label)
+    reduce = comm.reduce_store if push == "store" else comm.reduce_push if push else comm.reduce_p2p
+    reduce(segments, mk, label)
 
 
 def tp_double_block_p2p(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w: TPStreamWeights, txt_mod1, img_mod1,
                         txt_mod2, img_mod2, txt, img, txt_gate1, img_gate1, txt_gate2, img_gate2, pe, mask,
-                        s: TPScratch, mark=None, push: bool = False) -> None:
+                        s: TPScratch, mark=None, push=False) -> None:
     """tp_double_block with each row-split layer's all-reduce and residual update done by the
-    two-phase peer-memory kernels (_row_split_p2p, pull or push form); txt, img are this rank's
+    two-phase peer-memory kernels (_row_split_p2p: pull, copy-engine push or store form); txt, img are this rank's
     replicated F32 streams."""
     T = txt_mod1.shape[0]
     mk = mark or _no_mark
@@ -524,9 +544,9 @@ def tp_double_block_p2p(ops, comm: SymmetricComm, txt_w: TPStreamWeights, img_w:
 
 
 def tp_single_block_p2p(ops, comm: SymmetricComm, w: TPSingleWeights, x_mod, x, gate, pe, mask, s: TPScratch,
-                        mark=None, push: bool = False) -> None:
+                        mark=None, push=False) -> None:
     """tp_single_block with linear2's all-reduce and residual update by the two-phase
-    peer-memory kernels (pull or push form); x this rank's replicated F32 stream."""
+    peer-memory kernels (pull, copy-engine push or store form); x this rank's replicated F32 stream."""
     HDl = s.HDl
     mk = mark or _no_mark
     _linear1(ops, w, x_mod, pe, s)

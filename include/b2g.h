@@ -297,6 +297,22 @@ b2g_status b2g_tp_push_sums(void* const* sum_ptrs, int64_t rows, int64_t N, int 
 b2g_status b2g_tp_reduce_slots(const void* recv, void* sum, int64_t rows, int64_t N, int world, int rank,
                                void* stream);
 
+/* The store form of the same all-reduce (no reference counterpart): every transfer over NVLink
+ * is an SM store of 16 bytes a thread, none a load and none a copy-engine copy.  Shards as above;
+ * peer addresses are DEVICE arrays [world] here.
+ *   b2g_tp_scatter_rows: row m of this rank's bf16 partial [rows, N] (local, row stride N) goes to
+ *     its owner q = m / shard, slot `rank`, row m - q * shard of q's receive buffer (recv_ptrs:
+ *     the ranks' peer-mapped bf16 [world][shard][N] buffers).
+ *   b2g_tp_reduce_slots_bcast: sums this rank's receive slots in rank order (local reads), rounds
+ *     to bf16 and stores each of its rows into every rank's sum buffer (sum_ptrs: the ranks'
+ *     peer-mapped bf16 [rows, N] buffers, row stride N), its own included.
+ * A b2g_tp_barrier goes after each; each rank then applies b2g_bias_gated_residual from its own
+ * sum buffer.  world <= 8, N % 8 == 0, 16-byte aligned buffers. */
+b2g_status b2g_tp_scatter_rows(const void* part, void* const* recv_ptrs, int64_t rows, int64_t N, int world,
+                               int rank, void* stream);
+b2g_status b2g_tp_reduce_slots_bcast(const void* recv, void* const* sum_ptrs, int64_t rows, int64_t N, int world,
+                                     int rank, void* stream);
+
 /* Attention input projection with qk_norm and RoPE fused into the GEMM epilogue.  The
  * reference runs these as three linears into F32 q, k, v, then qk_norm (rms_norm per head with
  * a learned scale) on q and k (chroma.cuh:822-842 double block, chroma.cuh:1108-1116 single

@@ -71,7 +71,8 @@ def main() -> int:
     tp.tp_single_block_fused(ops, comm, ts, act["x_mod"], gates[4], pe, mask, scratch)
     fused = {"txt": comm.res_double[:T], "img": comm.res_double[T:], "x": comm.res_single}
     # And with the two-phase peer-memory all-reduce (b2g_tp_reduce_shard + b2g_tp_gather_residual),
-    # and its reduce-scatter form (b2g_gemm_scatter_rows + b2g_tp_reduce_slots).
+    # its copy-engine push form (b2g_tp_push_rows + b2g_tp_reduce_slots + b2g_tp_push_sums) and its
+    # SM-store form (b2g_tp_scatter_rows + b2g_tp_reduce_slots_bcast).
     p2p = {k: v.clone() for k, v in res.items()}
     tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
                            p2p["txt"], p2p["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch)
@@ -81,6 +82,11 @@ def main() -> int:
                            push["txt"], push["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch,
                            push=True)
     tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], push["x"], gates[4], pe, mask, scratch, push=True)
+    store = {k: v.clone() for k, v in res.items()}
+    tp.tp_double_block_p2p(ops, comm, tw, iw, act["txt_mod1"], act["img_mod1"], act["txt_mod2"], act["img_mod2"],
+                           store["txt"], store["img"], gates[0], gates[1], gates[2], gates[3], pe, mask, scratch,
+                           push="store")
+    tp.tp_single_block_p2p(ops, comm, ts, act["x_mod"], store["x"], gates[4], pe, mask, scratch, push="store")
     torch.cuda.synchronize()
     b2g.check_device_error()
     ok = True
@@ -107,6 +113,9 @@ def main() -> int:
         print(f"rank {rank}/{world} {k} push: err {err4:.3e} cos {cos4:.6f} identical-to-p2p "
               f"{torch.equal(push[k], p2p[k])}", flush=True)
         ok = ok and err4 <= 1e-2 and cos4 >= 0.9999
+        same5 = torch.equal(store[k], push[k])   # same sums in the same order, same residual kernel
+        print(f"rank {rank}/{world} {k} store: identical-to-push {same5}", flush=True)
+        ok = ok and same5
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
