@@ -462,7 +462,8 @@ def run_reference_config2(args) -> None:
     h.setup(42, FC_H, FC_W, *FC_REAL)
     n_fc = max(3, min(args.steps, 20))
     # The per-part legs first, as in the engine arm: before the sustained step loop drives the
-    # GPU into its power cap.
+    # GPU into its power cap, after a short idle.
+    _settle()
     approx_ms = h.bench_modulation(FC_TIMESTEP, max(5, min(args.steps, 30)), 3, FLUSH_BYTES)
     import torch
 
@@ -479,6 +480,7 @@ def run_reference_config2(args) -> None:
 
     dev = torch.device("cuda", 0)
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    _settle(torch)
     attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup), ref=ref)
     approx = approximator_leg(torch, dev, flush, None, None, 0, ms_list=approx_ms)
     approx["workload"] += "; the reference's own ChromaApproximator (linear() on cuBLASLt) in its forward_cfg build"
@@ -693,6 +695,8 @@ def run_engine_config2(args) -> None:
     del graphs, marked
 
     fc = forward_cfg_leg(args, torch, dev, flush, dropin=(world == 1 and not args.no_dropin))
+    if rank == 0:
+        _settle(torch)
     attn = attention_leg(torch, dev, flush, max(5, min(args.steps, 50)), max(3, args.warmup)) if rank == 0 else None
     t5 = (t5_encoder_leg(torch, b2g, dev, torch.Generator(device=dev).manual_seed(5), torch.cuda.current_stream(dev),
                          flush) if rank == 0 else None)
@@ -924,7 +928,8 @@ def forward_cfg_leg(args, torch, dev, flush, dropin: bool) -> dict:
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
     # The per-part legs first, before the sustained step loop drives the GPU into its power cap
-    # (the reference arm orders its legs the same way).
+    # (the reference arm orders its legs the same way), after a short idle.
+    _settle(torch)
     approx = approximator_leg(torch, dev, flush, stream, lambda mark=None: m.compute_modulation(s, mark),
                               max(5, min(args.steps, 30)))
     glu = nerf_glu_leg(torch, dev, flush, stream, s.P, max(5, min(args.steps, 30)), m=m)
@@ -1017,6 +1022,18 @@ WORKLOAD_TP1024 = ("config4's block pair at 1024^2: one double-stream + one sing
                    "tokens; 1 GPU: the unsharded block pair; N GPUs: tensor parallel (column-split qkv/linear1/mlp0 "
                    "by heads and MLP columns, row-split proj/mlp2/linear2 with the all-rank reduction fused into the "
                    "GEMM over NVLink peer memory, one cross-rank barrier kernel per row-split layer)")
+
+
+def _settle(torch=None, seconds: float = 2.0) -> None:
+    """Idle before a group of short per-part legs, in both arms alike: right after a sustained
+    load (a timed step loop, or initialising 20 GB of weights) the GPU runs short
+    memory-bound work up to ~30% slower for under a second (measured on the approximator:
+    476-485 us right after 200 block pairs, 373-375 us after 1 s idle)."""
+    import time
+
+    if torch is not None:
+        torch.cuda.synchronize()
+    time.sleep(seconds)
 
 
 class _EagerMarks:
